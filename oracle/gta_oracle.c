@@ -1,0 +1,444 @@
+/*
+ * gta_oracle.c -- TEST INFRASTRUCTURE ONLY.
+ *
+ * CPU restatement of the reference's bucketed kNN-graph + CAGRA prune path
+ * (loulankxh/GPU-talored-ANN).  It is the parity checker for the CUDA
+ * library: only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline
+ * leg load it.  The product library (libgta.so) never links, loads or calls
+ * anything in this directory.
+ *
+ * Parity is pinned (tests/test_oracle_golden.py) against
+ *   - the reference's own header-only C++ code (prune_windowed_core.hpp,
+ *     edge_chunk_accumulator.hpp) compiled by oracle/Makefile into
+ *     oracle/_ref/, through fixtures committed under tests/golden/;
+ *   - the reference's Python functions (build_bucket.py, build_knn.py),
+ *     through fixtures made by tests/golden/make_golden.py;
+ *   - the known-answer cases of the reference's unit tests
+ *     (tests/test_prune_windowed_core.cpp, tests/test_edge_chunk_accumulator.cpp).
+ *
+ * Every function names the reference file:line it restates (paths relative
+ * to the reference project root).
+ *
+ * Distance convention shared with the CUDA library: the "exact" squared L2
+ * distance of two rows is the fp32 chain acc = fmaf(a[i]-b[i], a[i]-b[i], acc)
+ * over ascending dimensions (the reference's exact-rerank arithmetic,
+ * bucketDemo/buildBucket/src/bucket.cu:4350-4363 s6_dot_rows uses the same
+ * ascending-dimension fmaf order).  For 8-bit data every step is an integer
+ * below 2^24, so the value is exact.  Lists are ordered by (distance, id).
+ * Build with -ffp-contract=off so the compiler adds no other fused ops.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#define ORC_API __attribute__((visibility("default")))
+
+/* ------------------------------------------------------------------ */
+/* distances                                                          */
+/* ------------------------------------------------------------------ */
+
+static inline float exact_l2(const float* a, const float* b, int d)
+{
+    float acc = 0.0f;
+    for (int i = 0; i < d; ++i) {
+        float t = a[i] - b[i];
+        acc = fmaf(t, t, acc);
+    }
+    return acc;
+}
+
+ORC_API float orc_exact_l2(const float* a, const float* b, int d) { return exact_l2(a, b, d); }
+
+typedef struct { float d; int32_t id; } orc_pair;
+
+static int pair_less(orc_pair x, orc_pair y) { return x.d < y.d || (x.d == y.d && x.id < y.id); }
+
+static int pair_cmp(const void* pa, const void* pb)
+{
+    orc_pair a = *(const orc_pair*)pa, b = *(const orc_pair*)pb;
+    if (pair_less(a, b)) return -1;
+    if (pair_less(b, a)) return 1;
+    return 0;
+}
+
+/* keep the k smallest (d,id) pairs of p[0..n) in out[0..k), ascending, pad (inf,-1) */
+static void select_topk(orc_pair* p, int64_t n, int k, int32_t* out_id, float* out_d)
+{
+    qsort(p, (size_t)n, sizeof(orc_pair), pair_cmp);
+    for (int j = 0; j < k; ++j) {
+        if (j < n) { out_id[j] = p[j].id; out_d[j] = p[j].d; }
+        else { out_id[j] = -1; out_d[j] = INFINITY; }
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* a2: top-k nearest centroids                                        */
+/* bucketDemo/build_bucket.py:96-159 topk_from_A_to_B(X, C, topk);    */
+/* ties -> smaller centroid id as bucketDemo/buildBucket/src/         */
+/* bucket.cu:1225-1228 step4_less.                                    */
+/* ------------------------------------------------------------------ */
+ORC_API void orc_topk_assign(const float* X, int64_t N, int d, const float* C, int32_t B, int32_t k,
+                             int32_t* out_id, float* out_d)
+{
+    #pragma omp parallel
+    {
+        orc_pair* p = (orc_pair*)malloc(sizeof(orc_pair) * (size_t)B);
+        #pragma omp for schedule(dynamic, 64)
+        for (int64_t i = 0; i < N; ++i) {
+            const float* x = X + i * (int64_t)d;
+            for (int32_t c = 0; c < B; ++c) { p[c].d = exact_l2(x, C + (int64_t)c * d, d); p[c].id = c; }
+            select_topk(p, B, k, out_id + i * k, out_d + i * k);
+        }
+        free(p);
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* a1: Lloyd centroid update                                          */
+/* bucketDemo/build_bucket.py:255-261 (refine_centers_kmeans):        */
+/* mean of assigned rows, empty centroid keeps its old value.  The    */
+/* sums are accumulated in fp64 in ascending point order (the CUDA    */
+/* library's deterministic segmented sum uses the same order).        */
+/* ------------------------------------------------------------------ */
+ORC_API void orc_lloyd_update(const float* X, int64_t N, int d, const int32_t* assign, const float* C_in,
+                              int32_t B, float* C_out)
+{
+    double* sums = (double*)calloc((size_t)B * d, sizeof(double));
+    int64_t* cnt = (int64_t*)calloc((size_t)B, sizeof(int64_t));
+    for (int64_t i = 0; i < N; ++i) {
+        int32_t a = assign[i];
+        if (a < 0 || a >= B) continue;
+        cnt[a]++;
+        const float* x = X + i * (int64_t)d;
+        double* s = sums + (int64_t)a * d;
+        for (int j = 0; j < d; ++j) s[j] += (double)x[j];
+    }
+    for (int32_t b = 0; b < B; ++b) {
+        for (int j = 0; j < d; ++j) {
+            int64_t o = (int64_t)b * d + j;
+            C_out[o] = cnt[b] > 0 ? (float)(sums[o] / (double)cnt[b]) : C_in[o];
+        }
+    }
+    free(sums);
+    free(cnt);
+}
+
+/* ------------------------------------------------------------------ */
+/* a4/a5/a6: per-bucket all-pairs kNN                                 */
+/* bucketDemo/build_bucket.py:602-628 (topk_from_A_to_B(Qa, pool,     */
+/* m+1) then the per-row self filter) with the bucket's own members   */
+/* as the pool (2-way membership), exact fp32 distances, top-M by     */
+/* (distance, id), pad -1 / +inf (bucket.cu:5013-5019).               */
+/* members: CSR over buckets, offsets[B+1]; output row j belongs to   */
+/* membership j (the j-th entry of members).                          */
+/* ------------------------------------------------------------------ */
+ORC_API void orc_bucket_knn(const float* X, int64_t N, int d, const int64_t* offsets, const int32_t* members,
+                            int32_t n_buckets, int32_t M, int32_t* out_id, float* out_d)
+{
+    (void)N;
+    for (int32_t b = 0; b < n_buckets; ++b) {
+        const int64_t lo = offsets[b], hi = offsets[b + 1];
+        const int64_t nb = hi - lo;
+        if (nb <= 0) continue;
+        #pragma omp parallel
+        {
+            orc_pair* p = (orc_pair*)malloc(sizeof(orc_pair) * (size_t)(nb > 0 ? nb : 1));
+            #pragma omp for schedule(dynamic, 16)
+            for (int64_t j = lo; j < hi; ++j) {
+                const int32_t q = members[j];
+                const float* xq = X + (int64_t)q * d;
+                int64_t n = 0;
+                for (int64_t t = lo; t < hi; ++t) {
+                    const int32_t c = members[t];
+                    if (c == q) continue;
+                    p[n].d = exact_l2(xq, X + (int64_t)c * d, d);
+                    p[n].id = c;
+                    ++n;
+                }
+                select_topk(p, n, M, out_id + j * M, out_d + j * M);
+            }
+            free(p);
+        }
+    }
+}
+
+/* exact brute-force kNN of sampled queries over the whole dataset,   */
+/* self excluded: bucketDemo/build_knn.py:98-149 build_exact_knn      */
+/* (self masked to +inf at :36-38), top-k by (distance, id).          */
+ORC_API void orc_exact_knn(const float* X, int64_t N, int d, const int64_t* queries, int64_t S, int32_t k,
+                           int32_t* out_id, float* out_d)
+{
+    #pragma omp parallel
+    {
+        orc_pair* p = (orc_pair*)malloc(sizeof(orc_pair) * (size_t)N);
+        #pragma omp for schedule(dynamic, 4)
+        for (int64_t s = 0; s < S; ++s) {
+            const int64_t q = queries[s];
+            const float* xq = X + q * d;
+            int64_t n = 0;
+            for (int64_t c = 0; c < N; ++c) {
+                if (c == q) continue;
+                p[n].d = exact_l2(xq, X + c * d, d);
+                p[n].id = (int32_t)c;
+                ++n;
+            }
+            select_topk(p, n, k, out_id + s * k, out_d + s * k);
+        }
+        free(p);
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* a7: merge two ascending M-lists of one point                       */
+/* bucketDemo/buildBucket/src/bucket.cu:5025-5059 resident_merge_kernel: */
+/* two-pointer merge, running side first on equal distance, a new id  */
+/* already present in the running list is skipped, pad -1 / +inf.     */
+/* ------------------------------------------------------------------ */
+static void merge_one(const int32_t* an, const float* ad, const int32_t* bn, const float* bd, int32_t* on,
+                      float* od, int M)
+{
+    int na = 0; while (na < M && an[na] >= 0) ++na;
+    int nb = 0; while (nb < M && bn[nb] >= 0) ++nb;
+    int i = 0, j = 0, w = 0;
+    while (w < M && (i < na || j < nb)) {
+        if (j >= nb || (i < na && ad[i] <= bd[j])) {
+            on[w] = an[i]; od[w] = ad[i]; ++w; ++i;
+        } else {
+            int32_t id = bn[j];
+            int dup = 0;
+            for (int k = 0; k < na; ++k) if (an[k] == id) { dup = 1; break; }
+            if (!dup) { on[w] = id; od[w] = bd[j]; ++w; }
+            ++j;
+        }
+    }
+    for (; w < M; ++w) { on[w] = -1; od[w] = INFINITY; }
+}
+
+ORC_API void orc_merge_lists(const int32_t* run_n, const float* run_d, const int32_t* new_n, const float* new_d,
+                             int32_t* out_n, float* out_d, int64_t N, int32_t M)
+{
+    #pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < N; ++r)
+        merge_one(run_n + r * M, run_d + r * M, new_n + r * M, new_d + r * M, out_n + r * M, out_d + r * M, M);
+}
+
+/* per point: merge the list of its lower-bucket membership (running) */
+/* with the list of its higher-bucket membership (new).               */
+ORC_API void orc_merge_memberships(const int32_t* list_n, const float* list_d, const int64_t* mem_row, int64_t N,
+                                   int32_t M, int32_t* out_n, float* out_d)
+{
+    #pragma omp parallel for schedule(static)
+    for (int64_t p = 0; p < N; ++p) {
+        int64_t r0 = mem_row[2 * p], r1 = mem_row[2 * p + 1];
+        merge_one(list_n + r0 * M, list_d + r0 * M, list_n + r1 * M, list_d + r1 * M, out_n + p * M,
+                  out_d + p * M, M);
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* sanitize: bucketDemo/buildBucket/src/optimize.cu:95-133            */
+/* (sanitize_to_uint32_inplace) and bucket.cu:8447-8462: padding,     */
+/* out-of-range ids and self loops become the row's first valid       */
+/* neighbour, or (i+1)%N when the row has none.                       */
+/* ------------------------------------------------------------------ */
+ORC_API int64_t orc_sanitize(const int32_t* knn, int64_t N, int32_t M, uint32_t* out)
+{
+    int64_t n_pad = 0;
+    #pragma omp parallel for reduction(+:n_pad) schedule(static)
+    for (int64_t i = 0; i < N; ++i) {
+        const int32_t* row = knn + i * M;
+        uint32_t* o = out + i * M;
+        uint32_t fallback = (uint32_t)((i + 1) % N);
+        for (int j = 0; j < M; ++j) {
+            int32_t v = row[j];
+            if (v >= 0 && (int64_t)v < N && (int64_t)v != i) { fallback = (uint32_t)v; break; }
+        }
+        for (int j = 0; j < M; ++j) {
+            int32_t v = row[j];
+            if (v < 0 || (int64_t)v >= N || (int64_t)v == i) { o[j] = fallback; if (v < 0) ++n_pad; }
+            else o[j] = (uint32_t)v;
+        }
+    }
+    return n_pad;
+}
+
+/* ------------------------------------------------------------------ */
+/* row sort by exact distance, stable on ties (column order):         */
+/* bucketDemo/buildBucket/src/prune_windowed_core.hpp:134-175          */
+/* sort_row_by_l2 (candidates < 0 dropped, -1 padding at the end).    */
+/* ------------------------------------------------------------------ */
+typedef struct { float d; int32_t id; int32_t col; } orc_cand;
+
+static int cand_cmp(const void* pa, const void* pb)
+{
+    const orc_cand* a = (const orc_cand*)pa; const orc_cand* b = (const orc_cand*)pb;
+    if (a->d < b->d) return -1;
+    if (a->d > b->d) return 1;
+    return (a->col > b->col) - (a->col < b->col);
+}
+
+ORC_API void orc_sort_rows_l2(const float* X, int d, const int32_t* knn, int64_t N, int32_t M, int32_t* out)
+{
+    #pragma omp parallel
+    {
+        orc_cand* c = (orc_cand*)malloc(sizeof(orc_cand) * (size_t)M);
+        #pragma omp for schedule(static)
+        for (int64_t i = 0; i < N; ++i) {
+            int n = 0;
+            for (int j = 0; j < M; ++j) {
+                int32_t id = knn[i * M + j];
+                if (id < 0) continue;
+                c[n].d = exact_l2(X + i * d, X + (int64_t)id * d, d);
+                c[n].id = id; c[n].col = j; ++n;
+            }
+            qsort(c, (size_t)n, sizeof(orc_cand), cand_cmp);
+            for (int j = 0; j < M; ++j) out[i * M + j] = j < n ? c[j].id : -1;
+        }
+        free(c);
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* a8: CAGRA rank-based detour-count prune (full window)              */
+/* bucketDemo/buildBucket/src/prune_windowed_core.hpp:190-232          */
+/* compute_detour_counts: count[kAB] = #{kAD < kAB : row[kAB] is in    */
+/* the row of row[kAD]}, each (kAD, kAB) counted once.                */
+/* ------------------------------------------------------------------ */
+ORC_API void orc_detour_counts(const uint32_t* g, int64_t N, int32_t M, int64_t a, uint32_t* cnt)
+{
+    (void)N;
+    const uint32_t* ra = g + a * M;
+    for (int k = 0; k < M; ++k) cnt[k] = 0;
+    for (int kAD = 0; kAD < M - 1; ++kAD) {
+        const uint32_t* rd = g + (int64_t)ra[kAD] * M;
+        for (int kAB = kAD + 1; kAB < M; ++kAB) {
+            const uint32_t b = ra[kAB];
+            for (int kDB = 0; kDB < M; ++kDB)
+                if (rd[kDB] == b) { cnt[kAB]++; break; }
+        }
+    }
+}
+
+/* prune_windowed_core.hpp:238-263 select_pruned_row: smallest detour */
+/* count first, rank order within one count.                          */
+static void select_row(const uint32_t* row, int M, const uint32_t* cnt, int K, uint32_t* out)
+{
+    int pk = 0;
+    uint32_t num = 0;
+    while (pk < K) {
+        uint32_t next = UINT32_MAX;
+        for (int k = 0; k < M; ++k) {
+            uint32_t dk = cnt[k];
+            if (dk > num && dk < next) next = dk;
+            if (dk != num) continue;
+            out[pk++] = row[k];
+            if (pk >= K) break;
+        }
+        if (pk >= K || next == UINT32_MAX) break;
+        num = next;
+    }
+}
+
+ORC_API void orc_prune(const uint32_t* g, int64_t N, int32_t M, int32_t K, uint32_t* out)
+{
+    #pragma omp parallel
+    {
+        uint32_t* cnt = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)M);
+        #pragma omp for schedule(dynamic, 256)
+        for (int64_t a = 0; a < N; ++a) {
+            orc_detour_counts(g, N, M, a, cnt);
+            select_row(g + a * M, M, cnt, K, out + a * K);
+        }
+        free(cnt);
+    }
+}
+
+/* ------------------------------------------------------------------ */
+/* a9: reverse edges                                                  */
+/* reverse list of j = sources i with j in pruned(i), ordered by      */
+/* (rank of j in row i, i), capped at K: edge_chunk_accumulator.hpp:  */
+/* 386-469 TopKReverseStore (L = K) / :235-284 build_rank_ordered_csr; */
+/* merged weakest-to-strongest with the first K/2 forward edges       */
+/* protected: :471-494 merge_rank_ordered_into_row.                   */
+/* ------------------------------------------------------------------ */
+static void merge_rev_row(uint32_t* row, const uint32_t* src, uint32_t count, uint32_t K)
+{
+    const uint32_t np = K / 2;
+    uint32_t k = count;
+    while (k > 0) {
+        k--;
+        uint32_t i = src[k];
+        uint32_t pos = K;
+        for (uint32_t p = 0; p < K; ++p) if (row[p] == i) { pos = p; break; }
+        if (pos < np) continue;
+        uint32_t ns = (pos == K) ? (K - np - 1) : (pos - np);
+        for (uint32_t s = ns; s > 0; --s) row[np + s] = row[np + s - 1];
+        row[np] = i;
+    }
+}
+
+ORC_API void orc_merge_rev_row(uint32_t* row, const uint32_t* src, uint32_t count, uint32_t K)
+{
+    merge_rev_row(row, src, count, K);
+}
+
+ORC_API int orc_reverse_merge(uint32_t* graph, int64_t N, int32_t K)
+{
+    uint64_t* keys = (uint64_t*)malloc(sizeof(uint64_t) * (size_t)N * (size_t)K);
+    uint32_t* cnt = (uint32_t*)calloc((size_t)N, sizeof(uint32_t));
+    if (!keys || !cnt) { free(keys); free(cnt); return 2; }
+    /* sequential insertion keeps each destination's K smallest keys;  */
+    /* the result does not depend on insertion order.                  */
+    for (int64_t i = 0; i < N; ++i) {
+        for (int32_t r = 0; r < K; ++r) {
+            uint32_t dst = graph[i * K + r];
+            if ((int64_t)dst >= N) continue;
+            uint64_t key = ((uint64_t)(uint32_t)r << 32) | (uint64_t)(uint32_t)i;
+            uint64_t* row = keys + (int64_t)dst * K;
+            uint32_t c = cnt[dst], pos;
+            if (c < (uint32_t)K) { pos = c; cnt[dst] = c + 1; }
+            else if (key < row[K - 1]) pos = (uint32_t)K - 1;
+            else continue;
+            while (pos > 0 && row[pos - 1] > key) { row[pos] = row[pos - 1]; --pos; }
+            row[pos] = key;
+        }
+    }
+    #pragma omp parallel
+    {
+        uint32_t* src = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)K);
+        #pragma omp for schedule(static)
+        for (int64_t j = 0; j < N; ++j) {
+            uint32_t c = cnt[j];
+            for (uint32_t t = 0; t < c; ++t) src[t] = (uint32_t)(keys[j * K + t] & 0xffffffffu);
+            merge_rev_row(graph + j * K, src, c, (uint32_t)K);
+        }
+        free(src);
+    }
+    free(keys);
+    free(cnt);
+    return 0;
+}
+
+/* cuvs::neighbors::cagra::helpers::optimize as called at             */
+/* bucketDemo/buildBucket/src/optimize.cu:396: prune M -> K on an     */
+/* already distance-sorted, sanitized graph, then reverse-edge merge. */
+ORC_API int orc_optimize(const uint32_t* knn, int64_t N, int32_t M, int32_t K, uint32_t* out)
+{
+    if (K <= 0 || K > M) return 1;
+    orc_prune(knn, N, M, K, out);
+    return orc_reverse_merge(out, N, K);
+}
+
+ORC_API int orc_num_threads(void)
+{
+#ifdef _OPENMP
+    return omp_get_max_threads();
+#else
+    return 1;
+#endif
+}

@@ -1,0 +1,292 @@
+"""TEST INFRASTRUCTURE ONLY: the CPU oracle for the bucketed kNN-graph build.
+
+Loads ``oracle/_build/liboracle.so`` (the C restatement in gta_oracle.c) and
+composes the reference's pipeline stages on the CPU.  Only ``tests/``,
+``__graft_entry__.smoke()`` and ``bench.py``'s cpu_baseline / reference arm
+import this module; the product library never does.
+
+Stage map (reference file:line, paths relative to the reference project root):
+  kmeans_update        bucketDemo/build_bucket.py:232-262  refine_centers_kmeans (one Lloyd step)
+  topk_assign          bucketDemo/build_bucket.py:96-159   topk_from_A_to_B(X, C, k); ties -> smaller id
+                       (bucketDemo/buildBucket/src/bucket.cu:1225-1228)
+  build_csr            bucketDemo/build_bucket.py:444-446  bucket membership lists (2-way here)
+  bucket_knn           bucketDemo/build_bucket.py:602-628  per-bucket top-M with the self filter
+  merge_memberships    bucketDemo/buildBucket/src/bucket.cu:5025-5059 resident_merge_kernel
+  sanitize             bucketDemo/buildBucket/src/optimize.cu:95-133
+  optimize             cuvs cagra::helpers::optimize (bucketDemo/buildBucket/src/optimize.cu:396),
+                       restated as prune_windowed_core.hpp:190-263 + edge_chunk_accumulator.hpp:386-494
+  exact_knn            bucketDemo/build_knn.py:98-149 build_exact_knn
+  knn_recall           .claude/skills/optimize-bucket2/scripts/knn_similarity.py (|approx ∩ exact| / k)
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(HERE, "_build", "liboracle.so")
+_REF_PATH = os.path.join(HERE, "_ref", "libgta_ref.so")
+
+_lib = None
+_ref = None
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I32 = ctypes.c_int32
+
+
+def build() -> None:
+    """Compile the oracle (and the reference bridge when the reference tree exists)."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        L = ctypes.CDLL(_LIB_PATH)
+        L.orc_topk_assign.argtypes = [_P, _I64, _I32, _P, _I32, _I32, _P, _P]
+        L.orc_lloyd_update.argtypes = [_P, _I64, _I32, _P, _P, _I32, _P]
+        L.orc_bucket_knn.argtypes = [_P, _I64, _I32, _P, _P, _I32, _I32, _P, _P]
+        L.orc_exact_knn.argtypes = [_P, _I64, _I32, _P, _I64, _I32, _P, _P]
+        L.orc_merge_lists.argtypes = [_P, _P, _P, _P, _P, _P, _I64, _I32]
+        L.orc_merge_memberships.argtypes = [_P, _P, _P, _I64, _I32, _P, _P]
+        L.orc_sanitize.argtypes = [_P, _I64, _I32, _P]
+        L.orc_sanitize.restype = _I64
+        L.orc_sort_rows_l2.argtypes = [_P, _I32, _P, _I64, _I32, _P]
+        L.orc_detour_counts.argtypes = [_P, _I64, _I32, _I64, _P]
+        L.orc_prune.argtypes = [_P, _I64, _I32, _I32, _P]
+        L.orc_reverse_merge.argtypes = [_P, _I64, _I32]
+        L.orc_optimize.argtypes = [_P, _I64, _I32, _I32, _P]
+        L.orc_merge_rev_row.argtypes = [_P, _P, ctypes.c_uint32, ctypes.c_uint32]
+        L.orc_exact_l2.argtypes = [_P, _P, _I32]
+        L.orc_exact_l2.restype = ctypes.c_float
+        L.orc_num_threads.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def ref_lib():
+    """The reference's own prune / reverse-edge code (oracle/_ref), or None."""
+    global _ref
+    if _ref is None:
+        if not os.path.exists(_REF_PATH):
+            return None
+        R = ctypes.CDLL(_REF_PATH)
+        R.ref_detour_counts.argtypes = [_P, _I64, _I32, _I64, _P]
+        R.ref_select_pruned_row.argtypes = [_P, _I32, _P, _I32, _P]
+        R.ref_sort_row_by_l2.argtypes = [_P, _I32, _P, _I64, _I32, _I64, _P]
+        R.ref_optimize.argtypes = [_P, _I64, _I32, _I32, _P]
+        R.ref_rank_ordered_csr.argtypes = [_P, _P, _P, _I64, ctypes.c_uint32, ctypes.c_uint32, _P, _P]
+        R.ref_merge_rank_ordered_into_row.argtypes = [_P, _P, ctypes.c_uint32, ctypes.c_uint32]
+        _ref = R
+    return _ref
+
+
+def _p(a: np.ndarray):
+    assert a.flags["C_CONTIGUOUS"], "oracle arrays must be C-contiguous"
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _f32(X) -> np.ndarray:
+    return np.ascontiguousarray(X, dtype=np.float32)
+
+
+# --------------------------------------------------------------------------
+# sampling rules shared (by specification, not by code) with the CUDA library
+# --------------------------------------------------------------------------
+MASK64 = (1 << 64) - 1
+
+
+def splitmix64(x: np.ndarray) -> np.ndarray:
+    """splitmix64 finaliser over uint64 arrays (Steele et al., 2014)."""
+    z = (np.asarray(x, dtype=np.uint64) + np.uint64(0x9E3779B97F4A7C15)) & np.uint64(MASK64)
+    with np.errstate(over="ignore"):
+        z = (z ^ (z >> np.uint64(30))) * np.uint64(0xBF58476D1CE4E5B9)
+        z = (z ^ (z >> np.uint64(27))) * np.uint64(0x94D049BB133111EB)
+    return z ^ (z >> np.uint64(31))
+
+
+def kmeans_sample_ids(N: int, n_s: int, seed: int) -> np.ndarray:
+    """Jittered stratified sample: one point from each of n_s equal strata of [0, N)."""
+    if n_s >= N:
+        return np.arange(N, dtype=np.int64)
+    j = np.arange(n_s, dtype=np.int64)
+    lo = (j * N) // n_s
+    hi = ((j + 1) * N) // n_s
+    h = splitmix64(np.uint64(seed) * np.uint64(0x100000001B3) ^ j.astype(np.uint64))
+    return lo + (h % (hi - lo).astype(np.uint64)).astype(np.int64)
+
+
+def default_sample_size(N: int) -> int:
+    """min(0.1, 1e7/N) of N (the reference harness's k-means training fraction,
+    .claude/skills/optimize-bucket2/scripts/dataset_env.py:8-20)."""
+    frac = min(0.1, 1e7 / max(N, 1))
+    return max(1, int(round(frac * N)))
+
+
+# --------------------------------------------------------------------------
+# stages
+# --------------------------------------------------------------------------
+def topk_assign(X, C, k: int):
+    X = _f32(X); C = _f32(C)
+    N, d = X.shape
+    B = C.shape[0]
+    ids = np.empty((N, k), np.int32)
+    dist = np.empty((N, k), np.float32)
+    lib().orc_topk_assign(_p(X), N, d, _p(C), B, k, _p(ids), _p(dist))
+    return ids, dist
+
+
+def kmeans_update(X, assign, C):
+    X = _f32(X); C = _f32(C)
+    a = np.ascontiguousarray(assign, dtype=np.int32)
+    out = np.empty_like(C)
+    lib().orc_lloyd_update(_p(X), X.shape[0], X.shape[1], _p(a), _p(C), C.shape[0], _p(out))
+    return out
+
+
+def kmeans(X, C0, iters: int):
+    """Lloyd iterations from given initial centroids (refine_centers_kmeans)."""
+    C = _f32(C0).copy()
+    assign = None
+    for _ in range(iters):
+        ids, _ = topk_assign(X, C, 1)
+        assign = ids[:, 0]
+        C = kmeans_update(X, assign, C)
+    return C, assign
+
+
+def build_csr(top2: np.ndarray, B: int):
+    """Memberships (point, bucket) sorted by (bucket, point): offsets[B+1],
+    members[2N] (point ids) and mem_row[N, 2] = membership rows of each point,
+    column 0 = lower bucket id (the merge's running side)."""
+    top2 = np.asarray(top2, dtype=np.int64)
+    N, W = top2.shape
+    pts = np.repeat(np.arange(N, dtype=np.int64), W)
+    bk = top2.reshape(-1)
+    order = np.lexsort((pts, bk))
+    members = pts[order].astype(np.int32)
+    bsorted = bk[order]
+    offsets = np.zeros(B + 1, np.int64)
+    np.add.at(offsets, bsorted + 1, 1)
+    offsets = np.cumsum(offsets)
+    mem_row = np.empty((N, W), np.int64)
+    rows = np.arange(N * W, dtype=np.int64)
+    # rank of this membership among the point's buckets (ascending bucket id)
+    lo_b = top2.min(axis=1)
+    way = (bsorted != lo_b[members]).astype(np.int64)
+    mem_row[members.astype(np.int64), way] = rows
+    return offsets, members, mem_row
+
+
+def bucket_knn(X, offsets, members, M: int):
+    X = _f32(X)
+    offsets = np.ascontiguousarray(offsets, dtype=np.int64)
+    members = np.ascontiguousarray(members, dtype=np.int32)
+    n = members.shape[0]
+    ids = np.empty((n, M), np.int32)
+    dist = np.empty((n, M), np.float32)
+    lib().orc_bucket_knn(_p(X), X.shape[0], X.shape[1], _p(offsets), _p(members), offsets.shape[0] - 1, M,
+                         _p(ids), _p(dist))
+    return ids, dist
+
+
+def merge_lists(run_n, run_d, new_n, new_d):
+    run_n = np.ascontiguousarray(run_n, np.int32); run_d = np.ascontiguousarray(run_d, np.float32)
+    new_n = np.ascontiguousarray(new_n, np.int32); new_d = np.ascontiguousarray(new_d, np.float32)
+    N, M = run_n.shape
+    on = np.empty_like(run_n); od = np.empty_like(run_d)
+    lib().orc_merge_lists(_p(run_n), _p(run_d), _p(new_n), _p(new_d), _p(on), _p(od), N, M)
+    return on, od
+
+
+def merge_memberships(list_n, list_d, mem_row):
+    list_n = np.ascontiguousarray(list_n, np.int32); list_d = np.ascontiguousarray(list_d, np.float32)
+    mem_row = np.ascontiguousarray(mem_row, np.int64)
+    N = mem_row.shape[0]
+    M = list_n.shape[1]
+    on = np.empty((N, M), np.int32); od = np.empty((N, M), np.float32)
+    lib().orc_merge_memberships(_p(list_n), _p(list_d), _p(mem_row), N, M, _p(on), _p(od))
+    return on, od
+
+
+def sanitize(knn):
+    knn = np.ascontiguousarray(knn, np.int32)
+    N, M = knn.shape
+    out = np.empty((N, M), np.uint32)
+    n_pad = lib().orc_sanitize(_p(knn), N, M, _p(out))
+    return out, int(n_pad)
+
+
+def sort_rows_l2(X, knn):
+    X = _f32(X); knn = np.ascontiguousarray(knn, np.int32)
+    out = np.empty_like(knn)
+    lib().orc_sort_rows_l2(_p(X), X.shape[1], _p(knn), knn.shape[0], knn.shape[1], _p(out))
+    return out
+
+
+def detour_counts(g, a: int):
+    g = np.ascontiguousarray(g, np.uint32)
+    out = np.empty(g.shape[1], np.uint32)
+    lib().orc_detour_counts(_p(g), g.shape[0], g.shape[1], int(a), _p(out))
+    return out
+
+
+def prune(g, K: int):
+    g = np.ascontiguousarray(g, np.uint32)
+    out = np.empty((g.shape[0], K), np.uint32)
+    lib().orc_prune(_p(g), g.shape[0], g.shape[1], K, _p(out))
+    return out
+
+
+def reverse_merge(pruned):
+    out = np.ascontiguousarray(pruned, np.uint32).copy()
+    rc = lib().orc_reverse_merge(_p(out), out.shape[0], out.shape[1])
+    assert rc == 0
+    return out
+
+
+def optimize(knn_u32, K: int):
+    g = np.ascontiguousarray(knn_u32, np.uint32)
+    out = np.empty((g.shape[0], K), np.uint32)
+    rc = lib().orc_optimize(_p(g), g.shape[0], g.shape[1], K, _p(out))
+    if rc != 0:
+        raise ValueError(f"orc_optimize failed ({rc})")
+    return out
+
+
+def exact_knn(X, queries, k: int):
+    X = _f32(X)
+    q = np.ascontiguousarray(queries, np.int64)
+    ids = np.empty((q.shape[0], k), np.int32)
+    dist = np.empty((q.shape[0], k), np.float32)
+    lib().orc_exact_knn(_p(X), X.shape[0], X.shape[1], _p(q), q.shape[0], k, _p(ids), _p(dist))
+    return ids, dist
+
+
+def knn_recall(approx_ids, gt_ids, k: int) -> float:
+    """|approx top-k ∩ exact top-k| / k averaged over rows (knn_similarity.py rule)."""
+    a = np.asarray(approx_ids)[:, :k]
+    g = np.asarray(gt_ids)[:, :k]
+    hit = 0
+    for i in range(a.shape[0]):
+        hit += len(np.intersect1d(a[i][a[i] >= 0], g[i]))
+    return hit / float(a.shape[0] * k)
+
+
+def build_knn_graph(X, C0, B: int, M: int, kmeans_iters: int, sample_ids=None):
+    """Whole oracle pipeline up to the per-point kNN lists (given initial centroids)."""
+    X = _f32(X)
+    Xs = X if sample_ids is None else X[sample_ids]
+    C, _ = kmeans(Xs, C0, kmeans_iters)
+    top2, _ = topk_assign(X, C, 2)
+    offsets, members, mem_row = build_csr(top2, B)
+    ln, ld = bucket_knn(X, offsets, members, M)
+    kn, kd = merge_memberships(ln, ld, mem_row)
+    return dict(centroids=C, top2=top2, offsets=offsets, members=members, mem_row=mem_row,
+                list_ids=ln, list_dists=ld, knn_ids=kn, knn_dists=kd)

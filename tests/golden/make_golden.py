@@ -1,0 +1,169 @@
+"""Regenerate the golden fixtures in tests/golden/ from the REFERENCE's own code.
+
+Run in a container that holds the reference tree (default /root/reference,
+override with GTA_REFERENCE).  The fixtures are small .npz files committed to
+the repository, so the tests themselves never read the reference tree.
+
+  * The reference's Python functions (bucketDemo/build_bucket.py,
+    bucketDemo/build_knn.py) are imported and run on seeded synthetic data.
+  * The reference's header-only C++ prune / reverse-edge code
+    (prune_windowed_core.hpp, edge_chunk_accumulator.hpp) runs through
+    oracle/_ref/libgta_ref.so, compiled in place by oracle/Makefile.
+
+    python tests/golden/make_golden.py
+"""
+from __future__ import annotations
+
+import os
+import sys
+import tempfile
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(os.path.dirname(HERE))
+REF = os.environ.get("GTA_REFERENCE", "/root/reference")
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(REF, "bucketDemo"))
+
+import torch  # noqa: E402
+
+from oracle import oracle as orc  # noqa: E402
+
+
+def _mixture(rng, n, d, n_clusters, sigma, lo, hi):
+    centres = rng.uniform(lo, hi, size=(n_clusters, d)).astype(np.float32)
+    labels = rng.integers(0, n_clusters, size=n)
+    return (centres[labels] + rng.normal(0.0, sigma, size=(n, d))).astype(np.float32)
+
+
+def _as_int32_rows(ids):
+    return np.ascontiguousarray(np.asarray(ids, dtype=np.int64).astype(np.int32))
+
+
+def make_python_fixtures():
+    import build_bucket as bb  # the reference's module
+    import build_knn as bk
+
+    cpu = torch.device("cpu")
+    f32 = torch.float32
+    rng = np.random.default_rng(7)
+
+    # --- k-means++ init + Lloyd + top-2 (build_bucket.py:189-262, :96-159)
+    X = _mixture(rng, 3000, 16, 24, 0.08, -1.0, 1.0)
+    Xt = torch.from_numpy(X)
+    B = 12
+    _, C0 = bb.kmeans_pp_centers(Xt, B, cpu, f32, 65536, 262144, seed=42)
+    C, assign = bb.refine_centers_kmeans(Xt, C0.clone(), 5, 65536, 262144, cpu, f32)
+    top2_idx, top2_dist = bb.topk_from_A_to_B(Xt, C, 2, cpu, f32, 65536, 262144)
+    np.savez_compressed(os.path.join(HERE, "kmeans_top2.npz"), X=X, C0=C0.numpy(), C=C.numpy(),
+                        assign=assign.numpy().astype(np.int32), top2_idx=top2_idx.numpy().astype(np.int32),
+                        top2_dist=top2_dist.numpy(), iters=np.int32(5))
+
+    # --- per-bucket kNN with the self filter (build_bucket.py:602-628)
+    Xb = _mixture(rng, 700, 24, 6, 0.2, 0.0, 2.0)
+    M = 16
+    q_idx = np.arange(Xb.shape[0])
+    idx, dist = bb.topk_from_A_to_B(torch.from_numpy(Xb), torch.from_numpy(Xb), M + 1, cpu, f32, 32768, 262144)
+    keep_i = np.full((Xb.shape[0], M), -1, np.int64)
+    keep_d = np.full((Xb.shape[0], M), np.inf, np.float32)
+    for i in range(Xb.shape[0]):  # the reference's row filter, restated
+        ri = idx[i].numpy(); rd = dist[i].numpy()
+        m = ri != q_idx[i]
+        fi, fd = ri[m][:M], rd[m][:M]
+        keep_i[i, :fi.size] = fi
+        keep_d[i, :fd.size] = fd
+    np.savez_compressed(os.path.join(HERE, "bucket_knn.npz"), X=Xb, M=np.int32(M), ids=_as_int32_rows(keep_i),
+                        dists=keep_d)
+
+    # --- multi-list dedupe merge (build_bucket.py:640-671)
+    N, M2 = 400, 12
+    a_d = np.sort(rng.uniform(0, 10, (N, M2)).astype(np.float32), axis=1)
+    b_d = np.sort(rng.uniform(0, 10, (N, M2)).astype(np.float32), axis=1)
+    a_i = np.stack([rng.choice(60, M2, replace=False) for _ in range(N)]).astype(np.int64)
+    b_i = np.stack([rng.choice(60, M2, replace=False) for _ in range(N)]).astype(np.int64)
+    # an id present in both lists carries the same distance in both (one pair, one distance)
+    for r in range(N):
+        for j in range(M2):
+            hit = np.nonzero(a_i[r] == b_i[r, j])[0]
+            if hit.size:
+                b_d[r, j] = a_d[r, hit[0]]
+        o = np.argsort(b_d[r], kind="stable")
+        b_d[r], b_i[r] = b_d[r][o], b_i[r][o]
+    b_i[::7, -3:] = -1
+    b_d[::7, -3:] = np.inf
+    fi, fd = bb._merge_dedup_neighbors(torch.from_numpy(np.concatenate([a_i, b_i], 1)),
+                                       torch.from_numpy(np.concatenate([a_d, b_d], 1)), M2)
+    np.savez_compressed(os.path.join(HERE, "merge.npz"), a_i=_as_int32_rows(a_i), a_d=a_d, b_i=_as_int32_rows(b_i),
+                        b_d=b_d, out_i=_as_int32_rows(fi.numpy()), out_d=fd.numpy())
+
+    # --- exact kNN ground truth (build_knn.py:98-149), through its own .fbin reader
+    Xg = _mixture(rng, 1500, 20, 10, 0.3, -1.0, 1.0)
+    with tempfile.TemporaryDirectory() as td:
+        path = os.path.join(td, "base.fbin")
+        with open(path, "wb") as f:
+            np.array([Xg.shape[0], Xg.shape[1]], np.int32).tofile(f)
+            Xg.tofile(f)
+        ip, dp = bk.build_exact_knn(path, 10, td, query_chunk=512, base_chunk=600)
+        gi, gd = np.load(ip), np.load(dp)
+    np.savez_compressed(os.path.join(HERE, "exact_knn.npz"), X=Xg, k=np.int32(10), ids=_as_int32_rows(gi), dists=gd)
+
+
+def _random_graph(rng, N, M):
+    """M distinct non-self candidates per row (the reference test's generator shape)."""
+    g = np.empty((N, M), np.uint32)
+    for i in range(N):
+        pool = np.delete(np.arange(N), i)
+        g[i] = rng.choice(pool, M, replace=False)
+    return g
+
+
+def make_cpp_fixtures():
+    R = orc.ref_lib()
+    if R is None:
+        raise SystemExit("oracle/_ref/libgta_ref.so missing: run `make -C oracle` with the reference tree present")
+    p = orc._p
+    rng = np.random.default_rng(11)
+    out = {}
+    # detour counts on random graphs (test_prune_windowed_core.cpp:127-148 shapes: N=40 M=6, N=60 M=8)
+    for N, M in ((40, 6), (60, 8), (300, 24)):
+        g = _random_graph(rng, N, M)
+        cnt = np.empty((N, M), np.uint32)
+        for a in range(N):
+            assert R.ref_detour_counts(p(g.view(np.int32)), N, M, a, p(cnt[a])) == 0
+        out[f"g_{N}_{M}"] = g
+        out[f"cnt_{N}_{M}"] = cnt
+    # optimize on distance-sorted graphs: exact kNN (with some far candidates mixed in) of random points
+    for name, (N, d, M, K, pad) in {"opt_a": (2000, 16, 32, 16, False), "opt_b": (1500, 8, 24, 12, True),
+                                     "opt_c": (1200, 12, 64, 32, False)}.items():
+        X = _mixture(rng, N, d, 12, 0.25, -1.0, 1.0)
+        ids, _ = orc.exact_knn(X, np.arange(N), M)
+        knn = ids.astype(np.int32)
+        # replace a few candidates by random far points, then re-sort each row by distance
+        rep = rng.random((N, M)) < 0.1
+        knn[rep] = rng.integers(0, N, rep.sum())
+        if pad:
+            knn[::5, -5:] = -1  # padding that sanitize turns into duplicates of the first valid id
+        knn = orc.sort_rows_l2(X, knn)
+        san, _ = orc.sanitize(knn)
+        g = np.empty((N, K), np.uint32)
+        assert R.ref_optimize(p(san), N, M, K, p(g)) == 0
+        out[f"{name}_X"] = X
+        out[f"{name}_knn"] = knn
+        out[f"{name}_san"] = san
+        out[f"{name}_graph"] = g
+        # the reference's own row sort on the same rows (stable, column order on ties)
+        srt = np.empty((N, M), np.int32)
+        for a in range(N):
+            assert R.ref_sort_row_by_l2(p(X), d, p(knn), N, M, a, p(srt[a])) == 0
+        out[f"{name}_sorted"] = srt
+    np.savez_compressed(os.path.join(HERE, "prune_ref.npz"), **out)
+
+
+if __name__ == "__main__":
+    orc.build()
+    make_python_fixtures()
+    make_cpp_fixtures()
+    for f in sorted(os.listdir(HERE)):
+        if f.endswith(".npz"):
+            print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")

@@ -1,0 +1,156 @@
+"""Pins the CPU oracle against the reference: the known-answer cases of the
+reference's own unit tests and the fixtures made from the reference's code by
+tests/golden/make_golden.py.  CPU only."""
+import numpy as np
+import pytest
+
+from oracle import oracle as orc
+
+
+def _near_tie_mask(d_sorted, rel=1e-5):
+    """True where an entry's distance is within rel of a neighbouring entry (order may legally differ)."""
+    d = np.asarray(d_sorted, np.float64)
+    tie = np.zeros(d.shape, bool)
+    close = np.abs(d[:, 1:] - d[:, :-1]) <= rel * np.maximum(np.abs(d[:, 1:]), 1e-30)
+    tie[:, 1:] |= close
+    tie[:, :-1] |= close
+    return tie
+
+
+# ---------------------------------------------------------------- prune / reverse edges
+def test_select_known_answer():
+    # test_prune_windowed_core.cpp:93-105: detour {0,0,1,1,2}, K=3 -> ids 10, 11, 12
+    g = np.array([[10, 11, 12, 13, 14]], np.uint32)
+    # drive the selection through prune with a crafted graph is awkward; check the rule directly
+    cnt = np.array([0, 0, 1, 1, 2], np.uint32)
+    order = sorted(range(5), key=lambda k: (cnt[k], k))[:3]
+    assert [int(g[0, k]) for k in order] == [10, 11, 12]
+
+
+def test_truncation_keeps_lowest_rank():
+    # test_edge_chunk_accumulator.cpp:185-220: K=6, 3 protected, 5 candidates for 3 free slots
+    row = np.arange(6, dtype=np.uint32)
+    src = np.array([13, 11, 14, 12, 10], np.uint32)  # rank order D,B,E,C,A
+    orc.lib().orc_merge_rev_row(orc._p(row), orc._p(src), 5, 6)
+    assert set(row[3:].tolist()) == {13, 11, 14}
+    assert row[:3].tolist() == [0, 1, 2]
+
+
+def test_sort_row_known_answer():
+    # test_prune_windowed_core.cpp:65-91: points on a line at 0,10,20,30,40; row of 2 = [4,0,3,1]
+    X = np.array([[0], [10], [20], [30], [40]], np.float32)
+    knn = np.array([[1, 2, 3, 4], [0, 2, 3, 4], [4, 0, 3, 1], [0, 1, 2, 4], [0, 1, 2, 3]], np.int32)
+    s = orc.sort_rows_l2(X, knn)
+    assert set(s[2, :2].tolist()) == {3, 1} and set(s[2, 2:].tolist()) == {4, 0}
+    assert s[2].tolist() == [3, 1, 4, 0]  # stable: column order among equal distances
+
+
+def _naive_detour(g, a):
+    """Independent triple loop of test_prune_windowed_core.cpp:45-63."""
+    M = g.shape[1]
+    out = np.zeros(M, np.uint32)
+    row = g[a]
+    for kAD in range(M - 1):
+        drow = set(g[row[kAD]].tolist())
+        for kAB in range(kAD + 1, M):
+            if row[kAB] in drow:
+                out[kAB] += 1
+    return out
+
+
+@pytest.mark.parametrize("N,M", [(40, 6), (60, 8), (300, 24)])
+def test_detour_counts_vs_reference(golden, N, M):
+    f = golden("prune_ref.npz")
+    g = f[f"g_{N}_{M}"]
+    ref = f[f"cnt_{N}_{M}"]
+    for a in range(N):
+        mine = orc.detour_counts(g, a)
+        np.testing.assert_array_equal(mine, ref[a])
+        if a < 40:
+            np.testing.assert_array_equal(mine, _naive_detour(g, a))
+
+
+@pytest.mark.parametrize("name", ["opt_a", "opt_b", "opt_c"])
+def test_optimize_bit_exact_vs_reference(golden, name):
+    f = golden("prune_ref.npz")
+    san, _ = orc.sanitize(f[f"{name}_knn"])
+    np.testing.assert_array_equal(san, f[f"{name}_san"])
+    K = f[f"{name}_graph"].shape[1]
+    np.testing.assert_array_equal(orc.optimize(san, K), f[f"{name}_graph"])
+
+
+@pytest.mark.parametrize("name", ["opt_a", "opt_b", "opt_c"])
+def test_sort_rows_vs_reference(golden, name):
+    f = golden("prune_ref.npz")
+    np.testing.assert_array_equal(orc.sort_rows_l2(f[f"{name}_X"], f[f"{name}_knn"]), f[f"{name}_sorted"])
+
+
+def test_sanitize_rules():
+    knn = np.array([[-1, 0, 2, 2], [-1, -1, -1, -1], [0, 7, 1, -1]], np.int32)
+    out, n_pad = orc.sanitize(knn)
+    # row 0: self (0) and -1 -> first valid neighbour 2; row 1: none valid -> (1+1)%3 = 2
+    assert out.tolist() == [[2, 2, 2, 2], [2, 2, 2, 2], [0, 0, 1, 0]]
+    assert n_pad == 6
+
+
+# ---------------------------------------------------------------- Python pipeline pieces
+def test_lloyd_matches_reference(golden):
+    f = golden("kmeans_top2.npz")
+    C, assign = orc.kmeans(f["X"], f["C0"], int(f["iters"]))
+    np.testing.assert_allclose(C, f["C"], rtol=1e-4, atol=1e-5)
+    assert (assign == f["assign"]).mean() > 0.999
+
+
+def test_top2_matches_reference(golden):
+    f = golden("kmeans_top2.npz")
+    ids, dist = orc.topk_assign(f["X"], f["C"], 2)
+    np.testing.assert_allclose(dist, f["top2_dist"], rtol=1e-4, atol=1e-4)
+    tie = np.abs(f["top2_dist"][:, 1] - f["top2_dist"][:, 0]) <= 1e-5 * f["top2_dist"][:, 1]
+    np.testing.assert_array_equal(ids[~tie], f["top2_idx"][~tie])
+
+
+def test_bucket_knn_matches_reference(golden):
+    f = golden("bucket_knn.npz")
+    X, M = f["X"], int(f["M"])
+    n = X.shape[0]
+    ids, dist = orc.bucket_knn(X, np.array([0, n], np.int64), np.arange(n, dtype=np.int32), M)
+    np.testing.assert_allclose(dist, f["dists"], rtol=1e-4, atol=1e-4)
+    ok = (ids == f["ids"]) | _near_tie_mask(f["dists"], 1e-4)
+    assert ok.all()
+
+
+def test_merge_matches_reference(golden):
+    f = golden("merge.npz")
+    on, od = orc.merge_lists(f["a_i"], f["a_d"], f["b_i"], f["b_d"])
+    np.testing.assert_array_equal(on, f["out_i"])
+    np.testing.assert_array_equal(od, f["out_d"])
+
+
+def test_exact_knn_matches_reference(golden):
+    f = golden("exact_knn.npz")
+    X, k = f["X"], int(f["k"])
+    ids, dist = orc.exact_knn(X, np.arange(X.shape[0]), k)
+    np.testing.assert_allclose(dist, f["dists"], rtol=1e-4, atol=1e-4)
+    ok = (ids == f["ids"]) | _near_tie_mask(f["dists"], 1e-4)
+    assert ok.all()
+
+
+# ---------------------------------------------------------------- host logic
+def test_csr_membership_rows():
+    top2 = np.array([[1, 0], [0, 2], [2, 1], [1, 2]])
+    offsets, members, mem_row = orc.build_csr(top2, 3)
+    assert offsets.tolist() == [0, 2, 5, 8]
+    assert members.tolist() == [0, 1, 0, 2, 3, 1, 2, 3]
+    # column 0 is the lower bucket id
+    for p in range(4):
+        b_lo, b_hi = sorted(top2[p])
+        assert offsets[b_lo] <= mem_row[p, 0] < offsets[b_lo + 1]
+        assert offsets[b_hi] <= mem_row[p, 1] < offsets[b_hi + 1]
+        assert members[mem_row[p, 0]] == p and members[mem_row[p, 1]] == p
+
+
+def test_kmeans_sample_is_stratified():
+    ids = orc.kmeans_sample_ids(1000, 100, seed=3)
+    assert ids.shape == (100,)
+    assert np.all((ids >= np.arange(100) * 10) & (ids < np.arange(1, 101) * 10))
+    np.testing.assert_array_equal(ids, orc.kmeans_sample_ids(1000, 100, seed=3))
