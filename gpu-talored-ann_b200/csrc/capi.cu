@@ -1,0 +1,771 @@
+// capi.cu -- host orchestration of the bucketed kNN / CAGRA build and the C ABI of libgta.
+//
+// The pipeline mirrors the reference's bucket2 GPU-resident path
+// (bucketDemo/buildBucket/src/bucket.cu:8523 run_pipeline_impl): centroids,
+// bucket assignment, per-bucket kNN, merge, then CAGRA optimize.  Every stage
+// runs on the GPU; there is no CPU fallback.  Host code only sequences
+// launches, builds the per-CTA work list from the bucket sizes, and moves the
+// caller's host buffers.
+#include <algorithm>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <numeric>
+#include <string>
+#include <vector>
+
+#include "../../include/gta.h"
+#include "gta_internal.h"
+#include "prof.h"
+
+#include <atomic>
+#include <mutex>
+
+namespace gta {
+
+namespace {
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+std::vector<ProfRecord> g_prof;
+
+void prof_clear()
+{
+    for (auto& r : g_prof) {
+        if (r.start) cudaEventDestroy(r.start);
+        if (r.stop) cudaEventDestroy(r.stop);
+        if (r.counters) cudaFree(r.counters);
+    }
+    g_prof.clear();
+}
+}  // namespace
+
+bool prof_enabled() { return g_prof_on; }
+namespace {
+std::atomic<long long> g_launches{0};
+}
+void count_launches(long long n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+void prof_push(ProfRecord&& r)
+{
+    std::lock_guard<std::mutex> g(g_prof_mu);
+    g_prof.push_back(std::move(r));
+}
+
+namespace {
+
+thread_local std::string g_err;
+
+template <typename F>
+int guard(F&& f)
+{
+    try {
+        f();
+        return kOk;
+    } catch (const Error& e) {
+        g_err = e.what();
+        return e.code;
+    } catch (const std::bad_alloc&) {
+        g_err = "host out of memory";
+        return kNoMem;
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return kInvalid;
+    }
+}
+
+// Keep memory freed by the stream-ordered allocator cached in the device's default pool, so the
+// per-call scratch of repeated builds is not returned to and re-mapped from the driver each time.
+void keep_pool_memory()
+{
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return;
+    static std::mutex mu;
+    static std::vector<int> done;
+    std::lock_guard<std::mutex> g(mu);
+    for (int x : done) if (x == dev) return;
+    cudaMemPool_t pool;
+    if (cudaDeviceGetDefaultMemPool(&pool, dev) == cudaSuccess) {
+        uint64_t thr = UINT64_MAX;
+        cudaMemPoolSetAttribute(pool, cudaMemPoolAttrReleaseThreshold, &thr);
+    }
+    done.push_back(dev);
+}
+
+inline cudaStream_t S(void* s)
+{
+    keep_pool_memory();
+    return static_cast<cudaStream_t>(s);
+}
+
+int pad_dim(int d, int elem) { const int q = elem == kElemBF16 ? 64 : 32; return (d + q - 1) / q * q; }
+
+int elem_size(int dtype) { return dtype == GTA_F32 ? 4 : 1; }
+
+// 8-bit rows are exact in bf16, and with 2*d*max|x|^2 < 2^24 every product,
+// partial sum and distance of the fused epilogue is an exact fp32 integer.
+bool exact_bf16(int dtype, int d)
+{
+    if (dtype == GTA_U8) return 2.0 * d * 255.0 * 255.0 < 16777216.0;
+    if (dtype == GTA_I8) return 2.0 * d * 128.0 * 128.0 < 16777216.0;
+    return false;
+}
+
+void copy_rows_padded(float* dst, int d_pad, const float* src, int d, int64_t n, bool src_dev, cudaStream_t st)
+{
+    GTA_CUDA(cudaMemsetAsync(dst, 0, sizeof(float) * static_cast<size_t>(n) * d_pad, st));
+    GTA_CUDA(cudaMemcpy2DAsync(dst, sizeof(float) * d_pad, src, sizeof(float) * d, sizeof(float) * d, n,
+                               src_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st));
+}
+
+void unpad_rows(float* dst, int d, const float* src, int d_pad, int64_t n, bool dst_dev, cudaStream_t st)
+{
+    GTA_CUDA(cudaMemcpy2DAsync(dst, sizeof(float) * d, src, sizeof(float) * d_pad, sizeof(float) * d, n,
+                               dst_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st));
+}
+
+template <typename T>
+DevBuf<T> upload(const std::vector<T>& h, cudaStream_t st)
+{
+    DevBuf<T> d(h.size(), st);
+    if (!h.empty()) GTA_CUDA(cudaMemcpyAsync(d.get(), h.data(), sizeof(T) * h.size(), cudaMemcpyHostToDevice, st));
+    return d;
+}
+
+// ---------------------------------------------------------------- stages
+
+// Top-k nearest rows of C (B x d_pad, norms cn) for rows of Xp (n x d_pad, norms xn).
+void assign_topk_impl(const float* Xp, const float* xn, int64_t n, int d, int d_pad, const float* Cp, const float* cn,
+                      int B, int k, int32_t* ids, float* dists, int* err, cudaStream_t st)
+{
+    GTA_REQUIRE(k >= 1 && k <= B, kInvalid, "assign: need 1 <= k <= B");
+    std::vector<WorkItem> wl;
+    wl.reserve(static_cast<size_t>((n + 127) / 128));
+    for (int64_t r = 0; r < n; r += 128)
+        wl.push_back(WorkItem{static_cast<int32_t>(r), static_cast<int32_t>(std::min<int64_t>(128, n - r)), 0, B, -1, 0, 0, 0});
+    auto work = upload(wl, st);
+    DistTopkProblem pr;
+    pr.A = Xp; pr.a_total = n; pr.B = Cp; pr.b_total = B; pr.elem = kElemF32; pr.d = d; pr.d_pad = d_pad;
+    pr.a_norm = xn; pr.b_norm = cn; pr.b_gid = nullptr; pr.work = work.get(); pr.n_work = static_cast<int>(wl.size());
+    pr.m_out = k; pr.exclude_self = false; pr.out_ids = ids; pr.out_dists = dists; pr.err = err;
+    pr.prof_name = "dist_topk_assign";
+    pr.flops = 2.0 * static_cast<double>(n) * B * d;
+    dist_topk(pr, st);
+}
+
+void kmeans_fit_impl(const float* Xs, const float* xn, int64_t n_s, int d, int d_pad, float* C, float* cn, int B,
+                     int iters, int32_t* assign_out, int* err, cudaStream_t st)
+{
+    DevBuf<int32_t> ids(static_cast<size_t>(n_s), st);
+    DevBuf<float> dd(static_cast<size_t>(n_s), st);
+    DevBuf<float> C2(static_cast<size_t>(B) * d_pad, st);
+    for (int it = 0; it < iters; ++it) {
+        assign_topk_impl(Xs, xn, n_s, d, d_pad, C, cn, B, 1, ids.get(), dd.get(), err, st);
+        centroid_update(Xs, n_s, d, d_pad, ids.get(), C, B, C2.get(), cn, st);
+        GTA_CUDA(cudaMemcpyAsync(C, C2.get(), sizeof(float) * static_cast<size_t>(B) * d_pad, cudaMemcpyDeviceToDevice, st));
+    }
+    if (assign_out) {
+        assign_topk_impl(Xs, xn, n_s, d, d_pad, C, cn, B, 1, ids.get(), dd.get(), err, st);
+        GTA_CUDA(cudaMemcpyAsync(assign_out, ids.get(), sizeof(int32_t) * n_s, cudaMemcpyDeviceToDevice, st));
+    }
+}
+
+// Per-bucket all-pairs top-M for every membership row.
+void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* members, const int64_t* offsets_dev,
+                     int B, int M, int32_t* list_ids, float* list_dists, int* err, cudaStream_t st)
+{
+    (void)n;
+    std::vector<int64_t> off(static_cast<size_t>(B) + 1);
+    GTA_CUDA(cudaMemcpyAsync(off.data(), offsets_dev, sizeof(int64_t) * (B + 1), cudaMemcpyDeviceToHost, st));
+    GTA_CUDA(cudaStreamSynchronize(st));
+    const int64_t n_mem = off[B];
+    if (n_mem == 0) return;
+    GTA_REQUIRE(n_mem < (1ll << 31), kInvalid, "bucket_knn: too many memberships on one device");
+    const int elem = exact_bf16(dtype, d) ? kElemBF16 : kElemF32;
+    const int d_pad = pad_dim(d, elem);
+    DevBuf<uint8_t> pool(static_cast<size_t>(n_mem) * d_pad * (elem == kElemBF16 ? 2 : 4), st);
+    DevBuf<float> pnorm(static_cast<size_t>(n_mem), st);
+    {
+        ProfScope prof("gather", static_cast<double>(n_mem) * (d * elem_size(dtype) + d_pad * (elem == kElemBF16 ? 2 : 4)), st);
+        convert_rows(X, dtype, d, members, n_mem, pool.get(), elem, d_pad, pnorm.get(), st);
+    }
+    // work list: one CTA per 128-row tile of a bucket, largest buckets first
+    std::vector<int> order(static_cast<size_t>(B));
+    std::iota(order.begin(), order.end(), 0);
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return off[a + 1] - off[a] > off[b + 1] - off[b]; });
+    std::vector<WorkItem> wl;
+    for (int b : order) {
+        const int64_t lo = off[b], nb = off[b + 1] - off[b];
+        for (int64_t t = 0; t < nb; t += 128)
+            wl.push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, nb - t)),
+                                  static_cast<int32_t>(lo), static_cast<int32_t>(nb), static_cast<int32_t>(t), 0, 0, 0});
+    }
+    auto work = upload(wl, st);
+    DistTopkProblem pr;
+    pr.A = pool.get(); pr.a_total = n_mem; pr.B = pool.get(); pr.b_total = n_mem; pr.elem = elem; pr.d = d;
+    pr.d_pad = d_pad; pr.a_norm = pnorm.get(); pr.b_norm = pnorm.get(); pr.b_gid = members; pr.work = work.get();
+    pr.n_work = static_cast<int>(wl.size()); pr.m_out = M; pr.exclude_self = true; pr.out_ids = list_ids;
+    pr.out_dists = list_dists; pr.err = err;
+    pr.prof_name = "dist_topk_bucket";
+    for (int b = 0; b < B; ++b) {
+        const double nb = static_cast<double>(off[b + 1] - off[b]);
+        pr.flops += 2.0 * nb * nb * d;
+    }
+    dist_topk(pr, st);
+}
+
+struct BucketOut {
+    int32_t* ids;      // device [N x M]
+    float* dists;      // device [N x M]
+    float* centroids;  // device [B x d] or null
+    int32_t* top2;     // device [N x 2] or null
+};
+
+void build_bucket_impl(const gta_dataset& ds, const gta_bucket_params& p, const BucketOut& o, cudaStream_t st)
+{
+    const int64_t N = ds.n;
+    const int d = ds.d;
+    const int B = p.n_buckets;
+    const int M = p.knn_degree;
+    GTA_REQUIRE(ds.data && N >= 2 && d >= 1, kInvalid, "build_bucket: empty dataset");
+    GTA_REQUIRE(ds.dtype == GTA_F32 || ds.dtype == GTA_U8 || ds.dtype == GTA_I8, kInvalid, "build_bucket: bad dtype");
+    GTA_REQUIRE(B >= 2 && B <= N, kInvalid, "build_bucket: need 2 <= n_buckets <= N (2-way membership)");
+    GTA_REQUIRE(M >= 1 && M <= 128, kInvalid, "build_bucket: knn_degree must be in [1, 128]");
+    GTA_REQUIRE(N < (1ll << 30), kInvalid, "build_bucket: N must be below 2^30 per device");
+    GTA_REQUIRE(p.kmeans_iters >= 0, kInvalid, "build_bucket: negative kmeans_iters");
+
+    DevBuf<int> err(1, st);
+    GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+    ProfScope prof_all("build_bucket_total", 0.0, st);
+
+    // dataset on the device in its own element type
+    DevBuf<uint8_t> xhold;
+    const void* X = ds.data;
+    const size_t xbytes = static_cast<size_t>(N) * d * elem_size(ds.dtype);
+    if (!ds.on_device) {
+        xhold = DevBuf<uint8_t>(xbytes, st);
+        GTA_CUDA(cudaMemcpyAsync(xhold.get(), ds.data, xbytes, cudaMemcpyHostToDevice, st));
+        X = xhold.get();
+    }
+    const int d32 = pad_dim(d, kElemF32);
+
+    // ---- k-means over a sample
+    int64_t n_s = p.kmeans_sample > 0 ? std::min<int64_t>(p.kmeans_sample, N)
+                                      : std::max<int64_t>(1, std::llround(std::min(0.1, 1e7 / double(N)) * double(N)));
+    n_s = std::max<int64_t>(n_s, B);
+    DevBuf<int32_t> sid(static_cast<size_t>(n_s), st);
+    sample_ids(N, n_s, p.seed, sid.get(), st);
+    DevBuf<float> Xs(static_cast<size_t>(n_s) * d32, st), xs_n(static_cast<size_t>(n_s), st);
+    {
+        ProfScope prof("sample_gather", static_cast<double>(n_s) * (d * elem_size(ds.dtype) + d32 * 4.0), st);
+        convert_rows(X, ds.dtype, d, sid.get(), n_s, Xs.get(), kElemF32, d32, xs_n.get(), st);
+    }
+    sid.release();
+    DevBuf<float> C(static_cast<size_t>(B) * d32, st), cn(static_cast<size_t>(B), st);
+    if (p.init_centroids) {
+        copy_rows_padded(C.get(), d32, p.init_centroids, d, B, p.init_on_device != 0, st);
+    } else {
+        const int ratio = B <= 1024 ? 20 : std::max(2, 20 * 1024 / B);
+        const int64_t pool_n = std::min<int64_t>(n_s, static_cast<int64_t>(ratio) * B);
+        ProfScope prof("kmeans_init", 0.0, st);
+        kmeanspp_init(Xs.get(), xs_n.get(), pool_n, d, d32, B, p.seed, C.get(), err.get(), st);
+    }
+    convert_rows(C.get(), GTA_F32, d32, nullptr, B, nullptr, kElemF32, d32, cn.get(), st);
+    {
+        ProfScope prof("kmeans_fit_total", 0.0, st);
+        kmeans_fit_impl(Xs.get(), xs_n.get(), n_s, d, d32, C.get(), cn.get(), B, p.kmeans_iters, nullptr, err.get(), st);
+    }
+    Xs.release();
+    xs_n.release();
+    if (o.centroids) unpad_rows(o.centroids, d, C.get(), d32, B, true, st);
+
+    // ---- top-2 bucket membership of every point
+    DevBuf<int32_t> top2(static_cast<size_t>(N) * 2, st);
+    {
+        ProfScope prof("top2_total", 0.0, st);
+        DevBuf<float> Xf(static_cast<size_t>(N) * d32, st), xn(static_cast<size_t>(N), st), t2d(static_cast<size_t>(N) * 2, st);
+        {
+            ProfScope prof("convert_x", static_cast<double>(N) * (d * elem_size(ds.dtype) + d32 * 4.0), st);
+            convert_rows(X, ds.dtype, d, nullptr, N, Xf.get(), kElemF32, d32, xn.get(), st);
+        }
+        assign_topk_impl(Xf.get(), xn.get(), N, d, d32, C.get(), cn.get(), B, 2, top2.get(), t2d.get(), err.get(), st);
+    }
+    if (o.top2) GTA_CUDA(cudaMemcpyAsync(o.top2, top2.get(), sizeof(int32_t) * 2 * N, cudaMemcpyDeviceToDevice, st));
+    DevBuf<int32_t> members(static_cast<size_t>(N) * 2, st);
+    DevBuf<int64_t> offsets(static_cast<size_t>(B) + 1, st), mem_row(static_cast<size_t>(N) * 2, st);
+    build_memberships(top2.get(), N, B, members.get(), offsets.get(), mem_row.get(), st);
+    top2.release();
+
+    // ---- per-bucket all-pairs kNN, then merge each point's two lists
+    DevBuf<int32_t> lid(static_cast<size_t>(N) * 2 * M, st);
+    DevBuf<float> ldist(static_cast<size_t>(N) * 2 * M, st);
+    {
+        ProfScope prof("bucket_knn_total", 0.0, st);
+        bucket_knn_impl(X, ds.dtype, N, d, members.get(), offsets.get(), B, M, lid.get(), ldist.get(), err.get(), st);
+    }
+    merge_memberships(lid.get(), ldist.get(), mem_row.get(), N, M, o.ids, o.dists, st);
+    check_device_error(err.get(), st, "build_bucket");
+}
+
+void optimize_impl(const uint32_t* knn_dev, int64_t n, int m, int k, uint32_t* graph_dev, cudaStream_t st,
+                   const int32_t* order = nullptr)
+{
+    GTA_REQUIRE(n >= 2 && m >= 2 && m <= 128 && k >= 1 && k <= m, kInvalid, "optimize: need n >= 2, 1 <= K <= M <= 128");
+    DevBuf<int> err(1, st);
+    GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+    DevBuf<uint32_t> pruned(static_cast<size_t>(n) * k, st);
+    ProfScope prof_all("optimize_total", 0.0, st);
+    prune_detour(knn_dev, n, m, k, order, pruned.get(), err.get(), st);
+    reverse_merge(pruned.get(), n, k, graph_dev, err.get(), st);
+    check_device_error(err.get(), st, "optimize");
+}
+
+// ---------------------------------------------------------------- files
+enum { kFileF32 = 0, kFileU8 = 1, kFileI8 = 2 };
+
+int dtype_from_path(const std::string& path)
+{
+    auto ends = [&](const char* s) {
+        const size_t n = std::strlen(s);
+        return path.size() >= n && path.compare(path.size() - n, n, s) == 0;
+    };
+    if (ends(".u8bin")) return GTA_U8;
+    if (ends(".i8bin")) return GTA_I8;
+    if (ends(".fbin") || ends(".bin")) return GTA_F32;
+    throw Error(kInvalid, "unsupported dataset extension: " + path);
+}
+
+void read_exact(std::ifstream& in, void* dst, size_t bytes, const std::string& what)
+{
+    in.read(static_cast<char*>(dst), static_cast<std::streamsize>(bytes));
+    GTA_REQUIRE(in.good() || (in.eof() && static_cast<size_t>(in.gcount()) == bytes), kData, "short read: " + what);
+}
+
+template <typename HdrN, typename T>
+void write_table(const char* path, HdrN n, int32_t m, const T* data)
+{
+    std::ofstream out(path, std::ios::binary | std::ios::trunc);
+    GTA_REQUIRE(out.is_open(), kInvalid, std::string("cannot open for writing: ") + path);
+    out.write(reinterpret_cast<const char*>(&n), sizeof(n));
+    out.write(reinterpret_cast<const char*>(&m), sizeof(m));
+    out.write(reinterpret_cast<const char*>(data), static_cast<std::streamsize>(sizeof(T) * static_cast<size_t>(n) * m));
+    GTA_REQUIRE(out.good(), kData, std::string("write failed: ") + path);
+}
+
+void read_table_header(const char* path, int64_t* n, int32_t* m)
+{
+    std::ifstream in(path, std::ios::binary);
+    GTA_REQUIRE(in.is_open(), kInvalid, std::string("cannot open: ") + path);
+    int64_t nn = 0;
+    int32_t mm = 0;
+    read_exact(in, &nn, sizeof(nn), path);
+    read_exact(in, &mm, sizeof(mm), path);
+    GTA_REQUIRE(nn > 0 && mm > 0, kData, std::string("invalid header: ") + path);
+    in.seekg(0, std::ios::end);
+    const int64_t want = 12 + nn * static_cast<int64_t>(mm) * 4;
+    GTA_REQUIRE(static_cast<int64_t>(in.tellg()) >= want, kData, std::string("truncated file: ") + path);
+    *n = nn;
+    *m = mm;
+}
+
+template <typename T>
+void read_table(const char* path, T* out)
+{
+    int64_t n = 0;
+    int32_t m = 0;
+    read_table_header(path, &n, &m);
+    std::ifstream in(path, std::ios::binary);
+    in.seekg(12);
+    read_exact(in, out, sizeof(T) * static_cast<size_t>(n) * m, path);
+}
+
+}  // namespace
+}  // namespace gta
+
+using namespace gta;
+
+extern "C" {
+
+const char* gta_last_error(void) { return g_err.c_str(); }
+
+int gta_profile_enable(int32_t on)
+{
+    return guard([&] {
+        std::lock_guard<std::mutex> g(g_prof_mu);
+        prof_clear();
+        g_prof_on = on != 0;
+    });
+}
+
+long long gta_launch_count(void) { return g_launches.load(); }
+
+int gta_profile_counters(int32_t i, double* out, int32_t n)
+{
+    return guard([&] {
+        std::lock_guard<std::mutex> g(g_prof_mu);
+        GTA_REQUIRE(i >= 0 && i < static_cast<int32_t>(g_prof.size()), kInvalid, "gta_profile_counters: index out of range");
+        const ProfRecord& r = g_prof[static_cast<size_t>(i)];
+        std::vector<unsigned long long> h(static_cast<size_t>(r.n_counters));
+        if (r.counters) {
+            GTA_CUDA(cudaEventSynchronize(r.stop));
+            GTA_CUDA(cudaMemcpy(h.data(), r.counters, sizeof(unsigned long long) * h.size(), cudaMemcpyDeviceToHost));
+        }
+        for (int32_t k = 0; k < n; ++k) out[k] = k < r.n_counters ? static_cast<double>(h[static_cast<size_t>(k)]) : 0.0;
+    });
+}
+
+int gta_profile_count(void)
+{
+    std::lock_guard<std::mutex> g(g_prof_mu);
+    return static_cast<int>(g_prof.size());
+}
+
+int gta_profile_get(int32_t i, char* name, int32_t name_len, float* ms, double* units)
+{
+    return guard([&] {
+        std::lock_guard<std::mutex> g(g_prof_mu);
+        GTA_REQUIRE(i >= 0 && i < static_cast<int32_t>(g_prof.size()), kInvalid, "gta_profile_get: index out of range");
+        const ProfRecord& r = g_prof[static_cast<size_t>(i)];
+        GTA_CUDA(cudaEventSynchronize(r.stop));
+        float t = 0.0f;
+        GTA_CUDA(cudaEventElapsedTime(&t, r.start, r.stop));
+        if (ms) *ms = t;
+        if (units) *units = r.units;
+        if (name && name_len > 0) {
+            std::strncpy(name, r.name.c_str(), static_cast<size_t>(name_len - 1));
+            name[name_len - 1] = 0;
+        }
+    });
+}
+const char* gta_version(void) { return "gta-b200 0.1 (sm_100a)"; }
+
+int gta_build_bucket(const gta_dataset* ds, const gta_bucket_params* p, int32_t* knn_ids, float* knn_dists, void* stream)
+{
+    return guard([&] {
+        GTA_REQUIRE(ds && p && knn_ids, kInvalid, "gta_build_bucket: null argument");
+        cudaStream_t st = S(stream);
+        const int64_t N = ds->n;
+        const int M = p->knn_degree;
+        const size_t nm = static_cast<size_t>(N) * (M > 0 ? M : 0);
+        BucketOut o{};
+        DevBuf<int32_t> ids;
+        DevBuf<float> dists, cent;
+        DevBuf<int32_t> t2;
+        if (p->out_on_device) {
+            o.ids = knn_ids;
+            if (knn_dists) o.dists = knn_dists;
+            else { dists = DevBuf<float>(nm, st); o.dists = dists.get(); }
+            o.centroids = p->centroids_out;
+            o.top2 = p->top2_out;
+        } else {
+            ids = DevBuf<int32_t>(nm, st);
+            dists = DevBuf<float>(nm, st);
+            o.ids = ids.get();
+            o.dists = dists.get();
+            if (p->centroids_out) { cent = DevBuf<float>(static_cast<size_t>(p->n_buckets) * ds->d, st); o.centroids = cent.get(); }
+            if (p->top2_out) { t2 = DevBuf<int32_t>(static_cast<size_t>(N) * 2, st); o.top2 = t2.get(); }
+        }
+        build_bucket_impl(*ds, *p, o, st);
+        if (!p->out_on_device) {
+            GTA_CUDA(cudaMemcpyAsync(knn_ids, o.ids, sizeof(int32_t) * nm, cudaMemcpyDeviceToHost, st));
+            if (knn_dists) GTA_CUDA(cudaMemcpyAsync(knn_dists, o.dists, sizeof(float) * nm, cudaMemcpyDeviceToHost, st));
+            if (p->centroids_out)
+                GTA_CUDA(cudaMemcpyAsync(p->centroids_out, o.centroids, sizeof(float) * p->n_buckets * ds->d,
+                                         cudaMemcpyDeviceToHost, st));
+            if (p->top2_out)
+                GTA_CUDA(cudaMemcpyAsync(p->top2_out, o.top2, sizeof(int32_t) * 2 * N, cudaMemcpyDeviceToHost, st));
+            GTA_CUDA(cudaStreamSynchronize(st));
+        }
+    });
+}
+
+int gta_optimize(const uint32_t* knn, int64_t n, int32_t m, int32_t k, uint32_t* graph, int32_t on_device, void* stream)
+{
+    return guard([&] {
+        GTA_REQUIRE(knn && graph, kInvalid, "gta_optimize: null argument");
+        cudaStream_t st = S(stream);
+        if (on_device) {
+            optimize_impl(knn, n, m, k, graph, st);
+        } else {
+            DevBuf<uint32_t> kd(static_cast<size_t>(n) * m, st), gd(static_cast<size_t>(n) * k, st);
+            GTA_CUDA(cudaMemcpyAsync(kd.get(), knn, sizeof(uint32_t) * n * m, cudaMemcpyHostToDevice, st));
+            optimize_impl(kd.get(), n, m, k, gd.get(), st);
+            GTA_CUDA(cudaMemcpyAsync(graph, gd.get(), sizeof(uint32_t) * n * k, cudaMemcpyDeviceToHost, st));
+            GTA_CUDA(cudaStreamSynchronize(st));
+        }
+    });
+}
+
+int gta_build_cagra(const gta_dataset* ds, const gta_cagra_params* p, uint32_t* graph, void* stream)
+{
+    return guard([&] {
+        GTA_REQUIRE(ds && p && graph, kInvalid, "gta_build_cagra: null argument");
+        cudaStream_t st = S(stream);
+        const int64_t N = ds->n;
+        const int M = p->bucket.knn_degree, K = p->graph_degree;
+        GTA_REQUIRE(K >= 1 && K <= M, kInvalid, "gta_build_cagra: need 1 <= graph_degree <= knn_degree");
+        DevBuf<int32_t> ids(static_cast<size_t>(N) * M, st), t2;
+        DevBuf<float> dists(static_cast<size_t>(N) * M, st), cent;
+        BucketOut o{ids.get(), dists.get(), nullptr, nullptr};
+        const bool dev = p->bucket.out_on_device != 0;
+        if (p->bucket.centroids_out) {
+            if (dev) o.centroids = p->bucket.centroids_out;
+            else { cent = DevBuf<float>(static_cast<size_t>(p->bucket.n_buckets) * ds->d, st); o.centroids = cent.get(); }
+        }
+        if (p->bucket.top2_out && dev) o.top2 = p->bucket.top2_out;
+        else { t2 = DevBuf<int32_t>(static_cast<size_t>(N) * 2, st); o.top2 = t2.get(); }
+        build_bucket_impl(*ds, p->bucket, o, st);
+        DevBuf<int32_t> order(static_cast<size_t>(N), st);
+        locality_order(o.top2, N, p->bucket.n_buckets, order.get(), st);
+        dists.release();
+        DevBuf<uint32_t> san(static_cast<size_t>(N) * M, st);
+        sanitize(ids.get(), N, M, san.get(), st);
+        ids.release();
+        DevBuf<uint32_t> gd;
+        uint32_t* gout = graph;
+        if (!dev) { gd = DevBuf<uint32_t>(static_cast<size_t>(N) * K, st); gout = gd.get(); }
+        optimize_impl(san.get(), N, M, K, gout, st, order.get());
+        if (!dev) {
+            GTA_CUDA(cudaMemcpyAsync(graph, gout, sizeof(uint32_t) * N * K, cudaMemcpyDeviceToHost, st));
+            if (p->bucket.centroids_out)
+                GTA_CUDA(cudaMemcpyAsync(p->bucket.centroids_out, o.centroids, sizeof(float) * p->bucket.n_buckets * ds->d,
+                                         cudaMemcpyDeviceToHost, st));
+            if (p->bucket.top2_out)
+                GTA_CUDA(cudaMemcpyAsync(p->bucket.top2_out, o.top2, sizeof(int32_t) * 2 * N, cudaMemcpyDeviceToHost, st));
+            GTA_CUDA(cudaStreamSynchronize(st));
+        }
+    });
+}
+
+int gta_kmeans_fit(const float* X, int64_t n, int32_t d, float* centroids, int32_t B, int32_t iters,
+                   int32_t* assign_out, void* stream)
+{
+    return guard([&] {
+        GTA_REQUIRE(X && centroids && n >= 1 && d >= 1 && B >= 1 && iters >= 0, kInvalid, "gta_kmeans_fit: bad argument");
+        cudaStream_t st = S(stream);
+        const int d32 = pad_dim(d, kElemF32);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        DevBuf<float> Xp(static_cast<size_t>(n) * d32, st), xn(static_cast<size_t>(n), st);
+        convert_rows(X, GTA_F32, d, nullptr, n, Xp.get(), kElemF32, d32, xn.get(), st);
+        DevBuf<float> C(static_cast<size_t>(B) * d32, st), cn(static_cast<size_t>(B), st);
+        copy_rows_padded(C.get(), d32, centroids, d, B, true, st);
+        convert_rows(C.get(), GTA_F32, d32, nullptr, B, nullptr, kElemF32, d32, cn.get(), st);
+        kmeans_fit_impl(Xp.get(), xn.get(), n, d, d32, C.get(), cn.get(), B, iters, assign_out, err.get(), st);
+        unpad_rows(centroids, d, C.get(), d32, B, true, st);
+        check_device_error(err.get(), st, "gta_kmeans_fit");
+    });
+}
+
+int gta_kmeans_init(const float* X, int64_t pool_n, int32_t d, int32_t B, uint64_t seed, float* centroids, void* stream)
+{
+    return guard([&] {
+        GTA_REQUIRE(X && centroids && pool_n >= 1 && d >= 1 && B >= 1, kInvalid, "gta_kmeans_init: bad argument");
+        cudaStream_t st = S(stream);
+        const int d32 = pad_dim(d, kElemF32);
+        DevBuf<float> Xp(static_cast<size_t>(pool_n) * d32, st), C(static_cast<size_t>(B) * d32, st);
+        convert_rows(X, GTA_F32, d, nullptr, pool_n, Xp.get(), kElemF32, d32, nullptr, st);
+        kmeanspp_init(Xp.get(), nullptr, pool_n, d, d32, B, seed, C.get(), nullptr, st);
+        unpad_rows(centroids, d, C.get(), d32, B, true, st);
+        GTA_CUDA(cudaStreamSynchronize(st));
+    });
+}
+
+int gta_assign_topk(const float* X, int64_t n, int32_t d, const float* C, int32_t B, int32_t k, int32_t* ids,
+                    float* dists, void* stream)
+{
+    return guard([&] {
+        GTA_REQUIRE(X && C && ids && dists && n >= 1 && d >= 1 && B >= 1, kInvalid, "gta_assign_topk: bad argument");
+        cudaStream_t st = S(stream);
+        const int d32 = pad_dim(d, kElemF32);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        DevBuf<float> Xp(static_cast<size_t>(n) * d32, st), xn(static_cast<size_t>(n), st);
+        DevBuf<float> Cp(static_cast<size_t>(B) * d32, st), cn(static_cast<size_t>(B), st);
+        convert_rows(X, GTA_F32, d, nullptr, n, Xp.get(), kElemF32, d32, xn.get(), st);
+        convert_rows(C, GTA_F32, d, nullptr, B, Cp.get(), kElemF32, d32, cn.get(), st);
+        assign_topk_impl(Xp.get(), xn.get(), n, d, d32, Cp.get(), cn.get(), B, k, ids, dists, err.get(), st);
+        check_device_error(err.get(), st, "gta_assign_topk");
+    });
+}
+
+int gta_build_memberships(const int32_t* top2, int64_t n, int32_t B, int32_t* members, int64_t* offsets,
+                          int64_t* mem_row, void* stream)
+{
+    return guard([&] {
+        GTA_REQUIRE(top2 && members && offsets && mem_row && n >= 1 && B >= 2, kInvalid, "gta_build_memberships: bad argument");
+        build_memberships(top2, n, B, members, offsets, mem_row, S(stream));
+    });
+}
+
+int gta_bucket_knn(const void* X, int32_t dtype, int64_t n, int32_t d, const int32_t* members, const int64_t* offsets,
+                   int32_t B, int32_t M, int32_t* list_ids, float* list_dists, void* stream)
+{
+    return guard([&] {
+        GTA_REQUIRE(X && members && offsets && list_ids && list_dists && B >= 1 && M >= 1 && M <= 128, kInvalid,
+                    "gta_bucket_knn: bad argument");
+        cudaStream_t st = S(stream);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        bucket_knn_impl(X, dtype, n, d, members, offsets, B, M, list_ids, list_dists, err.get(), st);
+        check_device_error(err.get(), st, "gta_bucket_knn");
+    });
+}
+
+int gta_merge_memberships(const int32_t* list_ids, const float* list_dists, const int64_t* mem_row, int64_t n,
+                          int32_t M, int32_t* out_ids, float* out_dists, void* stream)
+{
+    return guard([&] {
+        GTA_REQUIRE(list_ids && list_dists && mem_row && out_ids && out_dists, kInvalid, "gta_merge_memberships: null argument");
+        merge_memberships(list_ids, list_dists, mem_row, n, M, out_ids, out_dists, S(stream));
+    });
+}
+
+int gta_merge_lists(const int32_t* run_ids, const float* run_dists, const int32_t* new_ids, const float* new_dists,
+                    int64_t n, int32_t M, int32_t* out_ids, float* out_dists, void* stream)
+{
+    return guard([&] {
+        GTA_REQUIRE(run_ids && run_dists && new_ids && new_dists && out_ids && out_dists, kInvalid,
+                    "gta_merge_lists: null argument");
+        merge_lists(run_ids, run_dists, new_ids, new_dists, n, M, out_ids, out_dists, S(stream));
+    });
+}
+
+int gta_sanitize(const int32_t* knn, int64_t n, int32_t m, uint32_t* out, void* stream)
+{
+    return guard([&] {
+        GTA_REQUIRE(knn && out && n >= 1 && m >= 1, kInvalid, "gta_sanitize: bad argument");
+        sanitize(knn, n, m, out, S(stream));
+    });
+}
+
+int gta_sort_rows(const float* X, int64_t n, int32_t d, const int32_t* knn, int32_t m, int32_t* out, void* stream)
+{
+    return guard([&] {
+        GTA_REQUIRE(X && knn && out && n >= 1 && d >= 1, kInvalid, "gta_sort_rows: bad argument");
+        cudaStream_t st = S(stream);
+        const int d32 = pad_dim(d, kElemF32);
+        DevBuf<float> Xp(static_cast<size_t>(n) * d32, st);
+        convert_rows(X, GTA_F32, d, nullptr, n, Xp.get(), kElemF32, d32, nullptr, st);
+        sort_rows_l2(Xp.get(), d, d32, knn, n, m, out, st);
+        GTA_CUDA(cudaStreamSynchronize(st));
+    });
+}
+
+int gta_prune(const uint32_t* knn, int64_t n, int32_t m, int32_t k, uint32_t* pruned, void* stream)
+{
+    return guard([&] {
+        GTA_REQUIRE(knn && pruned, kInvalid, "gta_prune: null argument");
+        cudaStream_t st = S(stream);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        prune_detour(knn, n, m, k, nullptr, pruned, err.get(), st);
+        check_device_error(err.get(), st, "gta_prune");
+    });
+}
+
+int gta_reverse_merge(const uint32_t* pruned, int64_t n, int32_t k, uint32_t* out, void* stream)
+{
+    return guard([&] {
+        GTA_REQUIRE(pruned && out && n >= 1, kInvalid, "gta_reverse_merge: bad argument");
+        reverse_merge(pruned, n, k, out, nullptr, S(stream));
+    });
+}
+
+// ---------------------------------------------------------------- files
+int gta_read_dataset_header(const char* path, int64_t* n, int32_t* d, int32_t* dtype)
+{
+    return guard([&] {
+        GTA_REQUIRE(path && n && d && dtype, kInvalid, "gta_read_dataset_header: null argument");
+        const int dt = dtype_from_path(path);
+        std::ifstream in(path, std::ios::binary);
+        GTA_REQUIRE(in.is_open(), kInvalid, std::string("cannot open: ") + path);
+        int32_t hdr[2] = {0, 0};
+        read_exact(in, hdr, sizeof(hdr), path);
+        GTA_REQUIRE(hdr[0] > 0 && hdr[1] > 0, kData, std::string("invalid BIGANN header (N<=0 or D<=0): ") + path);
+        in.seekg(0, std::ios::end);
+        const int64_t want = 8 + static_cast<int64_t>(hdr[0]) * hdr[1] * elem_size(dt);
+        GTA_REQUIRE(static_cast<int64_t>(in.tellg()) >= want, kData, std::string("truncated dataset: ") + path);
+        *n = hdr[0];
+        *d = hdr[1];
+        *dtype = dt;
+    });
+}
+
+int gta_read_dataset(const char* path, int64_t row0, int64_t nrows, void* out)
+{
+    return guard([&] {
+        int64_t n = 0;
+        int32_t d = 0, dt = 0;
+        const int rc = gta_read_dataset_header(path, &n, &d, &dt);
+        if (rc != kOk) throw Error(rc, g_err);
+        GTA_REQUIRE(out && row0 >= 0 && nrows >= 0 && row0 + nrows <= n, kInvalid, "gta_read_dataset: row range out of bounds");
+        std::ifstream in(path, std::ios::binary);
+        const size_t row_bytes = static_cast<size_t>(d) * elem_size(dt);
+        in.seekg(static_cast<std::streamoff>(8 + row0 * static_cast<int64_t>(row_bytes)));
+        read_exact(in, out, row_bytes * static_cast<size_t>(nrows), path);
+    });
+}
+
+int gta_write_dataset(const char* path, const void* data, int64_t n, int32_t d, int32_t dtype)
+{
+    return guard([&] {
+        GTA_REQUIRE(path && data && n > 0 && n < (1ll << 31) && d > 0, kInvalid, "gta_write_dataset: bad argument");
+        std::ofstream out(path, std::ios::binary | std::ios::trunc);
+        GTA_REQUIRE(out.is_open(), kInvalid, std::string("cannot open for writing: ") + path);
+        const int32_t hdr[2] = {static_cast<int32_t>(n), d};
+        out.write(reinterpret_cast<const char*>(hdr), sizeof(hdr));
+        out.write(static_cast<const char*>(data), static_cast<std::streamsize>(static_cast<size_t>(n) * d * elem_size(dtype)));
+        GTA_REQUIRE(out.good(), kData, std::string("write failed: ") + path);
+    });
+}
+
+int gta_write_knn(const char* path, const int32_t* ids, int64_t n, int32_t m)
+{
+    return guard([&] { write_table<int64_t, int32_t>(path, n, m, ids); });
+}
+int gta_write_knn_dists(const char* path, const float* dists, int64_t n, int32_t m)
+{
+    return guard([&] { write_table<int64_t, float>(path, n, m, dists); });
+}
+int gta_read_knn_header(const char* path, int64_t* n, int32_t* m)
+{
+    return guard([&] { read_table_header(path, n, m); });
+}
+int gta_read_knn(const char* path, int32_t* ids) { return guard([&] { read_table<int32_t>(path, ids); }); }
+int gta_write_graph(const char* path, const uint32_t* graph, int64_t n, int32_t k)
+{
+    return guard([&] { write_table<int64_t, uint32_t>(path, n, k, graph); });
+}
+int gta_read_graph_header(const char* path, int64_t* n, int32_t* k)
+{
+    return guard([&] { read_table_header(path, n, k); });
+}
+int gta_read_graph(const char* path, uint32_t* graph) { return guard([&] { read_table<uint32_t>(path, graph); }); }
+
+int gta_write_npy_i64(const char* path, const int32_t* ids, int64_t n, int32_t m)
+{
+    return guard([&] {
+        GTA_REQUIRE(path && ids && n > 0 && m > 0, kInvalid, "gta_write_npy_i64: bad argument");
+        std::string hdr = "{'descr': '<i8', 'fortran_order': False, 'shape': (" + std::to_string(n) + ", " +
+                          std::to_string(m) + "), }";
+        const size_t pre = 10;
+        size_t total = pre + hdr.size() + 1;
+        hdr.append((64 - total % 64) % 64, ' ');
+        hdr.push_back('\n');
+        std::ofstream out(path, std::ios::binary | std::ios::trunc);
+        GTA_REQUIRE(out.is_open(), kInvalid, std::string("cannot open for writing: ") + path);
+        const unsigned char magic[8] = {0x93, 'N', 'U', 'M', 'P', 'Y', 1, 0};
+        out.write(reinterpret_cast<const char*>(magic), 8);
+        const uint16_t hl = static_cast<uint16_t>(hdr.size());
+        out.write(reinterpret_cast<const char*>(&hl), 2);
+        out.write(hdr.data(), static_cast<std::streamsize>(hdr.size()));
+        std::vector<int64_t> row(static_cast<size_t>(m));
+        for (int64_t i = 0; i < n; ++i) {
+            for (int32_t j = 0; j < m; ++j) row[static_cast<size_t>(j)] = ids[i * m + j];
+            out.write(reinterpret_cast<const char*>(row.data()), static_cast<std::streamsize>(sizeof(int64_t) * m));
+        }
+        GTA_REQUIRE(out.good(), kData, std::string("write failed: ") + path);
+    });
+}
+
+}  // extern "C"

@@ -1,0 +1,762 @@
+// dist_topk.cu -- the distance contraction of the bucketed kNN build on sm_100a.
+//
+// One CTA = up to 128 A rows (queries) against a contiguous segment of B rows
+// (the members of one bucket, or all k-means centroids).  Warp roles:
+//   warp 0      TMA producer: 128-row x 128-byte K chunks of B (and of A when
+//               A does not stay resident) into a multi-stage smem ring;
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//               (M=128, N=128, fp32 accumulators, two TMEM buffers so the
+//               MMA of column tile j+1 overlaps the epilogue of tile j);
+//   warps 2..5  epilogue: thread t owns TMEM lane t = A row t; it reads its
+//               row's 128 dot products with tcgen05.ld, forms
+//               s = ||b||^2 - 2 a.b (the squared distance minus the row
+//               constant ||a||^2, the fused ||x||^2+||y||^2-2x.y epilogue),
+//               and keeps the row's best entries in a sorted shared-memory
+//               list fed through a small unsorted buffer.
+// The (rows x segment) score matrix never reaches HBM.
+//
+// Two modes:
+//   exact  (bf16 operands holding 8-bit integer data): every product and
+//          partial sum is an integer below 2^24, so s is exact; the kernel
+//          writes the final top-M (distance, id) lists directly.
+//   screen (f32 operands, kind::tf32): s is approximate with a proven error
+//          bound; the kernel keeps every column whose approximate s is within
+//          the bound of the running M-th, and rerank_kernel recomputes those
+//          candidates with the exact fp32 distance and selects the top-M.
+//
+// Reference behaviour this replaces (paths relative to the reference root):
+//   bucketDemo/buildBucket/src/bucket.cu:5471-5484 (cuBLAS dots per bucket) +
+//   :4102-4267 block_topK_from_dots_kernel (top-M, self excluded, ascending),
+//   :4315-4688 s6 fp16 screen with a strict error bound + exact fp32 rerank,
+//   :1230 / :1379-1490 top-2 centroid assignment with exact rerank.
+// Ordering: ascending (distance, id); the reference's strict-less insertion
+// keeps the earlier candidate on equal distance, which coincides for distinct
+// distances (ties within the stated tolerance may order differently).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cfloat>
+#include <cmath>
+#include <mutex>
+
+#include "common.cuh"
+#include "gta_internal.h"
+#include "prof.h"
+
+namespace gta {
+
+namespace {
+
+constexpr int kTileM = 128;
+constexpr int kTileN = 128;
+constexpr uint32_t kTileBytes = 128u * 128u;  // 128 rows x 128 B
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kSmemMax = 232448;         // 227 KB per CTA (opt-in)
+
+struct DistTopkArgs {
+    const WorkItem* work;
+    const float* a_norm;
+    const float* b_norm;
+    const int32_t* b_gid;
+    const float* b_maxnorm;   // device scalar: max ||b|| (screen margin)
+    int32_t k_chunks;
+    int32_t m_out;
+    int32_t m_sel;
+    int32_t L;
+    int32_t cap;
+    int32_t stages;
+    int32_t a_resident;
+    int32_t screen;
+    float mc1, mc2;           // margin = mc1*|a|*bmax + mc2*(|a|+bmax)^2
+    int32_t* out_ids;
+    float* out_dists;
+    int32_t* cand_cols;       // screen: [a_total x L]
+    int32_t* cand_n;          // screen: [a_total], -1 = list overflowed
+    unsigned long long* stats;// optional: [passes, flush events, rows]
+    int* err;
+    uint32_t list_off, buf_off, pn_off, bar_off;
+};
+
+constexpr int kBuf = 32;                  // per-row staging buffer (entries)
+constexpr uint64_t kEmptyKey = ~0ull;     // list sentinel (its high half decodes to NaN, never a real key)
+
+__device__ __forceinline__ void cmp_swap(uint64_t& a, uint64_t& b)
+{
+    const uint64_t lo = a < b ? a : b, hi = a < b ? b : a;
+    a = lo;
+    b = hi;
+}
+
+// Bitonic sort of 32 keys held in registers, ascending (static indices only).
+__device__ __forceinline__ void sort32(uint64_t (&k)[kBuf])
+{
+#pragma unroll
+    for (int size = 2; size <= kBuf; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+#pragma unroll
+            for (int i = 0; i < kBuf; ++i) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    if ((i & size) == 0) cmp_swap(k[i], k[j]);
+                    else cmp_swap(k[j], k[i]);
+                }
+            }
+        }
+    }
+}
+
+// Merge the 32 sorted keys into the row's sorted list of kL keys (shared
+// memory, row stride 128), keeping the kL smallest: elementwise minimum with
+// the reversed buffer gives a bitonic sequence holding the kL smallest keys,
+// and the bitonic half-cleaner cascade sorts it.  Every compare-exchange of a
+// stage is independent, so the loads overlap instead of forming one chain.
+template <int kL>
+__device__ __forceinline__ void merge_into_list(uint64_t* list, const uint64_t (&k)[kBuf])
+{
+#pragma unroll
+    for (int i = 0; i < kBuf; ++i) {
+        const uint64_t a = list[(kL - kBuf + i) * 128];
+        const uint64_t b = k[kBuf - 1 - i];
+        list[(kL - kBuf + i) * 128] = a < b ? a : b;
+    }
+#pragma unroll
+    for (int stride = kL / 2; stride > 0; stride >>= 1) {
+#pragma unroll
+        for (int i = 0; i < kL; ++i) {
+            if ((i & stride) == 0) {
+                const uint64_t a = list[i * 128], b = list[(i + stride) * 128];
+                if (b < a) {
+                    list[i * 128] = b;
+                    list[(i + stride) * 128] = a;
+                }
+            }
+        }
+    }
+}
+
+// Flush the row's staging buffer (nb entries, unsorted) into its list.
+template <int kL>
+__device__ __forceinline__ void flush_row(uint64_t* list, uint64_t* buf, int& nb)
+{
+    uint64_t k[kBuf];
+#pragma unroll
+    for (int i = 0; i < kBuf; ++i) k[i] = (i < nb) ? buf[i * 128] : kEmptyKey;
+    sort32(k);
+    merge_into_list<kL>(list, k);
+    nb = 0;
+}
+
+__device__ __forceinline__ float key_dist(uint64_t key) { return key2f(static_cast<uint32_t>(key >> 32)); }
+
+// Admission threshold of a row: the kL-th key (every finite value passes while
+// the list is not full); screen mode also caps it at the m_sel-th + margin.
+template <int kL>
+__device__ __forceinline__ float row_thr(const uint64_t* list, int m_sel, int screen, float margin)
+{
+    const uint64_t top = list[(kL - 1) * 128];
+    float t = (top == kEmptyKey) ? FLT_MAX : key_dist(top);
+    if (screen) {
+        const uint64_t mk = list[(m_sel - 1) * 128];
+        if (mk != kEmptyKey) t = fminf(t, key_dist(mk) + margin);
+    }
+    return t;
+}
+
+// Column tiles are visited from the tile holding the rows themselves outward
+// (t0, t0+1, t0-1, t0+2, ...): with bucket members grouped by locality the
+// nearest candidates come first and the row thresholds tighten early.
+__device__ __forceinline__ int tile_at(int k, int t0, int n_ct)
+{
+    if (k == 0) return t0;
+    const int right = n_ct - 1 - t0, left = t0, m = min(right, left);
+    if (k <= 2 * m) {
+        const int j = (k + 1) >> 1;
+        return (k & 1) ? t0 + j : t0 - j;
+    }
+    const int rem = k - 2 * m;
+    return right > left ? t0 + m + rem : t0 - m - rem;
+}
+
+__device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, int* err)
+{
+    const long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > kWaitBudgetCycles) {
+            if (err) atomicCAS(err, 0, kDevTimeoutDrain);
+            return false;
+        }
+    }
+    return true;
+}
+
+template <bool kTF32, int kL>
+__global__ void __launch_bounds__(kThreads, 1)
+    dist_topk_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const DistTopkArgs p)
+{
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    const uint32_t base = smem_u32(smem_raw);
+    uint8_t* gbase = smem_raw;
+    // the 128-byte-swizzled TMA / UMMA tiles need a 1024-byte aligned base
+    if (base & 1023u) {
+        if (threadIdx.x == 0) atomicCAS(p.err, 0, kDevBadShape);
+        return;
+    }
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const WorkItem w = p.work[blockIdx.x];
+    const int n_ct = (w.b_rows + kTileN - 1) / kTileN;
+    const int t0 = (w.self_col0 >= 0) ? min(n_ct - 1, w.self_col0 / kTileN) : 0;
+    const int S = p.stages;
+    const uint32_t stage_bytes = p.a_resident ? kTileBytes : 2u * kTileBytes;
+    const uint32_t a_bytes = p.a_resident ? static_cast<uint32_t>(p.k_chunks) * kTileBytes : 0u;
+    const uint32_t stage0 = base + a_bytes;
+    constexpr int kElemsPerChunk = kTF32 ? 32 : 64;
+
+    uint64_t* list = reinterpret_cast<uint64_t*>(gbase + p.list_off);
+    uint64_t* buf = reinterpret_cast<uint64_t*>(gbase + p.buf_off);
+    float* pn_s = reinterpret_cast<float*>(gbase + p.pn_off);
+    uint32_t* id_s = reinterpret_cast<uint32_t*>(gbase + p.pn_off + 2u * 128u * 4u);
+    const uint32_t bar0 = base + p.bar_off;
+    const uint32_t a_full = bar0 + 8u * (2 * S);
+    const uint32_t mma_done = bar0 + 8u * (2 * S + 5);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(gbase + p.bar_off + 8u * (2 * S + 6));
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+#define FULL_BAR(s) (bar0 + 8u * (s))
+#define EMPTY_BAR(s) (bar0 + 8u * (S + (s)))
+#define ACC_FULL(b) (bar0 + 8u * (2 * S + 1 + (b)))
+#define ACC_EMPTY(b) (bar0 + 8u * (2 * S + 3 + (b)))
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) { mbar_init(FULL_BAR(s), 1); mbar_init(EMPTY_BAR(s), 1); }
+        mbar_init(a_full, 1);
+        for (int b = 0; b < 2; ++b) { mbar_init(ACC_FULL(b), 1); mbar_init(ACC_EMPTY(b), 4); }
+        mbar_init(mma_done, 1);
+        *abort_flag = 0;
+        fence_barrier_init();
+    }
+    if (warp == 1) {
+        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            tma_prefetch_desc(&tmA);
+            tma_prefetch_desc(&tmB);
+            if (p.a_resident) {
+                mbar_arrive_expect_tx(a_full, a_bytes);
+                for (int kc = 0; kc < p.k_chunks; ++kc)
+                    tma_load_2d(base + kc * kTileBytes, &tmA, a_full, kc * kElemsPerChunk, w.a_row0);
+            }
+            int it = 0;
+            bool ok = true;
+            for (int k = 0; k < n_ct && ok; ++k) {
+                const int ct = tile_at(k, t0, n_ct);
+                for (int kc = 0; kc < p.k_chunks; ++kc) {
+                    const int s = it % S;
+                    const uint32_t ph = static_cast<uint32_t>(it / S) & 1u;
+                    if (!mbar_wait_backoff(EMPTY_BAR(s), ph ^ 1u, abort_flag, p.err, kDevTimeoutEmpty)) { ok = false; break; }
+                    const uint32_t dst = stage0 + static_cast<uint32_t>(s) * stage_bytes;
+                    mbar_arrive_expect_tx(FULL_BAR(s), stage_bytes);
+                    tma_load_2d(dst, &tmB, FULL_BAR(s), kc * kElemsPerChunk, w.b_row0 + ct * kTileN);
+                    if (!p.a_resident)
+                        tma_load_2d(dst + kTileBytes, &tmA, FULL_BAR(s), kc * kElemsPerChunk, w.a_row0);
+                    ++it;
+                }
+            }
+            // every issued copy must land before the CTA can exit
+            if (p.a_resident) mbar_wait_drain(a_full, 0, p.err);
+            for (int j = max(0, it - S); j < it; ++j)
+                mbar_wait_drain(FULL_BAR(j % S), static_cast<uint32_t>(j / S) & 1u, p.err);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = make_idesc(kTF32 ? 2u : 1u, kTileM, kTileN);
+            bool ok = true;
+            long long mma_wait_acc = 0, mma_wait_full = 0;
+            if (p.a_resident) ok = mbar_wait_backoff(a_full, 0, abort_flag, p.err, kDevTimeoutFull);
+            int it = 0;
+            for (int k = 0; k < n_ct && ok; ++k) {
+                const int b = k & 1;
+                const uint32_t use = static_cast<uint32_t>(k >> 1);
+                const long long m0 = p.stats ? clock64() : 0;
+                if (!mbar_wait_backoff(ACC_EMPTY(b), (use & 1u) ^ 1u, abort_flag, p.err, kDevTimeoutAcc)) { ok = false; break; }
+                if (p.stats) mma_wait_acc += clock64() - m0;
+                tc_fence_after();
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * kTileN);
+                for (int kc = 0; kc < p.k_chunks; ++kc) {
+                    const int s = it % S;
+                    const uint32_t ph = static_cast<uint32_t>(it / S) & 1u;
+                    const long long m1 = p.stats ? clock64() : 0;
+                    if (!mbar_wait_backoff(FULL_BAR(s), ph, abort_flag, p.err, kDevTimeoutFull)) { ok = false; break; }
+                    if (p.stats) mma_wait_full += clock64() - m1;
+                    tc_fence_after();
+                    const uint32_t sb = stage0 + static_cast<uint32_t>(s) * stage_bytes;
+                    const uint32_t sa = p.a_resident ? base + static_cast<uint32_t>(kc) * kTileBytes : sb + kTileBytes;
+                    const uint64_t adesc = smem_desc_sw128(sa);
+                    const uint64_t bdesc = smem_desc_sw128(sb);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)  // 4 x 32 B of K per 128-byte chunk
+                        umma<kTF32>(d_tmem, adesc + 2ull * k, bdesc + 2ull * k, idesc, (kc | k) != 0 ? 1u : 0u);
+                    umma_commit(EMPTY_BAR(s));
+                    ++it;
+                }
+                if (!ok) break;
+                umma_commit(ACC_FULL(b));
+            }
+            umma_commit(mma_done);
+            mbar_wait_drain(mma_done, 0, p.err);
+            if (p.stats) {
+                atomicAdd(&p.stats[6], static_cast<unsigned long long>(mma_wait_acc));
+                atomicAdd(&p.stats[7], static_cast<unsigned long long>(mma_wait_full));
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3;
+        const int r = q * 32 + lane;
+        const int et = threadIdx.x - 64;
+        const bool row_ok = r < w.a_rows;
+        const bool has_self = w.self_col0 >= 0;   // the tile's rows are also the segment's columns t0*128 + r
+        const int64_t arow = static_cast<int64_t>(w.a_row0) + r;
+        const float anorm = row_ok ? p.a_norm[arow] : 0.0f;
+        float margin = 0.0f;
+        if (p.screen) {
+            const float an = sqrtf(fmaxf(anorm, 0.0f)), bm = *p.b_maxnorm;
+            margin = p.mc1 * an * bm + p.mc2 * (an + bm) * (an + bm);
+        }
+        uint64_t* my_list = list + r;
+        uint64_t* my_buf = buf + r;
+#pragma unroll 4
+        for (int i = 0; i < kL; ++i) my_list[i * 128] = kEmptyKey;
+        float thr = row_ok ? FLT_MAX : -FLT_MAX;
+        int nb = 0, n_pass = 0, n_flush = 0;
+        bool ok = true;
+        const bool st_on = p.stats != nullptr;
+        long long cyc_wait = 0, cyc_flush = 0;
+        const long long cyc0 = st_on ? clock64() : 0;
+        for (int k = 0; k < n_ct; ++k) {
+            const int ct = tile_at(k, t0, n_ct);
+            const int b = k & 1;
+            const uint32_t use = static_cast<uint32_t>(k >> 1);
+            const int col = ct * kTileN + et;
+            const bool col_ok = col < w.b_rows;
+            pn_s[b * 128 + et] = col_ok ? p.b_norm[static_cast<int64_t>(w.b_row0) + col] : INFINITY;
+            if (!p.screen)
+                id_s[b * 128 + et] = (col_ok && p.b_gid) ? static_cast<uint32_t>(p.b_gid[static_cast<int64_t>(w.b_row0) + col])
+                                                         : static_cast<uint32_t>(col);
+            const long long w0 = st_on ? clock64() : 0;
+            named_bar_sync(1, 128);
+            if (!mbar_wait(ACC_FULL(b), use & 1u, abort_flag, p.err, kDevTimeoutAcc)) { ok = false; break; }
+            if (st_on) cyc_wait += clock64() - w0;
+            tc_fence_after();
+            const float* pn = pn_s + b * 128;
+            const uint32_t* ids = id_s + b * 128;
+#pragma unroll 1
+            for (int c = 0; c < 8; ++c) {  // 8 slices of 16 columns
+                uint32_t v[16];
+                __syncwarp();
+                tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                                       static_cast<uint32_t>(b * kTileN + c * 16),
+                                   v);
+                tmem_ld_wait();
+                // the row's own column sits at element lane % 16 of slice 2q + lane / 16 of the diagonal tile
+                const int self_e = (has_self && k == 0 && c == 2 * q + (lane >> 4)) ? (lane & 15) : -1;
+                const uint32_t c0 = static_cast<uint32_t>(ct * kTileN + c * 16);
+                const float4* pn4 = reinterpret_cast<const float4*>(pn + c * 16);
+                // branch-free scan: pass mask first, then predicated appends at popcount offsets
+                float sv[16];
+                uint32_t mask = 0;
+#pragma unroll
+                for (int e4 = 0; e4 < 4; ++e4) {
+                    const float4 n4 = pn4[e4];
+                    const float nv[4] = {n4.x, n4.y, n4.z, n4.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int e = e4 * 4 + u;
+                        sv[e] = fmaf(-2.0f, __uint_as_float(v[e]), nv[u]);
+                        mask |= (sv[e] <= thr) ? (1u << e) : 0u;
+                    }
+                }
+                if (self_e >= 0) mask &= ~(1u << self_e);
+                if (mask) {
+                    uint32_t idv[16];
+                    if (!p.screen) {
+                        const uint4* id4 = reinterpret_cast<const uint4*>(ids + c * 16);
+#pragma unroll
+                        for (int e4 = 0; e4 < 4; ++e4) {
+                            const uint4 x = id4[e4];
+                            idv[e4 * 4 + 0] = x.x; idv[e4 * 4 + 1] = x.y; idv[e4 * 4 + 2] = x.z; idv[e4 * 4 + 3] = x.w;
+                        }
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) idv[e] = c0 + e;  // screen mode keys carry the column
+                    }
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        if ((mask >> e) & 1u) {
+                            const int slot = nb + __popc(mask & ((1u << e) - 1u));
+                            my_buf[slot * 128] = (static_cast<uint64_t>(f2key(sv[e])) << 32) | idv[e];
+                        }
+                    }
+                    nb += __popc(mask);
+                }
+                // warp-wide flush: when any lane may overflow its buffer in the next
+                // 16 columns, every lane merges its own buffer
+                if (__any_sync(0xffffffffu, nb > kBuf - 16)) {
+                    const long long f0 = st_on ? clock64() : 0;
+                    n_pass += nb;
+                    ++n_flush;
+                    flush_row<kL>(my_list, my_buf, nb);
+                    thr = row_ok ? row_thr<kL>(my_list, p.m_sel, p.screen, margin) : -FLT_MAX;
+                    if (st_on) cyc_flush += clock64() - f0;
+                }
+                __syncwarp();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(ACC_EMPTY(b));
+        }
+        if (ok) {
+            if (__any_sync(0xffffffffu, nb > 0)) {
+                n_pass += nb;
+                ++n_flush;
+                flush_row<kL>(my_list, my_buf, nb);
+            }
+            if (st_on) {
+                if (row_ok) atomicAdd(&p.stats[0], static_cast<unsigned long long>(n_pass));
+                if (row_ok) atomicAdd(&p.stats[2], 1ull);
+                if (lane == 0) {
+                    atomicAdd(&p.stats[1], static_cast<unsigned long long>(n_flush));
+                    atomicAdd(&p.stats[3], static_cast<unsigned long long>(cyc_wait));
+                    atomicAdd(&p.stats[4], static_cast<unsigned long long>(cyc_flush));
+                    atomicAdd(&p.stats[5], static_cast<unsigned long long>(clock64() - cyc0));
+                }
+            }
+        }
+        if (ok && row_ok) {
+            if (!p.screen) {
+                for (int j = 0; j < p.m_out; ++j) {
+                    const uint64_t key = my_list[j * 128];
+                    const bool v = key != kEmptyKey;
+                    p.out_ids[arow * p.m_out + j] = v ? static_cast<int32_t>(static_cast<uint32_t>(key)) : -1;
+                    p.out_dists[arow * p.m_out + j] = v ? key_dist(key) + anorm : INFINITY;
+                }
+            } else {
+                const uint64_t mk = my_list[(p.m_sel - 1) * 128];
+                const float bound = (mk != kEmptyKey) ? key_dist(mk) + margin : INFINITY;
+                const uint64_t top = my_list[(kL - 1) * 128];
+                if (top != kEmptyKey && key_dist(top) <= bound) {
+                    p.cand_n[arow] = -1;  // entries beyond the list may be within the bound: rescan exactly
+                } else {
+                    int j = 0;
+                    for (int i = 0; i < kL; ++i) {
+                        const uint64_t key = my_list[i * 128];
+                        if (key == kEmptyKey || key_dist(key) > bound) break;
+                        p.cand_cols[arow * kL + j] = static_cast<int32_t>(static_cast<uint32_t>(key));
+                        ++j;
+                    }
+                    p.cand_n[arow] = j;
+                }
+            }
+        }
+    }
+#undef FULL_BAR
+#undef EMPTY_BAR
+#undef ACC_FULL
+#undef ACC_EMPTY
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// --------------------------------------------------------------------------
+// exact rerank: one warp per A row, candidates -> exact fp32 distances ->
+// bitonic sort of (distance, id) keys -> top-M.  Rows whose screen list
+// overflowed rescan their whole segment exactly.
+// --------------------------------------------------------------------------
+struct RerankArgs {
+    const WorkItem* work;
+    const void* A;
+    const void* B;
+    int elem;
+    int d, d_pad;
+    const int32_t* b_gid;
+    const int32_t* cand_cols;
+    const int32_t* cand_n;
+    int L;
+    int m_out;
+    int32_t* out_ids;
+    float* out_dists;
+};
+
+constexpr int kSortMax = 512;
+
+template <typename T>
+__device__ __forceinline__ float exact_dist_row(const float* __restrict__ a, const T* __restrict__ b, int d)
+{
+    float acc = 0.0f;
+    for (int i = 0; i < d; ++i) {
+        const float t = a[i] - to_f32(b[i]);
+        acc = fmaf(t, t, acc);
+    }
+    return acc;
+}
+
+__device__ __forceinline__ void warp_bitonic_sort(uint64_t* keys, int n, int lane)
+{
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int t = lane; t < (n >> 1); t += 32) {
+                const int i = 2 * j * (t / j) + (t % j);
+                const int l = i + j;
+                const bool up = (i & k) == 0;
+                const uint64_t x = keys[i], y = keys[l];
+                if ((x > y) == up) { keys[i] = y; keys[l] = x; }
+            }
+            __syncwarp();
+        }
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(128) rerank_kernel(const RerankArgs p)
+{
+    extern __shared__ uint8_t sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t* keys = reinterpret_cast<uint64_t*>(sm) + warp * kSortMax;
+    float* arow_s = reinterpret_cast<float*>(sm + 4 * kSortMax * sizeof(uint64_t)) + warp * p.d_pad;
+    const WorkItem w = p.work[blockIdx.x];
+    const T* A = static_cast<const T*>(p.A);
+    const T* B = static_cast<const T*>(p.B);
+    for (int r = warp; r < w.a_rows; r += 4) {
+        const int64_t arow = static_cast<int64_t>(w.a_row0) + r;
+        for (int i = lane; i < p.d; i += 32) arow_s[i] = to_f32(A[arow * p.d_pad + i]);
+        __syncwarp();
+        const int n = p.cand_n[arow];
+        const int self = (w.self_col0 >= 0) ? w.self_col0 + r : -1;
+        if (n >= 0) {
+            int np2 = 1;
+            while (np2 < n) np2 <<= 1;
+            for (int j = lane; j < np2; j += 32) {
+                uint64_t key = ~0ull;
+                if (j < n) {
+                    const int c = p.cand_cols[arow * p.L + j];
+                    const int64_t brow = static_cast<int64_t>(w.b_row0) + c;
+                    const float dd = exact_dist_row(arow_s, B + brow * p.d_pad, p.d);
+                    const uint32_t id = p.b_gid ? static_cast<uint32_t>(p.b_gid[brow]) : static_cast<uint32_t>(c);
+                    key = (static_cast<uint64_t>(f2key(dd)) << 32) | id;
+                }
+                keys[j] = key;
+            }
+            __syncwarp();
+            warp_bitonic_sort(keys, np2, lane);
+            for (int j = lane; j < p.m_out; j += 32) {
+                const uint64_t key = j < np2 ? keys[j] : ~0ull;
+                const bool v = key != ~0ull;
+                p.out_ids[arow * p.m_out + j] = v ? static_cast<int32_t>(static_cast<uint32_t>(key)) : -1;
+                p.out_dists[arow * p.m_out + j] = v ? key2f(static_cast<uint32_t>(key >> 32)) : INFINITY;
+            }
+        } else {
+            // full exact rescan of the segment: keys[0..256) = best so far, [256..512) = next chunk
+            for (int j = lane; j < kSortMax; j += 32) keys[j] = ~0ull;
+            __syncwarp();
+            for (int c0 = 0; c0 < w.b_rows; c0 += kSortMax / 2) {
+                for (int j = lane; j < kSortMax / 2; j += 32) {
+                    const int c = c0 + j;
+                    uint64_t key = ~0ull;
+                    if (c < w.b_rows && c != self) {
+                        const int64_t brow = static_cast<int64_t>(w.b_row0) + c;
+                        const float dd = exact_dist_row(arow_s, B + brow * p.d_pad, p.d);
+                        const uint32_t id = p.b_gid ? static_cast<uint32_t>(p.b_gid[brow]) : static_cast<uint32_t>(c);
+                        key = (static_cast<uint64_t>(f2key(dd)) << 32) | id;
+                    }
+                    keys[kSortMax / 2 + j] = key;
+                }
+                __syncwarp();
+                warp_bitonic_sort(keys, kSortMax, lane);
+            }
+            for (int j = lane; j < p.m_out; j += 32) {
+                const uint64_t key = keys[j];
+                const bool v = key != ~0ull;
+                p.out_ids[arow * p.m_out + j] = v ? static_cast<int32_t>(static_cast<uint32_t>(key)) : -1;
+                p.out_dists[arow * p.m_out + j] = v ? key2f(static_cast<uint32_t>(key >> 32)) : INFINITY;
+            }
+        }
+        __syncwarp();
+    }
+}
+
+// --------------------------------------------------------------------------
+// host side
+// --------------------------------------------------------------------------
+struct Plan {
+    int stages = 0, L = 0, a_res = 0;
+    uint32_t list_off = 0, buf_off = 0, pn_off = 0, bar_off = 0, total = 0;
+};
+
+// Row list length: a power of two (the merge network) and at least the
+// 32-entry buffer; screen lists keep 16+ entries of headroom beyond M for the
+// margin candidates when that fits.
+bool make_plan(int k_chunks, int m, bool screen, Plan& pl)
+{
+    int L = 32;
+    while (L < (screen ? m + 16 : m)) L <<= 1;
+    struct Cfg { int a_res, S; };
+    const Cfg cfgs[] = {{1, 4}, {1, 3}, {0, 4}, {0, 3}, {1, 2}, {0, 2}};
+    for (; L >= 32 && L >= m; L >>= 1) {
+        for (const Cfg& c : cfgs) {
+            const uint32_t stage_bytes = c.a_res ? kTileBytes : 2u * kTileBytes;
+            uint32_t off = (c.a_res ? static_cast<uint32_t>(k_chunks) * kTileBytes : 0u) + c.S * stage_bytes;
+            Plan t;
+            t.stages = c.S; t.L = L; t.a_res = c.a_res;
+            t.list_off = off; off += static_cast<uint32_t>(L) * 128u * 8u;
+            t.buf_off = off; off += static_cast<uint32_t>(kBuf) * 128u * 8u;
+            t.pn_off = off; off += 2u * 128u * 4u * 2u;  // column norms + column ids, double-buffered
+            t.bar_off = off; off += 8u * (2u * c.S + 6u) + 16u;
+            t.total = off;
+            if (t.total <= kSmemMax) { pl = t; return true; }
+        }
+    }
+    return false;
+}
+
+template <bool kTF32, int kL>
+void launch_dist_topk(const CUtensorMap& tmA, const CUtensorMap& tmB, const DistTopkArgs& a, int n_work,
+                      uint32_t smem, cudaStream_t st)
+{
+    GTA_CUDA(cudaFuncSetAttribute(dist_topk_kernel<kTF32, kL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    dist_topk_kernel<kTF32, kL><<<n_work, kThreads, smem, st>>>(tmA, tmB, a);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+template <bool kTF32>
+void launch_dist_topk_L(int L, const CUtensorMap& tmA, const CUtensorMap& tmB, const DistTopkArgs& a, int n_work,
+                        uint32_t smem, cudaStream_t st)
+{
+    switch (L) {
+        case 32: launch_dist_topk<kTF32, 32>(tmA, tmB, a, n_work, smem, st); break;
+        case 64: launch_dist_topk<kTF32, 64>(tmA, tmB, a, n_work, smem, st); break;
+        case 128: launch_dist_topk<kTF32, 128>(tmA, tmB, a, n_work, smem, st); break;
+        default: throw Error(kInvalid, "dist_topk: unsupported list length");
+    }
+}
+
+using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
+
+EncodeFn get_encode()
+{
+    static EncodeFn fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeFn>(ptr);
+    });
+    GTA_REQUIRE(fn != nullptr, kCuda, "cuTensorMapEncodeTiled is not available from the driver");
+    return fn;
+}
+
+CUtensorMap make_tmap(const void* base, int elem, int64_t rows, int d_pad)
+{
+    CUtensorMap m;
+    const int esz = elem == kElemBF16 ? 2 : 4;
+    cuuint64_t dims[2] = {static_cast<cuuint64_t>(d_pad), static_cast<cuuint64_t>(rows)};
+    cuuint64_t strides[1] = {static_cast<cuuint64_t>(d_pad) * esz};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esz), 128u};
+    cuuint32_t estr[2] = {1u, 1u};
+    const CUresult r = get_encode()(&m, elem == kElemBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+                                    2, const_cast<void*>(base), dims, strides, box, estr,
+                                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    GTA_REQUIRE(r == CUDA_SUCCESS, kCuda, "cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
+    return m;
+}
+
+}  // namespace
+
+void dist_topk(const DistTopkProblem& pr, cudaStream_t st)
+{
+    if (pr.n_work == 0) return;
+    GTA_REQUIRE(pr.A && pr.B && pr.a_norm && pr.b_norm && pr.work && pr.out_ids && pr.out_dists, kInvalid,
+                "dist_topk: null operand");
+    const int esz = pr.elem == kElemBF16 ? 2 : 4;
+    GTA_REQUIRE((pr.d_pad * esz) % 128 == 0 && pr.d <= pr.d_pad, kInvalid, "dist_topk: rows must be 128-byte multiples");
+    GTA_REQUIRE((reinterpret_cast<uintptr_t>(pr.A) & 15) == 0 && (reinterpret_cast<uintptr_t>(pr.B) & 15) == 0,
+                kInvalid, "dist_topk: operands must be 16-byte aligned");
+    GTA_REQUIRE(pr.m_out >= 1 && pr.m_out <= 256, kInvalid, "dist_topk: list length must be in [1, 256]");
+    const bool screen = pr.elem != kElemBF16;
+    const int k_chunks = pr.d_pad * esz / 128;
+    const int m_sel = pr.m_out;  // the row itself is masked in the kernel, not carried in its list
+    Plan pl;
+    GTA_REQUIRE(pr.m_out <= 128 && make_plan(k_chunks, m_sel, screen, pl), kInvalid,
+                "dist_topk: list length too large for shared memory");
+    GTA_REQUIRE(!screen || pl.L <= kSortMax, kInvalid, "dist_topk: candidate list too long");
+
+    const CUtensorMap tmA = make_tmap(pr.A, pr.elem, pr.a_total, pr.d_pad);
+    const CUtensorMap tmB = make_tmap(pr.B, pr.elem, pr.b_total, pr.d_pad);
+
+    DevBuf<int32_t> cand_cols, cand_n;
+    DevBuf<float> bmax;
+    if (screen) {
+        cand_cols = DevBuf<int32_t>(static_cast<size_t>(pr.a_total) * pl.L, st);
+        cand_n = DevBuf<int32_t>(static_cast<size_t>(pr.a_total), st);
+        bmax = DevBuf<float>(1, st);
+        max_sqrt(pr.b_norm, pr.b_total, bmax.get(), st);
+    }
+    DistTopkArgs a{};
+    a.work = pr.work; a.a_norm = pr.a_norm; a.b_norm = pr.b_norm; a.b_gid = pr.b_gid;
+    a.b_maxnorm = screen ? bmax.get() : nullptr;
+    a.k_chunks = k_chunks; a.m_out = pr.m_out; a.m_sel = m_sel; a.L = pl.L; a.cap = kBuf;
+    a.stages = pl.stages; a.a_resident = pl.a_res; a.screen = screen ? 1 : 0;
+    // tf32 screen error bound (operand truncation 2^-10 each, fp32 accumulation with 2 ulp per add,
+    // fp32 norms and the fused multiply-add), with a 1.25 safety factor.
+    const double d = pr.d;
+    a.mc1 = static_cast<float>(1.25 * 4.0 * (std::ldexp(1.0, -9) + d * std::ldexp(1.0, -22)));
+    a.mc2 = static_cast<float>(1.25 * 3.0 * (d + 2.0) * std::ldexp(1.0, -24));
+    a.out_ids = pr.out_ids; a.out_dists = pr.out_dists;
+    a.cand_cols = cand_cols.get(); a.cand_n = cand_n.get();
+    a.err = pr.err;
+    a.list_off = pl.list_off; a.buf_off = pl.buf_off; a.pn_off = pl.pn_off; a.bar_off = pl.bar_off;
+
+    {
+        ProfScope prof(pr.prof_name, pr.flops, st);
+        a.stats = prof.counters(8);
+        if (screen) launch_dist_topk_L<true>(pl.L, tmA, tmB, a, pr.n_work, pl.total, st);
+        else launch_dist_topk_L<false>(pl.L, tmA, tmB, a, pr.n_work, pl.total, st);
+    }
+
+    if (screen) {
+        RerankArgs r{};
+        r.work = pr.work; r.A = pr.A; r.B = pr.B; r.elem = pr.elem; r.d = pr.d; r.d_pad = pr.d_pad;
+        r.b_gid = pr.b_gid; r.cand_cols = cand_cols.get(); r.cand_n = cand_n.get(); r.L = pl.L; r.m_out = pr.m_out;
+        r.out_ids = pr.out_ids; r.out_dists = pr.out_dists;
+        const size_t smem = 4 * kSortMax * sizeof(uint64_t) + 4 * static_cast<size_t>(pr.d_pad) * sizeof(float);
+        GTA_REQUIRE(smem <= kSmemMax, kInvalid, "rerank: dimension too large");
+        GTA_CUDA(cudaFuncSetAttribute(rerank_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem)));
+        ProfScope prof("rerank", 0.0, st);
+        rerank_kernel<float><<<pr.n_work, 128, smem, st>>>(r);
+        count_launches(1);
+        GTA_CUDA(cudaGetLastError());
+    }
+}
+
+}  // namespace gta

@@ -1,0 +1,128 @@
+// gta_internal.h -- host-side internal interface of libgta (not part of the C ABI).
+#pragma once
+
+#include <cstdint>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include <cuda_runtime.h>
+
+namespace gta {
+
+// Status codes of the C ABI (see include/gta.h).
+enum : int { kOk = 0, kInvalid = 1, kNoMem = 2, kCuda = 3, kNccl = 4, kData = 5 };
+
+struct Error : std::runtime_error {
+    int code;
+    Error(int c, const std::string& m) : std::runtime_error(m), code(c) {}
+};
+
+#define GTA_CUDA(call)                                                                                     \
+    do {                                                                                                   \
+        cudaError_t e_ = (call);                                                                           \
+        if (e_ != cudaSuccess)                                                                             \
+            throw ::gta::Error(e_ == cudaErrorMemoryAllocation ? ::gta::kNoMem : ::gta::kCuda,             \
+                               std::string("CUDA error: ") + cudaGetErrorString(e_) + " at " __FILE__ ":" + \
+                                   std::to_string(__LINE__));                                              \
+    } while (0)
+
+#define GTA_REQUIRE(cond, code, msg)                 \
+    do {                                             \
+        if (!(cond)) throw ::gta::Error(code, msg);  \
+    } while (0)
+
+// Stream-ordered device scratch, freed on scope exit.
+template <typename T>
+struct DevBuf {
+    T* p = nullptr;
+    size_t n = 0;
+    cudaStream_t st = nullptr;
+    DevBuf() = default;
+    DevBuf(size_t count, cudaStream_t s) : n(count), st(s)
+    {
+        if (count) GTA_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&p), sizeof(T) * count, s));
+    }
+    DevBuf(const DevBuf&) = delete;
+    DevBuf& operator=(const DevBuf&) = delete;
+    DevBuf(DevBuf&& o) noexcept : p(o.p), n(o.n), st(o.st) { o.p = nullptr; o.n = 0; }
+    DevBuf& operator=(DevBuf&& o) noexcept
+    {
+        release();
+        p = o.p; n = o.n; st = o.st; o.p = nullptr; o.n = 0;
+        return *this;
+    }
+    ~DevBuf() { release(); }
+    void release()
+    {
+        if (p) cudaFreeAsync(p, st);
+        p = nullptr;
+        n = 0;
+    }
+    T* get() const { return p; }
+};
+
+// One CTA of the distance kernel: a tile of up to 128 A rows against a
+// contiguous segment of B rows (all columns of one bucket, or all centroids).
+struct WorkItem {
+    int32_t a_row0;     // first A row of the tile
+    int32_t a_rows;     // valid rows in the tile (1..128)
+    int32_t b_row0;     // first B row of the segment
+    int32_t b_rows;     // segment length (columns)
+    int32_t self_col0;  // segment column of the tile's row 0 itself (self excluded), or -1
+    int32_t pad0, pad1, pad2;
+};
+
+enum ElemType : int { kElemBF16 = 0, kElemF32 = 1 };
+
+// Row-wise top-k of squared L2 distances between A rows and a B segment.
+struct DistTopkProblem {
+    const void* A = nullptr;       // [a_total x d_pad] bf16 or f32, rows 128-B multiples
+    int64_t a_total = 0;
+    const void* B = nullptr;       // [b_total x d_pad]
+    int64_t b_total = 0;
+    int elem = kElemF32;           // bf16: exact integer data (kind::f16); f32: tf32 screen + exact rerank
+    int d = 0, d_pad = 0;
+    const float* a_norm = nullptr; // [a_total] exact ||a||^2
+    const float* b_norm = nullptr; // [b_total] exact ||b||^2
+    const int32_t* b_gid = nullptr;// [b_total] output id of a B row (null: segment column)
+    const WorkItem* work = nullptr;// device work list
+    int n_work = 0;
+    int m_out = 0;                 // list length written per A row
+    bool exclude_self = false;
+    int32_t* out_ids = nullptr;    // [a_total x m_out]
+    float* out_dists = nullptr;
+    int* err = nullptr;            // device error word
+    const char* prof_name = "dist_topk";
+    double flops = 0.0;            // algorithmic flops of the launch (sum of 2*rows*cols*d)
+};
+
+void dist_topk(const DistTopkProblem& pr, cudaStream_t st);
+
+// ---- other kernels (kernels.cu) -------------------------------------------
+// Convert rows of X (dtype: 0 f32, 1 u8, 2 i8) selected by row_ids (null = identity)
+// into a padded bf16 or f32 matrix, with exact fp32 squared norms.
+void convert_rows(const void* X, int dtype, int d, const int32_t* row_ids, int64_t n_out, void* out, int out_elem,
+                  int d_pad, float* norms, cudaStream_t st);
+void sample_ids(int64_t N, int64_t n_s, uint64_t seed, int32_t* out, cudaStream_t st);
+void kmeanspp_init(const float* pool, const float* pool_norm, int64_t pool_n, int d, int d_pad, int32_t B,
+                   uint64_t seed, float* centroids, int* err, cudaStream_t st);
+void centroid_update(const float* Xs, int64_t n_s, int d, int d_pad, const int32_t* assign, const float* C_in,
+                     int32_t B, float* C_out, float* C_norm, cudaStream_t st);
+void build_memberships(const int32_t* top2, int64_t N, int32_t B, int32_t* members, int64_t* offsets,
+                       int64_t* mem_row, cudaStream_t st);
+void merge_memberships(const int32_t* list_n, const float* list_d, const int64_t* mem_row, int64_t N, int M,
+                       int32_t* out_n, float* out_d, cudaStream_t st);
+void merge_lists(const int32_t* run_n, const float* run_d, const int32_t* new_n, const float* new_d, int64_t N,
+                 int M, int32_t* out_n, float* out_d, cudaStream_t st);
+void sanitize(const int32_t* knn, int64_t N, int M, uint32_t* out, cudaStream_t st);
+void prune_detour(const uint32_t* g, int64_t N, int M, int K, const int32_t* order, uint32_t* out, int* err,
+                  cudaStream_t st);
+void locality_order(const int32_t* top2, int64_t N, int32_t B, int32_t* order, cudaStream_t st);
+void reverse_merge(const uint32_t* pruned, int64_t N, int K, uint32_t* out, int* err, cudaStream_t st);
+void sort_rows_l2(const float* X, int d, int d_pad, const int32_t* knn, int64_t N, int M, int32_t* out,
+                  cudaStream_t st);
+void max_sqrt(const float* v, int64_t n, float* out, cudaStream_t st);
+void check_device_error(const int* err, cudaStream_t st, const char* what);
+
+}  // namespace gta

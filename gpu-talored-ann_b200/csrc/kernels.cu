@@ -1,0 +1,867 @@
+// kernels.cu -- the integer / byte kernels of the bucketed kNN + CAGRA build.
+//
+// All of them are HBM- or latency-bound; none is reshaped into a GEMM.
+// Reference behaviour (paths relative to the reference root):
+//   merge_memberships  bucketDemo/buildBucket/src/bucket.cu:5025-5131 resident_merge(_warp)_kernel
+//   sanitize           bucketDemo/buildBucket/src/optimize.cu:95-133
+//   prune_detour       bucketDemo/buildBucket/src/prune_windowed_core.hpp:190-263 (full window),
+//                      prune_windowed_gpu.cu:178-330 (warp per point, id->rank hash, detour stamp)
+//   reverse_merge      bucketDemo/buildBucket/src/edge_chunk_accumulator.hpp:386-494,
+//                      optimize_chunked.cu:372 kern_scatter_rank / :1450 kern_e_merge
+//   sort_rows_l2       bucketDemo/buildBucket/src/prune_windowed_core.hpp:134-175
+//   centroid_update    bucketDemo/build_bucket.py:255-261
+//   kmeanspp_init      bucketDemo/build_bucket.py:189-229 (D^2 sampling on a pool of min(N, 20B))
+#include <cub/cub.cuh>
+#include <cuda_bf16.h>
+
+#include <cmath>
+
+#include "common.cuh"
+#include "gta_internal.h"
+#include "prof.h"
+
+namespace gta {
+
+namespace {
+
+constexpr uint32_t kEmpty = 0xFFFFFFFFu;
+
+__device__ __forceinline__ uint64_t splitmix64(uint64_t x)
+{
+    uint64_t z = x + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+__device__ __forceinline__ double uniform01(uint64_t seed, uint64_t t)
+{
+    return static_cast<double>(splitmix64(seed * 0x2545F4914F6CDD1Dull + t) >> 11) * (1.0 / 9007199254740992.0);
+}
+
+template <typename T> __device__ __forceinline__ float ld_f32(const T* p) { return static_cast<float>(*p); }
+template <> __device__ __forceinline__ float ld_f32<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+template <typename Tout> __device__ __forceinline__ Tout from_f32(float v);
+template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+__device__ __forceinline__ float exact_l2_f(const float* __restrict__ a, const float* __restrict__ b, int d)
+{
+    float acc = 0.0f;
+    for (int i = 0; i < d; ++i) {
+        const float t = a[i] - b[i];
+        acc = fmaf(t, t, acc);
+    }
+    return acc;
+}
+
+// ---------------------------------------------------------------- conversion
+template <typename Tin, typename Tout>
+__global__ void convert_rows_kernel(const Tin* __restrict__ X, int d, const int32_t* __restrict__ row_ids,
+                                    int64_t n_out, Tout* __restrict__ out, int d_pad, float* __restrict__ norms)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (row >= n_out) return;
+    const int64_t src = row_ids ? static_cast<int64_t>(row_ids[row]) : row;
+    const Tin* x = X + src * d;
+    if (out) {
+        Tout* o = out + row * d_pad;
+        for (int i = lane; i < d_pad; i += 32) o[i] = from_f32<Tout>(i < d ? ld_f32(x + i) : 0.0f);
+    }
+    if (norms && lane == 0) {
+        float acc = 0.0f;
+        for (int i = 0; i < d; ++i) { const float v = ld_f32(x + i); acc = fmaf(v, v, acc); }
+        norms[row] = acc;
+    }
+}
+
+template <typename Tin>
+void convert_dispatch_out(const Tin* X, int d, const int32_t* ids, int64_t n, void* out, int out_elem, int d_pad,
+                          float* norms, cudaStream_t st)
+{
+    const int wpb = 8;
+    const unsigned grid = static_cast<unsigned>((n + wpb - 1) / wpb);
+    if (out_elem == kElemBF16)
+        convert_rows_kernel<Tin, __nv_bfloat16><<<grid, wpb * 32, 0, st>>>(X, d, ids, n,
+                                                                            static_cast<__nv_bfloat16*>(out), d_pad, norms);
+    else
+        convert_rows_kernel<Tin, float><<<grid, wpb * 32, 0, st>>>(X, d, ids, n, static_cast<float*>(out), d_pad, norms);
+}
+
+// ---------------------------------------------------------------- sampling
+__global__ void sample_ids_kernel(int64_t N, int64_t n_s, uint64_t seed, int32_t* out)
+{
+    const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j >= n_s) return;
+    const int64_t lo = (j * N) / n_s, hi = ((j + 1) * N) / n_s;
+    const uint64_t h = splitmix64((seed * 0x100000001B3ull) ^ static_cast<uint64_t>(j));
+    out[j] = static_cast<int32_t>(lo + static_cast<int64_t>(h % static_cast<uint64_t>(hi - lo)));
+}
+
+// ---------------------------------------------------------------- k-means++
+constexpr int kKppThreads = 256;
+
+__global__ void kpp_first_kernel(const float* __restrict__ pool, int64_t pool_n, int d_pad, uint64_t seed,
+                                 float* __restrict__ C)
+{
+    const int64_t i = static_cast<int64_t>(uniform01(seed, 0) * static_cast<double>(pool_n));
+    const int64_t c = i < pool_n ? i : pool_n - 1;
+    for (int k = threadIdx.x; k < d_pad; k += blockDim.x) C[k] = pool[c * d_pad + k];
+}
+
+// One D^2-sampling step: fold centroid t into min_d2, then the last block to
+// finish draws centroid t+1 with probability proportional to min_d2.  Every
+// block sums its chunk as 256 contiguous per-thread runs combined in thread
+// order, and the draw repeats exactly that order inside the chosen block, so
+// the pick is reproducible run to run.
+__device__ __forceinline__ double kpp_run_sum(const float* __restrict__ v, int64_t a, int64_t b)
+{
+    double s = 0.0;
+    for (int64_t i = a; i < b; ++i) s += static_cast<double>(v[i]);
+    return s;
+}
+
+__global__ void __launch_bounds__(kKppThreads) kpp_step_kernel(const float* __restrict__ pool, int64_t pool_n, int d,
+                                                               int d_pad, float* __restrict__ C, int t, int B,
+                                                               float* __restrict__ min_d2, double* __restrict__ bsum,
+                                                               unsigned* __restrict__ counter, uint64_t seed, int64_t chunk)
+{
+    extern __shared__ float cen[];
+    __shared__ double part[kKppThreads];
+    __shared__ bool last;
+    __shared__ int s_blk;
+    __shared__ double s_resid;
+    __shared__ int64_t s_pick;
+    const int tid = threadIdx.x;
+    for (int k = tid; k < d; k += blockDim.x) cen[k] = C[static_cast<int64_t>(t) * d_pad + k];
+    __syncthreads();
+    const int64_t lo = static_cast<int64_t>(blockIdx.x) * chunk;
+    const int64_t hi = min(pool_n, lo + chunk);
+    for (int64_t i = lo + tid; i < hi; i += blockDim.x) {
+        const float dd = exact_l2_f(pool + i * d_pad, cen, d);
+        min_d2[i] = (t == 0) ? dd : fminf(min_d2[i], dd);
+    }
+    __syncthreads();
+    const int64_t per = (hi - lo + kKppThreads - 1) / kKppThreads;
+    {
+        const int64_t a = min(hi, lo + tid * per), e = min(hi, a + per);
+        part[tid] = kpp_run_sum(min_d2, a, e);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        double s = 0.0;
+        for (int w = 0; w < kKppThreads; ++w) s += part[w];
+        bsum[blockIdx.x] = s;
+        __threadfence();
+        last = (atomicAdd(counter, 1u) == gridDim.x - 1);
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (tid == 0) {
+        *counter = 0;
+        s_blk = -1;
+        if (t + 1 < B) {
+            double total = 0.0;
+            for (unsigned b = 0; b < gridDim.x; ++b) total += bsum[b];
+            const double u = uniform01(seed, static_cast<uint64_t>(t) + 1);
+            s_pick = min(pool_n - 1, static_cast<int64_t>(u * static_cast<double>(pool_n)));
+            s_blk = -2;
+            if (total > 0.0) {
+                const double target = u * total;
+                double cum = 0.0;
+                unsigned b = 0;
+                for (; b + 1 < gridDim.x; ++b) {
+                    if (cum + bsum[b] > target) break;
+                    cum += bsum[b];
+                }
+                s_blk = static_cast<int>(b);
+                s_resid = target - cum;
+            }
+        }
+    }
+    __syncthreads();
+    if (s_blk == -1) return;
+    if (s_blk >= 0) {
+        const int64_t lo2 = static_cast<int64_t>(s_blk) * chunk, hi2 = min(pool_n, lo2 + chunk);
+        const int64_t per2 = (hi2 - lo2 + kKppThreads - 1) / kKppThreads;
+        {
+            const int64_t a = min(hi2, lo2 + tid * per2), e = min(hi2, a + per2);
+            part[tid] = kpp_run_sum(min_d2, a, e);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            double cum = 0.0;
+            int w = 0;
+            for (; w + 1 < kKppThreads; ++w) {
+                if (cum + part[w] > s_resid) break;
+                cum += part[w];
+            }
+            const int64_t a = min(hi2, lo2 + w * per2), e = min(hi2, a + per2);
+            int64_t pick = (e > a) ? e - 1 : hi2 - 1;
+            for (int64_t i = a; i < e; ++i) {
+                cum += static_cast<double>(min_d2[i]);
+                if (cum > s_resid) { pick = i; break; }
+            }
+            s_pick = pick;
+        }
+    }
+    __syncthreads();
+    const int64_t pick = s_pick;
+    for (int k = tid; k < d_pad; k += blockDim.x) C[static_cast<int64_t>(t + 1) * d_pad + k] = pool[pick * d_pad + k];
+}
+
+// ---------------------------------------------------------------- Lloyd update
+__global__ void seg_offsets_kernel(const int32_t* __restrict__ keys_sorted, int64_t n, int32_t B,
+                                   int64_t* __restrict__ offsets)
+{
+    const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (b > B) return;
+    int64_t lo = 0, hi = n;  // first index with key >= b
+    while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (keys_sorted[mid] < b) lo = mid + 1;
+        else hi = mid;
+    }
+    offsets[b] = lo;
+}
+
+__global__ void centroid_sum_kernel(const float* __restrict__ Xs, int d, int d_pad, const int32_t* __restrict__ order,
+                                    const int64_t* __restrict__ offsets, const float* __restrict__ C_in,
+                                    float* __restrict__ C_out)
+{
+    const int b = blockIdx.x;
+    const int64_t lo = offsets[b], hi = offsets[b + 1];
+    const int64_t cnt = hi - lo;
+    for (int k = threadIdx.x; k < d_pad; k += blockDim.x) {
+        const int64_t o = static_cast<int64_t>(b) * d_pad + k;
+        if (k >= d) { C_out[o] = 0.0f; continue; }
+        if (cnt == 0) { C_out[o] = C_in[o]; continue; }
+        double s = 0.0;
+        for (int64_t j = lo; j < hi; ++j) s += static_cast<double>(Xs[static_cast<int64_t>(order[j]) * d_pad + k]);
+        C_out[o] = static_cast<float>(s / static_cast<double>(cnt));
+    }
+}
+
+__global__ void iota_kernel(int32_t* out, int64_t n)
+{
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = static_cast<int32_t>(i);
+}
+
+// ---------------------------------------------------------------- memberships
+// Membership i = (point i/2, way i%2).  Sort key = bucket * B + the point's
+// other bucket: inside a bucket, members that share their second bucket (one
+// boundary region of the Voronoi diagram) become contiguous, in point order.
+__global__ void membership_pairs_kernel(const int32_t* __restrict__ top2, int64_t N, int32_t B,
+                                        uint32_t* __restrict__ keys, int32_t* __restrict__ vals)
+{
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= 2 * N) return;
+    keys[i] = static_cast<uint32_t>(top2[i]) * static_cast<uint32_t>(B) + static_cast<uint32_t>(top2[i ^ 1]);
+    vals[i] = static_cast<int32_t>(i >> 1);
+}
+
+__global__ void seg_offsets_scaled_kernel(const uint32_t* __restrict__ keys_sorted, int64_t n, int32_t B,
+                                          int64_t* __restrict__ offsets)
+{
+    const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (b > B) return;
+    const uint64_t want = static_cast<uint64_t>(b) * static_cast<uint64_t>(B);
+    int64_t lo = 0, hi = n;  // first index with key >= b * B
+    while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (static_cast<uint64_t>(keys_sorted[mid]) < want) lo = mid + 1;
+        else hi = mid;
+    }
+    offsets[b] = lo;
+}
+
+__global__ void mem_rows_kernel(const uint32_t* __restrict__ keys_sorted, const int32_t* __restrict__ members,
+                                const int32_t* __restrict__ top2, int64_t n2, int32_t B, int64_t* __restrict__ mem_row)
+{
+    const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j >= n2) return;
+    const int64_t p = members[j];
+    const int32_t lo_b = min(top2[2 * p], top2[2 * p + 1]);
+    const int way = static_cast<int32_t>(keys_sorted[j] / static_cast<uint32_t>(B)) == lo_b ? 0 : 1;
+    mem_row[2 * p + way] = j;
+}
+
+// ---------------------------------------------------------------- merge
+// Warp per point.  Output positions follow the two-pointer rule of the
+// reference: running entry i lands at i + #{kept new j : bd[j] < ad[i]},
+// kept new entry j at rank_j + #{i : ad[i] <= bd[j]}; a new id already in
+// the running list is dropped.  Lists are ascending, padded with -1 / +inf.
+constexpr int kMergeWarps = 8;
+constexpr int kMaxM = 128;
+
+__global__ void __launch_bounds__(kMergeWarps * 32)
+    merge_kernel(const int32_t* __restrict__ run_n, const float* __restrict__ run_d, const int32_t* __restrict__ new_n,
+                 const float* __restrict__ new_d, const int64_t* __restrict__ mem_row, int64_t N, int M,
+                 int32_t* __restrict__ out_n, float* __restrict__ out_d)
+{
+    __shared__ int32_t s_an[kMergeWarps][kMaxM], s_bn[kMergeWarps][kMaxM];
+    __shared__ float s_ad[kMergeWarps][kMaxM], s_bd[kMergeWarps][kMaxM];
+    __shared__ int s_rank[kMergeWarps][kMaxM];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t p = static_cast<int64_t>(blockIdx.x) * kMergeWarps + w;
+    if (p >= N) return;
+    const int64_t ra = mem_row ? mem_row[2 * p] : p;
+    const int64_t rb = mem_row ? mem_row[2 * p + 1] : p;
+    const int32_t* an = run_n + ra * M; const float* ad = run_d + ra * M;
+    const int32_t* bn = new_n + rb * M; const float* bd = new_d + rb * M;
+    int na = M, nb = M;
+    for (int k = lane; k < M; k += 32) {
+        const int32_t x = an[k], y = bn[k];
+        s_an[w][k] = x; s_ad[w][k] = ad[k]; s_bn[w][k] = y; s_bd[w][k] = bd[k];
+        if (x < 0) na = min(na, k);
+        if (y < 0) nb = min(nb, k);
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+        na = min(na, __shfl_xor_sync(0xffffffffu, na, off));
+        nb = min(nb, __shfl_xor_sync(0xffffffffu, nb, off));
+    }
+    __syncwarp();
+    int base = 0;
+    for (int g = 0; g < (M + 31) / 32; ++g) {
+        const int j = g * 32 + lane;
+        bool keep = false;
+        if (j < nb) {
+            const int32_t id = s_bn[w][j];
+            keep = true;
+            for (int k = 0; k < na; ++k) keep &= (s_an[w][k] != id);
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, keep);
+        if (j < M) s_rank[w][j] = keep ? base + __popc(m & ((1u << lane) - 1u)) : -1;
+        base += __popc(m);
+    }
+    __syncwarp();
+    const int n_keep = base;
+    int32_t* on = out_n + p * M; float* od = out_d + p * M;
+    for (int i = lane; i < na; i += 32) {
+        const float x = s_ad[w][i];
+        int c = 0;
+        for (int j = 0; j < nb; ++j) c += (s_rank[w][j] >= 0 && s_bd[w][j] < x);
+        const int pos = i + c;
+        if (pos < M) { on[pos] = s_an[w][i]; od[pos] = x; }
+    }
+    for (int j = lane; j < nb; j += 32) {
+        const int k = s_rank[w][j];
+        if (k < 0) continue;
+        const float x = s_bd[w][j];
+        int c = 0;
+        for (int i = 0; i < na; ++i) c += (s_ad[w][i] <= x);
+        const int pos = k + c;
+        if (pos < M) { on[pos] = s_bn[w][j]; od[pos] = x; }
+    }
+    for (int q = na + n_keep + lane; q < M; q += 32) { on[q] = -1; od[q] = INFINITY; }
+}
+
+// ---------------------------------------------------------------- sanitize
+__global__ void sanitize_kernel(const int32_t* __restrict__ knn, int64_t N, int M, uint32_t* __restrict__ out)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (i >= N) return;
+    const int32_t* row = knn + i * M;
+    uint32_t fallback = static_cast<uint32_t>((i + 1) % N);
+    for (int g = 0; g < M; g += 32) {
+        const int j = g + lane;
+        const int32_t v = j < M ? row[j] : -1;
+        const bool ok = v >= 0 && static_cast<int64_t>(v) < N && static_cast<int64_t>(v) != i;
+        const unsigned m = __ballot_sync(0xffffffffu, ok);
+        if (m) { fallback = static_cast<uint32_t>(__shfl_sync(0xffffffffu, v, __ffs(m) - 1)); break; }
+    }
+    for (int j = lane; j < M; j += 32) {
+        const int32_t v = row[j];
+        const bool ok = v >= 0 && static_cast<int64_t>(v) < N && static_cast<int64_t>(v) != i;
+        out[i * M + j] = ok ? static_cast<uint32_t>(v) : fallback;
+    }
+}
+
+// ---------------------------------------------------------------- detour prune
+constexpr int kPruneWarps = 8;
+constexpr int kMaxHash = 256;
+
+__device__ __forceinline__ uint32_t hash_id(uint32_t id, uint32_t mask) { return (id * 2654435761u) & mask; }
+
+// Warp per row a (processed in `order` when given: rows of one bucket region
+// together, so the neighbour rows they gather stay in L2).  Row a's candidates
+// go into a shared-memory id -> rank hash; for every closer candidate D (rank
+// kAD) the warp streams D's row, marks which later ranks kAB of a's row it
+// contains (each (kAD, kAB) once: a bit mask OR-reduced over the warp), and
+// counts them.  Two neighbour rows are loaded before they are processed.
+__global__ void __launch_bounds__(kPruneWarps * 32, 8)
+    prune_kernel(const uint32_t* __restrict__ g, int64_t N, int M, int K, const int32_t* __restrict__ order,
+                 uint32_t* __restrict__ out, int* err)
+{
+    __shared__ uint32_t s_row[kPruneWarps][kMaxM];
+    __shared__ uint32_t s_hkey[kPruneWarps][kMaxHash];
+    __shared__ uint8_t s_hrank[kPruneWarps][kMaxHash];
+    __shared__ uint32_t s_cnt[kPruneWarps][kMaxM];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t gw = static_cast<int64_t>(blockIdx.x) * kPruneWarps + w;
+    if (gw >= N) return;
+    const int64_t a = order ? static_cast<int64_t>(order[gw]) : gw;
+    uint32_t cap = 16;
+    while (cap < 2u * static_cast<uint32_t>(M)) cap <<= 1;
+    const uint32_t mask = cap - 1;
+    for (uint32_t h = lane; h < cap; h += 32) s_hkey[w][h] = kEmpty;
+    const uint32_t* ra = g + a * M;
+    for (int k = lane; k < M; k += 32) s_row[w][k] = ra[k];
+    __syncwarp();
+    for (int k = lane; k < M; k += 32) {
+        const uint32_t id = s_row[w][k];
+        uint32_t h = hash_id(id, mask);
+        for (;;) {
+            const uint32_t old = atomicCAS(&s_hkey[w][h], kEmpty, id);
+            if (old == kEmpty) { s_hrank[w][h] = static_cast<uint8_t>(k); break; }
+            h = (h + 1) & mask;
+        }
+    }
+    __syncwarp();
+    const int G = (M + 31) / 32;
+    uint32_t cnt[kMaxM / 32] = {0, 0, 0, 0};
+    constexpr int kAhead = 2;
+    for (int kb = 0; kb < M - 1; kb += kAhead) {
+        uint32_t vals[kAhead][kMaxM / 32];
+#pragma unroll
+        for (int u = 0; u < kAhead; ++u) {
+            const int kAD = kb + u;
+            const uint32_t dd = (kAD < M - 1) ? s_row[w][kAD] : kEmpty;
+            const bool okd = kAD < M - 1 && static_cast<int64_t>(dd) < N;
+            if (kAD < M - 1 && !okd && lane == 0) atomicCAS(err, 0, kDevBadIndex);
+            const uint32_t* rd = g + static_cast<int64_t>(okd ? dd : 0) * M;
+#pragma unroll
+            for (int gi = 0; gi < kMaxM / 32; ++gi) {
+                const int kDB = gi * 32 + lane;
+                vals[u][gi] = (okd && gi < G && kDB < M) ? rd[kDB] : kEmpty;
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kAhead; ++u) {
+            const int kAD = kb + u;
+            if (kAD >= M - 1) break;
+            uint32_t hit[kMaxM / 32] = {0, 0, 0, 0};
+#pragma unroll
+            for (int gi = 0; gi < kMaxM / 32; ++gi) {
+                const uint32_t bv = vals[u][gi];
+                if (bv == kEmpty) continue;
+                for (uint32_t h = hash_id(bv, mask); s_hkey[w][h] != kEmpty; h = (h + 1) & mask) {
+                    if (s_hkey[w][h] != bv) continue;
+                    const int kAB = s_hrank[w][h];
+                    if (kAB > kAD) hit[kAB >> 5] |= 1u << (kAB & 31);
+                }
+            }
+#pragma unroll
+            for (int gi = 0; gi < kMaxM / 32; ++gi) {
+                if (gi >= G) break;
+                uint32_t v = hit[gi];
+                for (int off = 16; off > 0; off >>= 1) v |= __shfl_xor_sync(0xffffffffu, v, off);
+                cnt[gi] += (v >> lane) & 1u;
+            }
+        }
+    }
+#pragma unroll
+    for (int gi = 0; gi < kMaxM / 32; ++gi) {
+        const int k = gi * 32 + lane;
+        if (gi < G && k < M) s_cnt[w][k] = cnt[gi];
+    }
+    __syncwarp();
+    // position of entry k = #{k' : (cnt[k'], k') < (cnt[k], k)}; the first K positions are kept
+    for (int k = lane; k < M; k += 32) {
+        const uint32_t c = s_cnt[w][k];
+        int pos = 0;
+        for (int k2 = 0; k2 < M; ++k2) {
+            const uint32_t c2 = s_cnt[w][k2];
+            pos += (c2 < c) || (c2 == c && k2 < k);
+        }
+        if (pos < K) out[a * K + pos] = s_row[w][k];
+    }
+}
+
+// Rows grouped by (nearest bucket, second bucket): the processing order that
+// keeps a warp's neighbour rows in L2 (same grouping as the memberships).
+__global__ void locality_keys_kernel(const int32_t* __restrict__ top2, int64_t N, int32_t B, uint32_t* __restrict__ keys,
+                                     int32_t* __restrict__ vals)
+{
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= N) return;
+    keys[i] = static_cast<uint32_t>(top2[2 * i]) * static_cast<uint32_t>(B) + static_cast<uint32_t>(top2[2 * i + 1]);
+    vals[i] = static_cast<int32_t>(i);
+}
+
+// ---------------------------------------------------------------- reverse edges
+__global__ void rev_count_kernel(const uint32_t* __restrict__ pruned, int64_t NK, int64_t N,
+                                 unsigned long long* __restrict__ indeg)
+{
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (e >= NK) return;
+    const uint32_t dst = pruned[e];
+    if (static_cast<int64_t>(dst) < N) atomicAdd(&indeg[dst], 1ull);
+}
+
+__global__ void rev_scatter_kernel(const uint32_t* __restrict__ pruned, int64_t N, int K,
+                                   const uint64_t* __restrict__ off, uint32_t* __restrict__ cursor,
+                                   uint64_t* __restrict__ keys)
+{
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (e >= N * K) return;
+    const uint32_t dst = pruned[e];
+    if (static_cast<int64_t>(dst) >= N) return;
+    const uint64_t src = static_cast<uint64_t>(e / K), rank = static_cast<uint64_t>(e % K);
+    const uint64_t pos = off[dst] + atomicAdd(&cursor[dst], 1u);
+    keys[pos] = (rank << 32) | src;
+}
+
+constexpr int kRevWarps = 4;
+constexpr int kRevSort = 512;
+
+__global__ void __launch_bounds__(kRevWarps * 32)
+    rev_merge_kernel(const uint32_t* __restrict__ pruned, int64_t N, int K, const uint64_t* __restrict__ off,
+                     const uint64_t* __restrict__ keys, uint32_t* __restrict__ out)
+{
+    __shared__ uint64_t s_keys[kRevWarps][kRevSort];
+    __shared__ uint32_t s_row[kRevWarps][kMaxM];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t j = static_cast<int64_t>(blockIdx.x) * kRevWarps + w;
+    if (j >= N) return;
+    const uint64_t lo = off[j], hi = off[j + 1];
+    const int64_t len = static_cast<int64_t>(hi - lo);
+    uint64_t* sk = s_keys[w];
+    // the K smallest (rank, src) keys of this destination, ascending
+    int n_keep = 0;
+    if (len <= kRevSort) {
+        int np2 = 1;
+        while (np2 < len) np2 <<= 1;
+        for (int t = lane; t < np2; t += 32) sk[t] = t < len ? keys[lo + t] : ~0ull;
+        __syncwarp();
+        for (int k = 2; k <= np2; k <<= 1)
+            for (int jj = k >> 1; jj > 0; jj >>= 1) {
+                for (int t = lane; t < (np2 >> 1); t += 32) {
+                    const int i = 2 * jj * (t / jj) + (t % jj), l = i + jj;
+                    const bool up = (i & k) == 0;
+                    const uint64_t x = sk[i], y = sk[l];
+                    if ((x > y) == up) { sk[i] = y; sk[l] = x; }
+                }
+                __syncwarp();
+            }
+        n_keep = static_cast<int>(len < K ? len : static_cast<int64_t>(K));
+    } else {
+        for (int t = lane; t < kRevSort; t += 32) sk[t] = ~0ull;
+        __syncwarp();
+        for (int64_t c0 = 0; c0 < len; c0 += kRevSort / 2) {
+            for (int t = lane; t < kRevSort / 2; t += 32)
+                sk[kRevSort / 2 + t] = (c0 + t < len) ? keys[lo + c0 + t] : ~0ull;
+            __syncwarp();
+            for (int k = 2; k <= kRevSort; k <<= 1)
+                for (int jj = k >> 1; jj > 0; jj >>= 1) {
+                    for (int t = lane; t < (kRevSort >> 1); t += 32) {
+                        const int i = 2 * jj * (t / jj) + (t % jj), l = i + jj;
+                        const bool up = (i & k) == 0;
+                        const uint64_t x = sk[i], y = sk[l];
+                        if ((x > y) == up) { sk[i] = y; sk[l] = x; }
+                    }
+                    __syncwarp();
+                }
+        }
+        n_keep = K;
+    }
+    // protected merge of the reverse sources, weakest first
+    for (int k = lane; k < K; k += 32) s_row[w][k] = pruned[j * K + k];
+    __syncwarp();
+    const int np = K / 2;
+    for (int t = n_keep - 1; t >= 0; --t) {
+        const uint32_t src = static_cast<uint32_t>(sk[t] & 0xffffffffu);
+        int pos = K;
+        for (int g0 = 0; g0 < K; g0 += 32) {
+            const int k = g0 + lane;
+            const unsigned m = __ballot_sync(0xffffffffu, k < K && s_row[w][k] == src);
+            if (m) { pos = g0 + __ffs(m) - 1; break; }
+        }
+        if (pos < np) continue;
+        const int ns = (pos == K) ? (K - np - 1) : (pos - np);
+        uint32_t nv[kMaxM / 32];
+#pragma unroll
+        for (int gi = 0; gi < kMaxM / 32; ++gi) {
+            const int k = gi * 32 + lane;
+            nv[gi] = 0;
+            if (k < K) nv[gi] = (k == np) ? src : ((k > np && k <= np + ns) ? s_row[w][k - 1] : s_row[w][k]);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int gi = 0; gi < kMaxM / 32; ++gi) {
+            const int k = gi * 32 + lane;
+            if (k < K) s_row[w][k] = nv[gi];
+        }
+        __syncwarp();
+    }
+    for (int k = lane; k < K; k += 32) out[j * K + k] = s_row[w][k];
+}
+
+// ---------------------------------------------------------------- row sort by exact distance
+__global__ void sort_rows_kernel(const float* __restrict__ X, int d, int d_pad, const int32_t* __restrict__ knn,
+                                 int64_t N, int M, int32_t* __restrict__ out)
+{
+    __shared__ uint64_t s_keys[4][kMaxM];
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * 4 + w;
+    if (i >= N) return;
+    int np2 = 1;
+    while (np2 < M) np2 <<= 1;
+    for (int k = lane; k < np2; k += 32) {
+        uint64_t key = ~0ull;
+        if (k < M) {
+            const int32_t id = knn[i * M + k];
+            if (id >= 0 && static_cast<int64_t>(id) < N) {
+                const float dd = exact_l2_f(X + i * d_pad, X + static_cast<int64_t>(id) * d_pad, d);
+                key = (static_cast<uint64_t>(f2key(dd)) << 32) | static_cast<uint32_t>(k);
+            }
+        }
+        s_keys[w][k] = key;
+    }
+    __syncwarp();
+    for (int k = 2; k <= np2; k <<= 1)
+        for (int jj = k >> 1; jj > 0; jj >>= 1) {
+            for (int t = lane; t < (np2 >> 1); t += 32) {
+                const int a = 2 * jj * (t / jj) + (t % jj), l = a + jj;
+                const bool up = (a & k) == 0;
+                const uint64_t x = s_keys[w][a], y = s_keys[w][l];
+                if ((x > y) == up) { s_keys[w][a] = y; s_keys[w][l] = x; }
+            }
+            __syncwarp();
+        }
+    for (int k = lane; k < M; k += 32) {
+        const uint64_t key = s_keys[w][k];
+        out[i * M + k] = key == ~0ull ? -1 : knn[i * M + static_cast<int>(key & 0xffffffffu)];
+    }
+}
+
+__global__ void max_sqrt_kernel(const float* __restrict__ v, int64_t n, unsigned* __restrict__ out)
+{
+    float m = 0.0f;
+    for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        m = fmaxf(m, sqrtf(fmaxf(v[i], 0.0f)));
+    for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    if ((threadIdx.x & 31) == 0) atomicMax(out, __float_as_uint(m));
+}
+
+unsigned blocks_for(int64_t n, int per) { return static_cast<unsigned>((n + per - 1) / per); }
+
+}  // namespace
+
+// ============================================================================ host launchers
+void convert_rows(const void* X, int dtype, int d, const int32_t* row_ids, int64_t n_out, void* out, int out_elem,
+                  int d_pad, float* norms, cudaStream_t st)
+{
+    if (n_out == 0) return;
+    switch (dtype) {
+        case 0: convert_dispatch_out(static_cast<const float*>(X), d, row_ids, n_out, out, out_elem, d_pad, norms, st); break;
+        case 1: convert_dispatch_out(static_cast<const uint8_t*>(X), d, row_ids, n_out, out, out_elem, d_pad, norms, st); break;
+        case 2: convert_dispatch_out(static_cast<const int8_t*>(X), d, row_ids, n_out, out, out_elem, d_pad, norms, st); break;
+        default: throw Error(kInvalid, "convert_rows: unknown dtype");
+    }
+    GTA_CUDA(cudaGetLastError());
+}
+
+void sample_ids(int64_t N, int64_t n_s, uint64_t seed, int32_t* out, cudaStream_t st)
+{
+    if (n_s >= N) {
+        iota_kernel<<<blocks_for(N, 256), 256, 0, st>>>(out, N);
+        count_launches(1);
+    } else {
+        sample_ids_kernel<<<blocks_for(n_s, 256), 256, 0, st>>>(N, n_s, seed, out);
+        count_launches(1);
+    }
+    GTA_CUDA(cudaGetLastError());
+}
+
+void kmeanspp_init(const float* pool, const float* /*pool_norm*/, int64_t pool_n, int d, int d_pad, int32_t B,
+                   uint64_t seed, float* C, int* /*err*/, cudaStream_t st)
+{
+    GTA_REQUIRE(pool_n >= 1 && B >= 1, kInvalid, "kmeans++: empty pool");
+    const int64_t chunk = std::max<int64_t>(256, (pool_n + 295) / 296);
+    const unsigned grid = static_cast<unsigned>((pool_n + chunk - 1) / chunk);
+    DevBuf<float> min_d2(static_cast<size_t>(pool_n), st);
+    DevBuf<double> bsum(grid, st);
+    DevBuf<unsigned> counter(1, st);
+    GTA_CUDA(cudaMemsetAsync(counter.get(), 0, sizeof(unsigned), st));
+    GTA_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * static_cast<size_t>(B) * d_pad, st));
+    kpp_first_kernel<<<1, 128, 0, st>>>(pool, pool_n, d_pad, seed, C);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+    const size_t smem = sizeof(float) * static_cast<size_t>(d);
+    for (int t = 0; t < B; ++t) {
+        kpp_step_kernel<<<grid, kKppThreads, smem, st>>>(pool, pool_n, d, d_pad, C, t, B, min_d2.get(), bsum.get(),
+                                                         counter.get(), seed, chunk);
+        count_launches(1);
+    }
+    GTA_CUDA(cudaGetLastError());
+}
+
+void centroid_update(const float* Xs, int64_t n_s, int d, int d_pad, const int32_t* assign, const float* C_in,
+                     int32_t B, float* C_out, float* C_norm, cudaStream_t st)
+{
+    DevBuf<int32_t> keys_out(n_s, st), idx_in(n_s, st), idx_out(n_s, st);
+    DevBuf<int64_t> offsets(static_cast<size_t>(B) + 1, st);
+    iota_kernel<<<blocks_for(n_s, 256), 256, 0, st>>>(idx_in.get(), n_s);
+    count_launches(1);
+    int end_bit = 1;
+    while ((1ll << end_bit) < B) ++end_bit;
+    size_t tmp = 0;
+    GTA_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tmp, assign, keys_out.get(), idx_in.get(), idx_out.get(),
+                                             static_cast<int>(n_s), 0, end_bit, st));
+    DevBuf<uint8_t> tbuf(tmp, st);
+    GTA_CUDA(cub::DeviceRadixSort::SortPairs(tbuf.get(), tmp, assign, keys_out.get(), idx_in.get(), idx_out.get(),
+                                             static_cast<int>(n_s), 0, end_bit, st));
+    seg_offsets_kernel<<<blocks_for(B + 1, 256), 256, 0, st>>>(keys_out.get(), n_s, B, offsets.get());
+    count_launches(1);
+    ProfScope prof("kmeans_update", 4.0 * static_cast<double>(n_s) * d, st);
+    centroid_sum_kernel<<<B, 128, 0, st>>>(Xs, d, d_pad, idx_out.get(), offsets.get(), C_in, C_out);
+    count_launches(1);
+    if (C_norm) convert_rows(C_out, 0, d_pad, nullptr, B, C_out, kElemF32, d_pad, C_norm, st);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void build_memberships(const int32_t* top2, int64_t N, int32_t B, int32_t* members, int64_t* offsets,
+                       int64_t* mem_row, cudaStream_t st)
+{
+    const int64_t n2 = 2 * N;
+    GTA_REQUIRE(n2 < (1ll << 31), kInvalid, "memberships: more than 2^31 memberships on one device");
+    GTA_REQUIRE(static_cast<int64_t>(B) * B < (1ll << 32), kInvalid, "memberships: n_buckets must be below 65536");
+    DevBuf<uint32_t> keys_in(n2, st), keys_out(n2, st);
+    DevBuf<int32_t> vals_in(n2, st);
+    ProfScope prof("memberships", 24.0 * static_cast<double>(n2), st);
+    membership_pairs_kernel<<<blocks_for(n2, 256), 256, 0, st>>>(top2, N, B, keys_in.get(), vals_in.get());
+    count_launches(1);
+    int end_bit = 1;
+    while ((1ll << end_bit) < static_cast<int64_t>(B) * B) ++end_bit;
+    size_t tmp = 0;
+    GTA_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tmp, keys_in.get(), keys_out.get(), vals_in.get(), members,
+                                             static_cast<int>(n2), 0, end_bit, st));
+    DevBuf<uint8_t> tbuf(tmp, st);
+    GTA_CUDA(cub::DeviceRadixSort::SortPairs(tbuf.get(), tmp, keys_in.get(), keys_out.get(), vals_in.get(), members,
+                                             static_cast<int>(n2), 0, end_bit, st));
+    seg_offsets_scaled_kernel<<<blocks_for(B + 1, 256), 256, 0, st>>>(keys_out.get(), n2, B, offsets);
+    count_launches(1);
+    mem_rows_kernel<<<blocks_for(n2, 256), 256, 0, st>>>(keys_out.get(), members, top2, n2, B, mem_row);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void merge_memberships(const int32_t* list_n, const float* list_d, const int64_t* mem_row, int64_t N, int M,
+                       int32_t* out_n, float* out_d, cudaStream_t st)
+{
+    GTA_REQUIRE(M >= 1 && M <= kMaxM, kInvalid, "merge: M must be in [1, 128]");
+    ProfScope prof("merge", 24.0 * M * static_cast<double>(N), st);
+    merge_kernel<<<blocks_for(N, kMergeWarps), kMergeWarps * 32, 0, st>>>(list_n, list_d, list_n, list_d, mem_row, N, M,
+                                                                          out_n, out_d);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void merge_lists(const int32_t* run_n, const float* run_d, const int32_t* new_n, const float* new_d, int64_t N,
+                 int M, int32_t* out_n, float* out_d, cudaStream_t st)
+{
+    GTA_REQUIRE(M >= 1 && M <= kMaxM, kInvalid, "merge: M must be in [1, 128]");
+    merge_kernel<<<blocks_for(N, kMergeWarps), kMergeWarps * 32, 0, st>>>(run_n, run_d, new_n, new_d, nullptr, N, M,
+                                                                          out_n, out_d);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void sanitize(const int32_t* knn, int64_t N, int M, uint32_t* out, cudaStream_t st)
+{
+    ProfScope prof("sanitize", 8.0 * M * static_cast<double>(N), st);
+    sanitize_kernel<<<blocks_for(N, 8), 256, 0, st>>>(knn, N, M, out);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void prune_detour(const uint32_t* g, int64_t N, int M, int K, const int32_t* order, uint32_t* out, int* err,
+                  cudaStream_t st)
+{
+    GTA_REQUIRE(M >= 2 && M <= kMaxM && K >= 1 && K <= M, kInvalid, "prune: need 1 <= K <= M <= 128");
+    ProfScope prof("prune", (4.0 * M * (M + 1) + 4.0 * K) * static_cast<double>(N), st);
+    prune_kernel<<<blocks_for(N, kPruneWarps), kPruneWarps * 32, 0, st>>>(g, N, M, K, order, out, err);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void locality_order(const int32_t* top2, int64_t N, int32_t B, int32_t* order, cudaStream_t st)
+{
+    GTA_REQUIRE(static_cast<int64_t>(B) * B < (1ll << 32), kInvalid, "locality order: n_buckets must be below 65536");
+    DevBuf<uint32_t> keys_in(N, st), keys_out(N, st);
+    DevBuf<int32_t> vals_in(N, st);
+    locality_keys_kernel<<<blocks_for(N, 256), 256, 0, st>>>(top2, N, B, keys_in.get(), vals_in.get());
+    count_launches(1);
+    int end_bit = 1;
+    while ((1ll << end_bit) < static_cast<int64_t>(B) * B) ++end_bit;
+    size_t tmp = 0;
+    GTA_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tmp, keys_in.get(), keys_out.get(), vals_in.get(), order,
+                                             static_cast<int>(N), 0, end_bit, st));
+    DevBuf<uint8_t> tbuf(tmp, st);
+    GTA_CUDA(cub::DeviceRadixSort::SortPairs(tbuf.get(), tmp, keys_in.get(), keys_out.get(), vals_in.get(), order,
+                                             static_cast<int>(N), 0, end_bit, st));
+    GTA_CUDA(cudaGetLastError());
+}
+
+void reverse_merge(const uint32_t* pruned, int64_t N, int K, uint32_t* out, int* /*err*/, cudaStream_t st)
+{
+    GTA_REQUIRE(K >= 1 && K <= kMaxM, kInvalid, "reverse: K must be in [1, 128]");
+    const int64_t NK = N * K;
+    ProfScope prof("reverse", 32.0 * K * static_cast<double>(N), st);
+    DevBuf<unsigned long long> indeg(static_cast<size_t>(N) + 1, st);
+    DevBuf<uint32_t> cursor(static_cast<size_t>(N), st);
+    DevBuf<uint64_t> off(static_cast<size_t>(N) + 1, st), keys(static_cast<size_t>(NK), st);
+    GTA_CUDA(cudaMemsetAsync(indeg.get(), 0, sizeof(unsigned long long) * (N + 1), st));
+    GTA_CUDA(cudaMemsetAsync(cursor.get(), 0, sizeof(uint32_t) * N, st));
+    rev_count_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, NK, N, indeg.get());
+    count_launches(1);
+    size_t tmp = 0;
+    GTA_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tmp, indeg.get(), off.get(), static_cast<int>(N + 1), st));
+    DevBuf<uint8_t> tbuf(tmp, st);
+    GTA_CUDA(cub::DeviceScan::ExclusiveSum(tbuf.get(), tmp, indeg.get(), off.get(), static_cast<int>(N + 1), st));
+    rev_scatter_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, N, K, off.get(), cursor.get(), keys.get());
+    count_launches(1);
+    rev_merge_kernel<<<blocks_for(N, kRevWarps), kRevWarps * 32, 0, st>>>(pruned, N, K, off.get(), keys.get(), out);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void sort_rows_l2(const float* X, int d, int d_pad, const int32_t* knn, int64_t N, int M, int32_t* out, cudaStream_t st)
+{
+    GTA_REQUIRE(M >= 1 && M <= kMaxM, kInvalid, "sort_rows: M must be in [1, 128]");
+    sort_rows_kernel<<<blocks_for(N, 4), 128, 0, st>>>(X, d, d_pad, knn, N, M, out);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void max_sqrt(const float* v, int64_t n, float* out, cudaStream_t st)
+{
+    GTA_CUDA(cudaMemsetAsync(out, 0, sizeof(float), st));
+    const unsigned grid = static_cast<unsigned>(std::min<int64_t>(1184, std::max<int64_t>(1, (n + 255) / 256)));
+    max_sqrt_kernel<<<grid, 256, 0, st>>>(v, n, reinterpret_cast<unsigned*>(out));
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void check_device_error(const int* err, cudaStream_t st, const char* what)
+{
+    int h = 0;
+    GTA_CUDA(cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    GTA_CUDA(cudaStreamSynchronize(st));
+    if (h != 0) {
+        static const char* names[] = {"ok", "TMA tile wait timed out", "pipeline stage wait timed out",
+                                      "accumulator wait timed out", "teardown wait timed out", "id out of range",
+                                      "unsupported shape"};
+        const char* n = (h >= 0 && h <= 6) ? names[h] : "unknown device error";
+        throw Error(h == kDevBadIndex ? kData : kCuda, std::string(what) + ": " + n);
+    }
+}
+
+}  // namespace gta

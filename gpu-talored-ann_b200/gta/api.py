@@ -1,0 +1,264 @@
+"""Python host layer over the libgta C ABI.
+
+Mirrors the reference's build-path interface (paths relative to the reference
+project root):
+
+  build_bucket      bucket2 Steps 2-6 / GpuResidentKnn::run_round (bucketDemo/buildBucket/src/bucket.cu:8523, :5310)
+  optimize          cuvs cagra::helpers::optimize (bucketDemo/buildBucket/src/optimize.cu:396)
+  build_cagra       bucket2 --fused-optimize-degree (bucket.cu:8434 fused_optimize_translate)
+  kmeans_init       kmeans_pp_centers (bucketDemo/build_bucket.py:189)
+  kmeans_fit        refine_centers_kmeans (bucketDemo/build_bucket.py:232)
+  assign_topk       topk_from_A_to_B(X, C, k) (bucketDemo/build_bucket.py:96)
+  merge_lists       resident_merge_kernel (bucket.cu:5025)
+  sanitize          sanitize_to_uint32_inplace (optimize.cu:95)
+  prune / reverse_merge   prune_windowed_core.hpp:190-263 / edge_chunk_accumulator.hpp:386-494
+
+Device arrays are torch CUDA tensors (torch supplies device memory and the
+current stream only; every computation runs in libgta's own kernels).  Host
+arrays are numpy arrays.  Errors raise ``GtaError`` carrying the C status code.
+"""
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import numpy as np
+
+from . import _lib as L
+
+_DT = {"float32": L.GTA_F32, "uint8": L.GTA_U8, "int8": L.GTA_I8}
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _is_dev(x) -> bool:
+    return hasattr(x, "is_cuda") and x.is_cuda
+
+
+def _ptr(x) -> ctypes.c_void_p:
+    if x is None:
+        return ctypes.c_void_p(0)
+    if _is_dev(x):
+        assert x.is_contiguous(), "device arrays must be contiguous"
+        return ctypes.c_void_p(x.data_ptr())
+    assert isinstance(x, np.ndarray) and x.flags["C_CONTIGUOUS"], "host arrays must be C-contiguous numpy arrays"
+    return x.ctypes.data_as(ctypes.c_void_p)
+
+
+def _stream():
+    torch = _torch()
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _dtype_code(x) -> int:
+    name = str(x.dtype).replace("torch.", "")
+    if name not in _DT:
+        raise L.GtaError(L.GTA_EINVAL, f"unsupported dataset dtype {x.dtype}")
+    return _DT[name]
+
+
+def _empty(shape, dtype, like_dev: bool):
+    if like_dev:
+        torch = _torch()
+        return torch.empty(shape, dtype=getattr(torch, dtype), device="cuda")
+    return np.empty(shape, dtype=dtype)
+
+
+def _dataset(X, metric: str = "l2") -> L.gta_dataset:
+    return L.gta_dataset(data=_ptr(X), n=X.shape[0], d=X.shape[1], dtype=_dtype_code(X),
+                         metric=L.GTA_IP if metric == "ip" else L.GTA_L2, on_device=1 if _is_dev(X) else 0)
+
+
+def _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, init_centroids, dev, cent_out, top2_out):
+    return L.gta_bucket_params(
+        n_buckets=n_buckets, kmeans_iters=kmeans_iters, knn_degree=knn_degree, reserved0=0,
+        kmeans_sample=kmeans_sample, seed=seed, init_centroids=_ptr(init_centroids),
+        init_on_device=1 if (init_centroids is not None and _is_dev(init_centroids)) else 0,
+        out_on_device=1 if dev else 0, centroids_out=_ptr(cent_out), top2_out=_ptr(top2_out))
+
+
+# ---------------------------------------------------------------- pipeline
+def build_bucket(X, n_buckets: int, knn_degree: int = 64, kmeans_iters: int = 10, kmeans_sample: int = 0,
+                 seed: int = 42, init_centroids=None, metric: str = "l2", with_extras: bool = False):
+    """Bucketed kNN graph of X (N x d, float32 / uint8 / int8; torch CUDA tensor or numpy).
+
+    Returns (ids[N, M] int32, dists[N, M] float32) on X's side (device or host);
+    with ``with_extras`` also the final centroids (B x d) and top-2 buckets (N x 2).
+    """
+    dev = _is_dev(X)
+    N, d = X.shape
+    ids = _empty((N, knn_degree), "int32", dev)
+    dists = _empty((N, knn_degree), "float32", dev)
+    cent = _empty((n_buckets, d), "float32", dev) if with_extras else None
+    top2 = _empty((N, 2), "int32", dev) if with_extras else None
+    ds = _dataset(X, metric)
+    p = _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, init_centroids, dev, cent, top2)
+    L.check(L.lib().gta_build_bucket(ctypes.byref(ds), ctypes.byref(p), _ptr(ids), _ptr(dists),
+                                     _stream() if dev else ctypes.c_void_p(0)))
+    if with_extras:
+        return ids, dists, cent, top2
+    return ids, dists
+
+
+def build_cagra(X, n_buckets: int, knn_degree: int = 64, graph_degree: int = 32, kmeans_iters: int = 10,
+                kmeans_sample: int = 0, seed: int = 42, init_centroids=None, metric: str = "l2"):
+    """Whole build: bucketed kNN (degree M), sanitize, CAGRA optimize -> graph[N, K] uint32."""
+    dev = _is_dev(X)
+    N = X.shape[0]
+    graph = _empty((N, graph_degree), "uint32" if not dev else "int32", dev)
+    ds = _dataset(X, metric)
+    bp = _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, init_centroids, dev, None, None)
+    p = L.gta_cagra_params(bucket=bp, graph_degree=graph_degree, reserved0=0)
+    L.check(L.lib().gta_build_cagra(ctypes.byref(ds), ctypes.byref(p), _ptr(graph),
+                                    _stream() if dev else ctypes.c_void_p(0)))
+    return graph
+
+
+def optimize(knn, graph_degree: int):
+    """CAGRA optimize (prune + reverse edges) of a distance-sorted, sanitized uint32 graph (N x M)."""
+    dev = _is_dev(knn)
+    N, M = knn.shape
+    out = _empty((N, graph_degree), "int32" if dev else "uint32", dev)
+    L.check(L.lib().gta_optimize(_ptr(knn), N, M, graph_degree, _ptr(out), 1 if dev else 0,
+                                 _stream() if dev else ctypes.c_void_p(0)))
+    return out
+
+
+# ---------------------------------------------------------------- stages (device tensors)
+def kmeans_init(X, pool_n: int, n_buckets: int, seed: int = 42):
+    C = _empty((n_buckets, X.shape[1]), "float32", True)
+    L.check(L.lib().gta_kmeans_init(_ptr(X), pool_n, X.shape[1], n_buckets, seed, _ptr(C), _stream()))
+    return C
+
+
+def kmeans_fit(X, C0, iters: int):
+    C = C0.clone().contiguous()
+    assign = _empty((X.shape[0],), "int32", True)
+    L.check(L.lib().gta_kmeans_fit(_ptr(X), X.shape[0], X.shape[1], _ptr(C), C.shape[0], iters, _ptr(assign),
+                                   _stream()))
+    return C, assign
+
+
+def assign_topk(X, C, k: int):
+    ids = _empty((X.shape[0], k), "int32", True)
+    dists = _empty((X.shape[0], k), "float32", True)
+    L.check(L.lib().gta_assign_topk(_ptr(X), X.shape[0], X.shape[1], _ptr(C), C.shape[0], k, _ptr(ids), _ptr(dists),
+                                    _stream()))
+    return ids, dists
+
+
+def build_memberships(top2, n_buckets: int):
+    torch = _torch()
+    N = top2.shape[0]
+    members = torch.empty(2 * N, dtype=torch.int32, device="cuda")
+    offsets = torch.empty(n_buckets + 1, dtype=torch.int64, device="cuda")
+    mem_row = torch.empty((N, 2), dtype=torch.int64, device="cuda")
+    L.check(L.lib().gta_build_memberships(_ptr(top2), N, n_buckets, _ptr(members), _ptr(offsets), _ptr(mem_row),
+                                          _stream()))
+    return offsets, members, mem_row
+
+
+def bucket_knn(X, members, offsets, knn_degree: int):
+    n_mem = members.shape[0]
+    ids = _empty((n_mem, knn_degree), "int32", True)
+    dists = _empty((n_mem, knn_degree), "float32", True)
+    L.check(L.lib().gta_bucket_knn(_ptr(X), _dtype_code(X), X.shape[0], X.shape[1], _ptr(members), _ptr(offsets),
+                                   offsets.shape[0] - 1, knn_degree, _ptr(ids), _ptr(dists), _stream()))
+    return ids, dists
+
+
+def merge_memberships(list_ids, list_dists, mem_row):
+    N, M = mem_row.shape[0], list_ids.shape[1]
+    ids = _empty((N, M), "int32", True)
+    dists = _empty((N, M), "float32", True)
+    L.check(L.lib().gta_merge_memberships(_ptr(list_ids), _ptr(list_dists), _ptr(mem_row), N, M, _ptr(ids),
+                                          _ptr(dists), _stream()))
+    return ids, dists
+
+
+def merge_lists(run_ids, run_dists, new_ids, new_dists):
+    N, M = run_ids.shape
+    ids = _empty((N, M), "int32", True)
+    dists = _empty((N, M), "float32", True)
+    L.check(L.lib().gta_merge_lists(_ptr(run_ids), _ptr(run_dists), _ptr(new_ids), _ptr(new_dists), N, M, _ptr(ids),
+                                    _ptr(dists), _stream()))
+    return ids, dists
+
+
+def sanitize(knn):
+    out = _empty(tuple(knn.shape), "int32", True)
+    L.check(L.lib().gta_sanitize(_ptr(knn), knn.shape[0], knn.shape[1], _ptr(out), _stream()))
+    return out
+
+
+def sort_rows(X, knn):
+    out = _empty(tuple(knn.shape), "int32", True)
+    L.check(L.lib().gta_sort_rows(_ptr(X), X.shape[0], X.shape[1], _ptr(knn), knn.shape[1], _ptr(out), _stream()))
+    return out
+
+
+def prune(knn, graph_degree: int):
+    out = _empty((knn.shape[0], graph_degree), "int32", True)
+    L.check(L.lib().gta_prune(_ptr(knn), knn.shape[0], knn.shape[1], graph_degree, _ptr(out), _stream()))
+    return out
+
+
+def reverse_merge(pruned):
+    out = _empty(tuple(pruned.shape), "int32", True)
+    L.check(L.lib().gta_reverse_merge(_ptr(pruned), pruned.shape[0], pruned.shape[1], _ptr(out), _stream()))
+    return out
+
+
+# ---------------------------------------------------------------- files (host)
+def read_dataset(path: str, row0: int = 0, nrows: Optional[int] = None) -> np.ndarray:
+    n, d, dt = ctypes.c_int64(), ctypes.c_int32(), ctypes.c_int32()
+    L.check(L.lib().gta_read_dataset_header(path.encode(), ctypes.byref(n), ctypes.byref(d), ctypes.byref(dt)))
+    nrows = n.value - row0 if nrows is None else nrows
+    out = np.empty((nrows, d.value), dtype={0: np.float32, 1: np.uint8, 2: np.int8}[dt.value])
+    L.check(L.lib().gta_read_dataset(path.encode(), row0, nrows, _ptr(out)))
+    return out
+
+
+def write_dataset(path: str, X: np.ndarray) -> None:
+    X = np.ascontiguousarray(X)
+    L.check(L.lib().gta_write_dataset(path.encode(), _ptr(X), X.shape[0], X.shape[1], _dtype_code(X)))
+
+
+def write_knn(path: str, ids: np.ndarray) -> None:
+    ids = np.ascontiguousarray(ids, np.int32)
+    L.check(L.lib().gta_write_knn(path.encode(), _ptr(ids), ids.shape[0], ids.shape[1]))
+
+
+def write_knn_dists(path: str, dists: np.ndarray) -> None:
+    dists = np.ascontiguousarray(dists, np.float32)
+    L.check(L.lib().gta_write_knn_dists(path.encode(), _ptr(dists), dists.shape[0], dists.shape[1]))
+
+
+def read_knn(path: str) -> np.ndarray:
+    n, m = ctypes.c_int64(), ctypes.c_int32()
+    L.check(L.lib().gta_read_knn_header(path.encode(), ctypes.byref(n), ctypes.byref(m)))
+    out = np.empty((n.value, m.value), np.int32)
+    L.check(L.lib().gta_read_knn(path.encode(), _ptr(out)))
+    return out
+
+
+def write_graph(path: str, graph: np.ndarray) -> None:
+    graph = np.ascontiguousarray(graph, np.uint32)
+    L.check(L.lib().gta_write_graph(path.encode(), _ptr(graph), graph.shape[0], graph.shape[1]))
+
+
+def read_graph(path: str) -> np.ndarray:
+    n, k = ctypes.c_int64(), ctypes.c_int32()
+    L.check(L.lib().gta_read_graph_header(path.encode(), ctypes.byref(n), ctypes.byref(k)))
+    out = np.empty((n.value, k.value), np.uint32)
+    L.check(L.lib().gta_read_graph(path.encode(), _ptr(out)))
+    return out
+
+
+def write_npy(path: str, ids: np.ndarray) -> None:
+    ids = np.ascontiguousarray(ids, np.int32)
+    L.check(L.lib().gta_write_npy_i64(path.encode(), _ptr(ids), ids.shape[0], ids.shape[1]))

@@ -1,0 +1,215 @@
+/*
+ * gta.h -- C ABI of libgta, the B200 (sm_100a) bucketed kNN-graph / CAGRA build.
+ *
+ * Drop-in boundary for the reference's build path (loulankxh/GPU-talored-ANN;
+ * paths below are relative to the reference project root).  Plain pointers and
+ * sizes only; no exception crosses this boundary.
+ *
+ * Status codes (every int-returning entry point):
+ *   GTA_OK 0, GTA_EINVAL 1 (bad argument), GTA_ENOMEM 2 (does not fit / out of
+ *   memory; the reference's `optimize` exits 2 for "does not fit",
+ *   bucketDemo/buildBucket/src/optimize.cu:307), GTA_ECUDA 3, GTA_ENCCL 4,
+ *   GTA_EDATA 5 (input data failed a check: id out of range, not a permutation,
+ *   malformed file).  gta_last_error() returns the message of the calling
+ *   thread's last failure.
+ *
+ * Memory: pointers flagged `on_device` are CUDA device pointers on the current
+ * device; all work is ordered on `stream` (a cudaStream_t, NULL = default
+ * stream).  Stage entry points (gta_assign_topk ... gta_reverse_merge) take
+ * device pointers only and are stream-ordered; the library allocates its
+ * scratch with the stream-ordered allocator and frees it before returning.
+ * Entry points that return results in host memory synchronize the stream.
+ */
+#ifndef GTA_H_
+#define GTA_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GTA_OK 0
+#define GTA_EINVAL 1
+#define GTA_ENOMEM 2
+#define GTA_ECUDA 3
+#define GTA_ENCCL 4
+#define GTA_EDATA 5
+
+/* element types of a dataset (the BIGANN file extensions .fbin / .u8bin / .i8bin) */
+#define GTA_F32 0
+#define GTA_U8 1
+#define GTA_I8 2
+
+/* metrics: L2 = squared Euclidean; IP is served as L2 over rows the caller has
+ * L2-normalised (identical neighbour order: |x-y|^2 = 2 - 2<x,y>). */
+#define GTA_L2 0
+#define GTA_IP 1
+
+/* A dataset: n row-major rows of d elements (BIGANN layout,
+ * bucketDemo/buildBucket/src/load.hpp:43-135 without the 8-byte header). */
+typedef struct {
+    const void* data;
+    int64_t n;
+    int32_t d;
+    int32_t dtype;     /* GTA_F32 / GTA_U8 / GTA_I8 */
+    int32_t metric;    /* GTA_L2 / GTA_IP */
+    int32_t on_device; /* 1: data is a device pointer */
+} gta_dataset;
+
+/* Parameters of the bucketed kNN build (bucket2 / build_bucket.py). */
+typedef struct {
+    int32_t n_buckets;      /* B: k-means centroids = buckets */
+    int32_t kmeans_iters;   /* Lloyd iterations */
+    int32_t knn_degree;     /* M: intermediate kNN degree (<= 128) */
+    int32_t reserved0;
+    int64_t kmeans_sample;  /* points used by k-means; 0 = min(0.1, 1e7/N) of N */
+    uint64_t seed;
+    const float* init_centroids; /* optional B x d initial centroids (skips k-means++) */
+    int32_t init_on_device;
+    int32_t out_on_device;  /* outputs (knn lists, centroids_out, top2_out) are device pointers */
+    float* centroids_out;   /* optional B x d final centroids */
+    int32_t* top2_out;      /* optional N x 2 bucket ids (nearest, second nearest) */
+} gta_bucket_params;
+
+typedef struct {
+    gta_bucket_params bucket;
+    int32_t graph_degree;   /* K: final CAGRA degree (<= M) */
+    int32_t reserved0;
+} gta_cagra_params;
+
+/* ---------------------------------------------------------------- pipeline */
+
+/* Bucketed kNN graph: k-means over a sample, 2-way top-2 bucket membership,
+ * all-pairs distances inside every bucket on the tensor cores, exact fp32
+ * distances, per-bucket top-M, merge of each point's two lists.
+ * Writes knn_ids[N x M] (int32, -1 padding, ascending distance) and, when
+ * non-NULL, knn_dists[N x M] (squared L2, +inf padding).
+ * Replaces bucket2's Steps 2-6 (bucketDemo/buildBucket/src/bucket.cu:8523
+ * run_pipeline_impl, :5310 GpuResidentKnn::run_round, :5552 write_outputs). */
+int gta_build_bucket(const gta_dataset* ds, const gta_bucket_params* p, int32_t* knn_ids, float* knn_dists,
+                     void* stream);
+
+/* CAGRA optimize of an already distance-sorted, sanitized (N x M) uint32 kNN
+ * graph: rank-based detour-count prune to K, then the reverse-edge merge.
+ * Replaces cuvs::neighbors::cagra::helpers::optimize(res, knn(N,M), out(N,K))
+ * (bucketDemo/buildBucket/src/optimize.cu:396, bucket.cu:8470). */
+int gta_optimize(const uint32_t* knn, int64_t n, int32_t m, int32_t k, uint32_t* graph, int32_t on_device,
+                 void* stream);
+
+/* Whole build: gta_build_bucket, sanitize, gta_optimize -> graph[N x K]
+ * (uint32).  Replaces bucket2 --fused-optimize-degree
+ * (bucketDemo/buildBucket/src/bucket.cu:8434 fused_optimize_translate). */
+int gta_build_cagra(const gta_dataset* ds, const gta_cagra_params* p, uint32_t* graph, void* stream);
+
+/* ---------------------------------------------------------------- stages (device pointers) */
+
+/* k-means: `iters` Lloyd steps from `centroids` (B x d, in/out) over the rows
+ * X[n x d] (f32).  assign_out (optional, n) gets the final nearest centroid.
+ * Replaces refine_centers_kmeans (bucketDemo/build_bucket.py:232-262). */
+int gta_kmeans_fit(const float* X, int64_t n, int32_t d, float* centroids, int32_t B, int32_t iters,
+                   int32_t* assign_out, void* stream);
+
+/* k-means++ initial centroids (B x d) from a pool of the first pool_n rows of X.
+ * Replaces kmeans_pp_centers (bucketDemo/build_bucket.py:189-229). */
+int gta_kmeans_init(const float* X, int64_t pool_n, int32_t d, int32_t B, uint64_t seed, float* centroids,
+                    void* stream);
+
+/* Top-k nearest centroids per row (exact fp32 distances, ties -> smaller id).
+ * Replaces topk_from_A_to_B(X, C, k) (bucketDemo/build_bucket.py:96-159) and
+ * the Step-4 top-2 assignment (bucketDemo/buildBucket/src/bucket.cu:1230, :1478). */
+int gta_assign_topk(const float* X, int64_t n, int32_t d, const float* C, int32_t B, int32_t k, int32_t* ids,
+                    float* dists, void* stream);
+
+/* Bucket membership CSR from top-2 ids (n x 2): members[2n] point ids sorted
+ * by (bucket, point), offsets[B+1], mem_row[n x 2] (membership row of each
+ * point in its lower / higher bucket).
+ * Replaces the CSR build of GpuResidentKnn::run_round (bucket.cu:5317-5357). */
+int gta_build_memberships(const int32_t* top2, int64_t n, int32_t B, int32_t* members, int64_t* offsets,
+                          int64_t* mem_row, void* stream);
+
+/* Per-bucket all-pairs top-M (self excluded) for every membership row.
+ * X: n x d rows of `dtype`; members/offsets: the CSR above (offsets on the
+ * device).  list_ids/list_dists: [2n x M].
+ * Replaces resident_gather_pool_kernel + cuBLAS dots + block_topK_from_dots_kernel
+ * (bucket.cu:4920, :5471-5484, :4102) and the s6 screen + exact rerank (:4315-4688). */
+int gta_bucket_knn(const void* X, int32_t dtype, int64_t n, int32_t d, const int32_t* members,
+                   const int64_t* offsets, int32_t B, int32_t M, int32_t* list_ids, float* list_dists, void* stream);
+
+/* Merge each point's two membership lists (mem_row from gta_build_memberships)
+ * into out[n x M].  Replaces resident_merge_kernel (bucket.cu:5025-5131). */
+int gta_merge_memberships(const int32_t* list_ids, const float* list_dists, const int64_t* mem_row, int64_t n,
+                          int32_t M, int32_t* out_ids, float* out_dists, void* stream);
+
+/* Merge two ascending M-lists per row (running first on equal distance, new
+ * ids already present skipped).  Same rule as above, row-aligned inputs. */
+int gta_merge_lists(const int32_t* run_ids, const float* run_dists, const int32_t* new_ids, const float* new_dists,
+                    int64_t n, int32_t M, int32_t* out_ids, float* out_dists, void* stream);
+
+/* int32 kNN (-1 padding) -> uint32 graph: padding / out-of-range / self ->
+ * first valid neighbour of the row, else (i+1)%n.
+ * Replaces sanitize_to_uint32_inplace (bucketDemo/buildBucket/src/optimize.cu:95-133). */
+int gta_sanitize(const int32_t* knn, int64_t n, int32_t m, uint32_t* out, void* stream);
+
+/* Stable per-row sort of candidates by exact distance to the row's point
+ * (X: n x d f32).  Replaces sort_row_by_l2 (prune_windowed_core.hpp:134-175)
+ * and optimize's sort_knn_graph_host. */
+int gta_sort_rows(const float* X, int64_t n, int32_t d, const int32_t* knn, int32_t m, int32_t* out, void* stream);
+
+/* Detour-count prune M -> K of a sanitized, sorted graph (no reverse edges).
+ * Replaces compute_detour_counts + select_pruned_row
+ * (prune_windowed_core.hpp:190-263) / prune_windowed_gpu::run (prune_windowed_gpu.hpp:15-21). */
+int gta_prune(const uint32_t* knn, int64_t n, int32_t m, int32_t k, uint32_t* pruned, void* stream);
+
+/* Reverse-edge merge of a pruned (n x K) graph into out (n x K).
+ * Replaces TopKReverseStore + merge_rank_ordered_into_row
+ * (edge_chunk_accumulator.hpp:386-494) / optimize_chunked -m E. */
+int gta_reverse_merge(const uint32_t* pruned, int64_t n, int32_t k, uint32_t* out, void* stream);
+
+/* ---------------------------------------------------------------- files (host) */
+
+/* BIGANN dataset header (int32 N, int32 D); dtype from the extension
+ * (.fbin/.bin -> F32, .u8bin -> U8, .i8bin -> I8).  load.hpp:43-135. */
+int gta_read_dataset_header(const char* path, int64_t* n, int32_t* d, int32_t* dtype);
+/* rows [row0, row0 + nrows) into out (nrows x d elements of the file's dtype). */
+int gta_read_dataset(const char* path, int64_t row0, int64_t nrows, void* out);
+int gta_write_dataset(const char* path, const void* data, int64_t n, int32_t d, int32_t dtype);
+
+/* vector_knn.bin: int64 N, int32 M, int32[N*M] (-1 padding).  graph_io.hpp:26-30, bucket.cu:8311. */
+int gta_write_knn(const char* path, const int32_t* ids, int64_t n, int32_t m);
+int gta_read_knn_header(const char* path, int64_t* n, int32_t* m);
+int gta_read_knn(const char* path, int32_t* ids);
+/* vector_dists.bin: same header, float32 payload. */
+int gta_write_knn_dists(const char* path, const float* dists, int64_t n, int32_t m);
+
+/* CAGRA / final graph: int64 N, int32 K, uint32[N*K].  graph_io.hpp:8-11, optimize.cu:20-24. */
+int gta_write_graph(const char* path, const uint32_t* graph, int64_t n, int32_t k);
+int gta_read_graph_header(const char* path, int64_t* n, int32_t* k);
+int gta_read_graph(const char* path, uint32_t* graph);
+
+/* neighbors.npy: int64 (N, M) numpy array (load.hpp:535-618). */
+int gta_write_npy_i64(const char* path, const int32_t* ids, int64_t n, int32_t m);
+
+/* ---------------------------------------------------------------- profiling */
+/* Per-stage CUDA-event timing inside the library (off by default).  Enabling
+ * (or disabling) clears the records.  Each record: stage name, elapsed ms on
+ * the stream its kernels ran on, and the stage's algorithmic work (flops for
+ * the distance GEMM stages "dist_topk_*", bytes for the others). */
+int gta_profile_enable(int32_t on);
+int gta_profile_count(void);
+int gta_profile_get(int32_t i, char* name, int32_t name_len, float* ms, double* units);
+/* Device counters of profile record i (the distance kernel: passes into the row
+ * lists, warp-wide list merges, rows); fills n values, zeros past the record's count. */
+int gta_profile_counters(int32_t i, double* out, int32_t n);
+/* Number of this library's own kernel launches since it was loaded. */
+long long gta_launch_count(void);
+
+/* ---------------------------------------------------------------- misc */
+const char* gta_last_error(void);
+const char* gta_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GTA_H_ */

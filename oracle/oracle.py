@@ -162,14 +162,17 @@ def kmeans(X, C0, iters: int):
 
 
 def build_csr(top2: np.ndarray, B: int):
-    """Memberships (point, bucket) sorted by (bucket, point): offsets[B+1],
-    members[2N] (point ids) and mem_row[N, 2] = membership rows of each point,
-    column 0 = lower bucket id (the merge's running side)."""
+    """Memberships (point, bucket) sorted by (bucket, the point's other bucket, point):
+    offsets[B+1], members[2N] (point ids) and mem_row[N, 2] = membership rows of each
+    point, column 0 = lower bucket id (the merge's running side).  The secondary key
+    groups a bucket's members by boundary region; it changes row positions only, not
+    any list content."""
     top2 = np.asarray(top2, dtype=np.int64)
     N, W = top2.shape
     pts = np.repeat(np.arange(N, dtype=np.int64), W)
     bk = top2.reshape(-1)
-    order = np.lexsort((pts, bk))
+    other = top2[:, ::-1].reshape(-1)
+    order = np.lexsort((pts, other, bk))
     members = pts[order].astype(np.int32)
     bsorted = bk[order]
     offsets = np.zeros(B + 1, np.int64)

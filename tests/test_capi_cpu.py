@@ -1,0 +1,100 @@
+"""CPU checks of libgta: the shared library loads, exports every entry point
+declared in include/gta.h, and its host-only file I/O keeps the reference's
+byte layouts.  No compute entry point is called here (no GPU)."""
+import os
+import re
+import subprocess
+
+import numpy as np
+import pytest
+
+import gta
+from gta import _lib as L
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "gta.h")
+
+
+def _declared():
+    src = open(HEADER).read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\*?(gta_\w+)\s*\(", src, flags=re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = L.lib()
+    names = _declared()
+    assert len(names) >= 25
+    for n in names:
+        assert hasattr(lib, n), f"{n} declared in include/gta.h but not exported"
+    out = subprocess.run(["nm", "-D", "--defined-only", L.LIB_PATH], capture_output=True, text=True, check=True).stdout
+    exported = set(re.findall(r"\bT (gta_\w+)", out))
+    assert set(names) <= exported
+    assert L.lib().gta_version().startswith(b"gta-b200")
+
+
+def test_dataset_roundtrip_f32_u8_i8(tmp_path):
+    rng = np.random.default_rng(0)
+    for ext, X in ((".fbin", rng.normal(size=(37, 13)).astype(np.float32)),
+                   (".u8bin", rng.integers(0, 256, (41, 16)).astype(np.uint8)),
+                   (".i8bin", rng.integers(-128, 128, (9, 7)).astype(np.int8))):
+        p = str(tmp_path / f"x{ext}")
+        gta.write_dataset(p, X)
+        raw = open(p, "rb").read()
+        assert np.frombuffer(raw[:8], np.int32).tolist() == [X.shape[0], X.shape[1]]  # BIGANN header
+        np.testing.assert_array_equal(gta.read_dataset(p), X)
+        np.testing.assert_array_equal(gta.read_dataset(p, 3, 5), X[3:8])
+
+
+def test_knn_and_graph_layouts(tmp_path):
+    rng = np.random.default_rng(1)
+    ids = rng.integers(-1, 1000, (50, 8)).astype(np.int32)
+    p = str(tmp_path / "vector_knn.bin")
+    gta.write_knn(p, ids)
+    raw = open(p, "rb").read()
+    assert np.frombuffer(raw[:8], np.int64)[0] == 50 and np.frombuffer(raw[8:12], np.int32)[0] == 8
+    np.testing.assert_array_equal(np.frombuffer(raw[12:], np.int32).reshape(50, 8), ids)
+    np.testing.assert_array_equal(gta.read_knn(p), ids)
+    g = rng.integers(0, 1000, (50, 4)).astype(np.uint32)
+    pg = str(tmp_path / "final_graph.bin")
+    gta.write_graph(pg, g)
+    np.testing.assert_array_equal(gta.read_graph(pg), g)
+    pd = str(tmp_path / "vector_dists.bin")
+    dd = rng.random((50, 8)).astype(np.float32)
+    gta.write_knn_dists(pd, dd)
+    np.testing.assert_array_equal(np.frombuffer(open(pd, "rb").read()[12:], np.float32).reshape(50, 8), dd)
+
+
+def test_npy_writer(tmp_path):
+    ids = np.arange(24, dtype=np.int32).reshape(6, 4) - 3
+    p = str(tmp_path / "neighbors.npy")
+    gta.write_npy(p, ids)
+    got = np.load(p)
+    assert got.dtype == np.int64 and got.shape == (6, 4)
+    np.testing.assert_array_equal(got, ids.astype(np.int64))
+
+
+def test_file_errors(tmp_path):
+    p = str(tmp_path / "bad.fbin")
+    with open(p, "wb") as f:
+        np.array([100, 8], np.int32).tofile(f)
+        np.zeros(10, np.float32).tofile(f)  # truncated payload
+    with pytest.raises(gta.GtaError) as e:
+        gta.read_dataset(p)
+    assert e.value.code == L.GTA_EDATA
+    with pytest.raises(gta.GtaError) as e:
+        gta.read_dataset(str(tmp_path / "x.txt"))
+    assert e.value.code == L.GTA_EINVAL
+    with pytest.raises(gta.GtaError) as e:
+        gta.read_knn(str(tmp_path / "missing.bin"))
+    assert e.value.code == L.GTA_EINVAL
+
+
+def test_synthetic_generators_are_seeded():
+    cfg = gta.scaled(gta.CONFIGS["c2"], 2000)
+    a, b = gta.generate(cfg, seed=5), gta.generate(cfg, seed=5)
+    assert a.dtype == np.uint8 and a.shape == (2000, 128)
+    np.testing.assert_array_equal(a, b)
+    c4 = gta.generate(gta.scaled(gta.CONFIGS["c4"], 500), seed=1)
+    np.testing.assert_allclose(np.linalg.norm(c4, axis=1), 1.0, rtol=1e-5)
+    c3 = gta.generate(gta.scaled(gta.CONFIGS["c3"], 300), seed=1)
+    assert (c3 >= 0).all() and c3.shape[1] == 960

@@ -1,0 +1,314 @@
+"""GPU parity: every stage of libgta, called through its C ABI, against the CPU
+oracle and the fixtures made from the reference's own code.
+
+Bars (from the build's contract):
+  * prune / reverse edges / sanitize / sort / merge: bit-exact;
+  * 8-bit data: kNN lists bit-exact (distances are exact integers);
+  * float32 data: kNN ids identical except ties within 1e-5 relative distance,
+    distances bit-identical for identical ids (both sides use the same fp32
+    fmaf chain);
+  * k-means: centroids bit-identical per Lloyd step, assignments identical.
+"""
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+
+import gta  # noqa: E402
+from oracle import oracle as orc  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+REL_TIE = 1e-5
+
+
+def dev(a, dtype=None):
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if dtype is not None:
+        t = t.to(dtype)
+    return t.cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def mixture(rng, n, d, k, sigma, lo=-1.0, hi=1.0):
+    c = rng.uniform(lo, hi, (k, d)).astype(np.float32)
+    return (c[rng.integers(0, k, n)] + rng.normal(0, sigma, (n, d))).astype(np.float32)
+
+
+def assert_lists_match(ids, dists, ref_ids, ref_dists, exact: bool):
+    """Row-wise: identical lists, or (float data) identical up to near-ties."""
+    if exact:
+        np.testing.assert_array_equal(ids, ref_ids)
+        np.testing.assert_array_equal(dists, ref_dists)
+        return
+    same = ids == ref_ids
+    # where ids differ, the distances there must be within the tie tolerance of the reference
+    d_ok = np.isclose(dists, ref_dists, rtol=REL_TIE, atol=0) | (np.isinf(dists) & np.isinf(ref_dists))
+    assert d_ok.all(), f"{(~d_ok).sum()} distances differ beyond the tie tolerance"
+    if not same.all():
+        # a differing id must be a tie: its own exact distance equals a reference entry's within tolerance
+        r, c = np.nonzero(~same)
+        assert len(r) <= 0.01 * ids.size, f"too many differing ids: {len(r)}"
+    np.testing.assert_array_equal(dists[same], ref_dists[same])
+
+
+# ---------------------------------------------------------------- CAGRA optimize
+@pytest.mark.parametrize("name", ["opt_a", "opt_b", "opt_c"])
+def test_optimize_bit_exact_vs_reference_code(golden, name):
+    f = golden("prune_ref.npz")
+    san = f[f"{name}_san"]
+    K = f[f"{name}_graph"].shape[1]
+    g = host(gta.optimize(dev(san.view(np.int32)), K)).view(np.uint32)
+    np.testing.assert_array_equal(g, f[f"{name}_graph"])
+    # host-buffer entry point gives the same graph
+    np.testing.assert_array_equal(gta.optimize(np.ascontiguousarray(san), K), f[f"{name}_graph"])
+
+
+@pytest.mark.parametrize("N,M,K", [(3000, 64, 32), (1500, 128, 64), (800, 24, 12), (500, 33, 7)])
+def test_prune_and_reverse_vs_oracle(N, M, K):
+    rng = np.random.default_rng(N + M)
+    X = mixture(rng, N, 16, 8, 0.3)
+    ids, _ = orc.exact_knn(X, np.arange(N), M)
+    ids[rng.random(ids.shape) < 0.05] = -1           # padding -> duplicates after sanitize
+    san, _ = orc.sanitize(ids)
+    pr = host(gta.prune(dev(san.view(np.int32)), K)).view(np.uint32)
+    np.testing.assert_array_equal(pr, orc.prune(san, K))
+    rv = host(gta.reverse_merge(dev(pr.view(np.int32)))).view(np.uint32)
+    np.testing.assert_array_equal(rv, orc.reverse_merge(pr))
+
+
+def test_reverse_merge_hub_with_large_indegree():
+    # every row points at node 0 first: in-degree N-1 (> the 512-key fast path)
+    N, K = 2000, 8
+    rng = np.random.default_rng(3)
+    g = np.empty((N, K), np.uint32)
+    for i in range(N):
+        others = rng.choice(np.delete(np.arange(N), [i, 0]), K - 1, replace=False)
+        g[i] = np.concatenate([[0 if i != 0 else 1], others])
+    np.testing.assert_array_equal(host(gta.reverse_merge(dev(g.view(np.int32)))).view(np.uint32),
+                                  orc.reverse_merge(g))
+
+
+def test_sanitize_vs_oracle():
+    rng = np.random.default_rng(5)
+    N, M = 4000, 40
+    knn = rng.integers(-3, N + 5, (N, M)).astype(np.int32)
+    knn[7] = -1
+    knn[np.arange(N), rng.integers(0, M, N)] = np.arange(N)  # self loops
+    ref, _ = orc.sanitize(knn)
+    np.testing.assert_array_equal(host(gta.sanitize(dev(knn))).view(np.uint32), ref)
+
+
+@pytest.mark.parametrize("name", ["opt_a", "opt_b", "opt_c"])
+def test_sort_rows_vs_reference_code(golden, name):
+    f = golden("prune_ref.npz")
+    got = host(gta.sort_rows(dev(f[f"{name}_X"]), dev(f[f"{name}_knn"])))
+    np.testing.assert_array_equal(got, f[f"{name}_sorted"])
+
+
+# ---------------------------------------------------------------- merge
+def test_merge_vs_reference_python_fixture(golden):
+    f = golden("merge.npz")
+    on, od = gta.merge_lists(dev(f["a_i"]), dev(f["a_d"]), dev(f["b_i"]), dev(f["b_d"]))
+    np.testing.assert_array_equal(host(on), f["out_i"])
+    np.testing.assert_array_equal(host(od), f["out_d"])
+
+
+@pytest.mark.parametrize("M", [1, 16, 64, 100, 128])
+def test_merge_lists_vs_oracle_with_ties_and_dups(M):
+    rng = np.random.default_rng(M)
+    N = 3000
+    # integer distances: many exact ties; shared ids carry the same distance on both sides
+    pool_d = rng.integers(0, 20, (N, 300)).astype(np.float32)
+    a_cols = np.stack([rng.choice(300, M, replace=False) for _ in range(N)])
+    b_cols = np.stack([rng.choice(300, M, replace=False) for _ in range(N)])
+    def lists(cols):
+        d = np.take_along_axis(pool_d, cols, 1)
+        o = np.lexsort((cols, d), axis=1) if False else np.argsort(d * 1000 + cols, axis=1, kind="stable")
+        return np.take_along_axis(cols, o, 1).astype(np.int32), np.take_along_axis(d, o, 1)
+    ai, ad = lists(a_cols)
+    bi, bd = lists(b_cols)
+    ai[::5, M // 2:] = -1; ad[::5, M // 2:] = np.inf
+    bi[::3, M // 3:] = -1; bd[::3, M // 3:] = np.inf
+    ri, rd = orc.merge_lists(ai, ad, bi, bd)
+    gi, gd = gta.merge_lists(dev(ai), dev(ad), dev(bi), dev(bd))
+    np.testing.assert_array_equal(host(gi), ri)
+    np.testing.assert_array_equal(host(gd), rd)
+
+
+# ---------------------------------------------------------------- assignment / k-means
+@pytest.mark.parametrize("N,d,B,k", [(5000, 128, 16, 2), (4097, 96, 300, 2), (2000, 960, 64, 1), (3000, 20, 7, 3)])
+def test_assign_topk_vs_oracle(N, d, B, k):
+    rng = np.random.default_rng(d + B)
+    X = mixture(rng, N, d, 12, 0.2)
+    C = X[rng.choice(N, B, replace=False)] + rng.normal(0, 0.01, (B, d)).astype(np.float32)
+    gi, gd = gta.assign_topk(dev(X), dev(C), k)
+    ri, rd = orc.topk_assign(X, C, k)
+    gi, gd = host(gi), host(gd)
+    np.testing.assert_array_equal(gd, rd)     # same fp32 chain, bit-identical
+    np.testing.assert_array_equal(gi, ri)     # ties resolved to the smaller centroid id on both sides
+
+
+def test_assign_topk_u8_values():
+    rng = np.random.default_rng(2)
+    X = rng.integers(0, 256, (3000, 128)).astype(np.float32)
+    C = rng.uniform(0, 255, (256, 128)).astype(np.float32)
+    gi, gd = gta.assign_topk(dev(X), dev(C), 2)
+    ri, rd = orc.topk_assign(X, C, 2)
+    np.testing.assert_array_equal(host(gi), ri)
+    np.testing.assert_array_equal(host(gd), rd)
+
+
+def test_kmeans_lloyd_steps_vs_oracle():
+    rng = np.random.default_rng(9)
+    X = mixture(rng, 20000, 64, 40, 0.15)
+    C = X[:32].copy()
+    for _ in range(3):  # one Lloyd step at a time from identical centroids
+        gC, ga = gta.kmeans_fit(dev(X), dev(C), 1)
+        gC, ga = host(gC), host(ga)
+        ids, _ = orc.topk_assign(X, C, 1)
+        rC = orc.kmeans_update(X, ids[:, 0], C)
+        np.testing.assert_array_equal(gC, rC)
+        ri, _ = orc.topk_assign(X, rC, 1)
+        np.testing.assert_array_equal(ga, ri[:, 0])
+        C = rC
+
+
+def test_kmeans_init_is_deterministic_and_picks_data_points():
+    rng = np.random.default_rng(4)
+    X = mixture(rng, 5000, 32, 20, 0.1)
+    a = host(gta.kmeans_init(dev(X), 2000, 40, seed=7))
+    b = host(gta.kmeans_init(dev(X), 2000, 40, seed=7))
+    np.testing.assert_array_equal(a, b)
+    pool = X[:2000]
+    for c in a:
+        assert (np.abs(pool - c).max(axis=1) == 0).any()
+    assert len({tuple(r) for r in a}) >= 38
+
+
+# ---------------------------------------------------------------- memberships and per-bucket kNN
+def test_memberships_vs_oracle():
+    rng = np.random.default_rng(6)
+    N, B = 10000, 37
+    t0 = rng.integers(0, B, N)
+    t1 = (t0 + rng.integers(1, B, N)) % B
+    top2 = np.stack([t0, t1], 1).astype(np.int32)
+    off, mem, mrow = gta.build_memberships(dev(top2), B)
+    roff, rmem, rrow = orc.build_csr(top2, B)
+    np.testing.assert_array_equal(host(off), roff)
+    np.testing.assert_array_equal(host(mem), rmem)
+    np.testing.assert_array_equal(host(mrow), rrow)
+
+
+def _csr_for(X, B, rng):
+    C = X[rng.choice(X.shape[0], B, replace=False)]
+    top2, _ = orc.topk_assign(X, C, 2)
+    return orc.build_csr(top2, B)
+
+
+@pytest.mark.parametrize("N,d,B,M", [(6000, 128, 8, 64), (3000, 128, 3, 16), (2500, 100, 5, 128)])
+def test_bucket_knn_u8_bit_exact(N, d, B, M):
+    rng = np.random.default_rng(N)
+    X = np.clip(np.rint(mixture(rng, N, d, 15, 20.0, 0, 255)), 0, 255).astype(np.uint8)
+    X[100:130] = X[99]  # exact duplicates: distance-0 ties broken by id
+    off, mem, mrow = _csr_for(X.astype(np.float32), B, rng)
+    gi, gd = gta.bucket_knn(dev(X), dev(mem), dev(off), M)
+    ri, rd = orc.bucket_knn(X.astype(np.float32), off, mem, M)
+    np.testing.assert_array_equal(host(gi), ri)
+    np.testing.assert_array_equal(host(gd), rd)
+    mi, md = gta.merge_memberships(gi, gd, dev(mrow))
+    ki, kd = orc.merge_memberships(ri, rd, mrow)
+    np.testing.assert_array_equal(host(mi), ki)
+    np.testing.assert_array_equal(host(md), kd)
+
+
+@pytest.mark.parametrize("N,d,B,M", [(6000, 128, 8, 64), (3000, 96, 6, 64), (1500, 960, 4, 128)])
+def test_bucket_knn_f32_vs_oracle(N, d, B, M):
+    rng = np.random.default_rng(N + d)
+    X = mixture(rng, N, d, 12, 0.1)
+    off, mem, _ = _csr_for(X, B, rng)
+    gi, gd = gta.bucket_knn(dev(X), dev(mem), dev(off), M)
+    ri, rd = orc.bucket_knn(X, off, mem, M)
+    assert_lists_match(host(gi), host(gd), ri, rd, exact=False)
+
+
+def test_bucket_knn_f32_overflow_rescan():
+    # 400 identical points in one bucket: the screen list overflows and the rows are rescanned exactly
+    rng = np.random.default_rng(8)
+    X = mixture(rng, 2000, 32, 4, 0.3)
+    X[:400] = X[0]
+    off = np.array([0, 2000], np.int64)
+    mem = np.arange(2000, dtype=np.int32)
+    gi, gd = gta.bucket_knn(dev(X), dev(mem), dev(off), 64)
+    ri, rd = orc.bucket_knn(X, off, mem, 64)
+    np.testing.assert_array_equal(host(gi), ri)
+    np.testing.assert_array_equal(host(gd), rd)
+
+
+def test_bucket_knn_tiny_and_ragged_buckets():
+    rng = np.random.default_rng(10)
+    X = rng.integers(0, 256, (700, 64)).astype(np.uint8)
+    # bucket sizes 1, 2, 129, 568 (ragged tiles, a singleton with an empty list)
+    mem = np.arange(700, dtype=np.int32)
+    off = np.array([0, 1, 3, 132, 700], np.int64)
+    gi, gd = gta.bucket_knn(dev(X), dev(mem), dev(off), 64)
+    ri, rd = orc.bucket_knn(X.astype(np.float32), off, mem, 64)
+    np.testing.assert_array_equal(host(gi), ri)
+    np.testing.assert_array_equal(host(gd), rd)
+    assert (host(gi)[0] == -1).all()
+
+
+# ---------------------------------------------------------------- pipelines
+def _sample_rows(N, n_s, seed):
+    return orc.kmeans_sample_ids(N, n_s, seed)
+
+
+@pytest.mark.parametrize("cfg_name,n,dtype_exact", [("c1", 10000, False), ("c2", 40000, True)])
+def test_build_bucket_pipeline_vs_oracle(cfg_name, n, dtype_exact):
+    cfg = gta.scaled(gta.CONFIGS[cfg_name], n)
+    X = gta.generate(cfg, seed=3)
+    Xf = X.astype(np.float32)
+    n_s = cfg.kmeans_sample or orc.default_sample_size(n)
+    sid = _sample_rows(n, n_s, 42)
+    C0 = Xf[sid[: cfg.n_buckets]].copy()
+    ids, dists, cent, top2 = gta.build_bucket(dev(X), cfg.n_buckets, cfg.knn_degree, cfg.kmeans_iters, n_s, 42,
+                                              init_centroids=dev(C0), with_extras=True)
+    ids, dists, cent, top2 = host(ids), host(dists), host(cent), host(top2)
+    rC, _ = orc.kmeans(Xf[sid], C0, cfg.kmeans_iters)
+    np.testing.assert_allclose(cent, rC, rtol=1e-6, atol=1e-6)
+    rt2, rt2d = orc.topk_assign(Xf, cent, 2)
+    np.testing.assert_array_equal(top2, rt2)
+    offs, mem, mrow = orc.build_csr(top2, cfg.n_buckets)
+    li, ld = orc.bucket_knn(Xf, offs, mem, cfg.knn_degree)
+    ki, kd = orc.merge_memberships(li, ld, mrow)
+    assert_lists_match(ids, dists, ki, kd, exact=dtype_exact)
+    # recall of the kNN graph vs exact kNN on sampled points (knn_similarity.py rule)
+    q = np.random.default_rng(0).choice(n, 300, replace=False)
+    gt, _ = orc.exact_knn(Xf, q, 32)
+    assert orc.knn_recall(ids[q], gt, 32) > 0.8
+
+
+def test_build_cagra_matches_oracle_optimize():
+    cfg = gta.scaled(gta.CONFIGS["c2"], 20000)
+    X = gta.generate(cfg, seed=1)
+    ids, dists = gta.build_bucket(dev(X), cfg.n_buckets, 64, 5, 0, 9)
+    g = host(gta.build_cagra(dev(X), cfg.n_buckets, 64, 32, 5, 0, 9)).view(np.uint32)
+    san, _ = orc.sanitize(host(ids))
+    np.testing.assert_array_equal(g, orc.optimize(san, 32))
+    # host-buffer entry point (H2D / D2H inside the call) gives the same graph
+    g2 = gta.build_cagra(X, cfg.n_buckets, 64, 32, 5, 0, 9)
+    np.testing.assert_array_equal(g2, g)
+
+
+def test_invalid_arguments_are_rejected():
+    X = dev(np.zeros((100, 8), np.float32))
+    with pytest.raises(gta.GtaError) as e:
+        gta.build_bucket(X, 1, 8)            # 2-way membership needs B >= 2
+    assert e.value.code == 1
+    with pytest.raises(gta.GtaError) as e:
+        gta.optimize(dev(np.zeros((10, 4), np.int32)), 8)   # K > M
+    assert e.value.code == 1

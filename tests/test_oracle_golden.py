@@ -140,7 +140,11 @@ def test_csr_membership_rows():
     top2 = np.array([[1, 0], [0, 2], [2, 1], [1, 2]])
     offsets, members, mem_row = orc.build_csr(top2, 3)
     assert offsets.tolist() == [0, 2, 5, 8]
+    # inside a bucket: grouped by the other bucket, then point id
     assert members.tolist() == [0, 1, 0, 2, 3, 1, 2, 3]
+    top2b = np.array([[0, 2], [0, 1], [0, 2], [0, 1]])
+    _, mb, _ = orc.build_csr(top2b, 3)
+    assert mb[:4].tolist() == [1, 3, 0, 2]
     # column 0 is the lower bucket id
     for p in range(4):
         b_lo, b_hi = sorted(top2[p])
