@@ -41,6 +41,83 @@ void prof_clear()
 }  // namespace
 
 bool prof_enabled() { return g_prof_on; }
+
+// ---------------------------------------------------------------- workspace arenas
+namespace {
+struct Arena {
+    char* base = nullptr;
+    size_t cap = 0;   // bytes held
+    size_t off = 0;   // bump offset of the running call
+    size_t want = 0;  // high-water mark seen (arena size for the next call)
+};
+std::mutex g_ws_mu;
+std::vector<std::pair<std::pair<int, cudaStream_t>, Arena*>> g_arenas;
+thread_local Arena* t_arena = nullptr;
+thread_local int t_depth = 0;
+
+Arena* arena_for(int dev, cudaStream_t st)
+{
+    std::lock_guard<std::mutex> g(g_ws_mu);
+    for (auto& e : g_arenas)
+        if (e.first.first == dev && e.first.second == st) return e.second;
+    g_arenas.push_back({{dev, st}, new Arena()});
+    return g_arenas.back().second;
+}
+}  // namespace
+
+WorkspaceScope::WorkspaceScope(cudaStream_t st)
+{
+    if (t_depth++ > 0) return;  // nested entry points share the outer call's arena
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return;
+    Arena* a = arena_for(dev, st);
+    if (a->want > a->cap) {
+        if (a->base) {
+            cudaStreamSynchronize(st);
+            cudaFree(a->base);
+            a->base = nullptr;
+            a->cap = 0;
+        }
+        void* p = nullptr;
+        if (cudaMalloc(&p, a->want) == cudaSuccess) {
+            a->base = static_cast<char*>(p);
+            a->cap = a->want;
+        } else {
+            cudaGetLastError();  // fall back to the stream-ordered allocator for this call
+        }
+    }
+    a->off = 0;
+    t_arena = a;
+    active_ = true;
+}
+
+WorkspaceScope::~WorkspaceScope()
+{
+    --t_depth;
+    if (!active_) return;
+    t_arena = nullptr;
+}
+
+void* workspace_alloc(size_t bytes, cudaStream_t st, bool* from_arena)
+{
+    const size_t aligned = (bytes + 255) & ~static_cast<size_t>(255);
+    Arena* a = t_arena;
+    if (a) {
+        const size_t end = a->off + aligned;
+        if (end > a->want) a->want = end;
+        if (a->base && end <= a->cap) {
+            void* p = a->base + a->off;
+            a->off = end;
+            *from_arena = true;
+            return p;
+        }
+        a->off = end;  // account for it so the next call's arena covers this call
+    }
+    void* p = nullptr;
+    GTA_CUDA(cudaMallocAsync(&p, bytes, st));
+    *from_arena = false;
+    return p;
+}
 namespace {
 std::atomic<long long> g_launches{0};
 }
@@ -96,6 +173,8 @@ inline cudaStream_t S(void* s)
     keep_pool_memory();
     return static_cast<cudaStream_t>(s);
 }
+
+#define GTA_WORKSPACE(stream) ::gta::WorkspaceScope ws_scope_(S(stream))
 
 int pad_dim(int d, int elem) { const int q = elem == kElemBF16 ? 64 : 32; return (d + q - 1) / q * q; }
 
@@ -387,6 +466,26 @@ extern "C" {
 
 const char* gta_last_error(void) { return g_err.c_str(); }
 
+int gta_release_workspace(void)
+{
+    return guard([&] {
+        std::lock_guard<std::mutex> g(g_ws_mu);
+        GTA_REQUIRE(t_depth == 0, kInvalid, "gta_release_workspace: called inside a library call");
+        for (auto& e : g_arenas) {
+            if (e.second->base) {
+                int cur = 0;
+                cudaGetDevice(&cur);
+                cudaSetDevice(e.first.first);
+                cudaStreamSynchronize(e.first.second);
+                cudaFree(e.second->base);
+                cudaSetDevice(cur);
+            }
+            delete e.second;
+        }
+        g_arenas.clear();
+    });
+}
+
 int gta_profile_enable(int32_t on)
 {
     return guard([&] {
@@ -441,6 +540,7 @@ const char* gta_version(void) { return "gta-b200 0.1 (sm_100a)"; }
 int gta_build_bucket(const gta_dataset* ds, const gta_bucket_params* p, int32_t* knn_ids, float* knn_dists, void* stream)
 {
     return guard([&] {
+        GTA_WORKSPACE(stream);
         GTA_REQUIRE(ds && p && knn_ids, kInvalid, "gta_build_bucket: null argument");
         cudaStream_t st = S(stream);
         const int64_t N = ds->n;
@@ -481,6 +581,7 @@ int gta_build_bucket(const gta_dataset* ds, const gta_bucket_params* p, int32_t*
 int gta_optimize(const uint32_t* knn, int64_t n, int32_t m, int32_t k, uint32_t* graph, int32_t on_device, void* stream)
 {
     return guard([&] {
+        GTA_WORKSPACE(stream);
         GTA_REQUIRE(knn && graph, kInvalid, "gta_optimize: null argument");
         cudaStream_t st = S(stream);
         if (on_device) {
@@ -498,6 +599,7 @@ int gta_optimize(const uint32_t* knn, int64_t n, int32_t m, int32_t k, uint32_t*
 int gta_build_cagra(const gta_dataset* ds, const gta_cagra_params* p, uint32_t* graph, void* stream)
 {
     return guard([&] {
+        GTA_WORKSPACE(stream);
         GTA_REQUIRE(ds && p && graph, kInvalid, "gta_build_cagra: null argument");
         cudaStream_t st = S(stream);
         const int64_t N = ds->n;
@@ -540,6 +642,7 @@ int gta_kmeans_fit(const float* X, int64_t n, int32_t d, float* centroids, int32
                    int32_t* assign_out, void* stream)
 {
     return guard([&] {
+        GTA_WORKSPACE(stream);
         GTA_REQUIRE(X && centroids && n >= 1 && d >= 1 && B >= 1 && iters >= 0, kInvalid, "gta_kmeans_fit: bad argument");
         cudaStream_t st = S(stream);
         const int d32 = pad_dim(d, kElemF32);
@@ -559,6 +662,7 @@ int gta_kmeans_fit(const float* X, int64_t n, int32_t d, float* centroids, int32
 int gta_kmeans_init(const float* X, int64_t pool_n, int32_t d, int32_t B, uint64_t seed, float* centroids, void* stream)
 {
     return guard([&] {
+        GTA_WORKSPACE(stream);
         GTA_REQUIRE(X && centroids && pool_n >= 1 && d >= 1 && B >= 1, kInvalid, "gta_kmeans_init: bad argument");
         cudaStream_t st = S(stream);
         const int d32 = pad_dim(d, kElemF32);
@@ -574,6 +678,7 @@ int gta_assign_topk(const float* X, int64_t n, int32_t d, const float* C, int32_
                     float* dists, void* stream)
 {
     return guard([&] {
+        GTA_WORKSPACE(stream);
         GTA_REQUIRE(X && C && ids && dists && n >= 1 && d >= 1 && B >= 1, kInvalid, "gta_assign_topk: bad argument");
         cudaStream_t st = S(stream);
         const int d32 = pad_dim(d, kElemF32);
@@ -592,6 +697,7 @@ int gta_build_memberships(const int32_t* top2, int64_t n, int32_t B, int32_t* me
                           int64_t* mem_row, void* stream)
 {
     return guard([&] {
+        GTA_WORKSPACE(stream);
         GTA_REQUIRE(top2 && members && offsets && mem_row && n >= 1 && B >= 2, kInvalid, "gta_build_memberships: bad argument");
         build_memberships(top2, n, B, members, offsets, mem_row, S(stream));
     });
@@ -601,6 +707,7 @@ int gta_bucket_knn(const void* X, int32_t dtype, int64_t n, int32_t d, const int
                    int32_t B, int32_t M, int32_t* list_ids, float* list_dists, void* stream)
 {
     return guard([&] {
+        GTA_WORKSPACE(stream);
         GTA_REQUIRE(X && members && offsets && list_ids && list_dists && B >= 1 && M >= 1 && M <= 128, kInvalid,
                     "gta_bucket_knn: bad argument");
         cudaStream_t st = S(stream);
@@ -615,6 +722,7 @@ int gta_merge_memberships(const int32_t* list_ids, const float* list_dists, cons
                           int32_t M, int32_t* out_ids, float* out_dists, void* stream)
 {
     return guard([&] {
+        GTA_WORKSPACE(stream);
         GTA_REQUIRE(list_ids && list_dists && mem_row && out_ids && out_dists, kInvalid, "gta_merge_memberships: null argument");
         merge_memberships(list_ids, list_dists, mem_row, n, M, out_ids, out_dists, S(stream));
     });
@@ -624,6 +732,7 @@ int gta_merge_lists(const int32_t* run_ids, const float* run_dists, const int32_
                     int64_t n, int32_t M, int32_t* out_ids, float* out_dists, void* stream)
 {
     return guard([&] {
+        GTA_WORKSPACE(stream);
         GTA_REQUIRE(run_ids && run_dists && new_ids && new_dists && out_ids && out_dists, kInvalid,
                     "gta_merge_lists: null argument");
         merge_lists(run_ids, run_dists, new_ids, new_dists, n, M, out_ids, out_dists, S(stream));
@@ -633,6 +742,7 @@ int gta_merge_lists(const int32_t* run_ids, const float* run_dists, const int32_
 int gta_sanitize(const int32_t* knn, int64_t n, int32_t m, uint32_t* out, void* stream)
 {
     return guard([&] {
+        GTA_WORKSPACE(stream);
         GTA_REQUIRE(knn && out && n >= 1 && m >= 1, kInvalid, "gta_sanitize: bad argument");
         sanitize(knn, n, m, out, S(stream));
     });
@@ -641,6 +751,7 @@ int gta_sanitize(const int32_t* knn, int64_t n, int32_t m, uint32_t* out, void* 
 int gta_sort_rows(const float* X, int64_t n, int32_t d, const int32_t* knn, int32_t m, int32_t* out, void* stream)
 {
     return guard([&] {
+        GTA_WORKSPACE(stream);
         GTA_REQUIRE(X && knn && out && n >= 1 && d >= 1, kInvalid, "gta_sort_rows: bad argument");
         cudaStream_t st = S(stream);
         const int d32 = pad_dim(d, kElemF32);
@@ -654,6 +765,7 @@ int gta_sort_rows(const float* X, int64_t n, int32_t d, const int32_t* knn, int3
 int gta_prune(const uint32_t* knn, int64_t n, int32_t m, int32_t k, uint32_t* pruned, void* stream)
 {
     return guard([&] {
+        GTA_WORKSPACE(stream);
         GTA_REQUIRE(knn && pruned, kInvalid, "gta_prune: null argument");
         cudaStream_t st = S(stream);
         DevBuf<int> err(1, st);
@@ -666,6 +778,7 @@ int gta_prune(const uint32_t* knn, int64_t n, int32_t m, int32_t k, uint32_t* pr
 int gta_reverse_merge(const uint32_t* pruned, int64_t n, int32_t k, uint32_t* out, void* stream)
 {
     return guard([&] {
+        GTA_WORKSPACE(stream);
         GTA_REQUIRE(pruned && out && n >= 1, kInvalid, "gta_reverse_merge: bad argument");
         reverse_merge(pruned, n, k, out, nullptr, S(stream));
     });

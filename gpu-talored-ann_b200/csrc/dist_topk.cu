@@ -109,13 +109,24 @@ __device__ __forceinline__ void sort32(uint64_t (&k)[kBuf])
     }
 }
 
+// Bitonic merge (half-cleaners with strides 16..1) of 32 keys in registers.
+__device__ __forceinline__ void merge32(uint64_t (&k)[kBuf])
+{
+#pragma unroll
+    for (int stride = kBuf / 2; stride > 0; stride >>= 1) {
+#pragma unroll
+        for (int i = 0; i < kBuf; ++i)
+            if ((i & stride) == 0) cmp_swap(k[i], k[i + stride]);
+    }
+}
+
 // Merge the 32 sorted keys into the row's sorted list of kL keys (shared
 // memory, row stride 128), keeping the kL smallest: elementwise minimum with
 // the reversed buffer gives a bitonic sequence holding the kL smallest keys,
-// and the bitonic half-cleaner cascade sorts it.  Every compare-exchange of a
-// stage is independent, so the loads overlap instead of forming one chain.
+// and the bitonic half-cleaner cascade sorts it.  Strides of 32 and more run
+// on shared memory; each 32-key block then finishes in registers.
 template <int kL>
-__device__ __forceinline__ void merge_into_list(uint64_t* list, const uint64_t (&k)[kBuf])
+__device__ __forceinline__ void merge_into_list(uint64_t* list, uint64_t (&k)[kBuf])
 {
 #pragma unroll
     for (int i = 0; i < kBuf; ++i) {
@@ -124,7 +135,7 @@ __device__ __forceinline__ void merge_into_list(uint64_t* list, const uint64_t (
         list[(kL - kBuf + i) * 128] = a < b ? a : b;
     }
 #pragma unroll
-    for (int stride = kL / 2; stride > 0; stride >>= 1) {
+    for (int stride = kL / 2; stride >= kBuf; stride >>= 1) {
 #pragma unroll
         for (int i = 0; i < kL; ++i) {
             if ((i & stride) == 0) {
@@ -136,18 +147,40 @@ __device__ __forceinline__ void merge_into_list(uint64_t* list, const uint64_t (
             }
         }
     }
+#pragma unroll
+    for (int blk = 0; blk < kL; blk += kBuf) {
+#pragma unroll
+        for (int i = 0; i < kBuf; ++i) k[i] = list[(blk + i) * 128];
+        merge32(k);
+#pragma unroll
+        for (int i = 0; i < kBuf; ++i) list[(blk + i) * 128] = k[i];
+    }
 }
 
-// Flush the row's staging buffer (nb entries, unsorted) into its list.
+// Flush the row's staging buffer (nb entries, unsorted) into its list.  One
+// out-of-line copy (it is large and runs rarely); never called while a
+// tcgen05.ld of the caller is still in flight.
 template <int kL>
-__device__ __forceinline__ void flush_row(uint64_t* list, uint64_t* buf, int& nb)
+__device__ __noinline__ void flush_row(uint64_t* list, uint64_t* buf, int nb)
 {
     uint64_t k[kBuf];
 #pragma unroll
     for (int i = 0; i < kBuf; ++i) k[i] = (i < nb) ? buf[i * 128] : kEmptyKey;
     sort32(k);
     merge_into_list<kL>(list, k);
-    nb = 0;
+}
+
+// v[e] for a runtime e in [0, 16) through a 4-level select tree (static register indices).
+__device__ __forceinline__ uint32_t pick16(const uint32_t (&v)[16], int e)
+{
+    uint32_t l1[8], l2[4], l3[2];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) l1[i] = (e & 1) ? v[2 * i + 1] : v[2 * i];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) l2[i] = (e & 2) ? l1[2 * i + 1] : l1[2 * i];
+#pragma unroll
+    for (int i = 0; i < 2; ++i) l3[i] = (e & 4) ? l2[2 * i + 1] : l2[2 * i];
+    return (e & 8) ? l3[1] : l3[0];
 }
 
 __device__ __forceinline__ float key_dist(uint64_t key) { return key2f(static_cast<uint32_t>(key >> 32)); }
@@ -220,7 +253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* list = reinterpret_cast<uint64_t*>(gbase + p.list_off);
     uint64_t* buf = reinterpret_cast<uint64_t*>(gbase + p.buf_off);
     float* pn_s = reinterpret_cast<float*>(gbase + p.pn_off);
-    uint32_t* id_s = reinterpret_cast<uint32_t*>(gbase + p.pn_off + 2u * 128u * 4u);
+    uint32_t* id_s = reinterpret_cast<uint32_t*>(gbase + p.pn_off + 4u * 128u * 4u);
     const uint32_t bar0 = base + p.bar_off;
     const uint32_t a_full = bar0 + 8u * (2 * S);
     const uint32_t mma_done = bar0 + 8u * (2 * S + 5);
@@ -326,7 +359,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ epilogue
         const int q = warp & 3;
         const int r = q * 32 + lane;
-        const int et = threadIdx.x - 64;
         const bool row_ok = r < w.a_rows;
         const bool has_self = w.self_col0 >= 0;   // the tile's rows are also the segment's columns t0*128 + r
         const int64_t arow = static_cast<int64_t>(w.a_row0) + r;
@@ -346,35 +378,55 @@ __global__ void __launch_bounds__(kThreads, 1)
         const bool st_on = p.stats != nullptr;
         long long cyc_wait = 0, cyc_flush = 0;
         const long long cyc0 = st_on ? clock64() : 0;
+        // this warp's copy of the current tile's column norms / ids; lane l stages columns 4l..4l+3,
+        // and the values of the next tile are loaded into registers while this one is scanned
+        float* pnw = pn_s + q * 128;
+        uint32_t* idw = id_s + q * 128;
+        float pf_n[4];
+        uint32_t pf_i[4];
+        auto prefetch_cols = [&](int kk) {
+            const int ctn = tile_at(kk, t0, n_ct);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int col = ctn * kTileN + lane * 4 + j;
+                const bool cok = col < w.b_rows;
+                const int64_t brow = static_cast<int64_t>(w.b_row0) + col;
+                pf_n[j] = cok ? p.b_norm[brow] : INFINITY;
+                pf_i[j] = (!p.screen && cok && p.b_gid) ? static_cast<uint32_t>(p.b_gid[brow]) : static_cast<uint32_t>(col);
+            }
+        };
+        prefetch_cols(0);
         for (int k = 0; k < n_ct; ++k) {
             const int ct = tile_at(k, t0, n_ct);
             const int b = k & 1;
             const uint32_t use = static_cast<uint32_t>(k >> 1);
-            const int col = ct * kTileN + et;
-            const bool col_ok = col < w.b_rows;
-            pn_s[b * 128 + et] = col_ok ? p.b_norm[static_cast<int64_t>(w.b_row0) + col] : INFINITY;
-            if (!p.screen)
-                id_s[b * 128 + et] = (col_ok && p.b_gid) ? static_cast<uint32_t>(p.b_gid[static_cast<int64_t>(w.b_row0) + col])
-                                                         : static_cast<uint32_t>(col);
+            __syncwarp();
+            reinterpret_cast<float4*>(pnw)[lane] = make_float4(pf_n[0], pf_n[1], pf_n[2], pf_n[3]);
+            reinterpret_cast<uint4*>(idw)[lane] = make_uint4(pf_i[0], pf_i[1], pf_i[2], pf_i[3]);
+            __syncwarp();
+            if (k + 1 < n_ct) prefetch_cols(k + 1);
             const long long w0 = st_on ? clock64() : 0;
-            named_bar_sync(1, 128);
             if (!mbar_wait(ACC_FULL(b), use & 1u, abort_flag, p.err, kDevTimeoutAcc)) { ok = false; break; }
             if (st_on) cyc_wait += clock64() - w0;
             tc_fence_after();
-            const float* pn = pn_s + b * 128;
-            const uint32_t* ids = id_s + b * 128;
+            const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * kTileN);
+            uint32_t vn[16];
+            __syncwarp();
+            tmem_ld_32x32b_x16(tbase, vn);
 #pragma unroll 1
-            for (int c = 0; c < 8; ++c) {  // 8 slices of 16 columns
+            for (int c = 0; c < 8; ++c) {  // 8 slices of 16 columns; slice c+1 loads while c is scanned
                 uint32_t v[16];
-                __syncwarp();
-                tmem_ld_32x32b_x16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
-                                       static_cast<uint32_t>(b * kTileN + c * 16),
-                                   v);
-                tmem_ld_wait();
+                tmem_ld_wait_regs(vn);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] = vn[e];
+                if (c + 1 < 8) {
+                    __syncwarp();
+                    tmem_ld_32x32b_x16(tbase + static_cast<uint32_t>((c + 1) * 16), vn);
+                }
                 // the row's own column sits at element lane % 16 of slice 2q + lane / 16 of the diagonal tile
                 const int self_e = (has_self && k == 0 && c == 2 * q + (lane >> 4)) ? (lane & 15) : -1;
                 const uint32_t c0 = static_cast<uint32_t>(ct * kTileN + c * 16);
-                const float4* pn4 = reinterpret_cast<const float4*>(pn + c * 16);
+                const float4* pn4 = reinterpret_cast<const float4*>(pnw + c * 16);
                 // branch-free scan: pass mask first, then predicated appends at popcount offsets
                 float sv[16];
                 uint32_t mask = 0;
@@ -390,10 +442,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 if (self_e >= 0) mask &= ~(1u << self_e);
-                if (mask) {
-                    uint32_t idv[16];
+                // appends: one warp-uniform iteration per pass of the busiest lane
+                const int npass = __popc(mask);
+                const int rounds = __reduce_max_sync(0xffffffffu, static_cast<unsigned>(npass));
+                if (rounds > 0) {
+                    uint32_t kv[16], idv[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) kv[e] = f2key(sv[e]);
                     if (!p.screen) {
-                        const uint4* id4 = reinterpret_cast<const uint4*>(ids + c * 16);
+                        const uint4* id4 = reinterpret_cast<const uint4*>(idw + c * 16);
 #pragma unroll
                         for (int e4 = 0; e4 < 4; ++e4) {
                             const uint4 x = id4[e4];
@@ -403,22 +460,25 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int e = 0; e < 16; ++e) idv[e] = c0 + e;  // screen mode keys carry the column
                     }
-#pragma unroll
-                    for (int e = 0; e < 16; ++e) {
-                        if ((mask >> e) & 1u) {
-                            const int slot = nb + __popc(mask & ((1u << e) - 1u));
-                            my_buf[slot * 128] = (static_cast<uint64_t>(f2key(sv[e])) << 32) | idv[e];
+                    uint32_t m = mask;
+                    for (int i = 0; i < rounds; ++i) {
+                        const int e = __ffs(m) - 1;
+                        if (e >= 0) {
+                            my_buf[(nb + i) * 128] = (static_cast<uint64_t>(pick16(kv, e)) << 32) | pick16(idv, e);
+                            m &= m - 1u;
                         }
                     }
-                    nb += __popc(mask);
+                    nb += npass;
                 }
                 // warp-wide flush: when any lane may overflow its buffer in the next
                 // 16 columns, every lane merges its own buffer
                 if (__any_sync(0xffffffffu, nb > kBuf - 16)) {
+                    if (c + 1 < 8) tmem_ld_wait_regs(vn);  // no TMEM load in flight across the call
                     const long long f0 = st_on ? clock64() : 0;
                     n_pass += nb;
                     ++n_flush;
                     flush_row<kL>(my_list, my_buf, nb);
+                    nb = 0;
                     thr = row_ok ? row_thr<kL>(my_list, p.m_sel, p.screen, margin) : -FLT_MAX;
                     if (st_on) cyc_flush += clock64() - f0;
                 }
@@ -433,6 +493,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 n_pass += nb;
                 ++n_flush;
                 flush_row<kL>(my_list, my_buf, nb);
+                nb = 0;
             }
             if (st_on) {
                 if (row_ok) atomicAdd(&p.stats[0], static_cast<unsigned long long>(n_pass));
@@ -617,7 +678,7 @@ bool make_plan(int k_chunks, int m, bool screen, Plan& pl)
     int L = 32;
     while (L < (screen ? m + 16 : m)) L <<= 1;
     struct Cfg { int a_res, S; };
-    const Cfg cfgs[] = {{1, 4}, {1, 3}, {0, 4}, {0, 3}, {1, 2}, {0, 2}};
+    const Cfg cfgs[] = {{1, 4}, {1, 3}, {0, 4}, {0, 3}, {1, 2}, {0, 2}, {1, 1}, {0, 1}};
     for (; L >= 32 && L >= m; L >>= 1) {
         for (const Cfg& c : cfgs) {
             const uint32_t stage_bytes = c.a_res ? kTileBytes : 2u * kTileBytes;
@@ -626,7 +687,7 @@ bool make_plan(int k_chunks, int m, bool screen, Plan& pl)
             t.stages = c.S; t.L = L; t.a_res = c.a_res;
             t.list_off = off; off += static_cast<uint32_t>(L) * 128u * 8u;
             t.buf_off = off; off += static_cast<uint32_t>(kBuf) * 128u * 8u;
-            t.pn_off = off; off += 2u * 128u * 4u * 2u;  // column norms + column ids, double-buffered
+            t.pn_off = off; off += 4u * 128u * 4u * 2u;  // per epilogue warp: column norms, then column ids
             t.bar_off = off; off += 8u * (2u * c.S + 6u) + 16u;
             t.total = off;
             if (t.total <= kSmemMax) { pl = t; return true; }

@@ -32,30 +32,48 @@ struct Error : std::runtime_error {
         if (!(cond)) throw ::gta::Error(code, msg);  \
     } while (0)
 
-// Stream-ordered device scratch, freed on scope exit.
+// Device scratch of one library call.  Inside a top-level entry point
+// (WorkspaceScope), buffers come from a per-(device, stream) arena that is
+// reused by every later call on that stream: the arena grows to the call's
+// high-water mark once and is then served without any allocation.  Outside a
+// scope, or when the arena is too small, the stream-ordered allocator is used.
+void* workspace_alloc(size_t bytes, cudaStream_t st, bool* from_arena);
+
+class WorkspaceScope {
+public:
+    explicit WorkspaceScope(cudaStream_t st);
+    ~WorkspaceScope();
+    WorkspaceScope(const WorkspaceScope&) = delete;
+    WorkspaceScope& operator=(const WorkspaceScope&) = delete;
+
+private:
+    bool active_ = false;
+};
+
 template <typename T>
 struct DevBuf {
     T* p = nullptr;
     size_t n = 0;
     cudaStream_t st = nullptr;
+    bool arena = false;
     DevBuf() = default;
     DevBuf(size_t count, cudaStream_t s) : n(count), st(s)
     {
-        if (count) GTA_CUDA(cudaMallocAsync(reinterpret_cast<void**>(&p), sizeof(T) * count, s));
+        if (count) p = static_cast<T*>(workspace_alloc(sizeof(T) * count, s, &arena));
     }
     DevBuf(const DevBuf&) = delete;
     DevBuf& operator=(const DevBuf&) = delete;
-    DevBuf(DevBuf&& o) noexcept : p(o.p), n(o.n), st(o.st) { o.p = nullptr; o.n = 0; }
+    DevBuf(DevBuf&& o) noexcept : p(o.p), n(o.n), st(o.st), arena(o.arena) { o.p = nullptr; o.n = 0; }
     DevBuf& operator=(DevBuf&& o) noexcept
     {
         release();
-        p = o.p; n = o.n; st = o.st; o.p = nullptr; o.n = 0;
+        p = o.p; n = o.n; st = o.st; arena = o.arena; o.p = nullptr; o.n = 0;
         return *this;
     }
     ~DevBuf() { release(); }
     void release()
     {
-        if (p) cudaFreeAsync(p, st);
+        if (p && !arena) cudaFreeAsync(p, st);
         p = nullptr;
         n = 0;
     }

@@ -384,30 +384,33 @@ __global__ void sanitize_kernel(const int32_t* __restrict__ knn, int64_t N, int 
 
 // ---------------------------------------------------------------- detour prune
 constexpr int kPruneWarps = 8;
-constexpr int kMaxHash = 256;
-
-__device__ __forceinline__ uint32_t hash_id(uint32_t id, uint32_t mask) { return (id * 2654435761u) & mask; }
 
 // Warp per row a (processed in `order` when given: rows of one bucket region
 // together, so the neighbour rows they gather stay in L2).  Row a's candidates
-// go into a shared-memory id -> rank hash; for every closer candidate D (rank
-// kAD) the warp streams D's row, marks which later ranks kAB of a's row it
-// contains (each (kAD, kAB) once: a bit mask OR-reduced over the warp), and
-// counts them.  Two neighbour rows are loaded before they are processed.
-__global__ void __launch_bounds__(kPruneWarps * 32, 8)
+// go into a shared-memory id -> rank hash table sized 8x the row (load factor
+// <= 1/8, so nearly every lookup probes one slot and the warp stays converged);
+// duplicates of an id keep separate slots.  For every closer candidate D (rank
+// kAD) each lane looks its entries of D's row up, marks the later ranks kAB it
+// finds (each (kAD, kAB) once: a bit mask OR-reduced over the warp), and the
+// lanes owning those ranks count them.  Two neighbour rows are loaded ahead.
+constexpr int kPruneHash = 1024;
+
+__device__ __forceinline__ uint32_t hash_id(uint32_t id, uint32_t mask) { return (id * 2654435761u) >> 7 & mask; }
+
+__global__ void __launch_bounds__(kPruneWarps * 32)
     prune_kernel(const uint32_t* __restrict__ g, int64_t N, int M, int K, const int32_t* __restrict__ order,
                  uint32_t* __restrict__ out, int* err)
 {
+    __shared__ uint32_t s_hkey[kPruneWarps][kPruneHash];
+    __shared__ uint8_t s_hrank[kPruneWarps][kPruneHash];
     __shared__ uint32_t s_row[kPruneWarps][kMaxM];
-    __shared__ uint32_t s_hkey[kPruneWarps][kMaxHash];
-    __shared__ uint8_t s_hrank[kPruneWarps][kMaxHash];
     __shared__ uint32_t s_cnt[kPruneWarps][kMaxM];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int64_t gw = static_cast<int64_t>(blockIdx.x) * kPruneWarps + w;
     if (gw >= N) return;
     const int64_t a = order ? static_cast<int64_t>(order[gw]) : gw;
-    uint32_t cap = 16;
-    while (cap < 2u * static_cast<uint32_t>(M)) cap <<= 1;
+    uint32_t cap = 64;
+    while (cap < 8u * static_cast<uint32_t>(M)) cap <<= 1;
     const uint32_t mask = cap - 1;
     for (uint32_t h = lane; h < cap; h += 32) s_hkey[w][h] = kEmpty;
     const uint32_t* ra = g + a * M;
@@ -448,12 +451,16 @@ __global__ void __launch_bounds__(kPruneWarps * 32, 8)
             uint32_t hit[kMaxM / 32] = {0, 0, 0, 0};
 #pragma unroll
             for (int gi = 0; gi < kMaxM / 32; ++gi) {
+                if (gi >= G) break;
                 const uint32_t bv = vals[u][gi];
                 if (bv == kEmpty) continue;
-                for (uint32_t h = hash_id(bv, mask); s_hkey[w][h] != kEmpty; h = (h + 1) & mask) {
-                    if (s_hkey[w][h] != bv) continue;
-                    const int kAB = s_hrank[w][h];
-                    if (kAB > kAD) hit[kAB >> 5] |= 1u << (kAB & 31);
+                for (uint32_t h = hash_id(bv, mask);; h = (h + 1) & mask) {
+                    const uint32_t key = s_hkey[w][h];
+                    if (key == kEmpty) break;
+                    if (key == bv) {
+                        const int kAB = s_hrank[w][h];
+                        if (kAB > kAD) hit[kAB >> 5] |= 1u << (kAB & 31);
+                    }
                 }
             }
 #pragma unroll

@@ -75,6 +75,7 @@ _SIGS = {
     "gta_read_graph": [ctypes.c_char_p, _P],
     "gta_write_npy_i64": [ctypes.c_char_p, _P, _I64, _I32],
     "gta_profile_enable": [_I32],
+    "gta_release_workspace": [],
     "gta_profile_get": [_I32, ctypes.c_char_p, _I32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double)],
     "gta_profile_counters": [_I32, ctypes.POINTER(ctypes.c_double), _I32],
 }

@@ -16,8 +16,11 @@
  * Memory: pointers flagged `on_device` are CUDA device pointers on the current
  * device; all work is ordered on `stream` (a cudaStream_t, NULL = default
  * stream).  Stage entry points (gta_assign_topk ... gta_reverse_merge) take
- * device pointers only and are stream-ordered; the library allocates its
- * scratch with the stream-ordered allocator and frees it before returning.
+ * device pointers only and are stream-ordered.  Scratch memory comes from a
+ * workspace the library keeps per (device, stream): it grows to the largest
+ * call seen on that stream and is reused by later calls on the same stream
+ * (held until gta_release_workspace).  Calls on one stream are ordered by the
+ * stream; the same stream must not be driven from two host threads at once.
  * Entry points that return results in host memory synchronize the stream.
  */
 #ifndef GTA_H_
@@ -205,6 +208,8 @@ int gta_profile_counters(int32_t i, double* out, int32_t n);
 long long gta_launch_count(void);
 
 /* ---------------------------------------------------------------- misc */
+/* Free the per-(device, stream) workspaces (synchronizes those streams). */
+int gta_release_workspace(void);
 const char* gta_last_error(void);
 const char* gta_version(void);
 
