@@ -784,6 +784,16 @@ int gta_reverse_merge(const uint32_t* pruned, int64_t n, int32_t k, uint32_t* ou
     });
 }
 
+// Same reverse-edge merge as gta_reverse_merge, for callers that cannot allocate
+// device memory at call time; its scratch is a fixed array inside the library.
+int gta_reverse_merge_noalloc(const uint32_t* pruned, int64_t n, int32_t k, uint32_t* out, void* stream)
+{
+    return guard([&] { reverse_merge_noalloc(pruned, n, k, out, static_cast<cudaStream_t>(stream)); });
+}
+
+int64_t gta_reverse_merge_noalloc_max_rows(void) { return reverse_merge_noalloc_max_rows(); }
+int64_t gta_reverse_merge_noalloc_max_edges(void) { return reverse_merge_noalloc_max_edges(); }
+
 // ---------------------------------------------------------------- files
 int gta_read_dataset_header(const char* path, int64_t* n, int32_t* d, int32_t* dtype)
 {

@@ -138,6 +138,9 @@ void prune_detour(const uint32_t* g, int64_t N, int M, int K, const int32_t* ord
                   cudaStream_t st);
 void locality_order(const int32_t* top2, int64_t N, int32_t B, int32_t* order, cudaStream_t st);
 void reverse_merge(const uint32_t* pruned, int64_t N, int K, uint32_t* out, int* err, cudaStream_t st);
+void reverse_merge_noalloc(const uint32_t* pruned, int64_t N, int K, uint32_t* out, cudaStream_t st);
+int64_t reverse_merge_noalloc_max_rows();
+int64_t reverse_merge_noalloc_max_edges();
 void sort_rows_l2(const float* X, int d, int d_pad, const int32_t* knn, int64_t N, int M, int32_t* out,
                   cudaStream_t st);
 void max_sqrt(const float* v, int64_t n, float* out, cudaStream_t st);

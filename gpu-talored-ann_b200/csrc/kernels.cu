@@ -15,6 +15,9 @@
 #include <cuda_bf16.h>
 
 #include <cmath>
+#include <mutex>
+#include <string>
+#include <vector>
 
 #include "common.cuh"
 #include "gta_internal.h"
@@ -836,6 +839,79 @@ void reverse_merge(const uint32_t* pruned, int64_t N, int K, uint32_t* out, int*
     rev_scatter_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, N, K, off.get(), cursor.get(), keys.get());
     count_launches(1);
     rev_merge_kernel<<<blocks_for(N, kRevWarps), kRevWarps * 32, 0, st>>>(pruned, N, K, off.get(), keys.get(), out);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------- reverse-edge merge without allocation
+// Scratch of gta_reverse_merge_noalloc: one file-scope device array, resident on
+// every GPU that loads the library until the process exits.  Layout (each region
+// 256-byte aligned): in-degrees (u64, rows + 1), offsets (u64, rows + 1),
+// cursors (u32, rows), edge keys (u64, rows * K), scan temporary storage.
+namespace {
+constexpr int64_t kNoAllocMaxRows = 1ll << 17;
+constexpr int64_t kNoAllocMaxEdges = 1ll << 21;
+constexpr size_t kNoAllocScanBytes = 1u << 20;
+constexpr size_t align256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+constexpr size_t kNoAllocIndegOff = 0;
+constexpr size_t kNoAllocOffOff = kNoAllocIndegOff + align256(sizeof(unsigned long long) * (kNoAllocMaxRows + 1));
+constexpr size_t kNoAllocCursorOff = kNoAllocOffOff + align256(sizeof(uint64_t) * (kNoAllocMaxRows + 1));
+constexpr size_t kNoAllocKeysOff = kNoAllocCursorOff + align256(sizeof(uint32_t) * kNoAllocMaxRows);
+constexpr size_t kNoAllocScanOff = kNoAllocKeysOff + align256(sizeof(uint64_t) * kNoAllocMaxEdges);
+constexpr size_t kNoAllocBytes = kNoAllocScanOff + kNoAllocScanBytes;
+
+static __device__ __align__(256) unsigned char g_rev_scratch[kNoAllocBytes];
+
+std::mutex g_noalloc_mu;
+std::vector<std::pair<int, unsigned char*>> g_noalloc_addr;  // device -> address of g_rev_scratch there
+
+// Device address of the scratch array on the current device.  The host-side
+// name g_rev_scratch is only a stand-in, so the address is looked up once per
+// device (with that device current) and cached.
+unsigned char* noalloc_scratch()
+{
+    int dev = 0;
+    GTA_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    for (const auto& e : g_noalloc_addr)
+        if (e.first == dev) return e.second;
+    void* ptr = nullptr;
+    GTA_CUDA(cudaGetSymbolAddress(&ptr, g_rev_scratch));
+    g_noalloc_addr.push_back({dev, static_cast<unsigned char*>(ptr)});
+    return static_cast<unsigned char*>(ptr);
+}
+}  // namespace
+
+int64_t reverse_merge_noalloc_max_rows() { return kNoAllocMaxRows; }
+int64_t reverse_merge_noalloc_max_edges() { return kNoAllocMaxEdges; }
+
+void reverse_merge_noalloc(const uint32_t* pruned, int64_t N, int K, uint32_t* out, cudaStream_t st)
+{
+    GTA_REQUIRE(pruned && out && N >= 1 && K >= 1 && K <= kMaxM, kInvalid,
+                "reverse_merge_noalloc: need non-null buffers, n >= 1 and 1 <= k <= 128");
+    GTA_REQUIRE(N <= kNoAllocMaxRows && N * K <= kNoAllocMaxEdges, kInvalid,
+                "reverse_merge_noalloc: graph too large for the fixed scratch (at most " +
+                    std::to_string(kNoAllocMaxRows) + " rows and " + std::to_string(kNoAllocMaxEdges) +
+                    " edges); use gta_reverse_merge");
+    unsigned char* base = noalloc_scratch();
+    unsigned long long* indeg = reinterpret_cast<unsigned long long*>(base + kNoAllocIndegOff);
+    uint64_t* off = reinterpret_cast<uint64_t*>(base + kNoAllocOffOff);
+    uint32_t* cursor = reinterpret_cast<uint32_t*>(base + kNoAllocCursorOff);
+    uint64_t* keys = reinterpret_cast<uint64_t*>(base + kNoAllocKeysOff);
+    void* scan_tmp = base + kNoAllocScanOff;
+    const int64_t NK = N * K;
+    size_t tmp = 0;
+    GTA_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tmp, indeg, off, static_cast<int>(N + 1), st));
+    GTA_REQUIRE(tmp <= kNoAllocScanBytes, kInvalid, "reverse_merge_noalloc: scan scratch exceeds its reserve");
+    // the array keeps the previous call's contents: counters start from zero
+    GTA_CUDA(cudaMemsetAsync(indeg, 0, sizeof(unsigned long long) * (N + 1), st));
+    GTA_CUDA(cudaMemsetAsync(cursor, 0, sizeof(uint32_t) * N, st));
+    rev_count_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, NK, N, indeg);
+    count_launches(1);
+    GTA_CUDA(cub::DeviceScan::ExclusiveSum(scan_tmp, tmp, indeg, off, static_cast<int>(N + 1), st));
+    rev_scatter_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, N, K, off, cursor, keys);
+    count_launches(1);
+    rev_merge_kernel<<<blocks_for(N, kRevWarps), kRevWarps * 32, 0, st>>>(pruned, N, K, off, keys, out);
     count_launches(1);
     GTA_CUDA(cudaGetLastError());
 }

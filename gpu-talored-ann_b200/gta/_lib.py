@@ -63,6 +63,7 @@ _SIGS = {
     "gta_sort_rows": [_P, _I64, _I32, _P, _I32, _P, _P],
     "gta_prune": [_P, _I64, _I32, _I32, _P, _P],
     "gta_reverse_merge": [_P, _I64, _I32, _P, _P],
+    "gta_reverse_merge_noalloc": [_P, _I64, _I32, _P, _P],
     "gta_read_dataset_header": [ctypes.c_char_p, ctypes.POINTER(_I64), ctypes.POINTER(_I32), ctypes.POINTER(_I32)],
     "gta_read_dataset": [ctypes.c_char_p, _I64, _I64, _P],
     "gta_write_dataset": [ctypes.c_char_p, _P, _I64, _I32, _I32],
@@ -109,6 +110,9 @@ def lib() -> ctypes.CDLL:
         L.gta_profile_count.argtypes = []
         L.gta_launch_count.restype = ctypes.c_longlong
         L.gta_launch_count.argtypes = []
+        for fn in ("gta_reverse_merge_noalloc_max_rows", "gta_reverse_merge_noalloc_max_edges"):
+            getattr(L, fn).restype = ctypes.c_int64
+            getattr(L, fn).argtypes = []
         _lib = L
     return _lib
 

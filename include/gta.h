@@ -169,6 +169,26 @@ int gta_prune(const uint32_t* knn, int64_t n, int32_t m, int32_t k, uint32_t* pr
  * (edge_chunk_accumulator.hpp:386-494) / optimize_chunked -m E. */
 int gta_reverse_merge(const uint32_t* pruned, int64_t n, int32_t k, uint32_t* out, void* stream);
 
+/* Reverse-edge merge that allocates nothing: the same result as
+ * gta_reverse_merge, for callers that cannot allocate device memory when they
+ * call in -- for example a serving process whose allocator has reserved all of
+ * device memory up front, or a latency-critical loop where a cudaMalloc /
+ * cudaFree would synchronize the device and stall its other streams.  This
+ * entry point has no counterpart in the reference.
+ *
+ * Its scratch is one fixed array inside the library (about 19 MB, held on every
+ * GPU that loads the library until the process exits), so it accepts at most
+ * gta_reverse_merge_noalloc_max_rows() rows (131072) and
+ * gta_reverse_merge_noalloc_max_edges() edges (n * k <= 2097152, k <= 128) and
+ * rejects anything larger with GTA_EINVAL.  The first call on a device looks up
+ * the array's device address (cudaGetSymbolAddress); make that first call
+ * before any stream capture.  All calls share the array: calls whose work
+ * overlaps on the GPU (different streams, or several host threads) race and
+ * must be serialized by the caller. */
+int gta_reverse_merge_noalloc(const uint32_t* pruned, int64_t n, int32_t k, uint32_t* out, void* stream);
+int64_t gta_reverse_merge_noalloc_max_rows(void);
+int64_t gta_reverse_merge_noalloc_max_edges(void);
+
 /* ---------------------------------------------------------------- files (host) */
 
 /* BIGANN dataset header (int32 N, int32 D); dtype from the extension
