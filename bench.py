@@ -48,9 +48,10 @@ def _peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-# per-launch DRAM traffic of the dominant kernels from one ncu capture, in bytes
-# per algorithmic unit (profiles/dist_topk_c2.md); None until captured
-TRAFFIC_PER_UNIT = {}
+# DRAM bytes (read + write) per algorithmic unit of a kernel, from one ncu capture each
+# (profiles/dist_topk_kernel_c2_400k.md, profiles/prune_kernel_c2_400k.md; C2 distribution at
+# N = 400 000, scaled to a launch by its units: the traffic grows with the rows processed)
+TRAFFIC_PER_UNIT = {"dist_topk_bucket": 576.5e6 / 3.0868e12, "prune": 136.48e6 / 6.7072e9}
 
 
 # ---------------------------------------------------------------- clocks
