@@ -9,9 +9,13 @@ dataset: k-means on the sample, top-2 bucket assignment, per-bucket all-pairs
 tensor-core distances with fused top-M, merge, sanitize, CAGRA detour prune
 and reverse-edge merge.  The dataset is resident in HBM when timing starts.
 
-Multi-GPU (torchrun): every rank builds the graph of its own shard of the job
-(a different seeded dataset of the configured size); no collective sits on the
-data path, so the scaling is weak.  The job's time is the max over ranks.
+Multi-GPU (torchrun): one global build over all ranks (gta/dist.py).  Each rank
+holds N rows of the configured size (rank r: shard r of a seeded dataset with
+shared mixture centres) and the bucket count grows with the rank count, so the
+bucket size and the per-GPU work stay fixed (weak scaling).  k-means sums are
+all-reduced, points go to their buckets' owners and lists come back by
+all-to-all, and the id tables are all-gathered for the prune (NCCL).  The
+job's time is the max over ranks.
 
 --impl reference times the reference's CPU implementation of the path on this
 host's cores (the oracle's C restatement of the kNN stages plus the
@@ -195,14 +199,17 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
-    workload = (f"{cfg.name}: N={cfg.n} x d={cfg.d} {cfg.dtype}, {cfg.n_clusters}-Gaussian mixture, "
-                f"B={cfg.n_buckets} buckets (2-way), M={cfg.knn_degree}, K={cfg.graph_degree}, "
+    workload = (f"{cfg.name}: N={cfg.n} per GPU x d={cfg.d} {cfg.dtype}, {cfg.n_clusters}-Gaussian mixture, "
+                f"B={cfg.n_buckets} buckets per GPU (2-way), M={cfg.knn_degree}, K={cfg.graph_degree}, "
                 f"{cfg.kmeans_iters} Lloyd iterations")
-    config = {"workload": workload, "n_per_rank": cfg.n, "d": cfg.d, "dtype": cfg.dtype, "n_buckets": cfg.n_buckets,
+    n_buckets_job = cfg.n_buckets * world
+    config = {"workload": workload, "n_per_rank": cfg.n, "n_total": cfg.n * world, "d": cfg.d, "dtype": cfg.dtype,
+              "n_buckets": n_buckets_job,
               "knn_degree": cfg.knn_degree, "graph_degree": cfg.graph_degree, "kmeans_iters": cfg.kmeans_iters,
               "kmeans_sample": cfg.kmeans_sample or None,
               "l2": "inputs and intermediates larger than L2 (no flush needed)",
-              "parallelism": f"{world} rank(s), independent shard per rank" if world > 1 else "1 GPU"}
+              "parallelism": (f"{world} ranks, buckets sharded (NCCL all-reduce / all-to-all / all-gather)"
+                              if world > 1 else "1 GPU")}
 
     if args.impl == "reference":
         if rank != 0:
@@ -215,7 +222,9 @@ def main():
             if s >= args.warmup:
                 per.append(t)
         sec = statistics.mean(per)
-        value = cfg.n * world / sec / 1e6
+        # the CPU pipeline's cost is linear in N at a fixed bucket size, so the whole job's
+        # throughput on the host equals that of one shard: value = points / second of CPU work
+        value = cfg.n / sec / 1e6
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True, "scaling": "weak",
                 "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": config, "impl": "reference",
@@ -234,13 +243,22 @@ def main():
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
-    X = gta.generate(cfg, seed=42 + rank)
+    X = gta.generate_shard(cfg, rank, seed=42)
     Xd = torch.from_numpy(X).cuda()
     torch.cuda.synchronize()
+    import gta.dist as gd
 
-    def step():
-        return gta.build_cagra(Xd, cfg.n_buckets, cfg.knn_degree, cfg.graph_degree, cfg.kmeans_iters,
-                               cfg.kmeans_sample, 42)
+    prm = gd.ShardParams(n_buckets=n_buckets_job, knn_degree=cfg.knn_degree, graph_degree=cfg.graph_degree,
+                         kmeans_iters=cfg.kmeans_iters, kmeans_sample=cfg.kmeans_sample, seed=42)
+    last = {}
+
+    def step(Xin=Xd):
+        if world == 1:
+            return gta.build_cagra(Xin, cfg.n_buckets, cfg.knn_degree, cfg.graph_degree, cfg.kmeans_iters,
+                                   cfg.kmeans_sample, 42)
+        res = gd.build_sharded(Xin, prm)
+        last["res"] = res
+        return res.graph
 
     for _ in range(args.warmup):
         g = step()
@@ -314,15 +332,23 @@ def main():
         elif v["units"] > 0:
             stage_summary[k]["gbs"] = v["units"] / (v["ms"] / 1e3) / 1e9
 
-    # quality: recall@32 of the pre-prune kNN graph on 1000 sampled points (exact GT in fp64 on the GPU)
+    # quality: recall@32 of the pre-prune kNN graph on 1000 sampled points of rank 0's rows
+    # (exact GT over the whole job's dataset in fp64 on the GPU)
     recall = None
-    if rank == 0:
+    if world == 1:
         ids, _ = gta.build_bucket(Xd, cfg.n_buckets, cfg.knn_degree, cfg.kmeans_iters, cfg.kmeans_sample, 42)
+        Xall = Xd
+    else:
+        ids = last["res"].knn_ids
+        Xall = torch.empty((cfg.n * world, cfg.d), dtype=Xd.dtype, device="cuda")
+        dist.all_gather_into_tensor(Xall, Xd)
+    if rank == 0:
+        n_all = Xall.shape[0]
         q = torch.from_numpy(np.random.default_rng(0).choice(cfg.n, 1000, replace=False)).cuda()
-        Xq = Xd[q].double()
+        Xq = Xall[q].double()
         best = []
-        for c0 in range(0, cfg.n, 1 << 18):
-            Xc = Xd[c0:c0 + (1 << 18)].double()
+        for c0 in range(0, n_all, 1 << 18):
+            Xc = Xall[c0:c0 + (1 << 18)].double()
             dd = (Xq * Xq).sum(1, keepdim=True) + (Xc * Xc).sum(1)[None, :] - 2.0 * Xq @ Xc.T
             idx = torch.arange(c0, c0 + Xc.shape[0], device="cuda")
             dd[q[:, None] == idx[None, :]] = float("inf")
@@ -333,17 +359,26 @@ def main():
         gt = torch.gather(i, 1, torch.topk(v, 32, dim=1, largest=False).indices).cpu().numpy()
         approx = ids[q].cpu().numpy()[:, :32]
         recall = float(np.mean([len(np.intersect1d(approx[r], gt[r])) / 32.0 for r in range(1000)]))
+    del Xall
 
-    # end to end through the C ABI with host buffers (pinned), copies inside the timed region
+    # end to end with host buffers (pinned), copies inside the timed region: through the C ABI
+    # (gta_build_cagra) on one GPU, through the sharded build on several
     e2e = None
     if not args.no_e2e:
-        Xh = torch.from_numpy(X).pin_memory().numpy()
-        gh = torch.empty((cfg.n, cfg.graph_degree), dtype=torch.int32).pin_memory().numpy().view(np.uint32)
+        Xh = torch.from_numpy(X).pin_memory()
+        gh_t = torch.empty((cfg.n, cfg.graph_degree), dtype=torch.int32).pin_memory()
+        gh = gh_t.numpy().view(np.uint32)
         from gta import _lib as L
         import ctypes
 
         def step_host():
-            ds = L.gta_dataset(data=Xh.ctypes.data_as(ctypes.c_void_p), n=cfg.n, d=cfg.d,
+            if world > 1:
+                g = step(Xh.to("cuda", non_blocking=True))
+                gh_t.copy_(g, non_blocking=True)
+                torch.cuda.current_stream().synchronize()
+                return
+            Xn = Xh.numpy()
+            ds = L.gta_dataset(data=Xn.ctypes.data_as(ctypes.c_void_p), n=cfg.n, d=cfg.d,
                                dtype=L.GTA_U8 if cfg.dtype == "uint8" else L.GTA_F32, metric=0, on_device=0)
             bp = L.gta_bucket_params(n_buckets=cfg.n_buckets, kmeans_iters=cfg.kmeans_iters, knn_degree=cfg.knn_degree,
                                      reserved0=0, kmeans_sample=cfg.kmeans_sample, seed=42, init_centroids=None,
@@ -365,7 +400,8 @@ def main():
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
             e2e_s = float(t.item())
         e2e = {"value": cfg.n * world / e2e_s / 1e6, "unit": UNIT, "ms_per_step": e2e_s * 1e3,
-               "h2d_bytes_per_step": int(X.nbytes), "d2h_bytes_per_step": int(gh.nbytes)}
+               "h2d_bytes_per_step": int(X.nbytes), "d2h_bytes_per_step": int(gh.nbytes),
+               "path": "gta_build_cagra (C ABI, host buffers)" if world == 1 else "gta.dist.build_sharded"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:

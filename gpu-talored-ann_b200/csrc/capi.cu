@@ -249,8 +249,28 @@ void kmeans_fit_impl(const float* Xs, const float* xn, int64_t n_s, int d, int d
 }
 
 // Per-bucket all-pairs top-M for every membership row.
+// k-means sample size: min(0.1, 1e7 / N) of N unless given, at least B.
+int64_t kmeans_sample_size(int64_t N, int64_t requested, int B)
+{
+    int64_t n_s = requested > 0 ? std::min<int64_t>(requested, N)
+                                : std::max<int64_t>(1, std::llround(std::min(0.1, 1e7 / double(N)) * double(N)));
+    return std::max<int64_t>(n_s, B);
+}
+
+// k-means++ pool: min(sample, 20 B) rows (the ratio shrinks past 1024 buckets).
+int64_t kmeans_pool_size(int64_t n_s, int B)
+{
+    const int ratio = B <= 1024 ? 20 : std::max(2, 20 * 1024 / B);
+    return std::min<int64_t>(n_s, static_cast<int64_t>(ratio) * B);
+}
+
+uint64_t kmeans_pool_seed(uint64_t seed) { return seed ^ 0x9E3779B97F4A7C15ull; }
+
+// members: the row of X gathered into each membership slot (grouped by bucket);
+// gid: the id written to the lists for each slot (members when null).
 void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* members, const int64_t* offsets_dev,
-                     int B, int M, int32_t* list_ids, float* list_dists, int* err, cudaStream_t st)
+                     int B, int M, int32_t* list_ids, float* list_dists, int* err, cudaStream_t st,
+                     const int32_t* gid = nullptr)
 {
     (void)n;
     std::vector<int64_t> off(static_cast<size_t>(B) + 1);
@@ -281,7 +301,7 @@ void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* 
     auto work = upload(wl, st);
     DistTopkProblem pr;
     pr.A = pool.get(); pr.a_total = n_mem; pr.B = pool.get(); pr.b_total = n_mem; pr.elem = elem; pr.d = d;
-    pr.d_pad = d_pad; pr.a_norm = pnorm.get(); pr.b_norm = pnorm.get(); pr.b_gid = members; pr.work = work.get();
+    pr.d_pad = d_pad; pr.a_norm = pnorm.get(); pr.b_norm = pnorm.get(); pr.b_gid = gid ? gid : members; pr.work = work.get();
     pr.n_work = static_cast<int>(wl.size()); pr.m_out = M; pr.exclude_self = true; pr.out_ids = list_ids;
     pr.out_dists = list_dists; pr.err = err;
     pr.prof_name = "dist_topk_bucket";
@@ -328,9 +348,7 @@ void build_bucket_impl(const gta_dataset& ds, const gta_bucket_params& p, const 
     const int d32 = pad_dim(d, kElemF32);
 
     // ---- k-means over a sample
-    int64_t n_s = p.kmeans_sample > 0 ? std::min<int64_t>(p.kmeans_sample, N)
-                                      : std::max<int64_t>(1, std::llround(std::min(0.1, 1e7 / double(N)) * double(N)));
-    n_s = std::max<int64_t>(n_s, B);
+    const int64_t n_s = kmeans_sample_size(N, p.kmeans_sample, B);
     DevBuf<int32_t> sid(static_cast<size_t>(n_s), st);
     sample_ids(N, n_s, p.seed, sid.get(), st);
     DevBuf<float> Xs(static_cast<size_t>(n_s) * d32, st), xs_n(static_cast<size_t>(n_s), st);
@@ -343,10 +361,14 @@ void build_bucket_impl(const gta_dataset& ds, const gta_bucket_params& p, const 
     if (p.init_centroids) {
         copy_rows_padded(C.get(), d32, p.init_centroids, d, B, p.init_on_device != 0, st);
     } else {
-        const int ratio = B <= 1024 ? 20 : std::max(2, 20 * 1024 / B);
-        const int64_t pool_n = std::min<int64_t>(n_s, static_cast<int64_t>(ratio) * B);
+        // the k-means++ pool: its own stratified draw over all N rows
+        const int64_t pool_n = kmeans_pool_size(n_s, B);
         ProfScope prof("kmeans_init", 0.0, st);
-        kmeanspp_init(Xs.get(), xs_n.get(), pool_n, d, d32, B, p.seed, C.get(), err.get(), st);
+        DevBuf<int32_t> pid(static_cast<size_t>(pool_n), st);
+        sample_ids(N, pool_n, kmeans_pool_seed(p.seed), pid.get(), st);
+        DevBuf<float> Xp(static_cast<size_t>(pool_n) * d32, st);
+        convert_rows(X, ds.dtype, d, pid.get(), pool_n, Xp.get(), kElemF32, d32, nullptr, st);
+        kmeanspp_init(Xp.get(), nullptr, pool_n, d, d32, B, p.seed, C.get(), err.get(), st);
     }
     convert_rows(C.get(), GTA_F32, d32, nullptr, B, nullptr, kElemF32, d32, cn.get(), st);
     {
@@ -667,10 +689,12 @@ int gta_kmeans_init(const float* X, int64_t pool_n, int32_t d, int32_t B, uint64
         cudaStream_t st = S(stream);
         const int d32 = pad_dim(d, kElemF32);
         DevBuf<float> Xp(static_cast<size_t>(pool_n) * d32, st), C(static_cast<size_t>(B) * d32, st);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
         convert_rows(X, GTA_F32, d, nullptr, pool_n, Xp.get(), kElemF32, d32, nullptr, st);
-        kmeanspp_init(Xp.get(), nullptr, pool_n, d, d32, B, seed, C.get(), nullptr, st);
+        kmeanspp_init(Xp.get(), nullptr, pool_n, d, d32, B, seed, C.get(), err.get(), st);
         unpad_rows(centroids, d, C.get(), d32, B, true, st);
-        GTA_CUDA(cudaStreamSynchronize(st));
+        check_device_error(err.get(), st, "gta_kmeans_init");
     });
 }
 
@@ -793,6 +817,143 @@ int gta_reverse_merge_noalloc(const uint32_t* pruned, int64_t n, int32_t k, uint
 
 int64_t gta_reverse_merge_noalloc_max_rows(void) { return reverse_merge_noalloc_max_rows(); }
 int64_t gta_reverse_merge_noalloc_max_edges(void) { return reverse_merge_noalloc_max_edges(); }
+
+// ---------------------------------------------------------------- shard stages (multi-GPU build)
+int gta_kmeans_sizes(int64_t n, const gta_bucket_params* p, int64_t* n_sample, int64_t* pool_n, uint64_t* pool_seed)
+{
+    return guard([&] {
+        GTA_REQUIRE(p && n_sample && pool_n && pool_seed && n >= 2 && p->n_buckets >= 2 && p->n_buckets <= n, kInvalid,
+                    "gta_kmeans_sizes: bad argument");
+        *n_sample = kmeans_sample_size(n, p->kmeans_sample, p->n_buckets);
+        *pool_n = kmeans_pool_size(*n_sample, p->n_buckets);
+        *pool_seed = kmeans_pool_seed(p->seed);
+    });
+}
+
+int gta_sample_ids(int64_t n, int64_t n_s, uint64_t seed, int32_t* ids, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(ids && n >= 1 && n_s >= 1 && n_s <= n && n < (1ll << 31), kInvalid, "gta_sample_ids: bad argument");
+        sample_ids(n, n_s, seed, ids, S(stream));
+    });
+}
+
+int gta_gather_rows(const void* X, int32_t dtype, int64_t n, int32_t d, int64_t row0, const int32_t* ids,
+                    int64_t n_ids, float* out, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE((X || n == 0) && (ids || n_ids == 0) && (out || n_ids == 0) && d >= 1 && n >= 0 && n_ids >= 0,
+                    kInvalid, "gta_gather_rows: bad argument");
+        gather_range(X, dtype, d, row0, n, ids, n_ids, out, S(stream));
+    });
+}
+
+int gta_centroid_sums(const float* X, int64_t n, int32_t d, const int32_t* assign, int32_t B, double* sums,
+                      int64_t* counts, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(sums && counts && d >= 1 && B >= 1 && n >= 0 && (n == 0 || (X && assign)), kInvalid,
+                    "gta_centroid_sums: bad argument");
+        cudaStream_t st = S(stream);
+        if (n == 0) {
+            GTA_CUDA(cudaMemsetAsync(sums, 0, sizeof(double) * static_cast<size_t>(B) * d, st));
+            GTA_CUDA(cudaMemsetAsync(counts, 0, sizeof(int64_t) * static_cast<size_t>(B), st));
+            return;
+        }
+        centroid_partial(X, n, d, d, assign, B, sums, reinterpret_cast<long long*>(counts), st);
+    });
+}
+
+int gta_centroid_means(const double* sums, const int64_t* counts, int32_t B, int32_t d, float* centroids, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(sums && counts && centroids && B >= 1 && d >= 1, kInvalid, "gta_centroid_means: bad argument");
+        centroid_means(sums, reinterpret_cast<const long long*>(counts), centroids, B, d, centroids, S(stream));
+    });
+}
+
+int gta_group_memberships(const int32_t* bucket, const int32_t* other, int64_t n, int32_t B, int32_t* order,
+                          int64_t* offsets, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(offsets && B >= 2 && n >= 0 && (n == 0 || (bucket && other && order)), kInvalid,
+                    "gta_group_memberships: bad argument");
+        cudaStream_t st = S(stream);
+        if (n == 0) {
+            GTA_CUDA(cudaMemsetAsync(offsets, 0, sizeof(int64_t) * (static_cast<size_t>(B) + 1), st));
+            return;
+        }
+        group_rows(bucket, other, n, B, order, offsets, st);
+    });
+}
+
+int gta_bucket_knn_rows(const void* R, int32_t dtype, int64_t n, int32_t d, const int32_t* order, const int32_t* gid,
+                        const int64_t* offsets, int32_t B, int32_t M, int32_t* list_ids, float* list_dists, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(offsets && B >= 1 && M >= 1 && M <= 128 && n >= 0 &&
+                        (n == 0 || (R && order && gid && list_ids && list_dists)),
+                    kInvalid, "gta_bucket_knn_rows: bad argument");
+        if (n == 0) return;
+        cudaStream_t st = S(stream);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        DevBuf<int32_t> gid_sorted(static_cast<size_t>(n), st);
+        gather_i32(gid, order, n, gid_sorted.get(), st);
+        bucket_knn_impl(R, dtype, n, d, order, offsets, B, M, list_ids, list_dists, err.get(), st, gid_sorted.get());
+        check_device_error(err.get(), st, "gta_bucket_knn_rows");
+    });
+}
+
+int gta_sanitize_rows(const int32_t* knn, int64_t n_rows, int64_t row0, int64_t n, int32_t m, uint32_t* out,
+                      void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(m >= 1 && n >= 1 && row0 >= 0 && n_rows >= 0 && row0 + n_rows <= n &&
+                        (n_rows == 0 || (knn && out)),
+                    kInvalid, "gta_sanitize_rows: bad argument");
+        if (n_rows == 0) return;
+        sanitize_rows(knn, n_rows, row0, n, m, out, S(stream));
+    });
+}
+
+int gta_prune_rows(const uint32_t* knn, int64_t n, int32_t m, int32_t k, int64_t row0, int64_t n_rows,
+                   const int32_t* top2, int32_t B, uint32_t* pruned, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(knn && (pruned || n_rows == 0) && (!top2 || B >= 2), kInvalid, "gta_prune_rows: bad argument");
+        if (n_rows == 0) return;
+        cudaStream_t st = S(stream);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        DevBuf<int32_t> order;
+        if (top2) {
+            order = DevBuf<int32_t>(static_cast<size_t>(n_rows), st);
+            locality_order(top2, n_rows, B, order.get(), st);
+        }
+        prune_rows(knn, n, m, k, order.get(), row0, n_rows, pruned, err.get(), st);
+        check_device_error(err.get(), st, "gta_prune_rows");
+    });
+}
+
+int gta_reverse_merge_rows(const uint32_t* pruned, int64_t n, int32_t k, int64_t row0, int64_t n_rows, uint32_t* out,
+                           void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(pruned && n >= 1 && (out || n_rows == 0), kInvalid, "gta_reverse_merge_rows: bad argument");
+        if (n_rows == 0) return;
+        reverse_merge_rows(pruned, n, k, row0, n_rows, out, S(stream));
+    });
+}
 
 // ---------------------------------------------------------------- files
 int gta_read_dataset_header(const char* path, int64_t* n, int32_t* d, int32_t* dtype)

@@ -20,6 +20,7 @@ enum DevErr : int {
     kDevTimeoutDrain = 4,     // teardown wait ran out
     kDevBadIndex = 5,         // an id outside [0, N) met a bounds check
     kDevBadShape = 6,         // kernel launched with an unsupported shape
+    kDevTimeoutGrid = 7,      // a grid barrier of a cooperative launch never completed
 };
 
 constexpr long long kWaitBudgetCycles = 4000000000LL;   // ~2 s at 1.9 GHz
@@ -111,7 +112,7 @@ __device__ __forceinline__ bool mbar_wait_backoff(uint32_t bar, uint32_t parity,
     }
 }
 
-// ---- TMA (2-D tiled bulk tensor load, no multicast) -----------------------
+// ---- TMA (2-D tiled bulk tensor load into this CTA's shared memory) ---------
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint32_t bar, int32_t x, int32_t y)
 {
     asm volatile(
@@ -200,6 +201,39 @@ __device__ __forceinline__ void tmem_ld_wait_regs(uint32_t (&v)[16])
                  : "memory");
 }
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Store 32 consecutive 32-bit TMEM columns of the warp's 32 lanes (thread t -> lane base + t).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&v)[32])
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]), "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]), "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31]) : "memory");
+}
+// 32 lanes x 2 consecutive 32-bit TMEM columns (one 64-bit key per lane); waits for the load.
+__device__ __forceinline__ uint64_t tmem_ld_key(uint32_t taddr)
+{
+    uint32_t lo, hi;
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0, %1}, [%2];\n\t"
+                 "tcgen05.wait::ld.sync.aligned;"
+                 : "=r"(lo), "=r"(hi)
+                 : "r"(taddr)
+                 : "memory");
+    return (static_cast<uint64_t>(hi) << 32) | lo;
+}
+// Wait until this thread's tcgen05.st operations have completed.
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+// Wait for outstanding tcgen05.ld into one 32-register array.
+__device__ __forceinline__ void tmem_ld_wait_regs32(uint32_t (&a)[32])
+{
+    asm volatile("tcgen05.wait::ld.sync.aligned;" : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]), "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15]), "+r"(a[16]), "+r"(a[17]), "+r"(a[18]), "+r"(a[19]), "+r"(a[20]), "+r"(a[21]), "+r"(a[22]), "+r"(a[23]), "+r"(a[24]), "+r"(a[25]), "+r"(a[26]), "+r"(a[27]), "+r"(a[28]), "+r"(a[29]), "+r"(a[30]), "+r"(a[31]) : : "memory");
+}
+// Wait for outstanding tcgen05.ld into two 32-register arrays (in/out operands keep their uses below the wait).
+__device__ __forceinline__ void tmem_ld_wait_regs2x32(uint32_t (&a)[32], uint32_t (&b)[32])
+{
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]), "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15]), "+r"(a[16]), "+r"(a[17]), "+r"(a[18]), "+r"(a[19]), "+r"(a[20]), "+r"(a[21]), "+r"(a[22]), "+r"(a[23]), "+r"(a[24]), "+r"(a[25]), "+r"(a[26]), "+r"(a[27]), "+r"(a[28]), "+r"(a[29]), "+r"(a[30]), "+r"(a[31]),
+                   "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7]), "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]), "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15]), "+r"(b[16]), "+r"(b[17]), "+r"(b[18]), "+r"(b[19]), "+r"(b[20]), "+r"(b[21]), "+r"(b[22]), "+r"(b[23]), "+r"(b[24]), "+r"(b[25]), "+r"(b[26]), "+r"(b[27]), "+r"(b[28]), "+r"(b[29]), "+r"(b[30]), "+r"(b[31])
+                 :
+                 : "memory");
+}
 
 // Shared-memory matrix descriptor: K-major tile of 128-byte rows with the
 // 128-byte swizzle written by TMA (8-row atoms, 1024 B apart).

@@ -15,6 +15,13 @@
 //               list fed through a small unsorted buffer.
 // The (rows x segment) score matrix never reaches HBM.
 //
+// Two CTAs per SM (lists of up to 64 keys): 64-column tiles, two 64-column
+// accumulators and the row lists in TMEM (key i of a row in columns
+// 128 + 2i / 129 + 2i), a small shared-memory footprint, so that two CTAs --
+// two epilogue warps per SM sub-partition -- share each SM and hide each
+// other's scan latency.  Longer lists keep one CTA per SM, 128-column tiles
+// and the lists in shared memory.
+//
 // Two modes:
 //   exact  (bf16 operands holding 8-bit integer data): every product and
 //          partial sum is an integer below 2^24, so s is exact; the kernel
@@ -52,8 +59,8 @@ namespace {
 constexpr int kTileM = 128;
 constexpr int kTileN = 128;
 constexpr uint32_t kTileBytes = 128u * 128u;  // 128 rows x 128 B
-constexpr int kThreads = 192;
-constexpr uint32_t kTmemCols = 256;
+constexpr int kThreads = 192;                  // TMA, MMA, 4 epilogue warps
+constexpr uint32_t kSmemMax2 = 233472u / 2u - 1024u;  // per CTA when two share an SM
 constexpr uint32_t kSmemMax = 232448;         // 227 KB per CTA (opt-in)
 
 struct DistTopkArgs {
@@ -78,6 +85,7 @@ struct DistTopkArgs {
     unsigned long long* stats;// optional: [passes, flush events, rows]
     int* err;
     uint32_t list_off, buf_off, pn_off, bar_off;
+    uint32_t scr_off;           // two-CTA variant: per-lane score scratch
 };
 
 constexpr int kBuf = 32;                  // per-row staging buffer (entries)
@@ -170,6 +178,162 @@ __device__ __noinline__ void flush_row(uint64_t* list, uint64_t* buf, int nb)
     merge_into_list<kL>(list, k);
 }
 
+// ---- row lists in TMEM (paired epilogue): key i of the row in columns 2i (low
+// word) and 2i+1 (high word) of the list's column range.
+__device__ __forceinline__ void keys_load32(uint32_t taddr, uint64_t (&k)[32])
+{
+    uint32_t a[32], b[32];
+    tmem_ld_32x32b_x32(taddr, a);
+    tmem_ld_32x32b_x32(taddr + 32u, b);
+    tmem_ld_wait_regs2x32(a, b);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        k[i] = (static_cast<uint64_t>(a[2 * i + 1]) << 32) | a[2 * i];
+        k[16 + i] = (static_cast<uint64_t>(b[2 * i + 1]) << 32) | b[2 * i];
+    }
+}
+
+__device__ __forceinline__ void keys_store32(uint32_t taddr, const uint64_t (&k)[32])
+{
+    uint32_t a[32], b[32];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        a[2 * i] = static_cast<uint32_t>(k[i]);
+        a[2 * i + 1] = static_cast<uint32_t>(k[i] >> 32);
+        b[2 * i] = static_cast<uint32_t>(k[16 + i]);
+        b[2 * i + 1] = static_cast<uint32_t>(k[16 + i] >> 32);
+    }
+    tmem_st_32x32b_x32(taddr, a);
+    tmem_st_32x32b_x32(taddr + 32u, b);
+}
+
+__device__ __forceinline__ void keys_load16(uint32_t taddr, uint64_t (&k)[16])
+{
+    uint32_t a[32];
+    tmem_ld_32x32b_x32(taddr, a);
+    tmem_ld_wait_regs32(a);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) k[i] = (static_cast<uint64_t>(a[2 * i + 1]) << 32) | a[2 * i];
+}
+
+__device__ __forceinline__ void keys_store16(uint32_t taddr, const uint64_t (&k)[16])
+{
+    uint32_t a[32];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        a[2 * i] = static_cast<uint32_t>(k[i]);
+        a[2 * i + 1] = static_cast<uint32_t>(k[i] >> 32);
+    }
+    tmem_st_32x32b_x32(taddr, a);
+}
+
+__device__ __forceinline__ uint64_t min_key(uint64_t a, uint64_t b) { return a < b ? a : b; }
+__device__ __forceinline__ float key_dist(uint64_t key) { return key2f(static_cast<uint32_t>(key >> 32)); }
+
+struct ListTail {
+    uint64_t last;  // the list's kL-th key
+    uint64_t msel;  // its m_sel-th key (screen mode)
+};
+
+// Flush the row's staging buffer into its TMEM list of kL (32 or 64) keys,
+// keeping the kL smallest (same network as merge_into_list, in registers).
+template <int kL, bool kScreen>
+__device__ __noinline__ ListTail flush_tmem(uint32_t tl, const uint64_t* buf, int nb, int m_sel)
+{
+    uint64_t k[kBuf];
+#pragma unroll
+    for (int i = 0; i < kBuf; ++i) k[i] = (i < nb) ? buf[i * 128] : kEmptyKey;
+    sort32(k);
+    ListTail t{kEmptyKey, kEmptyKey};
+    if constexpr (kL == 32) {
+        uint64_t l[32];
+        keys_load32(tl, l);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) l[i] = min_key(l[i], k[31 - i]);
+        merge32(l);
+        keys_store32(tl, l);
+        t.last = l[31];
+    } else {
+        // 64 keys in four 16-key blocks of TMEM, worked on a block pair at a time
+        uint64_t a[16], b[16];
+        keys_load16(tl + 64u, a);  // keys 32..47 against buffer keys 31..16
+#pragma unroll
+        for (int i = 0; i < 16; ++i) a[i] = min_key(a[i], k[31 - i]);
+        keys_load16(tl + 96u, b);  // keys 48..63 against buffer keys 15..0
+#pragma unroll
+        for (int i = 0; i < 16; ++i) b[i] = min_key(b[i], k[15 - i]);
+        // stride-32 half-cleaner: (0..15, 32..47) and (16..31, 48..63)
+        uint64_t c[16];
+        keys_load16(tl, c);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) cmp_swap(c[i], a[i]);
+        keys_store16(tl, c);
+        keys_store16(tl + 64u, a);
+        keys_load16(tl + 32u, c);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) cmp_swap(c[i], b[i]);
+        keys_store16(tl + 32u, c);
+        keys_store16(tl + 96u, b);
+        tmem_st_wait();
+        // strides 16..1 inside each 32-key half
+        uint64_t l[32];
+        keys_load32(tl, l);
+        merge32(l);
+        keys_store32(tl, l);
+        keys_load32(tl + 64u, l);
+        merge32(l);
+        keys_store32(tl + 64u, l);
+        t.last = l[31];
+    }
+    tmem_st_wait();
+    // the m_sel-th key read back from TMEM (a runtime index into a register array would go to local memory)
+    if constexpr (kScreen) t.msel = tmem_ld_key(tl + 2u * static_cast<uint32_t>(m_sel - 1));
+    return t;
+}
+
+// Write a row's final TMEM list (kL keys, ascending): the top-m_out (distance,
+// id) pairs, or in screen mode the candidate columns within the margin of the
+// m_sel-th (-1 when entries beyond the list may qualify: exact rescan).
+// Warp-collective (TMEM loads); lanes without a row write nothing.
+template <int kL, bool kScreen>
+__device__ __noinline__ void list_out(uint32_t tl, bool row_ok, int64_t arow, float anorm, float margin, int m_out,
+                                      int m_sel, int32_t* out_ids, float* out_dists, int32_t* cand_cols, int32_t* cand_n)
+{
+    uint64_t msel = kEmptyKey;
+    if constexpr (kScreen) msel = tmem_ld_key(tl + 2u * static_cast<uint32_t>(m_sel - 1));
+    const float bound = (msel != kEmptyKey) ? key_dist(msel) + margin : INFINITY;
+    bool overflow = false;
+    if constexpr (kScreen) {
+        const uint64_t top = tmem_ld_key(tl + 2u * static_cast<uint32_t>(kL - 1));
+        overflow = top != kEmptyKey && key_dist(top) <= bound;
+        if (row_ok && overflow) cand_n[arow] = -1;  // entries beyond the list may be within the bound
+    }
+    int nc = 0;
+#pragma unroll 1
+    for (int blk = 0; blk < kL; blk += 32) {
+        uint64_t c[32];
+        keys_load32(tl + 2u * static_cast<uint32_t>(blk), c);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+            const uint64_t key = c[j];
+            if constexpr (!kScreen) {
+                if (row_ok && blk + j < m_out) {
+                    const bool vld = key != kEmptyKey;
+                    out_ids[arow * m_out + blk + j] = vld ? static_cast<int32_t>(static_cast<uint32_t>(key)) : -1;
+                    out_dists[arow * m_out + blk + j] = vld ? key_dist(key) + anorm : INFINITY;
+                }
+            } else {
+                const bool in = key != kEmptyKey && key_dist(key) <= bound;
+                if (row_ok && !overflow && in) cand_cols[arow * kL + blk + j] = static_cast<int32_t>(static_cast<uint32_t>(key));
+                nc += in ? 1 : 0;
+            }
+        }
+    }
+    if constexpr (kScreen) {
+        if (row_ok && !overflow) cand_n[arow] = nc;
+    }
+}
+
 // v[e] for a runtime e in [0, 16) through a 4-level select tree (static register indices).
 __device__ __forceinline__ uint32_t pick16(const uint32_t (&v)[16], int e)
 {
@@ -183,7 +347,6 @@ __device__ __forceinline__ uint32_t pick16(const uint32_t (&v)[16], int e)
     return (e & 8) ? l3[1] : l3[0];
 }
 
-__device__ __forceinline__ float key_dist(uint64_t key) { return key2f(static_cast<uint32_t>(key >> 32)); }
 
 // Admission threshold of a row: the kL-th key (every finite value passes while
 // the list is not full); screen mode also caps it at the m_sel-th + margin.
@@ -226,11 +389,17 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, i
     return true;
 }
 
-template <bool kTF32, int kL>
-__global__ void __launch_bounds__(kThreads, 1)
+// kV = 1: one CTA per SM, 128-column tiles, row lists in shared memory.
+// kV = 2: two CTAs per SM, 64-column tiles, row lists (at most 64 keys) in TMEM.
+template <bool kTF32, int kL, int kV>
+__global__ void __launch_bounds__(kThreads, kV)
     dist_topk_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const DistTopkArgs p)
 {
+    static_assert(kV == 1 || (kV == 2 && kL <= 64), "TMEM row lists hold at most 64 keys");
+    constexpr uint32_t kTmemCols = 256u;
+    constexpr int kTN = kV == 1 ? 128 : 64;                            // column tile
+    constexpr uint32_t kBChunk = static_cast<uint32_t>(kTN) * 128u;   // bytes of one B K-chunk
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t base = smem_u32(smem_raw);
     uint8_t* gbase = smem_raw;
@@ -242,10 +411,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const WorkItem w = p.work[blockIdx.x];
-    const int n_ct = (w.b_rows + kTileN - 1) / kTileN;
-    const int t0 = (w.self_col0 >= 0) ? min(n_ct - 1, w.self_col0 / kTileN) : 0;
+    const int n_ct = (w.b_rows + kTN - 1) / kTN;
+    const int t0 = (w.self_col0 >= 0) ? min(n_ct - 1, w.self_col0 / kTN) : 0;
     const int S = p.stages;
-    const uint32_t stage_bytes = p.a_resident ? kTileBytes : 2u * kTileBytes;
+    const uint32_t stage_bytes = p.a_resident ? kBChunk : kBChunk + kTileBytes;
     const uint32_t a_bytes = p.a_resident ? static_cast<uint32_t>(p.k_chunks) * kTileBytes : 0u;
     const uint32_t stage0 = base + a_bytes;
     constexpr int kElemsPerChunk = kTF32 ? 32 : 64;
@@ -301,9 +470,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (!mbar_wait_backoff(EMPTY_BAR(s), ph ^ 1u, abort_flag, p.err, kDevTimeoutEmpty)) { ok = false; break; }
                     const uint32_t dst = stage0 + static_cast<uint32_t>(s) * stage_bytes;
                     mbar_arrive_expect_tx(FULL_BAR(s), stage_bytes);
-                    tma_load_2d(dst, &tmB, FULL_BAR(s), kc * kElemsPerChunk, w.b_row0 + ct * kTileN);
+                    tma_load_2d(dst, &tmB, FULL_BAR(s), kc * kElemsPerChunk, w.b_row0 + ct * kTN);
                     if (!p.a_resident)
-                        tma_load_2d(dst + kTileBytes, &tmA, FULL_BAR(s), kc * kElemsPerChunk, w.a_row0);
+                        tma_load_2d(dst + kBChunk, &tmA, FULL_BAR(s), kc * kElemsPerChunk, w.a_row0);
                     ++it;
                 }
             }
@@ -315,7 +484,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = make_idesc(kTF32 ? 2u : 1u, kTileM, kTileN);
+            const uint32_t idesc = make_idesc(kTF32 ? 2u : 1u, kTileM, kTN);
             bool ok = true;
             long long mma_wait_acc = 0, mma_wait_full = 0;
             if (p.a_resident) ok = mbar_wait_backoff(a_full, 0, abort_flag, p.err, kDevTimeoutFull);
@@ -327,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (!mbar_wait_backoff(ACC_EMPTY(b), (use & 1u) ^ 1u, abort_flag, p.err, kDevTimeoutAcc)) { ok = false; break; }
                 if (p.stats) mma_wait_acc += clock64() - m0;
                 tc_fence_after();
-                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * kTileN);
+                const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * kTN);
                 for (int kc = 0; kc < p.k_chunks; ++kc) {
                     const int s = it % S;
                     const uint32_t ph = static_cast<uint32_t>(it / S) & 1u;
@@ -336,7 +505,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (p.stats) mma_wait_full += clock64() - m1;
                     tc_fence_after();
                     const uint32_t sb = stage0 + static_cast<uint32_t>(s) * stage_bytes;
-                    const uint32_t sa = p.a_resident ? base + static_cast<uint32_t>(kc) * kTileBytes : sb + kTileBytes;
+                    const uint32_t sa = p.a_resident ? base + static_cast<uint32_t>(kc) * kTileBytes : sb + kBChunk;
                     const uint64_t adesc = smem_desc_sw128(sa);
                     const uint64_t bdesc = smem_desc_sw128(sb);
 #pragma unroll
@@ -355,7 +524,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 atomicAdd(&p.stats[7], static_cast<unsigned long long>(mma_wait_full));
             }
         }
-    } else {
+    } else if constexpr (kV == 1) {
         // ------------------------------------------------------------ epilogue
         const int q = warp & 3;
         const int r = q * 32 + lane;
@@ -406,7 +575,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (k + 1 < n_ct) prefetch_cols(k + 1);
             const long long w0 = st_on ? clock64() : 0;
-            if (!mbar_wait(ACC_FULL(b), use & 1u, abort_flag, p.err, kDevTimeoutAcc)) { ok = false; break; }
+            const bool got = mbar_wait(ACC_FULL(b), use & 1u, abort_flag, p.err, kDevTimeoutAcc);
+            if (!__all_sync(0xffffffffu, got)) { ok = false; break; }  // the warp leaves together
             if (st_on) cyc_wait += clock64() - w0;
             tc_fence_after();
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * kTileN);
@@ -532,6 +702,159 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
             }
         }
+    } else {
+        // ------------------------------------------------------------ epilogue, lists in TMEM
+        const int q = warp & 3;  // TMEM lane quarter (a warp reaches lanes 32 * (warp % 4) ..)
+        const int r = q * 32 + lane;
+        const bool row_ok = r < w.a_rows;
+        const bool has_self = w.self_col0 >= 0;
+        const int64_t arow = static_cast<int64_t>(w.a_row0) + r;
+        const float anorm = row_ok ? p.a_norm[arow] : 0.0f;
+        float margin = 0.0f;
+        if (kTF32) {
+            const float an = sqrtf(fmaxf(anorm, 0.0f)), bm = *p.b_maxnorm;
+            margin = p.mc1 * an * bm + p.mc2 * (an + bm) * (an + bm);
+        }
+        const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
+        const uint32_t tl = lane_base + 2u * static_cast<uint32_t>(kTN);  // after the two accumulators
+        uint64_t* my_buf = buf + r;
+        float* scr = reinterpret_cast<float*>(gbase + p.scr_off) + (q * 32 + lane) * 20;
+        {
+            uint32_t e[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) e[i] = 0xffffffffu;
+#pragma unroll
+            for (int c = 0; c < 2 * kL; c += 32) tmem_st_32x32b_x32(tl + static_cast<uint32_t>(c), e);
+            tmem_st_wait();
+        }
+        float thr = row_ok ? FLT_MAX : -FLT_MAX;
+        int nb = 0, n_pass = 0, n_flush = 0;
+        bool ok = true;
+        const bool st_on = p.stats != nullptr;
+        long long cyc_wait = 0, cyc_flush = 0;
+        const long long cyc0 = st_on ? clock64() : 0;
+        // this warp's copy of the current tile's column norms / ids (lane l: columns 2l, 2l+1)
+        float* pnw = pn_s + q * 64;
+        uint32_t* idw = reinterpret_cast<uint32_t*>(pn_s + 4 * 64) + q * 64;
+        float pf_n[2];
+        uint32_t pf_i[2];
+        auto prefetch_cols = [&](int kk) {
+            const int ctn = tile_at(kk, t0, n_ct);
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int col = ctn * kTN + lane * 2 + j;
+                const bool cok = col < w.b_rows;
+                const int64_t brow = static_cast<int64_t>(w.b_row0) + col;
+                pf_n[j] = cok ? p.b_norm[brow] : INFINITY;
+                pf_i[j] = (!kTF32 && cok && p.b_gid) ? static_cast<uint32_t>(p.b_gid[brow]) : static_cast<uint32_t>(col);
+            }
+        };
+        // the row's own column: tile t0 + r / 64, slice (r % 64) / 16, element r % 16
+        const int self_ct = has_self ? t0 + (r >> 6) : -1;
+        const int self_c = (r & 63) >> 4;
+        prefetch_cols(0);
+        for (int k = 0; k < n_ct; ++k) {
+            const int ct = tile_at(k, t0, n_ct);
+            const int b = k & 1;
+            const uint32_t use = static_cast<uint32_t>(k >> 1);
+            __syncwarp();
+            reinterpret_cast<float2*>(pnw)[lane] = make_float2(pf_n[0], pf_n[1]);
+            reinterpret_cast<uint2*>(idw)[lane] = make_uint2(pf_i[0], pf_i[1]);
+            __syncwarp();
+            if (k + 1 < n_ct) prefetch_cols(k + 1);
+            const long long w0 = st_on ? clock64() : 0;
+            const bool got = mbar_wait(ACC_FULL(b), use & 1u, abort_flag, p.err, kDevTimeoutAcc);
+            if (!__all_sync(0xffffffffu, got)) { ok = false; break; }  // the warp leaves together
+            if (st_on) cyc_wait += clock64() - w0;
+            tc_fence_after();
+            const uint32_t tbase = lane_base + static_cast<uint32_t>(b * kTN);
+            uint32_t vn[16];
+            __syncwarp();
+            tmem_ld_32x32b_x16(tbase, vn);
+#pragma unroll 1
+            for (int c = 0; c < kTN / 16; ++c) {  // slices of 16 columns; slice c+1 loads while c is scanned
+                uint32_t v[16];
+                tmem_ld_wait_regs(vn);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) v[e] = vn[e];
+                if (c + 1 < kTN / 16) {
+                    __syncwarp();
+                    tmem_ld_32x32b_x16(tbase + static_cast<uint32_t>((c + 1) * 16), vn);
+                }
+                const int self_e = (ct == self_ct && c == self_c) ? (lane & 15) : -1;
+                const uint32_t c0 = static_cast<uint32_t>(ct * kTN + c * 16);
+                const float4* pn4 = reinterpret_cast<const float4*>(pnw + c * 16);
+                float sv[16];
+                uint32_t mask = 0;
+#pragma unroll
+                for (int e4 = 0; e4 < 4; ++e4) {
+                    const float4 n4 = pn4[e4];
+                    const float nv[4] = {n4.x, n4.y, n4.z, n4.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int e = e4 * 4 + u;
+                        sv[e] = fmaf(-2.0f, __uint_as_float(v[e]), nv[u]);
+                        mask |= (sv[e] <= thr) ? (1u << e) : 0u;
+                    }
+                }
+                if (self_e >= 0) mask &= ~(1u << self_e);
+                const int npass = __popc(mask);
+                const int rounds = __reduce_max_sync(0xffffffffu, static_cast<unsigned>(npass));
+                if (rounds > 0) {
+                    // scores to this lane's scratch, then one append per pass of the busiest lane
+                    float4* s4 = reinterpret_cast<float4*>(scr);
+#pragma unroll
+                    for (int e4 = 0; e4 < 4; ++e4)
+                        s4[e4] = make_float4(sv[e4 * 4], sv[e4 * 4 + 1], sv[e4 * 4 + 2], sv[e4 * 4 + 3]);
+                    uint32_t m = mask;
+                    for (int i = 0; i < rounds; ++i) {
+                        const int e = __ffs(m) - 1;
+                        if (e >= 0) {
+                            const uint32_t id = kTF32 ? c0 + static_cast<uint32_t>(e) : idw[c * 16 + e];
+                            my_buf[(nb + i) * 128] = (static_cast<uint64_t>(f2key(scr[e])) << 32) | id;
+                            m &= m - 1u;
+                        }
+                    }
+                    nb += npass;
+                }
+                if (__any_sync(0xffffffffu, nb > kBuf - 16)) {
+                    if (c + 1 < kTN / 16) tmem_ld_wait_regs(vn);  // no TMEM load in flight across the call
+                    const long long f0 = st_on ? clock64() : 0;
+                    n_pass += nb;
+                    ++n_flush;
+                    const ListTail lt = flush_tmem<kL, kTF32>(tl, my_buf, nb, p.m_sel);
+                    nb = 0;
+                    if (row_ok) {
+                        thr = (lt.last == kEmptyKey) ? FLT_MAX : key_dist(lt.last);
+                        if (kTF32 && lt.msel != kEmptyKey) thr = fminf(thr, key_dist(lt.msel) + margin);
+                    }
+                    if (st_on) cyc_flush += clock64() - f0;
+                }
+                __syncwarp();
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(ACC_EMPTY(b));
+        }
+        if (ok && __any_sync(0xffffffffu, nb > 0)) {
+            n_pass += nb;
+            ++n_flush;
+            flush_tmem<kL, kTF32>(tl, my_buf, nb, p.m_sel);
+            nb = 0;
+        }
+        if (ok && st_on) {
+            if (row_ok) atomicAdd(&p.stats[0], static_cast<unsigned long long>(n_pass));
+            if (row_ok) atomicAdd(&p.stats[2], 1ull);
+            if (lane == 0) {
+                atomicAdd(&p.stats[1], static_cast<unsigned long long>(n_flush));
+                atomicAdd(&p.stats[3], static_cast<unsigned long long>(cyc_wait));
+                atomicAdd(&p.stats[4], static_cast<unsigned long long>(cyc_flush));
+                atomicAdd(&p.stats[5], static_cast<unsigned long long>(clock64() - cyc0));
+            }
+        }
+        if (ok)  // warp-uniform: the TMEM loads inside are warp-collective
+            list_out<kL, kTF32>(tl, row_ok, arow, anorm, margin, p.m_out, p.m_sel, p.out_ids, p.out_dists, p.cand_cols,
+                                p.cand_n);
     }
 #undef FULL_BAR
 #undef EMPTY_BAR
@@ -666,25 +989,42 @@ __global__ void __launch_bounds__(128) rerank_kernel(const RerankArgs p)
 // host side
 // --------------------------------------------------------------------------
 struct Plan {
-    int stages = 0, L = 0, a_res = 0;
-    uint32_t list_off = 0, buf_off = 0, pn_off = 0, bar_off = 0, total = 0;
+    int stages = 0, L = 0, a_res = 0, variant = 1;
+    uint32_t list_off = 0, buf_off = 0, pn_off = 0, bar_off = 0, scr_off = 0, total = 0;
 };
 
 // Row list length: a power of two (the merge network) and at least the
 // 32-entry buffer; screen lists keep 16+ entries of headroom beyond M for the
-// margin candidates when that fits.
+// margin candidates when that fits.  Lists of up to 64 keys take the two-CTA
+// variant (64-column tiles, lists in TMEM) when its shared memory fits half an
+// SM; otherwise one CTA per SM with 128-column tiles and shared-memory lists.
 bool make_plan(int k_chunks, int m, bool screen, Plan& pl)
 {
     int L = 32;
     while (L < (screen ? m + 16 : m)) L <<= 1;
     struct Cfg { int a_res, S; };
-    const Cfg cfgs[] = {{1, 4}, {1, 3}, {0, 4}, {0, 3}, {1, 2}, {0, 2}, {1, 1}, {0, 1}};
+    const Cfg cfgs1[] = {{1, 4}, {1, 3}, {0, 4}, {0, 3}, {1, 2}, {0, 2}, {1, 1}, {0, 1}};
+    const Cfg cfgs2[] = {{1, 4}, {1, 3}, {0, 4}, {0, 3}, {1, 2}, {0, 2}};
     for (; L >= 32 && L >= m; L >>= 1) {
-        for (const Cfg& c : cfgs) {
+        if (L <= 64) {
+            for (const Cfg& c : cfgs2) {
+                const uint32_t stage_bytes = (c.a_res ? 0u : kTileBytes) + 64u * 128u;
+                uint32_t off = (c.a_res ? static_cast<uint32_t>(k_chunks) * kTileBytes : 0u) + c.S * stage_bytes;
+                Plan t;
+                t.stages = c.S; t.L = L; t.a_res = c.a_res; t.variant = 2;
+                t.buf_off = off; off += static_cast<uint32_t>(kBuf) * 128u * 8u;
+                t.pn_off = off; off += 4u * 64u * 4u * 2u;   // per epilogue warp: the tile's norms, then ids
+                t.scr_off = off; off += 4u * 32u * 20u * 4u; // per lane: 16 scores (80-byte stride)
+                t.bar_off = off; off += 8u * (2u * c.S + 6u) + 16u;
+                t.total = off;
+                if (t.total <= kSmemMax2) { pl = t; return true; }
+            }
+        }
+        for (const Cfg& c : cfgs1) {
             const uint32_t stage_bytes = c.a_res ? kTileBytes : 2u * kTileBytes;
             uint32_t off = (c.a_res ? static_cast<uint32_t>(k_chunks) * kTileBytes : 0u) + c.S * stage_bytes;
             Plan t;
-            t.stages = c.S; t.L = L; t.a_res = c.a_res;
+            t.stages = c.S; t.L = L; t.a_res = c.a_res; t.variant = 1;
             t.list_off = off; off += static_cast<uint32_t>(L) * 128u * 8u;
             t.buf_off = off; off += static_cast<uint32_t>(kBuf) * 128u * 8u;
             t.pn_off = off; off += 4u * 128u * 4u * 2u;  // per epilogue warp: column norms, then column ids
@@ -696,26 +1036,37 @@ bool make_plan(int k_chunks, int m, bool screen, Plan& pl)
     return false;
 }
 
-template <bool kTF32, int kL>
+template <bool kTF32, int kL, int kV>
 void launch_dist_topk(const CUtensorMap& tmA, const CUtensorMap& tmB, const DistTopkArgs& a, int n_work,
                       uint32_t smem, cudaStream_t st)
 {
-    GTA_CUDA(cudaFuncSetAttribute(dist_topk_kernel<kTF32, kL>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    dist_topk_kernel<kTF32, kL><<<n_work, kThreads, smem, st>>>(tmA, tmB, a);
+    auto fn = dist_topk_kernel<kTF32, kL, kV>;
+    GTA_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    GTA_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    fn<<<n_work, kThreads, smem, st>>>(tmA, tmB, a);
     count_launches(1);
     GTA_CUDA(cudaGetLastError());
 }
 
 template <bool kTF32>
-void launch_dist_topk_L(int L, const CUtensorMap& tmA, const CUtensorMap& tmB, const DistTopkArgs& a, int n_work,
-                        uint32_t smem, cudaStream_t st)
+void launch_dist_topk_L(int L, int variant, const CUtensorMap& tmA, const CUtensorMap& tmB, const DistTopkArgs& a,
+                        int n_work, uint32_t smem, cudaStream_t st)
 {
-    switch (L) {
-        case 32: launch_dist_topk<kTF32, 32>(tmA, tmB, a, n_work, smem, st); break;
-        case 64: launch_dist_topk<kTF32, 64>(tmA, tmB, a, n_work, smem, st); break;
-        case 128: launch_dist_topk<kTF32, 128>(tmA, tmB, a, n_work, smem, st); break;
-        default: throw Error(kInvalid, "dist_topk: unsupported list length");
+    if (variant == 2) {
+        switch (L) {
+            case 32: launch_dist_topk<kTF32, 32, 2>(tmA, tmB, a, n_work, smem, st); return;
+            case 64: launch_dist_topk<kTF32, 64, 2>(tmA, tmB, a, n_work, smem, st); return;
+            default: break;
+        }
+    } else {
+        switch (L) {
+            case 32: launch_dist_topk<kTF32, 32, 1>(tmA, tmB, a, n_work, smem, st); return;
+            case 64: launch_dist_topk<kTF32, 64, 1>(tmA, tmB, a, n_work, smem, st); return;
+            case 128: launch_dist_topk<kTF32, 128, 1>(tmA, tmB, a, n_work, smem, st); return;
+            default: break;
+        }
     }
+    throw Error(kInvalid, "dist_topk: unsupported list length");
 }
 
 using EncodeFn = PFN_cuTensorMapEncodeTiled_v12000;
@@ -735,13 +1086,13 @@ EncodeFn get_encode()
     return fn;
 }
 
-CUtensorMap make_tmap(const void* base, int elem, int64_t rows, int d_pad)
+CUtensorMap make_tmap(const void* base, int elem, int64_t rows, int d_pad, int box_rows = 128)
 {
     CUtensorMap m;
     const int esz = elem == kElemBF16 ? 2 : 4;
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(d_pad), static_cast<cuuint64_t>(rows)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(d_pad) * esz};
-    cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esz), 128u};
+    cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esz), static_cast<cuuint32_t>(box_rows)};
     cuuint32_t estr[2] = {1u, 1u};
     const CUresult r = get_encode()(&m, elem == kElemBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
                                     2, const_cast<void*>(base), dims, strides, box, estr,
@@ -772,7 +1123,7 @@ void dist_topk(const DistTopkProblem& pr, cudaStream_t st)
     GTA_REQUIRE(!screen || pl.L <= kSortMax, kInvalid, "dist_topk: candidate list too long");
 
     const CUtensorMap tmA = make_tmap(pr.A, pr.elem, pr.a_total, pr.d_pad);
-    const CUtensorMap tmB = make_tmap(pr.B, pr.elem, pr.b_total, pr.d_pad);
+    const CUtensorMap tmB = make_tmap(pr.B, pr.elem, pr.b_total, pr.d_pad, pl.variant == 2 ? 64 : 128);
 
     DevBuf<int32_t> cand_cols, cand_n;
     DevBuf<float> bmax;
@@ -796,12 +1147,13 @@ void dist_topk(const DistTopkProblem& pr, cudaStream_t st)
     a.cand_cols = cand_cols.get(); a.cand_n = cand_n.get();
     a.err = pr.err;
     a.list_off = pl.list_off; a.buf_off = pl.buf_off; a.pn_off = pl.pn_off; a.bar_off = pl.bar_off;
+    a.scr_off = pl.scr_off;
 
     {
         ProfScope prof(pr.prof_name, pr.flops, st);
         a.stats = prof.counters(8);
-        if (screen) launch_dist_topk_L<true>(pl.L, tmA, tmB, a, pr.n_work, pl.total, st);
-        else launch_dist_topk_L<false>(pl.L, tmA, tmB, a, pr.n_work, pl.total, st);
+        if (screen) launch_dist_topk_L<true>(pl.L, pl.variant, tmA, tmB, a, pr.n_work, pl.total, st);
+        else launch_dist_topk_L<false>(pl.L, pl.variant, tmA, tmB, a, pr.n_work, pl.total, st);
     }
 
     if (screen) {

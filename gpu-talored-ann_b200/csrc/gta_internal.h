@@ -144,6 +144,21 @@ int64_t reverse_merge_noalloc_max_edges();
 void sort_rows_l2(const float* X, int d, int d_pad, const int32_t* knn, int64_t N, int M, int32_t* out,
                   cudaStream_t st);
 void max_sqrt(const float* v, int64_t n, float* out, cudaStream_t st);
+// shard variants (one rank's part of a multi-GPU build)
+void gather_range(const void* X, int dtype, int d, int64_t row0, int64_t n, const int32_t* ids, int64_t n_ids,
+                  float* out, cudaStream_t st);
+void gather_i32(const int32_t* src, const int32_t* idx, int64_t n, int32_t* out, cudaStream_t st);
+void centroid_partial(const float* Xs, int64_t n_s, int d, int d_pad, const int32_t* assign, int32_t B, double* sums,
+                      long long* counts, cudaStream_t st);
+void centroid_means(const double* sums, const long long* counts, const float* C_in, int32_t B, int d, float* C_out,
+                    cudaStream_t st);
+void group_rows(const int32_t* bucket, const int32_t* other, int64_t n, int32_t B, int32_t* order, int64_t* offsets,
+                cudaStream_t st);
+void sanitize_rows(const int32_t* knn, int64_t n_rows, int64_t row0, int64_t N, int M, uint32_t* out, cudaStream_t st);
+void prune_rows(const uint32_t* g, int64_t N, int M, int K, const int32_t* order, int64_t row0, int64_t n_rows,
+                uint32_t* out, int* err, cudaStream_t st);
+void reverse_merge_rows(const uint32_t* pruned, int64_t N, int K, int64_t row0, int64_t n_rows, uint32_t* out,
+                        cudaStream_t st);
 void check_device_error(const int* err, cudaStream_t st, const char* what);
 
 }  // namespace gta

@@ -93,6 +93,29 @@ void convert_dispatch_out(const Tin* X, int d, const int32_t* ids, int64_t n, vo
         convert_rows_kernel<Tin, float><<<grid, wpb * 32, 0, st>>>(X, d, ids, n, static_cast<float*>(out), d_pad, norms);
 }
 
+// Rows of a shard holding global rows [row0, row0 + n): out[j] = X[ids[j] - row0]
+// as f32 (d columns), a zero row where ids[j] lies outside the shard.
+template <typename Tin>
+__global__ void gather_range_kernel(const Tin* __restrict__ X, int d, int64_t row0, int64_t n,
+                                    const int32_t* __restrict__ ids, int64_t n_ids, float* __restrict__ out)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t j = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (j >= n_ids) return;
+    const int64_t src = static_cast<int64_t>(ids[j]) - row0;
+    const bool in = src >= 0 && src < n;
+    const Tin* x = X + (in ? src : 0) * d;
+    float* o = out + j * d;
+    for (int i = lane; i < d; i += 32) o[i] = in ? ld_f32(x + i) : 0.0f;
+}
+
+__global__ void gather_i32_kernel(const int32_t* __restrict__ src, const int32_t* __restrict__ idx, int64_t n,
+                                  int32_t* __restrict__ out)
+{
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) out[i] = src[idx[i]];
+}
+
 // ---------------------------------------------------------------- sampling
 __global__ void sample_ids_kernel(int64_t N, int64_t n_s, uint64_t seed, int32_t* out)
 {
@@ -216,6 +239,150 @@ __global__ void __launch_bounds__(kKppThreads) kpp_step_kernel(const float* __re
     for (int k = tid; k < d_pad; k += blockDim.x) C[static_cast<int64_t>(t + 1) * d_pad + k] = pool[pick * d_pad + k];
 }
 
+// The whole D^2 sampling in one cooperative launch: one thread per pool point,
+// every CTA co-resident, a bounded grid barrier per centroid instead of a
+// kernel launch.  Step t folds centroid t into each point's min distance
+// (kept in a register), each CTA writes the fp64 inclusive prefix of its
+// points' weights and its total, and after the barrier every CTA draws the
+// same centroid t+1: the CTA whose cumulative total first exceeds u * total,
+// then the point whose prefix first exceeds the remainder.  Sums are fixed-order
+// scans, so the picks are reproducible run to run and on every GPU.
+constexpr int kKppCoopThreads = 256;
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p)
+{
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid barrier of a cooperative launch; gives up after the wait budget and
+// raises the abort flag that every CTA polls.  Returns false on abort.
+__device__ bool coop_barrier(unsigned* arrive, unsigned target, int* abort_flag, int* err, int* s_ok)
+{
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence();
+        atomicAdd(arrive, 1u);
+        const long long t0 = clock64();
+        int ok = 1;
+        while (ld_acquire_u32(arrive) < target) {
+            if (*reinterpret_cast<volatile int*>(abort_flag)) { ok = 0; break; }
+            if (clock64() - t0 > kWaitBudgetCycles) {
+                atomicExch(abort_flag, 1);
+                if (err) atomicCAS(err, 0, kDevTimeoutGrid);
+                ok = 0;
+                break;
+            }
+            __nanosleep(32);
+        }
+        __threadfence();
+        *s_ok = ok;
+    }
+    __syncthreads();
+    return *s_ok != 0;
+}
+
+// Inclusive fp64 prefix sum over the CTA's threads (fixed order).
+__device__ __forceinline__ double block_incl_scan(double v, double* s_warp)
+{
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const double u = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += u;
+    }
+    if (lane == 31) s_warp[w] = v;
+    __syncthreads();
+    if (w == 0) {
+        double t = lane < (kKppCoopThreads / 32) ? s_warp[lane] : 0.0;
+#pragma unroll
+        for (int o = 1; o < kKppCoopThreads / 32; o <<= 1) {
+            const double u = __shfl_up_sync(0xffffffffu, t, o);
+            if (lane >= o) t += u;
+        }
+        if (lane < kKppCoopThreads / 32) s_warp[lane] = t;
+    }
+    __syncthreads();
+    const double off = w > 0 ? s_warp[w - 1] : 0.0;
+    __syncthreads();
+    return v + off;
+}
+
+__global__ void __launch_bounds__(kKppCoopThreads)
+    kpp_coop_kernel(const float* __restrict__ pool, int64_t pool_n, int d, int d_pad, float* __restrict__ C, int B,
+                    uint64_t seed, double* __restrict__ gpre, double* __restrict__ gtot, unsigned* arrive,
+                    int* abort_flag, int* err)
+{
+    extern __shared__ float cen[];
+    __shared__ double s_warp[kKppCoopThreads / 32];
+    __shared__ int64_t s_pick;
+    __shared__ int s_blk, s_ok;
+    __shared__ double s_resid;
+    const int tid = threadIdx.x;
+    const int G = gridDim.x;
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * kKppCoopThreads + tid;
+    const bool valid = i < pool_n;
+    float md = INFINITY;
+    if (tid == 0) {
+        const int64_t f = static_cast<int64_t>(uniform01(seed, 0) * static_cast<double>(pool_n));
+        s_pick = f < pool_n ? f : pool_n - 1;
+    }
+    for (int t = 0; t < B; ++t) {
+        __syncthreads();
+        const int64_t pick = s_pick;
+        for (int k = tid; k < d; k += kKppCoopThreads) cen[k] = pool[pick * d_pad + k];
+        if (blockIdx.x == 0)
+            for (int k = tid; k < d_pad; k += kKppCoopThreads)
+                C[static_cast<int64_t>(t) * d_pad + k] = pool[pick * d_pad + k];
+        __syncthreads();
+        if (t + 1 >= B) break;
+        if (valid) md = fminf(md, exact_l2_f(pool + i * d_pad, cen, d));
+        const double incl = block_incl_scan(valid ? static_cast<double>(md) : 0.0, s_warp);
+        const int par = t & 1;
+        gpre[static_cast<int64_t>(par) * G * kKppCoopThreads + static_cast<int64_t>(blockIdx.x) * kKppCoopThreads + tid] = incl;
+        if (tid == kKppCoopThreads - 1) gtot[par * G + blockIdx.x] = incl;
+        if (!coop_barrier(arrive, static_cast<unsigned>(t + 1) * static_cast<unsigned>(G), abort_flag, err, &s_ok)) return;
+        // the draw, identical in every CTA: first the CTA, then the point inside it
+        const double u = uniform01(seed, static_cast<uint64_t>(t) + 1);
+        const double tot_b = tid < G ? __ldcg(gtot + par * G + tid) : 0.0;
+        const double cum_b = block_incl_scan(tot_b, s_warp);
+        if (tid == kKppCoopThreads - 1) {
+            s_resid = cum_b;  // the grand total (threads past G add zeros)
+            s_blk = -1;
+        }
+        __syncthreads();
+        const double total = s_resid;
+        const double target = u * total;
+        __syncthreads();
+        if (total > 0.0 && tid < G && cum_b > target && (tid == 0 || cum_b - tot_b <= target)) {
+            s_blk = tid;
+            s_resid = target - (cum_b - tot_b);
+        }
+        if (tid == 0 && !(total > 0.0)) s_pick = min(pool_n - 1, static_cast<int64_t>(u * static_cast<double>(pool_n)));
+        __syncthreads();
+        const int blk = s_blk;
+        if (total > 0.0) {
+            if (blk < 0) {
+                // rounding left the target past every cumulative total: the last CTA
+                if (tid == 0) { s_blk = G - 1; s_resid = 0.0; }
+                __syncthreads();
+            }
+            const int b = s_blk;
+            const double resid = s_resid;
+            const int64_t j = static_cast<int64_t>(b) * kKppCoopThreads + tid;
+            const int64_t rem = pool_n - static_cast<int64_t>(b) * kKppCoopThreads;
+            const int cnt = static_cast<int>(rem < kKppCoopThreads ? rem : kKppCoopThreads);
+            const double pre = tid < cnt ? __ldcg(gpre + static_cast<int64_t>(par) * G * kKppCoopThreads + j) : 0.0;
+            const double prev = (tid > 0 && tid < cnt) ? __ldcg(gpre + static_cast<int64_t>(par) * G * kKppCoopThreads + j - 1)
+                                                       : 0.0;
+            if (tid == 0) s_pick = static_cast<int64_t>(b) * kKppCoopThreads + cnt - 1;  // fallback: the CTA's last point
+            __syncthreads();
+            if (tid < cnt && pre > resid && (tid == 0 || prev <= resid)) s_pick = j;
+        }
+    }
+}
+
 // ---------------------------------------------------------------- Lloyd update
 __global__ void seg_offsets_kernel(const int32_t* __restrict__ keys_sorted, int64_t n, int32_t B,
                                    int64_t* __restrict__ offsets)
@@ -246,6 +413,30 @@ __global__ void centroid_sum_kernel(const float* __restrict__ Xs, int d, int d_p
         for (int64_t j = lo; j < hi; ++j) s += static_cast<double>(Xs[static_cast<int64_t>(order[j]) * d_pad + k]);
         C_out[o] = static_cast<float>(s / static_cast<double>(cnt));
     }
+}
+
+// Per-centroid fp64 sums (members in sorted order) and counts of a shard.
+__global__ void centroid_partial_kernel(const float* __restrict__ Xs, int d, int d_pad,
+                                        const int32_t* __restrict__ order, const int64_t* __restrict__ offsets,
+                                        double* __restrict__ sums, long long* __restrict__ counts)
+{
+    const int b = blockIdx.x;
+    const int64_t lo = offsets[b], hi = offsets[b + 1];
+    if (threadIdx.x == 0) counts[b] = hi - lo;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        double s = 0.0;
+        for (int64_t j = lo; j < hi; ++j) s += static_cast<double>(Xs[static_cast<int64_t>(order[j]) * d_pad + k]);
+        sums[static_cast<int64_t>(b) * d + k] = s;
+    }
+}
+
+__global__ void centroid_means_kernel(const double* __restrict__ sums, const long long* __restrict__ counts,
+                                      const float* __restrict__ C_in, int32_t B, int d, float* __restrict__ C_out)
+{
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<int64_t>(B) * d) return;
+    const long long c = counts[i / d];
+    C_out[i] = c > 0 ? static_cast<float>(sums[i] / static_cast<double>(c)) : C_in[i];
 }
 
 __global__ void iota_kernel(int32_t* out, int64_t n)
@@ -364,12 +555,15 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
 }
 
 // ---------------------------------------------------------------- sanitize
-__global__ void sanitize_kernel(const int32_t* __restrict__ knn, int64_t N, int M, uint32_t* __restrict__ out)
+// Rows [row0, row0 + n_rows) of an N-point graph (global ids), one warp per row.
+__global__ void sanitize_kernel(const int32_t* __restrict__ knn, int64_t n_rows, int64_t row0, int64_t N, int M,
+                                uint32_t* __restrict__ out)
 {
     const int lane = threadIdx.x & 31;
-    const int64_t i = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    if (i >= N) return;
-    const int32_t* row = knn + i * M;
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (r >= n_rows) return;
+    const int64_t i = row0 + r;
+    const int32_t* row = knn + r * M;
     uint32_t fallback = static_cast<uint32_t>((i + 1) % N);
     for (int g = 0; g < M; g += 32) {
         const int j = g + lane;
@@ -381,7 +575,7 @@ __global__ void sanitize_kernel(const int32_t* __restrict__ knn, int64_t N, int 
     for (int j = lane; j < M; j += 32) {
         const int32_t v = row[j];
         const bool ok = v >= 0 && static_cast<int64_t>(v) < N && static_cast<int64_t>(v) != i;
-        out[i * M + j] = ok ? static_cast<uint32_t>(v) : fallback;
+        out[r * M + j] = ok ? static_cast<uint32_t>(v) : fallback;
     }
 }
 
@@ -402,7 +596,7 @@ __device__ __forceinline__ uint32_t hash_id(uint32_t id, uint32_t mask) { return
 
 __global__ void __launch_bounds__(kPruneWarps * 32)
     prune_kernel(const uint32_t* __restrict__ g, int64_t N, int M, int K, const int32_t* __restrict__ order,
-                 uint32_t* __restrict__ out, int* err)
+                 int64_t row0, int64_t n_rows, uint32_t* __restrict__ out, int* err)
 {
     __shared__ uint32_t s_hkey[kPruneWarps][kPruneHash];
     __shared__ uint8_t s_hrank[kPruneWarps][kPruneHash];
@@ -410,8 +604,10 @@ __global__ void __launch_bounds__(kPruneWarps * 32)
     __shared__ uint32_t s_cnt[kPruneWarps][kMaxM];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int64_t gw = static_cast<int64_t>(blockIdx.x) * kPruneWarps + w;
-    if (gw >= N) return;
-    const int64_t a = order ? static_cast<int64_t>(order[gw]) : gw;
+    if (gw >= n_rows) return;
+    // rows row0 .. row0 + n_rows - 1 of the graph, visited in `order` (local indices)
+    const int64_t orow = order ? static_cast<int64_t>(order[gw]) : gw;
+    const int64_t a = row0 + orow;
     uint32_t cap = 64;
     while (cap < 8u * static_cast<uint32_t>(M)) cap <<= 1;
     const uint32_t mask = cap - 1;
@@ -489,8 +685,18 @@ __global__ void __launch_bounds__(kPruneWarps * 32)
             const uint32_t c2 = s_cnt[w][k2];
             pos += (c2 < c) || (c2 == c && k2 < k);
         }
-        if (pos < K) out[a * K + pos] = s_row[w][k];
+        if (pos < K) out[orow * K + pos] = s_row[w][k];
     }
+}
+
+// Received memberships grouped by (bucket, other bucket), stable in arrival order.
+__global__ void group_keys_kernel(const int32_t* __restrict__ bucket, const int32_t* __restrict__ other, int64_t n,
+                                  int32_t B, uint32_t* __restrict__ keys, int32_t* __restrict__ vals)
+{
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    keys[i] = static_cast<uint32_t>(bucket[i]) * static_cast<uint32_t>(B) + static_cast<uint32_t>(other[i]);
+    vals[i] = static_cast<int32_t>(i);
 }
 
 // Rows grouped by (nearest bucket, second bucket): the processing order that
@@ -505,25 +711,27 @@ __global__ void locality_keys_kernel(const int32_t* __restrict__ top2, int64_t N
 }
 
 // ---------------------------------------------------------------- reverse edges
-__global__ void rev_count_kernel(const uint32_t* __restrict__ pruned, int64_t NK, int64_t N,
+// Edges of the whole pruned graph (N x K, global ids); only destinations in
+// [lo, hi) are kept, at local index dst - lo.
+__global__ void rev_count_kernel(const uint32_t* __restrict__ pruned, int64_t NK, int64_t lo, int64_t hi,
                                  unsigned long long* __restrict__ indeg)
 {
     const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (e >= NK) return;
-    const uint32_t dst = pruned[e];
-    if (static_cast<int64_t>(dst) < N) atomicAdd(&indeg[dst], 1ull);
+    const int64_t dst = pruned[e];
+    if (dst >= lo && dst < hi) atomicAdd(&indeg[dst - lo], 1ull);
 }
 
-__global__ void rev_scatter_kernel(const uint32_t* __restrict__ pruned, int64_t N, int K,
+__global__ void rev_scatter_kernel(const uint32_t* __restrict__ pruned, int64_t N, int K, int64_t lo, int64_t hi,
                                    const uint64_t* __restrict__ off, uint32_t* __restrict__ cursor,
                                    uint64_t* __restrict__ keys)
 {
     const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (e >= N * K) return;
-    const uint32_t dst = pruned[e];
-    if (static_cast<int64_t>(dst) >= N) return;
+    const int64_t dst = pruned[e];
+    if (dst < lo || dst >= hi) return;
     const uint64_t src = static_cast<uint64_t>(e / K), rank = static_cast<uint64_t>(e % K);
-    const uint64_t pos = off[dst] + atomicAdd(&cursor[dst], 1u);
+    const uint64_t pos = off[dst - lo] + atomicAdd(&cursor[dst - lo], 1u);
     keys[pos] = (rank << 32) | src;
 }
 
@@ -531,8 +739,8 @@ constexpr int kRevWarps = 4;
 constexpr int kRevSort = 512;
 
 __global__ void __launch_bounds__(kRevWarps * 32)
-    rev_merge_kernel(const uint32_t* __restrict__ pruned, int64_t N, int K, const uint64_t* __restrict__ off,
-                     const uint64_t* __restrict__ keys, uint32_t* __restrict__ out)
+    rev_merge_kernel(const uint32_t* __restrict__ pruned, int64_t row0, int64_t N, int K,
+                     const uint64_t* __restrict__ off, const uint64_t* __restrict__ keys, uint32_t* __restrict__ out)
 {
     __shared__ uint64_t s_keys[kRevWarps][kRevSort];
     __shared__ uint32_t s_row[kRevWarps][kMaxM];
@@ -581,7 +789,7 @@ __global__ void __launch_bounds__(kRevWarps * 32)
         n_keep = K;
     }
     // protected merge of the reverse sources, weakest first
-    for (int k = lane; k < K; k += 32) s_row[w][k] = pruned[j * K + k];
+    for (int k = lane; k < K; k += 32) s_row[w][k] = pruned[(row0 + j) * K + k];
     __syncwarp();
     const int np = K / 2;
     for (int t = n_keep - 1; t >= 0; --t) {
@@ -691,9 +899,34 @@ void sample_ids(int64_t N, int64_t n_s, uint64_t seed, int32_t* out, cudaStream_
 }
 
 void kmeanspp_init(const float* pool, const float* /*pool_norm*/, int64_t pool_n, int d, int d_pad, int32_t B,
-                   uint64_t seed, float* C, int* /*err*/, cudaStream_t st)
+                   uint64_t seed, float* C, int* err, cudaStream_t st)
 {
     GTA_REQUIRE(pool_n >= 1 && B >= 1, kInvalid, "kmeans++: empty pool");
+    {
+        // one cooperative launch when every CTA fits on the device at once
+        const int G = static_cast<int>((pool_n + kKppCoopThreads - 1) / kKppCoopThreads);
+        const size_t smem1 = sizeof(float) * static_cast<size_t>(d);
+        int dev = 0, n_sm = 0, per_sm = 0, coop = 0;
+        GTA_CUDA(cudaGetDevice(&dev));
+        GTA_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+        GTA_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
+        GTA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kpp_coop_kernel, kKppCoopThreads, smem1));
+        if (coop && smem1 <= 48 * 1024 && G <= per_sm * n_sm && G <= kKppCoopThreads) {
+            DevBuf<double> gpre(static_cast<size_t>(2) * G * kKppCoopThreads, st), gtot(static_cast<size_t>(2) * G, st);
+            DevBuf<unsigned> arrive(2, st);
+            GTA_CUDA(cudaMemsetAsync(arrive.get(), 0, 2 * sizeof(unsigned), st));
+            GTA_CUDA(cudaMemsetAsync(C, 0, sizeof(float) * static_cast<size_t>(B) * d_pad, st));
+            unsigned* arr = arrive.get();
+            int* abort_flag = reinterpret_cast<int*>(arrive.get() + 1);
+            double* gp = gpre.get();
+            double* gt = gtot.get();
+            void* args[] = {const_cast<float**>(&pool), &pool_n, &d, &d_pad, &C, &B, &seed, &gp, &gt, &arr, &abort_flag, &err};
+            GTA_CUDA(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kpp_coop_kernel), dim3(G),
+                                                 dim3(kKppCoopThreads), args, smem1, st));
+            count_launches(1);
+            return;
+        }
+    }
     const int64_t chunk = std::max<int64_t>(256, (pool_n + 295) / 296);
     const unsigned grid = static_cast<unsigned>((pool_n + chunk - 1) / chunk);
     DevBuf<float> min_d2(static_cast<size_t>(pool_n), st);
@@ -787,7 +1020,7 @@ void merge_lists(const int32_t* run_n, const float* run_d, const int32_t* new_n,
 void sanitize(const int32_t* knn, int64_t N, int M, uint32_t* out, cudaStream_t st)
 {
     ProfScope prof("sanitize", 8.0 * M * static_cast<double>(N), st);
-    sanitize_kernel<<<blocks_for(N, 8), 256, 0, st>>>(knn, N, M, out);
+    sanitize_kernel<<<blocks_for(N, 8), 256, 0, st>>>(knn, N, 0, N, M, out);
     count_launches(1);
     GTA_CUDA(cudaGetLastError());
 }
@@ -797,7 +1030,7 @@ void prune_detour(const uint32_t* g, int64_t N, int M, int K, const int32_t* ord
 {
     GTA_REQUIRE(M >= 2 && M <= kMaxM && K >= 1 && K <= M, kInvalid, "prune: need 1 <= K <= M <= 128");
     ProfScope prof("prune", (4.0 * M * (M + 1) + 4.0 * K) * static_cast<double>(N), st);
-    prune_kernel<<<blocks_for(N, kPruneWarps), kPruneWarps * 32, 0, st>>>(g, N, M, K, order, out, err);
+    prune_kernel<<<blocks_for(N, kPruneWarps), kPruneWarps * 32, 0, st>>>(g, N, M, K, order, 0, N, out, err);
     count_launches(1);
     GTA_CUDA(cudaGetLastError());
 }
@@ -830,15 +1063,15 @@ void reverse_merge(const uint32_t* pruned, int64_t N, int K, uint32_t* out, int*
     DevBuf<uint64_t> off(static_cast<size_t>(N) + 1, st), keys(static_cast<size_t>(NK), st);
     GTA_CUDA(cudaMemsetAsync(indeg.get(), 0, sizeof(unsigned long long) * (N + 1), st));
     GTA_CUDA(cudaMemsetAsync(cursor.get(), 0, sizeof(uint32_t) * N, st));
-    rev_count_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, NK, N, indeg.get());
+    rev_count_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, NK, 0, N, indeg.get());
     count_launches(1);
     size_t tmp = 0;
     GTA_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tmp, indeg.get(), off.get(), static_cast<int>(N + 1), st));
     DevBuf<uint8_t> tbuf(tmp, st);
     GTA_CUDA(cub::DeviceScan::ExclusiveSum(tbuf.get(), tmp, indeg.get(), off.get(), static_cast<int>(N + 1), st));
-    rev_scatter_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, N, K, off.get(), cursor.get(), keys.get());
+    rev_scatter_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, N, K, 0, N, off.get(), cursor.get(), keys.get());
     count_launches(1);
-    rev_merge_kernel<<<blocks_for(N, kRevWarps), kRevWarps * 32, 0, st>>>(pruned, N, K, off.get(), keys.get(), out);
+    rev_merge_kernel<<<blocks_for(N, kRevWarps), kRevWarps * 32, 0, st>>>(pruned, 0, N, K, off.get(), keys.get(), out);
     count_launches(1);
     GTA_CUDA(cudaGetLastError());
 }
@@ -906,12 +1139,134 @@ void reverse_merge_noalloc(const uint32_t* pruned, int64_t N, int K, uint32_t* o
     // the array keeps the previous call's contents: counters start from zero
     GTA_CUDA(cudaMemsetAsync(indeg, 0, sizeof(unsigned long long) * (N + 1), st));
     GTA_CUDA(cudaMemsetAsync(cursor, 0, sizeof(uint32_t) * N, st));
-    rev_count_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, NK, N, indeg);
+    rev_count_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, NK, 0, N, indeg);
     count_launches(1);
     GTA_CUDA(cub::DeviceScan::ExclusiveSum(scan_tmp, tmp, indeg, off, static_cast<int>(N + 1), st));
-    rev_scatter_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, N, K, off, cursor, keys);
+    rev_scatter_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, N, K, 0, N, off, cursor, keys);
     count_launches(1);
-    rev_merge_kernel<<<blocks_for(N, kRevWarps), kRevWarps * 32, 0, st>>>(pruned, N, K, off, keys, out);
+    rev_merge_kernel<<<blocks_for(N, kRevWarps), kRevWarps * 32, 0, st>>>(pruned, 0, N, K, off, keys, out);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+// ============================================================================ shard variants
+void gather_range(const void* X, int dtype, int d, int64_t row0, int64_t n, const int32_t* ids, int64_t n_ids,
+                  float* out, cudaStream_t st)
+{
+    if (n_ids == 0) return;
+    const unsigned grid = static_cast<unsigned>((n_ids + 7) / 8);
+    switch (dtype) {
+        case 0: gather_range_kernel<<<grid, 256, 0, st>>>(static_cast<const float*>(X), d, row0, n, ids, n_ids, out); break;
+        case 1: gather_range_kernel<<<grid, 256, 0, st>>>(static_cast<const uint8_t*>(X), d, row0, n, ids, n_ids, out); break;
+        case 2: gather_range_kernel<<<grid, 256, 0, st>>>(static_cast<const int8_t*>(X), d, row0, n, ids, n_ids, out); break;
+        default: throw Error(kInvalid, "gather_rows: unknown dtype");
+    }
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void gather_i32(const int32_t* src, const int32_t* idx, int64_t n, int32_t* out, cudaStream_t st)
+{
+    if (n == 0) return;
+    gather_i32_kernel<<<blocks_for(n, 256), 256, 0, st>>>(src, idx, n, out);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+
+void centroid_partial(const float* Xs, int64_t n_s, int d, int d_pad, const int32_t* assign, int32_t B, double* sums,
+                      long long* counts, cudaStream_t st)
+{
+    DevBuf<int32_t> keys_out(n_s, st), idx_in(n_s, st), idx_out(n_s, st);
+    DevBuf<int64_t> offsets(static_cast<size_t>(B) + 1, st);
+    iota_kernel<<<blocks_for(n_s, 256), 256, 0, st>>>(idx_in.get(), n_s);
+    count_launches(1);
+    int end_bit = 1;
+    while ((1ll << end_bit) < B) ++end_bit;
+    size_t tmp = 0;
+    GTA_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tmp, assign, keys_out.get(), idx_in.get(), idx_out.get(),
+                                             static_cast<int>(n_s), 0, end_bit, st));
+    DevBuf<uint8_t> tbuf(tmp, st);
+    GTA_CUDA(cub::DeviceRadixSort::SortPairs(tbuf.get(), tmp, assign, keys_out.get(), idx_in.get(), idx_out.get(),
+                                             static_cast<int>(n_s), 0, end_bit, st));
+    seg_offsets_kernel<<<blocks_for(B + 1, 256), 256, 0, st>>>(keys_out.get(), n_s, B, offsets.get());
+    count_launches(1);
+    centroid_partial_kernel<<<B, 128, 0, st>>>(Xs, d, d_pad, idx_out.get(), offsets.get(), sums, counts);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void centroid_means(const double* sums, const long long* counts, const float* C_in, int32_t B, int d, float* C_out,
+                    cudaStream_t st)
+{
+    centroid_means_kernel<<<blocks_for(static_cast<int64_t>(B) * d, 256), 256, 0, st>>>(sums, counts, C_in, B, d, C_out);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void group_rows(const int32_t* bucket, const int32_t* other, int64_t n, int32_t B, int32_t* order, int64_t* offsets,
+                cudaStream_t st)
+{
+    GTA_REQUIRE(n < (1ll << 31) && static_cast<int64_t>(B) * B < (1ll << 32), kInvalid,
+                "group_rows: too many rows or buckets");
+    DevBuf<uint32_t> keys_in(n, st), keys_out(n, st);
+    DevBuf<int32_t> vals_in(n, st);
+    group_keys_kernel<<<blocks_for(n, 256), 256, 0, st>>>(bucket, other, n, B, keys_in.get(), vals_in.get());
+    count_launches(1);
+    int end_bit = 1;
+    while ((1ll << end_bit) < static_cast<int64_t>(B) * B) ++end_bit;
+    size_t tmp = 0;
+    GTA_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tmp, keys_in.get(), keys_out.get(), vals_in.get(), order,
+                                             static_cast<int>(n), 0, end_bit, st));
+    DevBuf<uint8_t> tbuf(tmp, st);
+    GTA_CUDA(cub::DeviceRadixSort::SortPairs(tbuf.get(), tmp, keys_in.get(), keys_out.get(), vals_in.get(), order,
+                                             static_cast<int>(n), 0, end_bit, st));
+    seg_offsets_scaled_kernel<<<blocks_for(B + 1, 256), 256, 0, st>>>(keys_out.get(), n, B, offsets);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void sanitize_rows(const int32_t* knn, int64_t n_rows, int64_t row0, int64_t N, int M, uint32_t* out, cudaStream_t st)
+{
+    ProfScope prof("sanitize", 8.0 * M * static_cast<double>(n_rows), st);
+    sanitize_kernel<<<blocks_for(n_rows, 8), 256, 0, st>>>(knn, n_rows, row0, N, M, out);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void prune_rows(const uint32_t* g, int64_t N, int M, int K, const int32_t* order, int64_t row0, int64_t n_rows,
+                uint32_t* out, int* err, cudaStream_t st)
+{
+    GTA_REQUIRE(M >= 2 && M <= kMaxM && K >= 1 && K <= M, kInvalid, "prune: need 1 <= K <= M <= 128");
+    GTA_REQUIRE(row0 >= 0 && n_rows >= 0 && row0 + n_rows <= N, kInvalid, "prune: row range outside the graph");
+    ProfScope prof("prune", (4.0 * M * (M + 1) + 4.0 * K) * static_cast<double>(n_rows), st);
+    prune_kernel<<<blocks_for(n_rows, kPruneWarps), kPruneWarps * 32, 0, st>>>(g, N, M, K, order, row0, n_rows, out, err);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void reverse_merge_rows(const uint32_t* pruned, int64_t N, int K, int64_t row0, int64_t n_rows, uint32_t* out,
+                        cudaStream_t st)
+{
+    GTA_REQUIRE(K >= 1 && K <= kMaxM && row0 >= 0 && row0 + n_rows <= N, kInvalid, "reverse: bad row range or K");
+    const int64_t NK = N * K, lo = row0, hi = row0 + n_rows;
+    ProfScope prof("reverse", 32.0 * K * static_cast<double>(n_rows), st);
+    DevBuf<unsigned long long> indeg(static_cast<size_t>(n_rows) + 1, st);
+    DevBuf<uint32_t> cursor(static_cast<size_t>(n_rows), st);
+    // every edge of the graph may point into this range: size the keys for all of them
+    DevBuf<uint64_t> off(static_cast<size_t>(n_rows) + 1, st), keys(static_cast<size_t>(NK), st);
+    GTA_CUDA(cudaMemsetAsync(indeg.get(), 0, sizeof(unsigned long long) * (n_rows + 1), st));
+    GTA_CUDA(cudaMemsetAsync(cursor.get(), 0, sizeof(uint32_t) * n_rows, st));
+    rev_count_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, NK, lo, hi, indeg.get());
+    count_launches(1);
+    size_t tmp = 0;
+    GTA_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tmp, indeg.get(), off.get(), static_cast<int>(n_rows + 1), st));
+    DevBuf<uint8_t> tbuf(tmp, st);
+    GTA_CUDA(cub::DeviceScan::ExclusiveSum(tbuf.get(), tmp, indeg.get(), off.get(), static_cast<int>(n_rows + 1), st));
+    rev_scatter_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, N, K, lo, hi, off.get(), cursor.get(), keys.get());
+    count_launches(1);
+    rev_merge_kernel<<<blocks_for(n_rows, kRevWarps), kRevWarps * 32, 0, st>>>(pruned, lo, n_rows, K, off.get(),
+                                                                                keys.get(), out);
     count_launches(1);
     GTA_CUDA(cudaGetLastError());
 }
@@ -941,8 +1296,8 @@ void check_device_error(const int* err, cudaStream_t st, const char* what)
     if (h != 0) {
         static const char* names[] = {"ok", "TMA tile wait timed out", "pipeline stage wait timed out",
                                       "accumulator wait timed out", "teardown wait timed out", "id out of range",
-                                      "unsupported shape"};
-        const char* n = (h >= 0 && h <= 6) ? names[h] : "unknown device error";
+                                      "unsupported shape", "grid barrier wait timed out"};
+        const char* n = (h >= 0 && h <= 7) ? names[h] : "unknown device error";
         throw Error(h == kDevBadIndex ? kData : kCuda, std::string(what) + ": " + n);
     }
 }

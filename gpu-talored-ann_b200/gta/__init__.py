@@ -24,4 +24,4 @@ from .api import (  # noqa: F401
     write_knn_dists,
     write_npy,
 )
-from .synth import CONFIGS, generate, scaled  # noqa: F401
+from .synth import CONFIGS, generate, generate_shard, scaled  # noqa: F401

@@ -64,6 +64,17 @@ _SIGS = {
     "gta_prune": [_P, _I64, _I32, _I32, _P, _P],
     "gta_reverse_merge": [_P, _I64, _I32, _P, _P],
     "gta_reverse_merge_noalloc": [_P, _I64, _I32, _P, _P],
+    "gta_kmeans_sizes": [_I64, ctypes.POINTER(gta_bucket_params), ctypes.POINTER(_I64), ctypes.POINTER(_I64),
+                         ctypes.POINTER(_U64)],
+    "gta_sample_ids": [_I64, _I64, _U64, _P, _P],
+    "gta_gather_rows": [_P, _I32, _I64, _I32, _I64, _P, _I64, _P, _P],
+    "gta_centroid_sums": [_P, _I64, _I32, _P, _I32, _P, _P, _P],
+    "gta_centroid_means": [_P, _P, _I32, _I32, _P, _P],
+    "gta_group_memberships": [_P, _P, _I64, _I32, _P, _P, _P],
+    "gta_bucket_knn_rows": [_P, _I32, _I64, _I32, _P, _P, _P, _I32, _I32, _P, _P, _P],
+    "gta_sanitize_rows": [_P, _I64, _I64, _I64, _I32, _P, _P],
+    "gta_prune_rows": [_P, _I64, _I32, _I32, _I64, _I64, _P, _I32, _P, _P],
+    "gta_reverse_merge_rows": [_P, _I64, _I32, _I64, _I64, _P, _P],
     "gta_read_dataset_header": [ctypes.c_char_p, ctypes.POINTER(_I64), ctypes.POINTER(_I32), ctypes.POINTER(_I32)],
     "gta_read_dataset": [ctypes.c_char_p, _I64, _I64, _P],
     "gta_write_dataset": [ctypes.c_char_p, _P, _I64, _I32, _I32],

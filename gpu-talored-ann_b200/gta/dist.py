@@ -1,0 +1,340 @@
+"""Multi-GPU bucketed kNN / CAGRA build: one process per GPU, torch.distributed
+(NCCL) for the exchanges, libgta kernels for every computation.
+
+This follows the multi-GPU plan of the reference's build (bucketDemo/buildBucket/src/
+bucket.cu: row-sharded k-means with all-reduced sums, buckets placed on owner GPUs,
+points and lists exchanged, then a merge on the point's owner), with one
+difference of layout: every rank keeps the original row order, so the reference's
+inverse permutation is the identity.
+
+A rank holds global rows [row0, row0 + n_local) of an N-row dataset (rank r's rows
+come before rank r+1's).  The steps and their exchanges:
+
+  1. k-means.  The k-means++ pool is drawn over all N ids (identical on every
+     rank), each rank fills the rows it holds and an all-reduce completes it; the
+     initial centroids are then computed identically everywhere.  Lloyd runs on the
+     rank's part of the global sample: local assignment, local fp64 sums and counts,
+     an all-reduce of both, new means.
+  2. Top-2 buckets of the local rows.
+  3. Bucket placement: global bucket sizes (all-reduce), then longest-processing-
+     time placement on the cost n_b^2, the same on every rank.
+  4. Points to bucket owners (all-to-all of rows and (id, bucket, other) triples),
+     grouped by (bucket, other) in arrival order: the membership order of the
+     single-GPU build.
+  5. Per-bucket all-pairs top-M on the owner.
+  6. Lists back to the points' owners (all-to-all), merged per point.
+  7. CAGRA: sanitize the local rows, all-gather the id table, prune the local rows,
+     all-gather the pruned graph, merge reverse edges into the local rows.
+
+For integer data (u8 / i8) every value the single-GPU build computes is
+reproduced exactly: the centroid sums are sums of integers in fp64, and every
+other stage sees the same inputs in the same order.  For f32 data the centroid
+sums are added in a different order, so centroids may differ in the last bit.
+
+``Stages`` is the per-rank compute interface; ``CudaStages`` binds libgta.  The
+driver itself only sorts, counts and moves data between ranks.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from . import _lib as L
+
+_ELEM = {torch.float32: L.GTA_F32, torch.uint8: L.GTA_U8, torch.int8: L.GTA_I8}
+
+
+@dataclass
+class ShardParams:
+    """Parameters of the build; the same meaning as gta_bucket_params / gta_cagra_params."""
+
+    n_buckets: int
+    knn_degree: int = 64
+    graph_degree: int = 0  # 0: stop after the kNN lists
+    kmeans_iters: int = 10
+    kmeans_sample: int = 0
+    seed: int = 42
+
+
+@dataclass
+class ShardResult:
+    row0: int
+    n_total: int
+    knn_ids: torch.Tensor  # n_local x M int32, global ids
+    knn_dists: torch.Tensor  # n_local x M float32
+    centroids: torch.Tensor  # B x d float32
+    top2: torch.Tensor  # n_local x 2 int32
+    graph: Optional[torch.Tensor] = None  # n_local x K (int32 view of uint32 ids)
+    owner: Optional[list] = None  # bucket -> rank
+    comm_bytes: int = 0  # bytes this rank sent
+
+
+# ---------------------------------------------------------------- libgta stages
+def _p(t: Optional[torch.Tensor]) -> ctypes.c_void_p:
+    if t is None:
+        return ctypes.c_void_p(0)
+    assert t.is_contiguous()
+    return ctypes.c_void_p(t.data_ptr())
+
+
+class CudaStages:
+    """The per-rank computations, each one libgta call on the current CUDA stream."""
+
+    def __init__(self):
+        self.L = L.lib()
+
+    @staticmethod
+    def _st():
+        return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+    def kmeans_sizes(self, n, prm: ShardParams):
+        bp = L.gta_bucket_params(n_buckets=prm.n_buckets, kmeans_iters=prm.kmeans_iters, knn_degree=prm.knn_degree,
+                                 kmeans_sample=prm.kmeans_sample, seed=prm.seed)
+        n_s, pool_n, pseed = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_uint64()
+        L.check(self.L.gta_kmeans_sizes(n, ctypes.byref(bp), ctypes.byref(n_s), ctypes.byref(pool_n),
+                                        ctypes.byref(pseed)))
+        return n_s.value, pool_n.value, pseed.value
+
+    def sample_ids(self, n, n_s, seed, device):
+        out = torch.empty(n_s, dtype=torch.int32, device=device)
+        L.check(self.L.gta_sample_ids(n, n_s, seed, _p(out), self._st()))
+        return out
+
+    def gather_rows(self, X, row0, ids):
+        out = torch.empty((ids.numel(), X.shape[1]), dtype=torch.float32, device=X.device)
+        L.check(self.L.gta_gather_rows(_p(X), _ELEM[X.dtype], X.shape[0], X.shape[1], row0, _p(ids), ids.numel(),
+                                       _p(out), self._st()))
+        return out
+
+    def kmeans_init(self, pool, B, seed):
+        C = torch.empty((B, pool.shape[1]), dtype=torch.float32, device=pool.device)
+        L.check(self.L.gta_kmeans_init(_p(pool), pool.shape[0], pool.shape[1], B, seed, _p(C), self._st()))
+        return C
+
+    def assign_topk(self, Xf, C, k):
+        n = Xf.shape[0]
+        ids = torch.empty((n, k), dtype=torch.int32, device=Xf.device)
+        dd = torch.empty((n, k), dtype=torch.float32, device=Xf.device)
+        if n:
+            L.check(self.L.gta_assign_topk(_p(Xf), n, Xf.shape[1], _p(C), C.shape[0], k, _p(ids), _p(dd), self._st()))
+        return ids
+
+    def centroid_sums(self, Xf, assign, B):
+        d = Xf.shape[1]
+        sums = torch.empty((B, d), dtype=torch.float64, device=Xf.device)
+        counts = torch.empty(B, dtype=torch.int64, device=Xf.device)
+        L.check(self.L.gta_centroid_sums(_p(Xf), Xf.shape[0], d, _p(assign), B, _p(sums), _p(counts), self._st()))
+        return sums, counts
+
+    def centroid_means(self, sums, counts, C):
+        C = C.clone()
+        L.check(self.L.gta_centroid_means(_p(sums), _p(counts), C.shape[0], C.shape[1], _p(C), self._st()))
+        return C
+
+    def group_memberships(self, bucket, other, B):
+        n = bucket.numel()
+        order = torch.empty(n, dtype=torch.int32, device=bucket.device)
+        offsets = torch.empty(B + 1, dtype=torch.int64, device=bucket.device)
+        L.check(self.L.gta_group_memberships(_p(bucket), _p(other), n, B, _p(order), _p(offsets), self._st()))
+        return order, offsets
+
+    def bucket_knn_rows(self, R, order, gid, offsets, M):
+        n = R.shape[0]
+        ids = torch.empty((n, M), dtype=torch.int32, device=R.device)
+        dd = torch.empty((n, M), dtype=torch.float32, device=R.device)
+        L.check(self.L.gta_bucket_knn_rows(_p(R), _ELEM[R.dtype], n, R.shape[1], _p(order), _p(gid), _p(offsets),
+                                           offsets.numel() - 1, M, _p(ids), _p(dd), self._st()))
+        return ids, dd
+
+    def merge_memberships(self, lid, ldist, mem_row):
+        n, M = mem_row.shape[0], lid.shape[1]
+        ids = torch.empty((n, M), dtype=torch.int32, device=lid.device)
+        dd = torch.empty((n, M), dtype=torch.float32, device=lid.device)
+        if n:
+            L.check(self.L.gta_merge_memberships(_p(lid), _p(ldist), _p(mem_row), n, M, _p(ids), _p(dd), self._st()))
+        return ids, dd
+
+    def sanitize_rows(self, knn, row0, n_total):
+        out = torch.empty(knn.shape, dtype=torch.int32, device=knn.device)
+        L.check(self.L.gta_sanitize_rows(_p(knn), knn.shape[0], row0, n_total, knn.shape[1], _p(out), self._st()))
+        return out
+
+    def prune_rows(self, g_full, K, row0, n_rows, top2, B):
+        out = torch.empty((n_rows, K), dtype=torch.int32, device=g_full.device)
+        L.check(self.L.gta_prune_rows(_p(g_full), g_full.shape[0], g_full.shape[1], K, row0, n_rows, _p(top2), B,
+                                      _p(out), self._st()))
+        return out
+
+    def reverse_merge_rows(self, pruned_full, row0, n_rows):
+        K = pruned_full.shape[1]
+        out = torch.empty((n_rows, K), dtype=torch.int32, device=pruned_full.device)
+        L.check(self.L.gta_reverse_merge_rows(_p(pruned_full), pruned_full.shape[0], K, row0, n_rows, _p(out),
+                                              self._st()))
+        return out
+
+
+# ---------------------------------------------------------------- host logic
+def place_buckets(sizes, world: int) -> list:
+    """Longest-processing-time placement of buckets on ranks by cost n_b^2.
+
+    Largest cost first (ties: lower bucket id), each to the least-loaded rank
+    (ties: lower rank).  Deterministic, so every rank computes the same owners.
+    """
+    sizes = [int(s) for s in sizes]
+    order = sorted(range(len(sizes)), key=lambda b: (-sizes[b] * sizes[b], b))
+    load = [0] * world
+    owner = [0] * len(sizes)
+    for b in order:
+        r = min(range(world), key=lambda q: (load[q], q))
+        owner[b] = r
+        load[r] += sizes[b] * sizes[b]
+    return owner
+
+
+def _exchange(send: torch.Tensor, send_counts: torch.Tensor, recv_counts: torch.Tensor, group=None) -> torch.Tensor:
+    """all_to_all_single of row-blocks with per-rank row counts."""
+    row_shape = tuple(send.shape[1:])
+    out = torch.empty((int(recv_counts.sum()),) + row_shape, dtype=send.dtype, device=send.device)
+    dist.all_to_all_single(out, send.contiguous(), recv_counts.tolist(), send_counts.tolist(), group=group)
+    return out
+
+
+def _all_gather_rows(local: torch.Tensor, counts: list, group=None) -> torch.Tensor:
+    """Concatenation of every rank's rows (rank order), for uneven row counts."""
+    world = len(counts)
+    mx = max(counts)
+    if all(c == mx for c in counts):
+        out = torch.empty((mx * world,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+        dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+        return out
+    pad = torch.zeros((mx,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    pad[: local.shape[0]] = local
+    buf = torch.empty((mx * world,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(buf, pad, group=group)
+    return torch.cat([buf[r * mx: r * mx + counts[r]] for r in range(world)])
+
+
+def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_centroids: Optional[torch.Tensor] = None,
+                  group=None) -> ShardResult:
+    """One rank's part of the multi-GPU build.  X_local: this rank's rows (contiguous
+    global row block, rank order), on the rank's device.  Collective: every rank of
+    ``group`` calls it with the same ``prm``."""
+    st = stages if stages is not None else CudaStages()
+    dev = X_local.device
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    n_local, d = X_local.shape
+    B, M = prm.n_buckets, prm.knn_degree
+    sent = 0
+
+    # ---- row ranges
+    cnt = torch.tensor([n_local], dtype=torch.int64, device=dev)
+    counts_t = torch.empty(world, dtype=torch.int64, device=dev)
+    dist.all_gather_into_tensor(counts_t, cnt, group=group)
+    counts = counts_t.tolist()
+    starts = [0] * (world + 1)
+    for r in range(world):
+        starts[r + 1] = starts[r] + counts[r]
+    N, row0 = starts[world], starts[rank]
+    if not (2 <= B <= N):
+        raise L.GtaError(L.GTA_EINVAL, "build_sharded: need 2 <= n_buckets <= N")
+
+    # ---- 1. k-means
+    n_s, pool_n, pool_seed = st.kmeans_sizes(N, prm)
+    if init_centroids is not None:
+        C = init_centroids.to(device=dev, dtype=torch.float32).contiguous()
+    else:
+        pool_ids = st.sample_ids(N, pool_n, pool_seed, dev)
+        pool = st.gather_rows(X_local, row0, pool_ids)
+        dist.all_reduce(pool, group=group)
+        C = st.kmeans_init(pool, B, prm.seed)
+        del pool
+    sid = st.sample_ids(N, n_s, prm.seed, dev)
+    mine = sid[(sid >= row0) & (sid < row0 + n_local)].contiguous()
+    Xs = st.gather_rows(X_local, row0, mine)
+    for _ in range(prm.kmeans_iters):
+        a = st.assign_topk(Xs, C, 1).reshape(-1).contiguous()
+        sums, cts = st.centroid_sums(Xs, a, B)
+        dist.all_reduce(sums, group=group)
+        dist.all_reduce(cts, group=group)
+        C = st.centroid_means(sums, cts, C)
+    del Xs
+
+    # ---- 2. top-2 buckets of the local rows
+    gid_local = torch.arange(row0, row0 + n_local, dtype=torch.int32, device=dev)
+    Xf = st.gather_rows(X_local, row0, gid_local)
+    top2 = st.assign_topk(Xf, C, 2).contiguous()
+    del Xf
+
+    # ---- 3. placement
+    sizes = torch.bincount(top2.reshape(-1).long(), minlength=B).to(torch.int64)
+    dist.all_reduce(sizes, group=group)
+    owner = place_buckets(sizes.tolist(), world)
+    owner_t = torch.tensor(owner, dtype=torch.int64, device=dev)
+
+    # ---- 4. memberships to bucket owners: slot s of point p is membership 2p+s
+    bucket = top2.reshape(-1)
+    other = top2.flip(1).reshape(-1)
+    dest = owner_t[bucket.long()]
+    perm = torch.sort(dest, stable=True).indices
+    send_counts = torch.bincount(dest, minlength=world).to(torch.int64)
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts, send_counts, group=group)
+    p_of = (perm // 2)
+    meta = torch.stack([gid_local[p_of], bucket[perm], other[perm]], dim=1).to(torch.int32)
+    rows = X_local[p_of]
+    elem = rows.element_size()
+    R = _exchange(rows.reshape(rows.shape[0], -1).view(torch.uint8), send_counts, recv_counts, group)
+    R = R.view(X_local.dtype).reshape(-1, d)
+    meta_r = _exchange(meta, send_counts, recv_counts, group)
+    sent += rows.numel() * elem + meta.numel() * 4
+    del rows, meta
+
+    # ---- 5. per-bucket top-M on the owner
+    gid_r = meta_r[:, 0].contiguous()
+    order, offsets = st.group_memberships(meta_r[:, 1].contiguous(), meta_r[:, 2].contiguous(), B)
+    lid, ldist = st.bucket_knn_rows(R, order, gid_r, offsets, M)
+    del R
+
+    # ---- 6. lists back to the points' owners, merged per point
+    og = gid_r[order.long()]
+    ob = meta_r[:, 1][order.long()]
+    starts_t = torch.tensor(starts[1:world], dtype=torch.int64, device=dev)
+    dest2 = torch.bucketize(og.long(), starts_t, right=True)
+    perm2 = torch.sort(dest2, stable=True).indices
+    send2 = torch.bincount(dest2, minlength=world).to(torch.int64)
+    recv2 = torch.empty_like(send2)
+    dist.all_to_all_single(recv2, send2, group=group)
+    meta2 = torch.stack([og[perm2], ob[perm2]], dim=1).to(torch.int32)
+    lid_b = _exchange(lid[perm2], send2, recv2, group)
+    ldist_b = _exchange(ldist[perm2], send2, recv2, group)
+    meta_b = _exchange(meta2, send2, recv2, group)
+    sent += lid.numel() * 8 + meta2.numel() * 4
+    del lid, ldist
+    p = (meta_b[:, 0].long() - row0)
+    lo_bucket = torch.minimum(top2[:, 0], top2[:, 1])
+    slot = (meta_b[:, 1] != lo_bucket[p]).long()
+    mem_row = torch.full((n_local, 2), -1, dtype=torch.int64, device=dev)
+    mem_row[p, slot] = torch.arange(meta_b.shape[0], dtype=torch.int64, device=dev)
+    knn_ids, knn_dists = st.merge_memberships(lid_b.contiguous(), ldist_b.contiguous(), mem_row)
+    del lid_b, ldist_b
+
+    res = ShardResult(row0=row0, n_total=N, knn_ids=knn_ids, knn_dists=knn_dists, centroids=C, top2=top2,
+                      owner=owner)
+    # ---- 7. CAGRA
+    if prm.graph_degree > 0:
+        K = prm.graph_degree
+        g_local = st.sanitize_rows(knn_ids, row0, N)
+        g_full = _all_gather_rows(g_local, counts, group)
+        sent += g_local.numel() * 4 * (world - 1)
+        pruned = st.prune_rows(g_full, K, row0, n_local, top2, B)
+        del g_full
+        p_full = _all_gather_rows(pruned, counts, group)
+        sent += pruned.numel() * 4 * (world - 1)
+        res.graph = st.reverse_merge_rows(p_full, row0, n_local)
+    res.comm_bytes = sent
+    return res

@@ -48,11 +48,14 @@ def scaled(cfg: Config, n: int, n_buckets: int | None = None) -> Config:
                      cfg.kmeans_sample else 0, "n_clusters": max(2, min(cfg.n_clusters, n // 10))})
 
 
-def generate(cfg: Config, seed: int = 42, chunk: int = 1 << 20) -> np.ndarray:
-    rng = np.random.default_rng(seed)
+def _centres(cfg: Config, rng) -> np.ndarray:
     centres = rng.uniform(cfg.centre_lo, cfg.centre_hi, size=(cfg.n_clusters, cfg.d)).astype(np.float32)
     if cfg.transform == "normalize":
         centres /= np.linalg.norm(centres, axis=1, keepdims=True)
+    return centres
+
+
+def _rows(cfg: Config, centres: np.ndarray, rng, chunk: int) -> np.ndarray:
     labels = rng.integers(0, cfg.n_clusters, size=cfg.n)
     out = np.empty((cfg.n, cfg.d), dtype=cfg.dtype)
     for s in range(0, cfg.n, chunk):
@@ -66,3 +69,19 @@ def generate(cfg: Config, seed: int = 42, chunk: int = 1 << 20) -> np.ndarray:
             x = np.clip(np.rint(x), 0, 255)
         out[s:e] = x.astype(cfg.dtype)
     return out
+
+
+def generate(cfg: Config, seed: int = 42, chunk: int = 1 << 20) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    centres = _centres(cfg, rng)
+    return _rows(cfg, centres, rng, chunk)
+
+
+def generate_shard(cfg: Config, shard: int, seed: int = 42, chunk: int = 1 << 20) -> np.ndarray:
+    """cfg.n rows of shard ``shard`` of a multi-shard dataset: the same mixture
+    centres as generate(cfg, seed), each shard with its own label / noise stream.
+    Shard 0 is generate(cfg, seed) itself."""
+    if shard == 0:
+        return generate(cfg, seed, chunk)
+    centres = _centres(cfg, np.random.default_rng(seed))
+    return _rows(cfg, centres, np.random.default_rng([seed, shard]), chunk)

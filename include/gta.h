@@ -189,6 +189,71 @@ int gta_reverse_merge_noalloc(const uint32_t* pruned, int64_t n, int32_t k, uint
 int64_t gta_reverse_merge_noalloc_max_rows(void);
 int64_t gta_reverse_merge_noalloc_max_edges(void);
 
+/* ---------------------------------------------------------------- shard stages
+ * One rank's part of the multi-GPU build (the plan of the reference's
+ * multi-GPU design: row-sharded k-means with all-reduced sums, buckets placed
+ * on owner GPUs, points and lists exchanged all-to-all, the id table gathered
+ * for the prune).  A rank holds global rows [row0, row0 + n_local) of an
+ * N-row dataset; every id below is global.  The collectives between these
+ * calls belong to the caller (torch.distributed / NCCL).  Device pointers,
+ * stream-ordered. */
+
+/* The sizes the build derives from N and its parameters: the k-means sample
+ * (min(0.1, 1e7/N) of N unless p->kmeans_sample is set, at least B), the
+ * k-means++ pool (min(sample, 20 B)) and the seed of the pool's draw. */
+int gta_kmeans_sizes(int64_t n, const gta_bucket_params* p, int64_t* n_sample, int64_t* pool_n, uint64_t* pool_seed);
+
+/* n_s ids drawn from [0, n), one uniformly from each of n_s equal strata
+ * (ascending).  The build's k-means sample and k-means++ pool; stands in for
+ * torch.randperm(N)[:pool_n] (bucketDemo/build_bucket.py:207). */
+int gta_sample_ids(int64_t n, int64_t n_s, uint64_t seed, int32_t* ids, void* stream);
+
+/* out[j] (d f32 values) = row ids[j] - row0 of the shard X (n rows of dtype),
+ * or zeros where ids[j] is outside [row0, row0 + n): summing every rank's
+ * output gives the rows of all ids. */
+int gta_gather_rows(const void* X, int32_t dtype, int64_t n, int32_t d, int64_t row0, const int32_t* ids,
+                    int64_t n_ids, float* out, void* stream);
+
+/* Lloyd partials of a shard: per centroid the fp64 sum of its rows (B x d)
+ * and their count (B).  After an all-reduce (sum) over ranks,
+ * gta_centroid_means turns them into the new centroids in place (a centroid
+ * with no rows keeps its value).  Replaces the scatter_add_ / bincount /
+ * divide of refine_centers_kmeans (bucketDemo/build_bucket.py:252-259). */
+int gta_centroid_sums(const float* X, int64_t n, int32_t d, const int32_t* assign, int32_t B, double* sums,
+                      int64_t* counts, void* stream);
+int gta_centroid_means(const double* sums, const int64_t* counts, int32_t B, int32_t d, float* centroids, void* stream);
+
+/* Received memberships (bucket, other bucket) grouped by (bucket, other),
+ * stable: order[n] lists them in that order, offsets[B+1] per bucket.  When
+ * every rank sends its memberships in row order and they arrive in rank order,
+ * this is the order of gta_build_memberships. */
+int gta_group_memberships(const int32_t* bucket, const int32_t* other, int64_t n, int32_t B, int32_t* order,
+                          int64_t* offsets, void* stream);
+
+/* gta_bucket_knn over rows that were sent to this rank: R holds the n received
+ * rows in arrival order, order/offsets come from gta_group_memberships, gid[n]
+ * is each received row's global id.  List j (of [n x M]) belongs to received
+ * row order[j] and holds global ids. */
+int gta_bucket_knn_rows(const void* R, int32_t dtype, int64_t n, int32_t d, const int32_t* order, const int32_t* gid,
+                        const int64_t* offsets, int32_t B, int32_t M, int32_t* list_ids, float* list_dists,
+                        void* stream);
+
+/* gta_sanitize for rows [row0, row0 + n_rows) of an n-row graph (knn and out
+ * hold only those rows). */
+int gta_sanitize_rows(const int32_t* knn, int64_t n_rows, int64_t row0, int64_t n, int32_t m, uint32_t* out,
+                      void* stream);
+
+/* gta_prune for rows [row0, row0 + n_rows) of the whole n x m graph knn;
+ * pruned holds those rows (n_rows x k).  top2 (n_rows x 2, may be NULL) sets
+ * the processing order only (rows grouped by their buckets for locality). */
+int gta_prune_rows(const uint32_t* knn, int64_t n, int32_t m, int32_t k, int64_t row0, int64_t n_rows,
+                   const int32_t* top2, int32_t B, uint32_t* pruned, void* stream);
+
+/* gta_reverse_merge for destination rows [row0, row0 + n_rows) of the whole
+ * n x k pruned graph; out holds those rows. */
+int gta_reverse_merge_rows(const uint32_t* pruned, int64_t n, int32_t k, int64_t row0, int64_t n_rows, uint32_t* out,
+                           void* stream);
+
 /* ---------------------------------------------------------------- files (host) */
 
 /* BIGANN dataset header (int32 N, int32 D); dtype from the extension

@@ -1,0 +1,144 @@
+"""Helpers for the multi-process tests of the sharded build (gta/dist.py).
+
+``OracleStages`` runs every per-rank computation of the sharded build with the
+CPU oracle (test infrastructure), so the driver's own logic -- row ranges, bucket
+placement, the all-to-all exchanges, the grouping of received memberships, the
+per-point merge rows and the gathers of the id tables -- can be checked on CPU
+ranks (gloo) against the single-process oracle pipeline.  ``gloo_worker`` and
+``nccl_worker`` are the per-rank entry points the tests spawn.
+"""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from oracle import oracle as orc
+
+
+def _np(t):
+    return t.detach().cpu().numpy()
+
+
+def _t(a, dtype=None):
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint32:
+        a = a.view(np.int32)
+    t = torch.from_numpy(a.copy())
+    return t if dtype is None else t.to(dtype)
+
+
+class OracleStages:
+    """The per-rank computations of gta.dist.build_sharded, done by the CPU oracle."""
+
+    def kmeans_sizes(self, n, prm):
+        n_s = min(prm.kmeans_sample, n) if prm.kmeans_sample > 0 else orc.default_sample_size(n)
+        n_s = max(n_s, prm.n_buckets)
+        return n_s, min(n_s, 20 * prm.n_buckets), 0
+
+    def sample_ids(self, n, n_s, seed, device):
+        return _t(orc.kmeans_sample_ids(n, n_s, seed), torch.int32)
+
+    def gather_rows(self, X, row0, ids):
+        x, i = _np(X), _np(ids).astype(np.int64) - row0
+        out = np.zeros((i.shape[0], x.shape[1]), np.float32)
+        ok = (i >= 0) & (i < x.shape[0])
+        out[ok] = x[i[ok]].astype(np.float32)
+        return _t(out)
+
+    def kmeans_init(self, pool, B, seed):
+        raise NotImplementedError("the oracle has no k-means++: pass init_centroids")
+
+    def assign_topk(self, Xf, C, k):
+        if Xf.shape[0] == 0:
+            return torch.empty((0, k), dtype=torch.int32)
+        return _t(orc.topk_assign(_np(Xf), _np(C), k)[0], torch.int32)
+
+    def centroid_sums(self, Xf, assign, B):
+        x, a = _np(Xf).astype(np.float64), _np(assign).astype(np.int64)
+        sums = np.zeros((B, x.shape[1]), np.float64)
+        np.add.at(sums, a, x)
+        return _t(sums), _t(np.bincount(a, minlength=B).astype(np.int64))
+
+    def centroid_means(self, sums, counts, C):
+        s, c, old = _np(sums), _np(counts), _np(C)
+        out = old.copy()
+        ne = c > 0
+        out[ne] = (s[ne] / c[ne, None].astype(np.float64)).astype(np.float32)
+        return _t(out)
+
+    def group_memberships(self, bucket, other, B):
+        b, o = _np(bucket).astype(np.int64), _np(other).astype(np.int64)
+        order = np.argsort(b * B + o, kind="stable")
+        offsets = np.zeros(B + 1, np.int64)
+        offsets[1:] = np.cumsum(np.bincount(b, minlength=B))
+        return _t(order.astype(np.int32)), _t(offsets)
+
+    def bucket_knn_rows(self, R, order, gid, offsets, M):
+        ids, dd = orc.bucket_knn(_np(R), _np(offsets), _np(order), M)
+        g = _np(gid)
+        out = np.where(ids >= 0, g[np.maximum(ids, 0)], -1).astype(np.int32)
+        return _t(out), _t(dd)
+
+    def merge_memberships(self, lid, ldist, mem_row):
+        ids, dd = orc.merge_memberships(_np(lid), _np(ldist), _np(mem_row))
+        return _t(ids), _t(dd)
+
+    def sanitize_rows(self, knn, row0, n_total):
+        k = _np(knn)
+        full = np.full((n_total, k.shape[1]), -1, np.int32)
+        full[row0:row0 + k.shape[0]] = k
+        return _t(orc.sanitize(full)[0][row0:row0 + k.shape[0]])
+
+    def prune_rows(self, g_full, K, row0, n_rows, top2, B):
+        return _t(orc.prune(_np(g_full).view(np.uint32), K)[row0:row0 + n_rows])
+
+    def reverse_merge_rows(self, pruned_full, row0, n_rows):
+        return _t(orc.reverse_merge(_np(pruned_full).view(np.uint32))[row0:row0 + n_rows])
+
+
+def _init(rank, world, port, backend):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    from datetime import timedelta
+
+    dist.init_process_group(backend, rank=rank, world_size=world, timeout=timedelta(seconds=120))
+
+
+def gloo_worker(rank, world, port, X, counts, C0, prm_kw, out_dir):
+    """One CPU rank: build_sharded with OracleStages on its row block; saves its results."""
+    import gta.dist as gd
+
+    _init(rank, world, port, "gloo")
+    try:
+        row0 = int(sum(counts[:rank]))
+        Xl = torch.from_numpy(np.ascontiguousarray(X[row0:row0 + counts[rank]]))
+        prm = gd.ShardParams(**prm_kw)
+        res = gd.build_sharded(Xl, prm, stages=OracleStages(), init_centroids=torch.from_numpy(C0))
+        np.savez(os.path.join(out_dir, f"rank{rank}.npz"), row0=res.row0, ids=_np(res.knn_ids),
+                 dists=_np(res.knn_dists), C=_np(res.centroids), top2=_np(res.top2),
+                 graph=_np(res.graph) if res.graph is not None else np.zeros(0), owner=np.array(res.owner))
+    finally:
+        dist.destroy_process_group()
+
+
+def nccl_worker(rank, world, port, X, prm_kw, out_dir):
+    """One GPU rank: build_sharded with the libgta stages; saves its results."""
+    import gta.dist as gd
+
+    torch.cuda.set_device(rank)
+    _init(rank, world, port, "nccl")
+    try:
+        n = X.shape[0]
+        bounds = [(n * r) // world for r in range(world + 1)]
+        Xl = torch.from_numpy(np.ascontiguousarray(X[bounds[rank]:bounds[rank + 1]])).cuda()
+        prm = gd.ShardParams(**prm_kw)
+        res = gd.build_sharded(Xl, prm)
+        torch.cuda.synchronize()
+        np.savez(os.path.join(out_dir, f"rank{rank}.npz"), row0=res.row0, ids=_np(res.knn_ids),
+                 dists=_np(res.knn_dists), C=_np(res.centroids), top2=_np(res.top2),
+                 graph=_np(res.graph) if res.graph is not None else np.zeros(0))
+    finally:
+        dist.destroy_process_group()

@@ -98,3 +98,26 @@ def test_synthetic_generators_are_seeded():
     np.testing.assert_allclose(np.linalg.norm(c4, axis=1), 1.0, rtol=1e-5)
     c3 = gta.generate(gta.scaled(gta.CONFIGS["c3"], 300), seed=1)
     assert (c3 >= 0).all() and c3.shape[1] == 960
+
+
+def test_shard_generator_shares_centres():
+    cfg = gta.scaled(gta.CONFIGS["c2"], 3000)
+    np.testing.assert_array_equal(gta.generate_shard(cfg, 0, seed=9), gta.generate(cfg, seed=9))
+    s1 = gta.generate_shard(cfg, 1, seed=9)
+    assert s1.shape == (3000, 128) and not np.array_equal(s1, gta.generate(cfg, seed=9))
+    np.testing.assert_array_equal(s1, gta.generate_shard(cfg, 1, seed=9))
+
+
+@pytest.mark.parametrize("n,b,req,n_s,pool", [(1_000_000, 256, 0, 100_000, 5120), (100_000_000, 8192, 0, 10_000_000,
+                                                                                      16384),
+                                              (8_000_000, 2048, 0, 800_000, 20480), (10_000, 16, 10_000, 10_000, 320),
+                                              (5_000, 600, 0, 600, 600)])
+def test_kmeans_sizes(n, b, req, n_s, pool):
+    """Host-only sizing rule shared by the single- and multi-GPU builds."""
+    import ctypes
+
+    bp = L.gta_bucket_params(n_buckets=b, kmeans_sample=req, seed=7)
+    a, c, s = ctypes.c_int64(), ctypes.c_int64(), ctypes.c_uint64()
+    L.check(L.lib().gta_kmeans_sizes(n, ctypes.byref(bp), ctypes.byref(a), ctypes.byref(c), ctypes.byref(s)))
+    assert (a.value, c.value) == (n_s, pool)
+    assert s.value != 7

@@ -1,0 +1,81 @@
+"""The sharded (multi-GPU) build's host logic on CPU ranks (gloo, world 2 and 3).
+
+Every per-rank computation is done by the CPU oracle (tests/dist_helpers.py), so
+these tests check what the driver in gta/dist.py adds: row ranges, bucket
+placement, the all-to-all exchanges of points and lists, the grouping of the
+received memberships, the per-point merge rows and the gathers of the id
+tables.  The concatenated per-rank results must equal the single-process oracle
+pipeline bit for bit (u8 data, so the fp64 centroid sums are exact)."""
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+import torch.multiprocessing as mp  # noqa: E402
+
+from oracle import oracle as orc  # noqa: E402
+import gta.dist as gd  # noqa: E402
+import dist_helpers  # noqa: E402
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _data(n, d, n_centres, seed):
+    rng = np.random.default_rng(seed)
+    centres = rng.uniform(0, 255, (n_centres, d))
+    lab = rng.integers(0, n_centres, n)
+    return np.clip(np.rint(centres[lab] + rng.normal(0, 20, (n, d))), 0, 255).astype(np.uint8)
+
+
+def test_place_buckets_is_deterministic_and_balanced():
+    rng = np.random.default_rng(5)
+    sizes = rng.integers(10, 500, 64).tolist()
+    own = gd.place_buckets(sizes, 4)
+    assert own == gd.place_buckets(sizes, 4)
+    load = np.zeros(4)
+    for b, r in enumerate(own):
+        load[r] += sizes[b] ** 2
+    # LPT: within the largest single item of the ideal share
+    assert load.max() - load.mean() <= max(s * s for s in sizes)
+    assert set(own) == {0, 1, 2, 3}
+    assert gd.place_buckets([5, 5], 1) == [0, 0]
+
+
+@pytest.mark.parametrize("world,counts", [(2, [1300, 1700]), (3, [1000, 1000, 1000])])
+def test_sharded_build_matches_single_pipeline(world, counts):
+    N, d, B, M, K, iters = sum(counts), 16, 8, 16, 8, 3
+    X = _data(N, d, 20, seed=7)
+    rng = np.random.default_rng(1)
+    C0 = X[rng.choice(N, B, replace=False)].astype(np.float32)
+    prm = dict(n_buckets=B, knn_degree=M, graph_degree=K, kmeans_iters=iters, kmeans_sample=0, seed=42)
+
+    # the single-process oracle pipeline on the same sample
+    n_s = max(orc.default_sample_size(N), B)
+    sid = orc.kmeans_sample_ids(N, n_s, 42)
+    ref = orc.build_knn_graph(X, C0, B, M, iters, sample_ids=sid)
+    g_ref = orc.optimize(orc.sanitize(ref["knn_ids"])[0], K)
+
+    with tempfile.TemporaryDirectory() as out:
+        mp.start_processes(dist_helpers.gloo_worker, args=(world, _free_port(), X, counts, C0, prm, out),
+                           nprocs=world, join=True, start_method="spawn")
+        parts = [np.load(f"{out}/rank{r}.npz") for r in range(world)]
+    ids = np.concatenate([p["ids"] for p in parts])
+    dists = np.concatenate([p["dists"] for p in parts])
+    graph = np.concatenate([p["graph"] for p in parts]).view(np.uint32)
+    top2 = np.concatenate([p["top2"] for p in parts])
+    for p in parts:
+        np.testing.assert_array_equal(p["C"], ref["centroids"])
+        np.testing.assert_array_equal(p["owner"], parts[0]["owner"])
+    assert len(set(parts[0]["owner"].tolist())) == world  # every rank owns buckets
+    np.testing.assert_array_equal(top2, ref["top2"])
+    np.testing.assert_array_equal(ids, ref["knn_ids"])
+    np.testing.assert_array_equal(dists, ref["knn_dists"])
+    np.testing.assert_array_equal(graph, g_ref)

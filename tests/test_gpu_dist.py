@@ -1,0 +1,129 @@
+"""The sharded (multi-GPU) build on GPUs: the row-range stage entry points against
+their whole-graph versions, and gta.dist.build_sharded over NCCL ranks against
+the single-GPU build of the same data (u8, so bit-exact: the fp64 centroid sums
+are sums of integers and every other stage sees the same inputs in the same
+order).  The two-rank case needs two GPUs and is skipped on one."""
+import socket
+import tempfile
+
+import numpy as np
+import pytest
+
+torch = pytest.importorskip("torch")
+import torch.multiprocessing as mp  # noqa: E402
+
+import gta  # noqa: E402
+import gta.dist as gd  # noqa: E402
+from gta import _lib as L  # noqa: E402
+import dist_helpers  # noqa: E402
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _data(n, d=64, seed=3):
+    cfg = gta.scaled(gta.CONFIGS["c2"], n)
+    cfg = gta.synth.Config(**{**cfg.__dict__, "d": d})
+    return gta.generate(cfg, seed=seed)
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _st():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def test_row_range_stages_match_whole_graph():
+    X = torch.from_numpy(_data(20000)).cuda()
+    ids, _ = gta.build_bucket(X, 16, 32, 3)
+    N, M, K = ids.shape[0], 32, 16
+    san = gta.sanitize(ids)
+    pruned = gta.prune(san, K)
+    final = gta.reverse_merge(pruned)
+    lib = L.lib()
+    for row0, n_rows in [(0, N), (0, 7000), (7000, 9000), (16000, 4000), (19999, 1)]:
+        s = torch.empty((n_rows, M), dtype=torch.int32, device="cuda")
+        L.check(lib.gta_sanitize_rows(_p(ids[row0:row0 + n_rows]), n_rows, row0, N, M, _p(s), _st()))
+        assert torch.equal(s, san[row0:row0 + n_rows])
+        top2 = torch.randint(0, 16, (n_rows, 2), dtype=torch.int32, device="cuda")
+        top2[:, 1] = (top2[:, 0] + 1) % 16
+        for t2 in (None, top2):
+            pr = torch.empty((n_rows, K), dtype=torch.int32, device="cuda")
+            L.check(lib.gta_prune_rows(_p(san), N, M, K, row0, n_rows, _p(t2), 16, _p(pr), _st()))
+            assert torch.equal(pr, pruned[row0:row0 + n_rows])
+        rv = torch.empty((n_rows, K), dtype=torch.int32, device="cuda")
+        L.check(lib.gta_reverse_merge_rows(_p(pruned), N, K, row0, n_rows, _p(rv), _st()))
+        assert torch.equal(rv, final[row0:row0 + n_rows])
+    bad = torch.empty((10, K), dtype=torch.int32, device="cuda")
+    assert lib.gta_prune_rows(_p(san), N, M, K, N - 5, 10, None, 16, _p(bad), _st()) == L.GTA_EINVAL
+
+
+def test_centroid_partials_and_grouping():
+    rng = np.random.default_rng(0)
+    Xs = torch.from_numpy(rng.integers(0, 256, (5000, 40)).astype(np.float32)).cuda()
+    a = torch.from_numpy(rng.integers(0, 12, 5000).astype(np.int32)).cuda()
+    a[a == 7] = 3  # one empty centroid keeps its value
+    C = torch.from_numpy(rng.normal(size=(12, 40)).astype(np.float32)).cuda()
+    st = gd.CudaStages()
+    sums, cts = st.centroid_sums(Xs, a, 12)
+    ref = torch.zeros((12, 40), dtype=torch.float64, device="cuda").index_add_(0, a.long(), Xs.double())
+    assert torch.equal(sums, ref)
+    assert torch.equal(cts, torch.bincount(a.long(), minlength=12))
+    newC = st.centroid_means(sums, cts, C)
+    exp = (ref / cts.clamp(min=1)[:, None].double()).float()
+    exp[7] = C[7]
+    assert torch.equal(newC, exp)
+    # grouping: stable by (bucket, other)
+    b = torch.from_numpy(rng.integers(0, 9, 3000).astype(np.int32)).cuda()
+    o = torch.from_numpy(rng.integers(0, 9, 3000).astype(np.int32)).cuda()
+    order, offs = st.group_memberships(b, o, 9)
+    key = (b.long() * 9 + o.long()).cpu().numpy()
+    assert np.array_equal(order.cpu().numpy(), np.argsort(key, kind="stable"))
+    assert np.array_equal(offs.cpu().numpy()[1:], np.cumsum(np.bincount(b.cpu().numpy(), minlength=9)))
+    # rows gathered from a shard, zero outside it
+    Xu = torch.from_numpy(rng.integers(0, 256, (100, 8)).astype(np.uint8)).cuda()
+    ids = torch.tensor([1000, 1050, 999, 1099, 1100], dtype=torch.int32, device="cuda")
+    g = st.gather_rows(Xu, 1000, ids)
+    assert torch.equal(g[0], Xu[0].float()) and torch.equal(g[1], Xu[50].float()) and torch.equal(g[3], Xu[99].float())
+    assert not g[2].any() and not g[4].any()
+
+
+def _run_ranks(world, X, prm):
+    with tempfile.TemporaryDirectory() as out:
+        mp.start_processes(dist_helpers.nccl_worker, args=(world, _free_port(), X, prm, out), nprocs=world,
+                           join=True, start_method="spawn")
+        return [dict(np.load(f"{out}/rank{r}.npz")) for r in range(world)]
+
+
+def _check_against_single(world):
+    N, B, M, K = 60000, 16, 32, 16
+    X = _data(N, d=128, seed=11)
+    prm = dict(n_buckets=B, knn_degree=M, graph_degree=K, kmeans_iters=4, kmeans_sample=0, seed=42)
+    parts = _run_ranks(world, X, prm)
+    Xd = torch.from_numpy(X).cuda()
+    ids, dists, C, top2 = gta.build_bucket(Xd, B, M, 4, 0, 42, with_extras=True)
+    graph = gta.build_cagra(Xd, B, M, K, 4, 0, 42)
+    for p in parts:
+        assert np.array_equal(p["C"], C.cpu().numpy())
+    assert np.array_equal(np.concatenate([p["top2"] for p in parts]), top2.cpu().numpy())
+    assert np.array_equal(np.concatenate([p["ids"] for p in parts]), ids.cpu().numpy())
+    assert np.array_equal(np.concatenate([p["dists"] for p in parts]), dists.cpu().numpy())
+    assert np.array_equal(np.concatenate([p["graph"] for p in parts]), graph.cpu().numpy())
+
+
+def test_sharded_one_rank_matches_single_gpu_build():
+    _check_against_single(1)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_sharded_two_ranks_match_single_gpu_build():
+    _check_against_single(2)
