@@ -239,7 +239,7 @@ void kmeans_fit_impl(const float* Xs, const float* xn, int64_t n_s, int d, int d
     DevBuf<float> C2(static_cast<size_t>(B) * d_pad, st);
     for (int it = 0; it < iters; ++it) {
         assign_topk_impl(Xs, xn, n_s, d, d_pad, C, cn, B, 1, ids.get(), dd.get(), err, st);
-        centroid_update(Xs, n_s, d, d_pad, ids.get(), C, B, C2.get(), cn, st);
+        centroid_update(Xs, n_s, d, d_pad, ids.get(), C, B, C2.get(), cn, err, st);
         GTA_CUDA(cudaMemcpyAsync(C, C2.get(), sizeof(float) * static_cast<size_t>(B) * d_pad, cudaMemcpyDeviceToDevice, st));
     }
     if (assign_out) {
@@ -393,7 +393,7 @@ void build_bucket_impl(const gta_dataset& ds, const gta_bucket_params& p, const 
     if (o.top2) GTA_CUDA(cudaMemcpyAsync(o.top2, top2.get(), sizeof(int32_t) * 2 * N, cudaMemcpyDeviceToDevice, st));
     DevBuf<int32_t> members(static_cast<size_t>(N) * 2, st);
     DevBuf<int64_t> offsets(static_cast<size_t>(B) + 1, st), mem_row(static_cast<size_t>(N) * 2, st);
-    build_memberships(top2.get(), N, B, members.get(), offsets.get(), mem_row.get(), st);
+    build_memberships(top2.get(), N, B, members.get(), offsets.get(), mem_row.get(), err.get(), st);
     top2.release();
 
     // ---- per-bucket all-pairs kNN, then merge each point's two lists
@@ -723,7 +723,11 @@ int gta_build_memberships(const int32_t* top2, int64_t n, int32_t B, int32_t* me
     return guard([&] {
         GTA_WORKSPACE(stream);
         GTA_REQUIRE(top2 && members && offsets && mem_row && n >= 1 && B >= 2, kInvalid, "gta_build_memberships: bad argument");
-        build_memberships(top2, n, B, members, offsets, mem_row, S(stream));
+        cudaStream_t st = S(stream);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        build_memberships(top2, n, B, members, offsets, mem_row, err.get(), st);
+        check_device_error(err.get(), st, "gta_build_memberships");
     });
 }
 
@@ -863,7 +867,10 @@ int gta_centroid_sums(const float* X, int64_t n, int32_t d, const int32_t* assig
             GTA_CUDA(cudaMemsetAsync(counts, 0, sizeof(int64_t) * static_cast<size_t>(B), st));
             return;
         }
-        centroid_partial(X, n, d, d, assign, B, sums, reinterpret_cast<long long*>(counts), st);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        centroid_partial(X, n, d, d, assign, B, sums, reinterpret_cast<long long*>(counts), err.get(), st);
+        check_device_error(err.get(), st, "gta_centroid_sums");
     });
 }
 

@@ -90,6 +90,36 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
+// Warp-wide bounded wait for the epilogue warps: lane 0 polls with a short
+// nanosleep backoff (32 lanes spinning on one mbarrier would take issue slots
+// and shared-memory cycles from the warps that work), then every lane observes
+// the completed phase once.  Warp-uniform result.
+__device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                               int code)
+{
+    int ok = 1;
+    if ((threadIdx.x & 31) == 0 && !mbar_try_wait(bar, parity)) {
+        const long long t0 = clock64();
+        uint32_t ns = 16;
+        for (;;) {
+            __nanosleep(ns);
+            if (mbar_try_wait(bar, parity)) break;
+            if (ns < 128) ns <<= 1;
+            if (*abort_flag) { ok = 0; break; }
+            if (clock64() - t0 > kWaitBudgetCycles) {
+                *abort_flag = 1;
+                if (err) atomicCAS(err, 0, code);
+                ok = 0;
+                break;
+            }
+        }
+    }
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    // the phase cannot advance again before this warp releases the buffer, so every lane's check succeeds
+    if (ok) ok = mbar_try_wait(bar, parity) ? 1 : 0;
+    return __all_sync(0xffffffffu, ok != 0);
+}
+
 // Same bounded wait with exponential nanosleep backoff, for the single-thread
 // producer / MMA roles: they share issue slots with epilogue warps, so they
 // must not spin hot while the epilogue works.

@@ -98,22 +98,35 @@ __device__ __forceinline__ void cmp_swap(uint64_t& a, uint64_t& b)
     b = hi;
 }
 
-// Bitonic sort of 32 keys held in registers, ascending (static indices only).
-__device__ __forceinline__ void sort32(uint64_t (&k)[kBuf])
+// One bitonic stage of stride S over 32 register keys; the direction of each
+// pair comes from the runtime block size (static indices, compact code).
+template <int S>
+__device__ __forceinline__ void bitonic_stage(uint64_t (&k)[kBuf], int size)
 {
 #pragma unroll
-    for (int size = 2; size <= kBuf; size <<= 1) {
-#pragma unroll
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-#pragma unroll
-            for (int i = 0; i < kBuf; ++i) {
-                const int j = i ^ stride;
-                if (j > i) {
-                    if ((i & size) == 0) cmp_swap(k[i], k[j]);
-                    else cmp_swap(k[j], k[i]);
-                }
-            }
+    for (int i = 0; i < kBuf; ++i) {
+        if ((i & S) == 0) {
+            const bool up = (i & size) == 0;
+            const uint64_t a = k[i], b = k[i + S];
+            const bool sw = (a > b) == up;
+            k[i] = sw ? b : a;
+            k[i + S] = sw ? a : b;
         }
+    }
+}
+
+// Bitonic sort of 32 keys held in registers, ascending.  The block-size loop
+// runs at run time so each stride's stage is emitted once (the flush is the
+// largest code on the epilogue path and competes for the instruction cache).
+__device__ __forceinline__ void sort32(uint64_t (&k)[kBuf])
+{
+#pragma unroll 1
+    for (int size = 2; size <= kBuf; size <<= 1) {
+        if (size > 16) bitonic_stage<16>(k, size);
+        if (size > 8) bitonic_stage<8>(k, size);
+        if (size > 4) bitonic_stage<4>(k, size);
+        if (size > 2) bitonic_stage<2>(k, size);
+        bitonic_stage<1>(k, size);
     }
 }
 
@@ -575,8 +588,7 @@ __global__ void __launch_bounds__(kThreads, kV)
             __syncwarp();
             if (k + 1 < n_ct) prefetch_cols(k + 1);
             const long long w0 = st_on ? clock64() : 0;
-            const bool got = mbar_wait(ACC_FULL(b), use & 1u, abort_flag, p.err, kDevTimeoutAcc);
-            if (!__all_sync(0xffffffffu, got)) { ok = false; break; }  // the warp leaves together
+            if (!mbar_wait_warp(ACC_FULL(b), use & 1u, abort_flag, p.err, kDevTimeoutAcc)) { ok = false; break; }
             if (st_on) cyc_wait += clock64() - w0;
             tc_fence_after();
             const uint32_t tbase = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * kTileN);
@@ -718,7 +730,8 @@ __global__ void __launch_bounds__(kThreads, kV)
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
         const uint32_t tl = lane_base + 2u * static_cast<uint32_t>(kTN);  // after the two accumulators
         uint64_t* my_buf = buf + r;
-        float* scr = reinterpret_cast<float*>(gbase + p.scr_off) + (q * 32 + lane) * 20;
+        // per warp: 4 groups of 32 float4 (scores e4*4 .. e4*4+3 of each lane), bank-conflict free
+        float* scr = reinterpret_cast<float*>(gbase + p.scr_off) + q * 512 + lane * 4;
         {
             uint32_t e[32];
 #pragma unroll
@@ -763,8 +776,7 @@ __global__ void __launch_bounds__(kThreads, kV)
             __syncwarp();
             if (k + 1 < n_ct) prefetch_cols(k + 1);
             const long long w0 = st_on ? clock64() : 0;
-            const bool got = mbar_wait(ACC_FULL(b), use & 1u, abort_flag, p.err, kDevTimeoutAcc);
-            if (!__all_sync(0xffffffffu, got)) { ok = false; break; }  // the warp leaves together
+            if (!mbar_wait_warp(ACC_FULL(b), use & 1u, abort_flag, p.err, kDevTimeoutAcc)) { ok = false; break; }
             if (st_on) cyc_wait += clock64() - w0;
             tc_fence_after();
             const uint32_t tbase = lane_base + static_cast<uint32_t>(b * kTN);
@@ -802,16 +814,16 @@ __global__ void __launch_bounds__(kThreads, kV)
                 const int rounds = __reduce_max_sync(0xffffffffu, static_cast<unsigned>(npass));
                 if (rounds > 0) {
                     // scores to this lane's scratch, then one append per pass of the busiest lane
-                    float4* s4 = reinterpret_cast<float4*>(scr);
 #pragma unroll
                     for (int e4 = 0; e4 < 4; ++e4)
-                        s4[e4] = make_float4(sv[e4 * 4], sv[e4 * 4 + 1], sv[e4 * 4 + 2], sv[e4 * 4 + 3]);
+                        *reinterpret_cast<float4*>(scr + e4 * 128) =
+                            make_float4(sv[e4 * 4], sv[e4 * 4 + 1], sv[e4 * 4 + 2], sv[e4 * 4 + 3]);
                     uint32_t m = mask;
                     for (int i = 0; i < rounds; ++i) {
                         const int e = __ffs(m) - 1;
                         if (e >= 0) {
                             const uint32_t id = kTF32 ? c0 + static_cast<uint32_t>(e) : idw[c * 16 + e];
-                            my_buf[(nb + i) * 128] = (static_cast<uint64_t>(f2key(scr[e])) << 32) | id;
+                            my_buf[(nb + i) * 128] = (static_cast<uint64_t>(f2key(scr[(e >> 2) * 128 + (e & 3)])) << 32) | id;
                             m &= m - 1u;
                         }
                     }
@@ -1014,7 +1026,7 @@ bool make_plan(int k_chunks, int m, bool screen, Plan& pl)
                 t.stages = c.S; t.L = L; t.a_res = c.a_res; t.variant = 2;
                 t.buf_off = off; off += static_cast<uint32_t>(kBuf) * 128u * 8u;
                 t.pn_off = off; off += 4u * 64u * 4u * 2u;   // per epilogue warp: the tile's norms, then ids
-                t.scr_off = off; off += 4u * 32u * 20u * 4u; // per lane: 16 scores (80-byte stride)
+                t.scr_off = off; off += 4u * 32u * 16u * 4u; // per lane: 16 scores
                 t.bar_off = off; off += 8u * (2u * c.S + 6u) + 16u;
                 t.total = off;
                 if (t.total <= kSmemMax2) { pl = t; return true; }

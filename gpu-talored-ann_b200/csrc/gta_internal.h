@@ -126,9 +126,10 @@ void sample_ids(int64_t N, int64_t n_s, uint64_t seed, int32_t* out, cudaStream_
 void kmeanspp_init(const float* pool, const float* pool_norm, int64_t pool_n, int d, int d_pad, int32_t B,
                    uint64_t seed, float* centroids, int* err, cudaStream_t st);
 void centroid_update(const float* Xs, int64_t n_s, int d, int d_pad, const int32_t* assign, const float* C_in,
-                     int32_t B, float* C_out, float* C_norm, cudaStream_t st);
+                     int32_t B, float* C_out, float* C_norm, int* err, cudaStream_t st);
+void check_ids(const int32_t* ids, int64_t n, int32_t hi, int* err, cudaStream_t st);
 void build_memberships(const int32_t* top2, int64_t N, int32_t B, int32_t* members, int64_t* offsets,
-                       int64_t* mem_row, cudaStream_t st);
+                       int64_t* mem_row, int* err, cudaStream_t st);
 void merge_memberships(const int32_t* list_n, const float* list_d, const int64_t* mem_row, int64_t N, int M,
                        int32_t* out_n, float* out_d, cudaStream_t st);
 void merge_lists(const int32_t* run_n, const float* run_d, const int32_t* new_n, const float* new_d, int64_t N,
@@ -149,7 +150,7 @@ void gather_range(const void* X, int dtype, int d, int64_t row0, int64_t n, cons
                   float* out, cudaStream_t st);
 void gather_i32(const int32_t* src, const int32_t* idx, int64_t n, int32_t* out, cudaStream_t st);
 void centroid_partial(const float* Xs, int64_t n_s, int d, int d_pad, const int32_t* assign, int32_t B, double* sums,
-                      long long* counts, cudaStream_t st);
+                      long long* counts, int* err, cudaStream_t st);
 void centroid_means(const double* sums, const long long* counts, const float* C_in, int32_t B, int d, float* C_out,
                     cudaStream_t st);
 void group_rows(const int32_t* bucket, const int32_t* other, int64_t n, int32_t B, int32_t* order, int64_t* offsets,

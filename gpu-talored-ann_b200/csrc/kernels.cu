@@ -449,13 +449,25 @@ __global__ void iota_kernel(int32_t* out, int64_t n)
 // Membership i = (point i/2, way i%2).  Sort key = bucket * B + the point's
 // other bucket: inside a bucket, members that share their second bucket (one
 // boundary region of the Voronoi diagram) become contiguous, in point order.
+// An id outside [0, B), or both ways naming one bucket, is recorded in *err and
+// gets the key past every bucket, so no later kernel indexes with it.
 __global__ void membership_pairs_kernel(const int32_t* __restrict__ top2, int64_t N, int32_t B,
-                                        uint32_t* __restrict__ keys, int32_t* __restrict__ vals)
+                                        uint32_t* __restrict__ keys, int32_t* __restrict__ vals, int* err)
 {
     const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (i >= 2 * N) return;
-    keys[i] = static_cast<uint32_t>(top2[i]) * static_cast<uint32_t>(B) + static_cast<uint32_t>(top2[i ^ 1]);
+    const int32_t a = top2[i], o = top2[i ^ 1];
+    const bool ok = a >= 0 && a < B && o >= 0 && o < B && a != o;
+    if (!ok) atomicCAS(err, 0, kDevBadIndex);
+    keys[i] = ok ? static_cast<uint32_t>(a) * static_cast<uint32_t>(B) + static_cast<uint32_t>(o) : 0xffffffffu;
     vals[i] = static_cast<int32_t>(i >> 1);
+}
+
+// Records in *err any id outside [0, hi).
+__global__ void check_ids_kernel(const int32_t* __restrict__ ids, int64_t n, int32_t hi, int* err)
+{
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n && (ids[i] < 0 || ids[i] >= hi)) atomicCAS(err, 0, kDevBadIndex);
 }
 
 __global__ void seg_offsets_scaled_kernel(const uint32_t* __restrict__ keys_sorted, int64_t n, int32_t B,
@@ -478,9 +490,11 @@ __global__ void mem_rows_kernel(const uint32_t* __restrict__ keys_sorted, const 
 {
     const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
     if (j >= n2) return;
+    const uint32_t bkt = keys_sorted[j] / static_cast<uint32_t>(B);
+    if (bkt >= static_cast<uint32_t>(B)) return;  // an invalid membership (recorded by membership_pairs_kernel)
     const int64_t p = members[j];
     const int32_t lo_b = min(top2[2 * p], top2[2 * p + 1]);
-    const int way = static_cast<int32_t>(keys_sorted[j] / static_cast<uint32_t>(B)) == lo_b ? 0 : 1;
+    const int way = static_cast<int32_t>(bkt) == lo_b ? 0 : 1;
     mem_row[2 * p + way] = j;
 }
 
@@ -497,6 +511,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
                  const float* __restrict__ new_d, const int64_t* __restrict__ mem_row, int64_t N, int M,
                  int32_t* __restrict__ out_n, float* __restrict__ out_d)
 {
+    // mem_row entries outside [0, 2N) (a membership that was never built) read as empty lists
     __shared__ int32_t s_an[kMergeWarps][kMaxM], s_bn[kMergeWarps][kMaxM];
     __shared__ float s_ad[kMergeWarps][kMaxM], s_bd[kMergeWarps][kMaxM];
     __shared__ int s_rank[kMergeWarps][kMaxM];
@@ -505,12 +520,13 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
     if (p >= N) return;
     const int64_t ra = mem_row ? mem_row[2 * p] : p;
     const int64_t rb = mem_row ? mem_row[2 * p + 1] : p;
-    const int32_t* an = run_n + ra * M; const float* ad = run_d + ra * M;
-    const int32_t* bn = new_n + rb * M; const float* bd = new_d + rb * M;
-    int na = M, nb = M;
+    const bool va = !mem_row || (ra >= 0 && ra < 2 * N), vb = !mem_row || (rb >= 0 && rb < 2 * N);
+    const int32_t* an = run_n + (va ? ra : 0) * M; const float* ad = run_d + (va ? ra : 0) * M;
+    const int32_t* bn = new_n + (vb ? rb : 0) * M; const float* bd = new_d + (vb ? rb : 0) * M;
+    int na = va ? M : 0, nb = vb ? M : 0;
     for (int k = lane; k < M; k += 32) {
-        const int32_t x = an[k], y = bn[k];
-        s_an[w][k] = x; s_ad[w][k] = ad[k]; s_bn[w][k] = y; s_bd[w][k] = bd[k];
+        const int32_t x = va ? an[k] : -1, y = vb ? bn[k] : -1;
+        s_an[w][k] = x; s_ad[w][k] = va ? ad[k] : INFINITY; s_bn[w][k] = y; s_bd[w][k] = vb ? bd[k] : INFINITY;
         if (x < 0) na = min(na, k);
         if (y < 0) nb = min(nb, k);
     }
@@ -946,9 +962,18 @@ void kmeanspp_init(const float* pool, const float* /*pool_norm*/, int64_t pool_n
     GTA_CUDA(cudaGetLastError());
 }
 
-void centroid_update(const float* Xs, int64_t n_s, int d, int d_pad, const int32_t* assign, const float* C_in,
-                     int32_t B, float* C_out, float* C_norm, cudaStream_t st)
+void check_ids(const int32_t* ids, int64_t n, int32_t hi, int* err, cudaStream_t st)
 {
+    if (n == 0) return;
+    check_ids_kernel<<<blocks_for(n, 256), 256, 0, st>>>(ids, n, hi, err);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void centroid_update(const float* Xs, int64_t n_s, int d, int d_pad, const int32_t* assign, const float* C_in,
+                     int32_t B, float* C_out, float* C_norm, int* err, cudaStream_t st)
+{
+    check_ids(assign, n_s, B, err, st);
     DevBuf<int32_t> keys_out(n_s, st), idx_in(n_s, st), idx_out(n_s, st);
     DevBuf<int64_t> offsets(static_cast<size_t>(B) + 1, st);
     iota_kernel<<<blocks_for(n_s, 256), 256, 0, st>>>(idx_in.get(), n_s);
@@ -971,7 +996,7 @@ void centroid_update(const float* Xs, int64_t n_s, int d, int d_pad, const int32
 }
 
 void build_memberships(const int32_t* top2, int64_t N, int32_t B, int32_t* members, int64_t* offsets,
-                       int64_t* mem_row, cudaStream_t st)
+                       int64_t* mem_row, int* err, cudaStream_t st)
 {
     const int64_t n2 = 2 * N;
     GTA_REQUIRE(n2 < (1ll << 31), kInvalid, "memberships: more than 2^31 memberships on one device");
@@ -979,7 +1004,7 @@ void build_memberships(const int32_t* top2, int64_t N, int32_t B, int32_t* membe
     DevBuf<uint32_t> keys_in(n2, st), keys_out(n2, st);
     DevBuf<int32_t> vals_in(n2, st);
     ProfScope prof("memberships", 24.0 * static_cast<double>(n2), st);
-    membership_pairs_kernel<<<blocks_for(n2, 256), 256, 0, st>>>(top2, N, B, keys_in.get(), vals_in.get());
+    membership_pairs_kernel<<<blocks_for(n2, 256), 256, 0, st>>>(top2, N, B, keys_in.get(), vals_in.get(), err);
     count_launches(1);
     int end_bit = 1;
     while ((1ll << end_bit) < static_cast<int64_t>(B) * B) ++end_bit;
@@ -991,6 +1016,7 @@ void build_memberships(const int32_t* top2, int64_t N, int32_t B, int32_t* membe
                                              static_cast<int>(n2), 0, end_bit, st));
     seg_offsets_scaled_kernel<<<blocks_for(B + 1, 256), 256, 0, st>>>(keys_out.get(), n2, B, offsets);
     count_launches(1);
+    GTA_CUDA(cudaMemsetAsync(mem_row, 0xff, sizeof(int64_t) * static_cast<size_t>(n2), st));  // -1: not built
     mem_rows_kernel<<<blocks_for(n2, 256), 256, 0, st>>>(keys_out.get(), members, top2, n2, B, mem_row);
     count_launches(1);
     GTA_CUDA(cudaGetLastError());
@@ -1175,8 +1201,9 @@ void gather_i32(const int32_t* src, const int32_t* idx, int64_t n, int32_t* out,
 
 
 void centroid_partial(const float* Xs, int64_t n_s, int d, int d_pad, const int32_t* assign, int32_t B, double* sums,
-                      long long* counts, cudaStream_t st)
+                      long long* counts, int* err, cudaStream_t st)
 {
+    check_ids(assign, n_s, B, err, st);
     DevBuf<int32_t> keys_out(n_s, st), idx_in(n_s, st), idx_out(n_s, st);
     DevBuf<int64_t> offsets(static_cast<size_t>(B) + 1, st);
     iota_kernel<<<blocks_for(n_s, 256), 256, 0, st>>>(idx_in.get(), n_s);

@@ -269,6 +269,8 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
     Xf = st.gather_rows(X_local, row0, gid_local)
     top2 = st.assign_topk(Xf, C, 2).contiguous()
     del Xf
+    if n_local and not bool(((top2 >= 0) & (top2 < B)).all()):
+        raise L.GtaError(L.GTA_EDATA, "build_sharded: a row has no valid bucket (non-finite input?)")
 
     # ---- 3. placement
     sizes = torch.bincount(top2.reshape(-1).long(), minlength=B).to(torch.int64)
