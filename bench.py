@@ -10,9 +10,9 @@ tensor-core distances with fused top-M, merge, sanitize, CAGRA detour prune
 and reverse-edge merge.  The dataset is resident in HBM when timing starts.
 
 Multi-GPU (torchrun): one global build over all ranks (gta/dist.py).  Each rank
-holds N rows of the configured size (rank r: shard r of a seeded dataset with
-shared mixture centres) and the bucket count grows with the rank count, so the
-bucket size and the per-GPU work stay fixed (weak scaling).  k-means sums are
+holds N rows of the configured size (rank r: shard r, a mixture of the configured
+shape with its own centres) and the bucket count grows with the rank count, so the
+per-GPU problem stays the configured one (weak scaling).  k-means sums are
 all-reduced, points go to their buckets' owners and lists come back by
 all-to-all, and the id tables are all-gathered for the prune (NCCL).  The
 job's time is the max over ranks.
@@ -209,7 +209,8 @@ def main():
               "kmeans_sample": cfg.kmeans_sample or None,
               "l2": "inputs and intermediates larger than L2 (no flush needed)",
               "parallelism": (f"{world} ranks, buckets sharded (NCCL all-reduce / all-to-all / all-gather)"
-                              if world > 1 else "1 GPU")}
+                              if world > 1 else "1 GPU"),
+              "shards": "rank r holds shard r: the configured mixture with its own centres (weak scaling)"}
 
     if args.impl == "reference":
         if rank != 0:
@@ -332,6 +333,23 @@ def main():
         elif v["units"] > 0:
             stage_summary[k]["gbs"] = v["units"] / (v["ms"] / 1e3) / 1e9
 
+    # bucket balance (k-means leaves buckets skewed; the bucket stage costs sum n_b^2) and, on
+    # several GPUs, the device time of each phase of one more (untimed) build
+    skew = phases = None
+    if world == 1:
+        _, _, _, t2 = gta.build_bucket(Xd, cfg.n_buckets, cfg.knn_degree, cfg.kmeans_iters, cfg.kmeans_sample, 42,
+                                       with_extras=True)
+        sizes = torch.bincount(t2.reshape(-1).long(), minlength=cfg.n_buckets).double()
+    else:
+        res = gd.build_sharded(Xd, prm, timing=True)
+        sizes = torch.tensor(res.sizes, dtype=torch.float64)
+        phases = {k: round(v, 3) for k, v in res.phase_ms.items()}
+        t = torch.tensor([phases[k] for k in phases], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        phases = {k: round(float(v), 3) for k, v in zip(phases, t.tolist())}
+    skew = {"max_bucket": int(sizes.max()), "sum_sq_over_balanced": float((sizes * sizes).sum() * sizes.numel()
+                                                                         / sizes.sum() ** 2)}
+
     # quality: recall@32 of the pre-prune kNN graph on 1000 sampled points of rank 0's rows
     # (exact GT over the whole job's dataset in fp64 on the GPU)
     recall = None
@@ -416,7 +434,8 @@ def main():
                 "vs_baseline": None, "dtype": "bf16" if cfg.dtype == "uint8" else "tf32",
                 "data": "synthetic (seeded Gaussian mixture)", "config": config, "roofline": roofline,
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-                "clocks": clocks, "recall_at_32": recall, "stages": stage_summary,
+                "clocks": clocks, "recall_at_32": recall, "bucket_skew": skew, "phases_ms_max_over_ranks": phases,
+                "stages": stage_summary,
                 "instrumented_ms_per_step": step_ms_sum}
         print(json.dumps(line))
     if world > 1:

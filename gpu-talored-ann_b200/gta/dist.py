@@ -70,7 +70,9 @@ class ShardResult:
     top2: torch.Tensor  # n_local x 2 int32
     graph: Optional[torch.Tensor] = None  # n_local x K (int32 view of uint32 ids)
     owner: Optional[list] = None  # bucket -> rank
+    sizes: Optional[list] = None  # memberships per bucket (whole job)
     comm_bytes: int = 0  # bytes this rank sent
+    phase_ms: Optional[dict] = None  # device time per phase when timing was requested
 
 
 # ---------------------------------------------------------------- libgta stages
@@ -218,12 +220,35 @@ def _all_gather_rows(local: torch.Tensor, counts: list, group=None) -> torch.Ten
     return torch.cat([buf[r * mx: r * mx + counts[r]] for r in range(world)])
 
 
+class _Phases:
+    """CUDA-event marks between the driver's phases (when timing is on)."""
+
+    def __init__(self, on: bool):
+        self.on = on and torch.cuda.is_available()
+        self.marks = []
+
+    def mark(self, name: str):
+        if self.on:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.marks.append((name, ev))
+
+    def result(self):
+        if not self.on or len(self.marks) < 2:
+            return None
+        torch.cuda.synchronize()
+        return {n: self.marks[i - 1][1].elapsed_time(e) for i, (n, e) in enumerate(self.marks) if i > 0}
+
+
 def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_centroids: Optional[torch.Tensor] = None,
-                  group=None) -> ShardResult:
+                  group=None, timing: bool = False) -> ShardResult:
     """One rank's part of the multi-GPU build.  X_local: this rank's rows (contiguous
     global row block, rank order), on the rank's device.  Collective: every rank of
-    ``group`` calls it with the same ``prm``."""
+    ``group`` calls it with the same ``prm``.  With ``timing`` the result carries the
+    device time of each phase (kernels and collectives) on this rank."""
     st = stages if stages is not None else CudaStages()
+    ph = _Phases(timing)
+    ph.mark("start")
     dev = X_local.device
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
@@ -253,6 +278,7 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
         dist.all_reduce(pool, group=group)
         C = st.kmeans_init(pool, B, prm.seed)
         del pool
+    ph.mark("kmeans_init")
     sid = st.sample_ids(N, n_s, prm.seed, dev)
     mine = sid[(sid >= row0) & (sid < row0 + n_local)].contiguous()
     Xs = st.gather_rows(X_local, row0, mine)
@@ -263,6 +289,7 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
         dist.all_reduce(cts, group=group)
         C = st.centroid_means(sums, cts, C)
     del Xs
+    ph.mark("lloyd")
 
     # ---- 2. top-2 buckets of the local rows
     gid_local = torch.arange(row0, row0 + n_local, dtype=torch.int32, device=dev)
@@ -275,8 +302,10 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
     # ---- 3. placement
     sizes = torch.bincount(top2.reshape(-1).long(), minlength=B).to(torch.int64)
     dist.all_reduce(sizes, group=group)
-    owner = place_buckets(sizes.tolist(), world)
+    sizes_l = sizes.tolist()
+    owner = place_buckets(sizes_l, world)
     owner_t = torch.tensor(owner, dtype=torch.int64, device=dev)
+    ph.mark("top2_placement")
 
     # ---- 4. memberships to bucket owners: slot s of point p is membership 2p+s
     bucket = top2.reshape(-1)
@@ -295,12 +324,14 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
     meta_r = _exchange(meta, send_counts, recv_counts, group)
     sent += rows.numel() * elem + meta.numel() * 4
     del rows, meta
+    ph.mark("exchange_points")
 
     # ---- 5. per-bucket top-M on the owner
     gid_r = meta_r[:, 0].contiguous()
     order, offsets = st.group_memberships(meta_r[:, 1].contiguous(), meta_r[:, 2].contiguous(), B)
     lid, ldist = st.bucket_knn_rows(R, order, gid_r, offsets, M)
     del R
+    ph.mark("bucket_knn")
 
     # ---- 6. lists back to the points' owners, merged per point
     og = gid_r[order.long()]
@@ -317,6 +348,7 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
     meta_b = _exchange(meta2, send2, recv2, group)
     sent += lid.numel() * 8 + meta2.numel() * 4
     del lid, ldist
+    ph.mark("exchange_lists")
     p = (meta_b[:, 0].long() - row0)
     lo_bucket = torch.minimum(top2[:, 0], top2[:, 1])
     slot = (meta_b[:, 1] != lo_bucket[p]).long()
@@ -324,19 +356,25 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
     mem_row[p, slot] = torch.arange(meta_b.shape[0], dtype=torch.int64, device=dev)
     knn_ids, knn_dists = st.merge_memberships(lid_b.contiguous(), ldist_b.contiguous(), mem_row)
     del lid_b, ldist_b
+    ph.mark("merge")
 
     res = ShardResult(row0=row0, n_total=N, knn_ids=knn_ids, knn_dists=knn_dists, centroids=C, top2=top2,
-                      owner=owner)
+                      owner=owner, sizes=sizes_l)
     # ---- 7. CAGRA
     if prm.graph_degree > 0:
         K = prm.graph_degree
         g_local = st.sanitize_rows(knn_ids, row0, N)
         g_full = _all_gather_rows(g_local, counts, group)
         sent += g_local.numel() * 4 * (world - 1)
+        ph.mark("gather_graph")
         pruned = st.prune_rows(g_full, K, row0, n_local, top2, B)
         del g_full
+        ph.mark("prune")
         p_full = _all_gather_rows(pruned, counts, group)
         sent += pruned.numel() * 4 * (world - 1)
+        ph.mark("gather_pruned")
         res.graph = st.reverse_merge_rows(p_full, row0, n_local)
+        ph.mark("reverse")
     res.comm_bytes = sent
+    res.phase_ms = ph.result()
     return res

@@ -78,10 +78,12 @@ def generate(cfg: Config, seed: int = 42, chunk: int = 1 << 20) -> np.ndarray:
 
 
 def generate_shard(cfg: Config, shard: int, seed: int = 42, chunk: int = 1 << 20) -> np.ndarray:
-    """cfg.n rows of shard ``shard`` of a multi-shard dataset: the same mixture
-    centres as generate(cfg, seed), each shard with its own label / noise stream.
-    Shard 0 is generate(cfg, seed) itself."""
+    """cfg.n rows of shard ``shard`` of a weak-scaling dataset: every shard is a
+    mixture of the configured shape with its own centres, labels and noise, so a
+    W-shard dataset is W independent copies of the configured problem (the bucket
+    count grows with W).  Shard 0 is generate(cfg, seed) itself."""
     if shard == 0:
         return generate(cfg, seed, chunk)
-    centres = _centres(cfg, np.random.default_rng(seed))
-    return _rows(cfg, centres, np.random.default_rng([seed, shard]), chunk)
+    rng = np.random.default_rng([seed, shard])
+    centres = _centres(cfg, rng)
+    return _rows(cfg, centres, rng, chunk)

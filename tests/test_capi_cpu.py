@@ -100,12 +100,13 @@ def test_synthetic_generators_are_seeded():
     assert (c3 >= 0).all() and c3.shape[1] == 960
 
 
-def test_shard_generator_shares_centres():
+def test_shard_generator_is_seeded_per_shard():
     cfg = gta.scaled(gta.CONFIGS["c2"], 3000)
     np.testing.assert_array_equal(gta.generate_shard(cfg, 0, seed=9), gta.generate(cfg, seed=9))
     s1 = gta.generate_shard(cfg, 1, seed=9)
     assert s1.shape == (3000, 128) and not np.array_equal(s1, gta.generate(cfg, seed=9))
     np.testing.assert_array_equal(s1, gta.generate_shard(cfg, 1, seed=9))
+    assert not np.array_equal(s1, gta.generate_shard(cfg, 2, seed=9))
 
 
 @pytest.mark.parametrize("n,b,req,n_s,pool", [(1_000_000, 256, 0, 100_000, 5120), (100_000_000, 8192, 0, 10_000_000,
