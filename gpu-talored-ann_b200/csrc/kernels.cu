@@ -266,7 +266,8 @@ __device__ bool coop_barrier(unsigned* arrive, unsigned target, int* abort_flag,
         atomicAdd(arrive, 1u);
         const long long t0 = clock64();
         int ok = 1;
-        while (ld_acquire_u32(arrive) < target) {
+        for (uint32_t it = 0; ld_acquire_u32(arrive) < target; ++it) {
+            if ((it & 15u) != 15u) continue;  // poll hot; check abort and the budget every 16 polls
             if (*reinterpret_cast<volatile int*>(abort_flag)) { ok = 0; break; }
             if (clock64() - t0 > kWaitBudgetCycles) {
                 atomicExch(abort_flag, 1);
@@ -274,7 +275,6 @@ __device__ bool coop_barrier(unsigned* arrive, unsigned target, int* abort_flag,
                 ok = 0;
                 break;
             }
-            __nanosleep(32);
         }
         __threadfence();
         *s_ok = ok;
@@ -309,12 +309,15 @@ __device__ __forceinline__ double block_incl_scan(double v, double* s_warp)
     return v + off;
 }
 
+// With `resident`, each CTA keeps its 256 pool rows in shared memory, transposed
+// (dimension-major, so thread t reads column t without bank conflicts).
 __global__ void __launch_bounds__(kKppCoopThreads)
     kpp_coop_kernel(const float* __restrict__ pool, int64_t pool_n, int d, int d_pad, float* __restrict__ C, int B,
                     uint64_t seed, double* __restrict__ gpre, double* __restrict__ gtot, unsigned* arrive,
-                    int* abort_flag, int* err)
+                    int* abort_flag, int* err, int resident)
 {
     extern __shared__ float cen[];
+    float* rows_t = cen + d_pad;  // resident: [d][256]
     __shared__ double s_warp[kKppCoopThreads / 32];
     __shared__ int64_t s_pick;
     __shared__ int s_blk, s_ok;
@@ -324,6 +327,8 @@ __global__ void __launch_bounds__(kKppCoopThreads)
     const int64_t i = static_cast<int64_t>(blockIdx.x) * kKppCoopThreads + tid;
     const bool valid = i < pool_n;
     float md = INFINITY;
+    if (resident)
+        for (int k = 0; k < d; ++k) rows_t[k * kKppCoopThreads + tid] = valid ? pool[i * d_pad + k] : 0.0f;
     if (tid == 0) {
         const int64_t f = static_cast<int64_t>(uniform01(seed, 0) * static_cast<double>(pool_n));
         s_pick = f < pool_n ? f : pool_n - 1;
@@ -337,7 +342,19 @@ __global__ void __launch_bounds__(kKppCoopThreads)
                 C[static_cast<int64_t>(t) * d_pad + k] = pool[pick * d_pad + k];
         __syncthreads();
         if (t + 1 >= B) break;
-        if (valid) md = fminf(md, exact_l2_f(pool + i * d_pad, cen, d));
+        if (valid) {
+            float dd;
+            if (resident) {  // the same fp32 chain as exact_l2_f, operands from shared memory
+                dd = 0.0f;
+                for (int k = 0; k < d; ++k) {
+                    const float t = rows_t[k * kKppCoopThreads + tid] - cen[k];
+                    dd = fmaf(t, t, dd);
+                }
+            } else {
+                dd = exact_l2_f(pool + i * d_pad, cen, d);
+            }
+            md = fminf(md, dd);
+        }
         const double incl = block_incl_scan(valid ? static_cast<double>(md) : 0.0, s_warp);
         const int par = t & 1;
         gpre[static_cast<int64_t>(par) * G * kKppCoopThreads + static_cast<int64_t>(blockIdx.x) * kKppCoopThreads + tid] = incl;
@@ -601,11 +618,13 @@ constexpr int kPruneWarps = 8;
 // Warp per row a (processed in `order` when given: rows of one bucket region
 // together, so the neighbour rows they gather stay in L2).  Row a's candidates
 // go into a shared-memory id -> rank hash table sized 8x the row (load factor
-// <= 1/8, so nearly every lookup probes one slot and the warp stays converged);
-// duplicates of an id keep separate slots.  For every closer candidate D (rank
-// kAD) each lane looks its entries of D's row up, marks the later ranks kAB it
-// finds (each (kAD, kAB) once: a bit mask OR-reduced over the warp), and the
-// lanes owning those ranks count them.  Two neighbour rows are loaded ahead.
+// <= 1/8); duplicates of an id keep separate slots.  Lane l takes the closer
+// candidates D = row[kAD] with kAD = l, l+32, ...: it reads D's whole row and
+// looks every entry up, setting bit kAB of its mask for each later rank kAB >
+// kAD whose candidate appears there (a set: a pair (kAD, kAB) counts once even
+// when D's row repeats an id).  The detour count of kAB is the number of masks
+// holding bit kAB, summed over the warp with ballots; no per-candidate
+// cross-lane reduction is needed.
 constexpr int kPruneHash = 1024;
 
 __device__ __forceinline__ uint32_t hash_id(uint32_t id, uint32_t mask) { return (id * 2654435761u) >> 7 & mask; }
@@ -641,56 +660,57 @@ __global__ void __launch_bounds__(kPruneWarps * 32)
         }
     }
     __syncwarp();
-    const int G = (M + 31) / 32;
-    uint32_t cnt[kMaxM / 32] = {0, 0, 0, 0};
-    constexpr int kAhead = 2;
-    for (int kb = 0; kb < M - 1; kb += kAhead) {
-        uint32_t vals[kAhead][kMaxM / 32];
+    // this lane's masks: slot j serves kAD = lane + 32 j, bit kAB of word kAB / 64
+    constexpr int kJ = kMaxM / 32;
+    uint64_t mk[kJ][2];
+    const int n_j = (M - 1 + 31) / 32;
+    const bool vec = (M & 3) == 0;
 #pragma unroll
-        for (int u = 0; u < kAhead; ++u) {
-            const int kAD = kb + u;
-            const uint32_t dd = (kAD < M - 1) ? s_row[w][kAD] : kEmpty;
-            const bool okd = kAD < M - 1 && static_cast<int64_t>(dd) < N;
-            if (kAD < M - 1 && !okd && lane == 0) atomicCAS(err, 0, kDevBadIndex);
-            const uint32_t* rd = g + static_cast<int64_t>(okd ? dd : 0) * M;
-#pragma unroll
-            for (int gi = 0; gi < kMaxM / 32; ++gi) {
-                const int kDB = gi * 32 + lane;
-                vals[u][gi] = (okd && gi < G && kDB < M) ? rd[kDB] : kEmpty;
-            }
+    for (int j = 0; j < kJ; ++j) {
+        mk[j][0] = 0;
+        mk[j][1] = 0;
+        const int kAD = lane + 32 * j;
+        if (j >= n_j || kAD >= M - 1) continue;
+        const uint32_t dd = s_row[w][kAD];
+        if (static_cast<int64_t>(dd) >= N) {
+            atomicCAS(err, 0, kDevBadIndex);
+            continue;
         }
-#pragma unroll
-        for (int u = 0; u < kAhead; ++u) {
-            const int kAD = kb + u;
-            if (kAD >= M - 1) break;
-            uint32_t hit[kMaxM / 32] = {0, 0, 0, 0};
-#pragma unroll
-            for (int gi = 0; gi < kMaxM / 32; ++gi) {
-                if (gi >= G) break;
-                const uint32_t bv = vals[u][gi];
-                if (bv == kEmpty) continue;
-                for (uint32_t h = hash_id(bv, mask);; h = (h + 1) & mask) {
-                    const uint32_t key = s_hkey[w][h];
-                    if (key == kEmpty) break;
-                    if (key == bv) {
-                        const int kAB = s_hrank[w][h];
-                        if (kAB > kAD) hit[kAB >> 5] |= 1u << (kAB & 31);
+        const uint32_t* rd = g + static_cast<int64_t>(dd) * M;
+        auto look = [&](uint32_t v) {
+            for (uint32_t h = hash_id(v, mask);; h = (h + 1) & mask) {
+                const uint32_t key = s_hkey[w][h];
+                if (key == kEmpty) break;
+                if (key == v) {
+                    const int kAB = s_hrank[w][h];
+                    if (kAB > kAD) {
+                        const uint64_t bit = 1ull << (kAB & 63);
+                        if (kAB < 64) mk[j][0] |= bit;
+                        else mk[j][1] |= bit;
                     }
                 }
             }
-#pragma unroll
-            for (int gi = 0; gi < kMaxM / 32; ++gi) {
-                if (gi >= G) break;
-                uint32_t v = hit[gi];
-                for (int off = 16; off > 0; off >>= 1) v |= __shfl_xor_sync(0xffffffffu, v, off);
-                cnt[gi] += (v >> lane) & 1u;
+        };
+        if (vec) {
+            const uint4* rd4 = reinterpret_cast<const uint4*>(rd);
+            for (int e4 = 0; e4 < (M >> 2); ++e4) {
+                const uint4 x = rd4[e4];
+                look(x.x); look(x.y); look(x.z); look(x.w);
             }
+        } else {
+            for (int e = 0; e < M; ++e) look(rd[e]);
         }
     }
+    // detour count of every rank: how many lanes' masks hold its bit
+    for (int kAB = 0; kAB < M; ++kAB) {
+        int c = 0;
 #pragma unroll
-    for (int gi = 0; gi < kMaxM / 32; ++gi) {
-        const int k = gi * 32 + lane;
-        if (gi < G && k < M) s_cnt[w][k] = cnt[gi];
+        for (int j = 0; j < kJ; ++j) {
+            if (j >= n_j) break;
+            const uint64_t word = kAB < 64 ? mk[j][0] : mk[j][1];
+            c += __popc(__ballot_sync(0xffffffffu, (word >> (kAB & 63)) & 1ull));
+        }
+        if (lane == (kAB & 31)) s_cnt[w][kAB] = static_cast<uint32_t>(c);
     }
     __syncwarp();
     // position of entry k = #{k' : (cnt[k'], k') < (cnt[k], k)}; the first K positions are kept
@@ -921,13 +941,22 @@ void kmeanspp_init(const float* pool, const float* /*pool_norm*/, int64_t pool_n
     {
         // one cooperative launch when every CTA fits on the device at once
         const int G = static_cast<int>((pool_n + kKppCoopThreads - 1) / kKppCoopThreads);
-        const size_t smem1 = sizeof(float) * static_cast<size_t>(d);
         int dev = 0, n_sm = 0, per_sm = 0, coop = 0;
         GTA_CUDA(cudaGetDevice(&dev));
         GTA_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
         GTA_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
+        // pool rows resident in shared memory when they fit (d <= 200: about 200 KB per CTA)
+        int resident = d <= 200 ? 1 : 0;
+        size_t smem1 = sizeof(float) * static_cast<size_t>(d_pad) * (resident ? 1 + kKppCoopThreads : 1);
+        GTA_CUDA(cudaFuncSetAttribute(kpp_coop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(sizeof(float) * static_cast<size_t>(d_pad) * (1 + kKppCoopThreads))));
         GTA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kpp_coop_kernel, kKppCoopThreads, smem1));
-        if (coop && smem1 <= 48 * 1024 && G <= per_sm * n_sm && G <= kKppCoopThreads) {
+        if (resident && G > per_sm * n_sm) {
+            resident = 0;
+            smem1 = sizeof(float) * static_cast<size_t>(d_pad);
+            GTA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kpp_coop_kernel, kKppCoopThreads, smem1));
+        }
+        if (coop && smem1 <= 227 * 1024 && G <= per_sm * n_sm && G <= kKppCoopThreads) {
             DevBuf<double> gpre(static_cast<size_t>(2) * G * kKppCoopThreads, st), gtot(static_cast<size_t>(2) * G, st);
             DevBuf<unsigned> arrive(2, st);
             GTA_CUDA(cudaMemsetAsync(arrive.get(), 0, 2 * sizeof(unsigned), st));
@@ -936,7 +965,8 @@ void kmeanspp_init(const float* pool, const float* /*pool_norm*/, int64_t pool_n
             int* abort_flag = reinterpret_cast<int*>(arrive.get() + 1);
             double* gp = gpre.get();
             double* gt = gtot.get();
-            void* args[] = {const_cast<float**>(&pool), &pool_n, &d, &d_pad, &C, &B, &seed, &gp, &gt, &arr, &abort_flag, &err};
+            void* args[] = {const_cast<float**>(&pool), &pool_n, &d, &d_pad, &C, &B, &seed, &gp, &gt, &arr, &abort_flag, &err,
+                            &resident};
             GTA_CUDA(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kpp_coop_kernel), dim3(G),
                                                  dim3(kKppCoopThreads), args, smem1, st));
             count_launches(1);
