@@ -52,10 +52,10 @@ def _peaks():
     return 6650.0, 1590.0, "fallback"
 
 
-# DRAM bytes (read + write) per algorithmic unit of a kernel, from one ncu capture each
-# (profiles/dist_topk_kernel_c2_400k.md, profiles/prune_kernel_c2_400k.md; C2 distribution at
-# N = 400 000, scaled to a launch by its units: the traffic grows with the rows processed)
-TRAFFIC_PER_UNIT = {"dist_topk_bucket": 576.5e6 / 3.0868e12, "prune": 136.48e6 / 6.7072e9}
+# DRAM bytes (read + write) per algorithmic unit of a kernel, from one ncu capture of each
+# kernel on the C2 distribution at N = 400 000, scaled to a launch by its units (the traffic
+# grows with the rows processed)
+TRAFFIC_PER_UNIT = {"dist_topk_bucket": 579.74e6 / 3.3773e12, "prune": 139.38e6 / 6.7069e9}
 
 
 # ---------------------------------------------------------------- clocks
