@@ -248,6 +248,11 @@ __device__ __forceinline__ uint64_t tmem_ld_key(uint32_t taddr)
                  : "memory");
     return (static_cast<uint64_t>(hi) << 32) | lo;
 }
+// Store 16 consecutive 32-bit TMEM columns of the warp's 32 lanes.
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&v)[16])
+{
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};" ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]) : "memory");
+}
 // Wait until this thread's tcgen05.st operations have completed.
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 // Wait for outstanding tcgen05.ld into one 32-register array.

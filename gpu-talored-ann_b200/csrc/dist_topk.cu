@@ -240,6 +240,26 @@ __device__ __forceinline__ void keys_store16(uint32_t taddr, const uint64_t (&k)
     tmem_st_32x32b_x32(taddr, a);
 }
 
+__device__ __forceinline__ void keys_load8(uint32_t taddr, uint64_t (&k)[8])
+{
+    uint32_t a[16];
+    tmem_ld_32x32b_x16(taddr, a);
+    tmem_ld_wait_regs(a);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) k[i] = (static_cast<uint64_t>(a[2 * i + 1]) << 32) | a[2 * i];
+}
+
+__device__ __forceinline__ void keys_store8(uint32_t taddr, const uint64_t (&k)[8])
+{
+    uint32_t a[16];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        a[2 * i] = static_cast<uint32_t>(k[i]);
+        a[2 * i + 1] = static_cast<uint32_t>(k[i] >> 32);
+    }
+    tmem_st_32x32b_x16(taddr, a);
+}
+
 __device__ __forceinline__ uint64_t min_key(uint64_t a, uint64_t b) { return a < b ? a : b; }
 __device__ __forceinline__ float key_dist(uint64_t key) { return key2f(static_cast<uint32_t>(key >> 32)); }
 
@@ -267,26 +287,27 @@ __device__ __noinline__ ListTail flush_tmem(uint32_t tl, const uint64_t* buf, in
         keys_store32(tl, l);
         t.last = l[31];
     } else {
-        // 64 keys in four 16-key blocks of TMEM, worked on a block pair at a time
-        uint64_t a[16], b[16];
-        keys_load16(tl + 64u, a);  // keys 32..47 against buffer keys 31..16
+        // 64 keys in eight 8-key blocks of TMEM (16 columns each), a block or a block pair at a time,
+        // so that at most the 32 buffer keys and 16 list keys are held at once
 #pragma unroll
-        for (int i = 0; i < 16; ++i) a[i] = min_key(a[i], k[31 - i]);
-        keys_load16(tl + 96u, b);  // keys 48..63 against buffer keys 15..0
+        for (int j = 0; j < 4; ++j) {  // keys 32 + 8j .. against buffer keys 31 - 8j ..
+            uint64_t a[8];
+            keys_load8(tl + 64u + 16u * j, a);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) b[i] = min_key(b[i], k[15 - i]);
-        // stride-32 half-cleaner: (0..15, 32..47) and (16..31, 48..63)
-        uint64_t c[16];
-        keys_load16(tl, c);
+            for (int i = 0; i < 8; ++i) a[i] = min_key(a[i], k[31 - 8 * j - i]);
+            keys_store8(tl + 64u + 16u * j, a);
+        }
+        tmem_st_wait();
 #pragma unroll
-        for (int i = 0; i < 16; ++i) cmp_swap(c[i], a[i]);
-        keys_store16(tl, c);
-        keys_store16(tl + 64u, a);
-        keys_load16(tl + 32u, c);
+        for (int j = 0; j < 4; ++j) {  // stride-32 half-cleaner: (8j.., 32 + 8j..)
+            uint64_t a[8], b[8];
+            keys_load8(tl + 16u * j, a);
+            keys_load8(tl + 64u + 16u * j, b);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) cmp_swap(c[i], b[i]);
-        keys_store16(tl + 32u, c);
-        keys_store16(tl + 96u, b);
+            for (int i = 0; i < 8; ++i) cmp_swap(a[i], b[i]);
+            keys_store8(tl + 16u * j, a);
+            keys_store8(tl + 64u + 16u * j, b);
+        }
         tmem_st_wait();
         // strides 16..1 inside each 32-key half
         uint64_t l[32];
