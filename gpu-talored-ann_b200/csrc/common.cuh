@@ -70,6 +70,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity)
     return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes (or about `ns` nanoseconds pass), waking as soon as it does.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity, uint32_t ns)
+{
+    uint32_t ok;
+    asm volatile(
+        "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3; selp.u32 %0, 1, 0, p; }"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(ns)
+        : "memory");
+    return ok != 0;
+}
+
 // Bounded wait on the phase with the given parity.  Gives up (returns false)
 // when the CTA-wide abort flag is raised by another warp or the clock budget
 // runs out; in the latter case records `code` in *err and raises the flag.
@@ -90,8 +103,8 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
     }
 }
 
-// Warp-wide bounded wait for the epilogue warps: lane 0 polls with a short
-// nanosleep backoff (32 lanes spinning on one mbarrier would take issue slots
+// Warp-wide bounded wait for the epilogue warps: lane 0 waits (suspended in
+// hardware between tries; 32 lanes polling one mbarrier would take issue slots
 // and shared-memory cycles from the warps that work), then every lane observes
 // the completed phase once.  Warp-uniform result.
 __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
@@ -100,11 +113,8 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, vo
     int ok = 1;
     if ((threadIdx.x & 31) == 0 && !mbar_try_wait(bar, parity)) {
         const long long t0 = clock64();
-        uint32_t ns = 16;
         for (;;) {
-            __nanosleep(ns);
-            if (mbar_try_wait(bar, parity)) break;
-            if (ns < 128) ns <<= 1;
+            if (mbar_try_wait_hint(bar, parity, 20000u)) break;
             if (*abort_flag) { ok = 0; break; }
             if (clock64() - t0 > kWaitBudgetCycles) {
                 *abort_flag = 1;
@@ -120,19 +130,16 @@ __device__ __forceinline__ bool mbar_wait_warp(uint32_t bar, uint32_t parity, vo
     return __all_sync(0xffffffffu, ok != 0);
 }
 
-// Same bounded wait with exponential nanosleep backoff, for the single-thread
-// producer / MMA roles: they share issue slots with epilogue warps, so they
-// must not spin hot while the epilogue works.
+// Same bounded wait for the single-thread producer / MMA roles: each try
+// suspends the thread in hardware (it takes no issue slots from the epilogue
+// warps) and wakes it as soon as the phase completes.
 __device__ __forceinline__ bool mbar_wait_backoff(uint32_t bar, uint32_t parity, volatile int* abort_flag, int* err,
                                                   int code)
 {
     if (mbar_try_wait(bar, parity)) return true;
     const long long t0 = clock64();
-    uint32_t ns = 32;
     for (;;) {
-        __nanosleep(ns);
-        if (mbar_try_wait(bar, parity)) return true;
-        if (ns < 256) ns <<= 1;
+        if (mbar_try_wait_hint(bar, parity, 20000u)) return true;
         if (*abort_flag) return false;
         if (clock64() - t0 > kWaitBudgetCycles) {
             *abort_flag = 1;
