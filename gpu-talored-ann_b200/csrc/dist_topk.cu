@@ -298,7 +298,7 @@ __device__ __noinline__ ListTail flush_tmem(uint32_t tl, const uint64_t* buf, in
             keys_store8(tl + 64u + 16u * j, a);
         }
         tmem_st_wait();
-#pragma unroll
+#pragma unroll 1
         for (int j = 0; j < 4; ++j) {  // stride-32 half-cleaner: (8j.., 32 + 8j..)
             uint64_t a[8], b[8];
             keys_load8(tl + 16u * j, a);
@@ -309,14 +309,14 @@ __device__ __noinline__ ListTail flush_tmem(uint32_t tl, const uint64_t* buf, in
             keys_store8(tl + 64u + 16u * j, b);
         }
         tmem_st_wait();
-        // strides 16..1 inside each 32-key half
+        // strides 16..1 inside each 32-key half (one copy of the network)
         uint64_t l[32];
-        keys_load32(tl, l);
-        merge32(l);
-        keys_store32(tl, l);
-        keys_load32(tl + 64u, l);
-        merge32(l);
-        keys_store32(tl + 64u, l);
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+            keys_load32(tl + 64u * hh, l);
+            merge32(l);
+            keys_store32(tl + 64u * hh, l);
+        }
         t.last = l[31];
     }
     tmem_st_wait();
@@ -751,8 +751,8 @@ __global__ void __launch_bounds__(kThreads, kV)
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
         const uint32_t tl = lane_base + 2u * static_cast<uint32_t>(kTN);  // after the two accumulators
         uint64_t* my_buf = buf + r;
-        // per warp: 4 groups of 32 float4 (scores e4*4 .. e4*4+3 of each lane), bank-conflict free
-        float* scr = reinterpret_cast<float*>(gbase + p.scr_off) + q * 512 + lane * 4;
+        // per warp: 16 rows of 32 floats (score e of lane l at [e][l]): conflict-free for any e per lane
+        float* scr = reinterpret_cast<float*>(gbase + p.scr_off) + q * 512 + lane;
         {
             uint32_t e[32];
 #pragma unroll
@@ -834,20 +834,17 @@ __global__ void __launch_bounds__(kThreads, kV)
                 const int npass = __popc(mask);
                 const int rounds = __reduce_max_sync(0xffffffffu, static_cast<unsigned>(npass));
                 if (rounds > 0) {
-                    // scores to this lane's scratch, then one append per pass of the busiest lane
+                    // scores to this lane's scratch, then one append per pass
 #pragma unroll
-                    for (int e4 = 0; e4 < 4; ++e4)
-                        *reinterpret_cast<float4*>(scr + e4 * 128) =
-                            make_float4(sv[e4 * 4], sv[e4 * 4 + 1], sv[e4 * 4 + 2], sv[e4 * 4 + 3]);
+                    for (int e = 0; e < 16; ++e) scr[e * 32] = sv[e];
                     uint32_t m = mask;
-                    for (int i = 0; i < rounds; ++i) {
+                    for (int i = nb; m != 0u; ++i) {  // this lane's passes, in column order
                         const int e = __ffs(m) - 1;
-                        if (e >= 0) {
-                            const uint32_t id = kTF32 ? c0 + static_cast<uint32_t>(e) : idw[c * 16 + e];
-                            my_buf[(nb + i) * 128] = (static_cast<uint64_t>(f2key(scr[(e >> 2) * 128 + (e & 3)])) << 32) | id;
-                            m &= m - 1u;
-                        }
+                        const uint32_t id = kTF32 ? c0 + static_cast<uint32_t>(e) : idw[c * 16 + e];
+                        my_buf[i * 128] = (static_cast<uint64_t>(f2key(scr[e * 32])) << 32) | id;
+                        m &= m - 1u;
                     }
+                    __syncwarp();
                     nb += npass;
                 }
                 if (__any_sync(0xffffffffu, nb > kBuf - 16)) {
