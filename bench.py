@@ -179,6 +179,30 @@ def cpu_pipeline_sample(X: np.ndarray, cfg, seed: int = 42, budget_buckets: int 
 
 
 # ---------------------------------------------------------------- main
+SEARCH_QUERIES = 2000
+SEARCH_SAMPLES = 16384
+
+
+def exact_knn(Xall, Xq, k: int, exclude=None) -> np.ndarray:
+    """Exact k nearest rows of ``Xall`` (device) for each row of ``Xq``, fp64 on the GPU;
+    ``exclude[i]`` (a row index of Xall) is left out of query i's answer."""
+    import torch
+
+    Xq = Xq.double()
+    best = []
+    for c0 in range(0, Xall.shape[0], 1 << 18):
+        Xc = Xall[c0:c0 + (1 << 18)].double()
+        dd = (Xq * Xq).sum(1, keepdim=True) + (Xc * Xc).sum(1)[None, :] - 2.0 * Xq @ Xc.T
+        if exclude is not None:
+            idx = torch.arange(c0, c0 + Xc.shape[0], device="cuda")
+            dd[exclude[:, None] == idx[None, :]] = float("inf")
+        v, i = torch.topk(dd, k, dim=1, largest=False)
+        best.append((v, i + c0))
+    v = torch.cat([b[0] for b in best], 1)
+    i = torch.cat([b[1] for b in best], 1)
+    return torch.gather(i, 1, torch.topk(v, k, dim=1, largest=False).indices).cpu().numpy()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -360,24 +384,43 @@ def main():
         ids = last["res"].knn_ids
         Xall = torch.empty((cfg.n * world, cfg.d), dtype=Xd.dtype, device="cuda")
         dist.all_gather_into_tensor(Xall, Xd)
+    if world > 1:
+        g_all = torch.empty((cfg.n * world, cfg.graph_degree), dtype=g.dtype, device="cuda")
+        dist.all_gather_into_tensor(g_all, g.contiguous())
+    else:
+        g_all = g
+    search_q = None
     if rank == 0:
-        n_all = Xall.shape[0]
         q = torch.from_numpy(np.random.default_rng(0).choice(cfg.n, 1000, replace=False)).cuda()
-        Xq = Xall[q].double()
-        best = []
-        for c0 in range(0, n_all, 1 << 18):
-            Xc = Xall[c0:c0 + (1 << 18)].double()
-            dd = (Xq * Xq).sum(1, keepdim=True) + (Xc * Xc).sum(1)[None, :] - 2.0 * Xq @ Xc.T
-            idx = torch.arange(c0, c0 + Xc.shape[0], device="cuda")
-            dd[q[:, None] == idx[None, :]] = float("inf")
-            v, i = torch.topk(dd, 32, dim=1, largest=False)
-            best.append((v, i + c0))
-        v = torch.cat([b[0] for b in best], 1)
-        i = torch.cat([b[1] for b in best], 1)
-        gt = torch.gather(i, 1, torch.topk(v, 32, dim=1, largest=False).indices).cpu().numpy()
+        gt = exact_knn(Xall, Xall[q], 32, exclude=q)
         approx = ids[q].cpu().numpy()[:, :32]
         recall = float(np.mean([len(np.intersect1d(approx[r], gt[r])) / 32.0 for r in range(1000)]))
-    del Xall
+        # graph search over the final graph with the reference search's defaults
+        # (topk 10, ef 200, 4 random entry points, seed 42) on held-out queries
+        Q = torch.from_numpy(gta.generate_queries(cfg, SEARCH_QUERIES)).cuda()
+        gt10 = exact_knn(Xall, Q, 10)
+        search_q = {"queries": int(Q.shape[0]), "topk": 10, "ef": 200, "num_entry": 4,
+                    "queries_from": "held-out rows of the same mixture"}
+        # (1) the reference's entry rule: 4 uniform random rows per query; (2) the 4 nearest of
+        # SEARCH_SAMPLES seeded random rows (random-sampling seeding).  The synthetic mixture's
+        # clusters are far apart, so the graph has one component per cluster and (1) only
+        # finds the query's cluster when an entry happens to fall in it.
+        ent_ref = gta.search_entries(Xall.shape[0], Q.shape[0], 4, 42)
+        samp = torch.from_numpy(np.random.default_rng(7).choice(Xall.shape[0], SEARCH_SAMPLES, replace=False)).cuda()
+        ent_smp = samp[torch.from_numpy(exact_knn(Xall[samp], Q, 4)).cuda()].int().cpu().numpy()
+        for tag, ent in (("reference_entries", ent_ref), ("sampled_entries", ent_smp)):
+            gta.search(Xall, g_all, Q, 10, 200, entries=ent)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            sid, _ = gta.search(Xall, g_all, Q, 10, 200, entries=ent)
+            e1.record()
+            torch.cuda.synchronize()
+            sid = sid.cpu().numpy()
+            search_q[tag] = {"recall_at_10": float(np.mean([len(np.intersect1d(sid[r], gt10[r])) / 10.0
+                                                            for r in range(Q.shape[0])])),
+                             "qps": Q.shape[0] / (e0.elapsed_time(e1) / 1e3)}
+        search_q["sampled_entries"]["samples"] = SEARCH_SAMPLES
+    del Xall, g_all
 
     # end to end with host buffers (pinned), copies inside the timed region: through the C ABI
     # (gta_build_cagra) on one GPU, through the sharded build on several
@@ -434,7 +477,7 @@ def main():
                 "vs_baseline": None, "dtype": "bf16" if cfg.dtype == "uint8" else "tf32",
                 "data": "synthetic (seeded Gaussian mixture)", "config": config, "roofline": roofline,
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-                "clocks": clocks, "recall_at_32": recall, "bucket_skew": skew, "phases_ms_max_over_ranks": phases,
+                "clocks": clocks, "recall_at_32": recall, "search": search_q, "bucket_skew": skew, "phases_ms_max_over_ranks": phases,
                 "stages": stage_summary,
                 "instrumented_ms_per_step": step_ms_sum}
         print(json.dumps(line))

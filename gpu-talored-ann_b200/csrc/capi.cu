@@ -822,6 +822,58 @@ int gta_reverse_merge_noalloc(const uint32_t* pruned, int64_t n, int32_t k, uint
 int64_t gta_reverse_merge_noalloc_max_rows(void) { return reverse_merge_noalloc_max_rows(); }
 int64_t gta_reverse_merge_noalloc_max_edges(void) { return reverse_merge_noalloc_max_edges(); }
 
+// ---------------------------------------------------------------- graph search
+int gta_search(const gta_dataset* base, const void* queries, int64_t nq, const uint32_t* graph, int32_t k_graph,
+               const int32_t* entries, int32_t n_entry, int32_t topk, int32_t ef, int32_t* out_ids, float* out_dists,
+               void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(base && base->data && queries && graph && entries && out_ids && out_dists && nq >= 0 &&
+                        base->n >= 1 && base->d >= 1 && k_graph >= 1 && n_entry >= 1,
+                    kInvalid, "gta_search: bad argument");
+        GTA_REQUIRE(base->dtype == GTA_F32 || base->dtype == GTA_U8 || base->dtype == GTA_I8, kInvalid,
+                    "gta_search: bad dtype");
+        if (nq == 0) return;
+        cudaStream_t st = S(stream);
+        const int64_t n = base->n;
+        const int d = base->d;
+        const size_t row = static_cast<size_t>(d) * elem_size(base->dtype);
+        const void* B = base->data;
+        const void* Q = queries;
+        const uint32_t* G = graph;
+        const int32_t* E = entries;
+        int32_t* oi = out_ids;
+        float* od = out_dists;
+        DevBuf<uint8_t> hb, hq, hg, he, hoi, hod;
+        if (!base->on_device) {  // host inputs: copy them in, results back out
+            hb = DevBuf<uint8_t>(row * n, st);
+            hq = DevBuf<uint8_t>(row * nq, st);
+            hg = DevBuf<uint8_t>(sizeof(uint32_t) * n * k_graph, st);
+            he = DevBuf<uint8_t>(sizeof(int32_t) * nq * n_entry, st);
+            hoi = DevBuf<uint8_t>(sizeof(int32_t) * nq * topk, st);
+            hod = DevBuf<uint8_t>(sizeof(float) * nq * topk, st);
+            GTA_CUDA(cudaMemcpyAsync(hb.get(), B, row * n, cudaMemcpyHostToDevice, st));
+            GTA_CUDA(cudaMemcpyAsync(hq.get(), Q, row * nq, cudaMemcpyHostToDevice, st));
+            GTA_CUDA(cudaMemcpyAsync(hg.get(), G, sizeof(uint32_t) * n * k_graph, cudaMemcpyHostToDevice, st));
+            GTA_CUDA(cudaMemcpyAsync(he.get(), E, sizeof(int32_t) * nq * n_entry, cudaMemcpyHostToDevice, st));
+            B = hb.get(); Q = hq.get();
+            G = reinterpret_cast<const uint32_t*>(hg.get());
+            E = reinterpret_cast<const int32_t*>(he.get());
+            oi = reinterpret_cast<int32_t*>(hoi.get());
+            od = reinterpret_cast<float*>(hod.get());
+        }
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        graph_search(B, base->dtype, n, d, G, k_graph, Q, nq, E, n_entry, topk, ef, oi, od, err.get(), st);
+        if (!base->on_device) {
+            GTA_CUDA(cudaMemcpyAsync(out_ids, oi, sizeof(int32_t) * nq * topk, cudaMemcpyDeviceToHost, st));
+            GTA_CUDA(cudaMemcpyAsync(out_dists, od, sizeof(float) * nq * topk, cudaMemcpyDeviceToHost, st));
+        }
+        check_device_error(err.get(), st, "gta_search");
+    });
+}
+
 // ---------------------------------------------------------------- shard stages (multi-GPU build)
 int gta_kmeans_sizes(int64_t n, const gta_bucket_params* p, int64_t* n_sample, int64_t* pool_n, uint64_t* pool_seed)
 {

@@ -21,6 +21,7 @@ enum DevErr : int {
     kDevBadIndex = 5,         // an id outside [0, N) met a bounds check
     kDevBadShape = 6,         // kernel launched with an unsupported shape
     kDevTimeoutGrid = 7,      // a grid barrier of a cooperative launch never completed
+    kDevOverflow = 8,         // a fixed-capacity structure (search visited set / candidates) filled up
 };
 
 constexpr long long kWaitBudgetCycles = 4000000000LL;   // ~2 s at 1.9 GHz

@@ -145,6 +145,10 @@ int64_t reverse_merge_noalloc_max_edges();
 void sort_rows_l2(const float* X, int d, int d_pad, const int32_t* knn, int64_t N, int M, int32_t* out,
                   cudaStream_t st);
 void max_sqrt(const float* v, int64_t n, float* out, cudaStream_t st);
+// best-first graph search, one warp per query (search.cu)
+void graph_search(const void* base, int dtype, int64_t n, int d, const uint32_t* graph, int kg, const void* queries,
+                  int64_t nq, const int32_t* entries, int ne, int topk, int ef, int32_t* out_ids, float* out_dists,
+                  int* err, cudaStream_t st);
 // shard variants (one rank's part of a multi-GPU build)
 void gather_range(const void* X, int dtype, int d, int64_t row0, int64_t n, const int32_t* ids, int64_t n_ids,
                   float* out, cudaStream_t st);

@@ -1353,9 +1353,10 @@ void check_device_error(const int* err, cudaStream_t st, const char* what)
     if (h != 0) {
         static const char* names[] = {"ok", "TMA tile wait timed out", "pipeline stage wait timed out",
                                       "accumulator wait timed out", "teardown wait timed out", "id out of range",
-                                      "unsupported shape", "grid barrier wait timed out"};
-        const char* n = (h >= 0 && h <= 7) ? names[h] : "unknown device error";
-        throw Error(h == kDevBadIndex ? kData : kCuda, std::string(what) + ": " + n);
+                                      "unsupported shape", "grid barrier wait timed out",
+                                      "search capacity exceeded (visited set or candidates; lower ef)"};
+        const char* n = (h >= 0 && h <= 8) ? names[h] : "unknown device error";
+        throw Error(h == kDevBadIndex ? kData : (h == kDevOverflow ? kNoMem : kCuda), std::string(what) + ": " + n);
     }
 }
 

@@ -17,6 +17,8 @@ from .api import (  # noqa: F401
     read_knn,
     reverse_merge,
     sanitize,
+    search,
+    search_entries,
     sort_rows,
     write_dataset,
     write_graph,
@@ -24,4 +26,4 @@ from .api import (  # noqa: F401
     write_knn_dists,
     write_npy,
 )
-from .synth import CONFIGS, generate, generate_shard, scaled  # noqa: F401
+from .synth import CONFIGS, generate, generate_queries, generate_shard, scaled  # noqa: F401

@@ -64,6 +64,7 @@ _SIGS = {
     "gta_prune": [_P, _I64, _I32, _I32, _P, _P],
     "gta_reverse_merge": [_P, _I64, _I32, _P, _P],
     "gta_reverse_merge_noalloc": [_P, _I64, _I32, _P, _P],
+    "gta_search": [ctypes.POINTER(gta_dataset), _P, _I64, _P, _I32, _P, _I32, _I32, _I32, _P, _P, _P],
     "gta_kmeans_sizes": [_I64, ctypes.POINTER(gta_bucket_params), ctypes.POINTER(_I64), ctypes.POINTER(_I64),
                          ctypes.POINTER(_U64)],
     "gta_sample_ids": [_I64, _I64, _U64, _P, _P],

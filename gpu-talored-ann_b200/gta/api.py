@@ -12,6 +12,7 @@ project root):
   merge_lists       resident_merge_kernel (bucket.cu:5025)
   sanitize          sanitize_to_uint32_inplace (optimize.cu:95)
   prune / reverse_merge   prune_windowed_core.hpp:190-263 / edge_chunk_accumulator.hpp:386-494
+  search            graph_search_single (bucketDemo/search.py:20-93)
 
 Device arrays are torch CUDA tensors (torch supplies device memory and the
 current stream only; every computation runs in libgta's own kernels).  Host
@@ -126,6 +127,49 @@ def optimize(knn, graph_degree: int):
     L.check(L.lib().gta_optimize(_ptr(knn), N, M, graph_degree, _ptr(out), 1 if dev else 0,
                                  _stream() if dev else ctypes.c_void_p(0)))
     return out
+
+
+# ---------------------------------------------------------------- graph search
+def search_entries(n: int, nq: int, num_entry: int = 4, seed: int = 42) -> np.ndarray:
+    """Entry points of the reference's search (bucketDemo/search.py:40-41 with the
+    generator of :163, called per query at :170-172): one numpy default_rng(seed) shared
+    by the queries in order,
+    ``np.unique(rng.integers(0, n, num_entry))`` per query; -1 pads a row."""
+    rng = np.random.default_rng(seed)
+    k = max(1, num_entry)
+    out = np.full((nq, k), -1, np.int32)
+    for i in range(nq):
+        u = np.unique(rng.integers(0, n, size=k, endpoint=False))
+        out[i, :u.size] = u
+    return out
+
+
+def search(base, graph, queries, topk: int = 10, ef: int = 200, num_entry: int = 4, seed: int = 42, entries=None):
+    """Best-first graph search of ``queries`` over ``graph`` (N x K ids) with the rule of
+    bucketDemo/search.py graph_search_single (its defaults: topk 10, ef 200, 4 random
+    entry points, seed 42).  ``base`` / ``queries`` / ``graph`` all on the device (torch)
+    or all on the host (numpy).  Returns (ids[nq, topk], dists[nq, topk])."""
+    dev = _is_dev(base)
+    n, d = base.shape
+    nq = queries.shape[0]
+    ef = max(ef, topk)
+    if entries is None:
+        entries = search_entries(n, nq, num_entry, seed)
+    if dev:
+        torch = _torch()
+        entries = torch.as_tensor(np.ascontiguousarray(entries, np.int32)).cuda()
+        graph = graph.contiguous()
+    else:
+        entries = np.ascontiguousarray(entries, np.int32)
+        graph = np.ascontiguousarray(graph).view(np.uint32) if graph.dtype.itemsize == 4 else \
+            np.ascontiguousarray(graph, np.uint32)
+    ids = _empty((nq, topk), "int32", dev)
+    dists = _empty((nq, topk), "float32", dev)
+    ds = _dataset(base)
+    L.check(L.lib().gta_search(ctypes.byref(ds), _ptr(queries), nq, _ptr(graph), graph.shape[1], _ptr(entries),
+                               entries.shape[1], topk, ef, _ptr(ids), _ptr(dists),
+                               _stream() if dev else ctypes.c_void_p(0)))
+    return ids, dists
 
 
 # ---------------------------------------------------------------- stages (device tensors)

@@ -87,3 +87,12 @@ def generate_shard(cfg: Config, shard: int, seed: int = 42, chunk: int = 1 << 20
     rng = np.random.default_rng([seed, shard])
     centres = _centres(cfg, rng)
     return _rows(cfg, centres, rng, chunk)
+
+
+def generate_queries(cfg: Config, nq: int, shard: int = 0, seed: int = 42) -> np.ndarray:
+    """``nq`` held-out rows drawn from the same mixture as ``generate_shard(cfg, shard, seed)``
+    (same centres, an independent row stream), for graph-search recall."""
+    rng = np.random.default_rng(seed if shard == 0 else [seed, shard])
+    centres = _centres(cfg, rng)
+    qcfg = Config(**{**cfg.__dict__, "n": nq})
+    return _rows(qcfg, centres, np.random.default_rng([seed, shard, 0x5EA4C4]), 1 << 20)

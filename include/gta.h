@@ -189,6 +189,25 @@ int gta_reverse_merge_noalloc(const uint32_t* pruned, int64_t n, int32_t k, uint
 int64_t gta_reverse_merge_noalloc_max_rows(void);
 int64_t gta_reverse_merge_noalloc_max_edges(void);
 
+/* ---------------------------------------------------------------- graph search */
+
+/* Best-first graph search of nq queries over `graph` (base->n x k_graph uint32
+ * ids): the rule of bucketDemo/search.py:20-93 graph_search_single -- the
+ * entry points of each query (n_entry per query, ascending, -1 = unused; the
+ * reference draws them with numpy's default_rng(42) and np.unique, see
+ * gta.search_entries) are visited in order, the (distance, id)-smallest
+ * candidate is expanded until its distance exceeds the worst of a full
+ * ef-entry best list, the best list is appended while short and otherwise
+ * its first maximum is replaced by a smaller distance.  Writes the topk
+ * nearest of the best list per query (ascending distance, ties by id; -1 / +inf
+ * padding).  Queries have base's dtype and d; base->on_device says whether all
+ * arrays are device (stream-ordered) or host (synchronous) memory.  One warp
+ * per query; 1 <= topk <= ef <= 256, d <= 1024.  Status 2 when a query visits
+ * more nodes than the per-query visited set holds (12 288): lower ef. */
+int gta_search(const gta_dataset* base, const void* queries, int64_t nq, const uint32_t* graph, int32_t k_graph,
+               const int32_t* entries, int32_t n_entry, int32_t topk, int32_t ef, int32_t* out_ids, float* out_dists,
+               void* stream);
+
 /* ---------------------------------------------------------------- shard stages
  * One rank's part of the multi-GPU build (the plan of the reference's
  * multi-GPU design: row-sharded k-means with all-reduced sums, buckets placed

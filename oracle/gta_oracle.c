@@ -442,3 +442,131 @@ ORC_API int orc_num_threads(void)
     return 1;
 #endif
 }
+
+/* ------------------------------------------------------------------ */
+/* graph search (bucketDemo/search.py:20-93 graph_search_single)      */
+/* ------------------------------------------------------------------ */
+/* The efSearch-style best-first search of the reference, per query:    */
+/* the given entry points (already drawn and de-duplicated, ascending:  */
+/* np.unique of rng.integers at :40-41) are visited in order; a min     */
+/* "heap" of (distance, id) candidates (heapq on tuples: :52-53) is     */
+/* expanded until the popped distance exceeds the worst of the best     */
+/* list once that holds ef entries (:54-57); the best list is an array  */
+/* in insertion order, appended while short and otherwise overwritten   */
+/* at the first position of its maximum when the new distance is       */
+/* smaller (:45-50, :73-80).  Neighbour ids outside [0, N) and visited  */
+/* ids are skipped (:62-67).  Output: the best list sorted by distance  */
+/* (ties by id), first topk, padded with -1 / +inf (:82-86).            */
+/* Distances: the exact fp32 chain over ascending dims (for 8-bit data  */
+/* every partial sum is an integer below 2^24, so the order of the      */
+/* reference's float32 dot is immaterial).                              */
+typedef struct { float d; uint32_t id; } orc_scand;
+
+static int cand_less(orc_scand a, orc_scand b) { return a.d < b.d || (a.d == b.d && a.id < b.id); }
+
+static void heap_push(orc_scand* h, int64_t* n, orc_scand c)
+{
+    int64_t i = (*n)++;
+    h[i] = c;
+    while (i > 0) {
+        int64_t p = (i - 1) / 2;
+        if (!cand_less(h[i], h[p])) break;
+        orc_scand t = h[i]; h[i] = h[p]; h[p] = t;
+        i = p;
+    }
+}
+
+static orc_scand heap_pop(orc_scand* h, int64_t* n)
+{
+    orc_scand top = h[0];
+    h[0] = h[--(*n)];
+    int64_t i = 0;
+    for (;;) {
+        int64_t l = 2 * i + 1, r = l + 1, m = i;
+        if (l < *n && cand_less(h[l], h[m])) m = l;
+        if (r < *n && cand_less(h[r], h[m])) m = r;
+        if (m == i) break;
+        orc_scand t = h[i]; h[i] = h[m]; h[m] = t;
+        i = m;
+    }
+    return top;
+}
+
+static void best_update(float* bd, uint32_t* bi, int32_t* bs, int32_t ef, float d, uint32_t id)
+{
+    if (*bs < ef) {
+        bd[*bs] = d;
+        bi[*bs] = id;
+        ++*bs;
+        return;
+    }
+    int32_t w = 0;
+    for (int32_t j = 1; j < ef; ++j)
+        if (bd[j] > bd[w]) w = j;
+    if (d < bd[w]) { bd[w] = d; bi[w] = id; }
+}
+
+static float best_worst(const float* bd, int32_t bs)
+{
+    float w = bd[0];
+    for (int32_t j = 1; j < bs; ++j)
+        if (bd[j] > w) w = bd[j];
+    return w;
+}
+
+static int cmp_best(const void* a, const void* b)
+{
+    const orc_scand* x = (const orc_scand*)a;
+    const orc_scand* y = (const orc_scand*)b;
+    if (x->d < y->d) return -1;
+    if (x->d > y->d) return 1;
+    return x->id < y->id ? -1 : (x->id > y->id);
+}
+
+/* base: N x d f32; graph: N x kg uint32; queries: nq x d f32; entries: nq x ne (ascending, -1 = unused). */
+ORC_API void orc_graph_search(const float* base, int64_t N, int32_t d, const uint32_t* graph, int32_t kg,
+                              const float* queries, int64_t nq, const int32_t* entries, int32_t ne, int32_t topk,
+                              int32_t ef, int32_t* out_ids, float* out_dists)
+{
+#pragma omp parallel for schedule(dynamic, 4)
+    for (int64_t q = 0; q < nq; ++q) {
+        const float* x = queries + q * d;
+        unsigned char* visited = (unsigned char*)calloc((size_t)N, 1);
+        orc_scand* heap = (orc_scand*)malloc(sizeof(orc_scand) * (size_t)(N + ne + 1));
+        float* bd = (float*)malloc(sizeof(float) * (size_t)ef);
+        uint32_t* bi = (uint32_t*)malloc(sizeof(uint32_t) * (size_t)ef);
+        int64_t hn = 0;
+        int32_t bs = 0;
+        for (int32_t e = 0; e < ne; ++e) {
+            const int32_t s = entries[q * ne + e];
+            if (s < 0 || (int64_t)s >= N || visited[s]) continue;
+            visited[s] = 1;
+            const float ds = exact_l2(x, base + (int64_t)s * d, d);
+            orc_scand c = {ds, (uint32_t)s};
+            heap_push(heap, &hn, c);
+            best_update(bd, bi, &bs, ef, ds, (uint32_t)s);
+        }
+        while (hn > 0) {
+            const orc_scand u = heap_pop(heap, &hn);
+            if (bs >= ef && u.d > best_worst(bd, bs)) break;
+            const uint32_t* nb = graph + (int64_t)u.id * kg;
+            for (int32_t j = 0; j < kg; ++j) {
+                const uint32_t v = nb[j];
+                if ((int64_t)v >= N || visited[v]) continue;
+                visited[v] = 1;
+                const float dv = exact_l2(x, base + (int64_t)v * d, d);
+                orc_scand c = {dv, v};
+                heap_push(heap, &hn, c);
+                best_update(bd, bi, &bs, ef, dv, v);
+            }
+        }
+        orc_scand* srt = (orc_scand*)malloc(sizeof(orc_scand) * (size_t)(bs > 0 ? bs : 1));
+        for (int32_t j = 0; j < bs; ++j) { srt[j].d = bd[j]; srt[j].id = bi[j]; }
+        qsort(srt, (size_t)bs, sizeof(orc_scand), cmp_best);
+        for (int32_t j = 0; j < topk; ++j) {
+            out_ids[q * topk + j] = j < bs ? (int32_t)srt[j].id : -1;
+            out_dists[q * topk + j] = j < bs ? srt[j].d : INFINITY;
+        }
+        free(srt); free(bi); free(bd); free(heap); free(visited);
+    }
+}

@@ -60,6 +60,8 @@ def lib():
         L.orc_sort_rows_l2.argtypes = [_P, _I32, _P, _I64, _I32, _P]
         L.orc_detour_counts.argtypes = [_P, _I64, _I32, _I64, _P]
         L.orc_prune.argtypes = [_P, _I64, _I32, _I32, _P]
+        L.orc_graph_search.argtypes = [_P, _I64, _I32, _P, _I32, _P, _I64, _P, _I32, _I32, _I32, _P, _P]
+        L.orc_graph_search.restype = None
         L.orc_reverse_merge.argtypes = [_P, _I64, _I32]
         L.orc_optimize.argtypes = [_P, _I64, _I32, _I32, _P]
         L.orc_merge_rev_row.argtypes = [_P, _P, ctypes.c_uint32, ctypes.c_uint32]
@@ -260,6 +262,33 @@ def optimize(knn_u32, K: int):
     rc = lib().orc_optimize(_p(g), g.shape[0], g.shape[1], K, _p(out))
     if rc != 0:
         raise ValueError(f"orc_optimize failed ({rc})")
+    return out
+
+
+def graph_search(base, graph, queries, entries, topk: int, ef: int):
+    """search.py:20-93 graph_search_single for every query, with the given entry
+    points (nq x ne, ascending, -1 unused): ids / distances (nq x topk)."""
+    base = _f32(base)
+    q = _f32(queries)
+    g = np.ascontiguousarray(graph, np.uint32)
+    e = np.ascontiguousarray(entries, np.int32)
+    nq = q.shape[0]
+    ids = np.empty((nq, topk), np.int32)
+    dist = np.empty((nq, topk), np.float32)
+    lib().orc_graph_search(_p(base), base.shape[0], base.shape[1], _p(g), g.shape[1], _p(q), nq, _p(e), e.shape[1],
+                           topk, ef, _p(ids), _p(dist))
+    return ids, dist
+
+
+def search_entries(n: int, nq: int, num_entry: int, seed: int = 42) -> np.ndarray:
+    """The entry points search.py draws (:40-41 with the generator of :163, called per query at :170-172): one
+    default_rng(seed) shared by the queries in order, np.unique per query; padded with -1."""
+    rng = np.random.default_rng(seed)
+    k = max(1, num_entry)
+    out = np.full((nq, k), -1, np.int32)
+    for i in range(nq):
+        u = np.unique(rng.integers(0, n, size=k, endpoint=False))
+        out[i, :u.size] = u
     return out
 
 

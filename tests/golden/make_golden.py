@@ -109,6 +109,30 @@ def make_python_fixtures():
     np.savez_compressed(os.path.join(HERE, "exact_knn.npz"), X=Xg, k=np.int32(10), ids=_as_int32_rows(gi), dists=gd)
 
 
+def make_search_fixture():
+    """search.py:20-93 graph_search_single on 8-bit data (exact float32 distances) over an
+    exact kNN graph, with the reference's own generator drawing the entry points."""
+    import search as rs  # the reference's module
+
+    rng = np.random.default_rng(11)
+    X = np.clip(np.rint(_mixture(rng, 3060, 24, 16, 18.0, 0.0, 255.0)), 0, 255).astype(np.uint8)
+    base, Q = X[:3000], X[3000:]
+    ids, _ = orc.exact_knn(base, np.arange(base.shape[0]), 13)
+    graph = np.ascontiguousarray(ids[:, 1:].astype(np.uint32))  # drop self (column 0)
+    topk, ef, ne = 10, 32, 4
+    r = np.random.default_rng(42)
+    out_i = np.full((Q.shape[0], topk), -1, np.int32)
+    out_d = np.full((Q.shape[0], topk), np.inf, np.float32)
+    bf, qf = base.astype(np.float32), Q.astype(np.float32)
+    for i in range(Q.shape[0]):
+        idx, dst = rs.graph_search_single(qf[i], bf, graph.astype(np.int64), topk, ef, r, num_entry=ne)
+        out_i[i, :idx.size] = idx
+        out_d[i, :dst.size] = dst
+    np.savez_compressed(os.path.join(HERE, "search.npz"), base=base, graph=graph, queries=Q,
+                        entries=orc.search_entries(base.shape[0], Q.shape[0], ne, 42), topk=np.int32(topk),
+                        ef=np.int32(ef), ids=out_i, dists=out_d)
+
+
 def _random_graph(rng, N, M):
     """M distinct non-self candidates per row (the reference test's generator shape)."""
     g = np.empty((N, M), np.uint32)
@@ -164,6 +188,7 @@ if __name__ == "__main__":
     orc.build()
     make_python_fixtures()
     make_cpp_fixtures()
+    make_search_fixture()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")

@@ -158,3 +158,22 @@ def test_kmeans_sample_is_stratified():
     assert ids.shape == (100,)
     assert np.all((ids >= np.arange(100) * 10) & (ids < np.arange(1, 101) * 10))
     np.testing.assert_array_equal(ids, orc.kmeans_sample_ids(1000, 100, seed=3))
+
+
+# ---------------------------------------------------------------- graph search
+def test_graph_search_matches_reference(golden):
+    # search.py:20-93 graph_search_single, run by tests/golden/make_golden.py with the reference's
+    # own generator; 8-bit data, so every distance is an exact float32 integer
+    f = golden("search.npz")
+    ids, dist = orc.graph_search(f["base"], f["graph"], f["queries"], f["entries"], int(f["topk"]), int(f["ef"]))
+    np.testing.assert_array_equal(dist, f["dists"])
+    np.testing.assert_array_equal(ids, f["ids"])
+
+
+def test_search_entries_follow_the_reference_generator():
+    e = orc.search_entries(1000, 5, 4, seed=42)
+    rng = np.random.default_rng(42)
+    for i in range(5):
+        u = np.unique(rng.integers(0, 1000, size=4, endpoint=False))
+        np.testing.assert_array_equal(e[i, :u.size], u)
+        assert (e[i, u.size:] == -1).all()
