@@ -442,7 +442,7 @@ def main():
             ds = L.gta_dataset(data=Xn.ctypes.data_as(ctypes.c_void_p), n=cfg.n, d=cfg.d,
                                dtype=L.GTA_U8 if cfg.dtype == "uint8" else L.GTA_F32, metric=0, on_device=0)
             bp = L.gta_bucket_params(n_buckets=cfg.n_buckets, kmeans_iters=cfg.kmeans_iters, knn_degree=cfg.knn_degree,
-                                     reserved0=0, kmeans_sample=cfg.kmeans_sample, seed=42, init_centroids=None,
+                                     rounds=1, kmeans_sample=cfg.kmeans_sample, seed=42, init_centroids=None,
                                      init_on_device=0, out_on_device=0, centroids_out=None, top2_out=None)
             p = L.gta_cagra_params(bucket=bp, graph_degree=cfg.graph_degree, reserved0=0)
             L.check(L.lib().gta_build_cagra(ctypes.byref(ds), ctypes.byref(p), gh.ctypes.data_as(ctypes.c_void_p), None))

@@ -1,0 +1,149 @@
+// bucket2: command-line front end of the bucketed kNN-graph build, with the
+// reference tool's options and outputs (bucketDemo/buildBucket/src/bucket.cu:9853
+// main, :9897-9954 options, :8545-8556 output subdirectory, :9755-9761 outputs).
+//
+//   bucket2 -i data.u8bin -o out --neighbors-m 64 --fused-optimize-degree 32 [--seed 42] [-t 1]
+//
+// writes out/k<knn-k>p<nprobe|knn-k>m<M>t<T>/ vector_knn.bin, vector_dists.bin (unless
+// --skip-dists), neighbors.npy (unless --skip-npy) and, with --fused-optimize-degree K,
+// final_graph.bin (sanitize + CAGRA prune + reverse edges, ids in the input order).
+// Bucketing is this library's: k-means over a sample, every point in its two nearest
+// buckets (--n-buckets, default N/3906, i.e. buckets of about 7 800 members). The
+// reference's memory / out-of-core / PQ / KMeans|| knobs are accepted and ignored.
+// Exit status: 0 ok, 1 error ("FATAL: ..." on stderr), like the reference.
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <filesystem>
+#include <string>
+#include <vector>
+
+#include "args.hpp"
+#include "gta.h"
+
+namespace {
+
+using Clock = std::chrono::steady_clock;
+
+double secs(Clock::time_point t0) { return std::chrono::duration<double>(Clock::now() - t0).count(); }
+
+void check(int rc, const char* what)
+{
+    if (rc != GTA_OK) throw std::runtime_error(std::string(what) + ": " + gta_last_error());
+}
+
+size_t elem_bytes(int32_t dtype) { return dtype == GTA_F32 ? 4 : 1; }
+
+int run(int argc, char** argv)
+{
+    const std::vector<cli::Opt> opts = {
+        {"input", 'i', false, "Input data file (.fbin/.bin/.u8bin/.i8bin)", ""},
+        {"output", 'o', false, "Output root directory", ""},
+        {"neighbors-m", 0, false, "Per-vector KNN neighbor count M (1..128)", "0"},
+        {"fused-optimize-degree", 0, false, "Prune + reverse edges to this degree, write final_graph.bin (0 = off)", "0"},
+        {"n-buckets", 0, false, "k-means buckets B (0 = N/3906)", "0"},
+        {"kmeans-iters", 0, false, "Lloyd iterations", "10"},
+        {"sample-rate", 0, false, "k-means sample fraction of N (default min(0.1, 1e7/N))", ""},
+        {"seed", 0, false, "Random seed", "42"},
+        {"iterations", 't', false, "Whole builds with seed+iter, lists dedupe-merged", "1"},
+        {"knn-k", 0, false, "Graph degree label of the output subdirectory", "32"},
+        {"nprobe", 0, false, "Output subdirectory label (0 = knn-k)", "0"},
+        {"skip-dists", 0, true, "Don't write vector_dists.bin", ""},
+        {"skip-npy", 0, true, "Don't write neighbors.npy", ""},
+        // accepted for drop-in compatibility, no effect on this build
+        {"cpu-limit", 0, false, "(ignored)", ""},
+        {"gpu-limit", 0, false, "(ignored)", ""},
+        {"bucket-vec-buffer", 0, false, "(ignored)", ""},
+        {"centroid-ratio", 0, false, "(ignored: buckets come from --n-buckets)", ""},
+        {"use-pq", 0, false, "(ignored)", ""},
+        {"kmeans-train-fraction", 0, false, "(ignored)", ""},
+        {"bucket-mem-mb", 0, false, "(ignored)", ""},
+        {"gpu-bucket-cache-mb", 0, false, "(ignored)", ""},
+        {"pq-bits-start", 0, false, "(ignored)", ""},
+        {"pq-bits-min", 0, false, "(ignored)", ""},
+        {"search-iters", 0, false, "(ignored)", ""},
+        {"order-window", 0, false, "(ignored)", ""},
+        {"cache-mb", 0, false, "(ignored)", ""},
+        {"out-of-core", 0, true, "(ignored)", ""},
+    };
+    cli::Args a("bucket2 (gta-b200)", opts);
+    if (!a.parse(argc, argv)) return 0;
+    const std::string input = a.required("input");
+    const std::string root = a.required("output");
+    const int M = static_cast<int>(a.i64("neighbors-m", 0));
+    const int K = static_cast<int>(a.i64("fused-optimize-degree", 0));
+    const int iters = static_cast<int>(a.i64("iterations", 1));
+    const int knn_k = static_cast<int>(a.i64("knn-k", 32));
+    const int nprobe = static_cast<int>(a.i64("nprobe", 0));
+    if (M < 1 || M > 128) throw std::runtime_error("--neighbors-m must be in [1, 128] (the kNN lists are the product)");
+    if (K < 0 || K > M) throw std::runtime_error("--fused-optimize-degree must be in [0, neighbors-m]");
+    if (iters < 1) throw std::runtime_error("iterations (" + std::to_string(iters) + ") must be >= 1");
+    if (nprobe > 256) throw std::runtime_error("nprobe exceeds MAX_NPROBE=256");
+
+    const auto t_all = Clock::now();
+    int64_t N = 0;
+    int32_t d = 0, dtype = 0;
+    check(gta_read_dataset_header(input.c_str(), &N, &d, &dtype), "read header");
+    std::printf("[main] %s: N=%lld d=%d dtype=%s\n", input.c_str(), static_cast<long long>(N), d,
+                dtype == GTA_F32 ? "f32" : dtype == GTA_U8 ? "u8" : "i8");
+    std::vector<uint8_t> X(static_cast<size_t>(N) * d * elem_bytes(dtype));
+    auto t0 = Clock::now();
+    check(gta_read_dataset(input.c_str(), 0, N, X.data()), "read dataset");
+    std::printf("=== Step 1: read dataset [%.3fs]\n", secs(t0));
+
+    int64_t B = a.i64("n-buckets", 0);
+    if (B <= 0) B = std::max<int64_t>(2, static_cast<int64_t>(std::llround(static_cast<double>(N) / 3906.0)));
+    int64_t sample = 0;
+    if (a.has("sample-rate")) sample = std::max<int64_t>(B, static_cast<int64_t>(a.f64("sample-rate", 0.1) * N));
+
+    const std::string dir = root + "/k" + std::to_string(knn_k) + "p" + std::to_string(nprobe > 0 ? nprobe : knn_k) +
+                            "m" + std::to_string(M) + "t" + std::to_string(iters);
+    std::filesystem::create_directories(dir);
+    std::printf("Output subdir: %s\n", dir.c_str());
+
+    gta_dataset ds{X.data(), N, d, dtype, GTA_L2, 0};
+    gta_bucket_params p{};
+    p.n_buckets = static_cast<int32_t>(B);
+    p.kmeans_iters = static_cast<int32_t>(a.i64("kmeans-iters", 10));
+    p.knn_degree = M;
+    p.rounds = iters;
+    p.kmeans_sample = sample;
+    p.seed = static_cast<uint64_t>(a.i64("seed", 42));
+    std::vector<int32_t> ids(static_cast<size_t>(N) * M);
+    std::vector<float> dists(static_cast<size_t>(N) * M);
+    t0 = Clock::now();
+    check(gta_build_bucket(&ds, &p, ids.data(), dists.data(), nullptr), "bucketed kNN build");
+    std::printf("=== Steps 2-6: k-means (B=%lld), top-2 buckets, per-bucket kNN (M=%d), merge, %d round(s) [%.3fs]\n",
+                static_cast<long long>(B), M, iters, secs(t0));
+
+    std::vector<uint32_t> graph;
+    if (K > 0) {
+        graph.resize(static_cast<size_t>(N) * K);
+        t0 = Clock::now();
+        check(gta_optimize_knn(nullptr, ids.data(), N, M, K, graph.data(), 0, nullptr), "optimize");
+        std::printf("=== fused optimize (prune + reverse edges to K=%d) [%.3fs]\n", K, secs(t0));
+    }
+
+    t0 = Clock::now();
+    check(gta_write_knn((dir + "/vector_knn.bin").c_str(), ids.data(), N, M), "write vector_knn.bin");
+    if (!a.flag("skip-dists"))
+        check(gta_write_knn_dists((dir + "/vector_dists.bin").c_str(), dists.data(), N, M), "write vector_dists.bin");
+    if (!a.flag("skip-npy"))
+        check(gta_write_npy_i64((dir + "/neighbors.npy").c_str(), ids.data(), N, M), "write neighbors.npy");
+    if (K > 0) check(gta_write_graph((dir + "/final_graph.bin").c_str(), graph.data(), N, K), "write final_graph.bin");
+    std::printf("=== write outputs [%.3fs]\n", secs(t0));
+    std::printf("Total: %.3fs\n", secs(t_all));
+    return 0;
+}
+
+}  // namespace
+
+int main(int argc, char** argv)
+{
+    try {
+        return run(argc, argv);
+    } catch (const std::exception& e) {
+        std::fprintf(stderr, "FATAL: %s\n", e.what());
+        return 1;
+    }
+}

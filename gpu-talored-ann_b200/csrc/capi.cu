@@ -319,7 +319,7 @@ struct BucketOut {
     int32_t* top2;     // device [N x 2] or null
 };
 
-void build_bucket_impl(const gta_dataset& ds, const gta_bucket_params& p, const BucketOut& o, cudaStream_t st)
+void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const BucketOut& o, cudaStream_t st)
 {
     const int64_t N = ds.n;
     const int d = ds.d;
@@ -405,6 +405,47 @@ void build_bucket_impl(const gta_dataset& ds, const gta_bucket_params& p, const 
     }
     merge_memberships(lid.get(), ldist.get(), mem_row.get(), N, M, o.ids, o.dists, st);
     check_device_error(err.get(), st, "build_bucket");
+}
+
+// bucket2 -t: rounds with seeds seed, seed+1, ... (bucket.cu:9938-9940); each round's lists merged
+// into the running lists with the resident merge rule (running first on equal distance, ids already
+// present skipped; bucket.cu:5025-5131).  Centroids / top-2 are those of the last round.
+void build_bucket_impl(const gta_dataset& ds, const gta_bucket_params& p, const BucketOut& o, cudaStream_t st)
+{
+    const int rounds = p.rounds > 1 ? p.rounds : 1;
+    GTA_REQUIRE(p.rounds >= 0, kInvalid, "build_bucket: negative rounds");
+    if (rounds == 1) {
+        build_bucket_round(ds, p, o, st);
+        return;
+    }
+    const int64_t N = ds.n;
+    const int M = p.knn_degree;
+    GTA_REQUIRE(ds.data && N >= 2 && M >= 1 && M <= 128, kInvalid, "build_bucket: bad dataset or knn_degree");
+    gta_dataset dd = ds;
+    DevBuf<uint8_t> xhold;
+    if (!ds.on_device) {  // one upload for all rounds
+        const size_t xbytes = static_cast<size_t>(N) * ds.d * elem_size(ds.dtype);
+        xhold = DevBuf<uint8_t>(xbytes, st);
+        GTA_CUDA(cudaMemcpyAsync(xhold.get(), ds.data, xbytes, cudaMemcpyHostToDevice, st));
+        dd.data = xhold.get();
+        dd.on_device = 1;
+    }
+    const size_t nm = static_cast<size_t>(N) * M;
+    DevBuf<int32_t> new_ids(nm, st), run_ids(nm, st);
+    DevBuf<float> new_d(nm, st), run_d(nm, st);
+    for (int r = 0; r < rounds; ++r) {
+        gta_bucket_params pr = p;
+        pr.rounds = 1;
+        pr.seed = p.seed + static_cast<uint64_t>(r);
+        const bool last = r == rounds - 1;
+        BucketOut ro{r == 0 ? o.ids : new_ids.get(), r == 0 ? o.dists : new_d.get(), last ? o.centroids : nullptr,
+                     last ? o.top2 : nullptr};
+        build_bucket_round(dd, pr, ro, st);
+        if (r == 0) continue;
+        GTA_CUDA(cudaMemcpyAsync(run_ids.get(), o.ids, sizeof(int32_t) * nm, cudaMemcpyDeviceToDevice, st));
+        GTA_CUDA(cudaMemcpyAsync(run_d.get(), o.dists, sizeof(float) * nm, cudaMemcpyDeviceToDevice, st));
+        merge_lists(run_ids.get(), run_d.get(), new_ids.get(), new_d.get(), N, M, o.ids, o.dists, st);
+    }
 }
 
 void optimize_impl(const uint32_t* knn_dev, int64_t n, int m, int k, uint32_t* graph_dev, cudaStream_t st,
@@ -559,6 +600,17 @@ int gta_profile_get(int32_t i, char* name, int32_t name_len, float* ms, double* 
 }
 const char* gta_version(void) { return "gta-b200 0.1 (sm_100a)"; }
 
+int gta_device_memory(int64_t* free_bytes, int64_t* total_bytes)
+{
+    return guard([&] {
+        GTA_REQUIRE(free_bytes && total_bytes, kInvalid, "gta_device_memory: null argument");
+        size_t f = 0, t = 0;
+        GTA_CUDA(cudaMemGetInfo(&f, &t));
+        *free_bytes = static_cast<int64_t>(f);
+        *total_bytes = static_cast<int64_t>(t);
+    });
+}
+
 int gta_build_bucket(const gta_dataset* ds, const gta_bucket_params* p, int32_t* knn_ids, float* knn_dists, void* stream)
 {
     return guard([&] {
@@ -613,6 +665,60 @@ int gta_optimize(const uint32_t* knn, int64_t n, int32_t m, int32_t k, uint32_t*
             GTA_CUDA(cudaMemcpyAsync(kd.get(), knn, sizeof(uint32_t) * n * m, cudaMemcpyHostToDevice, st));
             optimize_impl(kd.get(), n, m, k, gd.get(), st);
             GTA_CUDA(cudaMemcpyAsync(graph, gd.get(), sizeof(uint32_t) * n * k, cudaMemcpyDeviceToHost, st));
+            GTA_CUDA(cudaStreamSynchronize(st));
+        }
+    });
+}
+
+int gta_optimize_knn(const gta_dataset* ds, const int32_t* knn, int64_t n, int32_t m, int32_t k, uint32_t* graph,
+                     int32_t on_device, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(knn && graph && n >= 2 && m >= 2 && m <= 128 && k >= 1 && k <= m && n < (1ll << 31), kInvalid,
+                    "gta_optimize_knn: need knn, graph, 2 <= n < 2^31, 1 <= K <= M <= 128");
+        GTA_REQUIRE(!ds || (ds->data && ds->n == n && ds->d >= 1 && (ds->on_device != 0) == (on_device != 0) &&
+                            (ds->dtype == GTA_F32 || ds->dtype == GTA_U8 || ds->dtype == GTA_I8)),
+                    kInvalid, "gta_optimize_knn: dataset must match the graph's N and placement");
+        cudaStream_t st = S(stream);
+        const size_t nm = static_cast<size_t>(n) * m;
+        DevBuf<int32_t> kh;
+        const int32_t* kd = knn;
+        if (!on_device) {
+            kh = DevBuf<int32_t>(nm, st);
+            GTA_CUDA(cudaMemcpyAsync(kh.get(), knn, sizeof(int32_t) * nm, cudaMemcpyHostToDevice, st));
+            kd = kh.get();
+        }
+        DevBuf<uint32_t> san(nm, st);
+        sanitize(kd, n, m, san.get(), st);
+        kh.release();
+        if (ds) {  // stable sort of every sanitized row by exact L2 to its point
+            const int d = ds->d;
+            const int d32 = pad_dim(d, kElemF32);
+            const size_t xbytes = static_cast<size_t>(n) * d * elem_size(ds->dtype);
+            DevBuf<uint8_t> xh;
+            const void* X = ds->data;
+            if (!on_device) {
+                xh = DevBuf<uint8_t>(xbytes, st);
+                GTA_CUDA(cudaMemcpyAsync(xh.get(), ds->data, xbytes, cudaMemcpyHostToDevice, st));
+                X = xh.get();
+            }
+            DevBuf<float> Xp(static_cast<size_t>(n) * d32, st);
+            convert_rows(X, ds->dtype, d, nullptr, n, Xp.get(), kElemF32, d32, nullptr, st);
+            xh.release();
+            DevBuf<int32_t> sorted(nm, st);
+            sort_rows_l2(Xp.get(), d, d32, reinterpret_cast<const int32_t*>(san.get()), n, m, sorted.get(), st);
+            GTA_CUDA(cudaMemcpyAsync(san.get(), sorted.get(), sizeof(uint32_t) * nm, cudaMemcpyDeviceToDevice, st));
+        }
+        DevBuf<uint32_t> gd;
+        uint32_t* gout = graph;
+        if (!on_device) {
+            gd = DevBuf<uint32_t>(static_cast<size_t>(n) * k, st);
+            gout = gd.get();
+        }
+        optimize_impl(san.get(), n, m, k, gout, st);
+        if (!on_device) {
+            GTA_CUDA(cudaMemcpyAsync(graph, gout, sizeof(uint32_t) * n * k, cudaMemcpyDeviceToHost, st));
             GTA_CUDA(cudaStreamSynchronize(st));
         }
     });

@@ -37,7 +37,7 @@ class gta_dataset(ctypes.Structure):
 
 class gta_bucket_params(ctypes.Structure):
     _fields_ = [
-        ("n_buckets", _I32), ("kmeans_iters", _I32), ("knn_degree", _I32), ("reserved0", _I32),
+        ("n_buckets", _I32), ("kmeans_iters", _I32), ("knn_degree", _I32), ("rounds", _I32),
         ("kmeans_sample", _I64), ("seed", _U64),
         ("init_centroids", _P), ("init_on_device", _I32), ("out_on_device", _I32),
         ("centroids_out", _P), ("top2_out", _P),
@@ -52,6 +52,7 @@ _SIGS = {
     "gta_build_bucket": [ctypes.POINTER(gta_dataset), ctypes.POINTER(gta_bucket_params), _P, _P, _P],
     "gta_optimize": [_P, _I64, _I32, _I32, _P, _I32, _P],
     "gta_build_cagra": [ctypes.POINTER(gta_dataset), ctypes.POINTER(gta_cagra_params), _P, _P],
+    "gta_optimize_knn": [ctypes.POINTER(gta_dataset), _P, _I64, _I32, _I32, _P, _I32, _P],
     "gta_kmeans_fit": [_P, _I64, _I32, _P, _I32, _I32, _P, _P],
     "gta_kmeans_init": [_P, _I64, _I32, _I32, _U64, _P, _P],
     "gta_assign_topk": [_P, _I64, _I32, _P, _I32, _I32, _P, _P, _P],
@@ -89,6 +90,7 @@ _SIGS = {
     "gta_write_npy_i64": [ctypes.c_char_p, _P, _I64, _I32],
     "gta_profile_enable": [_I32],
     "gta_release_workspace": [],
+    "gta_device_memory": [ctypes.POINTER(_I64), ctypes.POINTER(_I64)],
     "gta_profile_get": [_I32, ctypes.c_char_p, _I32, ctypes.POINTER(ctypes.c_float), ctypes.POINTER(ctypes.c_double)],
     "gta_profile_counters": [_I32, ctypes.POINTER(ctypes.c_double), _I32],
 }

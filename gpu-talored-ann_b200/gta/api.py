@@ -74,9 +74,10 @@ def _dataset(X, metric: str = "l2") -> L.gta_dataset:
                          metric=L.GTA_IP if metric == "ip" else L.GTA_L2, on_device=1 if _is_dev(X) else 0)
 
 
-def _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, init_centroids, dev, cent_out, top2_out):
+def _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, init_centroids, dev, cent_out, top2_out,
+                   rounds=1):
     return L.gta_bucket_params(
-        n_buckets=n_buckets, kmeans_iters=kmeans_iters, knn_degree=knn_degree, reserved0=0,
+        n_buckets=n_buckets, kmeans_iters=kmeans_iters, knn_degree=knn_degree, rounds=rounds,
         kmeans_sample=kmeans_sample, seed=seed, init_centroids=_ptr(init_centroids),
         init_on_device=1 if (init_centroids is not None and _is_dev(init_centroids)) else 0,
         out_on_device=1 if dev else 0, centroids_out=_ptr(cent_out), top2_out=_ptr(top2_out))
@@ -84,11 +85,14 @@ def _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, ini
 
 # ---------------------------------------------------------------- pipeline
 def build_bucket(X, n_buckets: int, knn_degree: int = 64, kmeans_iters: int = 10, kmeans_sample: int = 0,
-                 seed: int = 42, init_centroids=None, metric: str = "l2", with_extras: bool = False):
+                 seed: int = 42, init_centroids=None, metric: str = "l2", with_extras: bool = False,
+                 rounds: int = 1):
     """Bucketed kNN graph of X (N x d, float32 / uint8 / int8; torch CUDA tensor or numpy).
 
     Returns (ids[N, M] int32, dists[N, M] float32) on X's side (device or host);
     with ``with_extras`` also the final centroids (B x d) and top-2 buckets (N x 2).
+    ``rounds`` > 1 repeats the build with seeds seed+1, ... and merges each round's
+    lists into the running ones (bucket2 ``-t``).
     """
     dev = _is_dev(X)
     N, d = X.shape
@@ -97,7 +101,8 @@ def build_bucket(X, n_buckets: int, knn_degree: int = 64, kmeans_iters: int = 10
     cent = _empty((n_buckets, d), "float32", dev) if with_extras else None
     top2 = _empty((N, 2), "int32", dev) if with_extras else None
     ds = _dataset(X, metric)
-    p = _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, init_centroids, dev, cent, top2)
+    p = _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, init_centroids, dev, cent, top2,
+                       rounds)
     L.check(L.lib().gta_build_bucket(ctypes.byref(ds), ctypes.byref(p), _ptr(ids), _ptr(dists),
                                      _stream() if dev else ctypes.c_void_p(0)))
     if with_extras:
@@ -106,13 +111,14 @@ def build_bucket(X, n_buckets: int, knn_degree: int = 64, kmeans_iters: int = 10
 
 
 def build_cagra(X, n_buckets: int, knn_degree: int = 64, graph_degree: int = 32, kmeans_iters: int = 10,
-                kmeans_sample: int = 0, seed: int = 42, init_centroids=None, metric: str = "l2"):
+                kmeans_sample: int = 0, seed: int = 42, init_centroids=None, metric: str = "l2", rounds: int = 1):
     """Whole build: bucketed kNN (degree M), sanitize, CAGRA optimize -> graph[N, K] uint32."""
     dev = _is_dev(X)
     N = X.shape[0]
     graph = _empty((N, graph_degree), "uint32" if not dev else "int32", dev)
     ds = _dataset(X, metric)
-    bp = _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, init_centroids, dev, None, None)
+    bp = _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, init_centroids, dev, None, None,
+                        rounds)
     p = L.gta_cagra_params(bucket=bp, graph_degree=graph_degree, reserved0=0)
     L.check(L.lib().gta_build_cagra(ctypes.byref(ds), ctypes.byref(p), _ptr(graph),
                                     _stream() if dev else ctypes.c_void_p(0)))
@@ -126,6 +132,19 @@ def optimize(knn, graph_degree: int):
     out = _empty((N, graph_degree), "int32" if dev else "uint32", dev)
     L.check(L.lib().gta_optimize(_ptr(knn), N, M, graph_degree, _ptr(out), 1 if dev else 0,
                                  _stream() if dev else ctypes.c_void_p(0)))
+    return out
+
+
+def optimize_knn(knn, graph_degree: int, X=None):
+    """The optimize tool (optimize.cu main): sanitize an int32 kNN graph (-1 padding), sort each
+    row by exact L2 to its point when ``X`` is given (else the rows must already be ascending:
+    ``--skip-sort``), prune + reverse edges -> graph[N, K] uint32 (int32 view on the device)."""
+    dev = _is_dev(knn)
+    N, M = knn.shape
+    out = _empty((N, graph_degree), "int32" if dev else "uint32", dev)
+    ds = _dataset(X) if X is not None else None
+    L.check(L.lib().gta_optimize_knn(ctypes.byref(ds) if ds is not None else None, _ptr(knn), N, M, graph_degree,
+                                     _ptr(out), 1 if dev else 0, _stream() if dev else ctypes.c_void_p(0)))
     return out
 
 

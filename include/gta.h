@@ -65,7 +65,8 @@ typedef struct {
     int32_t n_buckets;      /* B: k-means centroids = buckets */
     int32_t kmeans_iters;   /* Lloyd iterations */
     int32_t knn_degree;     /* M: intermediate kNN degree (<= 128) */
-    int32_t reserved0;
+    int32_t rounds;         /* bucket2 -t: whole builds with seeds seed, seed+1, ..., each
+                               round's lists merged into the running lists (0 or 1: one round) */
     int64_t kmeans_sample;  /* points used by k-means; 0 = min(0.1, 1e7/N) of N */
     uint64_t seed;
     const float* init_centroids; /* optional B x d initial centroids (skips k-means++) */
@@ -99,6 +100,17 @@ int gta_build_bucket(const gta_dataset* ds, const gta_bucket_params* p, int32_t*
  * (bucketDemo/buildBucket/src/optimize.cu:396, bucket.cu:8470). */
 int gta_optimize(const uint32_t* knn, int64_t n, int32_t m, int32_t k, uint32_t* graph, int32_t on_device,
                  void* stream);
+
+/* The optimize tool's steps on an int32 kNN graph (-1 padding): sanitize, then
+ * (when ds is non-NULL) the stable per-row sort by exact L2 distance to the
+ * row's point, then gta_optimize's prune + reverse edges -> graph[N x K].
+ * ds == NULL is --skip-sort (rows already ascending, e.g. bucket2's lists).
+ * on_device says where knn and graph live (and must equal ds->on_device).
+ * Replaces optimize's main, Steps 2-4 (bucketDemo/buildBucket/src/optimize.cu:
+ * sanitize_to_uint32_inplace :95-133, sort_knn_graph_host, helpers::optimize
+ * :396) and the first half of bucket2's fused_optimize_translate (bucket.cu:8434). */
+int gta_optimize_knn(const gta_dataset* ds, const int32_t* knn, int64_t n, int32_t m, int32_t k, uint32_t* graph,
+                     int32_t on_device, void* stream);
 
 /* Whole build: gta_build_bucket, sanitize, gta_optimize -> graph[N x K]
  * (uint32).  Replaces bucket2 --fused-optimize-degree
@@ -312,6 +324,9 @@ int gta_profile_counters(int32_t i, double* out, int32_t n);
 long long gta_launch_count(void);
 
 /* ---------------------------------------------------------------- misc */
+/* Free and total memory of the current device (bytes), for callers' fit checks
+ * (the optimize tool's --gpu-fit-margin test, optimize.cu:243-251). */
+int gta_device_memory(int64_t* free_bytes, int64_t* total_bytes);
 /* Free the per-(device, stream) workspaces (synchronizes those streams). */
 int gta_release_workspace(void);
 const char* gta_last_error(void);

@@ -133,6 +133,23 @@ def make_search_fixture():
                         ef=np.int32(ef), ids=out_i, dists=out_d)
 
 
+def make_eval_fixture():
+    """search.py:95-127 recall_vs_gt on random predictions with -1 padding, duplicates
+    and partial hits, for the evaluation front end's recall figures."""
+    import search as rs  # the reference's module
+
+    rng = np.random.default_rng(5)
+    nq, topk, k_gt = 200, 10, 100
+    gt = np.stack([rng.choice(1000, k_gt, replace=False) for _ in range(nq)]).astype(np.int32)
+    pred = np.where(rng.random((nq, topk)) < 0.6, gt[:, :topk], rng.integers(0, 1000, (nq, topk))).astype(np.int64)
+    pred[rng.random((nq, topk)) < 0.05] = -1
+    pred[::17, 3] = pred[::17, 2]  # duplicate ids in a row
+    out = {"pred": pred, "gt": gt, "topk": np.int32(topk)}
+    out["recall"] = np.array(rs.recall_vs_gt(pred, gt, topk), np.float64)
+    out["recall_k5"] = np.array(rs.recall_vs_gt(pred, gt, 5), np.float64)
+    np.savez_compressed(os.path.join(HERE, "eval_recall.npz"), **out)
+
+
 def _random_graph(rng, N, M):
     """M distinct non-self candidates per row (the reference test's generator shape)."""
     g = np.empty((N, M), np.uint32)
@@ -185,10 +202,17 @@ def make_cpp_fixtures():
 
 
 if __name__ == "__main__":
+    # `python make_golden.py [python] [cpp] [search] [eval]`: the named fixture groups (default all)
+    want = set(sys.argv[1:]) or {"python", "cpp", "search", "eval"}
     orc.build()
-    make_python_fixtures()
-    make_cpp_fixtures()
-    make_search_fixture()
+    if "python" in want:
+        make_python_fixtures()
+    if "cpp" in want:
+        make_cpp_fixtures()
+    if "search" in want:
+        make_search_fixture()
+    if "eval" in want:
+        make_eval_fixture()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")

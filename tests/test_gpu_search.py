@@ -47,3 +47,33 @@ def test_search_rejects_bad_arguments():
     with pytest.raises(gta.GtaError) as e:
         gta.search(b, g, b[:4], topk=10, ef=300)
     assert e.value.code == L.GTA_EINVAL
+
+
+def test_eval_command_line(golden, tmp_path):
+    """python -m gta.eval search over files: the recall lines of the reference's search.py
+    for the fixture's queries (their results are the reference's own)."""
+    import os
+    import subprocess
+    import sys
+
+    from gta import eval as ev
+
+    f = golden("search.npz")
+    gta.write_dataset(str(tmp_path / "base.u8bin"), f["base"])
+    gta.write_dataset(str(tmp_path / "query.u8bin"), f["queries"])
+    np.save(tmp_path / "index.npy", f["graph"].astype(np.int64))
+    dd = ((f["queries"][:, None, :].astype(np.int64) - f["base"][None].astype(np.int64)) ** 2).sum(-1)
+    gt = np.argsort(dd, axis=1, kind="stable")[:, :10]  # exact integers: ties by id
+    with open(tmp_path / "gt.ibin", "wb") as fh:
+        np.array(gt.shape, np.int32).tofile(fh)
+        gt.astype(np.int32).tofile(fh)
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, PYTHONPATH=os.path.join(root, "gpu-talored-ann_b200"))
+    r = subprocess.run([sys.executable, "-m", "gta.eval", "search", "--base", str(tmp_path / "base.u8bin"),
+                        "--query", str(tmp_path / "query.u8bin"), "--index", str(tmp_path / "index.npy"),
+                        "--gt", str(tmp_path / "gt.ibin"), "--topk", "10", "--ef", str(int(f["ef"])),
+                        "--num-entry", "4"], capture_output=True, text=True, timeout=300, env=env)
+    assert r.returncode == 0, r.stderr
+    want = ev.recall_vs_gt(f["ids"].astype(np.int64), gt, 10)
+    assert f"Recall@10 (recall mean overlap): {want[2]:.6f}" in r.stdout, r.stdout
+    assert f"Recall@10 (hit GT[:,0])         : {want[0]:.6f}" in r.stdout, r.stdout
