@@ -4,13 +4,22 @@
 //
 //   bucket2 -i data.u8bin -o out --neighbors-m 64 --fused-optimize-degree 32 [--seed 42] [-t 1]
 //
-// writes out/k<knn-k>p<nprobe|knn-k>m<M>t<T>/ vector_knn.bin, vector_dists.bin (unless
-// --skip-dists), neighbors.npy (unless --skip-npy) and, with --fused-optimize-degree K,
-// final_graph.bin (sanitize + CAGRA prune + reverse edges, ids in the input order).
+// writes into out/k<knn-k>p<nprobe|knn-k>m<M>t<T>/ what the reference's GPU-resident path
+// writes: the bucket-contiguous renumbering of the points (bucket.cu:9253-9456):
+// data_reordered.<ext>, inverse_perm.bin (uint32[N], new -> old), bucket_offsets.bin (int32 B,
+// uint32[B+1]), bucket_process_order.bin (int32 B, int32[B]), centroid_knn.bin (int64 B,
+// int32 K, uint32[B*K]); then, in the reordered id space, vector_knn.bin, vector_dists.bin
+// (unless --skip-dists) and neighbors.npy (unless --skip-npy); and with
+// --fused-optimize-degree K, final_graph.bin: sanitize + CAGRA prune + reverse edges in the
+// reordered space, translated back to the input order (bucket.cu:8434-8480).
 // Bucketing is this library's: k-means over a sample, every point in its two nearest
-// buckets (--n-buckets, default N/3906, i.e. buckets of about 7 800 members). The
-// reference's memory / out-of-core / PQ / KMeans|| knobs are accepted and ignored.
+// buckets (--n-buckets, default N/3906, i.e. buckets of about 7 800 members); the renumbering
+// groups points by their nearest bucket, buckets in the greedy order over the centroid kNN
+// graph (--knn-k neighbours, --order-window).  The kNN lists are built in the input order and
+// renumbered afterwards, so equal distances stay ordered by input id.  The reference's memory /
+// out-of-core / PQ / KMeans|| knobs are accepted and ignored.
 // Exit status: 0 ok, 1 error ("FATAL: ..." on stderr), like the reference.
+#include <algorithm>
 #include <chrono>
 #include <cmath>
 #include <cstdio>
@@ -34,6 +43,16 @@ void check(int rc, const char* what)
 
 size_t elem_bytes(int32_t dtype) { return dtype == GTA_F32 ? 4 : 1; }
 
+// int32 count, then the values (bucket_offsets.bin / bucket_process_order.bin, graph_io.hpp:195-227)
+template <typename T>
+void write_counted(const char* path, int32_t count, const T* v, size_t n)
+{
+    FILE* f = std::fopen(path, "wb");
+    if (!f) throw std::runtime_error(std::string("cannot open for writing: ") + path);
+    const bool ok = std::fwrite(&count, sizeof(count), 1, f) == 1 && std::fwrite(v, sizeof(T), n, f) == n;
+    if (std::fclose(f) != 0 || !ok) throw std::runtime_error(std::string("write failed: ") + path);
+}
+
 int run(int argc, char** argv)
 {
     const std::vector<cli::Opt> opts = {
@@ -48,6 +67,7 @@ int run(int argc, char** argv)
         {"iterations", 't', false, "Whole builds with seed+iter, lists dedupe-merged", "1"},
         {"knn-k", 0, false, "Graph degree label of the output subdirectory", "32"},
         {"nprobe", 0, false, "Output subdirectory label (0 = knn-k)", "0"},
+        {"order-window", 0, false, "Window of the bucket processing order (0 = max(4 knn-k, 16))", "0"},
         {"skip-dists", 0, true, "Don't write vector_dists.bin", ""},
         {"skip-npy", 0, true, "Don't write neighbors.npy", ""},
         // accepted for drop-in compatibility, no effect on this build
@@ -62,7 +82,6 @@ int run(int argc, char** argv)
         {"pq-bits-start", 0, false, "(ignored)", ""},
         {"pq-bits-min", 0, false, "(ignored)", ""},
         {"search-iters", 0, false, "(ignored)", ""},
-        {"order-window", 0, false, "(ignored)", ""},
         {"cache-mb", 0, false, "(ignored)", ""},
         {"out-of-core", 0, true, "(ignored)", ""},
     };
@@ -111,25 +130,65 @@ int run(int argc, char** argv)
     p.seed = static_cast<uint64_t>(a.i64("seed", 42));
     std::vector<int32_t> ids(static_cast<size_t>(N) * M);
     std::vector<float> dists(static_cast<size_t>(N) * M);
+    std::vector<float> cent(static_cast<size_t>(B) * d);
+    std::vector<int32_t> top2(static_cast<size_t>(N) * 2);
+    p.centroids_out = cent.data();
+    p.top2_out = top2.data();
     t0 = Clock::now();
     check(gta_build_bucket(&ds, &p, ids.data(), dists.data(), nullptr), "bucketed kNN build");
     std::printf("=== Steps 2-6: k-means (B=%lld), top-2 buckets, per-bucket kNN (M=%d), merge, %d round(s) [%.3fs]\n",
                 static_cast<long long>(B), M, iters, secs(t0));
 
+    // bucket-contiguous renumbering: order of the buckets, new ids, reordered rows and lists
+    t0 = Clock::now();
+    const int ck = static_cast<int>(std::min<int64_t>({static_cast<int64_t>(knn_k), B - 1, 127}));
+    std::vector<int32_t> order(static_cast<size_t>(B)), cknn(static_cast<size_t>(B) * ck);
+    check(gta_bucket_order(cent.data(), static_cast<int32_t>(B), d, ck, static_cast<int32_t>(a.i64("order-window", 0)),
+                           order.data(), cknn.data(), 0, nullptr),
+          "bucket order");
+    std::vector<uint32_t> inv(static_cast<size_t>(N));
+    std::vector<int64_t> offsets(static_cast<size_t>(B) + 1);
+    check(gta_bucket_reorder(top2.data(), N, 2, static_cast<int32_t>(B), order.data(), inv.data(), offsets.data(), 0,
+                             nullptr),
+          "bucket reorder");
+    std::vector<uint8_t> Xr(X.size());
+    check(gta_permute_rows(X.data(), N, static_cast<int64_t>(d) * static_cast<int64_t>(elem_bytes(dtype)), inv.data(),
+                           Xr.data(), 0, nullptr),
+          "reorder dataset");
+    std::vector<int32_t> ids_new(ids.size());
+    std::vector<float> dists_new(dists.size());
+    check(gta_permute_graph(ids.data(), N, M, inv.data(), 0, 1, ids_new.data(), 0, nullptr), "renumber kNN lists");
+    check(gta_permute_rows(dists.data(), N, 4ll * M, inv.data(), dists_new.data(), 0, nullptr), "reorder distances");
+    std::printf("=== Step 4.5: bucket order (centroid kNN k=%d) + renumbering [%.3fs]\n", ck, secs(t0));
+
     std::vector<uint32_t> graph;
     if (K > 0) {
         graph.resize(static_cast<size_t>(N) * K);
+        std::vector<uint32_t> graph_new(graph.size());
         t0 = Clock::now();
-        check(gta_optimize_knn(nullptr, ids.data(), N, M, K, graph.data(), 0, nullptr), "optimize");
-        std::printf("=== fused optimize (prune + reverse edges to K=%d) [%.3fs]\n", K, secs(t0));
+        check(gta_optimize_knn(nullptr, ids_new.data(), N, M, K, graph_new.data(), 0, nullptr), "optimize");
+        check(gta_permute_graph(reinterpret_cast<const int32_t*>(graph_new.data()), N, K, inv.data(), 1, 0,
+                                reinterpret_cast<int32_t*>(graph.data()), 0, nullptr),
+              "translate ids");
+        std::printf("=== fused optimize (prune + reverse edges to K=%d) + translate ids [%.3fs]\n", K, secs(t0));
     }
 
     t0 = Clock::now();
-    check(gta_write_knn((dir + "/vector_knn.bin").c_str(), ids.data(), N, M), "write vector_knn.bin");
+    const std::string ext = std::filesystem::path(input).extension().string();
+    check(gta_write_dataset((dir + "/data_reordered" + ext).c_str(), Xr.data(), N, d, dtype), "write data_reordered");
+    check(gta_write_u32((dir + "/inverse_perm.bin").c_str(), inv.data(), N), "write inverse_perm.bin");
+    {
+        std::vector<uint32_t> off32(offsets.begin(), offsets.end());
+        write_counted((dir + "/bucket_offsets.bin").c_str(), static_cast<int32_t>(B), off32.data(), off32.size());
+        write_counted((dir + "/bucket_process_order.bin").c_str(), static_cast<int32_t>(B), order.data(), order.size());
+    }
+    check(gta_write_graph((dir + "/centroid_knn.bin").c_str(), reinterpret_cast<const uint32_t*>(cknn.data()), B, ck),
+          "write centroid_knn.bin");
+    check(gta_write_knn((dir + "/vector_knn.bin").c_str(), ids_new.data(), N, M), "write vector_knn.bin");
     if (!a.flag("skip-dists"))
-        check(gta_write_knn_dists((dir + "/vector_dists.bin").c_str(), dists.data(), N, M), "write vector_dists.bin");
+        check(gta_write_knn_dists((dir + "/vector_dists.bin").c_str(), dists_new.data(), N, M), "write vector_dists.bin");
     if (!a.flag("skip-npy"))
-        check(gta_write_npy_i64((dir + "/neighbors.npy").c_str(), ids.data(), N, M), "write neighbors.npy");
+        check(gta_write_npy_i64((dir + "/neighbors.npy").c_str(), ids_new.data(), N, M), "write neighbors.npy");
     if (K > 0) check(gta_write_graph((dir + "/final_graph.bin").c_str(), graph.data(), N, K), "write final_graph.bin");
     std::printf("=== write outputs [%.3fs]\n", secs(t0));
     std::printf("Total: %.3fs\n", secs(t_all));

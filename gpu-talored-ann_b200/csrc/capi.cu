@@ -520,6 +520,64 @@ void read_table(const char* path, T* out)
     read_exact(in, out, sizeof(T) * static_cast<size_t>(n) * m, path);
 }
 
+// ---- bucket-contiguous renumbering: host arrays are staged through device buffers
+
+template <typename T>
+const T* stage_in(const T* src, size_t count, bool on_device, DevBuf<T>& hold, cudaStream_t st)
+{
+    if (on_device || !src) return src;
+    hold = DevBuf<T>(count, st);
+    GTA_CUDA(cudaMemcpyAsync(hold.get(), src, sizeof(T) * count, cudaMemcpyHostToDevice, st));
+    return hold.get();
+}
+
+template <typename T>
+T* stage_out(T* dst, size_t count, bool on_device, DevBuf<T>& hold, cudaStream_t st)
+{
+    if (on_device || !dst) return dst;
+    hold = DevBuf<T>(count, st);
+    return hold.get();
+}
+
+template <typename T>
+void copy_back(T* dst, const DevBuf<T>& hold, size_t count, bool on_device, cudaStream_t st)
+{
+    if (on_device || !dst) return;
+    GTA_CUDA(cudaMemcpyAsync(dst, hold.get(), sizeof(T) * count, cudaMemcpyDeviceToHost, st));
+}
+
+
+// Parses a NumPy v1/v2/v3 header of a C-order little-endian int64 2-D array; returns the data offset.
+int64_t npy_i64_header(std::ifstream& in, const std::string& path, int64_t* n, int32_t* m)
+{
+    unsigned char magic[8];
+    read_exact(in, magic, 8, path);
+    GTA_REQUIRE(magic[0] == 0x93 && std::memcmp(magic + 1, "NUMPY", 5) == 0, kData, "not a .npy file: " + path);
+    uint32_t hl = 0;
+    int64_t pre = 0;
+    if (magic[6] == 1) {
+        uint16_t h16 = 0;
+        read_exact(in, &h16, 2, path);
+        hl = h16;
+        pre = 10;
+    } else {
+        read_exact(in, &hl, 4, path);
+        pre = 12;
+    }
+    std::string hdr(hl, ' ');
+    read_exact(in, hdr.data(), hl, path);
+    GTA_REQUIRE(hdr.find("'<i8'") != std::string::npos, kData, "npy dtype must be little-endian int64: " + path);
+    GTA_REQUIRE(hdr.find("'fortran_order': False") != std::string::npos, kData, "npy must be C order: " + path);
+    const size_t sp = hdr.find("'shape': (");
+    GTA_REQUIRE(sp != std::string::npos, kData, "npy header without shape: " + path);
+    long long a = 0, b = 0;
+    GTA_REQUIRE(std::sscanf(hdr.c_str() + sp + 10, "%lld, %lld", &a, &b) == 2 && a > 0 && b > 0 && b < (1ll << 31),
+                kData, "npy must be a non-empty 2-D array: " + path);
+    *n = a;
+    *m = static_cast<int32_t>(b);
+    return pre + hl;
+}
+
 }  // namespace
 }  // namespace gta
 
@@ -721,6 +779,123 @@ int gta_optimize_knn(const gta_dataset* ds, const int32_t* knn, int64_t n, int32
             GTA_CUDA(cudaMemcpyAsync(graph, gout, sizeof(uint32_t) * n * k, cudaMemcpyDeviceToHost, st));
             GTA_CUDA(cudaStreamSynchronize(st));
         }
+    });
+}
+
+
+int gta_bucket_order(const float* centroids, int32_t B, int32_t d, int32_t k, int32_t window, int32_t* order,
+                     int32_t* centroid_knn, int32_t on_device, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(centroids && order && B >= 2 && d >= 1 && k >= 1 && k < B && k <= 127, kInvalid,
+                    "gta_bucket_order: need centroids, order, 1 <= k < B, k <= 127");
+        cudaStream_t st = S(stream);
+        const bool dev = on_device != 0;
+        DevBuf<float> ch;
+        const float* C = stage_in(centroids, static_cast<size_t>(B) * d, dev, ch, st);
+        const int d32 = pad_dim(d, kElemF32);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        DevBuf<float> Cp(static_cast<size_t>(B) * d32, st), cn(static_cast<size_t>(B), st);
+        convert_rows(C, GTA_F32, d, nullptr, B, Cp.get(), kElemF32, d32, cn.get(), st);
+        const int k1 = k + 1;
+        DevBuf<int32_t> ids(static_cast<size_t>(B) * k1, st);
+        DevBuf<float> dd(static_cast<size_t>(B) * k1, st);
+        assign_topk_impl(Cp.get(), cn.get(), B, d, d32, Cp.get(), cn.get(), B, k1, ids.get(), dd.get(), err.get(), st);
+        check_device_error(err.get(), st, "gta_bucket_order");
+        std::vector<int32_t> h(static_cast<size_t>(B) * k1), adj(static_cast<size_t>(B) * k);
+        GTA_CUDA(cudaMemcpyAsync(h.data(), ids.get(), sizeof(int32_t) * h.size(), cudaMemcpyDeviceToHost, st));
+        GTA_CUDA(cudaStreamSynchronize(st));
+        for (int32_t b = 0; b < B; ++b) {  // drop the bucket itself (else the farthest of the k + 1)
+            int w = 0;
+            bool dropped = false;
+            for (int j = 0; j < k1 && w < k; ++j) {
+                const int32_t v = h[static_cast<size_t>(b) * k1 + j];
+                if (v == b && !dropped) { dropped = true; continue; }
+                adj[static_cast<size_t>(b) * k + w++] = v;
+            }
+        }
+        const int32_t win = window > 0 ? window : std::max<int32_t>(4 * k, 16);
+        std::vector<int32_t> ord(static_cast<size_t>(B));
+        bucket_order(adj.data(), B, k, win, ord.data());
+        if (dev) {
+            GTA_CUDA(cudaMemcpyAsync(order, ord.data(), sizeof(int32_t) * B, cudaMemcpyHostToDevice, st));
+            if (centroid_knn)
+                GTA_CUDA(cudaMemcpyAsync(centroid_knn, adj.data(), sizeof(int32_t) * adj.size(), cudaMemcpyHostToDevice, st));
+            GTA_CUDA(cudaStreamSynchronize(st));  // the host vectors die here
+        } else {
+            std::memcpy(order, ord.data(), sizeof(int32_t) * B);
+            if (centroid_knn) std::memcpy(centroid_knn, adj.data(), sizeof(int32_t) * adj.size());
+        }
+    });
+}
+
+int gta_bucket_reorder(const int32_t* assign, int64_t n, int32_t stride, int32_t B, const int32_t* order,
+                       uint32_t* inverse_perm, int64_t* offsets, int32_t on_device, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(assign && inverse_perm && n >= 1 && B >= 1 && stride >= 1, kInvalid, "gta_bucket_reorder: bad argument");
+        cudaStream_t st = S(stream);
+        const bool dev = on_device != 0;
+        DevBuf<int32_t> ah, oh;
+        DevBuf<uint32_t> ih;
+        DevBuf<int64_t> fh;
+        const int32_t* a = stage_in(assign, static_cast<size_t>(n) * stride, dev, ah, st);
+        const int32_t* o = stage_in(order, static_cast<size_t>(B), dev, oh, st);
+        uint32_t* inv = stage_out(inverse_perm, static_cast<size_t>(n), dev, ih, st);
+        int64_t* off = stage_out(offsets, static_cast<size_t>(B) + 1, dev, fh, st);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        bucket_reorder(a, n, stride, B, o, inv, off, err.get(), st);
+        copy_back(inverse_perm, ih, static_cast<size_t>(n), dev, st);
+        copy_back(offsets, fh, static_cast<size_t>(B) + 1, dev, st);
+        check_device_error(err.get(), st, "gta_bucket_reorder");
+    });
+}
+
+int gta_permute_rows(const void* X, int64_t n, int64_t row_bytes, const uint32_t* inverse_perm, void* out,
+                     int32_t on_device, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(X && inverse_perm && out && n >= 1 && row_bytes >= 1, kInvalid, "gta_permute_rows: bad argument");
+        cudaStream_t st = S(stream);
+        const bool dev = on_device != 0;
+        const size_t bytes = static_cast<size_t>(n) * static_cast<size_t>(row_bytes);
+        DevBuf<uint8_t> xh, oh;
+        DevBuf<uint32_t> ih;
+        const uint8_t* x = stage_in(static_cast<const uint8_t*>(X), bytes, dev, xh, st);
+        const uint32_t* inv = stage_in(inverse_perm, static_cast<size_t>(n), dev, ih, st);
+        uint8_t* o = stage_out(static_cast<uint8_t*>(out), bytes, dev, oh, st);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        permute_rows(x, n, row_bytes, inv, o, err.get(), st);
+        copy_back(static_cast<uint8_t*>(out), oh, bytes, dev, st);
+        check_device_error(err.get(), st, "gta_permute_rows");
+    });
+}
+
+int gta_permute_graph(const int32_t* g, int64_t n, int32_t m, const uint32_t* inverse_perm, int32_t to_original,
+                      int32_t keep_padding, int32_t* out, int32_t on_device, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(g && inverse_perm && out && n >= 1 && m >= 1, kInvalid, "gta_permute_graph: bad argument");
+        cudaStream_t st = S(stream);
+        const bool dev = on_device != 0;
+        const size_t nm = static_cast<size_t>(n) * m;
+        DevBuf<int32_t> gh, oh;
+        DevBuf<uint32_t> ih;
+        const int32_t* gg = stage_in(g, nm, dev, gh, st);
+        const uint32_t* inv = stage_in(inverse_perm, static_cast<size_t>(n), dev, ih, st);
+        int32_t* o = stage_out(out, nm, dev, oh, st);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        permute_graph(gg, n, m, inv, to_original != 0, keep_padding != 0, o, err.get(), st);
+        copy_back(out, oh, nm, dev, st);
+        check_device_error(err.get(), st, "gta_permute_graph");
     });
 }
 
@@ -1190,6 +1365,73 @@ int gta_read_graph_header(const char* path, int64_t* n, int32_t* k)
     return guard([&] { read_table_header(path, n, k); });
 }
 int gta_read_graph(const char* path, uint32_t* graph) { return guard([&] { read_table<uint32_t>(path, graph); }); }
+
+int gta_write_u32(const char* path, const uint32_t* v, int64_t n)
+{
+    return guard([&] {
+        GTA_REQUIRE(path && (v || n == 0) && n >= 0, kInvalid, "gta_write_u32: bad argument");
+        std::ofstream out(path, std::ios::binary | std::ios::trunc);
+        GTA_REQUIRE(out.is_open(), kInvalid, std::string("cannot open for writing: ") + path);
+        out.write(reinterpret_cast<const char*>(v), static_cast<std::streamsize>(sizeof(uint32_t) * n));
+        GTA_REQUIRE(out.good(), kData, std::string("write failed: ") + path);
+    });
+}
+
+int gta_read_u32_count(const char* path, int64_t* n)
+{
+    return guard([&] {
+        GTA_REQUIRE(path && n, kInvalid, "gta_read_u32_count: bad argument");
+        std::ifstream in(path, std::ios::binary | std::ios::ate);
+        GTA_REQUIRE(in.is_open(), kInvalid, std::string("cannot open: ") + path);
+        const int64_t bytes = static_cast<int64_t>(in.tellg());
+        GTA_REQUIRE(bytes % 4 == 0, kData, std::string("size is not a multiple of 4 bytes: ") + path);
+        *n = bytes / 4;
+    });
+}
+
+int gta_read_u32(const char* path, uint32_t* v)
+{
+    return guard([&] {
+        GTA_REQUIRE(path && v, kInvalid, "gta_read_u32: bad argument");
+        std::ifstream in(path, std::ios::binary | std::ios::ate);
+        GTA_REQUIRE(in.is_open(), kInvalid, std::string("cannot open: ") + path);
+        const int64_t bytes = static_cast<int64_t>(in.tellg());
+        in.seekg(0);
+        read_exact(in, v, static_cast<size_t>(bytes), path);
+    });
+}
+
+
+int gta_read_npy_i64_header(const char* path, int64_t* n, int32_t* m)
+{
+    return guard([&] {
+        GTA_REQUIRE(path && n && m, kInvalid, "gta_read_npy_i64_header: bad argument");
+        std::ifstream in(path, std::ios::binary);
+        GTA_REQUIRE(in.is_open(), kInvalid, std::string("cannot open: ") + path);
+        npy_i64_header(in, path, n, m);
+    });
+}
+
+int gta_read_npy_i64(const char* path, int32_t* ids)
+{
+    return guard([&] {
+        GTA_REQUIRE(path && ids, kInvalid, "gta_read_npy_i64: bad argument");
+        std::ifstream in(path, std::ios::binary);
+        GTA_REQUIRE(in.is_open(), kInvalid, std::string("cannot open: ") + path);
+        int64_t n = 0;
+        int32_t m = 0;
+        npy_i64_header(in, path, &n, &m);
+        std::vector<int64_t> row(static_cast<size_t>(m));
+        for (int64_t i = 0; i < n; ++i) {
+            read_exact(in, row.data(), sizeof(int64_t) * m, path);
+            for (int32_t j = 0; j < m; ++j) {
+                const int64_t v = row[static_cast<size_t>(j)];
+                GTA_REQUIRE(v >= -1 && v < (1ll << 31), kData, "npy value outside [-1, 2^31): " + std::string(path));
+                ids[i * m + j] = static_cast<int32_t>(v);
+            }
+        }
+    });
+}
 
 int gta_write_npy_i64(const char* path, const int32_t* ids, int64_t n, int32_t m)
 {

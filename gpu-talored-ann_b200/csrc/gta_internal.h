@@ -149,6 +149,14 @@ void max_sqrt(const float* v, int64_t n, float* out, cudaStream_t st);
 void graph_search(const void* base, int dtype, int64_t n, int d, const uint32_t* graph, int kg, const void* queries,
                   int64_t nq, const int32_t* entries, int ne, int topk, int ef, int32_t* out_ids, float* out_dists,
                   int* err, cudaStream_t st);
+// bucket-contiguous renumbering (reorder.cu)
+void bucket_reorder(const int32_t* assign, int64_t n, int32_t stride, int32_t B, const int32_t* order,
+                    uint32_t* inverse_perm, int64_t* offsets, int* err, cudaStream_t st);
+void permute_rows(const void* X, int64_t n, int64_t row_bytes, const uint32_t* inverse_perm, void* out, int* err,
+                  cudaStream_t st);
+void permute_graph(const int32_t* g, int64_t n, int32_t m, const uint32_t* inverse_perm, bool to_original,
+                   bool keep_padding, int32_t* out, int* err, cudaStream_t st);
+void bucket_order(const int32_t* adj, int32_t B, int32_t K, int32_t window, int32_t* order);  // host
 // shard variants (one rank's part of a multi-GPU build)
 void gather_range(const void* X, int dtype, int d, int64_t row0, int64_t n, const int32_t* ids, int64_t n_ids,
                   float* out, cudaStream_t st);

@@ -66,6 +66,10 @@ _SIGS = {
     "gta_reverse_merge": [_P, _I64, _I32, _P, _P],
     "gta_reverse_merge_noalloc": [_P, _I64, _I32, _P, _P],
     "gta_search": [ctypes.POINTER(gta_dataset), _P, _I64, _P, _I32, _P, _I32, _I32, _I32, _P, _P, _P],
+    "gta_bucket_order": [_P, _I32, _I32, _I32, _I32, _P, _P, _I32, _P],
+    "gta_bucket_reorder": [_P, _I64, _I32, _I32, _P, _P, _P, _I32, _P],
+    "gta_permute_rows": [_P, _I64, _I64, _P, _P, _I32, _P],
+    "gta_permute_graph": [_P, _I64, _I32, _P, _I32, _I32, _P, _I32, _P],
     "gta_kmeans_sizes": [_I64, ctypes.POINTER(gta_bucket_params), ctypes.POINTER(_I64), ctypes.POINTER(_I64),
                          ctypes.POINTER(_U64)],
     "gta_sample_ids": [_I64, _I64, _U64, _P, _P],
@@ -88,6 +92,11 @@ _SIGS = {
     "gta_read_graph_header": [ctypes.c_char_p, ctypes.POINTER(_I64), ctypes.POINTER(_I32)],
     "gta_read_graph": [ctypes.c_char_p, _P],
     "gta_write_npy_i64": [ctypes.c_char_p, _P, _I64, _I32],
+    "gta_read_npy_i64_header": [ctypes.c_char_p, ctypes.POINTER(_I64), ctypes.POINTER(_I32)],
+    "gta_read_npy_i64": [ctypes.c_char_p, _P],
+    "gta_write_u32": [ctypes.c_char_p, _P, _I64],
+    "gta_read_u32_count": [ctypes.c_char_p, ctypes.POINTER(_I64)],
+    "gta_read_u32": [ctypes.c_char_p, _P],
     "gta_profile_enable": [_I32],
     "gta_release_workspace": [],
     "gta_device_memory": [ctypes.POINTER(_I64), ctypes.POINTER(_I64)],

@@ -276,6 +276,64 @@ def reverse_merge(pruned):
     return out
 
 
+# ---------------------------------------------------------------- bucket-contiguous renumbering
+def _side(x):
+    dev = _is_dev(x)
+    return dev, (_stream() if dev else ctypes.c_void_p(0))
+
+
+def bucket_order(centroids, k: int = 32, window: int = 0):
+    """Processing order of the buckets (bucket2 Step 3 + bucket_order.hpp): exact kNN graph of
+    the centroids (k columns, self excluded) and the greedy windowed order over it.
+    Returns (order[B] int32, centroid_knn[B, k] int32) on the centroids' side."""
+    dev, st = _side(centroids)
+    B, d = centroids.shape
+    order = _empty((B,), "int32", dev)
+    knn = _empty((B, k), "int32", dev)
+    L.check(L.lib().gta_bucket_order(_ptr(centroids), B, d, k, window, _ptr(order), _ptr(knn), 1 if dev else 0, st))
+    return order, knn
+
+
+def bucket_reorder(assign, n_buckets: int, order=None):
+    """compute_bucket_reorder: new ids bucket by bucket in ``order`` (default 0..B-1), ascending
+    old id inside a bucket.  ``assign`` is (N,) or an (N, 2) top-2 table (column 0 is used).
+    Returns (inverse_perm[N] uint32 (int32 view on the device), offsets[B+1] int64)."""
+    dev, st = _side(assign)
+    n = assign.shape[0]
+    stride = 1 if assign.ndim == 1 else assign.shape[1]
+    inv = _empty((n,), "int32" if dev else "uint32", dev)
+    off = _empty((n_buckets + 1,), "int64", dev)
+    L.check(L.lib().gta_bucket_reorder(_ptr(assign), n, stride, n_buckets, _ptr(order), _ptr(inv), _ptr(off),
+                                       1 if dev else 0, st))
+    return inv, off
+
+
+def permute_rows(X, inverse_perm):
+    """Row i of the result = row inverse_perm[i] of X (the reordered dataset)."""
+    dev, st = _side(X)
+    if dev:
+        torch = _torch()
+        out = torch.empty_like(X)
+    else:
+        out = np.empty_like(X)
+    row_bytes = X[0].numel() * X.element_size() if dev else X[0].nbytes
+    L.check(L.lib().gta_permute_rows(_ptr(X), X.shape[0], row_bytes, _ptr(inverse_perm), _ptr(out), 1 if dev else 0, st))
+    return out
+
+
+def permute_graph(g, inverse_perm, to_original: bool = True, keep_padding: bool = False):
+    """translate_ids (to_original) or the renumbering into the reordered id space of an
+    N x M id table; -1 padding kept when ``keep_padding``."""
+    dev, st = _side(g)
+    if not dev:
+        g = np.ascontiguousarray(g)
+        g = g.view(np.int32) if g.dtype.itemsize == 4 else g.astype(np.int32)
+    out = _empty(tuple(g.shape), "int32", dev)
+    L.check(L.lib().gta_permute_graph(_ptr(g), g.shape[0], g.shape[1], _ptr(inverse_perm), int(to_original),
+                                      int(keep_padding), _ptr(out), 1 if dev else 0, st))
+    return out
+
+
 # ---------------------------------------------------------------- files (host)
 def read_dataset(path: str, row0: int = 0, nrows: Optional[int] = None) -> np.ndarray:
     n, d, dt = ctypes.c_int64(), ctypes.c_int32(), ctypes.c_int32()
@@ -319,6 +377,28 @@ def read_graph(path: str) -> np.ndarray:
     L.check(L.lib().gta_read_graph_header(path.encode(), ctypes.byref(n), ctypes.byref(k)))
     out = np.empty((n.value, k.value), np.uint32)
     L.check(L.lib().gta_read_graph(path.encode(), _ptr(out)))
+    return out
+
+
+def read_npy_i64(path: str) -> np.ndarray:
+    """An int64 (N, M) .npy narrowed to int32 by the library's reader (-1 padding kept)."""
+    n, m = ctypes.c_int64(), ctypes.c_int32()
+    L.check(L.lib().gta_read_npy_i64_header(path.encode(), ctypes.byref(n), ctypes.byref(m)))
+    out = np.empty((n.value, m.value), np.int32)
+    L.check(L.lib().gta_read_npy_i64(path.encode(), _ptr(out)))
+    return out
+
+
+def write_u32(path: str, v: np.ndarray) -> None:
+    v = np.ascontiguousarray(v, np.uint32)
+    L.check(L.lib().gta_write_u32(path.encode(), _ptr(v), v.size))
+
+
+def read_u32(path: str) -> np.ndarray:
+    n = ctypes.c_int64()
+    L.check(L.lib().gta_read_u32_count(path.encode(), ctypes.byref(n)))
+    out = np.empty(n.value, np.uint32)
+    L.check(L.lib().gta_read_u32(path.encode(), _ptr(out)))
     return out
 
 

@@ -220,6 +220,45 @@ int gta_search(const gta_dataset* base, const void* queries, int64_t nq, const u
                const int32_t* entries, int32_t n_entry, int32_t topk, int32_t ef, int32_t* out_ids, float* out_dists,
                void* stream);
 
+/* ---------------------------------------------------------------- bucket-contiguous renumbering
+ * bucket2 renumbers the points after the first round so that every bucket is a
+ * contiguous id range (data_reordered.<ext>, inverse_perm.bin[new] = old), runs
+ * the rest of the pipeline in that id space and translates the final graph back
+ * (translate_ids).  Every entry takes an on_device flag: 1 = all arrays are
+ * device pointers (stream-ordered), 0 = host arrays (synchronous). */
+
+/* Processing order of B buckets (order[pos] = bucket): exact kNN graph of the
+ * centroids (B x d f32, self excluded, k <= 127 columns, written to centroid_knn
+ * when non-NULL, ties to the smaller id), then the greedy windowed order of
+ * bucket_order.hpp:143-200 over it (window <= 0: max(4k, 16), bucket.cu:9023-9025).
+ * Replaces bucket2 Step 3 (centroid_self_knn_bf, bucket.cu:3241) + the order. */
+int gta_bucket_order(const float* centroids, int32_t B, int32_t d, int32_t k, int32_t window, int32_t* order,
+                     int32_t* centroid_knn, int32_t on_device, void* stream);
+
+/* New ids bucket by bucket in `order` (NULL: 0..B-1), ascending old id inside a
+ * bucket: inverse_perm[new] = old (n), offsets[pos] = first new id of bucket
+ * order[pos] (B+1, may be NULL).  The bucket of point i is assign[i * stride]
+ * (stride 2 reads column 0 of a top-2 table).  Status 5 when a point has no
+ * valid bucket or order is not a permutation.
+ * Replaces compute_bucket_reorder (bucketDemo/buildBucket/src/bucket.cu:8356-8417). */
+int gta_bucket_reorder(const int32_t* assign, int64_t n, int32_t stride, int32_t B, const int32_t* order,
+                       uint32_t* inverse_perm, int64_t* offsets, int32_t on_device, void* stream);
+
+/* out row i = X row inverse_perm[i] (n rows of row_bytes bytes): the reordered
+ * dataset (bucket.cu:9253-9403, data_reordered.<ext>). */
+int gta_permute_rows(const void* X, int64_t n, int64_t row_bytes, const uint32_t* inverse_perm, void* out,
+                     int32_t on_device, void* stream);
+
+/* Renumber an n x m graph.  to_original = 1: rows and ids from the reordered id
+ * space back to the original one, out[inv[i]][j] = inv[g[i][j]]
+ * (translate_graph_ids.hpp:75-200, the translate_ids tool); to_original = 0: the
+ * other way, out[i][j] = perm[g[inv[i]][j]] with perm = inverse of inv.
+ * keep_padding = 1 keeps negative ids as -1 (the .npy path); otherwise they are
+ * an error like any id >= n.  Status 5 on a bad id or when inverse_perm is not a
+ * permutation of [0, n). */
+int gta_permute_graph(const int32_t* g, int64_t n, int32_t m, const uint32_t* inverse_perm, int32_t to_original,
+                      int32_t keep_padding, int32_t* out, int32_t on_device, void* stream);
+
 /* ---------------------------------------------------------------- shard stages
  * One rank's part of the multi-GPU build (the plan of the reference's
  * multi-GPU design: row-sharded k-means with all-reduced sums, buckets placed
@@ -306,8 +345,17 @@ int gta_write_graph(const char* path, const uint32_t* graph, int64_t n, int32_t 
 int gta_read_graph_header(const char* path, int64_t* n, int32_t* k);
 int gta_read_graph(const char* path, uint32_t* graph);
 
-/* neighbors.npy: int64 (N, M) numpy array (load.hpp:535-618). */
+/* neighbors.npy: int64 (N, M) numpy array (load.hpp:535-618).  The reader takes
+ * a C-order little-endian int64 2-D array and narrows it to int32 (values must
+ * lie in [-1, 2^31); -1 = padding); status 5 otherwise. */
 int gta_write_npy_i64(const char* path, const int32_t* ids, int64_t n, int32_t m);
+int gta_read_npy_i64_header(const char* path, int64_t* n, int32_t* m);
+int gta_read_npy_i64(const char* path, int32_t* ids);
+
+/* Raw uint32 arrays without a header (inverse_perm.bin, bucket.cu:9445). */
+int gta_write_u32(const char* path, const uint32_t* v, int64_t n);
+int gta_read_u32_count(const char* path, int64_t* n);
+int gta_read_u32(const char* path, uint32_t* v);
 
 /* ---------------------------------------------------------------- profiling */
 /* Per-stage CUDA-event timing inside the library (off by default).  Enabling

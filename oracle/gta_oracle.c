@@ -570,3 +570,124 @@ ORC_API void orc_graph_search(const float* base, int64_t N, int32_t d, const uin
         free(srt); free(bi); free(bd); free(heap); free(visited);
     }
 }
+
+/* ------------------------------------------------------------------ */
+/* bucket-contiguous renumbering                                        */
+/* ------------------------------------------------------------------ */
+
+/* compute_bucket_reorder (bucketDemo/buildBucket/src/bucket.cu:8356-8417):
+ * bucket b = assign[i * stride]; ranges laid out in `order` (NULL: 0..B-1);
+ * inside a bucket ascending old id; inv[new] = old; offsets[pos] (B+1).
+ * Returns the number of points placed (n when every point has a bucket). */
+ORC_API int64_t orc_bucket_reorder(const int32_t* assign, int64_t n, int32_t stride, int32_t B, const int32_t* order,
+                                   uint32_t* inv, int64_t* offsets)
+{
+    int64_t* count = (int64_t*)calloc((size_t)B, sizeof(int64_t));
+    int64_t* start = (int64_t*)calloc((size_t)B, sizeof(int64_t));
+    for (int64_t i = 0; i < n; ++i) {
+        const int32_t b = assign[i * stride];
+        if (b >= 0 && b < B) count[b]++;
+    }
+    int64_t run = 0;
+    offsets[0] = 0;
+    for (int32_t p = 0; p < B; ++p) {
+        const int32_t b = order ? order[p] : p;
+        start[b] = run;
+        run += count[b];
+        offsets[p + 1] = run;
+    }
+    for (int64_t i = 0; i < n; ++i) {
+        const int32_t b = assign[i * stride];
+        if (b >= 0 && b < B) inv[start[b]++] = (uint32_t)i;
+    }
+    free(count);
+    free(start);
+    return run;
+}
+
+/* translate_graph_to_original_order / translate_npy_to_original_order
+ * (translate_graph_ids.hpp:75-200) for to_original = 1: row inv[i] gets row i with
+ * ids mapped through inv; to_original = 0: row i gets old row inv[i] with ids
+ * mapped old -> new.  Negative ids stay -1 (keep_padding) else count as bad, like
+ * ids >= n.  Returns the number of bad ids (0 on success); -1 when inv is not a
+ * permutation of [0, n). */
+ORC_API int64_t orc_permute_graph(const int32_t* g, int64_t n, int32_t m, const uint32_t* inv, int32_t to_original,
+                                  int32_t keep_padding, int32_t* out)
+{
+    int32_t* perm = (int32_t*)malloc(sizeof(int32_t) * (size_t)n);
+    for (int64_t i = 0; i < n; ++i) perm[i] = -1;
+    for (int64_t i = 0; i < n; ++i) {
+        if ((int64_t)inv[i] >= n || perm[inv[i]] != -1) { free(perm); return -1; }
+        perm[inv[i]] = (int32_t)i;
+    }
+    int64_t bad = 0;
+    for (int64_t i = 0; i < n; ++i) {
+        const int64_t src = to_original ? i : (int64_t)inv[i];
+        const int64_t dst = to_original ? (int64_t)inv[i] : i;
+        for (int32_t j = 0; j < m; ++j) {
+            const int32_t v = g[src * m + j];
+            int32_t w = -1;
+            if (v < 0) bad += !keep_padding;
+            else if ((int64_t)v >= n) ++bad;
+            else w = to_original ? (int32_t)inv[v] : perm[v];
+            out[dst * m + j] = w;
+        }
+    }
+    free(perm);
+    return bad;
+}
+
+/* compute_bucket_processing_order (bucket_order.hpp:143-200) over the flat
+ * bucket graph adj (B x K; adjacency_from_flat_graph :202-218 drops ids that are
+ * the bucket itself or >= B; negative ids are dropped here too).  Plain O(B^2)
+ * selection: next = argmax (score, id) over touched unplaced buckets, else the
+ * lowest unplaced id; score = shared neighbour entries with the last `window`
+ * placed buckets. */
+ORC_API void orc_bucket_order(const int32_t* adj, int32_t B, int32_t K, int32_t window, int32_t* order)
+{
+    if (window < 1) window = 1;
+    int64_t* score = (int64_t*)calloc((size_t)B, sizeof(int64_t));
+    char* placed = (char*)calloc((size_t)B, 1);
+    char* touched = (char*)calloc((size_t)B, 1);
+    int32_t* deg = (int32_t*)calloc((size_t)B, sizeof(int32_t));
+    int32_t* nb = (int32_t*)malloc(sizeof(int32_t) * (size_t)B * (size_t)(K > 0 ? K : 1));
+    for (int32_t v = 0; v < B; ++v)
+        for (int32_t k = 0; k < K; ++k) {
+            const int32_t u = adj[(int64_t)v * K + k];
+            if (u >= 0 && u < B && u != v) nb[(int64_t)v * K + deg[v]++] = u;
+        }
+    /* score change of every unplaced v when x enters (+1) or leaves (-1) the window:
+     * for each neighbour entry u of x, each entry of v equal to u */
+#define ORC_SHIFT(x, delta)                                                           \
+    do {                                                                              \
+        for (int32_t a_ = 0; a_ < deg[x]; ++a_) {                                     \
+            const int32_t u_ = nb[(int64_t)(x) * K + a_];                             \
+            for (int32_t v_ = 0; v_ < B; ++v_) {                                      \
+                if (placed[v_]) continue;                                             \
+                for (int32_t b_ = 0; b_ < deg[v_]; ++b_)                              \
+                    if (nb[(int64_t)v_ * K + b_] == u_) { score[v_] += (delta); touched[v_] = 1; } \
+            }                                                                         \
+        }                                                                             \
+    } while (0)
+    int32_t start = 0;
+    for (int32_t v = 1; v < B; ++v)
+        if (deg[v] > deg[start]) start = v;
+    order[0] = start;
+    placed[start] = 1;
+    ORC_SHIFT(start, 1);
+    for (int32_t i = 1; i < B; ++i) {
+        if (i > window) ORC_SHIFT(order[i - window - 1], -1);
+        int32_t pick = -1;
+        for (int32_t v = 0; v < B; ++v)
+            if (!placed[v] && touched[v] && (pick < 0 || score[v] > score[pick] || (score[v] == score[pick] && v > pick)))
+                pick = v;
+        if (pick < 0)
+            for (int32_t v = 0; v < B && pick < 0; ++v)
+                if (!placed[v]) pick = v;
+        order[i] = pick;
+        placed[pick] = 1;
+        ORC_SHIFT(pick, 1);
+    }
+#undef ORC_SHIFT
+    free(score); free(placed); free(touched); free(deg); free(nb);
+}

@@ -68,6 +68,12 @@ def lib():
         L.orc_exact_l2.argtypes = [_P, _P, _I32]
         L.orc_exact_l2.restype = ctypes.c_float
         L.orc_num_threads.restype = ctypes.c_int
+        L.orc_bucket_reorder.argtypes = [_P, _I64, _I32, _I32, _P, _P, _P]
+        L.orc_bucket_reorder.restype = _I64
+        L.orc_permute_graph.argtypes = [_P, _I64, _I32, _P, _I32, _I32, _P]
+        L.orc_permute_graph.restype = _I64
+        L.orc_bucket_order.argtypes = [_P, _I32, _I32, _I32, _P]
+        L.orc_bucket_order.restype = None
         _lib = L
     return _lib
 
@@ -85,6 +91,9 @@ def ref_lib():
         R.ref_optimize.argtypes = [_P, _I64, _I32, _I32, _P]
         R.ref_rank_ordered_csr.argtypes = [_P, _P, _P, _I64, ctypes.c_uint32, ctypes.c_uint32, _P, _P]
         R.ref_merge_rank_ordered_into_row.argtypes = [_P, _P, ctypes.c_uint32, ctypes.c_uint32]
+        R.ref_bucket_order.argtypes = [_P, _I64, _I32, _I32, _P]
+        R.ref_translate_graph.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p]
+        R.ref_translate_npy.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p]
         _ref = R
     return _ref
 
@@ -289,6 +298,36 @@ def search_entries(n: int, nq: int, num_entry: int, seed: int = 42) -> np.ndarra
     for i in range(nq):
         u = np.unique(rng.integers(0, n, size=k, endpoint=False))
         out[i, :u.size] = u
+    return out
+
+
+def bucket_reorder(assign, B: int, order=None, stride: int = 1):
+    """compute_bucket_reorder (bucket.cu:8356-8417): (inverse_perm uint32[placed], offsets int64[B+1])."""
+    a = np.ascontiguousarray(assign, np.int32)
+    n = a.size // stride
+    inv = np.zeros(n, np.uint32)
+    off = np.zeros(B + 1, np.int64)
+    o = None if order is None else np.ascontiguousarray(order, np.int32)
+    placed = lib().orc_bucket_reorder(_p(a), n, stride, B, _p(o) if o is not None else None, _p(inv), _p(off))
+    return inv[:placed], off
+
+
+def permute_graph(g, inv, to_original: bool, keep_padding: bool):
+    """translate_graph_ids.hpp:75-200 (to_original) and its inverse; returns (out, bad) with
+    bad = -1 when inv is not a permutation."""
+    g = np.ascontiguousarray(g).view(np.int32) if np.asarray(g).dtype.itemsize == 4 else np.ascontiguousarray(g, np.int32)
+    inv = np.ascontiguousarray(inv, np.uint32)
+    out = np.empty_like(g)
+    bad = lib().orc_permute_graph(_p(g), g.shape[0], g.shape[1], _p(inv), int(to_original), int(keep_padding), _p(out))
+    return out, int(bad)
+
+
+def bucket_order(adj, window: int):
+    """compute_bucket_processing_order (bucket_order.hpp:143-200) over a flat (B, K) bucket graph."""
+    adj = np.ascontiguousarray(adj, np.int32)
+    B, K = adj.shape
+    out = np.empty(B, np.int32)
+    lib().orc_bucket_order(_p(adj), B, K, window, _p(out))
     return out
 
 

@@ -12,6 +12,10 @@
 //   bucketDemo/buildBucket/src/edge_chunk_accumulator.hpp
 //       EdgeRecord (:54), build_rank_ordered_csr (:235), TopKReverseStore (:386),
 //       merge_rank_ordered_into_row (:471)
+//   bucketDemo/buildBucket/src/bucket_order.hpp
+//       compute_bucket_processing_order (:143), adjacency_from_flat_graph (:202)
+//   bucketDemo/buildBucket/src/translate_graph_ids.hpp
+//       translate_graph_to_original_order (:75), translate_npy_to_original_order (:180)
 //
 // Used to (1) generate the golden fixtures under tests/golden/ and (2) time
 // the reference's own CPU prune + reverse-edge code as bench.py's reference
@@ -23,6 +27,8 @@
 
 #include "prune_windowed_core.hpp"
 #include "edge_chunk_accumulator.hpp"
+#include "bucket_order.hpp"
+#include "translate_graph_ids.hpp"
 
 #define REF_API extern "C" __attribute__((visibility("default")))
 
@@ -129,4 +135,32 @@ REF_API int ref_rank_ordered_csr(const uint32_t* dst, const uint32_t* src, const
 REF_API void ref_merge_rank_ordered_into_row(uint32_t* row, const uint32_t* src, uint32_t count, uint32_t K)
 {
     edge_chunk::merge_rank_ordered_into_row(row, src, count, K);
+}
+
+// Bucket processing order of a flat (B, K) uint32 bucket graph.
+REF_API int ref_bucket_order(const uint32_t* graph, int64_t B, int32_t K, int32_t window, int32_t* out)
+{
+    try {
+        auto order = bucket_order::compute_bucket_processing_order(
+            bucket_order::adjacency_from_flat_graph(graph, B, K), window);
+        std::memcpy(out, order.data(), sizeof(int32_t) * order.size());
+        return 0;
+    } catch (...) { return 5; }
+}
+
+// translate_ids on files: a graph .bin (int64 N, int32 K, uint32) or a .npy (int64).
+REF_API int ref_translate_graph(const char* graph_path, const char* inv_path, const char* out_path)
+{
+    try {
+        translate_ids::translate_graph_to_original_order(graph_path, inv_path, out_path);
+        return 0;
+    } catch (...) { return 5; }
+}
+
+REF_API int ref_translate_npy(const char* npy_path, const char* inv_path, const char* out_path)
+{
+    try {
+        translate_ids::translate_npy_to_original_order(npy_path, inv_path, out_path);
+        return 0;
+    } catch (...) { return 5; }
 }

@@ -150,6 +150,49 @@ def make_eval_fixture():
     np.savez_compressed(os.path.join(HERE, "eval_recall.npz"), **out)
 
 
+def make_reorder_fixture():
+    """The reference's own bucket_order.hpp (processing order of a bucket graph) and
+    translate_graph_ids.hpp (graph .bin and .npy back to the original id order), compiled
+    in place into oracle/_ref, on seeded random inputs."""
+    R = orc.ref_lib()
+    if R is None:
+        raise SystemExit("oracle/_ref/libgta_ref.so missing: run `make -C oracle` with the reference tree present")
+    p = orc._p
+    rng = np.random.default_rng(23)
+    out = {}
+    cases = [(40, 6, 8), (100, 10, 16), (256, 32, 128), (64, 8, 1), (50, 4, 200)]
+    for c, (B, K, w) in enumerate(cases):
+        adj = rng.integers(0, B, (B, K)).astype(np.uint32)
+        adj[rng.random((B, K)) < 0.05] = B + 3  # entries the adjacency drops
+        order = np.empty(B, np.int32)
+        assert R.ref_bucket_order(p(adj), B, K, w, p(order)) == 0
+        out[f"order_adj_{c}"] = adj
+        out[f"order_window_{c}"] = np.int32(w)
+        out[f"order_{c}"] = order
+    N, K = 3000, 12
+    inv = rng.permutation(N).astype(np.uint32)
+    g = rng.integers(0, N, (N, K)).astype(np.uint32)
+    gp = g.astype(np.int64)
+    gp[rng.random((N, K)) < 0.1] = -1
+    with tempfile.TemporaryDirectory() as td:
+        gpath, ipath, opath = (os.path.join(td, f) for f in ("g.bin", "inv.bin", "o.bin"))
+        with open(gpath, "wb") as f:
+            np.array([N], np.int64).tofile(f)
+            np.array([K], np.int32).tofile(f)
+            g.tofile(f)
+        inv.tofile(ipath)
+        assert R.ref_translate_graph(gpath.encode(), ipath.encode(), opath.encode()) == 0
+        out["translate_bin"] = np.fromfile(opath, dtype=np.uint32, offset=12).reshape(N, K)
+        npath, nopath = os.path.join(td, "g.npy"), os.path.join(td, "o.npy")
+        np.save(npath, gp)
+        assert R.ref_translate_npy(npath.encode(), ipath.encode(), nopath.encode()) == 0
+        out["translate_npy"] = np.load(nopath)
+    out["translate_inv"] = inv
+    out["translate_g"] = g
+    out["translate_g_pad"] = gp
+    np.savez_compressed(os.path.join(HERE, "reorder.npz"), **out)
+
+
 def _random_graph(rng, N, M):
     """M distinct non-self candidates per row (the reference test's generator shape)."""
     g = np.empty((N, M), np.uint32)
@@ -202,8 +245,8 @@ def make_cpp_fixtures():
 
 
 if __name__ == "__main__":
-    # `python make_golden.py [python] [cpp] [search] [eval]`: the named fixture groups (default all)
-    want = set(sys.argv[1:]) or {"python", "cpp", "search", "eval"}
+    # `python make_golden.py [python] [cpp] [search] [eval] [reorder]`: the named fixture groups (default all)
+    want = set(sys.argv[1:]) or {"python", "cpp", "search", "eval", "reorder"}
     orc.build()
     if "python" in want:
         make_python_fixtures()
@@ -213,6 +256,8 @@ if __name__ == "__main__":
         make_search_fixture()
     if "eval" in want:
         make_eval_fixture()
+    if "reorder" in want:
+        make_reorder_fixture()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")

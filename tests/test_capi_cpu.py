@@ -122,3 +122,22 @@ def test_kmeans_sizes(n, b, req, n_s, pool):
     L.check(L.lib().gta_kmeans_sizes(n, ctypes.byref(bp), ctypes.byref(a), ctypes.byref(c), ctypes.byref(s)))
     assert (a.value, c.value) == (n_s, pool)
     assert s.value != 7
+
+
+def test_npy_reader_and_u32_files(tmp_path):
+    ids = np.array([[0, 5, -1], [7, 2147483647, 3]], np.int32)
+    p = str(tmp_path / "n.npy")
+    gta.write_npy(p, ids)
+    np.testing.assert_array_equal(gta.read_npy_i64(p), ids)
+    np.save(tmp_path / "np.npy", ids.astype(np.int64))  # numpy's own writer
+    np.testing.assert_array_equal(gta.read_npy_i64(str(tmp_path / "np.npy")), ids)
+    np.save(tmp_path / "big.npy", np.array([[1 << 31]], np.int64))
+    with pytest.raises(gta.GtaError):
+        gta.read_npy_i64(str(tmp_path / "big.npy"))
+    np.save(tmp_path / "f.npy", np.zeros((2, 2), np.float32))
+    with pytest.raises(gta.GtaError):
+        gta.read_npy_i64(str(tmp_path / "f.npy"))
+    v = np.arange(10, dtype=np.uint32) * 7
+    gta.write_u32(str(tmp_path / "inv.bin"), v)
+    np.testing.assert_array_equal(gta.read_u32(str(tmp_path / "inv.bin")), v)
+    assert (tmp_path / "inv.bin").stat().st_size == 40  # raw, no header

@@ -46,18 +46,42 @@ def test_bucket2_outputs(data, rounds):
     dists = np.fromfile(sub / "vector_dists.bin", dtype=np.float32, offset=12).reshape(ids.shape)
     graph = gta.read_graph(str(sub / "final_graph.bin"))
     npy = np.load(sub / "neighbors.npy")
+    inv = gta.read_u32(str(sub / "inverse_perm.bin"))
     # the library's build with the same parameters (rounds merged by the reference's merge rule)
     ri, rd = gta.build_bucket(X, 6, 32, 5, 0, 7)
     for r in range(1, rounds):
         ni, nd = gta.build_bucket(X, 6, 32, 5, 0, 7 + r)
         ri, rd = orc.merge_lists(ri, rd, ni, nd)
-    np.testing.assert_array_equal(ids, ri)
-    np.testing.assert_array_equal(dists, rd)
-    np.testing.assert_array_equal(npy, ri.astype(np.int64))
-    li, ld = gta.build_bucket(X, 6, 32, 5, 0, 7, rounds=rounds)
+    li, ld, cent, top2 = gta.build_bucket(X, 6, 32, 5, 0, 7, rounds=rounds, with_extras=True)
     np.testing.assert_array_equal(li, ri)
-    san, _ = orc.sanitize(ri)
-    np.testing.assert_array_equal(graph, orc.optimize(san, 16))
+    # renumbering: centroid kNN (k = min(knn-k, B-1)) -> bucket order -> nearest-bucket ranges
+    ck = 5
+    cid, _ = orc.topk_assign(cent, cent, ck + 1)
+    adj = np.array([[v for v in row if v != b][:ck] for b, row in enumerate(cid)], np.int32)
+    order = orc.bucket_order(adj, max(4 * ck, 16))
+    want_inv, want_off = orc.bucket_reorder(top2[:, 0].copy(), 6, order=order)
+    np.testing.assert_array_equal(inv, want_inv)
+    np.testing.assert_array_equal(np.fromfile(sub / "bucket_offsets.bin", dtype=np.uint32, offset=4), want_off)
+    np.testing.assert_array_equal(np.fromfile(sub / "bucket_process_order.bin", dtype=np.int32, offset=4), order)
+    np.testing.assert_array_equal(gta.read_graph(str(sub / "centroid_knn.bin")).view(np.int32), adj)
+    np.testing.assert_array_equal(gta.read_dataset(str(sub / "data_reordered.u8bin")), X[inv])
+    ids_new, bad = orc.permute_graph(ri, inv, False, True)
+    assert bad == 0
+    np.testing.assert_array_equal(ids, ids_new)
+    np.testing.assert_array_equal(dists, rd[inv])
+    np.testing.assert_array_equal(npy, ids_new.astype(np.int64))
+    # final graph: optimize in the reordered space, translated back to the input order
+    g_new = orc.optimize(orc.sanitize(ids_new)[0], 16)
+    want_graph, _ = orc.permute_graph(g_new, inv, True, False)
+    np.testing.assert_array_equal(graph, want_graph.view(np.uint32))
+    # translate_ids on the reordered-space graph, as .bin and as .npy
+    gta.write_graph(str(sub / "graph_new_ids.bin"), g_new)
+    run(os.path.join(BIN, "translate_ids"), "-g", sub / "graph_new_ids.bin", "-p", sub / "inverse_perm.bin",
+        "-o", sub / "translated.bin")
+    np.testing.assert_array_equal(gta.read_graph(str(sub / "translated.bin")), graph)
+    run(os.path.join(BIN, "translate_ids"), "-g", sub / "neighbors.npy", "-p", sub / "inverse_perm.bin",
+        "-o", sub / "neighbors_orig.npy")
+    np.testing.assert_array_equal(np.load(sub / "neighbors_orig.npy"), ri.astype(np.int64))
 
 
 def test_optimize_tool_sorts_and_prunes(data):

@@ -177,3 +177,47 @@ def test_search_entries_follow_the_reference_generator():
         u = np.unique(rng.integers(0, 1000, size=4, endpoint=False))
         np.testing.assert_array_equal(e[i, :u.size], u)
         assert (e[i, u.size:] == -1).all()
+
+
+# ---------------------------------------------------------------- bucket-contiguous renumbering
+def test_bucket_order_matches_reference(golden):
+    f = golden("reorder.npz")
+    c = 0
+    while f"order_{c}" in f:
+        got = orc.bucket_order(f[f"order_adj_{c}"].view(np.int32), int(f[f"order_window_{c}"]))
+        np.testing.assert_array_equal(got, f[f"order_{c}"])
+        c += 1
+    assert c == 5
+
+
+def test_translate_matches_reference(golden):
+    f = golden("reorder.npz")
+    out, bad = orc.permute_graph(f["translate_g"], f["translate_inv"], True, False)
+    assert bad == 0
+    np.testing.assert_array_equal(out.view(np.uint32), f["translate_bin"])
+    out, bad = orc.permute_graph(f["translate_g_pad"].astype(np.int32), f["translate_inv"], True, True)
+    assert bad == 0
+    np.testing.assert_array_equal(out.astype(np.int64), f["translate_npy"])
+    # renumbering to the new ids and back is the identity
+    fwd, _ = orc.permute_graph(f["translate_g"], f["translate_inv"], False, False)
+    back, _ = orc.permute_graph(fwd, f["translate_inv"], True, False)
+    np.testing.assert_array_equal(back.view(np.uint32), f["translate_g"])
+
+
+def test_bucket_reorder_known_answer():
+    # buckets of points 0..7: [2, 0, 1, 2, 0, 2, 1, 0]; processing order 2, 0, 1
+    assign = np.array([2, 0, 1, 2, 0, 2, 1, 0], np.int32)
+    inv, off = orc.bucket_reorder(assign, 3, order=np.array([2, 0, 1], np.int32))
+    np.testing.assert_array_equal(inv, [0, 3, 5, 1, 4, 7, 2, 6])
+    np.testing.assert_array_equal(off, [0, 3, 6, 8])
+    # column 0 of a top-2 table, identity order
+    top2 = np.stack([assign, (assign + 1) % 3], 1)
+    inv2, off2 = orc.bucket_reorder(top2.reshape(-1), 3, stride=2)
+    np.testing.assert_array_equal(inv2, [1, 4, 7, 2, 6, 0, 3, 5])
+    np.testing.assert_array_equal(off2, [0, 3, 5, 8])
+    # an unassigned point is left out (the caller treats that as an error)
+    inv3, _ = orc.bucket_reorder(np.array([0, -1, 1], np.int32), 2)
+    np.testing.assert_array_equal(inv3, [0, 2])
+    # a duplicate in inverse_perm is refused
+    _, bad = orc.permute_graph(np.zeros((3, 1), np.int32), np.array([0, 0, 1], np.uint32), True, False)
+    assert bad == -1

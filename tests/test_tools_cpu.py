@@ -29,6 +29,7 @@ def run(*args):
                  "--knn-k", "--nprobe", "--skip-dists", "--skip-npy", "--out-of-core", "--centroid-ratio"]),
     ("optimize", ["--input", "--knn-graph", "--output", "--output-degree", "--skip-sort", "--save-npy",
                   "--force-chunked", "--gpu-fit-margin"]),
+    ("translate_ids", ["--graph", "--inverse-perm", "--output", "--out-buffer-mb"]),
 ])
 def test_help_lists_reference_options(name, opts):
     r = run(tool(name), "--help")
@@ -66,3 +67,14 @@ def test_optimize_argument_errors(tmp_path):
     assert r.returncode == 1 and "> input degree" in r.stderr
     r = run(op, "-i", data, "-g", knn, "-o", str(tmp_path / "g.bin"), "--output-degree", "0")
     assert r.returncode == 1 and "must be > 0" in r.stderr
+
+
+def test_translate_ids_argument_errors(tmp_path):
+    tr = tool("translate_ids")
+    g = str(tmp_path / "g.bin")
+    gta.write_graph(g, np.zeros((5, 2), np.uint32))
+    gta.write_u32(str(tmp_path / "inv.bin"), np.arange(4, dtype=np.uint32))
+    r = run(tr, "-g", g, "-p", str(tmp_path / "inv.bin"), "-o", str(tmp_path / "o.bin"))
+    assert r.returncode == 1 and "graph N=5" in r.stderr
+    r = run(tr, "-g", g, "-o", str(tmp_path / "o.bin"))
+    assert r.returncode == 1 and "--inverse-perm" in r.stderr
