@@ -217,6 +217,10 @@ void assign_topk_impl(const float* Xp, const float* xn, int64_t n, int d, int d_
                       int B, int k, int32_t* ids, float* dists, int* err, cudaStream_t st)
 {
     GTA_REQUIRE(k >= 1 && k <= B, kInvalid, "assign: need 1 <= k <= B");
+    if (assign_exact_applies(B, k)) {  // few centroids: exact chain on the FP32 pipe, no screen
+        assign_exact(Xp, GTA_F32, n, d_pad, d, nullptr, Cp, d_pad, B, k, ids, dists, st);
+        return;
+    }
     std::vector<WorkItem> wl;
     wl.reserve(static_cast<size_t>((n + 127) / 128));
     for (int64_t r = 0; r < n; r += 128)
@@ -231,15 +235,28 @@ void assign_topk_impl(const float* Xp, const float* xn, int64_t n, int d, int d_
     dist_topk(pr, st);
 }
 
+// The sample's rows in the dataset's own element type (for the exact assignment, which then
+// reads 8-bit rows instead of the f32 copy): row_ids[i] is sample row i's row of X.
+struct RawRows {
+    const void* X = nullptr;
+    int dtype = GTA_F32;
+    int ldx = 0;
+    const int32_t* row_ids = nullptr;
+};
+
 void kmeans_fit_impl(const float* Xs, const float* xn, int64_t n_s, int d, int d_pad, float* C, float* cn, int B,
-                     int iters, int32_t* assign_out, int* err, cudaStream_t st)
+                     int iters, int32_t* assign_out, int* err, cudaStream_t st, bool integer_rows = false,
+                     const RawRows& raw = RawRows())
 {
     DevBuf<int32_t> ids(static_cast<size_t>(n_s), st);
     DevBuf<float> dd(static_cast<size_t>(n_s), st);
     DevBuf<float> C2(static_cast<size_t>(B) * d_pad, st);
     for (int it = 0; it < iters; ++it) {
-        assign_topk_impl(Xs, xn, n_s, d, d_pad, C, cn, B, 1, ids.get(), dd.get(), err, st);
-        centroid_update(Xs, n_s, d, d_pad, ids.get(), C, B, C2.get(), cn, err, st);
+        if (raw.X && assign_exact_applies(B, 1))
+            assign_exact(raw.X, raw.dtype, n_s, raw.ldx, d, raw.row_ids, C, d_pad, B, 1, ids.get(), dd.get(), st);
+        else
+            assign_topk_impl(Xs, xn, n_s, d, d_pad, C, cn, B, 1, ids.get(), dd.get(), err, st);
+        centroid_update(Xs, n_s, d, d_pad, ids.get(), C, B, C2.get(), cn, err, st, integer_rows);
         GTA_CUDA(cudaMemcpyAsync(C, C2.get(), sizeof(float) * static_cast<size_t>(B) * d_pad, cudaMemcpyDeviceToDevice, st));
     }
     if (assign_out) {
@@ -356,7 +373,6 @@ void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const
         ProfScope prof("sample_gather", static_cast<double>(n_s) * (d * elem_size(ds.dtype) + d32 * 4.0), st);
         convert_rows(X, ds.dtype, d, sid.get(), n_s, Xs.get(), kElemF32, d32, xs_n.get(), st);
     }
-    sid.release();
     DevBuf<float> C(static_cast<size_t>(B) * d32, st), cn(static_cast<size_t>(B), st);
     if (p.init_centroids) {
         copy_rows_padded(C.get(), d32, p.init_centroids, d, B, p.init_on_device != 0, st);
@@ -373,22 +389,31 @@ void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const
     convert_rows(C.get(), GTA_F32, d32, nullptr, B, nullptr, kElemF32, d32, cn.get(), st);
     {
         ProfScope prof("kmeans_fit_total", 0.0, st);
-        kmeans_fit_impl(Xs.get(), xs_n.get(), n_s, d, d32, C.get(), cn.get(), B, p.kmeans_iters, nullptr, err.get(), st);
+        RawRows raw;
+        if (ds.dtype != GTA_F32) raw = RawRows{X, ds.dtype, d, sid.get()};  // 8-bit rows: a quarter of the f32 reads
+        kmeans_fit_impl(Xs.get(), xs_n.get(), n_s, d, d32, C.get(), cn.get(), B, p.kmeans_iters, nullptr, err.get(), st,
+                        ds.dtype != GTA_F32, raw);
     }
     Xs.release();
     xs_n.release();
+    sid.release();
     if (o.centroids) unpad_rows(o.centroids, d, C.get(), d32, B, true, st);
 
     // ---- top-2 bucket membership of every point
     DevBuf<int32_t> top2(static_cast<size_t>(N) * 2, st);
     {
         ProfScope prof("top2_total", 0.0, st);
-        DevBuf<float> Xf(static_cast<size_t>(N) * d32, st), xn(static_cast<size_t>(N), st), t2d(static_cast<size_t>(N) * 2, st);
-        {
-            ProfScope prof("convert_x", static_cast<double>(N) * (d * elem_size(ds.dtype) + d32 * 4.0), st);
-            convert_rows(X, ds.dtype, d, nullptr, N, Xf.get(), kElemF32, d32, xn.get(), st);
+        DevBuf<float> t2d(static_cast<size_t>(N) * 2, st);
+        if (assign_exact_applies(B, 2)) {  // straight from the dataset's own element type
+            assign_exact(X, ds.dtype, N, d, d, nullptr, C.get(), d32, B, 2, top2.get(), t2d.get(), st);
+        } else {
+            DevBuf<float> Xf(static_cast<size_t>(N) * d32, st), xn(static_cast<size_t>(N), st);
+            {
+                ProfScope prof("convert_x", static_cast<double>(N) * (d * elem_size(ds.dtype) + d32 * 4.0), st);
+                convert_rows(X, ds.dtype, d, nullptr, N, Xf.get(), kElemF32, d32, xn.get(), st);
+            }
+            assign_topk_impl(Xf.get(), xn.get(), N, d, d32, C.get(), cn.get(), B, 2, top2.get(), t2d.get(), err.get(), st);
         }
-        assign_topk_impl(Xf.get(), xn.get(), N, d, d32, C.get(), cn.get(), B, 2, top2.get(), t2d.get(), err.get(), st);
     }
     if (o.top2) GTA_CUDA(cudaMemcpyAsync(o.top2, top2.get(), sizeof(int32_t) * 2 * N, cudaMemcpyDeviceToDevice, st));
     DevBuf<int32_t> members(static_cast<size_t>(N) * 2, st);

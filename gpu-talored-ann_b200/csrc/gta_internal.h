@@ -125,8 +125,10 @@ void convert_rows(const void* X, int dtype, int d, const int32_t* row_ids, int64
 void sample_ids(int64_t N, int64_t n_s, uint64_t seed, int32_t* out, cudaStream_t st);
 void kmeanspp_init(const float* pool, const float* pool_norm, int64_t pool_n, int d, int d_pad, int32_t B,
                    uint64_t seed, float* centroids, int* err, cudaStream_t st);
+// integer_rows: every row value is an integer (8-bit data), so the fp64 sums may be formed in
+// any order (exact); otherwise they are accumulated in ascending point order
 void centroid_update(const float* Xs, int64_t n_s, int d, int d_pad, const int32_t* assign, const float* C_in,
-                     int32_t B, float* C_out, float* C_norm, int* err, cudaStream_t st);
+                     int32_t B, float* C_out, float* C_norm, int* err, cudaStream_t st, bool integer_rows = false);
 void check_ids(const int32_t* ids, int64_t n, int32_t hi, int* err, cudaStream_t st);
 void build_memberships(const int32_t* top2, int64_t N, int32_t B, int32_t* members, int64_t* offsets,
                        int64_t* mem_row, int* err, cudaStream_t st);
@@ -149,6 +151,13 @@ void max_sqrt(const float* v, int64_t n, float* out, cudaStream_t st);
 void graph_search(const void* base, int dtype, int64_t n, int d, const uint32_t* graph, int kg, const void* queries,
                   int64_t nq, const int32_t* entries, int ne, int topk, int ef, int32_t* out_ids, float* out_dists,
                   int* err, cudaStream_t st);
+// exact assignment to few centroids on the FP32 pipe (assign.cu); X rows of `dtype` with row
+// stride ldx elements, centroids f32 with row stride ldc
+constexpr int kAssignExactMaxB = 384;
+bool assign_exact_applies(int B, int k);
+// (row_ids: row of X for each point, null = identity)
+void assign_exact(const void* X, int dtype, int64_t n, int ldx, int d, const int32_t* row_ids, const float* C, int ldc,
+                  int B, int k, int32_t* ids, float* dists, cudaStream_t st);
 // bucket-contiguous renumbering (reorder.cu)
 void bucket_reorder(const int32_t* assign, int64_t n, int32_t stride, int32_t B, const int32_t* order,
                     uint32_t* inverse_perm, int64_t* offsets, int* err, cudaStream_t st);

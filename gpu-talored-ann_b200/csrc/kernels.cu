@@ -432,6 +432,47 @@ __global__ void centroid_sum_kernel(const float* __restrict__ Xs, int d, int d_p
     }
 }
 
+// Integer-valued rows (8-bit data): every partial sum is an integer below 2^53, so fp64 adds
+// are exact in any order and the sums equal the ascending-order sums bit for bit.  A CTA
+// takes kSumRange consecutive sorted members (one thread per dimension), accumulates runs of
+// one centroid in registers and adds each run to the centroid's sums atomically.
+constexpr int kSumRange = 256;
+
+__global__ void centroid_sum_int_kernel(const float* __restrict__ Xs, int d, int d_pad, const int32_t* __restrict__ order,
+                                        const int32_t* __restrict__ keys_sorted, int64_t n, int32_t B,
+                                        double* __restrict__ sums)
+{
+    const int64_t lo = static_cast<int64_t>(blockIdx.x) * kSumRange;
+    const int64_t hi = lo + kSumRange < n ? lo + kSumRange : n;
+    for (int k = threadIdx.x; k < d; k += blockDim.x) {
+        int32_t cur = keys_sorted[lo];
+        double acc = 0.0;
+        for (int64_t j = lo; j < hi; ++j) {
+            const int32_t a = keys_sorted[j];
+            if (a != cur) {
+                if (cur >= 0 && cur < B) atomicAdd(&sums[static_cast<int64_t>(cur) * d + k], acc);
+                cur = a;
+                acc = 0.0;
+            }
+            acc += static_cast<double>(Xs[static_cast<int64_t>(order[j]) * d_pad + k]);
+        }
+        if (cur >= 0 && cur < B) atomicAdd(&sums[static_cast<int64_t>(cur) * d + k], acc);
+    }
+}
+
+__global__ void centroid_means_int_kernel(const double* __restrict__ sums, const int64_t* __restrict__ offsets,
+                                          const float* __restrict__ C_in, int32_t B, int d, int d_pad,
+                                          float* __restrict__ C_out)
+{
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i >= static_cast<int64_t>(B) * d_pad) return;
+    const int64_t b = i / d_pad;
+    const int k = static_cast<int>(i - b * d_pad);
+    const int64_t cnt = offsets[b + 1] - offsets[b];
+    if (k >= d) C_out[i] = 0.0f;
+    else C_out[i] = cnt > 0 ? static_cast<float>(sums[b * d + k] / static_cast<double>(cnt)) : C_in[i];
+}
+
 // Per-centroid fp64 sums (members in sorted order) and counts of a shard.
 __global__ void centroid_partial_kernel(const float* __restrict__ Xs, int d, int d_pad,
                                         const int32_t* __restrict__ order, const int64_t* __restrict__ offsets,
@@ -1001,7 +1042,7 @@ void check_ids(const int32_t* ids, int64_t n, int32_t hi, int* err, cudaStream_t
 }
 
 void centroid_update(const float* Xs, int64_t n_s, int d, int d_pad, const int32_t* assign, const float* C_in,
-                     int32_t B, float* C_out, float* C_norm, int* err, cudaStream_t st)
+                     int32_t B, float* C_out, float* C_norm, int* err, cudaStream_t st, bool integer_rows)
 {
     check_ids(assign, n_s, B, err, st);
     DevBuf<int32_t> keys_out(n_s, st), idx_in(n_s, st), idx_out(n_s, st);
@@ -1019,8 +1060,18 @@ void centroid_update(const float* Xs, int64_t n_s, int d, int d_pad, const int32
     seg_offsets_kernel<<<blocks_for(B + 1, 256), 256, 0, st>>>(keys_out.get(), n_s, B, offsets.get());
     count_launches(1);
     ProfScope prof("kmeans_update", 4.0 * static_cast<double>(n_s) * d, st);
-    centroid_sum_kernel<<<B, 128, 0, st>>>(Xs, d, d_pad, idx_out.get(), offsets.get(), C_in, C_out);
-    count_launches(1);
+    if (integer_rows && n_s > 0) {
+        DevBuf<double> sums(static_cast<size_t>(B) * d, st);
+        GTA_CUDA(cudaMemsetAsync(sums.get(), 0, sizeof(double) * static_cast<size_t>(B) * d, st));
+        centroid_sum_int_kernel<<<blocks_for(n_s, kSumRange), 128, 0, st>>>(Xs, d, d_pad, idx_out.get(), keys_out.get(),
+                                                                            n_s, B, sums.get());
+        centroid_means_int_kernel<<<blocks_for(static_cast<int64_t>(B) * d_pad, 256), 256, 0, st>>>(
+            sums.get(), offsets.get(), C_in, B, d, d_pad, C_out);
+        count_launches(2);
+    } else {
+        centroid_sum_kernel<<<B, 128, 0, st>>>(Xs, d, d_pad, idx_out.get(), offsets.get(), C_in, C_out);
+        count_launches(1);
+    }
     if (C_norm) convert_rows(C_out, 0, d_pad, nullptr, B, C_out, kElemF32, d_pad, C_norm, st);
     GTA_CUDA(cudaGetLastError());
 }
