@@ -666,70 +666,100 @@ constexpr int kPruneWarps = 8;
 // when D's row repeats an id).  The detour count of kAB is the number of masks
 // holding bit kAB, summed over the warp with ballots; no per-candidate
 // cross-lane reduction is needed.
-constexpr int kPruneHash = 1024;
 
 __device__ __forceinline__ uint32_t hash_id(uint32_t id, uint32_t mask) { return (id * 2654435761u) >> 7 & mask; }
+
+// Per warp in dynamic shared memory: the id -> rank hash of the row (cap 64-bit slots, id in
+// the high word, rank in the low word; all ones = empty), the row, its detour counts and the
+// count histogram / next free position of every count.
+__host__ __device__ __forceinline__ uint32_t prune_cap(int M)
+{
+    uint32_t cap = 64;
+    while (cap < 8u * static_cast<uint32_t>(M)) cap <<= 1;
+    return cap;
+}
+
+// bytes of one warp's region, a multiple of 16 so that every warp's 64-bit slots stay aligned
+__host__ __device__ __forceinline__ uint32_t prune_per_warp(int M)
+{
+    return (prune_cap(M) * 8u + 12u * static_cast<uint32_t>(M) + 15u) & ~15u;
+}
 
 __global__ void __launch_bounds__(kPruneWarps * 32)
     prune_kernel(const uint32_t* __restrict__ g, int64_t N, int M, int K, const int32_t* __restrict__ order,
                  int64_t row0, int64_t n_rows, uint32_t* __restrict__ out, int* err)
 {
-    __shared__ uint32_t s_hkey[kPruneWarps][kPruneHash];
-    __shared__ uint8_t s_hrank[kPruneWarps][kPruneHash];
-    __shared__ uint32_t s_row[kPruneWarps][kMaxM];
-    __shared__ uint32_t s_cnt[kPruneWarps][kMaxM];
+    extern __shared__ __align__(16) uint8_t prune_smem[];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const uint32_t cap = prune_cap(M);
+    const uint32_t mask = cap - 1;
+    const size_t per_warp = prune_per_warp(M);
+    uint64_t* s_slot = reinterpret_cast<uint64_t*>(prune_smem + w * per_warp);
+    uint32_t* s_row = reinterpret_cast<uint32_t*>(s_slot + cap);
+    uint32_t* s_cnt = s_row + M;
+    uint32_t* s_next = s_cnt + M;
     const int64_t gw = static_cast<int64_t>(blockIdx.x) * kPruneWarps + w;
     if (gw >= n_rows) return;
     // rows row0 .. row0 + n_rows - 1 of the graph, visited in `order` (local indices)
     const int64_t orow = order ? static_cast<int64_t>(order[gw]) : gw;
     const int64_t a = row0 + orow;
-    uint32_t cap = 64;
-    while (cap < 8u * static_cast<uint32_t>(M)) cap <<= 1;
-    const uint32_t mask = cap - 1;
-    for (uint32_t h = lane; h < cap; h += 32) s_hkey[w][h] = kEmpty;
+    for (uint32_t h = lane; h < cap; h += 32) s_slot[h] = ~0ull;
     const uint32_t* ra = g + a * M;
-    for (int k = lane; k < M; k += 32) s_row[w][k] = ra[k];
-    __syncwarp();
     for (int k = lane; k < M; k += 32) {
-        const uint32_t id = s_row[w][k];
-        uint32_t h = hash_id(id, mask);
-        for (;;) {
-            const uint32_t old = atomicCAS(&s_hkey[w][h], kEmpty, id);
-            if (old == kEmpty) { s_hrank[w][h] = static_cast<uint8_t>(k); break; }
-            h = (h + 1) & mask;
+        s_row[k] = ra[k];
+        s_cnt[k] = 0;
+        s_next[k] = 0;
+    }
+    __syncwarp();
+    // A repeated id (sanitize pads with the row's first neighbour) gets a slot per rank; every
+    // slot holding the id that a later copy passes is flagged (kDupFlag), so a lookup goes on
+    // past a match only when more copies follow along the probe chain.
+    constexpr uint64_t kDupFlag = 1ull << 31;
+    for (int k = lane; k < M; k += 32) {
+        const uint32_t id = s_row[k];
+        const uint64_t mine = (static_cast<uint64_t>(id) << 32) | static_cast<uint32_t>(k);
+        for (uint32_t h = hash_id(id, mask);; h = (h + 1) & mask) {
+            unsigned long long* sp = reinterpret_cast<unsigned long long*>(&s_slot[h]);
+            const unsigned long long old = atomicCAS(sp, ~0ull, mine);
+            if (old == ~0ull) break;
+            if (static_cast<uint32_t>(old >> 32) == id) atomicOr(sp, kDupFlag);
         }
     }
     __syncwarp();
-    // this lane's masks: slot j serves kAD = lane + 32 j, bit kAB of word kAB / 64
+    // Lane l takes kAD = l + 32 j and marks in a mask every later rank kAB whose id appears in
+    // row(row[kAD]) (each (D, B) pair once); at load factor <= 1/8 almost every lookup ends at
+    // its first slot, so the probe loop is the rare path.
     constexpr int kJ = kMaxM / 32;
-    uint64_t mk[kJ][2];
     const int n_j = (M - 1 + 31) / 32;
     const bool vec = (M & 3) == 0;
 #pragma unroll
     for (int j = 0; j < kJ; ++j) {
-        mk[j][0] = 0;
-        mk[j][1] = 0;
         const int kAD = lane + 32 * j;
         if (j >= n_j || kAD >= M - 1) continue;
-        const uint32_t dd = s_row[w][kAD];
+        const uint32_t dd = s_row[kAD];
         if (static_cast<int64_t>(dd) >= N) {
             atomicCAS(err, 0, kDevBadIndex);
             continue;
         }
         const uint32_t* rd = g + static_cast<int64_t>(dd) * M;
+        uint64_t m0 = 0, m1 = 0;
         auto look = [&](uint32_t v) {
-            for (uint32_t h = hash_id(v, mask);; h = (h + 1) & mask) {
-                const uint32_t key = s_hkey[w][h];
-                if (key == kEmpty) break;
-                if (key == v) {
-                    const int kAB = s_hrank[w][h];
-                    if (kAB > kAD) {
-                        const uint64_t bit = 1ull << (kAB & 63);
-                        if (kAB < 64) mk[j][0] |= bit;
-                        else mk[j][1] |= bit;
-                    }
+            uint32_t h = hash_id(v, mask);
+            for (;;) {
+                uint64_t sl = s_slot[h];
+                while (static_cast<uint32_t>(sl >> 32) != v) {
+                    if (sl == ~0ull) return;
+                    h = (h + 1) & mask;
+                    sl = s_slot[h];
                 }
+                const int kAB = static_cast<int>(static_cast<uint32_t>(sl) & 0x7fu);
+                if (kAB > kAD) {
+                    const uint64_t bit = 1ull << (kAB & 63);
+                    if (kAB < 64) m0 |= bit;
+                    else m1 |= bit;
+                }
+                if (!(sl & kDupFlag)) return;
+                h = (h + 1) & mask;
             }
         };
         if (vec) {
@@ -741,30 +771,52 @@ __global__ void __launch_bounds__(kPruneWarps * 32)
         } else {
             for (int e = 0; e < M; ++e) look(rd[e]);
         }
-    }
-    // detour count of every rank: how many lanes' masks hold its bit
-    for (int kAB = 0; kAB < M; ++kAB) {
-        int c = 0;
-#pragma unroll
-        for (int j = 0; j < kJ; ++j) {
-            if (j >= n_j) break;
-            const uint64_t word = kAB < 64 ? mk[j][0] : mk[j][1];
-            c += __popc(__ballot_sync(0xffffffffu, (word >> (kAB & 63)) & 1ull));
+        // detour counts: one shared-memory increment per marked (D, B) pair
+        while (m0) {
+            atomicAdd(&s_cnt[__ffsll(static_cast<long long>(m0)) - 1], 1u);
+            m0 &= m0 - 1;
         }
-        if (lane == (kAB & 31)) s_cnt[w][kAB] = static_cast<uint32_t>(c);
+        while (m1) {
+            atomicAdd(&s_cnt[64 + __ffsll(static_cast<long long>(m1)) - 1], 1u);
+            m1 &= m1 - 1;
+        }
     }
     __syncwarp();
-    // position of entry k = #{k' : (cnt[k'], k') < (cnt[k], k)}; the first K positions are kept
-    for (int k = lane; k < M; k += 32) {
-        const uint32_t c = s_cnt[w][k];
-        int pos = 0;
-        for (int k2 = 0; k2 < M; ++k2) {
-            const uint32_t c2 = s_cnt[w][k2];
-            pos += (c2 < c) || (c2 == c && k2 < k);
+    // position of entry k = #{k' : (cnt[k'], k') < (cnt[k], k)}: counts histogram -> exclusive
+    // prefix = first position of each count; entries of equal count in ascending k
+    for (int k = lane; k < M; k += 32) atomicAdd(&s_next[s_cnt[k]], 1u);
+    __syncwarp();
+    uint32_t carry = 0;
+    for (int c0 = 0; c0 < M; c0 += 32) {
+        const uint32_t v = c0 + lane < M ? s_next[c0 + lane] : 0u;
+        uint32_t incl = v;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+            if (lane >= o) incl += t;
         }
-        if (pos < K) out[orow * K + pos] = s_row[w][k];
+        if (c0 + lane < M) s_next[c0 + lane] = carry + incl - v;
+        carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    __syncwarp();
+    const unsigned lt = (1u << lane) - 1u;
+    for (int k0 = 0; k0 < M; k0 += 32) {
+        const int k = k0 + lane;
+        const bool has = k < M;
+        const uint32_t c = has ? s_cnt[k] : 0xFFFFFFFFu;
+        const unsigned grp = __match_any_sync(0xffffffffu, c);
+        const uint32_t base = has ? s_next[c] : 0u;
+        __syncwarp();
+        if (has) {
+            const uint32_t pos = base + static_cast<uint32_t>(__popc(grp & lt));
+            if (pos < static_cast<uint32_t>(K)) out[orow * K + pos] = s_row[k];
+            if ((grp & lt) == 0u) s_next[c] = base + static_cast<uint32_t>(__popc(grp));  // the group's first lane
+        }
+        __syncwarp();
     }
 }
+
+size_t prune_smem_bytes(int M) { return static_cast<size_t>(kPruneWarps) * prune_per_warp(M); }
 
 // Received memberships grouped by (bucket, other bucket), stable in arrival order.
 __global__ void group_keys_kernel(const int32_t* __restrict__ bucket, const int32_t* __restrict__ other, int64_t n,
@@ -1137,7 +1189,9 @@ void prune_detour(const uint32_t* g, int64_t N, int M, int K, const int32_t* ord
 {
     GTA_REQUIRE(M >= 2 && M <= kMaxM && K >= 1 && K <= M, kInvalid, "prune: need 1 <= K <= M <= 128");
     ProfScope prof("prune", (4.0 * M * (M + 1) + 4.0 * K) * static_cast<double>(N), st);
-    prune_kernel<<<blocks_for(N, kPruneWarps), kPruneWarps * 32, 0, st>>>(g, N, M, K, order, 0, N, out, err);
+    const size_t smem = prune_smem_bytes(M);
+    GTA_CUDA(cudaFuncSetAttribute(prune_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    prune_kernel<<<blocks_for(N, kPruneWarps), kPruneWarps * 32, smem, st>>>(g, N, M, K, order, 0, N, out, err);
     count_launches(1);
     GTA_CUDA(cudaGetLastError());
 }
@@ -1348,7 +1402,10 @@ void prune_rows(const uint32_t* g, int64_t N, int M, int K, const int32_t* order
     GTA_REQUIRE(M >= 2 && M <= kMaxM && K >= 1 && K <= M, kInvalid, "prune: need 1 <= K <= M <= 128");
     GTA_REQUIRE(row0 >= 0 && n_rows >= 0 && row0 + n_rows <= N, kInvalid, "prune: row range outside the graph");
     ProfScope prof("prune", (4.0 * M * (M + 1) + 4.0 * K) * static_cast<double>(n_rows), st);
-    prune_kernel<<<blocks_for(n_rows, kPruneWarps), kPruneWarps * 32, 0, st>>>(g, N, M, K, order, row0, n_rows, out, err);
+    const size_t smem = prune_smem_bytes(M);
+    GTA_CUDA(cudaFuncSetAttribute(prune_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    prune_kernel<<<blocks_for(n_rows, kPruneWarps), kPruneWarps * 32, smem, st>>>(g, N, M, K, order, row0, n_rows, out,
+                                                                                    err);
     count_launches(1);
     GTA_CUDA(cudaGetLastError());
 }
