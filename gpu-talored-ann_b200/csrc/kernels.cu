@@ -744,6 +744,9 @@ __global__ void __launch_bounds__(kPruneWarps * 32)
         const uint32_t* rd = g + static_cast<int64_t>(dd) * M;
         uint64_t m0 = 0, m1 = 0;
         auto look = [&](uint32_t v) {
+            // ids of the graph are < N < 2^31; anything else (all ones included, which would
+            // read as the high word of an empty slot) is in no row
+            if (static_cast<int64_t>(v) >= N) return;
             uint32_t h = hash_id(v, mask);
             for (;;) {
                 uint64_t sl = s_slot[h];
