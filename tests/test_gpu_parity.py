@@ -315,3 +315,14 @@ def test_invalid_arguments_are_rejected():
     with pytest.raises(gta.GtaError) as e:
         gta.optimize(dev(np.zeros((10, 4), np.int32)), 8)   # K > M
     assert e.value.code == 1
+
+
+def test_prune_refuses_out_of_range_neighbours():
+    """A neighbour id outside [0, N) is a data error (status 5), never an out-of-range read."""
+    rng = np.random.default_rng(9)
+    g = np.stack([rng.choice(np.delete(np.arange(50), i), 8, replace=False) for i in range(50)]).astype(np.uint32)
+    g[7, 3] = 50 + 11          # a neighbour row that does not exist
+    g[9, 5] = 0xFFFFFFFF       # all ones
+    with pytest.raises(gta.GtaError) as e:
+        gta.prune(dev(g.view(np.int32)), 4)
+    assert e.value.code == 5
