@@ -801,19 +801,10 @@ __global__ void __launch_bounds__(kThreads, kV)
             if (st_on) cyc_wait += clock64() - w0;
             tc_fence_after();
             const uint32_t tbase = lane_base + static_cast<uint32_t>(b * kTN);
-            uint32_t vn[16];
-            __syncwarp();
-            tmem_ld_32x32b_x16(tbase, vn);
-#pragma unroll 1
-            for (int c = 0; c < kTN / 16; ++c) {  // slices of 16 columns; slice c+1 loads while c is scanned
-                uint32_t v[16];
-                tmem_ld_wait_regs(vn);
-#pragma unroll
-                for (int e = 0; e < 16; ++e) v[e] = vn[e];
-                if (c + 1 < kTN / 16) {
-                    __syncwarp();
-                    tmem_ld_32x32b_x16(tbase + static_cast<uint32_t>((c + 1) * 16), vn);
-                }
+            // slices of 16 columns in two register sets: slice c + 1 loads into the other set
+            // while c is scanned (no register copies; the slice loop is unrolled)
+            uint32_t va[16], vb[16];
+            auto scan_slice = [&](int c, const uint32_t (&v)[16], uint32_t (&nxt)[16], bool nxt_in_flight) {
                 const int self_e = (ct == self_ct && c == self_c) ? (lane & 15) : -1;
                 const uint32_t c0 = static_cast<uint32_t>(ct * kTN + c * 16);
                 const float4* pn4 = reinterpret_cast<const float4*>(pnw + c * 16);
@@ -848,7 +839,7 @@ __global__ void __launch_bounds__(kThreads, kV)
                     nb += npass;
                 }
                 if (__any_sync(0xffffffffu, nb > kBuf - 16)) {
-                    if (c + 1 < kTN / 16) tmem_ld_wait_regs(vn);  // no TMEM load in flight across the call
+                    if (nxt_in_flight) tmem_ld_wait_regs(nxt);  // no TMEM load in flight across the call
                     const long long f0 = st_on ? clock64() : 0;
                     n_pass += nb;
                     ++n_flush;
@@ -861,6 +852,28 @@ __global__ void __launch_bounds__(kThreads, kV)
                     if (st_on) cyc_flush += clock64() - f0;
                 }
                 __syncwarp();
+            };
+            constexpr int kSlices = kTN / 16;
+            __syncwarp();
+            tmem_ld_32x32b_x16(tbase, va);
+#pragma unroll
+            for (int c = 0; c < kSlices; ++c) {
+                const bool more = c + 1 < kSlices;
+                if ((c & 1) == 0) {
+                    tmem_ld_wait_regs(va);
+                    if (more) {
+                        __syncwarp();
+                        tmem_ld_32x32b_x16(tbase + static_cast<uint32_t>((c + 1) * 16), vb);
+                    }
+                    scan_slice(c, va, vb, more);
+                } else {
+                    tmem_ld_wait_regs(vb);
+                    if (more) {
+                        __syncwarp();
+                        tmem_ld_32x32b_x16(tbase + static_cast<uint32_t>((c + 1) * 16), va);
+                    }
+                    scan_slice(c, vb, va, more);
+                }
             }
             tc_fence_before();
             __syncwarp();
