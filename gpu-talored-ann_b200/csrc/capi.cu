@@ -473,6 +473,276 @@ void build_bucket_impl(const gta_dataset& ds, const gta_bucket_params& p, const 
     }
 }
 
+// ---------------------------------------------------------------- reference bucketing (bucket2)
+struct Bucket2Out {
+    int32_t* ids;        // device [N x M]
+    float* dists;        // device [N x M]
+    int32_t* assign;     // device [N] or null
+    int32_t* cid;        // device [B_req] or null
+    int32_t n_buckets;   // set by the round
+};
+
+constexpr int kKparRounds = 3;            // bucket.cu:2964 FIXED_NITER
+constexpr double kKparOvershoot = 1.5;    // bucket.cu:2965 TOTAL_OVERSHOOT
+constexpr size_t kPoolBudgetBytes = size_t(8) << 30;  // gathered pool rows held at once
+
+int64_t bucket2_requested(int64_t N, float ratio)
+{
+    const double r = ratio > 0.0f ? static_cast<double>(ratio) : 0.01;
+    return std::max<int64_t>(2, static_cast<int64_t>(static_cast<double>(N) * r));
+}
+
+// KMeans|| candidates (bucket.cu:2919-3117) and their uniform subsample (:3150-3172) -> point ids
+std::vector<int32_t> kmeans_parallel_ids(const float* Xf, const float* xn, int64_t N, int d, int d32, const void* X,
+                                         int dtype, int64_t n_req, uint64_t seed, int* err, cudaStream_t st)
+{
+    const int32_t c0 = static_cast<int32_t>(mix64(seed ^ 0xA0761D6478BD642Full) % static_cast<uint64_t>(N));
+    std::vector<int32_t> cand{c0};
+    DevBuf<uint8_t> chosen(static_cast<size_t>(N), st), sel(static_cast<size_t>(N), st);
+    GTA_CUDA(cudaMemsetAsync(chosen.get(), 0, static_cast<size_t>(N), st));
+    GTA_CUDA(cudaMemsetAsync(chosen.get() + c0, 1, 1, st));
+    DevBuf<float> min_d(static_cast<size_t>(N), st), d_new(static_cast<size_t>(N), st);
+    DevBuf<int32_t> tmp_ids(static_cast<size_t>(N), st), new_ids(static_cast<size_t>(N), st);
+    DevBuf<double> psi(1, st);
+    // distance to the first point (one centroid: the exact chain)
+    assign_topk_impl(Xf, xn, N, d, d32, Xf + static_cast<int64_t>(c0) * d32, xn + c0, 1, 1, tmp_ids.get(), min_d.get(),
+                     err, st);
+    const double lk = kKparOvershoot / kKparRounds * static_cast<double>(n_req);
+    for (int r = 0; r < kKparRounds; ++r) {
+        kpar_psi(min_d.get(), N, psi.get(), st);
+        kpar_sample(min_d.get(), N, seed, r, lk, psi.get(), chosen.get(), sel.get(), st);
+        const int64_t n_new = select_flagged(sel.get(), N, new_ids.get(), st);
+        if (n_new == 0) break;
+        const size_t old = cand.size();
+        cand.resize(old + static_cast<size_t>(n_new));
+        GTA_CUDA(cudaMemcpyAsync(cand.data() + old, new_ids.get(), sizeof(int32_t) * n_new, cudaMemcpyDeviceToHost, st));
+        if (r + 1 < kKparRounds) {  // distances to the new candidates (not after the last round, :3080)
+            DevBuf<float> Cn(static_cast<size_t>(n_new) * d32, st), cnn(static_cast<size_t>(n_new), st);
+            convert_rows(X, dtype, d, new_ids.get(), n_new, Cn.get(), kElemF32, d32, cnn.get(), st);
+            assign_topk_impl(Xf, xn, N, d, d32, Cn.get(), cnn.get(), static_cast<int>(n_new), 1, tmp_ids.get(),
+                             d_new.get(), err, st);
+            min_update(min_d.get(), d_new.get(), N, st);
+        }
+        GTA_CUDA(cudaStreamSynchronize(st));  // cand is read on the host below
+    }
+    const int64_t n_cand = static_cast<int64_t>(cand.size());
+    if (n_cand <= n_req) return cand;
+    // partial Fisher-Yates over the candidate positions with a splitmix64 stream
+    std::vector<int32_t> perm(static_cast<size_t>(n_cand));
+    std::iota(perm.begin(), perm.end(), 0);
+    const uint64_t s2 = seed ^ 0x5851F42D4C957F2Dull;
+    for (int64_t k = 0; k < n_req; ++k) {
+        const int64_t j = k + static_cast<int64_t>(mix64(s2 + static_cast<uint64_t>(k)) %
+                                                   static_cast<uint64_t>(n_cand - k));
+        std::swap(perm[static_cast<size_t>(k)], perm[static_cast<size_t>(j)]);
+    }
+    std::vector<int32_t> ids(static_cast<size_t>(n_req));
+    for (int64_t k = 0; k < n_req; ++k) ids[static_cast<size_t>(k)] = cand[static_cast<size_t>(perm[static_cast<size_t>(k)])];
+    return ids;
+}
+
+void build_bucket2_round(const void* X, int dtype, int64_t N, int d, const gta_bucket2_params& p, uint64_t seed,
+                         Bucket2Out& o, cudaStream_t st)
+{
+    const int M = p.knn_degree;
+    const int64_t n_req = bucket2_requested(N, p.centroid_ratio);
+    GTA_REQUIRE(n_req <= N, kInvalid, "build_bucket2: more buckets than points");
+    DevBuf<int> err(1, st);
+    GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+    ProfScope prof_all("build_bucket2_total", 0.0, st);
+    const int d32 = pad_dim(d, kElemF32);
+    DevBuf<float> Xf(static_cast<size_t>(N) * d32, st), xn(static_cast<size_t>(N), st);
+    convert_rows(X, dtype, d, nullptr, N, Xf.get(), kElemF32, d32, xn.get(), st);
+
+    // ---- Step 2: KMeans|| data-point centroids
+    std::vector<int32_t> cid_h;
+    {
+        ProfScope prof("kmeans_parallel", 0.0, st);
+        cid_h = kmeans_parallel_ids(Xf.get(), xn.get(), N, d, d32, X, dtype, n_req, seed, err.get(), st);
+    }
+    const int32_t B = static_cast<int32_t>(cid_h.size());
+    GTA_REQUIRE(B >= 2, kData, "build_bucket2: KMeans|| found fewer than two centroids");
+    auto cid = upload(cid_h, st);
+    DevBuf<float> C(static_cast<size_t>(B) * d32, st), cn(static_cast<size_t>(B), st);
+    convert_rows(X, dtype, d, cid.get(), B, C.get(), kElemF32, d32, cn.get(), st);
+
+    // ---- Step 3: centroid kNN graph (self excluded): the pools' neighbour buckets
+    int P = p.nprobe > 0 ? p.nprobe : (p.knn_k > 0 ? p.knn_k : 32);
+    P = std::min<int>(P, B - 1);
+    std::vector<int32_t> adj(static_cast<size_t>(B) * std::max(P, 0));
+    if (P > 0) {
+        ProfScope prof("centroid_knn", 0.0, st);
+        DevBuf<int32_t> ki(static_cast<size_t>(B) * (P + 1), st);
+        DevBuf<float> kd(static_cast<size_t>(B) * (P + 1), st);
+        assign_topk_impl(C.get(), cn.get(), B, d, d32, C.get(), cn.get(), B, P + 1, ki.get(), kd.get(), err.get(), st);
+        std::vector<int32_t> h(static_cast<size_t>(B) * (P + 1));
+        GTA_CUDA(cudaMemcpyAsync(h.data(), ki.get(), sizeof(int32_t) * h.size(), cudaMemcpyDeviceToHost, st));
+        GTA_CUDA(cudaStreamSynchronize(st));
+        for (int32_t b = 0; b < B; ++b) {  // drop the bucket itself (else the farthest of the P + 1)
+            int w = 0;
+            bool dropped = false;
+            for (int j = 0; j <= P && w < P; ++j) {
+                const int32_t v = h[static_cast<size_t>(b) * (P + 1) + j];
+                if (v == b && !dropped) { dropped = true; continue; }
+                adj[static_cast<size_t>(b) * P + w++] = v;
+            }
+        }
+    }
+
+    // ---- Step 4: top-2 centroids, balanced 1-way assignment
+    DevBuf<int32_t> assign(static_cast<size_t>(N), st);
+    {
+        ProfScope prof("top2_total", 0.0, st);
+        DevBuf<int32_t> top2(static_cast<size_t>(N) * 2, st);
+        DevBuf<float> t2d(static_cast<size_t>(N) * 2, st);
+        assign_topk_impl(Xf.get(), xn.get(), N, d, d32, C.get(), cn.get(), B, 2, top2.get(), t2d.get(), err.get(), st);
+        balanced_assign(top2.get(), cid.get(), B, N, assign.get(), err.get(), st);
+    }
+    Xf.release();
+    xn.release();
+    DevBuf<int32_t> members(static_cast<size_t>(N), st);
+    DevBuf<int64_t> offsets(static_cast<size_t>(B) + 1, st);
+    group_by_key(assign.get(), N, B, members.get(), offsets.get(), err.get(), st);
+    check_device_error(err.get(), st, "build_bucket2");  // buckets must be sound before the pools are planned
+    std::vector<int64_t> off(static_cast<size_t>(B) + 1);
+    GTA_CUDA(cudaMemcpyAsync(off.data(), offsets.get(), sizeof(int64_t) * (B + 1), cudaMemcpyDeviceToHost, st));
+    GTA_CUDA(cudaStreamSynchronize(st));
+
+    // ---- Step 6: every bucket's points against its pool (own bucket first, then its P neighbours)
+    const int S = P + 1;
+    std::vector<int32_t> seg_b(static_cast<size_t>(B) * S);
+    std::vector<int64_t> pool_size(static_cast<size_t>(B));
+    for (int32_t c = 0; c < B; ++c) {
+        int64_t sz = 0;
+        for (int j = 0; j < S; ++j) {
+            int32_t b = j == 0 ? c : adj[static_cast<size_t>(c) * P + (j - 1)];
+            if (b < 0 || b >= B) b = -1;
+            seg_b[static_cast<size_t>(c) * S + j] = b;
+            if (b >= 0) sz += off[b + 1] - off[b];
+        }
+        pool_size[static_cast<size_t>(c)] = sz;
+    }
+    auto seg_b_d = upload(seg_b, st);
+    const int elem = exact_bf16(dtype, d) ? kElemBF16 : kElemF32;
+    const int d_pad = pad_dim(d, elem);
+    const size_t row_bytes = static_cast<size_t>(d_pad) * (elem == kElemBF16 ? 2 : 4);
+    const int64_t max_pool = *std::max_element(pool_size.begin(), pool_size.end());
+    const int64_t cap_rows = std::max<int64_t>(max_pool, static_cast<int64_t>(kPoolBudgetBytes / row_bytes));
+    DevBuf<int32_t> lids(static_cast<size_t>(N) * M, st);
+    DevBuf<float> ldist(static_cast<size_t>(N) * M, st);
+    {
+        ProfScope prof("pool_knn_total", 0.0, st);
+        for (int32_t c_lo = 0; c_lo < B;) {
+            int32_t c_hi = c_lo;
+            int64_t rows = 0;
+            while (c_hi < B && rows + pool_size[static_cast<size_t>(c_hi)] <= cap_rows) rows += pool_size[static_cast<size_t>(c_hi++)];
+            const int32_t nb = c_hi - c_lo;
+            std::vector<int64_t> pool_off(static_cast<size_t>(nb)), seg_dst(static_cast<size_t>(nb) * S);
+            int64_t run = 0;
+            for (int32_t c = c_lo; c < c_hi; ++c) {
+                pool_off[static_cast<size_t>(c - c_lo)] = run;
+                for (int j = 0; j < S; ++j) {
+                    seg_dst[static_cast<size_t>(c - c_lo) * S + j] = run;
+                    const int32_t b = seg_b[static_cast<size_t>(c) * S + j];
+                    if (b >= 0) run += off[b + 1] - off[b];
+                }
+            }
+            const int64_t n_pool = run;
+            const int64_t q0 = off[c_lo], n_q = off[c_hi] - q0;
+            if (n_q > 0 && n_pool > 0) {
+                auto seg_dst_d = upload(seg_dst, st);
+                DevBuf<int32_t> pool_ids(static_cast<size_t>(n_pool), st);
+                pool_fill(members.get(), offsets.get(), seg_b_d.get(), seg_dst_d.get(), S, c_lo, nb, pool_ids.get(), st);
+                DevBuf<uint8_t> Bp(static_cast<size_t>(n_pool) * row_bytes, st), Ap(static_cast<size_t>(n_q) * row_bytes, st);
+                DevBuf<float> bn(static_cast<size_t>(n_pool), st), an(static_cast<size_t>(n_q), st);
+                {
+                    ProfScope prof("gather", static_cast<double>(n_pool + n_q) * (d * elem_size(dtype) + row_bytes), st);
+                    convert_rows(X, dtype, d, pool_ids.get(), n_pool, Bp.get(), elem, d_pad, bn.get(), st);
+                    convert_rows(X, dtype, d, members.get() + q0, n_q, Ap.get(), elem, d_pad, an.get(), st);
+                }
+                // work list: one CTA per 128 query rows of a bucket, largest pools first
+                std::vector<int32_t> ord(static_cast<size_t>(nb));
+                std::iota(ord.begin(), ord.end(), c_lo);
+                std::stable_sort(ord.begin(), ord.end(), [&](int32_t a, int32_t b) {
+                    return pool_size[static_cast<size_t>(a)] > pool_size[static_cast<size_t>(b)];
+                });
+                std::vector<WorkItem> wl;
+                double flops = 0.0;
+                for (int32_t c : ord) {
+                    const int64_t nc = off[c + 1] - off[c];
+                    const int64_t ps = pool_size[static_cast<size_t>(c)];
+                    flops += 2.0 * static_cast<double>(nc) * static_cast<double>(ps) * d;
+                    for (int64_t t = 0; t < nc; t += 128)
+                        wl.push_back(WorkItem{static_cast<int32_t>(off[c] - q0 + t),
+                                              static_cast<int32_t>(std::min<int64_t>(128, nc - t)),
+                                              static_cast<int32_t>(pool_off[static_cast<size_t>(c - c_lo)]),
+                                              static_cast<int32_t>(ps), static_cast<int32_t>(t), 0, 0, 0});
+                }
+                if (!wl.empty()) {
+                    auto work = upload(wl, st);
+                    DistTopkProblem pr;
+                    pr.A = Ap.get(); pr.a_total = n_q; pr.B = Bp.get(); pr.b_total = n_pool; pr.elem = elem; pr.d = d;
+                    pr.d_pad = d_pad; pr.a_norm = an.get(); pr.b_norm = bn.get(); pr.b_gid = pool_ids.get();
+                    pr.work = work.get(); pr.n_work = static_cast<int>(wl.size()); pr.m_out = M; pr.exclude_self = true;
+                    pr.out_ids = lids.get() + q0 * M; pr.out_dists = ldist.get() + q0 * M; pr.err = err.get();
+                    pr.prof_name = "dist_topk_pool";
+                    pr.flops = flops;
+                    dist_topk(pr, st);
+                }
+                GTA_CUDA(cudaStreamSynchronize(st));  // the batch's buffers are released next
+            }
+            c_lo = c_hi;
+        }
+    }
+    // per-point lists (one membership each)
+    DevBuf<int64_t> mem_row(static_cast<size_t>(N) * 2, st);
+    one_way_rows(members.get(), N, mem_row.get(), st);
+    merge_memberships(lids.get(), ldist.get(), mem_row.get(), N, M, o.ids, o.dists, st);
+    if (o.assign) GTA_CUDA(cudaMemcpyAsync(o.assign, assign.get(), sizeof(int32_t) * N, cudaMemcpyDeviceToDevice, st));
+    if (o.cid) GTA_CUDA(cudaMemcpyAsync(o.cid, cid.get(), sizeof(int32_t) * B, cudaMemcpyDeviceToDevice, st));
+    o.n_buckets = B;
+    check_device_error(err.get(), st, "build_bucket2");
+}
+
+void build_bucket2_impl(const gta_dataset& ds, const gta_bucket2_params& p, Bucket2Out& o, cudaStream_t st)
+{
+    const int64_t N = ds.n;
+    const int M = p.knn_degree;
+    GTA_REQUIRE(ds.data && N >= 2 && ds.d >= 1 && N < (1ll << 30), kInvalid, "build_bucket2: need 2 <= N < 2^30");
+    GTA_REQUIRE(ds.dtype == GTA_F32 || ds.dtype == GTA_U8 || ds.dtype == GTA_I8, kInvalid, "build_bucket2: bad dtype");
+    GTA_REQUIRE(M >= 1 && M <= 128, kInvalid, "build_bucket2: knn_degree must be in [1, 128]");
+    GTA_REQUIRE(p.nprobe >= 0 && p.nprobe <= 127 && p.knn_k >= 0 && p.knn_k <= 127 && p.rounds >= 0 &&
+                    p.centroid_ratio >= 0.0f && p.centroid_ratio <= 1.0f,
+                kInvalid, "build_bucket2: need 0 <= nprobe, knn_k <= 127, 0 <= centroid_ratio <= 1");
+    const void* X = ds.data;
+    DevBuf<uint8_t> xhold;
+    if (!ds.on_device) {
+        const size_t xbytes = static_cast<size_t>(N) * ds.d * elem_size(ds.dtype);
+        xhold = DevBuf<uint8_t>(xbytes, st);
+        GTA_CUDA(cudaMemcpyAsync(xhold.get(), ds.data, xbytes, cudaMemcpyHostToDevice, st));
+        X = xhold.get();
+    }
+    const int rounds = p.rounds > 1 ? p.rounds : 1;
+    const size_t nm = static_cast<size_t>(N) * M;
+    DevBuf<int32_t> new_ids, run_ids;
+    DevBuf<float> new_d, run_d;
+    if (rounds > 1) {
+        new_ids = DevBuf<int32_t>(nm, st); run_ids = DevBuf<int32_t>(nm, st);
+        new_d = DevBuf<float>(nm, st); run_d = DevBuf<float>(nm, st);
+    }
+    for (int r = 0; r < rounds; ++r) {
+        const bool last = r == rounds - 1;
+        Bucket2Out ro{r == 0 ? o.ids : new_ids.get(), r == 0 ? o.dists : new_d.get(), last ? o.assign : nullptr,
+                      last ? o.cid : nullptr, 0};
+        build_bucket2_round(X, ds.dtype, N, ds.d, p, p.seed + static_cast<uint64_t>(r), ro, st);
+        o.n_buckets = ro.n_buckets;
+        if (r == 0) continue;
+        GTA_CUDA(cudaMemcpyAsync(run_ids.get(), o.ids, sizeof(int32_t) * nm, cudaMemcpyDeviceToDevice, st));
+        GTA_CUDA(cudaMemcpyAsync(run_d.get(), o.dists, sizeof(float) * nm, cudaMemcpyDeviceToDevice, st));
+        merge_lists(run_ids.get(), run_d.get(), new_ids.get(), new_d.get(), N, M, o.ids, o.dists, st);
+    }
+}
+
 void optimize_impl(const uint32_t* knn_dev, int64_t n, int m, int k, uint32_t* graph_dev, cudaStream_t st,
                    const int32_t* order = nullptr)
 {
@@ -730,6 +1000,49 @@ int gta_build_bucket(const gta_dataset* ds, const gta_bucket_params* p, int32_t*
                                          cudaMemcpyDeviceToHost, st));
             if (p->top2_out)
                 GTA_CUDA(cudaMemcpyAsync(p->top2_out, o.top2, sizeof(int32_t) * 2 * N, cudaMemcpyDeviceToHost, st));
+            GTA_CUDA(cudaStreamSynchronize(st));
+        }
+    });
+}
+
+int gta_build_bucket2(const gta_dataset* ds, const gta_bucket2_params* p, int32_t* knn_ids, float* knn_dists,
+                      void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(ds && p && knn_ids, kInvalid, "gta_build_bucket2: null argument");
+        cudaStream_t st = S(stream);
+        const int64_t N = ds->n;
+        const size_t nm = static_cast<size_t>(N) * (p->knn_degree > 0 ? p->knn_degree : 0);
+        const int64_t n_req = bucket2_requested(N, p->centroid_ratio);
+        const bool dev = p->out_on_device != 0;
+        DevBuf<int32_t> ih, ah, ch;
+        DevBuf<float> dh;
+        Bucket2Out o{};
+        if (dev) {
+            o.ids = knn_ids;
+            if (knn_dists) o.dists = knn_dists;
+            else { dh = DevBuf<float>(nm, st); o.dists = dh.get(); }
+            o.assign = p->assign_out;
+            o.cid = p->centroid_ids_out;
+        } else {
+            ih = DevBuf<int32_t>(nm, st);
+            dh = DevBuf<float>(nm, st);
+            o.ids = ih.get();
+            o.dists = dh.get();
+            if (p->assign_out) { ah = DevBuf<int32_t>(static_cast<size_t>(N), st); o.assign = ah.get(); }
+            if (p->centroid_ids_out) { ch = DevBuf<int32_t>(static_cast<size_t>(n_req), st); o.cid = ch.get(); }
+        }
+        build_bucket2_impl(*ds, *p, o, st);
+        if (p->n_buckets_out) *p->n_buckets_out = o.n_buckets;
+        if (!dev) {
+            GTA_CUDA(cudaMemcpyAsync(knn_ids, o.ids, sizeof(int32_t) * nm, cudaMemcpyDeviceToHost, st));
+            if (knn_dists) GTA_CUDA(cudaMemcpyAsync(knn_dists, o.dists, sizeof(float) * nm, cudaMemcpyDeviceToHost, st));
+            if (p->assign_out)
+                GTA_CUDA(cudaMemcpyAsync(p->assign_out, o.assign, sizeof(int32_t) * N, cudaMemcpyDeviceToHost, st));
+            if (p->centroid_ids_out)
+                GTA_CUDA(cudaMemcpyAsync(p->centroid_ids_out, o.cid, sizeof(int32_t) * o.n_buckets,
+                                         cudaMemcpyDeviceToHost, st));
             GTA_CUDA(cudaStreamSynchronize(st));
         }
     });

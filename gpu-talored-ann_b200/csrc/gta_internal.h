@@ -158,6 +158,32 @@ bool assign_exact_applies(int B, int k);
 // (row_ids: row of X for each point, null = identity)
 void assign_exact(const void* X, int dtype, int64_t n, int ldx, int d, const int32_t* row_ids, const float* C, int ldc,
                   int B, int k, int32_t* ids, float* dists, cudaStream_t st);
+// reference-bucketing build (bucket2.cu): splitmix64 streams shared with the oracle
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t x)
+{
+    uint64_t z = x + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+// 53 random bits for point i in KMeans|| round r (u = bits * 2^-53)
+__host__ __device__ __forceinline__ uint64_t kpar_uniform_bits(uint64_t seed, int round, uint64_t i)
+{
+    return mix64(seed * 0x9E3779B97F4A7C15ull + 0xD1B54A32D192ED03ull * static_cast<uint64_t>(round + 1) + i) >> 11;
+}
+constexpr int64_t kKparPsiTarget = 16384;  // psi subsample size (bucket.cu:2999)
+void kpar_psi(const float* min_d, int64_t n, double* psi, cudaStream_t st);
+void kpar_sample(const float* min_d, int64_t n, uint64_t seed, int round, double lk, const double* psi, uint8_t* chosen,
+                 uint8_t* sel, cudaStream_t st);
+int64_t select_flagged(const uint8_t* flags, int64_t n, int32_t* out, cudaStream_t st);  // ids in order; syncs
+void min_update(float* min_d, const float* d_new, int64_t n, cudaStream_t st);
+void balanced_assign(const int32_t* top2, const int32_t* cid, int32_t n_c, int64_t n, int32_t* assign, int* err,
+                     cudaStream_t st);
+void pool_fill(const int32_t* members, const int64_t* offsets, const int32_t* seg_b, const int64_t* seg_dst, int32_t S,
+               int32_t c_lo, int32_t n_buckets, int32_t* pool_ids, cudaStream_t st);
+void one_way_rows(const int32_t* members, int64_t n, int64_t* mem_row, cudaStream_t st);
+// order = 0..n-1 sorted stably by key (keys in [0, B), else err), offsets[b] = first index of key b
+void group_by_key(const int32_t* keys, int64_t n, int32_t B, int32_t* order, int64_t* offsets, int* err, cudaStream_t st);
 // bucket-contiguous renumbering (reorder.cu)
 void bucket_reorder(const int32_t* assign, int64_t n, int32_t stride, int32_t B, const int32_t* order,
                     uint32_t* inverse_perm, int64_t* offsets, int* err, cudaStream_t st);

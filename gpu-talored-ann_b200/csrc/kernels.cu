@@ -1131,6 +1131,26 @@ void centroid_update(const float* Xs, int64_t n_s, int d, int d_pad, const int32
     GTA_CUDA(cudaGetLastError());
 }
 
+void group_by_key(const int32_t* keys, int64_t n, int32_t B, int32_t* order, int64_t* offsets, int* err, cudaStream_t st)
+{
+    GTA_REQUIRE(n >= 1 && n < (1ll << 31) && B >= 1, kInvalid, "group_by_key: need 1 <= n < 2^31, B >= 1");
+    check_ids(keys, n, B, err, st);
+    DevBuf<int32_t> keys_out(static_cast<size_t>(n), st), idx_in(static_cast<size_t>(n), st);
+    iota_kernel<<<blocks_for(n, 256), 256, 0, st>>>(idx_in.get(), n);
+    count_launches(1);
+    int end_bit = 1;
+    while ((1ll << end_bit) < B) ++end_bit;
+    size_t tmp = 0;
+    GTA_CUDA(cub::DeviceRadixSort::SortPairs(nullptr, tmp, keys, keys_out.get(), idx_in.get(), order,
+                                             static_cast<int>(n), 0, end_bit, st));
+    DevBuf<uint8_t> tbuf(tmp, st);
+    GTA_CUDA(cub::DeviceRadixSort::SortPairs(tbuf.get(), tmp, keys, keys_out.get(), idx_in.get(), order,
+                                             static_cast<int>(n), 0, end_bit, st));
+    seg_offsets_kernel<<<blocks_for(B + 1, 256), 256, 0, st>>>(keys_out.get(), n, B, offsets);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
 void build_memberships(const int32_t* top2, int64_t N, int32_t B, int32_t* members, int64_t* offsets,
                        int64_t* mem_row, int* err, cudaStream_t st)
 {

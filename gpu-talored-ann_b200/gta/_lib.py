@@ -44,6 +44,15 @@ class gta_bucket_params(ctypes.Structure):
     ]
 
 
+class gta_bucket2_params(ctypes.Structure):
+    _fields_ = [
+        ("knn_degree", _I32), ("nprobe", _I32), ("knn_k", _I32), ("rounds", _I32),
+        ("centroid_ratio", ctypes.c_float), ("reserved0", _I32), ("seed", _U64),
+        ("out_on_device", _I32), ("reserved1", _I32),
+        ("assign_out", _P), ("centroid_ids_out", _P), ("n_buckets_out", ctypes.POINTER(_I32)),
+    ]
+
+
 class gta_cagra_params(ctypes.Structure):
     _fields_ = [("bucket", gta_bucket_params), ("graph_degree", _I32), ("reserved0", _I32)]
 
@@ -52,6 +61,7 @@ _SIGS = {
     "gta_build_bucket": [ctypes.POINTER(gta_dataset), ctypes.POINTER(gta_bucket_params), _P, _P, _P],
     "gta_optimize": [_P, _I64, _I32, _I32, _P, _I32, _P],
     "gta_build_cagra": [ctypes.POINTER(gta_dataset), ctypes.POINTER(gta_cagra_params), _P, _P],
+    "gta_build_bucket2": [ctypes.POINTER(gta_dataset), ctypes.POINTER(gta_bucket2_params), _P, _P, _P],
     "gta_optimize_knn": [ctypes.POINTER(gta_dataset), _P, _I64, _I32, _I32, _P, _I32, _P],
     "gta_kmeans_fit": [_P, _I64, _I32, _P, _I32, _I32, _P, _P],
     "gta_kmeans_init": [_P, _I64, _I32, _I32, _U64, _P, _P],

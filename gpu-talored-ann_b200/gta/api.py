@@ -110,6 +110,33 @@ def build_bucket(X, n_buckets: int, knn_degree: int = 64, kmeans_iters: int = 10
     return ids, dists
 
 
+def build_bucket2(X, knn_degree: int = 64, nprobe: int = 0, centroid_ratio: float = 0.01, seed: int = 42,
+                  rounds: int = 1, knn_k: int = 0, with_extras: bool = False):
+    """kNN graph with the reference's own bucketing (its bucket2 tool): KMeans|| data-point
+    centroids (max(2, N * centroid_ratio) requested), balanced 1-way buckets, every bucket's
+    points searched in the pool of their bucket and its ``nprobe`` nearest buckets (0: knn_k,
+    0: 32), ``rounds`` builds merged.  Returns (ids[N, M], dists[N, M]); with ``with_extras``
+    also the bucket of every point (N,) and the centroids' point ids."""
+    dev = _is_dev(X)
+    N = X.shape[0]
+    ids = _empty((N, knn_degree), "int32", dev)
+    dists = _empty((N, knn_degree), "float32", dev)
+    n_req = max(2, int(float(N) * (float(np.float32(centroid_ratio)) if centroid_ratio > 0 else 0.01)))
+    assign = _empty((N,), "int32", dev) if with_extras else None
+    cid = _empty((n_req,), "int32", dev) if with_extras else None
+    nb = ctypes.c_int32(0)
+    p = L.gta_bucket2_params(knn_degree=knn_degree, nprobe=nprobe, knn_k=knn_k, rounds=rounds,
+                             centroid_ratio=centroid_ratio, reserved0=0, seed=seed, out_on_device=1 if dev else 0,
+                             reserved1=0, assign_out=_ptr(assign), centroid_ids_out=_ptr(cid),
+                             n_buckets_out=ctypes.pointer(nb))
+    ds = _dataset(X)
+    L.check(L.lib().gta_build_bucket2(ctypes.byref(ds), ctypes.byref(p), _ptr(ids), _ptr(dists),
+                                      _stream() if dev else ctypes.c_void_p(0)))
+    if with_extras:
+        return ids, dists, assign, cid[: nb.value]
+    return ids, dists
+
+
 def build_cagra(X, n_buckets: int, knn_degree: int = 64, graph_degree: int = 32, kmeans_iters: int = 10,
                 kmeans_sample: int = 0, seed: int = 42, init_centroids=None, metric: str = "l2", rounds: int = 1):
     """Whole build: bucketed kNN (degree M), sanitize, CAGRA optimize -> graph[N, K] uint32."""

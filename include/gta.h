@@ -82,6 +82,25 @@ typedef struct {
     int32_t reserved0;
 } gta_cagra_params;
 
+/* Parameters of the reference-bucketing build (the bucketing of the reference's
+ * bucket2 tool): data-point centroids by KMeans||, every point in one bucket
+ * (nearest or second-nearest centroid, balancing bucket sizes), each bucket's
+ * points searched against a pool of the bucket and its nprobe nearest buckets. */
+typedef struct {
+    int32_t knn_degree;       /* M: per-point list length (bucket2 --neighbors-m), 1..128 */
+    int32_t nprobe;           /* neighbour buckets in a pool (bucket2 --nprobe; 0 = knn_k), <= 127 */
+    int32_t knn_k;            /* bucket2 --knn-k: the pool width when nprobe is 0 (0 = 32) */
+    int32_t rounds;           /* bucket2 -t: builds with seeds seed, seed+1, ... merged (0 or 1: one) */
+    float centroid_ratio;     /* buckets = max(2, N * ratio) requested (bucket2 --centroid-ratio; 0 = 0.01) */
+    int32_t reserved0;
+    uint64_t seed;
+    int32_t out_on_device;    /* outputs are device pointers */
+    int32_t reserved1;
+    int32_t* assign_out;      /* optional N: the bucket of every point (last round) */
+    int32_t* centroid_ids_out;/* optional: the centroids' point ids (room for max(2, N * ratio)) */
+    int32_t* n_buckets_out;   /* optional HOST pointer: the number of buckets of the last round */
+} gta_bucket2_params;
+
 /* ---------------------------------------------------------------- pipeline */
 
 /* Bucketed kNN graph: k-means over a sample, 2-way top-2 bucket membership,
@@ -93,6 +112,20 @@ typedef struct {
  * run_pipeline_impl, :5310 GpuResidentKnn::run_round, :5552 write_outputs). */
 int gta_build_bucket(const gta_dataset* ds, const gta_bucket_params* p, int32_t* knn_ids, float* knn_dists,
                      void* stream);
+
+/* kNN graph with the reference's own bucketing (gta_bucket2_params): KMeans||
+ * (three rounds taking each point with probability 0.5 B d(x)^2 / psi, then a
+ * uniform subsample of the candidates to B), exact centroid kNN graph, top-2
+ * centroids of every point with the balanced choice (the second when its bucket
+ * is below 0.8 x the first's size, sizes as they stood at the start of each
+ * 1024-point batch), then for every bucket the exact top-M of its points over
+ * the pool of its own and its nprobe nearest buckets' points (self excluded).
+ * Writes knn_ids / knn_dists [N x M] like gta_build_bucket.
+ * Replaces bucket2 Steps 2-6 on the GPU-resident path
+ * (bucketDemo/buildBucket/src/bucket.cu:2833 select_centroids_on_gpu_kmeans_parallel,
+ * :3241 centroid_self_knn_bf, :1552 batch_assign_with_cagra_anns, :5310 run_round). */
+int gta_build_bucket2(const gta_dataset* ds, const gta_bucket2_params* p, int32_t* knn_ids, float* knn_dists,
+                      void* stream);
 
 /* CAGRA optimize of an already distance-sorted, sanitized (N x M) uint32 kNN
  * graph: rank-based detour-count prune to K, then the reverse-edge merge.

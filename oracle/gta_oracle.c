@@ -691,3 +691,166 @@ ORC_API void orc_bucket_order(const int32_t* adj, int32_t B, int32_t K, int32_t 
 #undef ORC_SHIFT
     free(score); free(placed); free(touched); free(deg); free(nb);
 }
+
+/* ------------------------------------------------------------------ */
+/* reference bucketing (the reference's bucket2 tool)                   */
+/* ------------------------------------------------------------------ */
+
+static uint64_t orc_mix64(uint64_t x)
+{
+    uint64_t z = x + 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+static uint64_t orc_kpar_bits(uint64_t seed, int round, uint64_t i)
+{
+    return orc_mix64(seed * 0x9E3779B97F4A7C15ull + 0xD1B54A32D192ED03ull * (uint64_t)(round + 1) + i) >> 11;
+}
+
+/* KMeans|| (bucketDemo/buildBucket/src/bucket.cu:2919-3117): first point from the seed; three
+ * rounds; psi = strided-subsample fp64 sum of the current squared distances (stride N/16384,
+ * lane-strided partial sums reduced by a 16-8-4-2-1 tree) scaled by N / samples; point i is
+ * taken when not yet taken and u_i < 0.5 n_req d_i / psi; distances refreshed with the new
+ * candidates except after the last round.  Then (:3150-3172) a uniform subsample of the
+ * candidates down to n_req (partial Fisher-Yates).  Writes the centroid point ids, returns
+ * their number (<= n_req). */
+ORC_API int64_t orc_kmeans_parallel(const float* X, int64_t N, int d, int64_t n_req, uint64_t seed, int32_t* out)
+{
+    const int32_t c0 = (int32_t)(orc_mix64(seed ^ 0xA0761D6478BD642Full) % (uint64_t)N);
+    unsigned char* chosen = (unsigned char*)calloc((size_t)N, 1);
+    float* min_d = (float*)malloc(sizeof(float) * (size_t)N);
+    int32_t* cand = (int32_t*)malloc(sizeof(int32_t) * (size_t)N);
+    int64_t n_cand = 0;
+    cand[n_cand++] = c0;
+    chosen[c0] = 1;
+    for (int64_t i = 0; i < N; ++i) min_d[i] = exact_l2(X + i * d, X + (int64_t)c0 * d, d);
+    const double lk = 1.5 / 3.0 * (double)n_req;
+    const int64_t stride = N / 16384 > 1 ? N / 16384 : 1;
+    const int64_t sub_n = N / stride;
+    for (int r = 0; r < 3; ++r) {
+        double s[32];
+        for (int l = 0; l < 32; ++l) {
+            s[l] = 0.0;
+            for (int64_t j = l; j < sub_n; j += 32) s[l] += (double)min_d[j * stride];
+        }
+        for (int o = 16; o > 0; o >>= 1)
+            for (int l = 0; l < o; ++l) s[l] += s[l + o];
+        const double psi = s[0] * ((double)N / (double)sub_n);
+        const int64_t first_new = n_cand;
+        for (int64_t i = 0; i < N; ++i) {
+            const double u = (double)orc_kpar_bits(seed, r, (uint64_t)i) * 0x1.0p-53;
+            if (!chosen[i] && u < (lk * (double)min_d[i]) / psi) {
+                chosen[i] = 1;
+                cand[n_cand++] = (int32_t)i;
+            }
+        }
+        if (n_cand == first_new) break;
+        if (r + 1 < 3) {
+#pragma omp parallel for schedule(static)
+            for (int64_t i = 0; i < N; ++i) {
+                float m = min_d[i];
+                for (int64_t c = first_new; c < n_cand; ++c) {
+                    const float v = exact_l2(X + i * d, X + (int64_t)cand[c] * d, d);
+                    if (v < m) m = v;
+                }
+                min_d[i] = m;
+            }
+        }
+    }
+    int64_t n_out = n_cand;
+    if (n_cand <= n_req) {
+        memcpy(out, cand, sizeof(int32_t) * (size_t)n_cand);
+    } else {
+        int32_t* perm = (int32_t*)malloc(sizeof(int32_t) * (size_t)n_cand);
+        for (int64_t k = 0; k < n_cand; ++k) perm[k] = (int32_t)k;
+        const uint64_t s2 = seed ^ 0x5851F42D4C957F2Dull;
+        for (int64_t k = 0; k < n_req; ++k) {
+            const int64_t j = k + (int64_t)(orc_mix64(s2 + (uint64_t)k) % (uint64_t)(n_cand - k));
+            const int32_t t = perm[k]; perm[k] = perm[j]; perm[j] = t;
+        }
+        for (int64_t k = 0; k < n_req; ++k) out[k] = cand[perm[k]];
+        free(perm);
+        n_out = n_req;
+    }
+    free(chosen); free(min_d); free(cand);
+    return n_out;
+}
+
+/* Balanced 1-way assignment (bucket.cu:1655-1660, :2276-2301): centroid points stay in their
+ * own bucket, every bucket starts at size 1; the other points in index order, 1024 at a time,
+ * choose the second-nearest centroid when its size is below 0.8 x the nearest's size (sizes as
+ * at the start of the batch), then the batch's choices are counted.  Returns the number of
+ * top-2 entries out of range (0 on success). */
+ORC_API int64_t orc_balanced_assign(const int32_t* top2, int64_t N, int32_t B, const int32_t* cid, int32_t* assign)
+{
+    int64_t* size = (int64_t*)malloc(sizeof(int64_t) * (size_t)B);
+    unsigned char* is_c = (unsigned char*)calloc((size_t)N, 1);
+    int32_t* chosen = (int32_t*)malloc(sizeof(int32_t) * 1024);
+    int64_t bad = 0;
+    for (int32_t c = 0; c < B; ++c) { size[c] = 1; assign[cid[c]] = c; is_c[cid[c]] = 1; }
+    int64_t i = 0;
+    while (i < N) {
+        int nb = 0;
+        int64_t ids[1024];
+        while (nb < 1024 && i < N) {
+            if (!is_c[i]) ids[nb++] = i;
+            ++i;
+        }
+        for (int t = 0; t < nb; ++t) {
+            const int32_t c1 = top2[2 * ids[t]], c2 = top2[2 * ids[t] + 1];
+            if (c1 < 0 || c1 >= B || c2 < 0 || c2 >= B) { chosen[t] = -1; ++bad; continue; }
+            chosen[t] = ((double)size[c2] < 0.8 * (double)size[c1]) ? c2 : c1;
+            assign[ids[t]] = chosen[t];
+        }
+        for (int t = 0; t < nb; ++t)
+            if (chosen[t] >= 0) size[chosen[t]]++;
+    }
+    free(size); free(is_c); free(chosen);
+    return bad;
+}
+
+/* Per-bucket pool kNN (bucket.cu:5310-5365, the resident round): the pool of bucket c is its
+ * points (ascending id) followed by those of adj[c][0..P) (ids >= B or negative skipped);
+ * each point of c gets the exact top-M of its pool, itself excluded, by (distance, id). */
+ORC_API void orc_pool_knn(const float* X, int64_t N, int d, const int32_t* assign, int32_t B, const int32_t* adj,
+                          int32_t P, int32_t M, int32_t* out_ids, float* out_d)
+{
+    int64_t* off = (int64_t*)calloc((size_t)B + 1, sizeof(int64_t));
+    int32_t* mem = (int32_t*)malloc(sizeof(int32_t) * (size_t)N);
+    for (int64_t i = 0; i < N; ++i) off[assign[i] + 1]++;
+    for (int32_t c = 0; c < B; ++c) off[c + 1] += off[c];
+    int64_t* cur = (int64_t*)malloc(sizeof(int64_t) * (size_t)B);
+    for (int32_t c = 0; c < B; ++c) cur[c] = off[c];
+    for (int64_t i = 0; i < N; ++i) mem[cur[assign[i]]++] = (int32_t)i;
+#pragma omp parallel for schedule(dynamic)
+    for (int32_t c = 0; c < B; ++c) {
+        int64_t ps = 0;
+        for (int j = 0; j <= P; ++j) {
+            const int32_t b = j == 0 ? c : adj[(int64_t)c * P + j - 1];
+            if (b >= 0 && b < B) ps += off[b + 1] - off[b];
+        }
+        int32_t* pool = (int32_t*)malloc(sizeof(int32_t) * (size_t)(ps > 0 ? ps : 1));
+        orc_pair* cand = (orc_pair*)malloc(sizeof(orc_pair) * (size_t)(ps > 0 ? ps : 1));
+        int64_t w = 0;
+        for (int j = 0; j <= P; ++j) {
+            const int32_t b = j == 0 ? c : adj[(int64_t)c * P + j - 1];
+            if (b < 0 || b >= B) continue;
+            for (int64_t k = off[b]; k < off[b + 1]; ++k) pool[w++] = mem[k];
+        }
+        for (int64_t q = off[c]; q < off[c + 1]; ++q) {
+            const int32_t pt = mem[q];
+            int64_t nc = 0;
+            for (int64_t k = 0; k < ps; ++k) {
+                if (k == q - off[c]) continue;  /* the point itself (its own position in segment 0) */
+                cand[nc].d = exact_l2(X + (int64_t)pt * d, X + (int64_t)pool[k] * d, d);
+                cand[nc].id = pool[k];
+                ++nc;
+            }
+            select_topk(cand, nc, M, out_ids + (int64_t)pt * M, out_d + (int64_t)pt * M);
+        }
+        free(pool); free(cand);
+    }
+    free(off); free(mem); free(cur);
+}

@@ -74,6 +74,12 @@ def lib():
         L.orc_permute_graph.restype = _I64
         L.orc_bucket_order.argtypes = [_P, _I32, _I32, _I32, _P]
         L.orc_bucket_order.restype = None
+        L.orc_kmeans_parallel.argtypes = [_P, _I64, _I32, _I64, ctypes.c_uint64, _P]
+        L.orc_kmeans_parallel.restype = _I64
+        L.orc_balanced_assign.argtypes = [_P, _I64, _I32, _P, _P]
+        L.orc_balanced_assign.restype = _I64
+        L.orc_pool_knn.argtypes = [_P, _I64, _I32, _P, _I32, _P, _I32, _I32, _P, _P]
+        L.orc_pool_knn.restype = None
         _lib = L
     return _lib
 
@@ -329,6 +335,70 @@ def bucket_order(adj, window: int):
     out = np.empty(B, np.int32)
     lib().orc_bucket_order(_p(adj), B, K, window, _p(out))
     return out
+
+
+def bucket2_requested(N: int, ratio: float) -> int:
+    """max(2, floor(N * r)) with r the ratio as a C float widened to double (0 means 0.01)."""
+    r = float(np.float32(ratio)) if ratio > 0 else 0.01
+    return max(2, int(float(N) * r))
+
+
+def kmeans_parallel(X, n_req: int, seed: int) -> np.ndarray:
+    """KMeans|| data-point centroids (bucket.cu:2919-3172 restated): their point ids."""
+    X = _f32(X)
+    out = np.empty(n_req, np.int32)
+    n = lib().orc_kmeans_parallel(_p(X), X.shape[0], X.shape[1], n_req, ctypes.c_uint64(seed & (2**64 - 1)), _p(out))
+    return out[:n].copy()
+
+
+def balanced_assign(top2, B: int, cid) -> np.ndarray:
+    """The balanced 1-way choice (bucket.cu:1655-1660, :2276-2301), 1024-point batches."""
+    top2 = np.ascontiguousarray(top2, np.int32)
+    cid = np.ascontiguousarray(cid, np.int32)
+    out = np.full(top2.shape[0], -1, np.int32)
+    bad = lib().orc_balanced_assign(_p(top2), top2.shape[0], B, _p(cid), _p(out))
+    assert bad == 0
+    return out
+
+
+def pool_knn(X, assign, B: int, adj, M: int):
+    """Own + neighbour-bucket pool kNN of every point (bucket.cu:5310-5365 restated)."""
+    X = _f32(X)
+    assign = np.ascontiguousarray(assign, np.int32)
+    adj = np.ascontiguousarray(adj, np.int32).reshape(B, -1)
+    P = adj.shape[1]
+    ids = np.empty((X.shape[0], M), np.int32)
+    dist = np.empty((X.shape[0], M), np.float32)
+    lib().orc_pool_knn(_p(X), X.shape[0], X.shape[1], _p(assign), B, _p(adj), P, M, _p(ids), _p(dist))
+    return ids, dist
+
+
+def build_bucket2(X, M: int, nprobe: int = 0, centroid_ratio: float = 0.01, seed: int = 42, rounds: int = 1,
+                  knn_k: int = 0):
+    """The reference-bucketing build restated: (ids, dists, assign, centroid ids) of the last round,
+    rounds merged with the resident merge rule."""
+    Xf = _f32(X)
+    N = Xf.shape[0]
+    n_req = bucket2_requested(N, centroid_ratio)
+    run = None
+    for r in range(max(1, rounds)):
+        cid = kmeans_parallel(Xf, n_req, seed + r)
+        B = cid.size
+        C = Xf[cid]
+        P = nprobe if nprobe > 0 else (knn_k if knn_k > 0 else 32)
+        P = min(P, B - 1)
+        adj = np.zeros((B, max(P, 0)), np.int32)
+        if P > 0:
+            ki, _ = topk_assign(C, C, P + 1)
+            for b in range(B):
+                row = list(ki[b])
+                row.remove(b) if b in row else row.pop()
+                adj[b] = row[:P]
+        top2, _ = topk_assign(Xf, C, 2)
+        assign = balanced_assign(top2, B, cid)
+        ids, dist = pool_knn(Xf, assign, B, adj, M)
+        run = (ids, dist) if run is None else merge_lists(run[0], run[1], ids, dist)
+    return run[0], run[1], assign, cid
 
 
 def exact_knn(X, queries, k: int):
