@@ -12,12 +12,15 @@
 // (unless --skip-dists) and neighbors.npy (unless --skip-npy); and with
 // --fused-optimize-degree K, final_graph.bin: sanitize + CAGRA prune + reverse edges in the
 // reordered space, translated back to the input order (bucket.cu:8434-8480).
-// Bucketing is this library's: k-means over a sample, every point in its two nearest
-// buckets (--n-buckets, default N/3906, i.e. buckets of about 7 800 members); the renumbering
-// groups points by their nearest bucket, buckets in the greedy order over the centroid kNN
-// graph (--knn-k neighbours, --order-window).  The kNN lists are built in the input order and
-// renumbered afterwards, so equal distances stay ordered by input id.  The reference's memory /
-// out-of-core / PQ / KMeans|| knobs are accepted and ignored.
+// --bucketing reference (the default) is the reference tool's own bucketing (gta_build_bucket2):
+// KMeans|| data-point centroids (N x --centroid-ratio), balanced 1-way buckets, every bucket
+// searched in the pool of itself and its --nprobe (0: --knn-k) nearest buckets.
+// --bucketing top2 is this library's 2-way build: k-means over a sample, every point in its two
+// nearest buckets (--n-buckets, default N/3906, i.e. buckets of about 7 800 members).
+// The renumbering groups points by their bucket (the nearest one for top2), buckets in the greedy
+// order over the centroid kNN graph (--knn-k neighbours, --order-window).  The kNN lists are
+// built in the input order and renumbered afterwards, so equal distances stay ordered by input
+// id.  The reference's memory / out-of-core / PQ knobs are accepted and ignored.
 // Exit status: 0 ok, 1 error ("FATAL: ..." on stderr), like the reference.
 #include <algorithm>
 #include <chrono>
@@ -60,13 +63,15 @@ int run(int argc, char** argv)
         {"output", 'o', false, "Output root directory", ""},
         {"neighbors-m", 0, false, "Per-vector KNN neighbor count M (1..128)", "0"},
         {"fused-optimize-degree", 0, false, "Prune + reverse edges to this degree, write final_graph.bin (0 = off)", "0"},
-        {"n-buckets", 0, false, "k-means buckets B (0 = N/3906)", "0"},
-        {"kmeans-iters", 0, false, "Lloyd iterations", "10"},
-        {"sample-rate", 0, false, "k-means sample fraction of N (default min(0.1, 1e7/N))", ""},
+        {"bucketing", 0, false, "reference (KMeans||, 1-way, own + nprobe pools) or top2 (2-way k-means)", "reference"},
+        {"centroid-ratio", 0, false, "reference bucketing: buckets = N x ratio", "0.01"},
+        {"n-buckets", 0, false, "top2 bucketing: k-means buckets B (0 = N/3906)", "0"},
+        {"kmeans-iters", 0, false, "top2 bucketing: Lloyd iterations", "10"},
+        {"sample-rate", 0, false, "top2 bucketing: k-means sample fraction of N (default min(0.1, 1e7/N))", ""},
         {"seed", 0, false, "Random seed", "42"},
         {"iterations", 't', false, "Whole builds with seed+iter, lists dedupe-merged", "1"},
-        {"knn-k", 0, false, "Graph degree label of the output subdirectory", "32"},
-        {"nprobe", 0, false, "Output subdirectory label (0 = knn-k)", "0"},
+        {"knn-k", 0, false, "Centroid graph degree (bucket order; the pool width when nprobe is 0)", "32"},
+        {"nprobe", 0, false, "reference bucketing: neighbour buckets in a pool (0 = knn-k, <= 127)", "0"},
         {"order-window", 0, false, "Window of the bucket processing order (0 = max(4 knn-k, 16))", "0"},
         {"skip-dists", 0, true, "Don't write vector_dists.bin", ""},
         {"skip-npy", 0, true, "Don't write neighbors.npy", ""},
@@ -74,7 +79,6 @@ int run(int argc, char** argv)
         {"cpu-limit", 0, false, "(ignored)", ""},
         {"gpu-limit", 0, false, "(ignored)", ""},
         {"bucket-vec-buffer", 0, false, "(ignored)", ""},
-        {"centroid-ratio", 0, false, "(ignored: buckets come from --n-buckets)", ""},
         {"use-pq", 0, false, "(ignored)", ""},
         {"kmeans-train-fraction", 0, false, "(ignored)", ""},
         {"bucket-mem-mb", 0, false, "(ignored)", ""},
@@ -97,7 +101,11 @@ int run(int argc, char** argv)
     if (M < 1 || M > 128) throw std::runtime_error("--neighbors-m must be in [1, 128] (the kNN lists are the product)");
     if (K < 0 || K > M) throw std::runtime_error("--fused-optimize-degree must be in [0, neighbors-m]");
     if (iters < 1) throw std::runtime_error("iterations (" + std::to_string(iters) + ") must be >= 1");
-    if (nprobe > 256) throw std::runtime_error("nprobe exceeds MAX_NPROBE=256");
+    if (nprobe < 0 || nprobe > 127) throw std::runtime_error("nprobe must be in [0, 127] (this build's limit)");
+    if (knn_k < 1 || knn_k > 127) throw std::runtime_error("knn-k must be in [1, 127]");
+    const std::string bucketing = a.str("bucketing", "reference");
+    if (bucketing != "reference" && bucketing != "top2")
+        throw std::runtime_error("--bucketing must be reference or top2, not " + bucketing);
 
     const auto t_all = Clock::now();
     int64_t N = 0;
@@ -110,34 +118,67 @@ int run(int argc, char** argv)
     check(gta_read_dataset(input.c_str(), 0, N, X.data()), "read dataset");
     std::printf("=== Step 1: read dataset [%.3fs]\n", secs(t0));
 
-    int64_t B = a.i64("n-buckets", 0);
-    if (B <= 0) B = std::max<int64_t>(2, static_cast<int64_t>(std::llround(static_cast<double>(N) / 3906.0)));
-    int64_t sample = 0;
-    if (a.has("sample-rate")) sample = std::max<int64_t>(B, static_cast<int64_t>(a.f64("sample-rate", 0.1) * N));
-
     const std::string dir = root + "/k" + std::to_string(knn_k) + "p" + std::to_string(nprobe > 0 ? nprobe : knn_k) +
                             "m" + std::to_string(M) + "t" + std::to_string(iters);
     std::filesystem::create_directories(dir);
     std::printf("Output subdir: %s\n", dir.c_str());
 
     gta_dataset ds{X.data(), N, d, dtype, GTA_L2, 0};
-    gta_bucket_params p{};
-    p.n_buckets = static_cast<int32_t>(B);
-    p.kmeans_iters = static_cast<int32_t>(a.i64("kmeans-iters", 10));
-    p.knn_degree = M;
-    p.rounds = iters;
-    p.kmeans_sample = sample;
-    p.seed = static_cast<uint64_t>(a.i64("seed", 42));
+    const uint64_t seed = static_cast<uint64_t>(a.i64("seed", 42));
     std::vector<int32_t> ids(static_cast<size_t>(N) * M);
     std::vector<float> dists(static_cast<size_t>(N) * M);
-    std::vector<float> cent(static_cast<size_t>(B) * d);
-    std::vector<int32_t> top2(static_cast<size_t>(N) * 2);
-    p.centroids_out = cent.data();
-    p.top2_out = top2.data();
+    std::vector<float> cent;              // B x d
+    std::vector<int32_t> bucket_of(static_cast<size_t>(N));
+    int64_t B = 0;
     t0 = Clock::now();
-    check(gta_build_bucket(&ds, &p, ids.data(), dists.data(), nullptr), "bucketed kNN build");
-    std::printf("=== Steps 2-6: k-means (B=%lld), top-2 buckets, per-bucket kNN (M=%d), merge, %d round(s) [%.3fs]\n",
-                static_cast<long long>(B), M, iters, secs(t0));
+    if (bucketing == "reference") {
+        const float ratio = static_cast<float>(a.f64("centroid-ratio", 0.01));
+        const int64_t n_req = std::max<int64_t>(2, static_cast<int64_t>(static_cast<double>(N) * static_cast<double>(ratio)));
+        std::vector<int32_t> cid(static_cast<size_t>(n_req));
+        int32_t nb = 0;
+        gta_bucket2_params q{};
+        q.knn_degree = M;
+        q.nprobe = nprobe;
+        q.knn_k = knn_k;
+        q.rounds = iters;
+        q.centroid_ratio = ratio;
+        q.seed = seed;
+        q.assign_out = bucket_of.data();
+        q.centroid_ids_out = cid.data();
+        q.n_buckets_out = &nb;
+        check(gta_build_bucket2(&ds, &q, ids.data(), dists.data(), nullptr), "reference-bucketing kNN build");
+        B = nb;
+        cent.resize(static_cast<size_t>(B) * d);  // the centroids are data points
+        for (int64_t c = 0; c < B; ++c)
+            for (int k = 0; k < d; ++k) {
+                const size_t e = static_cast<size_t>(cid[static_cast<size_t>(c)]) * d + k;
+                cent[static_cast<size_t>(c) * d + k] =
+                    dtype == GTA_F32 ? reinterpret_cast<const float*>(X.data())[e]
+                    : dtype == GTA_U8 ? static_cast<float>(X[e]) : static_cast<float>(reinterpret_cast<const int8_t*>(X.data())[e]);
+            }
+        std::printf("=== Steps 2-6: KMeans|| (%lld buckets), balanced 1-way assignment, pool kNN (nprobe %d, M=%d), "
+                    "%d round(s) [%.3fs]\n", static_cast<long long>(B), nprobe > 0 ? nprobe : knn_k, M, iters, secs(t0));
+    } else {
+        B = a.i64("n-buckets", 0);
+        if (B <= 0) B = std::max<int64_t>(2, static_cast<int64_t>(std::llround(static_cast<double>(N) / 3906.0)));
+        int64_t sample = 0;
+        if (a.has("sample-rate")) sample = std::max<int64_t>(B, static_cast<int64_t>(a.f64("sample-rate", 0.1) * N));
+        gta_bucket_params p{};
+        p.n_buckets = static_cast<int32_t>(B);
+        p.kmeans_iters = static_cast<int32_t>(a.i64("kmeans-iters", 10));
+        p.knn_degree = M;
+        p.rounds = iters;
+        p.kmeans_sample = sample;
+        p.seed = seed;
+        cent.resize(static_cast<size_t>(B) * d);
+        std::vector<int32_t> top2(static_cast<size_t>(N) * 2);
+        p.centroids_out = cent.data();
+        p.top2_out = top2.data();
+        check(gta_build_bucket(&ds, &p, ids.data(), dists.data(), nullptr), "bucketed kNN build");
+        for (int64_t i = 0; i < N; ++i) bucket_of[static_cast<size_t>(i)] = top2[static_cast<size_t>(2 * i)];
+        std::printf("=== Steps 2-6: k-means (B=%lld), top-2 buckets, per-bucket kNN (M=%d), merge, %d round(s) [%.3fs]\n",
+                    static_cast<long long>(B), M, iters, secs(t0));
+    }
 
     // bucket-contiguous renumbering: order of the buckets, new ids, reordered rows and lists
     t0 = Clock::now();
@@ -148,8 +189,8 @@ int run(int argc, char** argv)
           "bucket order");
     std::vector<uint32_t> inv(static_cast<size_t>(N));
     std::vector<int64_t> offsets(static_cast<size_t>(B) + 1);
-    check(gta_bucket_reorder(top2.data(), N, 2, static_cast<int32_t>(B), order.data(), inv.data(), offsets.data(), 0,
-                             nullptr),
+    check(gta_bucket_reorder(bucket_of.data(), N, 1, static_cast<int32_t>(B), order.data(), inv.data(), offsets.data(),
+                             0, nullptr),
           "bucket reorder");
     std::vector<uint8_t> Xr(X.size());
     check(gta_permute_rows(X.data(), N, static_cast<int64_t>(d) * static_cast<int64_t>(elem_bytes(dtype)), inv.data(),

@@ -40,7 +40,7 @@ def test_bucket2_outputs(data, rounds):
     d, path, X = data
     out = d / f"out{rounds}"
     run(os.path.join(BIN, "bucket2"), "-i", path, "-o", out, "--neighbors-m", 32, "--fused-optimize-degree", 16,
-        "--n-buckets", 6, "--kmeans-iters", 5, "--seed", 7, "-t", rounds, "--knn-k", 16)
+        "--bucketing", "top2", "--n-buckets", 6, "--kmeans-iters", 5, "--seed", 7, "-t", rounds, "--knn-k", 16)
     sub = out / f"k16p16m32t{rounds}"
     ids = gta.read_knn(str(sub / "vector_knn.bin"))
     dists = np.fromfile(sub / "vector_dists.bin", dtype=np.float32, offset=12).reshape(ids.shape)
@@ -82,6 +82,28 @@ def test_bucket2_outputs(data, rounds):
     run(os.path.join(BIN, "translate_ids"), "-g", sub / "neighbors.npy", "-p", sub / "inverse_perm.bin",
         "-o", sub / "neighbors_orig.npy")
     np.testing.assert_array_equal(np.load(sub / "neighbors_orig.npy"), ri.astype(np.int64))
+
+
+def test_bucket2_reference_bucketing(data):
+    """The default bucketing: the reference tool's (KMeans||, balanced 1-way, own + nprobe pools)."""
+    d, path, X = data
+    out = d / "outref"
+    run(os.path.join(BIN, "bucket2"), "-i", path, "-o", out, "--neighbors-m", 32, "--fused-optimize-degree", 16,
+        "--centroid-ratio", 0.005, "--nprobe", 6, "--knn-k", 8, "--seed", 9)
+    sub = out / "k8p6m32t1"
+    ri, rd, ra, rc = orc.build_bucket2(X, 32, 6, 0.005, 9)
+    B = rc.size
+    cent = X[rc].astype(np.float32)
+    cid, _ = orc.topk_assign(cent, cent, 9)
+    adj = np.array([[v for v in row if v != b][:8] for b, row in enumerate(cid)], np.int32)
+    order = orc.bucket_order(adj, max(4 * 8, 16))
+    inv, _ = orc.bucket_reorder(ra, B, order=order)
+    np.testing.assert_array_equal(gta.read_u32(str(sub / "inverse_perm.bin")), inv)
+    ids_new, _ = orc.permute_graph(ri, inv, False, True)
+    np.testing.assert_array_equal(gta.read_knn(str(sub / "vector_knn.bin")), ids_new)
+    g_new = orc.optimize(orc.sanitize(ids_new)[0], 16)
+    want, _ = orc.permute_graph(g_new, inv, True, False)
+    np.testing.assert_array_equal(gta.read_graph(str(sub / "final_graph.bin")), want.view(np.uint32))
 
 
 def test_optimize_tool_sorts_and_prunes(data):

@@ -26,7 +26,8 @@ def run(*args):
 
 @pytest.mark.parametrize("name,opts", [
     ("bucket2", ["--input", "--output", "--neighbors-m", "--fused-optimize-degree", "--seed", "--iterations",
-                 "--knn-k", "--nprobe", "--skip-dists", "--skip-npy", "--out-of-core", "--centroid-ratio"]),
+                 "--knn-k", "--nprobe", "--skip-dists", "--skip-npy", "--out-of-core", "--centroid-ratio",
+                 "--bucketing"]),
     ("optimize", ["--input", "--knn-graph", "--output", "--output-degree", "--skip-sort", "--save-npy",
                   "--force-chunked", "--gpu-fit-margin"]),
     ("translate_ids", ["--graph", "--inverse-perm", "--output", "--out-buffer-mb"]),
@@ -50,6 +51,10 @@ def test_bucket2_argument_errors(tmp_path):
     assert r.returncode == 1 and "fused-optimize-degree" in r.stderr
     r = run(b2, "-i", data, "-o", str(tmp_path), "--neighbors-m", "8", "-t", "0")
     assert r.returncode == 1 and "iterations" in r.stderr
+    r = run(b2, "-i", data, "-o", str(tmp_path), "--neighbors-m", "8", "--bucketing", "random")
+    assert r.returncode == 1 and "--bucketing" in r.stderr
+    r = run(b2, "-i", data, "-o", str(tmp_path), "--neighbors-m", "8", "--nprobe", "200")
+    assert r.returncode == 1 and "nprobe" in r.stderr
     r = run(b2, "-i", data, "-o", str(tmp_path), "--bogus", "1")
     assert r.returncode == 1 and "unknown option" in r.stderr
 
