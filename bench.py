@@ -420,6 +420,22 @@ def main():
                                                             for r in range(Q.shape[0])])),
                              "qps": Q.shape[0] / (e0.elapsed_time(e1) / 1e3)}
         search_q["sampled_entries"]["samples"] = SEARCH_SAMPLES
+    # the reference tool's own bucketing (KMeans||, balanced 1-way, own + nprobe pools) on the same
+    # data: device time of one build and recall@32 of its lists on the same sampled points
+    ref_bucketing = None
+    if world == 1 and rank == 0:
+        gta.build_bucket2(Xd, cfg.knn_degree, 32, 0.01, 42)  # warm-up
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        rids, _ = gta.build_bucket2(Xd, cfg.knn_degree, 32, 0.01, 42)
+        e1.record()
+        torch.cuda.synchronize()
+        rms = e0.elapsed_time(e1)
+        approx = rids[q].cpu().numpy()[:, :32]
+        ref_bucketing = {"centroid_ratio": 0.01, "nprobe": 32, "ms": rms, "value": cfg.n / (rms / 1e3) / 1e6,
+                         "unit": UNIT, "recall_at_32": float(np.mean([len(np.intersect1d(approx[r], gt[r])) / 32.0
+                                                                      for r in range(1000)])),
+                         "stage": "kNN lists only (no CAGRA optimize)"}
     del Xall, g_all
 
     # end to end with host buffers (pinned), copies inside the timed region: through the C ABI
@@ -477,7 +493,7 @@ def main():
                 "vs_baseline": None, "dtype": "bf16" if cfg.dtype == "uint8" else "tf32",
                 "data": "synthetic (seeded Gaussian mixture)", "config": config, "roofline": roofline,
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-                "clocks": clocks, "recall_at_32": recall, "search": search_q, "bucket_skew": skew, "phases_ms_max_over_ranks": phases,
+                "clocks": clocks, "recall_at_32": recall, "search": search_q, "reference_bucketing": ref_bucketing, "bucket_skew": skew, "phases_ms_max_over_ranks": phases,
                 "stages": stage_summary,
                 "instrumented_ms_per_step": step_ms_sum}
         print(json.dumps(line))

@@ -235,6 +235,26 @@ void assign_topk_impl(const float* Xp, const float* xn, int64_t n, int d, int d_
     dist_topk(pr, st);
 }
 
+// Top-k of bf16 rows (8-bit data held exactly) against bf16 centroid rows: the tensor-core path
+// with exact integer distances, no screen and no rerank.
+void assign_topk_bf16(const void* Xb, const float* xn, int64_t n, int d, int d_pad, const void* Cb, const float* cn,
+                      int B, int k, int32_t* ids, float* dists, int* err, cudaStream_t st)
+{
+    GTA_REQUIRE(k >= 1 && k <= B, kInvalid, "assign: need 1 <= k <= B");
+    std::vector<WorkItem> wl;
+    wl.reserve(static_cast<size_t>((n + 127) / 128));
+    for (int64_t r = 0; r < n; r += 128)
+        wl.push_back(WorkItem{static_cast<int32_t>(r), static_cast<int32_t>(std::min<int64_t>(128, n - r)), 0, B, -1, 0, 0, 0});
+    auto work = upload(wl, st);
+    DistTopkProblem pr;
+    pr.A = Xb; pr.a_total = n; pr.B = Cb; pr.b_total = B; pr.elem = kElemBF16; pr.d = d; pr.d_pad = d_pad;
+    pr.a_norm = xn; pr.b_norm = cn; pr.b_gid = nullptr; pr.work = work.get(); pr.n_work = static_cast<int>(wl.size());
+    pr.m_out = k; pr.exclude_self = false; pr.out_ids = ids; pr.out_dists = dists; pr.err = err;
+    pr.prof_name = "dist_topk_assign";
+    pr.flops = 2.0 * static_cast<double>(n) * B * d;
+    dist_topk(pr, st);
+}
+
 // The sample's rows in the dataset's own element type (for the exact assignment, which then
 // reads 8-bit rows instead of the f32 copy): row_ids[i] is sample row i's row of X.
 struct RawRows {
@@ -492,21 +512,78 @@ int64_t bucket2_requested(int64_t N, float ratio)
     return std::max<int64_t>(2, static_cast<int64_t>(static_cast<double>(N) * r));
 }
 
+// The dataset prepared for nearest-centroid queries where centroids are data points: 8-bit rows
+// held exactly as bf16 (tensor cores, exact integer distances), other data as padded f32 (tf32
+// screen + exact rerank); few centroids (<= 384, k <= 4) take the exact FP32-pipe path.
+struct Space {
+    const void* X = nullptr;
+    int dtype = GTA_F32;
+    int64_t N = 0;
+    int d = 0;
+    bool ex8 = false;
+    int elem = kElemF32;
+    int d_pad = 0;
+    size_t row_bytes = 0;
+    DevBuf<uint8_t> rows;
+    DevBuf<float> norms;
+
+    Space(const void* X_, int dtype_, int64_t N_, int d_, cudaStream_t st) : X(X_), dtype(dtype_), N(N_), d(d_)
+    {
+        ex8 = exact_bf16(dtype, d);
+        elem = ex8 ? kElemBF16 : kElemF32;
+        d_pad = pad_dim(d, elem);
+        row_bytes = static_cast<size_t>(d_pad) * (ex8 ? 2 : 4);
+        rows = DevBuf<uint8_t>(static_cast<size_t>(N) * row_bytes, st);
+        norms = DevBuf<float>(static_cast<size_t>(N), st);
+        convert_rows(X, dtype, d, nullptr, N, rows.get(), elem, d_pad, norms.get(), st);
+    }
+    const void* row(int64_t i) const { return rows.get() + static_cast<size_t>(i) * row_bytes; }
+
+    // top-k of the queries (all N points, or the rows q_ids) among the points c_ids
+    void assign(const int32_t* q_ids, int64_t nq, const int32_t* c_ids, int nC, int k, int32_t* ids, float* dists,
+                int* err, cudaStream_t st) const
+    {
+        if (assign_exact_applies(nC, k)) {
+            const int d32 = pad_dim(d, kElemF32);
+            DevBuf<float> Cf(static_cast<size_t>(nC) * d32, st);
+            convert_rows(X, dtype, d, c_ids, nC, Cf.get(), kElemF32, d32, nullptr, st);
+            assign_exact(X, dtype, nq, d, d, q_ids, Cf.get(), d32, nC, k, ids, dists, st);
+            return;
+        }
+        DevBuf<uint8_t> Cr(static_cast<size_t>(nC) * row_bytes, st), Qr;
+        DevBuf<float> cn(static_cast<size_t>(nC), st), qn;
+        convert_rows(X, dtype, d, c_ids, nC, Cr.get(), elem, d_pad, cn.get(), st);
+        const void* Q = rows.get();
+        const float* qnp = norms.get();
+        if (q_ids) {
+            Qr = DevBuf<uint8_t>(static_cast<size_t>(nq) * row_bytes, st);
+            qn = DevBuf<float>(static_cast<size_t>(nq), st);
+            convert_rows(X, dtype, d, q_ids, nq, Qr.get(), elem, d_pad, qn.get(), st);
+            Q = Qr.get();
+            qnp = qn.get();
+        }
+        if (ex8)
+            assign_topk_bf16(Q, qnp, nq, d, d_pad, Cr.get(), cn.get(), nC, k, ids, dists, err, st);
+        else
+            assign_topk_impl(static_cast<const float*>(Q), qnp, nq, d, d_pad, reinterpret_cast<const float*>(Cr.get()),
+                             cn.get(), nC, k, ids, dists, err, st);
+    }
+};
+
 // KMeans|| candidates (bucket.cu:2919-3117) and their uniform subsample (:3150-3172) -> point ids
-std::vector<int32_t> kmeans_parallel_ids(const float* Xf, const float* xn, int64_t N, int d, int d32, const void* X,
-                                         int dtype, int64_t n_req, uint64_t seed, int* err, cudaStream_t st)
+std::vector<int32_t> kmeans_parallel_ids(const Space& sp, int64_t n_req, uint64_t seed, int* err, cudaStream_t st)
 {
+    const int64_t N = sp.N;
     const int32_t c0 = static_cast<int32_t>(mix64(seed ^ 0xA0761D6478BD642Full) % static_cast<uint64_t>(N));
     std::vector<int32_t> cand{c0};
     DevBuf<uint8_t> chosen(static_cast<size_t>(N), st), sel(static_cast<size_t>(N), st);
     GTA_CUDA(cudaMemsetAsync(chosen.get(), 0, static_cast<size_t>(N), st));
     GTA_CUDA(cudaMemsetAsync(chosen.get() + c0, 1, 1, st));
     DevBuf<float> min_d(static_cast<size_t>(N), st), d_new(static_cast<size_t>(N), st);
-    DevBuf<int32_t> tmp_ids(static_cast<size_t>(N), st), new_ids(static_cast<size_t>(N), st);
+    DevBuf<int32_t> tmp_ids(static_cast<size_t>(N), st), new_ids(static_cast<size_t>(N), st), c0d(1, st);
+    GTA_CUDA(cudaMemcpyAsync(c0d.get(), &c0, sizeof(int32_t), cudaMemcpyHostToDevice, st));
     DevBuf<double> psi(1, st);
-    // distance to the first point (one centroid: the exact chain)
-    assign_topk_impl(Xf, xn, N, d, d32, Xf + static_cast<int64_t>(c0) * d32, xn + c0, 1, 1, tmp_ids.get(), min_d.get(),
-                     err, st);
+    sp.assign(nullptr, N, c0d.get(), 1, 1, tmp_ids.get(), min_d.get(), err, st);  // distance to the first point
     const double lk = kKparOvershoot / kKparRounds * static_cast<double>(n_req);
     for (int r = 0; r < kKparRounds; ++r) {
         kpar_psi(min_d.get(), N, psi.get(), st);
@@ -517,10 +594,7 @@ std::vector<int32_t> kmeans_parallel_ids(const float* Xf, const float* xn, int64
         cand.resize(old + static_cast<size_t>(n_new));
         GTA_CUDA(cudaMemcpyAsync(cand.data() + old, new_ids.get(), sizeof(int32_t) * n_new, cudaMemcpyDeviceToHost, st));
         if (r + 1 < kKparRounds) {  // distances to the new candidates (not after the last round, :3080)
-            DevBuf<float> Cn(static_cast<size_t>(n_new) * d32, st), cnn(static_cast<size_t>(n_new), st);
-            convert_rows(X, dtype, d, new_ids.get(), n_new, Cn.get(), kElemF32, d32, cnn.get(), st);
-            assign_topk_impl(Xf, xn, N, d, d32, Cn.get(), cnn.get(), static_cast<int>(n_new), 1, tmp_ids.get(),
-                             d_new.get(), err, st);
+            sp.assign(nullptr, N, new_ids.get(), static_cast<int>(n_new), 1, tmp_ids.get(), d_new.get(), err, st);
             min_update(min_d.get(), d_new.get(), N, st);
         }
         GTA_CUDA(cudaStreamSynchronize(st));  // cand is read on the host below
@@ -550,21 +624,17 @@ void build_bucket2_round(const void* X, int dtype, int64_t N, int d, const gta_b
     DevBuf<int> err(1, st);
     GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
     ProfScope prof_all("build_bucket2_total", 0.0, st);
-    const int d32 = pad_dim(d, kElemF32);
-    DevBuf<float> Xf(static_cast<size_t>(N) * d32, st), xn(static_cast<size_t>(N), st);
-    convert_rows(X, dtype, d, nullptr, N, Xf.get(), kElemF32, d32, xn.get(), st);
+    Space sp(X, dtype, N, d, st);
 
     // ---- Step 2: KMeans|| data-point centroids
     std::vector<int32_t> cid_h;
     {
         ProfScope prof("kmeans_parallel", 0.0, st);
-        cid_h = kmeans_parallel_ids(Xf.get(), xn.get(), N, d, d32, X, dtype, n_req, seed, err.get(), st);
+        cid_h = kmeans_parallel_ids(sp, n_req, seed, err.get(), st);
     }
     const int32_t B = static_cast<int32_t>(cid_h.size());
     GTA_REQUIRE(B >= 2, kData, "build_bucket2: KMeans|| found fewer than two centroids");
     auto cid = upload(cid_h, st);
-    DevBuf<float> C(static_cast<size_t>(B) * d32, st), cn(static_cast<size_t>(B), st);
-    convert_rows(X, dtype, d, cid.get(), B, C.get(), kElemF32, d32, cn.get(), st);
 
     // ---- Step 3: centroid kNN graph (self excluded): the pools' neighbour buckets
     int P = p.nprobe > 0 ? p.nprobe : (p.knn_k > 0 ? p.knn_k : 32);
@@ -574,7 +644,7 @@ void build_bucket2_round(const void* X, int dtype, int64_t N, int d, const gta_b
         ProfScope prof("centroid_knn", 0.0, st);
         DevBuf<int32_t> ki(static_cast<size_t>(B) * (P + 1), st);
         DevBuf<float> kd(static_cast<size_t>(B) * (P + 1), st);
-        assign_topk_impl(C.get(), cn.get(), B, d, d32, C.get(), cn.get(), B, P + 1, ki.get(), kd.get(), err.get(), st);
+        sp.assign(cid.get(), B, cid.get(), B, P + 1, ki.get(), kd.get(), err.get(), st);
         std::vector<int32_t> h(static_cast<size_t>(B) * (P + 1));
         GTA_CUDA(cudaMemcpyAsync(h.data(), ki.get(), sizeof(int32_t) * h.size(), cudaMemcpyDeviceToHost, st));
         GTA_CUDA(cudaStreamSynchronize(st));
@@ -595,11 +665,9 @@ void build_bucket2_round(const void* X, int dtype, int64_t N, int d, const gta_b
         ProfScope prof("top2_total", 0.0, st);
         DevBuf<int32_t> top2(static_cast<size_t>(N) * 2, st);
         DevBuf<float> t2d(static_cast<size_t>(N) * 2, st);
-        assign_topk_impl(Xf.get(), xn.get(), N, d, d32, C.get(), cn.get(), B, 2, top2.get(), t2d.get(), err.get(), st);
+        sp.assign(nullptr, N, cid.get(), B, 2, top2.get(), t2d.get(), err.get(), st);
         balanced_assign(top2.get(), cid.get(), B, N, assign.get(), err.get(), st);
     }
-    Xf.release();
-    xn.release();
     DevBuf<int32_t> members(static_cast<size_t>(N), st);
     DevBuf<int64_t> offsets(static_cast<size_t>(B) + 1, st);
     group_by_key(assign.get(), N, B, members.get(), offsets.get(), err.get(), st);

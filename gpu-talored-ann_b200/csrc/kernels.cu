@@ -60,23 +60,71 @@ __device__ __forceinline__ float exact_l2_f(const float* __restrict__ a, const f
 }
 
 // ---------------------------------------------------------------- conversion
+// four consecutive elements as f32 (the caller guarantees the alignment of the access)
+__device__ __forceinline__ void load4_f32(const float* p, float (&v)[4])
+{
+    const float4 q = *reinterpret_cast<const float4*>(p);
+    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+}
+__device__ __forceinline__ void load4_f32(const uint8_t* p, float (&v)[4])
+{
+    const uchar4 q = *reinterpret_cast<const uchar4*>(p);
+    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+}
+__device__ __forceinline__ void load4_f32(const int8_t* p, float (&v)[4])
+{
+    const char4 q = *reinterpret_cast<const char4*>(p);
+    v[0] = q.x; v[1] = q.y; v[2] = q.z; v[3] = q.w;
+}
+__device__ __forceinline__ void load4_f32(const __nv_bfloat16* p, float (&v)[4])
+{
+    for (int u = 0; u < 4; ++u) v[u] = __bfloat162float(p[u]);
+}
+__device__ __forceinline__ void store4_from_f32(float* p, const float (&v)[4])
+{
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ void store4_from_f32(__nv_bfloat16* p, const float (&v)[4])
+{
+    __nv_bfloat162 a = __floats2bfloat162_rn(v[0], v[1]), b = __floats2bfloat162_rn(v[2], v[3]);
+    uint2 u;
+    u.x = *reinterpret_cast<uint32_t*>(&a);
+    u.y = *reinterpret_cast<uint32_t*>(&b);
+    *reinterpret_cast<uint2*>(p) = u;
+}
+
 template <typename Tin, typename Tout>
 __global__ void convert_rows_kernel(const Tin* __restrict__ X, int d, const int32_t* __restrict__ row_ids,
-                                    int64_t n_out, Tout* __restrict__ out, int d_pad, float* __restrict__ norms)
+                                    int64_t n_out, Tout* __restrict__ out, int d_pad, float* __restrict__ norms, int vec4)
 {
     const int lane = threadIdx.x & 31;
     const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (row >= n_out) return;
     const int64_t src = row_ids ? static_cast<int64_t>(row_ids[row]) : row;
     const Tin* x = X + src * d;
-    if (out) {
-        Tout* o = out + row * d_pad;
-        for (int i = lane; i < d_pad; i += 32) o[i] = from_f32<Tout>(i < d ? ld_f32(x + i) : 0.0f);
+    Tout* o = out ? out + row * d_pad : nullptr;
+    // squared norm: per-lane fma chains, then a butterfly sum (exact for 8-bit rows, where every
+    // partial sum is an integer below 2^24)
+    float acc = 0.0f;
+    if (vec4) {  // d % 4 == 0, rows 4-element aligned: four elements per lane and access
+        for (int g = lane; 4 * g < d_pad; g += 32) {
+            float v[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+            if (4 * g < d) load4_f32(x + 4 * g, v);
+#pragma unroll
+            for (int u = 0; u < 4; ++u) acc = fmaf(v[u], v[u], acc);
+            if (o) store4_from_f32(o + 4 * g, v);
+        }
+    } else {
+        for (int i = lane; i < d_pad; i += 32) {
+            const float v = i < d ? ld_f32(x + i) : 0.0f;
+            acc = fmaf(v, v, acc);
+            if (o) o[i] = from_f32<Tout>(v);
+        }
     }
-    if (norms && lane == 0) {
-        float acc = 0.0f;
-        for (int i = 0; i < d; ++i) { const float v = ld_f32(x + i); acc = fmaf(v, v, acc); }
-        norms[row] = acc;
+    if (norms) {
+#pragma unroll
+        for (int m = 16; m > 0; m >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, m);
+        if (lane == 0) norms[row] = acc;
     }
 }
 
@@ -86,11 +134,17 @@ void convert_dispatch_out(const Tin* X, int d, const int32_t* ids, int64_t n, vo
 {
     const int wpb = 8;
     const unsigned grid = static_cast<unsigned>((n + wpb - 1) / wpb);
+    const size_t in_align = sizeof(Tin) * 4, out_align = (out_elem == kElemBF16 ? 2 : 4) * 4;
+    const int vec4 = (d % 4 == 0) && (d_pad % 4 == 0) && (reinterpret_cast<uintptr_t>(X) % in_align == 0) &&
+                     (reinterpret_cast<uintptr_t>(out) % out_align == 0);
     if (out_elem == kElemBF16)
         convert_rows_kernel<Tin, __nv_bfloat16><<<grid, wpb * 32, 0, st>>>(X, d, ids, n,
-                                                                            static_cast<__nv_bfloat16*>(out), d_pad, norms);
+                                                                            static_cast<__nv_bfloat16*>(out), d_pad, norms,
+                                                                            vec4);
     else
-        convert_rows_kernel<Tin, float><<<grid, wpb * 32, 0, st>>>(X, d, ids, n, static_cast<float*>(out), d_pad, norms);
+        convert_rows_kernel<Tin, float><<<grid, wpb * 32, 0, st>>>(X, d, ids, n, static_cast<float*>(out), d_pad, norms,
+                                                                    vec4);
+    count_launches(1);
 }
 
 // Rows of a shard holding global rows [row0, row0 + n): out[j] = X[ids[j] - row0]
