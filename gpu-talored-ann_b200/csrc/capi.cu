@@ -305,15 +305,23 @@ uint64_t kmeans_pool_seed(uint64_t seed) { return seed ^ 0x9E3779B97F4A7C15ull; 
 
 // members: the row of X gathered into each membership slot (grouped by bucket);
 // gid: the id written to the lists for each slot (members when null).
+// Buckets [b_lo, b_hi) (all when b_hi < 0) of the membership CSR: list row j - offsets[b_lo] is
+// membership j.  off_host: the offsets already on the host (else read from offsets_dev).
 void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* members, const int64_t* offsets_dev,
                      int B, int M, int32_t* list_ids, float* list_dists, int* err, cudaStream_t st,
-                     const int32_t* gid = nullptr)
+                     const int32_t* gid = nullptr, int b_lo = 0, int b_hi = -1, const int64_t* off_host = nullptr)
 {
     (void)n;
+    if (b_hi < 0) b_hi = B;
     std::vector<int64_t> off(static_cast<size_t>(B) + 1);
-    GTA_CUDA(cudaMemcpyAsync(off.data(), offsets_dev, sizeof(int64_t) * (B + 1), cudaMemcpyDeviceToHost, st));
-    GTA_CUDA(cudaStreamSynchronize(st));
-    const int64_t n_mem = off[B];
+    if (off_host) {
+        std::copy(off_host, off_host + B + 1, off.begin());
+    } else {
+        GTA_CUDA(cudaMemcpyAsync(off.data(), offsets_dev, sizeof(int64_t) * (B + 1), cudaMemcpyDeviceToHost, st));
+        GTA_CUDA(cudaStreamSynchronize(st));
+    }
+    const int64_t j0 = off[static_cast<size_t>(b_lo)];
+    const int64_t n_mem = off[static_cast<size_t>(b_hi)] - j0;
     if (n_mem == 0) return;
     GTA_REQUIRE(n_mem < (1ll << 31), kInvalid, "bucket_knn: too many memberships on one device");
     const int elem = exact_bf16(dtype, d) ? kElemBF16 : kElemF32;
@@ -322,15 +330,15 @@ void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* 
     DevBuf<float> pnorm(static_cast<size_t>(n_mem), st);
     {
         ProfScope prof("gather", static_cast<double>(n_mem) * (d * elem_size(dtype) + d_pad * (elem == kElemBF16 ? 2 : 4)), st);
-        convert_rows(X, dtype, d, members, n_mem, pool.get(), elem, d_pad, pnorm.get(), st);
+        convert_rows(X, dtype, d, members + j0, n_mem, pool.get(), elem, d_pad, pnorm.get(), st);
     }
     // work list: one CTA per 128-row tile of a bucket, largest buckets first
-    std::vector<int> order(static_cast<size_t>(B));
-    std::iota(order.begin(), order.end(), 0);
+    std::vector<int> order(static_cast<size_t>(b_hi - b_lo));
+    std::iota(order.begin(), order.end(), b_lo);
     std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return off[a + 1] - off[a] > off[b + 1] - off[b]; });
     std::vector<WorkItem> wl;
     for (int b : order) {
-        const int64_t lo = off[b], nb = off[b + 1] - off[b];
+        const int64_t lo = off[b] - j0, nb = off[b + 1] - off[b];
         for (int64_t t = 0; t < nb; t += 128)
             wl.push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, nb - t)),
                                   static_cast<int32_t>(lo), static_cast<int32_t>(nb), static_cast<int32_t>(t), 0, 0, 0});
@@ -338,11 +346,11 @@ void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* 
     auto work = upload(wl, st);
     DistTopkProblem pr;
     pr.A = pool.get(); pr.a_total = n_mem; pr.B = pool.get(); pr.b_total = n_mem; pr.elem = elem; pr.d = d;
-    pr.d_pad = d_pad; pr.a_norm = pnorm.get(); pr.b_norm = pnorm.get(); pr.b_gid = gid ? gid : members; pr.work = work.get();
-    pr.n_work = static_cast<int>(wl.size()); pr.m_out = M; pr.exclude_self = true; pr.out_ids = list_ids;
-    pr.out_dists = list_dists; pr.err = err;
+    pr.d_pad = d_pad; pr.a_norm = pnorm.get(); pr.b_norm = pnorm.get(); pr.b_gid = (gid ? gid : members) + j0;
+    pr.work = work.get(); pr.n_work = static_cast<int>(wl.size()); pr.m_out = M; pr.exclude_self = true;
+    pr.out_ids = list_ids; pr.out_dists = list_dists; pr.err = err;
     pr.prof_name = "dist_topk_bucket";
-    for (int b = 0; b < B; ++b) {
+    for (int b = b_lo; b < b_hi; ++b) {
         const double nb = static_cast<double>(off[b + 1] - off[b]);
         pr.flops += 2.0 * nb * nb * d;
     }
@@ -355,6 +363,8 @@ struct BucketOut {
     float* centroids;  // device [B x d] or null
     int32_t* top2;     // device [N x 2] or null
 };
+
+constexpr size_t kTop2ChunkBytes = size_t(8) << 30;  // f32 rows converted at once for the top-2 pass
 
 void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const BucketOut& o, cudaStream_t st)
 {
@@ -426,13 +436,20 @@ void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const
         DevBuf<float> t2d(static_cast<size_t>(N) * 2, st);
         if (assign_exact_applies(B, 2)) {  // straight from the dataset's own element type
             assign_exact(X, ds.dtype, N, d, d, nullptr, C.get(), d32, B, 2, top2.get(), t2d.get(), st);
-        } else {
-            DevBuf<float> Xf(static_cast<size_t>(N) * d32, st), xn(static_cast<size_t>(N), st);
-            {
-                ProfScope prof("convert_x", static_cast<double>(N) * (d * elem_size(ds.dtype) + d32 * 4.0), st);
-                convert_rows(X, ds.dtype, d, nullptr, N, Xf.get(), kElemF32, d32, xn.get(), st);
+        } else {  // the f32 copy of the rows in chunks of at most kTop2ChunkBytes
+            const int64_t chunk = std::max<int64_t>(128, static_cast<int64_t>(kTop2ChunkBytes / (static_cast<size_t>(d32) * 4)));
+            DevBuf<float> Xf(static_cast<size_t>(std::min(N, chunk)) * d32, st), xn(static_cast<size_t>(std::min(N, chunk)), st);
+            DevBuf<int32_t> rid(static_cast<size_t>(std::min(N, chunk)), st);
+            for (int64_t r0 = 0; r0 < N; r0 += chunk) {
+                const int64_t nr = std::min(chunk, N - r0);
+                const void* Xr = static_cast<const uint8_t*>(X) + static_cast<size_t>(r0) * d * elem_size(ds.dtype);
+                {
+                    ProfScope prof("convert_x", static_cast<double>(nr) * (d * elem_size(ds.dtype) + d32 * 4.0), st);
+                    convert_rows(Xr, ds.dtype, d, nullptr, nr, Xf.get(), kElemF32, d32, xn.get(), st);
+                }
+                assign_topk_impl(Xf.get(), xn.get(), nr, d, d32, C.get(), cn.get(), B, 2, top2.get() + 2 * r0,
+                                 t2d.get() + 2 * r0, err.get(), st);
             }
-            assign_topk_impl(Xf.get(), xn.get(), N, d, d32, C.get(), cn.get(), B, 2, top2.get(), t2d.get(), err.get(), st);
         }
     }
     if (o.top2) GTA_CUDA(cudaMemcpyAsync(o.top2, top2.get(), sizeof(int32_t) * 2 * N, cudaMemcpyDeviceToDevice, st));
@@ -441,14 +458,46 @@ void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const
     build_memberships(top2.get(), N, B, members.get(), offsets.get(), mem_row.get(), err.get(), st);
     top2.release();
 
-    // ---- per-bucket all-pairs kNN, then merge each point's two lists
-    DevBuf<int32_t> lid(static_cast<size_t>(N) * 2 * M, st);
-    DevBuf<float> ldist(static_cast<size_t>(N) * 2 * M, st);
-    {
+    // ---- per-bucket all-pairs kNN, then merge each point's two lists.  When the memberships' pool
+    // rows and lists do not fit the device budget, buckets are processed in ascending batches that
+    // do, each batch's lists merged into the per-point lists as it completes (first memberships
+    // copied, second ones merged: the same lists as the one-pass build).
+    const int64_t n_mem = 2 * N;
+    const int elem = exact_bf16(ds.dtype, d) ? kElemBF16 : kElemF32;
+    const double per_row = static_cast<double>(pad_dim(d, elem)) * (elem == kElemBF16 ? 2 : 4) + 8.0 * M + 8.0;
+    size_t free_b = 0, total_b = 0;
+    GTA_CUDA(cudaMemGetInfo(&free_b, &total_b));
+    const double budget = p.device_budget > 0 ? static_cast<double>(p.device_budget) : 0.8 * static_cast<double>(free_b);
+    if (static_cast<double>(n_mem) * per_row <= budget) {
+        DevBuf<int32_t> lid(static_cast<size_t>(n_mem) * M, st);
+        DevBuf<float> ldist(static_cast<size_t>(n_mem) * M, st);
+        {
+            ProfScope prof("bucket_knn_total", 0.0, st);
+            bucket_knn_impl(X, ds.dtype, N, d, members.get(), offsets.get(), B, M, lid.get(), ldist.get(), err.get(), st);
+        }
+        merge_memberships(lid.get(), ldist.get(), mem_row.get(), N, M, o.ids, o.dists, st);
+    } else {
+        std::vector<int64_t> off(static_cast<size_t>(B) + 1);
+        GTA_CUDA(cudaMemcpyAsync(off.data(), offsets.get(), sizeof(int64_t) * (B + 1), cudaMemcpyDeviceToHost, st));
+        GTA_CUDA(cudaStreamSynchronize(st));
+        const int64_t cap = std::max<int64_t>(1, static_cast<int64_t>(budget / per_row));
         ProfScope prof("bucket_knn_total", 0.0, st);
-        bucket_knn_impl(X, ds.dtype, N, d, members.get(), offsets.get(), B, M, lid.get(), ldist.get(), err.get(), st);
+        for (int b_lo = 0; b_lo < B;) {
+            int b_hi = b_lo + 1;  // at least one bucket per batch
+            while (b_hi < B && off[b_hi + 1] - off[b_lo] <= cap) ++b_hi;
+            const int64_t j0 = off[b_lo], nb = off[b_hi] - j0;
+            if (nb > 0) {
+                DevBuf<int32_t> lid(static_cast<size_t>(nb) * M, st);
+                DevBuf<float> ldist(static_cast<size_t>(nb) * M, st);
+                bucket_knn_impl(X, ds.dtype, N, d, members.get(), offsets.get(), B, M, lid.get(), ldist.get(), err.get(),
+                                st, nullptr, b_lo, b_hi, off.data());
+                merge_membership_batch(lid.get(), ldist.get(), members.get(), mem_row.get(), j0, nb, N, M, o.ids,
+                                       o.dists, st);
+                GTA_CUDA(cudaStreamSynchronize(st));  // the batch's buffers are released next
+            }
+            b_lo = b_hi;
+        }
     }
-    merge_memberships(lid.get(), ldist.get(), mem_row.get(), N, M, o.ids, o.dists, st);
     check_device_error(err.get(), st, "build_bucket");
 }
 

@@ -134,6 +134,10 @@ void build_memberships(const int32_t* top2, int64_t N, int32_t B, int32_t* membe
                        int64_t* mem_row, int* err, cudaStream_t st);
 void merge_memberships(const int32_t* list_n, const float* list_d, const int64_t* mem_row, int64_t N, int M,
                        int32_t* out_n, float* out_d, cudaStream_t st);
+// membership rows j0 .. j0 + n - 1 (their lists in bl / bd) into the per-point lists, first memberships
+// copied, second ones merged (the order of merge_memberships)
+void merge_membership_batch(const int32_t* bl, const float* bd, const int32_t* members, const int64_t* mem_row,
+                            int64_t j0, int64_t n, int64_t N, int M, int32_t* out_n, float* out_d, cudaStream_t st);
 void merge_lists(const int32_t* run_n, const float* run_d, const int32_t* new_n, const float* new_d, int64_t N,
                  int M, int32_t* out_n, float* out_d, cudaStream_t st);
 void sanitize(const int32_t* knn, int64_t N, int M, uint32_t* out, cudaStream_t st);

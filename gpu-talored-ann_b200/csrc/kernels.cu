@@ -618,27 +618,18 @@ __global__ void mem_rows_kernel(const uint32_t* __restrict__ keys_sorted, const 
 constexpr int kMergeWarps = 8;
 constexpr int kMaxM = 128;
 
-__global__ void __launch_bounds__(kMergeWarps * 32)
-    merge_kernel(const int32_t* __restrict__ run_n, const float* __restrict__ run_d, const int32_t* __restrict__ new_n,
-                 const float* __restrict__ new_d, const int64_t* __restrict__ mem_row, int64_t N, int M,
-                 int32_t* __restrict__ out_n, float* __restrict__ out_d)
+// One warp merges the running list a (na valid entries used) with the new list b: b's entries
+// whose id is already in a are dropped, the rest merged by distance with a's entries first on
+// equal distance; out may alias a (both lists are staged in shared memory first).
+__device__ __forceinline__ void merge_warp(const int32_t* an, const float* ad, bool va, const int32_t* bn,
+                                           const float* bd, bool vb, int M, int32_t* on, float* od, int32_t* s_an,
+                                           int32_t* s_bn, float* s_ad, float* s_bd, int* s_rank)
 {
-    // mem_row entries outside [0, 2N) (a membership that was never built) read as empty lists
-    __shared__ int32_t s_an[kMergeWarps][kMaxM], s_bn[kMergeWarps][kMaxM];
-    __shared__ float s_ad[kMergeWarps][kMaxM], s_bd[kMergeWarps][kMaxM];
-    __shared__ int s_rank[kMergeWarps][kMaxM];
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    const int64_t p = static_cast<int64_t>(blockIdx.x) * kMergeWarps + w;
-    if (p >= N) return;
-    const int64_t ra = mem_row ? mem_row[2 * p] : p;
-    const int64_t rb = mem_row ? mem_row[2 * p + 1] : p;
-    const bool va = !mem_row || (ra >= 0 && ra < 2 * N), vb = !mem_row || (rb >= 0 && rb < 2 * N);
-    const int32_t* an = run_n + (va ? ra : 0) * M; const float* ad = run_d + (va ? ra : 0) * M;
-    const int32_t* bn = new_n + (vb ? rb : 0) * M; const float* bd = new_d + (vb ? rb : 0) * M;
+    const int lane = threadIdx.x & 31;
     int na = va ? M : 0, nb = vb ? M : 0;
     for (int k = lane; k < M; k += 32) {
         const int32_t x = va ? an[k] : -1, y = vb ? bn[k] : -1;
-        s_an[w][k] = x; s_ad[w][k] = va ? ad[k] : INFINITY; s_bn[w][k] = y; s_bd[w][k] = vb ? bd[k] : INFINITY;
+        s_an[k] = x; s_ad[k] = va ? ad[k] : INFINITY; s_bn[k] = y; s_bd[k] = vb ? bd[k] : INFINITY;
         if (x < 0) na = min(na, k);
         if (y < 0) nb = min(nb, k);
     }
@@ -652,34 +643,81 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
         const int j = g * 32 + lane;
         bool keep = false;
         if (j < nb) {
-            const int32_t id = s_bn[w][j];
+            const int32_t id = s_bn[j];
             keep = true;
-            for (int k = 0; k < na; ++k) keep &= (s_an[w][k] != id);
+            for (int k = 0; k < na; ++k) keep &= (s_an[k] != id);
         }
         const unsigned m = __ballot_sync(0xffffffffu, keep);
-        if (j < M) s_rank[w][j] = keep ? base + __popc(m & ((1u << lane) - 1u)) : -1;
+        if (j < M) s_rank[j] = keep ? base + __popc(m & ((1u << lane) - 1u)) : -1;
         base += __popc(m);
     }
     __syncwarp();
     const int n_keep = base;
-    int32_t* on = out_n + p * M; float* od = out_d + p * M;
     for (int i = lane; i < na; i += 32) {
-        const float x = s_ad[w][i];
+        const float x = s_ad[i];
         int c = 0;
-        for (int j = 0; j < nb; ++j) c += (s_rank[w][j] >= 0 && s_bd[w][j] < x);
+        for (int j = 0; j < nb; ++j) c += (s_rank[j] >= 0 && s_bd[j] < x);
         const int pos = i + c;
-        if (pos < M) { on[pos] = s_an[w][i]; od[pos] = x; }
+        if (pos < M) { on[pos] = s_an[i]; od[pos] = x; }
     }
     for (int j = lane; j < nb; j += 32) {
-        const int k = s_rank[w][j];
+        const int k = s_rank[j];
         if (k < 0) continue;
-        const float x = s_bd[w][j];
+        const float x = s_bd[j];
         int c = 0;
-        for (int i = 0; i < na; ++i) c += (s_ad[w][i] <= x);
+        for (int i = 0; i < na; ++i) c += (s_ad[i] <= x);
         const int pos = k + c;
-        if (pos < M) { on[pos] = s_bn[w][j]; od[pos] = x; }
+        if (pos < M) { on[pos] = s_bn[j]; od[pos] = x; }
     }
     for (int q = na + n_keep + lane; q < M; q += 32) { on[q] = -1; od[q] = INFINITY; }
+    __syncwarp();
+}
+
+__global__ void __launch_bounds__(kMergeWarps * 32)
+    merge_kernel(const int32_t* __restrict__ run_n, const float* __restrict__ run_d, const int32_t* __restrict__ new_n,
+                 const float* __restrict__ new_d, const int64_t* __restrict__ mem_row, int64_t N, int M,
+                 int32_t* __restrict__ out_n, float* __restrict__ out_d)
+{
+    // mem_row entries outside [0, 2N) (a membership that was never built) read as empty lists
+    __shared__ int32_t s_an[kMergeWarps][kMaxM], s_bn[kMergeWarps][kMaxM];
+    __shared__ float s_ad[kMergeWarps][kMaxM], s_bd[kMergeWarps][kMaxM];
+    __shared__ int s_rank[kMergeWarps][kMaxM];
+    const int w = threadIdx.x >> 5;
+    const int64_t p = static_cast<int64_t>(blockIdx.x) * kMergeWarps + w;
+    if (p >= N) return;
+    const int64_t ra = mem_row ? mem_row[2 * p] : p;
+    const int64_t rb = mem_row ? mem_row[2 * p + 1] : p;
+    const bool va = !mem_row || (ra >= 0 && ra < 2 * N), vb = !mem_row || (rb >= 0 && rb < 2 * N);
+    merge_warp(run_n + (va ? ra : 0) * M, run_d + (va ? ra : 0) * M, va, new_n + (vb ? rb : 0) * M,
+               new_d + (vb ? rb : 0) * M, vb, M, out_n + p * M, out_d + p * M, s_an[w], s_bn[w], s_ad[w], s_bd[w],
+               s_rank[w]);
+}
+
+// A batch of membership rows j0 .. j0 + n - 1 (lists at row j - j0 of bl / bd) into the per-point
+// lists out: pass 0 copies every row that is its point's first (lower-bucket) membership, pass 1
+// merges every row that is the second into what the first left there (the order of
+// merge_memberships, so a bucket-batched build equals the one-pass build).
+__global__ void __launch_bounds__(kMergeWarps * 32)
+    merge_batch_kernel(const int32_t* __restrict__ bl, const float* __restrict__ bd, const int32_t* __restrict__ members,
+                       const int64_t* __restrict__ mem_row, int64_t j0, int64_t n, int64_t N, int M, int pass,
+                       int32_t* __restrict__ out_n, float* __restrict__ out_d)
+{
+    __shared__ int32_t s_an[kMergeWarps][kMaxM], s_bn[kMergeWarps][kMaxM];
+    __shared__ float s_ad[kMergeWarps][kMaxM], s_bd[kMergeWarps][kMaxM];
+    __shared__ int s_rank[kMergeWarps][kMaxM];
+    const int w = threadIdx.x >> 5;
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * kMergeWarps + w;
+    if (r >= n) return;
+    const int64_t j = j0 + r;
+    const int64_t pt = members[j];
+    if (pt < 0 || pt >= N) return;
+    const bool first = mem_row[2 * pt] == j;
+    if ((pass == 0) != first) return;
+    int32_t* on = out_n + pt * M;
+    float* od = out_d + pt * M;
+    // pass 0: merge with an empty running list (= the list itself); pass 1: with the running one
+    merge_warp(on, od, pass == 1, bl + r * M, bd + r * M, true, M, on, od, s_an[w], s_bn[w], s_ad[w], s_bd[w],
+               s_rank[w]);
 }
 
 // ---------------------------------------------------------------- sanitize
@@ -1240,6 +1278,18 @@ void merge_memberships(const int32_t* list_n, const float* list_d, const int64_t
     merge_kernel<<<blocks_for(N, kMergeWarps), kMergeWarps * 32, 0, st>>>(list_n, list_d, list_n, list_d, mem_row, N, M,
                                                                           out_n, out_d);
     count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void merge_membership_batch(const int32_t* bl, const float* bd, const int32_t* members, const int64_t* mem_row,
+                            int64_t j0, int64_t n, int64_t N, int M, int32_t* out_n, float* out_d, cudaStream_t st)
+{
+    GTA_REQUIRE(M >= 1 && M <= kMaxM, kInvalid, "merge: M must be in [1, 128]");
+    if (n <= 0) return;
+    for (int pass = 0; pass < 2; ++pass)
+        merge_batch_kernel<<<blocks_for(n, kMergeWarps), kMergeWarps * 32, 0, st>>>(bl, bd, members, mem_row, j0, n, N, M,
+                                                                                     pass, out_n, out_d);
+    count_launches(2);
     GTA_CUDA(cudaGetLastError());
 }
 

@@ -40,7 +40,7 @@ class gta_bucket_params(ctypes.Structure):
         ("n_buckets", _I32), ("kmeans_iters", _I32), ("knn_degree", _I32), ("rounds", _I32),
         ("kmeans_sample", _I64), ("seed", _U64),
         ("init_centroids", _P), ("init_on_device", _I32), ("out_on_device", _I32),
-        ("centroids_out", _P), ("top2_out", _P),
+        ("centroids_out", _P), ("top2_out", _P), ("device_budget", _I64),
     ]
 
 

@@ -75,8 +75,9 @@ def _dataset(X, metric: str = "l2") -> L.gta_dataset:
 
 
 def _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, init_centroids, dev, cent_out, top2_out,
-                   rounds=1):
+                   rounds=1, device_budget=0):
     return L.gta_bucket_params(
+        device_budget=device_budget,
         n_buckets=n_buckets, kmeans_iters=kmeans_iters, knn_degree=knn_degree, rounds=rounds,
         kmeans_sample=kmeans_sample, seed=seed, init_centroids=_ptr(init_centroids),
         init_on_device=1 if (init_centroids is not None and _is_dev(init_centroids)) else 0,
@@ -86,13 +87,14 @@ def _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, ini
 # ---------------------------------------------------------------- pipeline
 def build_bucket(X, n_buckets: int, knn_degree: int = 64, kmeans_iters: int = 10, kmeans_sample: int = 0,
                  seed: int = 42, init_centroids=None, metric: str = "l2", with_extras: bool = False,
-                 rounds: int = 1):
+                 rounds: int = 1, device_budget: int = 0):
     """Bucketed kNN graph of X (N x d, float32 / uint8 / int8; torch CUDA tensor or numpy).
 
     Returns (ids[N, M] int32, dists[N, M] float32) on X's side (device or host);
     with ``with_extras`` also the final centroids (B x d) and top-2 buckets (N x 2).
     ``rounds`` > 1 repeats the build with seeds seed+1, ... and merges each round's
-    lists into the running ones (bucket2 ``-t``).
+    lists into the running ones (bucket2 ``-t``).  ``device_budget`` (bytes, 0 = 80% of free
+    device memory) bounds the bucket kNN stage; buckets beyond it run in batches, same result.
     """
     dev = _is_dev(X)
     N, d = X.shape
@@ -102,7 +104,7 @@ def build_bucket(X, n_buckets: int, knn_degree: int = 64, kmeans_iters: int = 10
     top2 = _empty((N, 2), "int32", dev) if with_extras else None
     ds = _dataset(X, metric)
     p = _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, init_centroids, dev, cent, top2,
-                       rounds)
+                       rounds, device_budget)
     L.check(L.lib().gta_build_bucket(ctypes.byref(ds), ctypes.byref(p), _ptr(ids), _ptr(dists),
                                      _stream() if dev else ctypes.c_void_p(0)))
     if with_extras:
@@ -138,14 +140,15 @@ def build_bucket2(X, knn_degree: int = 64, nprobe: int = 0, centroid_ratio: floa
 
 
 def build_cagra(X, n_buckets: int, knn_degree: int = 64, graph_degree: int = 32, kmeans_iters: int = 10,
-                kmeans_sample: int = 0, seed: int = 42, init_centroids=None, metric: str = "l2", rounds: int = 1):
+                kmeans_sample: int = 0, seed: int = 42, init_centroids=None, metric: str = "l2", rounds: int = 1,
+                device_budget: int = 0):
     """Whole build: bucketed kNN (degree M), sanitize, CAGRA optimize -> graph[N, K] uint32."""
     dev = _is_dev(X)
     N = X.shape[0]
     graph = _empty((N, graph_degree), "uint32" if not dev else "int32", dev)
     ds = _dataset(X, metric)
     bp = _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, init_centroids, dev, None, None,
-                        rounds)
+                        rounds, device_budget)
     p = L.gta_cagra_params(bucket=bp, graph_degree=graph_degree, reserved0=0)
     L.check(L.lib().gta_build_cagra(ctypes.byref(ds), ctypes.byref(p), _ptr(graph),
                                     _stream() if dev else ctypes.c_void_p(0)))

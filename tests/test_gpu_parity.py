@@ -326,3 +326,18 @@ def test_prune_refuses_out_of_range_neighbours():
     with pytest.raises(gta.GtaError) as e:
         gta.prune(dev(g.view(np.int32)), 4)
     assert e.value.code == 5
+
+
+@pytest.mark.parametrize("cfg_name,n,budget", [("c2", 30000, 1 << 20), ("c2", 30000, 6 << 20), ("c1", 10000, 1 << 20)])
+def test_budgeted_bucket_batches_equal_one_pass(cfg_name, n, budget):
+    """A device budget far below the memberships' pool + lists runs the buckets in batches;
+    the lists and the final graph are the one-pass build's, bit for bit."""
+    cfg = gta.scaled(gta.CONFIGS[cfg_name], n)
+    X = dev(gta.generate(cfg, seed=5))
+    a_ids, a_d = gta.build_bucket(X, cfg.n_buckets, cfg.knn_degree, 3, 0, 9)
+    b_ids, b_d = gta.build_bucket(X, cfg.n_buckets, cfg.knn_degree, 3, 0, 9, device_budget=budget)
+    np.testing.assert_array_equal(host(b_ids), host(a_ids))
+    np.testing.assert_array_equal(host(b_d), host(a_d))
+    ga = gta.build_cagra(X, cfg.n_buckets, cfg.knn_degree, cfg.graph_degree, 3, 0, 9)
+    gb = gta.build_cagra(X, cfg.n_buckets, cfg.knn_degree, cfg.graph_degree, 3, 0, 9, device_budget=budget)
+    np.testing.assert_array_equal(host(gb), host(ga))
