@@ -213,6 +213,8 @@ def main():
     ap.add_argument("--n", type=int, default=0, help="override N (smaller case, e.g. for profiling)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="skip the graph-search and reference-bucketing measurements (large configs)")
     args = ap.parse_args()
 
     import gta
@@ -395,6 +397,7 @@ def main():
         gt = exact_knn(Xall, Xall[q], 32, exclude=q)
         approx = ids[q].cpu().numpy()[:, :32]
         recall = float(np.mean([len(np.intersect1d(approx[r], gt[r])) / 32.0 for r in range(1000)]))
+    if rank == 0 and not args.no_extras:
         # graph search over the final graph with the reference search's defaults
         # (topk 10, ef 200, 4 random entry points, seed 42) on held-out queries
         Q = torch.from_numpy(gta.generate_queries(cfg, SEARCH_QUERIES)).cuda()
@@ -423,7 +426,7 @@ def main():
     # the reference tool's own bucketing (KMeans||, balanced 1-way, own + nprobe pools) on the same
     # data: device time of one build and recall@32 of its lists on the same sampled points
     ref_bucketing = None
-    if world == 1 and rank == 0:
+    if world == 1 and rank == 0 and not args.no_extras:
         gta.build_bucket2(Xd, cfg.knn_degree, 32, 0.01, 42)  # warm-up
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()

@@ -271,7 +271,55 @@ void launch_exact(const T* X, int64_t n, int ldx, int d, const int32_t* row_ids,
 #undef GTA_ASSIGN_LAUNCH
 }
 
+// [x | x | 0] rows for the split screen (x: d of the ld-strided f32 rows)
+__global__ void dup_rows_kernel(const float* __restrict__ X, int d, int ld, int64_t n, float* __restrict__ out, int pitch)
+{
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (e >= n * pitch) return;
+    const int64_t r = e / pitch;
+    const int k = static_cast<int>(e - r * pitch);
+    out[e] = k < d ? X[r * ld + k] : (k < 2 * d ? X[r * ld + k - d] : 0.0f);
+}
+
+// [hi | lo | 0] centroid rows: hi = c with its low 13 mantissa bits cleared, lo the same of c - hi;
+// both are exact tf32 values (whatever the tensor core does with the bits below tf32), and
+// |c - hi - lo| <= 2^-20 |c|
+__device__ __forceinline__ float tf32_trunc(float v) { return __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); }
+
+__global__ void split_rows_kernel(const float* __restrict__ C, int d, int ld, int64_t n, float* __restrict__ out,
+                                  int pitch)
+{
+    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (e >= n * pitch) return;
+    const int64_t r = e / pitch;
+    const int k = static_cast<int>(e - r * pitch);
+    float v = 0.0f;
+    if (k < d) {
+        v = tf32_trunc(C[r * ld + k]);
+    } else if (k < 2 * d) {
+        const float c = C[r * ld + k - d];
+        v = tf32_trunc(c - tf32_trunc(c));
+    }
+    out[e] = v;
+}
+
 }  // namespace
+
+void dup_rows(const float* X, int d, int ld, int64_t n, float* out, int pitch, cudaStream_t st)
+{
+    const int64_t tot = n * pitch;
+    dup_rows_kernel<<<static_cast<unsigned>((tot + 255) / 256), 256, 0, st>>>(X, d, ld, n, out, pitch);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+void split_rows_tf32(const float* C, int d, int ld, int64_t n, float* out, int pitch, cudaStream_t st)
+{
+    const int64_t tot = n * pitch;
+    split_rows_kernel<<<static_cast<unsigned>((tot + 255) / 256), 256, 0, st>>>(C, d, ld, n, out, pitch);
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
 
 bool assign_exact_applies(int B, int k) { return B <= kAssignExactMaxB && k >= 1 && k <= 4; }
 

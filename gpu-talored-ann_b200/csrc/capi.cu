@@ -213,13 +213,29 @@ DevBuf<T> upload(const std::vector<T>& h, cudaStream_t st)
 // ---------------------------------------------------------------- stages
 
 // Top-k nearest rows of C (B x d_pad, norms cn) for rows of Xp (n x d_pad, norms xn).
+// int_rows: every value of the rows Xp is an integer exact in tf32 (8-bit data).  The tensor-core
+// screen then runs on split operands ([x | x] against [hi | lo] centroids, K = 2d) whose dot products
+// are within 2^-20 of exact, so far fewer candidates need the exact rerank.  X2 (optional): the
+// [x | x] rows already built (pitch pad_dim(2d)).
 void assign_topk_impl(const float* Xp, const float* xn, int64_t n, int d, int d_pad, const float* Cp, const float* cn,
-                      int B, int k, int32_t* ids, float* dists, int* err, cudaStream_t st)
+                      int B, int k, int32_t* ids, float* dists, int* err, cudaStream_t st, bool int_rows = false,
+                      const float* X2 = nullptr)
 {
     GTA_REQUIRE(k >= 1 && k <= B, kInvalid, "assign: need 1 <= k <= B");
     if (assign_exact_applies(B, k)) {  // few centroids: exact chain on the FP32 pipe, no screen
         assign_exact(Xp, GTA_F32, n, d_pad, d, nullptr, Cp, d_pad, B, k, ids, dists, st);
         return;
+    }
+    DevBuf<float> A2, C2;
+    const int pitch2 = pad_dim(2 * d, kElemF32);
+    if (int_rows) {
+        if (!X2) {
+            A2 = DevBuf<float>(static_cast<size_t>(n) * pitch2, st);
+            dup_rows(Xp, d, d_pad, n, A2.get(), pitch2, st);
+            X2 = A2.get();
+        }
+        C2 = DevBuf<float>(static_cast<size_t>(B) * pitch2, st);
+        split_rows_tf32(Cp, d, d_pad, B, C2.get(), pitch2, st);
     }
     std::vector<WorkItem> wl;
     wl.reserve(static_cast<size_t>((n + 127) / 128));
@@ -232,6 +248,12 @@ void assign_topk_impl(const float* Xp, const float* xn, int64_t n, int d, int d_
     pr.m_out = k; pr.exclude_self = false; pr.out_ids = ids; pr.out_dists = dists; pr.err = err;
     pr.prof_name = "dist_topk_assign";
     pr.flops = 2.0 * static_cast<double>(n) * B * d;
+    if (int_rows) {
+        pr.A = X2; pr.B = C2.get(); pr.d_pad = pitch2;
+        pr.b_exact = Cp; pr.b_exact_pitch = d_pad;
+        pr.screen_trunc = 0x1p-19;
+        pr.screen_k = 2 * d;
+    }
     dist_topk(pr, st);
 }
 
@@ -271,11 +293,17 @@ void kmeans_fit_impl(const float* Xs, const float* xn, int64_t n_s, int d, int d
     DevBuf<int32_t> ids(static_cast<size_t>(n_s), st);
     DevBuf<float> dd(static_cast<size_t>(n_s), st);
     DevBuf<float> C2(static_cast<size_t>(B) * d_pad, st);
+    DevBuf<float> X2;  // [x | x] rows of the split screen, built once for all steps
+    if (integer_rows && !assign_exact_applies(B, 1) && iters > 0) {
+        const int pitch2 = pad_dim(2 * d, kElemF32);
+        X2 = DevBuf<float>(static_cast<size_t>(n_s) * pitch2, st);
+        dup_rows(Xs, d, d_pad, n_s, X2.get(), pitch2, st);
+    }
     for (int it = 0; it < iters; ++it) {
         if (raw.X && assign_exact_applies(B, 1))
             assign_exact(raw.X, raw.dtype, n_s, raw.ldx, d, raw.row_ids, C, d_pad, B, 1, ids.get(), dd.get(), st);
         else
-            assign_topk_impl(Xs, xn, n_s, d, d_pad, C, cn, B, 1, ids.get(), dd.get(), err, st);
+            assign_topk_impl(Xs, xn, n_s, d, d_pad, C, cn, B, 1, ids.get(), dd.get(), err, st, integer_rows, X2.get());
         centroid_update(Xs, n_s, d, d_pad, ids.get(), C, B, C2.get(), cn, err, st, integer_rows);
         GTA_CUDA(cudaMemcpyAsync(C, C2.get(), sizeof(float) * static_cast<size_t>(B) * d_pad, cudaMemcpyDeviceToDevice, st));
     }
@@ -364,7 +392,7 @@ struct BucketOut {
     int32_t* top2;     // device [N x 2] or null
 };
 
-constexpr size_t kTop2ChunkBytes = size_t(8) << 30;  // f32 rows converted at once for the top-2 pass
+constexpr size_t kTop2ChunkBytes = size_t(4) << 30;  // f32 rows converted at once for the top-2 pass
 
 void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const BucketOut& o, cudaStream_t st)
 {
@@ -448,7 +476,7 @@ void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const
                     convert_rows(Xr, ds.dtype, d, nullptr, nr, Xf.get(), kElemF32, d32, xn.get(), st);
                 }
                 assign_topk_impl(Xf.get(), xn.get(), nr, d, d32, C.get(), cn.get(), B, 2, top2.get() + 2 * r0,
-                                 t2d.get() + 2 * r0, err.get(), st);
+                                 t2d.get() + 2 * r0, err.get(), st, ds.dtype != GTA_F32);
             }
         }
     }

@@ -919,9 +919,10 @@ __global__ void __launch_bounds__(kThreads, kV)
 struct RerankArgs {
     const WorkItem* work;
     const void* A;
-    const void* B;
+    const void* B;       // rows read for the exact distances (pitch b_pitch)
     int elem;
-    int d, d_pad;
+    int d, d_pad;        // d_pad: the pitch of A
+    int b_pitch;
     const int32_t* b_gid;
     const int32_t* cand_cols;
     const int32_t* cand_n;
@@ -984,7 +985,7 @@ __global__ void __launch_bounds__(128) rerank_kernel(const RerankArgs p)
                 if (j < n) {
                     const int c = p.cand_cols[arow * p.L + j];
                     const int64_t brow = static_cast<int64_t>(w.b_row0) + c;
-                    const float dd = exact_dist_row(arow_s, B + brow * p.d_pad, p.d);
+                    const float dd = exact_dist_row(arow_s, B + brow * p.b_pitch, p.d);
                     const uint32_t id = p.b_gid ? static_cast<uint32_t>(p.b_gid[brow]) : static_cast<uint32_t>(c);
                     key = (static_cast<uint64_t>(f2key(dd)) << 32) | id;
                 }
@@ -1008,7 +1009,7 @@ __global__ void __launch_bounds__(128) rerank_kernel(const RerankArgs p)
                     uint64_t key = ~0ull;
                     if (c < w.b_rows && c != self) {
                         const int64_t brow = static_cast<int64_t>(w.b_row0) + c;
-                        const float dd = exact_dist_row(arow_s, B + brow * p.d_pad, p.d);
+                        const float dd = exact_dist_row(arow_s, B + brow * p.b_pitch, p.d);
                         const uint32_t id = p.b_gid ? static_cast<uint32_t>(p.b_gid[brow]) : static_cast<uint32_t>(c);
                         key = (static_cast<uint64_t>(f2key(dd)) << 32) | id;
                     }
@@ -1184,7 +1185,8 @@ void dist_topk(const DistTopkProblem& pr, cudaStream_t st)
     // tf32 screen error bound (operand truncation 2^-10 each, fp32 accumulation with 2 ulp per add,
     // fp32 norms and the fused multiply-add), with a 1.25 safety factor.
     const double d = pr.d;
-    a.mc1 = static_cast<float>(1.25 * 4.0 * (std::ldexp(1.0, -9) + d * std::ldexp(1.0, -22)));
+    const double kacc = pr.screen_k > 0 ? pr.screen_k : pr.d;
+    a.mc1 = static_cast<float>(1.25 * 4.0 * (pr.screen_trunc + kacc * std::ldexp(1.0, -22)));
     a.mc2 = static_cast<float>(1.25 * 3.0 * (d + 2.0) * std::ldexp(1.0, -24));
     a.out_ids = pr.out_ids; a.out_dists = pr.out_dists;
     a.cand_cols = cand_cols.get(); a.cand_n = cand_n.get();
@@ -1201,7 +1203,9 @@ void dist_topk(const DistTopkProblem& pr, cudaStream_t st)
 
     if (screen) {
         RerankArgs r{};
-        r.work = pr.work; r.A = pr.A; r.B = pr.B; r.elem = pr.elem; r.d = pr.d; r.d_pad = pr.d_pad;
+        r.work = pr.work; r.A = pr.A; r.elem = pr.elem; r.d = pr.d; r.d_pad = pr.d_pad;
+        r.B = pr.b_exact ? pr.b_exact : pr.B;
+        r.b_pitch = pr.b_exact ? pr.b_exact_pitch : pr.d_pad;
         r.b_gid = pr.b_gid; r.cand_cols = cand_cols.get(); r.cand_n = cand_n.get(); r.L = pl.L; r.m_out = pr.m_out;
         r.out_ids = pr.out_ids; r.out_dists = pr.out_dists;
         const size_t smem = 4 * kSortMax * sizeof(uint64_t) + 4 * static_cast<size_t>(pr.d_pad) * sizeof(float);

@@ -113,6 +113,14 @@ struct DistTopkProblem {
     int* err = nullptr;            // device error word
     const char* prof_name = "dist_topk";
     double flops = 0.0;            // algorithmic flops of the launch (sum of 2*rows*cols*d)
+    // screen error model (tf32): relative operand-truncation error of the dot products and the
+    // number of products accumulated; split operands (integer rows [x | x] against centroid rows
+    // [hi | lo], both parts exact in tf32) cut the truncation term from 2^-9 to 2^-19
+    double screen_trunc = 0x1p-9;
+    int screen_k = 0;              // 0: d
+    // rows the exact rerank reads for B (default B / d_pad): the unsplit centroids
+    const void* b_exact = nullptr;
+    int b_exact_pitch = 0;
 };
 
 void dist_topk(const DistTopkProblem& pr, cudaStream_t st);
@@ -188,6 +196,10 @@ void pool_fill(const int32_t* members, const int64_t* offsets, const int32_t* se
 void one_way_rows(const int32_t* members, int64_t n, int64_t* mem_row, cudaStream_t st);
 // order = 0..n-1 sorted stably by key (keys in [0, B), else err), offsets[b] = first index of key b
 void group_by_key(const int32_t* keys, int64_t n, int32_t B, int32_t* order, int64_t* offsets, int* err, cudaStream_t st);
+// split operands for the tf32 screen of integer-valued rows against f32 centroids (assign.cu):
+// rows [x | x | 0] and centroid rows [hi | lo | 0] of pitch `pitch` (>= 2d, 32-float multiple)
+void dup_rows(const float* X, int d, int ld, int64_t n, float* out, int pitch, cudaStream_t st);
+void split_rows_tf32(const float* C, int d, int ld, int64_t n, float* out, int pitch, cudaStream_t st);
 // bucket-contiguous renumbering (reorder.cu)
 void bucket_reorder(const int32_t* assign, int64_t n, int32_t stride, int32_t B, const int32_t* order,
                     uint32_t* inverse_perm, int64_t* offsets, int* err, cudaStream_t st);

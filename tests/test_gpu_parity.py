@@ -341,3 +341,26 @@ def test_budgeted_bucket_batches_equal_one_pass(cfg_name, n, budget):
     ga = gta.build_cagra(X, cfg.n_buckets, cfg.knn_degree, cfg.graph_degree, 3, 0, 9)
     gb = gta.build_cagra(X, cfg.n_buckets, cfg.knn_degree, cfg.graph_degree, 3, 0, 9, device_budget=budget)
     np.testing.assert_array_equal(host(gb), host(ga))
+
+
+def test_build_bucket_many_buckets_u8_split_screen():
+    """More than 384 buckets on 8-bit data: the Lloyd steps and the top-2 pass run the tensor-core
+    screen on split operands ([x | x] against [hi | lo] centroids) with the exact rerank; centroids,
+    top-2 and lists must equal the oracle's."""
+    cfg = gta.scaled(gta.CONFIGS["c2"], 60000, n_buckets=500)
+    X = gta.generate(cfg, seed=8)
+    Xf = X.astype(np.float32)
+    n_s = 20000
+    sid = _sample_rows(60000, n_s, 42)
+    C0 = Xf[sid[:500]].copy()
+    ids, dists, cent, top2 = gta.build_bucket(dev(X), 500, 32, 3, n_s, 42, init_centroids=dev(C0), with_extras=True)
+    ids, dists, cent, top2 = host(ids), host(dists), host(cent), host(top2)
+    rC, _ = orc.kmeans(Xf[sid], C0, 3)
+    np.testing.assert_array_equal(cent, rC)
+    rt2, _ = orc.topk_assign(Xf, cent, 2)
+    np.testing.assert_array_equal(top2, rt2)
+    offs, mem, mrow = orc.build_csr(top2, 500)
+    li, ld = orc.bucket_knn(Xf, offs, mem, 32)
+    ki, kd = orc.merge_memberships(li, ld, mrow)
+    np.testing.assert_array_equal(ids, ki)
+    np.testing.assert_array_equal(dists, kd)
