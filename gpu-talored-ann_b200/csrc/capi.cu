@@ -1465,9 +1465,16 @@ int gta_kmeans_init(const float* X, int64_t pool_n, int32_t d, int32_t B, uint64
 int gta_assign_topk(const float* X, int64_t n, int32_t d, const float* C, int32_t B, int32_t k, int32_t* ids,
                     float* dists, void* stream)
 {
+    return gta_assign_topk_ex(X, n, d, C, B, k, ids, dists, 0, stream);
+}
+
+int gta_assign_topk_ex(const float* X, int64_t n, int32_t d, const float* C, int32_t B, int32_t k, int32_t* ids,
+                       float* dists, int32_t flags, void* stream)
+{
     return guard([&] {
         GTA_WORKSPACE(stream);
-        GTA_REQUIRE(X && C && ids && dists && n >= 1 && d >= 1 && B >= 1, kInvalid, "gta_assign_topk: bad argument");
+        GTA_REQUIRE(X && C && ids && dists && n >= 1 && d >= 1 && B >= 1 && (flags & ~GTA_ROWS_INTEGER) == 0, kInvalid,
+                    "gta_assign_topk: bad argument");
         cudaStream_t st = S(stream);
         const int d32 = pad_dim(d, kElemF32);
         DevBuf<int> err(1, st);
@@ -1476,7 +1483,8 @@ int gta_assign_topk(const float* X, int64_t n, int32_t d, const float* C, int32_
         DevBuf<float> Cp(static_cast<size_t>(B) * d32, st), cn(static_cast<size_t>(B), st);
         convert_rows(X, GTA_F32, d, nullptr, n, Xp.get(), kElemF32, d32, xn.get(), st);
         convert_rows(C, GTA_F32, d, nullptr, B, Cp.get(), kElemF32, d32, cn.get(), st);
-        assign_topk_impl(Xp.get(), xn.get(), n, d, d32, Cp.get(), cn.get(), B, k, ids, dists, err.get(), st);
+        assign_topk_impl(Xp.get(), xn.get(), n, d, d32, Cp.get(), cn.get(), B, k, ids, dists, err.get(), st,
+                         (flags & GTA_ROWS_INTEGER) != 0);
         check_device_error(err.get(), st, "gta_assign_topk");
     });
 }

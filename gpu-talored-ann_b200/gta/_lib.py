@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(PKG_DIR, "lib", "libgta.so")
 CSRC = os.path.join(PKG_DIR, "csrc")
 
 GTA_OK, GTA_EINVAL, GTA_ENOMEM, GTA_ECUDA, GTA_ENCCL, GTA_EDATA = range(6)
+GTA_ROWS_INTEGER = 1
 GTA_F32, GTA_U8, GTA_I8 = 0, 1, 2
 GTA_L2, GTA_IP = 0, 1
 
@@ -66,6 +67,7 @@ _SIGS = {
     "gta_kmeans_fit": [_P, _I64, _I32, _P, _I32, _I32, _P, _P],
     "gta_kmeans_init": [_P, _I64, _I32, _I32, _U64, _P, _P],
     "gta_assign_topk": [_P, _I64, _I32, _P, _I32, _I32, _P, _P, _P],
+    "gta_assign_topk_ex": [_P, _I64, _I32, _P, _I32, _I32, _P, _P, _I32, _P],
     "gta_build_memberships": [_P, _I64, _I32, _P, _P, _P, _P],
     "gta_bucket_knn": [_P, _I32, _I64, _I32, _P, _P, _I32, _I32, _P, _P, _P],
     "gta_merge_memberships": [_P, _P, _P, _I64, _I32, _P, _P, _P],

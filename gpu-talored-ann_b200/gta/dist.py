@@ -117,12 +117,13 @@ class CudaStages:
         L.check(self.L.gta_kmeans_init(_p(pool), pool.shape[0], pool.shape[1], B, seed, _p(C), self._st()))
         return C
 
-    def assign_topk(self, Xf, C, k):
+    def assign_topk(self, Xf, C, k, integer_rows=False):
         n = Xf.shape[0]
         ids = torch.empty((n, k), dtype=torch.int32, device=Xf.device)
         dd = torch.empty((n, k), dtype=torch.float32, device=Xf.device)
         if n:
-            L.check(self.L.gta_assign_topk(_p(Xf), n, Xf.shape[1], _p(C), C.shape[0], k, _p(ids), _p(dd), self._st()))
+            L.check(self.L.gta_assign_topk_ex(_p(Xf), n, Xf.shape[1], _p(C), C.shape[0], k, _p(ids), _p(dd),
+                                              L.GTA_ROWS_INTEGER if integer_rows else 0, self._st()))
         return ids
 
     def centroid_sums(self, Xf, assign, B):
@@ -253,6 +254,7 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     n_local, d = X_local.shape
+    int_rows = X_local.dtype in (torch.uint8, torch.int8)  # exact in tf32: the split assignment screen
     B, M = prm.n_buckets, prm.knn_degree
     sent = 0
 
@@ -283,7 +285,7 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
     mine = sid[(sid >= row0) & (sid < row0 + n_local)].contiguous()
     Xs = st.gather_rows(X_local, row0, mine)
     for _ in range(prm.kmeans_iters):
-        a = st.assign_topk(Xs, C, 1).reshape(-1).contiguous()
+        a = st.assign_topk(Xs, C, 1, int_rows).reshape(-1).contiguous()
         sums, cts = st.centroid_sums(Xs, a, B)
         dist.all_reduce(sums, group=group)
         dist.all_reduce(cts, group=group)
@@ -294,7 +296,7 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
     # ---- 2. top-2 buckets of the local rows
     gid_local = torch.arange(row0, row0 + n_local, dtype=torch.int32, device=dev)
     Xf = st.gather_rows(X_local, row0, gid_local)
-    top2 = st.assign_topk(Xf, C, 2).contiguous()
+    top2 = st.assign_topk(Xf, C, 2, int_rows).contiguous()
     del Xf
     if n_local and not bool(((top2 >= 0) & (top2 < B)).all()):
         raise L.GtaError(L.GTA_EDATA, "build_sharded: a row has no valid bucket (non-finite input?)")

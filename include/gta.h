@@ -172,6 +172,14 @@ int gta_kmeans_init(const float* X, int64_t pool_n, int32_t d, int32_t B, uint64
 int gta_assign_topk(const float* X, int64_t n, int32_t d, const float* C, int32_t B, int32_t k, int32_t* ids,
                     float* dists, void* stream);
 
+/* The same with flags.  GTA_ROWS_INTEGER: every value of X is an integer of magnitude
+ * below 2048 (8-bit data), which lets the tensor-core screen split the centroids into two
+ * tf32-exact parts (error 2^-20 instead of 2^-9, far fewer exact reranks); a caller that sets
+ * it for other rows gets undefined lists. */
+#define GTA_ROWS_INTEGER 1
+int gta_assign_topk_ex(const float* X, int64_t n, int32_t d, const float* C, int32_t B, int32_t k, int32_t* ids,
+                       float* dists, int32_t flags, void* stream);
+
 /* Bucket membership CSR from top-2 ids (n x 2): members[2n] point ids sorted
  * by (bucket, point), offsets[B+1], mem_row[n x 2] (membership row of each
  * point in its lower / higher bucket).

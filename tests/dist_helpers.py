@@ -51,7 +51,7 @@ class OracleStages:
     def kmeans_init(self, pool, B, seed):
         raise NotImplementedError("the oracle has no k-means++: pass init_centroids")
 
-    def assign_topk(self, Xf, C, k):
+    def assign_topk(self, Xf, C, k, integer_rows=False):  # the oracle is exact whatever the rows
         if Xf.shape[0] == 0:
             return torch.empty((0, k), dtype=torch.int32)
         return _t(orc.topk_assign(_np(Xf), _np(C), k)[0], torch.int32)

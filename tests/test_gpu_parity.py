@@ -364,3 +364,20 @@ def test_build_bucket_many_buckets_u8_split_screen():
     ki, kd = orc.merge_memberships(li, ld, mrow)
     np.testing.assert_array_equal(ids, ki)
     np.testing.assert_array_equal(dists, kd)
+
+
+@pytest.mark.parametrize("B,k", [(600, 1), (1000, 2)])
+def test_assign_topk_integer_rows_split_screen(B, k):
+    """gta_assign_topk_ex with GTA_ROWS_INTEGER (8-bit rows as f32) equals the exact oracle."""
+    rng = np.random.default_rng(B)
+    X = rng.integers(0, 256, (20000, 96)).astype(np.float32)
+    C = (rng.integers(0, 256, (B, 96)) + rng.random((B, 96))).astype(np.float32)
+    ids = torch.empty((20000, k), dtype=torch.int32, device="cuda")
+    dd = torch.empty((20000, k), dtype=torch.float32, device="cuda")
+    from gta import _lib as L
+    Xd, Cd = dev(X), dev(C)
+    L.check(L.lib().gta_assign_topk_ex(Xd.data_ptr(), 20000, 96, Cd.data_ptr(), B, k, ids.data_ptr(), dd.data_ptr(),
+                                       L.GTA_ROWS_INTEGER, torch.cuda.current_stream().cuda_stream))
+    ri, rd = orc.topk_assign(X, C, k)
+    np.testing.assert_array_equal(host(ids), ri)
+    np.testing.assert_array_equal(host(dd), rd)
