@@ -11,6 +11,7 @@
 #include <cstdio>
 #include <cstring>
 #include <fstream>
+#include <map>
 #include <numeric>
 #include <string>
 #include <vector>
@@ -393,6 +394,8 @@ struct BucketOut {
 };
 
 constexpr size_t kTop2ChunkBytes = size_t(4) << 30;  // f32 rows converted at once for the top-2 pass
+std::mutex g_devmem_mu;
+std::map<int, size_t> g_devmem_total;  // total memory of each device, queried once
 
 void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const BucketOut& o, cudaStream_t st)
 {
@@ -493,9 +496,28 @@ void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const
     const int64_t n_mem = 2 * N;
     const int elem = exact_bf16(ds.dtype, d) ? kElemBF16 : kElemF32;
     const double per_row = static_cast<double>(pad_dim(d, elem)) * (elem == kElemBF16 ? 2 : 4) + 8.0 * M + 8.0;
-    size_t free_b = 0, total_b = 0;
-    GTA_CUDA(cudaMemGetInfo(&free_b, &total_b));
-    const double budget = p.device_budget > 0 ? static_cast<double>(p.device_budget) : 0.8 * static_cast<double>(free_b);
+    double budget = static_cast<double>(p.device_budget);
+    if (budget <= 0.0) {  // the free memory is queried only for stages that may not fit
+        int dev = 0;
+        GTA_CUDA(cudaGetDevice(&dev));
+        size_t total_b = 0;
+        {
+            std::lock_guard<std::mutex> g(g_devmem_mu);
+            auto it = g_devmem_total.find(dev);
+            if (it == g_devmem_total.end()) {
+                cudaDeviceProp prop{};
+                GTA_CUDA(cudaGetDeviceProperties(&prop, dev));
+                it = g_devmem_total.emplace(dev, prop.totalGlobalMem).first;
+            }
+            total_b = it->second;
+        }
+        budget = 0.25 * static_cast<double>(total_b);
+        if (static_cast<double>(n_mem) * per_row > budget) {
+            size_t free_b = 0, tot = 0;
+            GTA_CUDA(cudaMemGetInfo(&free_b, &tot));
+            budget = 0.8 * static_cast<double>(free_b);
+        }
+    }
     if (static_cast<double>(n_mem) * per_row <= budget) {
         DevBuf<int32_t> lid(static_cast<size_t>(n_mem) * M, st);
         DevBuf<float> ldist(static_cast<size_t>(n_mem) * M, st);
