@@ -620,10 +620,14 @@ constexpr int kMaxM = 128;
 
 // One warp merges the running list a (na valid entries used) with the new list b: b's entries
 // whose id is already in a are dropped, the rest merged by distance with a's entries first on
-// equal distance; out may alias a (both lists are staged in shared memory first).
+// equal distance; out may alias a (both lists are staged in shared memory first).  Both lists are
+// ascending, so every output position is a binary search in the other list; a's ids sit in a
+// small open-addressing table for the duplicate test.
+constexpr int kMergeHash = 512;  // >= 4 * kMaxM slots
+
 __device__ __forceinline__ void merge_warp(const int32_t* an, const float* ad, bool va, const int32_t* bn,
                                            const float* bd, bool vb, int M, int32_t* on, float* od, int32_t* s_an,
-                                           int32_t* s_bn, float* s_ad, float* s_bd, int* s_rank)
+                                           int32_t* s_bn, float* s_ad, float* s_bd, int* s_pref, uint32_t* s_hash)
 {
     const int lane = threadIdx.x & 31;
     int na = va ? M : 0, nb = vb ? M : 0;
@@ -633,40 +637,69 @@ __device__ __forceinline__ void merge_warp(const int32_t* an, const float* ad, b
         if (x < 0) na = min(na, k);
         if (y < 0) nb = min(nb, k);
     }
+    for (int h = lane; h < kMergeHash; h += 32) s_hash[h] = kEmpty;
     for (int off = 16; off > 0; off >>= 1) {
         na = min(na, __shfl_xor_sync(0xffffffffu, na, off));
         nb = min(nb, __shfl_xor_sync(0xffffffffu, nb, off));
     }
     __syncwarp();
+    constexpr uint32_t hmask = kMergeHash - 1;
+    for (int k = lane; k < na; k += 32) {  // a's ids (>= 0) into the table
+        const uint32_t id = static_cast<uint32_t>(s_an[k]);
+        for (uint32_t h = (id * 2654435761u) >> 7 & hmask;; h = (h + 1) & hmask) {
+            const uint32_t old = atomicCAS(&s_hash[h], kEmpty, id);
+            if (old == kEmpty || old == id) break;
+        }
+    }
+    __syncwarp();
+    // kept new entries: s_pref[j] = number kept among b[0 .. j)
     int base = 0;
     for (int g = 0; g < (M + 31) / 32; ++g) {
         const int j = g * 32 + lane;
         bool keep = false;
         if (j < nb) {
-            const int32_t id = s_bn[j];
+            const uint32_t id = static_cast<uint32_t>(s_bn[j]);
             keep = true;
-            for (int k = 0; k < na; ++k) keep &= (s_an[k] != id);
+            for (uint32_t h = (id * 2654435761u) >> 7 & hmask;; h = (h + 1) & hmask) {
+                const uint32_t key = s_hash[h];
+                if (key == kEmpty) break;
+                if (key == id) { keep = false; break; }
+            }
         }
         const unsigned m = __ballot_sync(0xffffffffu, keep);
-        if (j < M) s_rank[j] = keep ? base + __popc(m & ((1u << lane) - 1u)) : -1;
+        const int before = base + __popc(m & ((1u << lane) - 1u));
+        if (j < M) s_pref[j] = keep ? before : -1 - before;  // a dropped entry stores -(kept before it) - 1
         base += __popc(m);
     }
     __syncwarp();
     const int n_keep = base;
+    auto kept_before = [&](int p) {  // number of kept new entries among b[0 .. p)
+        if (p >= nb) return n_keep;
+        const int v = s_pref[p];
+        return v >= 0 ? v : -1 - v;
+    };
     for (int i = lane; i < na; i += 32) {
         const float x = s_ad[i];
-        int c = 0;
-        for (int j = 0; j < nb; ++j) c += (s_rank[j] >= 0 && s_bd[j] < x);
-        const int pos = i + c;
+        int lo = 0, hi = nb;  // first b entry with distance >= x
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (s_bd[mid] < x) lo = mid + 1;
+            else hi = mid;
+        }
+        const int pos = i + kept_before(lo);
         if (pos < M) { on[pos] = s_an[i]; od[pos] = x; }
     }
     for (int j = lane; j < nb; j += 32) {
-        const int k = s_rank[j];
+        const int k = s_pref[j];
         if (k < 0) continue;
         const float x = s_bd[j];
-        int c = 0;
-        for (int i = 0; i < na; ++i) c += (s_ad[i] <= x);
-        const int pos = k + c;
+        int lo = 0, hi = na;  // first a entry with distance > x
+        while (lo < hi) {
+            const int mid = (lo + hi) >> 1;
+            if (s_ad[mid] <= x) lo = mid + 1;
+            else hi = mid;
+        }
+        const int pos = k + lo;
         if (pos < M) { on[pos] = s_bn[j]; od[pos] = x; }
     }
     for (int q = na + n_keep + lane; q < M; q += 32) { on[q] = -1; od[q] = INFINITY; }
@@ -682,6 +715,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
     __shared__ int32_t s_an[kMergeWarps][kMaxM], s_bn[kMergeWarps][kMaxM];
     __shared__ float s_ad[kMergeWarps][kMaxM], s_bd[kMergeWarps][kMaxM];
     __shared__ int s_rank[kMergeWarps][kMaxM];
+    __shared__ uint32_t s_hash[kMergeWarps][kMergeHash];
     const int w = threadIdx.x >> 5;
     const int64_t p = static_cast<int64_t>(blockIdx.x) * kMergeWarps + w;
     if (p >= N) return;
@@ -690,7 +724,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
     const bool va = !mem_row || (ra >= 0 && ra < 2 * N), vb = !mem_row || (rb >= 0 && rb < 2 * N);
     merge_warp(run_n + (va ? ra : 0) * M, run_d + (va ? ra : 0) * M, va, new_n + (vb ? rb : 0) * M,
                new_d + (vb ? rb : 0) * M, vb, M, out_n + p * M, out_d + p * M, s_an[w], s_bn[w], s_ad[w], s_bd[w],
-               s_rank[w]);
+               s_rank[w], s_hash[w]);
 }
 
 // A batch of membership rows j0 .. j0 + n - 1 (lists at row j - j0 of bl / bd) into the per-point
@@ -705,6 +739,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
     __shared__ int32_t s_an[kMergeWarps][kMaxM], s_bn[kMergeWarps][kMaxM];
     __shared__ float s_ad[kMergeWarps][kMaxM], s_bd[kMergeWarps][kMaxM];
     __shared__ int s_rank[kMergeWarps][kMaxM];
+    __shared__ uint32_t s_hash[kMergeWarps][kMergeHash];
     const int w = threadIdx.x >> 5;
     const int64_t r = static_cast<int64_t>(blockIdx.x) * kMergeWarps + w;
     if (r >= n) return;
@@ -717,7 +752,7 @@ __global__ void __launch_bounds__(kMergeWarps * 32)
     float* od = out_d + pt * M;
     // pass 0: merge with an empty running list (= the list itself); pass 1: with the running one
     merge_warp(on, od, pass == 1, bl + r * M, bd + r * M, true, M, on, od, s_an[w], s_bn[w], s_ad[w], s_bd[w],
-               s_rank[w]);
+               s_rank[w], s_hash[w]);
 }
 
 // ---------------------------------------------------------------- sanitize
