@@ -79,31 +79,6 @@ __device__ __forceinline__ void load_dims<int8_t>(const int8_t* __restrict__ row
     load_dims_8bit(row, k0, d, vec, x);
 }
 
-// Two fp32 lanes per instruction (sm_100 packed f32x2: each lane rounds exactly like the
-// scalar instruction, so the chain is unchanged).
-__device__ __forceinline__ unsigned long long f2_pack(float lo, float hi)
-{
-    unsigned long long r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-    return r;
-}
-__device__ __forceinline__ void f2_unpack(unsigned long long v, float& lo, float& hi)
-{
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
-}
-__device__ __forceinline__ unsigned long long f2_sub(unsigned long long a, unsigned long long b)
-{
-    unsigned long long r;
-    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-__device__ __forceinline__ unsigned long long f2_fma(unsigned long long a, unsigned long long b, unsigned long long c)
-{
-    unsigned long long r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
-
 template <int K>
 __device__ __forceinline__ void keep_k(float (&bd)[K], int32_t (&bi)[K], float cv, int32_t ci)
 {

@@ -804,52 +804,70 @@ __global__ void __launch_bounds__(kThreads, kV)
             // slices of 16 columns in two register sets: slice c + 1 loads into the other set
             // while c is scanned (no register copies; the slice loop is unrolled)
             uint32_t va[16], vb[16];
+            // One slice of 16 columns: scores s = |y|^2 - 2 x.y by packed f32x2 fma, the pass test
+            // s <= thr as the sign of thr - s (an IEEE difference is +0 exactly when the two are
+            // equal and never takes the wrong sign; thr is never -0), one funnel shift per score
+            // to collect the signs: bit 15 - e of `fail` is set where score e lies above thr.
             auto scan_slice = [&](int c, const uint32_t (&v)[16], uint32_t (&nxt)[16], bool nxt_in_flight) {
                 const int self_e = (ct == self_ct && c == self_c) ? (lane & 15) : -1;
                 const uint32_t c0 = static_cast<uint32_t>(ct * kTN + c * 16);
-                const float4* pn4 = reinterpret_cast<const float4*>(pnw + c * 16);
-                float sv[16];
-                uint32_t mask = 0;
+                const ulonglong2* pn2 = reinterpret_cast<const ulonglong2*>(pnw + c * 16);
+                const unsigned long long thr2 = f2_pack(thr, thr), m2 = f2_pack(-2.0f, -2.0f);
+                unsigned long long s2[8];
+                uint32_t fail = 0;
 #pragma unroll
                 for (int e4 = 0; e4 < 4; ++e4) {
-                    const float4 n4 = pn4[e4];
-                    const float nv[4] = {n4.x, n4.y, n4.z, n4.w};
+                    const ulonglong2 n4 = pn2[e4];  // column norms 4 e4 .. 4 e4 + 3, two packed pairs
+                    s2[2 * e4] = f2_fma(m2, f2_pack(__uint_as_float(v[4 * e4]), __uint_as_float(v[4 * e4 + 1])), n4.x);
+                    s2[2 * e4 + 1] =
+                        f2_fma(m2, f2_pack(__uint_as_float(v[4 * e4 + 2]), __uint_as_float(v[4 * e4 + 3])), n4.y);
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int e = e4 * 4 + u;
-                        sv[e] = fmaf(-2.0f, __uint_as_float(v[e]), nv[u]);
-                        mask |= (sv[e] <= thr) ? (1u << e) : 0u;
+                    for (int j = 0; j < 2; ++j) {
+                        const unsigned long long dd = f2_sub(thr2, s2[2 * e4 + j]);
+                        fail = __funnelshift_l(static_cast<uint32_t>(dd), fail, 1);
+                        fail = __funnelshift_l(static_cast<uint32_t>(dd >> 32), fail, 1);
                     }
                 }
-                if (self_e >= 0) mask &= ~(1u << self_e);
-                const int npass = __popc(mask);
-                const int rounds = __reduce_max_sync(0xffffffffu, static_cast<unsigned>(npass));
-                if (rounds > 0) {
-                    // scores to this lane's scratch, then one append per pass
+                uint32_t m = ~fail & 0xffffu;  // passes: bit 15 - e for score e
+                if (self_e >= 0) m &= ~(1u << (15 - self_e));
+                if (__any_sync(0xffffffffu, m != 0u)) {
+                    // scores to this lane's scratch, read back by the appends
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) scr[e * 32] = sv[e];
-                    uint32_t m = mask;
-                    for (int i = nb; m != 0u; ++i) {  // this lane's passes, in column order
-                        const int e = __ffs(m) - 1;
+                    for (int e2 = 0; e2 < 8; ++e2) {
+                        float lo, hi;
+                        f2_unpack(s2[e2], lo, hi);
+                        scr[(2 * e2) * 32] = lo;
+                        scr[(2 * e2 + 1) * 32] = hi;
+                    }
+                    int npass = __popc(m);
+                    // flush only when a lane's buffer cannot take this slice's passes
+                    if (__any_sync(0xffffffffu, nb + npass > kBuf)) {
+                        if (nxt_in_flight) tmem_ld_wait_regs(nxt);  // no TMEM load in flight across the call
+                        const long long f0 = st_on ? clock64() : 0;
+                        n_pass += nb;
+                        ++n_flush;
+                        const ListTail lt = flush_tmem<kL, kTF32>(tl, my_buf, nb, p.m_sel);
+                        nb = 0;
+                        if (row_ok) {
+                            thr = (lt.last == kEmptyKey) ? FLT_MAX : key_dist(lt.last);
+                            if (kTF32 && lt.msel != kEmptyKey) thr = fminf(thr, key_dist(lt.msel) + margin);
+                            thr += 0.0f;  // -0 -> +0 for the sign test
+                        }
+                        // this slice's passes against the new threshold
+                        m = 0u;
+#pragma unroll
+                        for (int e = 0; e < 16; ++e) m |= (scr[e * 32] <= thr) ? (1u << (15 - e)) : 0u;
+                        if (self_e >= 0) m &= ~(1u << (15 - self_e));
+                        npass = __popc(m);
+                        if (st_on) cyc_flush += clock64() - f0;
+                    }
+                    for (int i = nb; m != 0u; ++i) {  // this lane's passes
+                        const int e = 15 - (__ffs(m) - 1);
                         const uint32_t id = kTF32 ? c0 + static_cast<uint32_t>(e) : idw[c * 16 + e];
                         my_buf[i * 128] = (static_cast<uint64_t>(f2key(scr[e * 32])) << 32) | id;
                         m &= m - 1u;
                     }
-                    __syncwarp();
                     nb += npass;
-                }
-                if (__any_sync(0xffffffffu, nb > kBuf - 16)) {
-                    if (nxt_in_flight) tmem_ld_wait_regs(nxt);  // no TMEM load in flight across the call
-                    const long long f0 = st_on ? clock64() : 0;
-                    n_pass += nb;
-                    ++n_flush;
-                    const ListTail lt = flush_tmem<kL, kTF32>(tl, my_buf, nb, p.m_sel);
-                    nb = 0;
-                    if (row_ok) {
-                        thr = (lt.last == kEmptyKey) ? FLT_MAX : key_dist(lt.last);
-                        if (kTF32 && lt.msel != kEmptyKey) thr = fminf(thr, key_dist(lt.msel) + margin);
-                    }
-                    if (st_on) cyc_flush += clock64() - f0;
                 }
                 __syncwarp();
             };
