@@ -332,13 +332,32 @@ int64_t kmeans_pool_size(int64_t n_s, int B)
 
 uint64_t kmeans_pool_seed(uint64_t seed) { return seed ^ 0x9E3779B97F4A7C15ull; }
 
+// Which membership rows a bucket kNN call computes.  Within a bucket the memberships are grouped
+// by partner (the point's other bucket): first the points for which the bucket is the higher of
+// their two (partner below it), then those for which it is the lower.  The lower-bucket list of a
+// point is the running side of its merge; once it is known, its M-th distance bounds the merged
+// list, so the higher-bucket row only needs the columns within that distance that are not also
+// members of the lower bucket (those are in the lower list already, or beyond its M-th): the
+// merged lists are unchanged (running side first on equal distance, ids of the running list
+// dropped from the new one).
+struct KnnPhase {
+    int phase = 0;                     // 0: all rows; 1: lower-bucket rows; 2: higher-bucket rows, seeded; 3: 1 then 2
+    const int64_t* split = nullptr;    // host [B]: first membership of each bucket with its partner above it
+    const int32_t* partner = nullptr;  // device [memberships]: the partner of each membership (CSR order)
+    const float* seed = nullptr;       // phase 2: device, by point id, stride seed_stride
+    int64_t seed_stride = 1;
+    const int64_t* mem_row = nullptr;  // phase 3: seeds read from the phase-1 rows of the lists
+    int64_t n_points = 0;              // phase 3: N
+};
+
 // members: the row of X gathered into each membership slot (grouped by bucket);
 // gid: the id written to the lists for each slot (members when null).
 // Buckets [b_lo, b_hi) (all when b_hi < 0) of the membership CSR: list row j - offsets[b_lo] is
 // membership j.  off_host: the offsets already on the host (else read from offsets_dev).
 void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* members, const int64_t* offsets_dev,
                      int B, int M, int32_t* list_ids, float* list_dists, int* err, cudaStream_t st,
-                     const int32_t* gid = nullptr, int b_lo = 0, int b_hi = -1, const int64_t* off_host = nullptr)
+                     const int32_t* gid = nullptr, int b_lo = 0, int b_hi = -1, const int64_t* off_host = nullptr,
+                     const KnnPhase& ph = KnnPhase())
 {
     (void)n;
     if (b_hi < 0) b_hi = B;
@@ -365,25 +384,53 @@ void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* 
     std::vector<int> order(static_cast<size_t>(b_hi - b_lo));
     std::iota(order.begin(), order.end(), b_lo);
     std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return off[a + 1] - off[a] > off[b + 1] - off[b]; });
-    std::vector<WorkItem> wl;
-    for (int b : order) {
-        const int64_t lo = off[b] - j0, nb = off[b + 1] - off[b];
-        for (int64_t t = 0; t < nb; t += 128)
-            wl.push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, nb - t)),
-                                  static_cast<int32_t>(lo), static_cast<int32_t>(nb), static_cast<int32_t>(t), 0, 0, 0});
-    }
-    auto work = upload(wl, st);
+    GTA_REQUIRE(ph.phase == 0 || (ph.split && ph.partner && (ph.phase != 2 || ph.seed) && (ph.phase != 3 || ph.mem_row)),
+                kInvalid, "bucket_knn: phased rows need the split, partner and seed arrays");
+    // rows [r_lo, r_hi) of bucket b's segment for a phase
+    auto rows_of = [&](int b, int phase, int64_t& r_lo, int64_t& r_hi) {
+        const int64_t nb = off[b + 1] - off[b];
+        const int64_t s = phase == 0 ? 0 : std::min(nb, std::max<int64_t>(0, ph.split[b] - off[b]));
+        r_lo = phase == 1 ? s : 0;
+        r_hi = phase == 2 ? s : nb;
+    };
     DistTopkProblem pr;
     pr.A = pool.get(); pr.a_total = n_mem; pr.B = pool.get(); pr.b_total = n_mem; pr.elem = elem; pr.d = d;
     pr.d_pad = d_pad; pr.a_norm = pnorm.get(); pr.b_norm = pnorm.get(); pr.b_gid = (gid ? gid : members) + j0;
-    pr.work = work.get(); pr.n_work = static_cast<int>(wl.size()); pr.m_out = M; pr.exclude_self = true;
+    pr.m_out = M; pr.exclude_self = true;
     pr.out_ids = list_ids; pr.out_dists = list_dists; pr.err = err;
     pr.prof_name = "dist_topk_bucket";
-    for (int b = b_lo; b < b_hi; ++b) {
-        const double nb = static_cast<double>(off[b + 1] - off[b]);
-        pr.flops += 2.0 * nb * nb * d;
+    DevBuf<float> seeds;
+    auto run = [&](int phase) {
+        std::vector<WorkItem> wl;
+        double flops = 0.0;
+        for (int b : order) {
+            const int64_t lo = off[b] - j0, nb = off[b + 1] - off[b];
+            int64_t r_lo = 0, r_hi = 0;
+            rows_of(b, phase, r_lo, r_hi);
+            for (int64_t t = r_lo; t < r_hi; t += 128)
+                wl.push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, r_hi - t)),
+                                      static_cast<int32_t>(lo), static_cast<int32_t>(nb), static_cast<int32_t>(t), 0, 0, 0});
+            flops += 2.0 * static_cast<double>(r_hi - r_lo) * static_cast<double>(nb) * d;
+        }
+        if (wl.empty()) return;
+        auto work = upload(wl, st);
+        DistTopkProblem q = pr;
+        q.work = work.get(); q.n_work = static_cast<int>(wl.size()); q.flops = flops;
+        if (phase == 2) {
+            q.partner = ph.partner + j0;
+            if (ph.phase == 3) { q.seed = seeds.get(); q.seed_stride = 1; }
+            else { q.seed = ph.seed; q.seed_stride = ph.seed_stride; }
+        }
+        dist_topk(q, st);
+    };
+    if (ph.phase == 3) {
+        run(1);
+        seeds = DevBuf<float>(static_cast<size_t>(ph.n_points), st);
+        seeds_from_lists(list_dists, ph.mem_row, ph.n_points, M, j0, n_mem, seeds.get(), st);
+        run(2);
+    } else {
+        run(ph.phase);
     }
-    dist_topk(pr, st);
 }
 
 struct BucketOut {
@@ -486,15 +533,31 @@ void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const
     if (o.top2) GTA_CUDA(cudaMemcpyAsync(o.top2, top2.get(), sizeof(int32_t) * 2 * N, cudaMemcpyDeviceToDevice, st));
     DevBuf<int32_t> members(static_cast<size_t>(N) * 2, st);
     DevBuf<int64_t> offsets(static_cast<size_t>(B) + 1, st), mem_row(static_cast<size_t>(N) * 2, st);
-    build_memberships(top2.get(), N, B, members.get(), offsets.get(), mem_row.get(), err.get(), st);
+    // exact data with short lists: lower-bucket rows first, then the higher-bucket rows seeded
+    // by them (same lists; see KnnPhase)
+    const int elem = exact_bf16(ds.dtype, d) ? kElemBF16 : kElemF32;
+    const bool phased = dist_topk_seedable(elem, pad_dim(d, elem), M);
+    DevBuf<int64_t> split_d;
+    DevBuf<int32_t> partner;
+    std::vector<int64_t> split_h;
+    if (phased) {
+        split_d = DevBuf<int64_t>(static_cast<size_t>(B), st);
+        partner = DevBuf<int32_t>(static_cast<size_t>(N) * 2, st);
+    }
+    build_memberships(top2.get(), N, B, members.get(), offsets.get(), mem_row.get(), err.get(), st, split_d.get(),
+                      partner.get());
     top2.release();
+    if (phased) {
+        split_h.resize(static_cast<size_t>(B));
+        GTA_CUDA(cudaMemcpyAsync(split_h.data(), split_d.get(), sizeof(int64_t) * B, cudaMemcpyDeviceToHost, st));
+        GTA_CUDA(cudaStreamSynchronize(st));
+    }
 
     // ---- per-bucket all-pairs kNN, then merge each point's two lists.  When the memberships' pool
     // rows and lists do not fit the device budget, buckets are processed in ascending batches that
     // do, each batch's lists merged into the per-point lists as it completes (first memberships
     // copied, second ones merged: the same lists as the one-pass build).
     const int64_t n_mem = 2 * N;
-    const int elem = exact_bf16(ds.dtype, d) ? kElemBF16 : kElemF32;
     const double per_row = static_cast<double>(pad_dim(d, elem)) * (elem == kElemBF16 ? 2 : 4) + 8.0 * M + 8.0;
     double budget = static_cast<double>(p.device_budget);
     if (budget <= 0.0) {  // the free memory is queried only for stages that may not fit
@@ -523,7 +586,13 @@ void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const
         DevBuf<float> ldist(static_cast<size_t>(n_mem) * M, st);
         {
             ProfScope prof("bucket_knn_total", 0.0, st);
-            bucket_knn_impl(X, ds.dtype, N, d, members.get(), offsets.get(), B, M, lid.get(), ldist.get(), err.get(), st);
+            KnnPhase ph;
+            if (phased) {
+                ph.phase = 3; ph.split = split_h.data(); ph.partner = partner.get();
+                ph.mem_row = mem_row.get(); ph.n_points = N;
+            }
+            bucket_knn_impl(X, ds.dtype, N, d, members.get(), offsets.get(), B, M, lid.get(), ldist.get(), err.get(), st,
+                            nullptr, 0, -1, nullptr, ph);
         }
         merge_memberships(lid.get(), ldist.get(), mem_row.get(), N, M, o.ids, o.dists, st);
     } else {
@@ -532,20 +601,29 @@ void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const
         GTA_CUDA(cudaStreamSynchronize(st));
         const int64_t cap = std::max<int64_t>(1, static_cast<int64_t>(budget / per_row));
         ProfScope prof("bucket_knn_total", 0.0, st);
-        for (int b_lo = 0; b_lo < B;) {
-            int b_hi = b_lo + 1;  // at least one bucket per batch
-            while (b_hi < B && off[b_hi + 1] - off[b_lo] <= cap) ++b_hi;
-            const int64_t j0 = off[b_lo], nb = off[b_hi] - j0;
-            if (nb > 0) {
-                DevBuf<int32_t> lid(static_cast<size_t>(nb) * M, st);
-                DevBuf<float> ldist(static_cast<size_t>(nb) * M, st);
-                bucket_knn_impl(X, ds.dtype, N, d, members.get(), offsets.get(), B, M, lid.get(), ldist.get(), err.get(),
-                                st, nullptr, b_lo, b_hi, off.data());
-                merge_membership_batch(lid.get(), ldist.get(), members.get(), mem_row.get(), j0, nb, N, M, o.ids,
-                                       o.dists, st);
-                GTA_CUDA(cudaStreamSynchronize(st));  // the batch's buffers are released next
+        // phased: a sweep over the batches for the lower-bucket rows (copied into the per-point
+        // lists), then one for the higher-bucket rows seeded by those lists (merged into them)
+        for (int sweep = phased ? 1 : 0; sweep <= (phased ? 2 : 0); ++sweep) {
+            KnnPhase ph;
+            if (phased) {
+                ph.phase = sweep; ph.split = split_h.data(); ph.partner = partner.get();
+                ph.seed = o.dists + (M - 1); ph.seed_stride = M;
             }
-            b_lo = b_hi;
+            for (int b_lo = 0; b_lo < B;) {
+                int b_hi = b_lo + 1;  // at least one bucket per batch
+                while (b_hi < B && off[b_hi + 1] - off[b_lo] <= cap) ++b_hi;
+                const int64_t j0 = off[b_lo], nb = off[b_hi] - j0;
+                if (nb > 0) {
+                    DevBuf<int32_t> lid(static_cast<size_t>(nb) * M, st);
+                    DevBuf<float> ldist(static_cast<size_t>(nb) * M, st);
+                    bucket_knn_impl(X, ds.dtype, N, d, members.get(), offsets.get(), B, M, lid.get(), ldist.get(),
+                                    err.get(), st, nullptr, b_lo, b_hi, off.data(), ph);
+                    merge_membership_batch(lid.get(), ldist.get(), members.get(), mem_row.get(), j0, nb, N, M, o.ids,
+                                           o.dists, st, sweep == 0 ? 3 : sweep);
+                    GTA_CUDA(cudaStreamSynchronize(st));  // the batch's buffers are released next
+                }
+                b_lo = b_hi;
+            }
         }
     }
     check_device_error(err.get(), st, "build_bucket");

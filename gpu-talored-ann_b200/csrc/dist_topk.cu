@@ -86,6 +86,9 @@ struct DistTopkArgs {
     int* err;
     uint32_t list_off, buf_off, pn_off, bar_off;
     uint32_t scr_off;           // two-CTA variant: per-lane score scratch
+    const float* seed;          // two-CTA exact variant: per-row starting thresholds (see DistTopkProblem)
+    int64_t seed_stride;
+    const int32_t* partner;
 };
 
 constexpr int kBuf = 32;                  // per-row staging buffer (entries)
@@ -761,7 +764,15 @@ __global__ void __launch_bounds__(kThreads, kV)
             for (int c = 0; c < 2 * kL; c += 32) tmem_st_32x32b_x32(tl + static_cast<uint32_t>(c), e);
             tmem_st_wait();
         }
-        float thr = row_ok ? FLT_MAX : -FLT_MAX;
+        // seeded rows: a known bound on the merged list (exact scores, so seed - ||a||^2 is exact)
+        const bool seeded = !kTF32 && p.seed != nullptr;
+        float seed_thr = FLT_MAX;
+        int32_t skip_partner = -1;
+        if (seeded && row_ok) {
+            seed_thr = fminf(p.seed[static_cast<int64_t>(p.b_gid[arow]) * p.seed_stride] - anorm, FLT_MAX) + 0.0f;
+            skip_partner = p.partner[arow];
+        }
+        float thr = row_ok ? seed_thr : -FLT_MAX;
         int nb = 0, n_pass = 0, n_flush = 0;
         bool ok = true;
         const bool st_on = p.stats != nullptr;
@@ -784,8 +795,11 @@ __global__ void __launch_bounds__(kThreads, kV)
             }
         };
         // the row's own column: tile t0 + r / 64, slice (r % 64) / 16, element r % 16
-        const int self_ct = has_self ? t0 + (r >> 6) : -1;
-        const int self_c = (r & 63) >> 4;
+        // the row's own column self_col0 + r: its tile, 16-column slice and element
+        const int self_col = w.self_col0 + r;
+        const int self_ct = has_self ? (self_col / kTN) : -1;
+        const int self_c = (self_col % kTN) >> 4;
+        const int self_el = self_col & 15;
         prefetch_cols(0);
         for (int k = 0; k < n_ct; ++k) {
             const int ct = tile_at(k, t0, n_ct);
@@ -809,7 +823,7 @@ __global__ void __launch_bounds__(kThreads, kV)
             // equal and never takes the wrong sign; thr is never -0), one funnel shift per score
             // to collect the signs: bit 15 - e of `fail` is set where score e lies above thr.
             auto scan_slice = [&](int c, const uint32_t (&v)[16], uint32_t (&nxt)[16], bool nxt_in_flight) {
-                const int self_e = (ct == self_ct && c == self_c) ? (lane & 15) : -1;
+                const int self_e = (ct == self_ct && c == self_c) ? self_el : -1;
                 const uint32_t c0 = static_cast<uint32_t>(ct * kTN + c * 16);
                 const ulonglong2* pn2 = reinterpret_cast<const ulonglong2*>(pnw + c * 16);
                 const unsigned long long thr2 = f2_pack(thr, thr), m2 = f2_pack(-2.0f, -2.0f);
@@ -839,7 +853,7 @@ __global__ void __launch_bounds__(kThreads, kV)
                         scr[(2 * e2) * 32] = lo;
                         scr[(2 * e2 + 1) * 32] = hi;
                     }
-                    int npass = __popc(m);
+                    const int npass = __popc(m);
                     // flush only when a lane's buffer cannot take this slice's passes
                     if (__any_sync(0xffffffffu, nb + npass > kBuf)) {
                         if (nxt_in_flight) tmem_ld_wait_regs(nxt);  // no TMEM load in flight across the call
@@ -851,23 +865,26 @@ __global__ void __launch_bounds__(kThreads, kV)
                         if (row_ok) {
                             thr = (lt.last == kEmptyKey) ? FLT_MAX : key_dist(lt.last);
                             if (kTF32 && lt.msel != kEmptyKey) thr = fminf(thr, key_dist(lt.msel) + margin);
-                            thr += 0.0f;  // -0 -> +0 for the sign test
+                            thr = fminf(thr, seed_thr) + 0.0f;  // -0 -> +0 for the sign test
                         }
                         // this slice's passes against the new threshold
                         m = 0u;
 #pragma unroll
                         for (int e = 0; e < 16; ++e) m |= (scr[e * 32] <= thr) ? (1u << (15 - e)) : 0u;
                         if (self_e >= 0) m &= ~(1u << (15 - self_e));
-                        npass = __popc(m);
                         if (st_on) cyc_flush += clock64() - f0;
                     }
-                    for (int i = nb; m != 0u; ++i) {  // this lane's passes
+                    int i = nb;
+                    while (m != 0u) {  // this lane's passes
                         const int e = 15 - (__ffs(m) - 1);
+                        m &= m - 1u;
+                        // seeded rows skip the points of their other bucket (already in that list)
+                        if (seeded && p.partner[static_cast<int64_t>(w.b_row0) + c0 + e] == skip_partner) continue;
                         const uint32_t id = kTF32 ? c0 + static_cast<uint32_t>(e) : idw[c * 16 + e];
                         my_buf[i * 128] = (static_cast<uint64_t>(f2key(scr[e * 32])) << 32) | id;
-                        m &= m - 1u;
+                        ++i;
                     }
-                    nb += npass;
+                    nb = i;
                 }
                 __syncwarp();
             };
@@ -1166,6 +1183,13 @@ CUtensorMap make_tmap(const void* base, int elem, int64_t rows, int d_pad, int b
 
 }  // namespace
 
+bool dist_topk_seedable(int elem, int d_pad, int m_out)
+{
+    if (elem != kElemBF16 || m_out < 1 || m_out > 64) return false;
+    Plan pl;
+    return make_plan(d_pad * 2 / 128, m_out, false, pl) && pl.variant == 2;
+}
+
 void dist_topk(const DistTopkProblem& pr, cudaStream_t st)
 {
     if (pr.n_work == 0) return;
@@ -1211,6 +1235,11 @@ void dist_topk(const DistTopkProblem& pr, cudaStream_t st)
     a.err = pr.err;
     a.list_off = pl.list_off; a.buf_off = pl.buf_off; a.pn_off = pl.pn_off; a.bar_off = pl.bar_off;
     a.scr_off = pl.scr_off;
+    if (pr.seed) {
+        GTA_REQUIRE(!screen && pl.variant == 2 && pr.partner && pr.b_gid, kInvalid,
+                    "dist_topk: seeded rows need exact data, lists of at most 64 and partner / id arrays");
+        a.seed = pr.seed; a.seed_stride = pr.seed_stride; a.partner = pr.partner;
+    }
 
     {
         ProfScope prof(pr.prof_name, pr.flops, st);

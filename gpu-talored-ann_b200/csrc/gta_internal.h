@@ -121,9 +121,18 @@ struct DistTopkProblem {
     // rows the exact rerank reads for B (default B / d_pad): the unsplit centroids
     const void* b_exact = nullptr;
     int b_exact_pitch = 0;
+    // seeded rows (exact data, lists of at most 64): each A row starts from the threshold
+    // seed[gid * seed_stride] - ||a||^2 (gid = b_gid of the row; seed: a distance already known to
+    // bound the row's merged list) and drops the columns whose partner[] equals the row's own
+    // partner[] (points already seen through the row's other membership); null: no seeding
+    const float* seed = nullptr;
+    int64_t seed_stride = 1;
+    const int32_t* partner = nullptr;  // [a_total] (A and B rows are the same pool)
 };
 
 void dist_topk(const DistTopkProblem& pr, cudaStream_t st);
+// true when dist_topk accepts seeded rows for this shape (exact data, two-CTA variant)
+bool dist_topk_seedable(int elem, int d_pad, int m_out);
 
 // ---- other kernels (kernels.cu) -------------------------------------------
 // Convert rows of X (dtype: 0 f32, 1 u8, 2 i8) selected by row_ids (null = identity)
@@ -138,14 +147,25 @@ void kmeanspp_init(const float* pool, const float* pool_norm, int64_t pool_n, in
 void centroid_update(const float* Xs, int64_t n_s, int d, int d_pad, const int32_t* assign, const float* C_in,
                      int32_t B, float* C_out, float* C_norm, int* err, cudaStream_t st, bool integer_rows = false);
 void check_ids(const int32_t* ids, int64_t n, int32_t hi, int* err, cudaStream_t st);
+// Memberships grouped by bucket, within a bucket by the point's other bucket (its partner),
+// then by point.  split (optional, [B]): first membership of each bucket whose partner is above
+// the bucket (before it: the points for which the bucket is the higher of the two); partner
+// (optional, [2N]): the other bucket of each membership's point.
 void build_memberships(const int32_t* top2, int64_t N, int32_t B, int32_t* members, int64_t* offsets,
-                       int64_t* mem_row, int* err, cudaStream_t st);
+                       int64_t* mem_row, int* err, cudaStream_t st, int64_t* split = nullptr,
+                       int32_t* partner = nullptr);
+// seed[p] = the M-th distance of point p's lower-bucket list (rows j0 .. j0 + n_rows of the
+// list buffer, +inf when that row is elsewhere)
+void seeds_from_lists(const float* list_d, const int64_t* mem_row, int64_t N, int M, int64_t j0, int64_t n_rows,
+                      float* seed, cudaStream_t st);
 void merge_memberships(const int32_t* list_n, const float* list_d, const int64_t* mem_row, int64_t N, int M,
                        int32_t* out_n, float* out_d, cudaStream_t st);
 // membership rows j0 .. j0 + n - 1 (their lists in bl / bd) into the per-point lists, first memberships
 // copied, second ones merged (the order of merge_memberships)
+// passes: bit 0 copies the batch's lower-bucket lists, bit 1 merges its higher-bucket lists
 void merge_membership_batch(const int32_t* bl, const float* bd, const int32_t* members, const int64_t* mem_row,
-                            int64_t j0, int64_t n, int64_t N, int M, int32_t* out_n, float* out_d, cudaStream_t st);
+                            int64_t j0, int64_t n, int64_t N, int M, int32_t* out_n, float* out_d, cudaStream_t st,
+                            int passes = 3);
 void merge_lists(const int32_t* run_n, const float* run_d, const int32_t* new_n, const float* new_d, int64_t N,
                  int M, int32_t* out_n, float* out_d, cudaStream_t st);
 void sanitize(const int32_t* knn, int64_t N, int M, uint32_t* out, cudaStream_t st);

@@ -597,6 +597,41 @@ __global__ void seg_offsets_scaled_kernel(const uint32_t* __restrict__ keys_sort
     offsets[b] = lo;
 }
 
+// first index of bucket b's memberships whose partner is above b (keys b * B + partner)
+__global__ void phase_split_kernel(const uint32_t* __restrict__ keys_sorted, int64_t n, int32_t B,
+                                   int64_t* __restrict__ split)
+{
+    const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    const uint64_t want = static_cast<uint64_t>(b) * static_cast<uint64_t>(B) + static_cast<uint64_t>(b);
+    int64_t lo = 0, hi = n;
+    while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (static_cast<uint64_t>(keys_sorted[mid]) < want) lo = mid + 1;
+        else hi = mid;
+    }
+    split[b] = lo;
+}
+
+__global__ void partner_kernel(const uint32_t* __restrict__ keys_sorted, int64_t n, int32_t B,
+                               int32_t* __restrict__ partner)
+{
+    const int64_t j = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    const uint32_t k = keys_sorted[j];
+    partner[j] = k < static_cast<uint32_t>(B) * static_cast<uint32_t>(B) ? static_cast<int32_t>(k % static_cast<uint32_t>(B))
+                                                                          : -1;
+}
+
+__global__ void seeds_from_lists_kernel(const float* __restrict__ list_d, const int64_t* __restrict__ mem_row,
+                                        int64_t N, int M, int64_t j0, int64_t n_rows, float* __restrict__ seed)
+{
+    const int64_t p = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (p >= N) return;
+    const int64_t r = mem_row[2 * p] - j0;
+    seed[p] = (r >= 0 && r < n_rows) ? list_d[r * M + (M - 1)] : INFINITY;
+}
+
 __global__ void mem_rows_kernel(const uint32_t* __restrict__ keys_sorted, const int32_t* __restrict__ members,
                                 const int32_t* __restrict__ top2, int64_t n2, int32_t B, int64_t* __restrict__ mem_row)
 {
@@ -1279,7 +1314,7 @@ void group_by_key(const int32_t* keys, int64_t n, int32_t B, int32_t* order, int
 }
 
 void build_memberships(const int32_t* top2, int64_t N, int32_t B, int32_t* members, int64_t* offsets,
-                       int64_t* mem_row, int* err, cudaStream_t st)
+                       int64_t* mem_row, int* err, cudaStream_t st, int64_t* split, int32_t* partner)
 {
     const int64_t n2 = 2 * N;
     GTA_REQUIRE(n2 < (1ll << 31), kInvalid, "memberships: more than 2^31 memberships on one device");
@@ -1302,6 +1337,22 @@ void build_memberships(const int32_t* top2, int64_t N, int32_t B, int32_t* membe
     GTA_CUDA(cudaMemsetAsync(mem_row, 0xff, sizeof(int64_t) * static_cast<size_t>(n2), st));  // -1: not built
     mem_rows_kernel<<<blocks_for(n2, 256), 256, 0, st>>>(keys_out.get(), members, top2, n2, B, mem_row);
     count_launches(1);
+    if (split) {
+        phase_split_kernel<<<blocks_for(B, 256), 256, 0, st>>>(keys_out.get(), n2, B, split);
+        count_launches(1);
+    }
+    if (partner) {
+        partner_kernel<<<blocks_for(n2, 256), 256, 0, st>>>(keys_out.get(), n2, B, partner);
+        count_launches(1);
+    }
+    GTA_CUDA(cudaGetLastError());
+}
+
+void seeds_from_lists(const float* list_d, const int64_t* mem_row, int64_t N, int M, int64_t j0, int64_t n_rows,
+                      float* seed, cudaStream_t st)
+{
+    seeds_from_lists_kernel<<<blocks_for(N, 256), 256, 0, st>>>(list_d, mem_row, N, M, j0, n_rows, seed);
+    count_launches(1);
     GTA_CUDA(cudaGetLastError());
 }
 
@@ -1317,14 +1368,17 @@ void merge_memberships(const int32_t* list_n, const float* list_d, const int64_t
 }
 
 void merge_membership_batch(const int32_t* bl, const float* bd, const int32_t* members, const int64_t* mem_row,
-                            int64_t j0, int64_t n, int64_t N, int M, int32_t* out_n, float* out_d, cudaStream_t st)
+                            int64_t j0, int64_t n, int64_t N, int M, int32_t* out_n, float* out_d, cudaStream_t st,
+                            int passes)
 {
     GTA_REQUIRE(M >= 1 && M <= kMaxM, kInvalid, "merge: M must be in [1, 128]");
     if (n <= 0) return;
-    for (int pass = 0; pass < 2; ++pass)
+    for (int pass = 0; pass < 2; ++pass) {
+        if (!((passes >> pass) & 1)) continue;
         merge_batch_kernel<<<blocks_for(n, kMergeWarps), kMergeWarps * 32, 0, st>>>(bl, bd, members, mem_row, j0, n, N, M,
                                                                                      pass, out_n, out_d);
-    count_launches(2);
+        count_launches(1);
+    }
     GTA_CUDA(cudaGetLastError());
 }
 
