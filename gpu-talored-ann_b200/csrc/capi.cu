@@ -417,6 +417,7 @@ void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* 
         DistTopkProblem q = pr;
         q.work = work.get(); q.n_work = static_cast<int>(wl.size()); q.flops = flops;
         if (phase == 2) {
+            q.prof_name = "dist_topk_bucket_seeded";
             q.partner = ph.partner + j0;
             if (ph.phase == 3) { q.seed = seeds.get(); q.seed_stride = 1; }
             else { q.seed = ph.seed; q.seed_stride = ph.seed_stride; }
