@@ -177,7 +177,8 @@ inline cudaStream_t S(void* s)
 
 #define GTA_WORKSPACE(stream) ::gta::WorkspaceScope ws_scope_(S(stream))
 
-int pad_dim(int d, int elem) { const int q = elem == kElemBF16 ? 64 : 32; return (d + q - 1) / q * q; }
+// operand rows padded to 128-byte multiples (one TMA / MMA K chunk)
+int pad_dim(int d, int elem) { const int q = 128 / elem_bytes(elem); return (d + q - 1) / q * q; }
 
 int elem_size(int dtype) { return dtype == GTA_F32 ? 4 : 1; }
 
@@ -188,6 +189,15 @@ bool exact_bf16(int dtype, int d)
     if (dtype == GTA_U8) return 2.0 * d * 255.0 * 255.0 < 16777216.0;
     if (dtype == GTA_I8) return 2.0 * d * 128.0 * 128.0 < 16777216.0;
     return false;
+}
+
+// Operand type of the bucket kNN: the dataset's own bytes for u8 rows when the 8-bit MMA path
+// applies (lists of at most 64), bf16 for other exact 8-bit rows, else f32 (tf32 screen).
+int knn_elem(int dtype, int d, int M)
+{
+    if (!exact_bf16(dtype, d)) return kElemF32;
+    if (dtype == GTA_U8 && dist_topk_u8_fits(pad_dim(d, kElemU8), M)) return kElemU8;
+    return kElemBF16;
 }
 
 void copy_rows_padded(float* dst, int d_pad, const float* src, int d, int64_t n, bool src_dev, cudaStream_t st)
@@ -372,12 +382,12 @@ void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* 
     const int64_t n_mem = off[static_cast<size_t>(b_hi)] - j0;
     if (n_mem == 0) return;
     GTA_REQUIRE(n_mem < (1ll << 31), kInvalid, "bucket_knn: too many memberships on one device");
-    const int elem = exact_bf16(dtype, d) ? kElemBF16 : kElemF32;
+    const int elem = knn_elem(dtype, d, M);
     const int d_pad = pad_dim(d, elem);
-    DevBuf<uint8_t> pool(static_cast<size_t>(n_mem) * d_pad * (elem == kElemBF16 ? 2 : 4), st);
+    DevBuf<uint8_t> pool(static_cast<size_t>(n_mem) * d_pad * elem_bytes(elem), st);
     DevBuf<float> pnorm(static_cast<size_t>(n_mem), st);
     {
-        ProfScope prof("gather", static_cast<double>(n_mem) * (d * elem_size(dtype) + d_pad * (elem == kElemBF16 ? 2 : 4)), st);
+        ProfScope prof("gather", static_cast<double>(n_mem) * (d * elem_size(dtype) + d_pad * elem_bytes(elem)), st);
         convert_rows(X, dtype, d, members + j0, n_mem, pool.get(), elem, d_pad, pnorm.get(), st);
     }
     // work list: one CTA per 128-row tile of a bucket, largest buckets first
@@ -536,7 +546,7 @@ void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const
     DevBuf<int64_t> offsets(static_cast<size_t>(B) + 1, st), mem_row(static_cast<size_t>(N) * 2, st);
     // exact data with short lists: lower-bucket rows first, then the higher-bucket rows seeded
     // by them (same lists; see KnnPhase)
-    const int elem = exact_bf16(ds.dtype, d) ? kElemBF16 : kElemF32;
+    const int elem = knn_elem(ds.dtype, d, M);
     const bool phased = dist_topk_seedable(elem, pad_dim(d, elem), M);
     DevBuf<int64_t> split_d;
     DevBuf<int32_t> partner;
@@ -559,7 +569,7 @@ void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const
     // do, each batch's lists merged into the per-point lists as it completes (first memberships
     // copied, second ones merged: the same lists as the one-pass build).
     const int64_t n_mem = 2 * N;
-    const double per_row = static_cast<double>(pad_dim(d, elem)) * (elem == kElemBF16 ? 2 : 4) + 8.0 * M + 8.0;
+    const double per_row = static_cast<double>(pad_dim(d, elem)) * elem_bytes(elem) + 8.0 * M + 8.0;
     double budget = static_cast<double>(p.device_budget);
     if (budget <= 0.0) {  // the free memory is queried only for stages that may not fit
         int dev = 0;

@@ -225,6 +225,16 @@ __device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t adesc, uint64_t b
     }
 }
 
+// D[tmem] += A[smem] * B[smem]^T on unsigned 8-bit operands (kind::i8, K = 32 bytes per
+// instruction), exact int32 accumulation onto D's current contents.
+__device__ __forceinline__ void umma_u8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc)
+{
+    asm volatile("{ .reg .pred p; setp.ne.b32 p, 1, 0; tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p; }" ::"r"(
+                     tmem_d),
+                 "l"(adesc), "l"(bdesc), "r"(idesc)
+                 : "memory");
+}
+
 // Arrive once on an mbarrier when all previously issued MMAs of this thread complete.
 __device__ __forceinline__ void umma_commit(uint32_t bar)
 {
@@ -321,6 +331,11 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr)
 __host__ __device__ constexpr uint32_t make_idesc(uint32_t fmt, uint32_t M, uint32_t N)
 {
     return (1u << 4) | (fmt << 7) | (fmt << 10) | ((N >> 3) << 17) | ((M >> 4) << 24);
+}
+// kind::i8: int32 accumulate (c_format 2), A and B unsigned 8-bit (format 0), both K-major.
+__host__ __device__ constexpr uint32_t make_idesc_u8(uint32_t M, uint32_t N)
+{
+    return (2u << 4) | ((N >> 3) << 17) | ((M >> 4) << 24);
 }
 
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads)

@@ -428,12 +428,19 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity, i
 
 // kV = 1: one CTA per SM, 128-column tiles, row lists in shared memory.
 // kV = 2: two CTAs per SM, 64-column tiles, row lists (at most 64 keys) in TMEM.
-template <bool kTF32, int kL, int kV>
+// kU8: unsigned 8-bit operand rows (the dataset's own bytes) on kind::i8 MMAs: half the MMA
+//      instructions and operand bytes of bf16.  The accumulators start at 0x4B000000, so each
+//      int32 result reads as the float 2^23 + x.y (exact for 0 <= x.y < 2^23); the scan
+//      screens with fl(s - 2^24) against fl(thr - 2^24) (rounding is monotone: no admitted
+//      column is missed) and every admitted column's exact score is recomputed and rechecked.
+constexpr uint32_t kMagicU8 = 0x4B000000u;  // the float 2^23
+template <bool kTF32, int kL, int kV, bool kU8 = false>
 __global__ void __launch_bounds__(kThreads, kV)
     dist_topk_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const DistTopkArgs p)
 {
     static_assert(kV == 1 || (kV == 2 && kL <= 64), "TMEM row lists hold at most 64 keys");
+    static_assert(!kU8 || (kV == 2 && !kTF32), "8-bit operands take the two-CTA exact variant");
     constexpr uint32_t kTmemCols = 256u;
     constexpr int kTN = kV == 1 ? 128 : 64;                            // column tile
     constexpr uint32_t kBChunk = static_cast<uint32_t>(kTN) * 128u;   // bytes of one B K-chunk
@@ -454,7 +461,7 @@ __global__ void __launch_bounds__(kThreads, kV)
     const uint32_t stage_bytes = p.a_resident ? kBChunk : kBChunk + kTileBytes;
     const uint32_t a_bytes = p.a_resident ? static_cast<uint32_t>(p.k_chunks) * kTileBytes : 0u;
     const uint32_t stage0 = base + a_bytes;
-    constexpr int kElemsPerChunk = kTF32 ? 32 : 64;
+    constexpr int kElemsPerChunk = kU8 ? 128 : (kTF32 ? 32 : 64);
 
     uint64_t* list = reinterpret_cast<uint64_t*>(gbase + p.list_off);
     uint64_t* buf = reinterpret_cast<uint64_t*>(gbase + p.buf_off);
@@ -486,6 +493,21 @@ __global__ void __launch_bounds__(kThreads, kV)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
+    if constexpr (kU8) {
+        // both accumulator stages start at the offset (each epilogue warp arms its own lanes)
+        if (warp >= 2) {
+            uint32_t mg[32];
+#pragma unroll
+            for (int i = 0; i < 32; ++i) mg[i] = kMagicU8;
+            const uint32_t lb = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+#pragma unroll
+            for (int c = 0; c < 2 * kTN; c += 32) tmem_st_32x32b_x32(lb + static_cast<uint32_t>(c), mg);
+            tmem_st_wait();
+        }
+        tc_fence_before();
+        __syncthreads();
+        tc_fence_after();
+    }
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
@@ -521,7 +543,7 @@ __global__ void __launch_bounds__(kThreads, kV)
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            const uint32_t idesc = make_idesc(kTF32 ? 2u : 1u, kTileM, kTN);
+            const uint32_t idesc = kU8 ? make_idesc_u8(kTileM, kTN) : make_idesc(kTF32 ? 2u : 1u, kTileM, kTN);
             bool ok = true;
             long long mma_wait_acc = 0, mma_wait_full = 0;
             if (p.a_resident) ok = mbar_wait_backoff(a_full, 0, abort_flag, p.err, kDevTimeoutFull);
@@ -546,8 +568,10 @@ __global__ void __launch_bounds__(kThreads, kV)
                     const uint64_t adesc = smem_desc_sw128(sa);
                     const uint64_t bdesc = smem_desc_sw128(sb);
 #pragma unroll
-                    for (int k = 0; k < 4; ++k)  // 4 x 32 B of K per 128-byte chunk
-                        umma<kTF32>(d_tmem, adesc + 2ull * k, bdesc + 2ull * k, idesc, (kc | k) != 0 ? 1u : 0u);
+                    for (int k = 0; k < 4; ++k) {  // 4 x 32 B of K per 128-byte chunk
+                        if constexpr (kU8) umma_u8(d_tmem, adesc + 2ull * k, bdesc + 2ull * k, idesc);
+                        else umma<kTF32>(d_tmem, adesc + 2ull * k, bdesc + 2ull * k, idesc, (kc | k) != 0 ? 1u : 0u);
+                    }
                     umma_commit(EMPTY_BAR(s));
                     ++it;
                 }
@@ -826,7 +850,13 @@ __global__ void __launch_bounds__(kThreads, kV)
                 const int self_e = (ct == self_ct && c == self_c) ? self_el : -1;
                 const uint32_t c0 = static_cast<uint32_t>(ct * kTN + c * 16);
                 const ulonglong2* pn2 = reinterpret_cast<const ulonglong2*>(pnw + c * 16);
-                const unsigned long long thr2 = f2_pack(thr, thr), m2 = f2_pack(-2.0f, -2.0f);
+                // 8-bit operands: v reads as 2^23 + x.y, so the fma below gives fl(s - 2^24)
+                const float thr_s = kU8 ? thr - 16777216.0f : thr;
+                const unsigned long long thr2 = f2_pack(thr_s, thr_s), m2 = f2_pack(-2.0f, -2.0f);
+                // the exact score of element e of this slice from the scratch copy
+                auto exact_score = [&](int e) {
+                    return kU8 ? fmaf(-2.0f, scr[e * 32] - 8388608.0f, pnw[c * 16 + e]) : scr[e * 32];
+                };
                 unsigned long long s2[8];
                 uint32_t fail = 0;
 #pragma unroll
@@ -845,13 +875,18 @@ __global__ void __launch_bounds__(kThreads, kV)
                 uint32_t m = ~fail & 0xffffu;  // passes: bit 15 - e for score e
                 if (self_e >= 0) m &= ~(1u << (15 - self_e));
                 if (__any_sync(0xffffffffu, m != 0u)) {
-                    // scores to this lane's scratch, read back by the appends
+                    // scores (8-bit operands: the raw 2^23 + x.y) to this lane's scratch, read back by the appends
+                    if constexpr (kU8) {
 #pragma unroll
-                    for (int e2 = 0; e2 < 8; ++e2) {
-                        float lo, hi;
-                        f2_unpack(s2[e2], lo, hi);
-                        scr[(2 * e2) * 32] = lo;
-                        scr[(2 * e2 + 1) * 32] = hi;
+                        for (int e = 0; e < 16; ++e) scr[e * 32] = __uint_as_float(v[e]);
+                    } else {
+#pragma unroll
+                        for (int e2 = 0; e2 < 8; ++e2) {
+                            float lo, hi;
+                            f2_unpack(s2[e2], lo, hi);
+                            scr[(2 * e2) * 32] = lo;
+                            scr[(2 * e2 + 1) * 32] = hi;
+                        }
                     }
                     const int npass = __popc(m);
                     // flush only when a lane's buffer cannot take this slice's passes
@@ -870,7 +905,7 @@ __global__ void __launch_bounds__(kThreads, kV)
                         // this slice's passes against the new threshold
                         m = 0u;
 #pragma unroll
-                        for (int e = 0; e < 16; ++e) m |= (scr[e * 32] <= thr) ? (1u << (15 - e)) : 0u;
+                        for (int e = 0; e < 16; ++e) m |= (exact_score(e) <= thr) ? (1u << (15 - e)) : 0u;
                         if (self_e >= 0) m &= ~(1u << (15 - self_e));
                         if (st_on) cyc_flush += clock64() - f0;
                     }
@@ -878,10 +913,12 @@ __global__ void __launch_bounds__(kThreads, kV)
                     while (m != 0u) {  // this lane's passes
                         const int e = 15 - (__ffs(m) - 1);
                         m &= m - 1u;
+                        const float se = exact_score(e);
+                        if (kU8 && !(se <= thr)) continue;  // admitted by the rounded screen only
                         // seeded rows skip the points of their other bucket (already in that list)
                         if (seeded && p.partner[static_cast<int64_t>(w.b_row0) + c0 + e] == skip_partner) continue;
                         const uint32_t id = kTF32 ? c0 + static_cast<uint32_t>(e) : idw[c * 16 + e];
-                        my_buf[i * 128] = (static_cast<uint64_t>(f2key(scr[e * 32])) << 32) | id;
+                        my_buf[i * 128] = (static_cast<uint64_t>(f2key(se)) << 32) | id;
                         ++i;
                     }
                     nb = i;
@@ -909,6 +946,15 @@ __global__ void __launch_bounds__(kThreads, kV)
                     }
                     scan_slice(c, vb, va, more);
                 }
+            }
+            if constexpr (kU8) {  // re-arm the stage with the offset for its next tile
+                uint32_t mg[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) mg[i] = kMagicU8;
+                __syncwarp();
+                tmem_st_32x32b_x32(tbase, mg);
+                tmem_st_32x32b_x32(tbase + 32u, mg);
+                tmem_st_wait();
             }
             tc_fence_before();
             __syncwarp();
@@ -1115,11 +1161,11 @@ bool make_plan(int k_chunks, int m, bool screen, Plan& pl)
     return false;
 }
 
-template <bool kTF32, int kL, int kV>
+template <bool kTF32, int kL, int kV, bool kU8 = false>
 void launch_dist_topk(const CUtensorMap& tmA, const CUtensorMap& tmB, const DistTopkArgs& a, int n_work,
                       uint32_t smem, cudaStream_t st)
 {
-    auto fn = dist_topk_kernel<kTF32, kL, kV>;
+    auto fn = dist_topk_kernel<kTF32, kL, kV, kU8>;
     GTA_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     GTA_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     fn<<<n_work, kThreads, smem, st>>>(tmA, tmB, a);
@@ -1168,12 +1214,15 @@ EncodeFn get_encode()
 CUtensorMap make_tmap(const void* base, int elem, int64_t rows, int d_pad, int box_rows = 128)
 {
     CUtensorMap m;
-    const int esz = elem == kElemBF16 ? 2 : 4;
+    const int esz = elem_bytes(elem);
     cuuint64_t dims[2] = {static_cast<cuuint64_t>(d_pad), static_cast<cuuint64_t>(rows)};
     cuuint64_t strides[1] = {static_cast<cuuint64_t>(d_pad) * esz};
     cuuint32_t box[2] = {static_cast<cuuint32_t>(128 / esz), static_cast<cuuint32_t>(box_rows)};
     cuuint32_t estr[2] = {1u, 1u};
-    const CUresult r = get_encode()(&m, elem == kElemBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32,
+    const CUtensorMapDataType ty = elem == kElemU8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : elem == kElemBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    const CUresult r = get_encode()(&m, ty,
                                     2, const_cast<void*>(base), dims, strides, box, estr,
                                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -1185,9 +1234,15 @@ CUtensorMap make_tmap(const void* base, int elem, int64_t rows, int d_pad, int b
 
 bool dist_topk_seedable(int elem, int d_pad, int m_out)
 {
-    if (elem != kElemBF16 || m_out < 1 || m_out > 64) return false;
+    if (elem == kElemF32 || m_out < 1 || m_out > 64) return false;
     Plan pl;
-    return make_plan(d_pad * 2 / 128, m_out, false, pl) && pl.variant == 2;
+    return make_plan(d_pad * elem_bytes(elem) / 128, m_out, false, pl) && pl.variant == 2;
+}
+
+bool dist_topk_u8_fits(int d_pad, int m_out)
+{
+    Plan pl;
+    return m_out >= 1 && m_out <= 64 && d_pad % 128 == 0 && make_plan(d_pad / 128, m_out, false, pl) && pl.variant == 2;
 }
 
 void dist_topk(const DistTopkProblem& pr, cudaStream_t st)
@@ -1195,12 +1250,12 @@ void dist_topk(const DistTopkProblem& pr, cudaStream_t st)
     if (pr.n_work == 0) return;
     GTA_REQUIRE(pr.A && pr.B && pr.a_norm && pr.b_norm && pr.work && pr.out_ids && pr.out_dists, kInvalid,
                 "dist_topk: null operand");
-    const int esz = pr.elem == kElemBF16 ? 2 : 4;
+    const int esz = elem_bytes(pr.elem);
     GTA_REQUIRE((pr.d_pad * esz) % 128 == 0 && pr.d <= pr.d_pad, kInvalid, "dist_topk: rows must be 128-byte multiples");
     GTA_REQUIRE((reinterpret_cast<uintptr_t>(pr.A) & 15) == 0 && (reinterpret_cast<uintptr_t>(pr.B) & 15) == 0,
                 kInvalid, "dist_topk: operands must be 16-byte aligned");
     GTA_REQUIRE(pr.m_out >= 1 && pr.m_out <= 256, kInvalid, "dist_topk: list length must be in [1, 256]");
-    const bool screen = pr.elem != kElemBF16;
+    const bool screen = pr.elem == kElemF32;
     const int k_chunks = pr.d_pad * esz / 128;
     const int m_sel = pr.m_out;  // the row itself is masked in the kernel, not carried in its list
     Plan pl;
@@ -1244,8 +1299,16 @@ void dist_topk(const DistTopkProblem& pr, cudaStream_t st)
     {
         ProfScope prof(pr.prof_name, pr.flops, st);
         a.stats = prof.counters(8);
-        if (screen) launch_dist_topk_L<true>(pl.L, pl.variant, tmA, tmB, a, pr.n_work, pl.total, st);
-        else launch_dist_topk_L<false>(pl.L, pl.variant, tmA, tmB, a, pr.n_work, pl.total, st);
+        if (pr.elem == kElemU8) {
+            GTA_REQUIRE(pl.variant == 2 && (pl.L == 32 || pl.L == 64), kInvalid,
+                        "dist_topk: 8-bit operands need lists of at most 64 in the two-CTA variant");
+            if (pl.L == 32) launch_dist_topk<false, 32, 2, true>(tmA, tmB, a, pr.n_work, pl.total, st);
+            else launch_dist_topk<false, 64, 2, true>(tmA, tmB, a, pr.n_work, pl.total, st);
+        } else if (screen) {
+            launch_dist_topk_L<true>(pl.L, pl.variant, tmA, tmB, a, pr.n_work, pl.total, st);
+        } else {
+            launch_dist_topk_L<false>(pl.L, pl.variant, tmA, tmB, a, pr.n_work, pl.total, st);
+        }
     }
 
     if (screen) {

@@ -91,7 +91,10 @@ struct WorkItem {
     int32_t pad0, pad1, pad2;
 };
 
-enum ElemType : int { kElemBF16 = 0, kElemF32 = 1 };
+// operand rows of the distance kernel: bf16 (8-bit data held exactly, kind::f16), f32 (tf32
+// screen + exact rerank), u8 (the dataset's own bytes, kind::i8)
+enum ElemType : int { kElemBF16 = 0, kElemF32 = 1, kElemU8 = 2 };
+inline int elem_bytes(int elem) { return elem == kElemU8 ? 1 : elem == kElemBF16 ? 2 : 4; }
 
 // Row-wise top-k of squared L2 distances between A rows and a B segment.
 struct DistTopkProblem {
@@ -133,6 +136,8 @@ struct DistTopkProblem {
 void dist_topk(const DistTopkProblem& pr, cudaStream_t st);
 // true when dist_topk accepts seeded rows for this shape (exact data, two-CTA variant)
 bool dist_topk_seedable(int elem, int d_pad, int m_out);
+// true when 8-bit operand rows (kElemU8, rows padded to 128 bytes) run for this list length
+bool dist_topk_u8_fits(int d_pad, int m_out);
 
 // ---- other kernels (kernels.cu) -------------------------------------------
 // Convert rows of X (dtype: 0 f32, 1 u8, 2 i8) selected by row_ids (null = identity)

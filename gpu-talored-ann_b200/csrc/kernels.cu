@@ -48,6 +48,8 @@ template <> __device__ __forceinline__ float ld_f32<__nv_bfloat16>(const __nv_bf
 template <typename Tout> __device__ __forceinline__ Tout from_f32(float v);
 template <> __device__ __forceinline__ float from_f32<float>(float v) { return v; }
 template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+// 8-bit operand rows: the values are the dataset's own bytes (0 .. 255), held exactly
+template <> __device__ __forceinline__ uint8_t from_f32<uint8_t>(float v) { return static_cast<uint8_t>(v); }
 
 __device__ __forceinline__ float exact_l2_f(const float* __restrict__ a, const float* __restrict__ b, int d)
 {
@@ -83,6 +85,11 @@ __device__ __forceinline__ void load4_f32(const __nv_bfloat16* p, float (&v)[4])
 __device__ __forceinline__ void store4_from_f32(float* p, const float (&v)[4])
 {
     *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ void store4_from_f32(uint8_t* p, const float (&v)[4])
+{
+    *reinterpret_cast<uchar4*>(p) = make_uchar4(static_cast<uint8_t>(v[0]), static_cast<uint8_t>(v[1]),
+                                                static_cast<uint8_t>(v[2]), static_cast<uint8_t>(v[3]));
 }
 __device__ __forceinline__ void store4_from_f32(__nv_bfloat16* p, const float (&v)[4])
 {
@@ -134,10 +141,14 @@ void convert_dispatch_out(const Tin* X, int d, const int32_t* ids, int64_t n, vo
 {
     const int wpb = 8;
     const unsigned grid = static_cast<unsigned>((n + wpb - 1) / wpb);
-    const size_t in_align = sizeof(Tin) * 4, out_align = (out_elem == kElemBF16 ? 2 : 4) * 4;
+    const size_t in_align = sizeof(Tin) * 4, out_align = static_cast<size_t>(elem_bytes(out_elem)) * 4;
     const int vec4 = (d % 4 == 0) && (d_pad % 4 == 0) && (reinterpret_cast<uintptr_t>(X) % in_align == 0) &&
                      (reinterpret_cast<uintptr_t>(out) % out_align == 0);
-    if (out_elem == kElemBF16)
+    if (out_elem == kElemU8) {
+        GTA_REQUIRE(sizeof(Tin) == 1 && static_cast<Tin>(-1) > 0, kInvalid, "convert_rows: 8-bit operand rows need u8 data");
+        convert_rows_kernel<Tin, uint8_t><<<grid, wpb * 32, 0, st>>>(X, d, ids, n, static_cast<uint8_t*>(out), d_pad,
+                                                                      norms, vec4);
+    } else if (out_elem == kElemBF16)
         convert_rows_kernel<Tin, __nv_bfloat16><<<grid, wpb * 32, 0, st>>>(X, d, ids, n,
                                                                             static_cast<__nv_bfloat16*>(out), d_pad, norms,
                                                                             vec4);
