@@ -858,20 +858,24 @@ __global__ void __launch_bounds__(kThreads, kV)
                     return kU8 ? fmaf(-2.0f, scr[e * 32] - 8388608.0f, pnw[c * 16 + e]) : scr[e * 32];
                 };
                 unsigned long long s2[8];
-                uint32_t fail = 0;
+                // four independent 4-bit groups (short dependency chains), then one combine
+                uint32_t f4[4];
 #pragma unroll
                 for (int e4 = 0; e4 < 4; ++e4) {
                     const ulonglong2 n4 = pn2[e4];  // column norms 4 e4 .. 4 e4 + 3, two packed pairs
                     s2[2 * e4] = f2_fma(m2, f2_pack(__uint_as_float(v[4 * e4]), __uint_as_float(v[4 * e4 + 1])), n4.x);
                     s2[2 * e4 + 1] =
                         f2_fma(m2, f2_pack(__uint_as_float(v[4 * e4 + 2]), __uint_as_float(v[4 * e4 + 3])), n4.y);
+                    uint32_t g = 0;
 #pragma unroll
                     for (int j = 0; j < 2; ++j) {
                         const unsigned long long dd = f2_sub(thr2, s2[2 * e4 + j]);
-                        fail = __funnelshift_l(static_cast<uint32_t>(dd), fail, 1);
-                        fail = __funnelshift_l(static_cast<uint32_t>(dd >> 32), fail, 1);
+                        g = __funnelshift_l(static_cast<uint32_t>(dd), g, 1);
+                        g = __funnelshift_l(static_cast<uint32_t>(dd >> 32), g, 1);
                     }
+                    f4[e4] = g;
                 }
+                const uint32_t fail = (f4[0] << 12) | (f4[1] << 8) | (f4[2] << 4) | f4[3];
                 uint32_t m = ~fail & 0xffffu;  // passes: bit 15 - e for score e
                 if (self_e >= 0) m &= ~(1u << (15 - self_e));
                 if (__any_sync(0xffffffffu, m != 0u)) {
