@@ -53,9 +53,9 @@ def _peaks():
 
 
 # DRAM bytes (read + write) per algorithmic unit of a kernel, from one ncu capture of each
-# kernel on the C2 distribution at N = 400 000, scaled to a launch by its units (the traffic
-# grows with the rows processed)
-TRAFFIC_PER_UNIT = {"dist_topk_bucket": 579.74e6 / 3.3773e12, "prune": 139.38e6 / 6.7069e9}
+# kernel on the C2 distribution (bucket distance kernel, u8 operands: N = 600 000; prune:
+# N = 400 000), scaled to a launch by its units (the traffic grows with the rows processed)
+TRAFFIC_PER_UNIT = {"dist_topk_bucket": 430.70e6 / 3.3754e12, "prune": 139.38e6 / 6.7069e9}
 
 
 # ---------------------------------------------------------------- clocks
