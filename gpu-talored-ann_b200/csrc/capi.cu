@@ -879,9 +879,9 @@ void build_bucket2_round(const void* X, int dtype, int64_t N, int d, const gta_b
         pool_size[static_cast<size_t>(c)] = sz;
     }
     auto seg_b_d = upload(seg_b, st);
-    const int elem = exact_bf16(dtype, d) ? kElemBF16 : kElemF32;
+    const int elem = knn_elem(dtype, d, M);
     const int d_pad = pad_dim(d, elem);
-    const size_t row_bytes = static_cast<size_t>(d_pad) * (elem == kElemBF16 ? 2 : 4);
+    const size_t row_bytes = static_cast<size_t>(d_pad) * elem_bytes(elem);
     const int64_t max_pool = *std::max_element(pool_size.begin(), pool_size.end());
     const int64_t cap_rows = std::max<int64_t>(max_pool, static_cast<int64_t>(kPoolBudgetBytes / row_bytes));
     DevBuf<int32_t> lids(static_cast<size_t>(N) * M, st);

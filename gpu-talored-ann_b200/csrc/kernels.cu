@@ -938,7 +938,17 @@ __global__ void __launch_bounds__(kPruneWarps * 32)
                 h = (h + 1) & mask;
             }
         };
-        if (vec) {
+        if ((M & 15) == 0) {
+            // 16 ids per batch: four 16-byte loads in flight before the lookups that use them
+            const uint4* rd4 = reinterpret_cast<const uint4*>(rd);
+            for (int e16 = 0; e16 < (M >> 4); ++e16) {
+                uint4 x[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) x[u] = __ldg(rd4 + 4 * e16 + u);
+#pragma unroll
+                for (int u = 0; u < 4; ++u) { look(x[u].x); look(x[u].y); look(x[u].z); look(x[u].w); }
+            }
+        } else if (vec) {
             const uint4* rd4 = reinterpret_cast<const uint4*>(rd);
             for (int e4 = 0; e4 < (M >> 2); ++e4) {
                 const uint4 x = rd4[e4];
