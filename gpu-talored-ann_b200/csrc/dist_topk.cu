@@ -930,6 +930,22 @@ __global__ void __launch_bounds__(kThreads, kV)
                 __syncwarp();
             };
             constexpr int kSlices = kTN / 16;
+            // the stage goes back to the MMA as soon as its last slice is in registers (before
+            // that slice is scanned); 8-bit operands first re-arm it with the offset
+            auto release_stage = [&]() {
+                if constexpr (kU8) {
+                    uint32_t mg[32];
+#pragma unroll
+                    for (int i = 0; i < 32; ++i) mg[i] = kMagicU8;
+                    __syncwarp();
+                    tmem_st_32x32b_x32(tbase, mg);
+                    tmem_st_32x32b_x32(tbase + 32u, mg);
+                    tmem_st_wait();
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(ACC_EMPTY(b));
+            };
             __syncwarp();
             tmem_ld_32x32b_x16(tbase, va);
 #pragma unroll
@@ -940,6 +956,8 @@ __global__ void __launch_bounds__(kThreads, kV)
                     if (more) {
                         __syncwarp();
                         tmem_ld_32x32b_x16(tbase + static_cast<uint32_t>((c + 1) * 16), vb);
+                    } else {
+                        release_stage();
                     }
                     scan_slice(c, va, vb, more);
                 } else {
@@ -947,22 +965,12 @@ __global__ void __launch_bounds__(kThreads, kV)
                     if (more) {
                         __syncwarp();
                         tmem_ld_32x32b_x16(tbase + static_cast<uint32_t>((c + 1) * 16), va);
+                    } else {
+                        release_stage();
                     }
                     scan_slice(c, vb, va, more);
                 }
             }
-            if constexpr (kU8) {  // re-arm the stage with the offset for its next tile
-                uint32_t mg[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) mg[i] = kMagicU8;
-                __syncwarp();
-                tmem_st_32x32b_x32(tbase, mg);
-                tmem_st_32x32b_x32(tbase + 32u, mg);
-                tmem_st_wait();
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(ACC_EMPTY(b));
         }
         if (ok && __any_sync(0xffffffffu, nb > 0)) {
             n_pass += nb;
