@@ -210,10 +210,14 @@ def _csr_for(X, B, rng):
     return orc.build_csr(top2, B)
 
 
-@pytest.mark.parametrize("N,d,B,M", [(6000, 128, 8, 64), (3000, 128, 3, 16), (2500, 100, 5, 128)])
-def test_bucket_knn_u8_bit_exact(N, d, B, M):
+# u8 rows with M <= 64 run on kind::i8 operands, int8 rows and longer lists on bf16 operands
+@pytest.mark.parametrize("N,d,B,M,dtype", [(6000, 128, 8, 64, np.uint8), (3000, 128, 3, 16, np.uint8),
+                                           (2500, 100, 5, 128, np.uint8), (3000, 128, 4, 64, np.int8),
+                                           (2000, 40, 3, 32, np.uint8)])
+def test_bucket_knn_8bit_bit_exact(N, d, B, M, dtype):
     rng = np.random.default_rng(N)
-    X = np.clip(np.rint(mixture(rng, N, d, 15, 20.0, 0, 255)), 0, 255).astype(np.uint8)
+    X = np.clip(np.rint(mixture(rng, N, d, 15, 20.0, 0, 255)), 0, 255)
+    X = (X - 128 if dtype == np.int8 else X).astype(dtype)
     X[100:130] = X[99]  # exact duplicates: distance-0 ties broken by id
     off, mem, mrow = _csr_for(X.astype(np.float32), B, rng)
     gi, gd = gta.bucket_knn(dev(X), dev(mem), dev(off), M)
