@@ -1853,6 +1853,41 @@ int gta_bucket_knn_rows(const void* R, int32_t dtype, int64_t n, int32_t d, cons
     });
 }
 
+int gta_bucket_knn_rows_phased(const void* R, int32_t dtype, int64_t n, int32_t d, const int32_t* order,
+                               const int32_t* gid, const int64_t* offsets, const int32_t* partner, int32_t B, int32_t M,
+                               int32_t phase, const float* seed, int32_t* list_ids, float* list_dists, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(offsets && B >= 1 && M >= 1 && M <= 128 && n >= 0 && (phase == 1 || phase == 2) &&
+                        (n == 0 || (R && order && gid && partner && list_ids && list_dists)) &&
+                        (phase == 1 || n == 0 || seed),
+                    kInvalid, "gta_bucket_knn_rows_phased: bad argument");
+        if (n == 0) return;
+        cudaStream_t st = S(stream);
+        const int elem = knn_elem(dtype, d, M);
+        const bool seedable = dist_topk_seedable(elem, pad_dim(d, elem), M);
+        if (!seedable && phase == 2) return;  // phase 1 wrote every row
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        DevBuf<int32_t> gid_sorted(static_cast<size_t>(n), st);
+        gather_i32(gid, order, n, gid_sorted.get(), st);
+        KnnPhase ph;
+        std::vector<int64_t> split_h;
+        if (seedable) {
+            DevBuf<int64_t> split_d(static_cast<size_t>(B), st);
+            split_from_partner(partner, offsets, B, split_d.get(), st);
+            split_h.resize(static_cast<size_t>(B));
+            GTA_CUDA(cudaMemcpyAsync(split_h.data(), split_d.get(), sizeof(int64_t) * B, cudaMemcpyDeviceToHost, st));
+            GTA_CUDA(cudaStreamSynchronize(st));
+            ph.phase = phase; ph.split = split_h.data(); ph.partner = partner; ph.seed = seed; ph.seed_stride = 1;
+        }
+        bucket_knn_impl(R, dtype, n, d, order, offsets, B, M, list_ids, list_dists, err.get(), st, gid_sorted.get(), 0,
+                        -1, nullptr, ph);
+        check_device_error(err.get(), st, "gta_bucket_knn_rows_phased");
+    });
+}
+
 int gta_sanitize_rows(const int32_t* knn, int64_t n_rows, int64_t row0, int64_t n, int32_t m, uint32_t* out,
                       void* stream)
 {

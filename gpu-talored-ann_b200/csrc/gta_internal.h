@@ -159,6 +159,9 @@ void check_ids(const int32_t* ids, int64_t n, int32_t hi, int* err, cudaStream_t
 void build_memberships(const int32_t* top2, int64_t N, int32_t B, int32_t* members, int64_t* offsets,
                        int64_t* mem_row, int* err, cudaStream_t st, int64_t* split = nullptr,
                        int32_t* partner = nullptr);
+// split[b] = first of bucket b's grouped rows (offsets) whose partner is above b; the rows of a
+// bucket ascend by partner
+void split_from_partner(const int32_t* partner, const int64_t* offsets, int32_t B, int64_t* split, cudaStream_t st);
 // seed[p] = the M-th distance of point p's lower-bucket list (rows j0 .. j0 + n_rows of the
 // list buffer, +inf when that row is elsewhere)
 void seeds_from_lists(const float* list_d, const int64_t* mem_row, int64_t N, int M, int64_t j0, int64_t n_rows,

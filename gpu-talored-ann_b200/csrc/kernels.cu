@@ -634,6 +634,22 @@ __global__ void partner_kernel(const uint32_t* __restrict__ keys_sorted, int64_t
                                                                           : -1;
 }
 
+// split[b] = first grouped row of bucket b whose partner is above b (rows of a bucket ascend
+// by partner)
+__global__ void split_from_partner_kernel(const int32_t* __restrict__ partner, const int64_t* __restrict__ offsets,
+                                          int32_t B, int64_t* __restrict__ split)
+{
+    const int64_t b = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    int64_t lo = offsets[b], hi = offsets[b + 1];
+    while (lo < hi) {
+        const int64_t mid = (lo + hi) >> 1;
+        if (partner[mid] <= static_cast<int32_t>(b)) lo = mid + 1;
+        else hi = mid;
+    }
+    split[b] = lo;
+}
+
 __global__ void seeds_from_lists_kernel(const float* __restrict__ list_d, const int64_t* __restrict__ mem_row,
                                         int64_t N, int M, int64_t j0, int64_t n_rows, float* __restrict__ seed)
 {
@@ -1366,6 +1382,13 @@ void build_memberships(const int32_t* top2, int64_t N, int32_t B, int32_t* membe
         partner_kernel<<<blocks_for(n2, 256), 256, 0, st>>>(keys_out.get(), n2, B, partner);
         count_launches(1);
     }
+    GTA_CUDA(cudaGetLastError());
+}
+
+void split_from_partner(const int32_t* partner, const int64_t* offsets, int32_t B, int64_t* split, cudaStream_t st)
+{
+    split_from_partner_kernel<<<blocks_for(B, 256), 256, 0, st>>>(partner, offsets, B, split);
+    count_launches(1);
     GTA_CUDA(cudaGetLastError());
 }
 

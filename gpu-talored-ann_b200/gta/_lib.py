@@ -90,6 +90,7 @@ _SIGS = {
     "gta_centroid_means": [_P, _P, _I32, _I32, _P, _P],
     "gta_group_memberships": [_P, _P, _I64, _I32, _P, _P, _P],
     "gta_bucket_knn_rows": [_P, _I32, _I64, _I32, _P, _P, _P, _I32, _I32, _P, _P, _P],
+    "gta_bucket_knn_rows_phased": [_P, _I32, _I64, _I32, _P, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _P],
     "gta_sanitize_rows": [_P, _I64, _I64, _I64, _I32, _P, _P],
     "gta_prune_rows": [_P, _I64, _I32, _I32, _I64, _I64, _P, _I32, _P, _P],
     "gta_reverse_merge_rows": [_P, _I64, _I32, _I64, _I64, _P, _P],

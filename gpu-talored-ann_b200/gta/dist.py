@@ -21,7 +21,10 @@ come before rank r+1's).  The steps and their exchanges:
   4. Points to bucket owners (all-to-all of rows and (id, bucket, other) triples),
      grouped by (bucket, other) in arrival order: the membership order of the
      single-GPU build.
-  5. Per-bucket all-pairs top-M on the owner.
+  5. Per-bucket all-pairs top-M on the owner, in two passes: the rows whose bucket is
+     the lower of their point's two, then (after an all-reduce (min) of each point's
+     lower-list M-th distance by global id) the other rows, bounded by that distance
+     and skipping the points of the lower bucket; the merged lists are unchanged.
   6. Lists back to the points' owners (all-to-all), merged per point.
   7. CAGRA: sanitize the local rows, all-gather the id table, prune the local rows,
      all-gather the pruned graph, merge reverse edges into the local rows.
@@ -152,6 +155,13 @@ class CudaStages:
         L.check(self.L.gta_bucket_knn_rows(_p(R), _ELEM[R.dtype], n, R.shape[1], _p(order), _p(gid), _p(offsets),
                                            offsets.numel() - 1, M, _p(ids), _p(dd), self._st()))
         return ids, dd
+
+    def bucket_knn_rows_phased(self, R, order, gid, offsets, partner, M, phase, seed, lid, ldist):
+        """Rows of one phase into lid / ldist (see gta_bucket_knn_rows_phased)."""
+        n = R.shape[0]
+        L.check(self.L.gta_bucket_knn_rows_phased(_p(R), _ELEM[R.dtype], n, R.shape[1], _p(order), _p(gid),
+                                                  _p(offsets), _p(partner), offsets.numel() - 1, M, phase, _p(seed),
+                                                  _p(lid), _p(ldist), self._st()))
 
     def merge_memberships(self, lid, ldist, mem_row):
         n, M = mem_row.shape[0], lid.shape[1]
@@ -328,11 +338,24 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
     del rows, meta
     ph.mark("exchange_points")
 
-    # ---- 5. per-bucket top-M on the owner
+    # ---- 5. per-bucket top-M on the owner: first the rows whose bucket is the lower of their
+    # point's two, then the others, bounded by the point's lower-bucket list (its M-th distance,
+    # gathered by global id over the ranks) and skipping the points of that lower bucket
     gid_r = meta_r[:, 0].contiguous()
     order, offsets = st.group_memberships(meta_r[:, 1].contiguous(), meta_r[:, 2].contiguous(), B)
-    lid, ldist = st.bucket_knn_rows(R, order, gid_r, offsets, M)
-    del R
+    n_r = R.shape[0]
+    ol = order.long()
+    bucket_s = meta_r[:, 1][ol]
+    partner_s = meta_r[:, 2][ol].contiguous()
+    lid = torch.full((n_r, M), -1, dtype=torch.int32, device=dev)
+    ldist = torch.full((n_r, M), float("inf"), dtype=torch.float32, device=dev)
+    st.bucket_knn_rows_phased(R, order, gid_r, offsets, partner_s, M, 1, None, lid, ldist)
+    seed = torch.full((N,), float("inf"), dtype=torch.float32, device=dev)
+    lower = partner_s > bucket_s
+    seed[gid_r[ol][lower].long()] = ldist[lower, M - 1]
+    dist.all_reduce(seed, op=dist.ReduceOp.MIN, group=group)
+    st.bucket_knn_rows_phased(R, order, gid_r, offsets, partner_s, M, 2, seed, lid, ldist)
+    del R, seed
     ph.mark("bucket_knn")
 
     # ---- 6. lists back to the points' owners, merged per point

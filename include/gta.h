@@ -352,6 +352,20 @@ int gta_bucket_knn_rows(const void* R, int32_t dtype, int64_t n, int32_t d, cons
                         const int64_t* offsets, int32_t B, int32_t M, int32_t* list_ids, float* list_dists,
                         void* stream);
 
+/* gta_bucket_knn_rows in two passes (the sharded build's seeded higher-bucket rows).
+ * partner[j] is the other bucket of grouped row j (rows grouped by (bucket, partner) as
+ * gta_group_memberships orders them).  phase 1 writes the rows whose partner is above their
+ * bucket (the points' lower-bucket lists); phase 2 writes the others, each starting from the
+ * bound seed[gid] (by global id: the point's lower-bucket list's m-th distance, +inf when
+ * unknown) and skipping the columns whose partner equals the row's (points already in the lower
+ * list).  Merged with gta_merge_memberships, the lists equal those of gta_bucket_knn_rows.
+ * For shapes without seeded rows (f32 data, lists longer than 64) phase 1 writes every row and
+ * phase 2 none.  list_ids / list_dists: rows of the other phase are left as they are.
+ * Replaces the same interface as gta_bucket_knn_rows. */
+int gta_bucket_knn_rows_phased(const void* R, int32_t dtype, int64_t n, int32_t d, const int32_t* order,
+                               const int32_t* gid, const int64_t* offsets, const int32_t* partner, int32_t B, int32_t M,
+                               int32_t phase, const float* seed, int32_t* list_ids, float* list_dists, void* stream);
+
 /* gta_sanitize for rows [row0, row0 + n_rows) of an n-row graph (knn and out
  * hold only those rows). */
 int gta_sanitize_rows(const int32_t* knn, int64_t n_rows, int64_t row0, int64_t n, int32_t m, uint32_t* out,

@@ -82,6 +82,42 @@ class OracleStages:
         out = np.where(ids >= 0, g[np.maximum(ids, 0)], -1).astype(np.int32)
         return _t(out), _t(dd)
 
+    def bucket_knn_rows_phased(self, R, order, gid, offsets, partner, M, phase, seed, lid, ldist):
+        """Phase 1: the oracle's lists of the rows whose partner is above their bucket.  Phase 2:
+        the other rows restricted as the library restricts them (columns of the row's partner
+        bucket dropped, distance at most the point's seed, ties by received row as the oracle
+        breaks them), so the merged lists check the seeding argument too."""
+        Rn, o, g, off, part = _np(R), _np(order).astype(np.int64), _np(gid), _np(offsets), _np(partner)
+        n = o.shape[0]
+        if n == 0:
+            return
+        B = off.shape[0] - 1
+        bucket = np.repeat(np.arange(B), np.diff(off))
+        lower = part > bucket
+        if phase == 1:
+            ids, dd = orc.bucket_knn(Rn, off, o.astype(np.int32), M)
+            out = np.where(ids >= 0, g[np.maximum(ids, 0)], -1).astype(np.int32)
+            rows = torch.from_numpy(np.nonzero(lower)[0])
+            lid[rows] = torch.from_numpy(out[lower])
+            ldist[rows] = torch.from_numpy(dd[lower])
+            return
+        sd = _np(seed)
+        X = Rn.astype(np.float64)
+        for j in np.nonzero(~lower)[0]:
+            b = bucket[j]
+            cols = np.arange(off[b], off[b + 1])
+            cols = cols[(cols != j) & (part[cols] != part[j])]
+            dv = ((X[o[cols]] - X[o[j]]) ** 2).sum(1)
+            keep = dv <= sd[g[o[j]]]
+            cols, dv = cols[keep], dv[keep]
+            srt = np.lexsort((o[cols], dv))[:M]
+            row_i = np.full(M, -1, np.int32)
+            row_d = np.full(M, np.inf, np.float32)
+            row_i[:len(srt)] = g[o[cols[srt]]]
+            row_d[:len(srt)] = dv[srt]
+            lid[int(j)] = torch.from_numpy(row_i)
+            ldist[int(j)] = torch.from_numpy(row_d)
+
     def merge_memberships(self, lid, ldist, mem_row):
         ids, dd = orc.merge_memberships(_np(lid), _np(ldist), _np(mem_row))
         return _t(ids), _t(dd)
