@@ -52,6 +52,15 @@ def _peaks():
     return 6650.0, 1590.0, "fallback"
 
 
+def _compute_dtype(cfg) -> str:
+    """Operand type of the bucket distance kernel: u8 rows with lists of at most 64 run on
+    kind::i8 MMAs (int32 accumulation), other 8-bit rows on bf16, f32 rows on a tf32 screen
+    with an exact fp32 rerank."""
+    if cfg.dtype == "uint8" and cfg.knn_degree <= 64:
+        return "u8"
+    return "bf16" if cfg.dtype in ("uint8", "int8") else "tf32"
+
+
 # DRAM bytes (read + write) per algorithmic unit of a kernel, from one ncu capture of each
 # kernel on the C2 distribution (bucket distance kernel, u8 operands: N = 600 000; prune:
 # N = 400 000), scaled to a launch by its units (the traffic grows with the rows processed)
@@ -343,6 +352,9 @@ def main():
             achieved = per_launch_units / per_launch_s / 1e12
             roofline = {"kernel": dom, "bound": "tensor", "achieved": achieved, "peak": tflops, "unit": "TFLOP/s",
                         "frac": achieved / tflops, "peak_source": f"{peak_src} bf16 burst"}
+            if _compute_dtype(cfg) == "u8":
+                roofline["note"] = ("kind::i8 MMAs: operations per second against the measured bf16 burst "
+                                    "(no measured i8 peak; the nominal dense i8 rate is twice bf16)")
         else:
             achieved = per_launch_units / per_launch_s / 1e9
             roofline = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
@@ -502,7 +514,7 @@ def main():
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-                "vs_baseline": None, "dtype": "bf16" if cfg.dtype == "uint8" else "tf32",
+                "vs_baseline": None, "dtype": _compute_dtype(cfg),
                 "data": "synthetic (seeded Gaussian mixture)", "config": config, "roofline": roofline,
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
                 "clocks": clocks, "recall_at_32": recall, "search": search_q, "reference_bucketing": ref_bucketing, "bucket_skew": skew, "phases_ms_max_over_ranks": phases,
