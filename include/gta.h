@@ -74,9 +74,11 @@ typedef struct {
     int32_t out_on_device;  /* outputs (knn lists, centroids_out, top2_out) are device pointers */
     float* centroids_out;   /* optional B x d final centroids */
     int32_t* top2_out;      /* optional N x 2 bucket ids (nearest, second nearest) */
-    int64_t device_budget;  /* bytes the bucket kNN stage may hold at once (0 = 80% of free device
-                               memory); when the memberships' pool rows and lists exceed it, buckets
-                               are processed in ascending batches that fit, with the same result */
+    int64_t device_budget;  /* bytes the bucket kNN stage may hold at once (0: one pass when the
+                               stage needs at most a quarter of the device's memory, else 80% of the
+                               free device memory); when the memberships' pool rows and lists exceed
+                               it, buckets are processed in ascending batches that fit, with the
+                               same result */
 } gta_bucket_params;
 
 typedef struct {
