@@ -3,7 +3,8 @@
 //   bucket_reorder      compute_bucket_reorder (bucketDemo/buildBucket/src/bucket.cu:8356-8417):
 //                       new ids laid out bucket by bucket in processing order, points of one
 //                       bucket in ascending old id; inverse_perm[new] = old
-//   permute_rows        the inline dataset reorder of bucket2 round 1 (bucket.cu:9253-9403):
+//   permute_rows        the inline dataset reorder bucket2 does in its first build round
+//                       (bucket.cu:9253-9403):
 //                       row new of the output = row inverse_perm[new] of the input
 //   permute_graph       to_original: translate_graph_to_original_order /
 //                       translate_npy_to_original_order (translate_graph_ids.hpp:75-200):

@@ -1,7 +1,7 @@
 """Regenerate the golden fixtures in tests/golden/ from the REFERENCE's own code.
 
-Run in a container that holds the reference tree (default /root/reference,
-override with GTA_REFERENCE).  The fixtures are small .npz files committed to
+Run where the reference tree is present (its project root in GTA_REFERENCE,
+or the container's default location).  The fixtures are small .npz files committed to
 the repository, so the tests themselves never read the reference tree.
 
   * The reference's Python functions (bucketDemo/build_bucket.py,
