@@ -1,6 +1,8 @@
 """CPU checks of libgta: the shared library loads, exports every entry point
 declared in include/gta.h, and its host-only file I/O keeps the reference's
-byte layouts.  No compute entry point is called here (no GPU)."""
+byte layouts.  Compute entry points are called here only with arguments they reject before
+any device work (no GPU)."""
+import ctypes
 import os
 import re
 import subprocess
@@ -87,6 +89,18 @@ def test_file_errors(tmp_path):
     with pytest.raises(gta.GtaError) as e:
         gta.read_knn(str(tmp_path / "missing.bin"))
     assert e.value.code == L.GTA_EINVAL
+
+
+def test_phased_bucket_knn_rejects_bad_arguments_before_device_work():
+    """gta_bucket_knn_rows_phased takes phase 1 or 2, and phase 2 needs the seeds."""
+    f = L.lib().gta_bucket_knn_rows_phased
+    dummy = ctypes.c_void_p(16)  # never dereferenced: the checks come first
+    args = lambda phase, seed: (dummy, L.GTA_U8, 100, 16, dummy, dummy, dummy, dummy, 4, 8, phase, seed, dummy,
+                                dummy, ctypes.c_void_p(0))
+    assert f(*args(3, dummy)) == L.GTA_EINVAL
+    assert b"bad argument" in L.lib().gta_last_error()
+    assert f(*args(2, ctypes.c_void_p(0))) == L.GTA_EINVAL
+    assert f(*args(0, dummy)) == L.GTA_EINVAL
 
 
 def test_synthetic_generators_are_seeded():
