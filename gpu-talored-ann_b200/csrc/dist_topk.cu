@@ -23,9 +23,11 @@
 // and the lists in shared memory.
 //
 // Two modes:
-//   exact  (bf16 operands holding 8-bit integer data): every product and
-//          partial sum is an integer below 2^24, so s is exact; the kernel
-//          writes the final top-M (distance, id) lists directly.
+//   exact  (8-bit integer data: kind::i8 MMAs on the u8 rows themselves with
+//          int32 accumulation, or kind::f16 with bf16 operands for other 8-bit
+//          rows): every product and partial sum is an integer below 2^24, so s
+//          is exact; the kernel writes the final top-M (distance, id) lists
+//          directly.
 //   screen (f32 operands, kind::tf32): s is approximate with a proven error
 //          bound; the kernel keeps every column whose approximate s is within
 //          the bound of the running M-th, and rerank_kernel recomputes those

@@ -1,7 +1,7 @@
 """Regenerate the golden fixtures in tests/golden/ from the REFERENCE's own code.
 
-Run where the reference tree is present (its project root in GTA_REFERENCE,
-or the container's default location).  The fixtures are small .npz files committed to
+Run where the reference tree is present, with its project root in the
+GTA_REFERENCE environment variable (required).  The fixtures are small .npz files committed to
 the repository, so the tests themselves never read the reference tree.
 
   * The reference's Python functions (bucketDemo/build_bucket.py,
@@ -10,7 +10,7 @@ the repository, so the tests themselves never read the reference tree.
     (prune_windowed_core.hpp, edge_chunk_accumulator.hpp) runs through
     oracle/_ref/libgta_ref.so, compiled in place by oracle/Makefile.
 
-    python tests/golden/make_golden.py
+    GTA_REFERENCE=<reference root> python tests/golden/make_golden.py
 """
 from __future__ import annotations
 
@@ -22,7 +22,9 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("GTA_REFERENCE", "/root/reference")
+REF = os.environ.get("GTA_REFERENCE", "")
+if not REF or not os.path.isdir(os.path.join(REF, "bucketDemo")):
+    sys.exit("make_golden.py: set GTA_REFERENCE to the reference project root (the directory holding bucketDemo/)")
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.join(REF, "bucketDemo"))
 
@@ -150,6 +152,24 @@ def make_eval_fixture():
     np.savez_compressed(os.path.join(HERE, "eval_recall.npz"), **out)
 
 
+def make_occlusion_fixture():
+    """prune.py:8-83 prune_graph (the reference's Python occlusion prune) on an exact kNN graph
+    with -1 padding, self entries and out-of-range ids mixed in, with and without a degree cap."""
+    import prune as rp  # the reference's module
+
+    rng = np.random.default_rng(31)
+    X = _mixture(rng, 600, 12, 8, 0.3, -1.0, 1.0)
+    ids, _ = orc.exact_knn(X, np.arange(600), 20)
+    nb = ids.astype(np.int64)
+    nb[rng.random(nb.shape) < 0.05] = -1
+    nb[::11, 4] = np.arange(0, 600, 11)      # the row's own id
+    nb[::13, 7] = 600 + 5                    # beyond N
+    out = {"X": X, "neighbors": nb}
+    out["pruned"] = rp.prune_graph(X, nb, None)
+    out["pruned_k8"] = rp.prune_graph(X, nb, 8)
+    np.savez_compressed(os.path.join(HERE, "occlusion.npz"), **out)
+
+
 def make_reorder_fixture():
     """The reference's own bucket_order.hpp (processing order of a bucket graph) and
     translate_graph_ids.hpp (graph .bin and .npy back to the original id order), compiled
@@ -245,8 +265,9 @@ def make_cpp_fixtures():
 
 
 if __name__ == "__main__":
-    # `python make_golden.py [python] [cpp] [search] [eval] [reorder]`: the named fixture groups (default all)
-    want = set(sys.argv[1:]) or {"python", "cpp", "search", "eval", "reorder"}
+    # `python make_golden.py [python] [cpp] [search] [eval] [reorder] [occlusion]`: the named fixture groups
+    # (default all)
+    want = set(sys.argv[1:]) or {"python", "cpp", "search", "eval", "reorder", "occlusion"}
     orc.build()
     if "python" in want:
         make_python_fixtures()
@@ -258,6 +279,8 @@ if __name__ == "__main__":
         make_eval_fixture()
     if "reorder" in want:
         make_reorder_fixture()
+    if "occlusion" in want:
+        make_occlusion_fixture()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")
