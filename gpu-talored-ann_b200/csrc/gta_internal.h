@@ -134,6 +134,32 @@ struct DistTopkProblem {
 };
 
 void dist_topk(const DistTopkProblem& pr, cudaStream_t st);
+
+// Float-row per-bucket kNN (screen.cu): pool row j is dataset row ids[j] (X: n x d rows of
+// dtype, dense); each work item's A rows get their exact top-m_out (fp32 chain) over the item's
+// segment of pool rows (self excluded), written with output ids gid[].  A tensor-core screen
+// (fp16 parts of the scaled rows, `parts` = 2: hi + lo) keeps every column within a proven
+// margin of the row's M-th; an exact rerank over the dataset's rows picks the list.
+struct ScreenProblem {
+    const void* X = nullptr;
+    int dtype = 0;                  // GTA_F32 / GTA_U8 / GTA_I8 (include/gta.h)
+    int d = 0;
+    const int32_t* ids = nullptr;   // [n_rows] pool row -> dataset row
+    const int32_t* gid = nullptr;   // [n_rows] pool row -> output id
+    int64_t n_rows = 0;
+    const WorkItem* work = nullptr;
+    int n_work = 0;
+    int max_cols = 0;               // longest segment (at most 2^17)
+    int m_out = 0;
+    int parts = 2;
+    int32_t* out_ids = nullptr;     // [n_rows x m_out]
+    float* out_dists = nullptr;
+    int* err = nullptr;
+    const char* prof_name = "dist_topk_bucket";
+    double flops = 0.0;
+};
+void screen_knn(const ScreenProblem& pr, cudaStream_t st);
+int screen_list_len(int m);
 // true when dist_topk accepts seeded rows for this shape (exact data, two-CTA variant)
 bool dist_topk_seedable(int elem, int d_pad, int m_out);
 // true when 8-bit operand rows (kElemU8, rows padded to 128 bytes) run for this list length
@@ -250,7 +276,7 @@ void sanitize_rows(const int32_t* knn, int64_t n_rows, int64_t row0, int64_t N, 
 void prune_rows(const uint32_t* g, int64_t N, int M, int K, const int32_t* order, int64_t row0, int64_t n_rows,
                 uint32_t* out, int* err, cudaStream_t st);
 void reverse_merge_rows(const uint32_t* pruned, int64_t N, int K, int64_t row0, int64_t n_rows, uint32_t* out,
-                        cudaStream_t st);
+                        int* err, cudaStream_t st);
 void check_device_error(const int* err, cudaStream_t st, const char* what);
 
 }  // namespace gta

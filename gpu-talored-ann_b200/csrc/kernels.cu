@@ -1042,113 +1042,190 @@ __global__ void locality_keys_kernel(const int32_t* __restrict__ top2, int64_t N
 }
 
 // ---------------------------------------------------------------- reverse edges
-// Edges of the whole pruned graph (N x K, global ids); only destinations in
-// [lo, hi) are kept, at local index dst - lo.
-__global__ void rev_count_kernel(const uint32_t* __restrict__ pruned, int64_t NK, int64_t lo, int64_t hi,
-                                 unsigned long long* __restrict__ indeg)
+// The reverse list of destination j: the sources i with j in pruned(i), ordered by
+// (rank of j in row i, i) and capped at K (edge_chunk_accumulator.hpp:386-469
+// TopKReverseStore, :235-284 build_rank_ordered_csr).  One edge is one key
+// rank << src_bits | src, so ascending keys are exactly that order; the key is 32 bits
+// wide whenever bits(N - 1) + bits(K - 1) <= 32 (every configuration up to 2^27 rows at
+// K = 32), else 64 bits.
+
+__device__ __forceinline__ void report_error(int* err, int code)
 {
-    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (e >= NK) return;
-    const int64_t dst = pruned[e];
-    if (dst >= lo && dst < hi) atomicAdd(&indeg[dst - lo], 1ull);
+    if (err) atomicCAS(err, 0, code);
 }
 
+// One warp per source row of the whole pruned graph (N x K, global ids); destinations
+// in [lo, hi) are counted at local index dst - lo.  An id >= N is reported as
+// kDevBadIndex (the entry point returns GTA_EDATA) and dropped.
+__global__ void rev_count_kernel(const uint32_t* __restrict__ pruned, int64_t N, int K, int64_t lo, int64_t hi,
+                                 unsigned long long* __restrict__ indeg, int* __restrict__ err)
+{
+    const int lane = threadIdx.x & 31;
+    const int64_t src = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (src >= N) return;
+    for (int r = lane; r < K; r += 32) {
+        const int64_t dst = pruned[src * K + r];
+        if (dst >= N) {
+            report_error(err, kDevBadIndex);
+            continue;
+        }
+        if (dst >= lo && dst < hi) atomicAdd(&indeg[dst - lo], 1ull);
+    }
+}
+
+// Each edge's key into its destination's segment of the CSR (slot order within a
+// segment is arbitrary; the merge sorts it).
+template <typename KeyT>
 __global__ void rev_scatter_kernel(const uint32_t* __restrict__ pruned, int64_t N, int K, int64_t lo, int64_t hi,
-                                   const uint64_t* __restrict__ off, uint32_t* __restrict__ cursor,
-                                   uint64_t* __restrict__ keys)
+                                   int src_bits, const uint64_t* __restrict__ off, uint32_t* __restrict__ cursor,
+                                   KeyT* __restrict__ keys)
 {
-    const int64_t e = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (e >= N * K) return;
-    const int64_t dst = pruned[e];
-    if (dst < lo || dst >= hi) return;
-    const uint64_t src = static_cast<uint64_t>(e / K), rank = static_cast<uint64_t>(e % K);
-    const uint64_t pos = off[dst - lo] + atomicAdd(&cursor[dst - lo], 1u);
-    keys[pos] = (rank << 32) | src;
+    const int lane = threadIdx.x & 31;
+    const int64_t src = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    if (src >= N) return;
+    for (int r = lane; r < K; r += 32) {
+        const int64_t dst = pruned[src * K + r];
+        if (dst < lo || dst >= hi) continue;  // hi <= N: out-of-range ids were reported by the count
+        const uint64_t pos = off[dst - lo] + atomicAdd(&cursor[dst - lo], 1u);
+        keys[pos] = (static_cast<KeyT>(r) << src_bits) | static_cast<KeyT>(src);
+    }
 }
 
-constexpr int kRevWarps = 4;
-constexpr int kRevSort = 512;
-
-__global__ void __launch_bounds__(kRevWarps * 32)
-    rev_merge_kernel(const uint32_t* __restrict__ pruned, int64_t row0, int64_t N, int K,
-                     const uint64_t* __restrict__ off, const uint64_t* __restrict__ keys, uint32_t* __restrict__ out)
+// One compare-exchange stage of a warp-wide bitonic network over 32 R keys held as
+// v[r] = element 32 r + lane: partners at distance j, direction set by bit k.
+template <typename KeyT, int R>
+__device__ __forceinline__ void bitonic_stage(KeyT (&v)[R], int lane, int k, int j)
 {
-    __shared__ uint64_t s_keys[kRevWarps][kRevSort];
-    __shared__ uint32_t s_row[kRevWarps][kMaxM];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int e = 32 * r + lane;
+        const bool up = (e & k) == 0;
+        if (j >= 32) {
+            const int rp = r ^ (j >> 5);
+            if (rp > r) {
+                const KeyT a = v[r], b = v[rp];
+                const KeyT mn = a < b ? a : b, mx = a < b ? b : a;
+                v[r] = up ? mn : mx;
+                v[rp] = up ? mx : mn;
+            }
+        } else {
+            const KeyT o = __shfl_xor_sync(0xffffffffu, v[r], j);
+            const bool take_min = ((lane & j) == 0) == up;
+            v[r] = take_min ? (o < v[r] ? o : v[r]) : (o > v[r] ? o : v[r]);
+        }
+    }
+}
+
+template <typename KeyT, int R>
+__device__ __forceinline__ void warp_sort_keys(KeyT (&v)[R], int lane)
+{
+#pragma unroll
+    for (int k = 2; k <= 32 * R; k <<= 1)
+#pragma unroll
+        for (int j = k >> 1; j > 0; j >>= 1) bitonic_stage<KeyT, R>(v, lane, k, j);
+}
+
+// best <- the 32 R smallest of (best, c), both ascending: the element-wise minimum of
+// best and reversed c is bitonic and holds them; one merge pass sorts it.
+template <typename KeyT, int R>
+__device__ __forceinline__ void warp_merge_lowest(KeyT (&best)[R], const KeyT (&c)[R], int lane)
+{
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const KeyT t = __shfl_sync(0xffffffffu, c[R - 1 - r], 31 - lane);
+        best[r] = t < best[r] ? t : best[r];
+    }
+#pragma unroll
+    for (int j = 16 * R; j > 0; j >>= 1) bitonic_stage<KeyT, R>(best, lane, 32 * R, j);
+}
+
+constexpr int kRevWarps = 8;
+
+// One warp per destination j (rows [row0, row0 + n_rows) of the pruned graph):
+//  1. the min(len, K) smallest keys of j's segment, ascending, by a register bitonic
+//     sort of 32 R keys per chunk and a keep-lowest merge across chunks (K <= 32 R);
+//  2. the protected merge of edge_chunk_accumulator.hpp:471-494 merge_rank_ordered_into_row
+//     (sources inserted weakest first after the first K/2 forward edges, an id already in
+//     the row moved instead of repeated, the last entry dropped when the row is full), in
+//     its closed form: the first K/2 entries stay; then the reverse sources strongest first,
+//     each kept only if it is not among the first K/2 and not a repeat of a stronger one;
+//     then the remaining forward entries in order, less the first copy of every kept source;
+//     the row cut at K.  (Serial insertion is a move-to-front list of capacity K - K/2, whose
+//     final content is its distinct accesses by recency followed by what was never touched.)
+template <typename KeyT, int R>
+__global__ void __launch_bounds__(kRevWarps * 32)
+    rev_merge_kernel(const uint32_t* __restrict__ pruned, int64_t row0, int64_t n_rows, int K, int src_bits,
+                     const uint64_t* __restrict__ off, const KeyT* __restrict__ keys, uint32_t* __restrict__ out)
+{
+    __shared__ uint32_t s_src[kRevWarps][32 * R], s_row[kRevWarps][32 * R], s_out[kRevWarps][32 * R];
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
     const int64_t j = static_cast<int64_t>(blockIdx.x) * kRevWarps + w;
-    if (j >= N) return;
-    const uint64_t lo = off[j], hi = off[j + 1];
-    const int64_t len = static_cast<int64_t>(hi - lo);
-    uint64_t* sk = s_keys[w];
-    // the K smallest (rank, src) keys of this destination, ascending
-    int n_keep = 0;
-    if (len <= kRevSort) {
-        int np2 = 1;
-        while (np2 < len) np2 <<= 1;
-        for (int t = lane; t < np2; t += 32) sk[t] = t < len ? keys[lo + t] : ~0ull;
-        __syncwarp();
-        for (int k = 2; k <= np2; k <<= 1)
-            for (int jj = k >> 1; jj > 0; jj >>= 1) {
-                for (int t = lane; t < (np2 >> 1); t += 32) {
-                    const int i = 2 * jj * (t / jj) + (t % jj), l = i + jj;
-                    const bool up = (i & k) == 0;
-                    const uint64_t x = sk[i], y = sk[l];
-                    if ((x > y) == up) { sk[i] = y; sk[l] = x; }
-                }
-                __syncwarp();
-            }
-        n_keep = static_cast<int>(len < K ? len : static_cast<int64_t>(K));
-    } else {
-        for (int t = lane; t < kRevSort; t += 32) sk[t] = ~0ull;
-        __syncwarp();
-        for (int64_t c0 = 0; c0 < len; c0 += kRevSort / 2) {
-            for (int t = lane; t < kRevSort / 2; t += 32)
-                sk[kRevSort / 2 + t] = (c0 + t < len) ? keys[lo + c0 + t] : ~0ull;
-            __syncwarp();
-            for (int k = 2; k <= kRevSort; k <<= 1)
-                for (int jj = k >> 1; jj > 0; jj >>= 1) {
-                    for (int t = lane; t < (kRevSort >> 1); t += 32) {
-                        const int i = 2 * jj * (t / jj) + (t % jj), l = i + jj;
-                        const bool up = (i & k) == 0;
-                        const uint64_t x = sk[i], y = sk[l];
-                        if ((x > y) == up) { sk[i] = y; sk[l] = x; }
-                    }
-                    __syncwarp();
-                }
-        }
-        n_keep = K;
+    if (j >= n_rows) return;
+    const KeyT kNone = ~static_cast<KeyT>(0);
+    const uint64_t lo = off[j];
+    const int64_t len = static_cast<int64_t>(off[j + 1] - lo);
+    uint32_t* row = s_row[w];
+    uint32_t* sel = s_out[w];
+    for (int k = lane; k < K; k += 32) row[k] = pruned[(row0 + j) * K + k];
+    KeyT best[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+        const int64_t e = 32 * r + lane;
+        best[r] = e < len ? keys[lo + e] : kNone;
     }
-    // protected merge of the reverse sources, weakest first
-    for (int k = lane; k < K; k += 32) s_row[w][k] = pruned[(row0 + j) * K + k];
+    warp_sort_keys<KeyT, R>(best, lane);
+    for (int64_t c0 = 32 * R; c0 < len; c0 += 32 * R) {
+        KeyT c[R];
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+            const int64_t e = c0 + 32 * r + lane;
+            c[r] = e < len ? keys[lo + e] : kNone;
+        }
+        warp_sort_keys<KeyT, R>(c, lane);
+        warp_merge_lowest<KeyT, R>(best, c, lane);
+    }
+    const KeyT src_mask = (static_cast<KeyT>(1) << src_bits) - 1;
+#pragma unroll
+    for (int r = 0; r < R; ++r) s_src[w][32 * r + lane] = static_cast<uint32_t>(best[r] & src_mask);
     __syncwarp();
+    const int n_keep = static_cast<int>(len < K ? len : K);
     const int np = K / 2;
-    for (int t = n_keep - 1; t >= 0; --t) {
-        const uint32_t src = static_cast<uint32_t>(sk[t] & 0xffffffffu);
-        int pos = K;
-        for (int g0 = 0; g0 < K; g0 += 32) {
-            const int k = g0 + lane;
-            const unsigned m = __ballot_sync(0xffffffffu, k < K && s_row[w][k] == src);
-            if (m) { pos = g0 + __ffs(m) - 1; break; }
-        }
-        if (pos < np) continue;
-        const int ns = (pos == K) ? (K - np - 1) : (pos - np);
-        uint32_t nv[kMaxM / 32];
-#pragma unroll
-        for (int gi = 0; gi < kMaxM / 32; ++gi) {
-            const int k = gi * 32 + lane;
-            nv[gi] = 0;
-            if (k < K) nv[gi] = (k == np) ? src : ((k > np && k <= np + ns) ? s_row[w][k - 1] : s_row[w][k]);
-        }
-        __syncwarp();
-#pragma unroll
-        for (int gi = 0; gi < kMaxM / 32; ++gi) {
-            const int k = gi * 32 + lane;
-            if (k < K) s_row[w][k] = nv[gi];
+    const unsigned lt = (1u << lane) - 1u;
+    // reverse sources, strongest first: not protected, first occurrence
+    int nu = 0;
+    for (int g0 = 0; g0 < n_keep; g0 += 32) {
+        const int t = g0 + lane;
+        const uint32_t src = t < n_keep ? s_src[w][t] : kEmpty;
+        bool keep = t < n_keep;
+        for (int p = 0; p < np; ++p) keep &= row[p] != src;
+        for (int p = 0; p < g0; ++p) keep &= s_src[w][p] != src;
+        keep &= (__ffs(__match_any_sync(0xffffffffu, src)) - 1) == lane;
+        const unsigned b = __ballot_sync(0xffffffffu, keep);
+        const int pos = np + nu + __popc(b & lt);
+        if (keep && pos < K) sel[pos] = src;
+        nu += __popc(b);
+    }
+    __syncwarp();
+    if (nu < K - np) {
+        // the forward entries after the protected ones, less the first copy of each kept source
+        int nr = 0;
+        for (int g0 = np; g0 < K; g0 += 32) {
+            const int q = g0 + lane;
+            const uint32_t o = q < K ? row[q] : kEmpty;
+            bool in_sel = false;
+            for (int i = 0; i < nu; ++i) in_sel |= sel[np + i] == o;
+            bool first = true;
+            for (int p = np; p < g0; ++p) first &= row[p] != o;
+            first &= (__ffs(__match_any_sync(0xffffffffu, o)) - 1) == lane;
+            const bool keep = q < K && !(in_sel && first);
+            const unsigned b = __ballot_sync(0xffffffffu, keep);
+            const int pos = np + nu + nr + __popc(b & lt);
+            if (keep && pos < K) sel[pos] = o;
+            nr += __popc(b);
         }
         __syncwarp();
     }
-    for (int k = lane; k < K; k += 32) out[j * K + k] = s_row[w][k];
+    for (int k = lane; k < K; k += 32) out[j * K + k] = k < np ? row[k] : sel[k];
 }
 
 // ---------------------------------------------------------------- row sort by exact distance
@@ -1243,8 +1320,14 @@ void kmeanspp_init(const float* pool, const float* /*pool_norm*/, int64_t pool_n
         // pool rows resident in shared memory when they fit (d <= 200: about 200 KB per CTA)
         int resident = d <= 200 ? 1 : 0;
         size_t smem1 = sizeof(float) * static_cast<size_t>(d_pad) * (resident ? 1 + kKppCoopThreads : 1);
+        if (smem1 > 227 * 1024) {
+            // one centroid row alone does not fit either: the per-centroid launches below
+            resident = 0;
+            smem1 = sizeof(float) * static_cast<size_t>(d_pad);
+        }
+        // the attribute covers the layout chosen here (the non-resident one needs less)
         GTA_CUDA(cudaFuncSetAttribute(kpp_coop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(sizeof(float) * static_cast<size_t>(d_pad) * (1 + kKppCoopThreads))));
+                                      static_cast<int>(std::min<size_t>(smem1, 227 * 1024))));
         GTA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kpp_coop_kernel, kKppCoopThreads, smem1));
         if (resident && G > per_sm * n_sm) {
             resident = 0;
@@ -1474,34 +1557,104 @@ void locality_order(const int32_t* top2, int64_t N, int32_t B, int32_t* order, c
     GTA_CUDA(cudaGetLastError());
 }
 
-void reverse_merge(const uint32_t* pruned, int64_t N, int K, uint32_t* out, int* /*err*/, cudaStream_t st)
+namespace {
+
+int bits_for(uint64_t x) { return x ? 64 - __builtin_clzll(x) : 0; }
+
+// Where one reverse-edge merge keeps its scratch: in-degrees (u64, rows + 1), CSR offsets
+// (u64, rows + 1), cursors (u32, rows), edge keys (N * K keys of key_bytes) and the scan's
+// temporary storage.
+struct RevScratch {
+    unsigned long long* indeg;
+    uint64_t* off;
+    uint32_t* cursor;
+    void* keys;
+    void* scan_tmp;
+    size_t scan_bytes;
+};
+
+// bytes of one edge key: 4 when rank and source fit together in 32 bits
+int rev_key_bytes(int64_t N, int K)
 {
-    GTA_REQUIRE(K >= 1 && K <= kMaxM, kInvalid, "reverse: K must be in [1, 128]");
-    const int64_t NK = N * K;
-    ProfScope prof("reverse", 32.0 * K * static_cast<double>(N), st);
-    DevBuf<unsigned long long> indeg(static_cast<size_t>(N) + 1, st);
-    DevBuf<uint32_t> cursor(static_cast<size_t>(N), st);
-    DevBuf<uint64_t> off(static_cast<size_t>(N) + 1, st), keys(static_cast<size_t>(NK), st);
-    GTA_CUDA(cudaMemsetAsync(indeg.get(), 0, sizeof(unsigned long long) * (N + 1), st));
-    GTA_CUDA(cudaMemsetAsync(cursor.get(), 0, sizeof(uint32_t) * N, st));
-    rev_count_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, NK, 0, N, indeg.get());
-    count_launches(1);
+    return std::max(1, bits_for(static_cast<uint64_t>(N - 1))) + bits_for(static_cast<uint64_t>(K - 1)) <= 32 ? 4 : 8;
+}
+
+size_t rev_scan_bytes(int64_t n_rows)
+{
     size_t tmp = 0;
-    GTA_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tmp, indeg.get(), off.get(), static_cast<int>(N + 1), st));
-    DevBuf<uint8_t> tbuf(tmp, st);
-    GTA_CUDA(cub::DeviceScan::ExclusiveSum(tbuf.get(), tmp, indeg.get(), off.get(), static_cast<int>(N + 1), st));
-    rev_scatter_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, N, K, 0, N, off.get(), cursor.get(), keys.get());
+    GTA_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tmp, static_cast<unsigned long long*>(nullptr),
+                                           static_cast<uint64_t*>(nullptr), static_cast<int>(n_rows + 1)));
+    return tmp;
+}
+
+template <typename KeyT>
+void rev_scatter_merge(const uint32_t* pruned, int64_t N, int K, int64_t lo, int64_t n_rows, int src_bits,
+                       const RevScratch& s, uint32_t* out, cudaStream_t st)
+{
+    KeyT* keys = static_cast<KeyT*>(s.keys);
+    rev_scatter_kernel<KeyT><<<blocks_for(N, 8), 256, 0, st>>>(pruned, N, K, lo, lo + n_rows, src_bits, s.off,
+                                                               s.cursor, keys);
+    const unsigned grid = blocks_for(n_rows, kRevWarps);
+    if (K <= 32)
+        rev_merge_kernel<KeyT, 1><<<grid, kRevWarps * 32, 0, st>>>(pruned, lo, n_rows, K, src_bits, s.off, keys, out);
+    else if (K <= 64)
+        rev_merge_kernel<KeyT, 2><<<grid, kRevWarps * 32, 0, st>>>(pruned, lo, n_rows, K, src_bits, s.off, keys, out);
+    else
+        rev_merge_kernel<KeyT, 4><<<grid, kRevWarps * 32, 0, st>>>(pruned, lo, n_rows, K, src_bits, s.off, keys, out);
+    count_launches(2);
+}
+
+// Reverse-edge merge of the destinations [lo, lo + n_rows) of the pruned graph (N x K,
+// global ids) into out (n_rows x K): in-degree count (ids >= N reported in *err), offsets
+// by an exclusive scan, keys scattered into each destination's segment, one warp per
+// destination for its K smallest keys and the protected merge.
+void reverse_merge_core(const uint32_t* pruned, int64_t N, int K, int64_t lo, int64_t n_rows, uint32_t* out,
+                        const RevScratch& s, int* err, cudaStream_t st)
+{
+    const int src_bits = std::max(1, bits_for(static_cast<uint64_t>(N - 1)));
+    GTA_CUDA(cudaMemsetAsync(s.indeg, 0, sizeof(unsigned long long) * (n_rows + 1), st));
+    GTA_CUDA(cudaMemsetAsync(s.cursor, 0, sizeof(uint32_t) * n_rows, st));
+    rev_count_kernel<<<blocks_for(N, 8), 256, 0, st>>>(pruned, N, K, lo, lo + n_rows, s.indeg, err);
     count_launches(1);
-    rev_merge_kernel<<<blocks_for(N, kRevWarps), kRevWarps * 32, 0, st>>>(pruned, 0, N, K, off.get(), keys.get(), out);
-    count_launches(1);
+    size_t tmp = s.scan_bytes;
+    GTA_CUDA(cub::DeviceScan::ExclusiveSum(s.scan_tmp, tmp, s.indeg, s.off, static_cast<int>(n_rows + 1), st));
+    if (rev_key_bytes(N, K) == 4)
+        rev_scatter_merge<uint32_t>(pruned, N, K, lo, n_rows, src_bits, s, out, st);
+    else
+        rev_scatter_merge<unsigned long long>(pruned, N, K, lo, n_rows, src_bits, s, out, st);
     GTA_CUDA(cudaGetLastError());
+}
+
+// the same merge with its scratch from the call's workspace
+void reverse_merge_ws(const uint32_t* pruned, int64_t N, int K, int64_t lo, int64_t n_rows, uint32_t* out, int* err,
+                      cudaStream_t st)
+{
+    const size_t scan_bytes = rev_scan_bytes(n_rows);
+    DevBuf<unsigned long long> indeg(static_cast<size_t>(n_rows) + 1, st);
+    DevBuf<uint64_t> off(static_cast<size_t>(n_rows) + 1, st);
+    DevBuf<uint32_t> cursor(static_cast<size_t>(n_rows), st);
+    // every edge of the graph may point into the range: keys for all of them
+    DevBuf<uint8_t> keys(static_cast<size_t>(N) * K * rev_key_bytes(N, K), st);
+    DevBuf<uint8_t> scan(scan_bytes, st);
+    const RevScratch s{indeg.get(), off.get(), cursor.get(), keys.get(), scan.get(), scan_bytes};
+    reverse_merge_core(pruned, N, K, lo, n_rows, out, s, err, st);
+}
+
+}  // namespace
+
+void reverse_merge(const uint32_t* pruned, int64_t N, int K, uint32_t* out, int* err, cudaStream_t st)
+{
+    GTA_REQUIRE(N >= 1 && K >= 1 && K <= kMaxM, kInvalid, "reverse: need n >= 1 and K in [1, 128]");
+    ProfScope prof("reverse", 32.0 * K * static_cast<double>(N), st);
+    reverse_merge_ws(pruned, N, K, 0, N, out, err, st);
 }
 
 // ---------------------------------------------------------------- reverse-edge merge without allocation
 // Scratch of gta_reverse_merge_noalloc: one file-scope device array, resident on
 // every GPU that loads the library until the process exits.  Layout (each region
 // 256-byte aligned): in-degrees (u64, rows + 1), offsets (u64, rows + 1),
-// cursors (u32, rows), edge keys (u64, rows * K), scan temporary storage.
+// cursors (u32, rows), edge keys (up to 8 bytes each, edges), scan temporary
+// storage, and the call's device error word.
 namespace {
 constexpr int64_t kNoAllocMaxRows = 1ll << 17;
 constexpr int64_t kNoAllocMaxEdges = 1ll << 21;
@@ -1512,26 +1665,19 @@ constexpr size_t kNoAllocOffOff = kNoAllocIndegOff + align256(sizeof(unsigned lo
 constexpr size_t kNoAllocCursorOff = kNoAllocOffOff + align256(sizeof(uint64_t) * (kNoAllocMaxRows + 1));
 constexpr size_t kNoAllocKeysOff = kNoAllocCursorOff + align256(sizeof(uint32_t) * kNoAllocMaxRows);
 constexpr size_t kNoAllocScanOff = kNoAllocKeysOff + align256(sizeof(uint64_t) * kNoAllocMaxEdges);
-constexpr size_t kNoAllocBytes = kNoAllocScanOff + kNoAllocScanBytes;
+constexpr size_t kNoAllocErrOff = kNoAllocScanOff + kNoAllocScanBytes;
+constexpr size_t kNoAllocBytes = kNoAllocErrOff + 256;
 
 static __device__ __align__(256) unsigned char g_rev_scratch[kNoAllocBytes];
 
-std::mutex g_noalloc_mu;
-std::vector<std::pair<int, unsigned char*>> g_noalloc_addr;  // device -> address of g_rev_scratch there
-
-// Device address of the scratch array on the current device.  The host-side
-// name g_rev_scratch is only a stand-in, so the address is looked up once per
-// device (with that device current) and cached.
+// Device address of the scratch array in the current context.  The host-side name
+// g_rev_scratch is only a stand-in, so the address is looked up with the caller's
+// device current, on every call (a cached address would go stale after a device
+// reset or in another context of the same device).
 unsigned char* noalloc_scratch()
 {
-    int dev = 0;
-    GTA_CUDA(cudaGetDevice(&dev));
-    std::lock_guard<std::mutex> g(g_noalloc_mu);
-    for (const auto& e : g_noalloc_addr)
-        if (e.first == dev) return e.second;
     void* ptr = nullptr;
     GTA_CUDA(cudaGetSymbolAddress(&ptr, g_rev_scratch));
-    g_noalloc_addr.push_back({dev, static_cast<unsigned char*>(ptr)});
     return static_cast<unsigned char*>(ptr);
 }
 }  // namespace
@@ -1548,26 +1694,21 @@ void reverse_merge_noalloc(const uint32_t* pruned, int64_t N, int K, uint32_t* o
                     std::to_string(kNoAllocMaxRows) + " rows and " + std::to_string(kNoAllocMaxEdges) +
                     " edges); use gta_reverse_merge");
     unsigned char* base = noalloc_scratch();
-    unsigned long long* indeg = reinterpret_cast<unsigned long long*>(base + kNoAllocIndegOff);
-    uint64_t* off = reinterpret_cast<uint64_t*>(base + kNoAllocOffOff);
-    uint32_t* cursor = reinterpret_cast<uint32_t*>(base + kNoAllocCursorOff);
-    uint64_t* keys = reinterpret_cast<uint64_t*>(base + kNoAllocKeysOff);
-    void* scan_tmp = base + kNoAllocScanOff;
-    const int64_t NK = N * K;
-    size_t tmp = 0;
-    GTA_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tmp, indeg, off, static_cast<int>(N + 1), st));
-    GTA_REQUIRE(tmp <= kNoAllocScanBytes, kInvalid, "reverse_merge_noalloc: scan scratch exceeds its reserve");
-    // the array keeps the previous call's contents: counters start from zero
-    GTA_CUDA(cudaMemsetAsync(indeg, 0, sizeof(unsigned long long) * (N + 1), st));
-    GTA_CUDA(cudaMemsetAsync(cursor, 0, sizeof(uint32_t) * N, st));
-    rev_count_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, NK, 0, N, indeg);
-    count_launches(1);
-    GTA_CUDA(cub::DeviceScan::ExclusiveSum(scan_tmp, tmp, indeg, off, static_cast<int>(N + 1), st));
-    rev_scatter_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, N, K, 0, N, off, cursor, keys);
-    count_launches(1);
-    rev_merge_kernel<<<blocks_for(N, kRevWarps), kRevWarps * 32, 0, st>>>(pruned, 0, N, K, off, keys, out);
-    count_launches(1);
-    GTA_CUDA(cudaGetLastError());
+    const size_t scan_bytes = rev_scan_bytes(N);
+    GTA_REQUIRE(scan_bytes <= kNoAllocScanBytes, kInvalid, "reverse_merge_noalloc: scan scratch exceeds its reserve");
+    const RevScratch s{reinterpret_cast<unsigned long long*>(base + kNoAllocIndegOff),
+                       reinterpret_cast<uint64_t*>(base + kNoAllocOffOff),
+                       reinterpret_cast<uint32_t*>(base + kNoAllocCursorOff), base + kNoAllocKeysOff,
+                       base + kNoAllocScanOff, kNoAllocScanBytes};
+    // the array keeps the previous call's contents: the error word (and, in the core, the
+    // counters) start from zero
+    int* err = reinterpret_cast<int*>(base + kNoAllocErrOff);
+    GTA_CUDA(cudaMemsetAsync(err, 0, sizeof(int), st));
+    reverse_merge_core(pruned, N, K, 0, N, out, s, err, st);
+    int h = 0;
+    GTA_CUDA(cudaMemcpyAsync(&h, err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    GTA_CUDA(cudaStreamSynchronize(st));
+    GTA_REQUIRE(h == 0, kData, "reverse_merge_noalloc: a neighbour id is outside [0, n)");
 }
 
 // ============================================================================ shard variants
@@ -1671,29 +1812,12 @@ void prune_rows(const uint32_t* g, int64_t N, int M, int K, const int32_t* order
 }
 
 void reverse_merge_rows(const uint32_t* pruned, int64_t N, int K, int64_t row0, int64_t n_rows, uint32_t* out,
-                        cudaStream_t st)
+                        int* err, cudaStream_t st)
 {
-    GTA_REQUIRE(K >= 1 && K <= kMaxM && row0 >= 0 && row0 + n_rows <= N, kInvalid, "reverse: bad row range or K");
-    const int64_t NK = N * K, lo = row0, hi = row0 + n_rows;
+    GTA_REQUIRE(K >= 1 && K <= kMaxM && row0 >= 0 && n_rows >= 1 && row0 + n_rows <= N, kInvalid,
+                "reverse: bad row range or K");
     ProfScope prof("reverse", 32.0 * K * static_cast<double>(n_rows), st);
-    DevBuf<unsigned long long> indeg(static_cast<size_t>(n_rows) + 1, st);
-    DevBuf<uint32_t> cursor(static_cast<size_t>(n_rows), st);
-    // every edge of the graph may point into this range: size the keys for all of them
-    DevBuf<uint64_t> off(static_cast<size_t>(n_rows) + 1, st), keys(static_cast<size_t>(NK), st);
-    GTA_CUDA(cudaMemsetAsync(indeg.get(), 0, sizeof(unsigned long long) * (n_rows + 1), st));
-    GTA_CUDA(cudaMemsetAsync(cursor.get(), 0, sizeof(uint32_t) * n_rows, st));
-    rev_count_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, NK, lo, hi, indeg.get());
-    count_launches(1);
-    size_t tmp = 0;
-    GTA_CUDA(cub::DeviceScan::ExclusiveSum(nullptr, tmp, indeg.get(), off.get(), static_cast<int>(n_rows + 1), st));
-    DevBuf<uint8_t> tbuf(tmp, st);
-    GTA_CUDA(cub::DeviceScan::ExclusiveSum(tbuf.get(), tmp, indeg.get(), off.get(), static_cast<int>(n_rows + 1), st));
-    rev_scatter_kernel<<<blocks_for(NK, 256), 256, 0, st>>>(pruned, N, K, lo, hi, off.get(), cursor.get(), keys.get());
-    count_launches(1);
-    rev_merge_kernel<<<blocks_for(n_rows, kRevWarps), kRevWarps * 32, 0, st>>>(pruned, lo, n_rows, K, off.get(),
-                                                                                keys.get(), out);
-    count_launches(1);
-    GTA_CUDA(cudaGetLastError());
+    reverse_merge_ws(pruned, N, K, row0, n_rows, out, err, st);
 }
 
 void sort_rows_l2(const float* X, int d, int d_pad, const int32_t* knn, int64_t N, int M, int32_t* out, cudaStream_t st)

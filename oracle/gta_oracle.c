@@ -54,6 +54,13 @@ static inline float exact_l2(const float* a, const float* b, int d)
 
 ORC_API float orc_exact_l2(const float* a, const float* b, int d) { return exact_l2(a, b, d); }
 
+/* exact distances of n (row, row) pairs of X (n x d): out[i] = exact_l2(X[a[i]], X[b[i]]) */
+ORC_API void orc_pair_l2(const float* X, int32_t d, const int32_t* a, const int32_t* b, int64_t n, float* out)
+{
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) out[i] = exact_l2(X + (int64_t)a[i] * d, X + (int64_t)b[i] * d, d);
+}
+
 typedef struct { float d; int32_t id; } orc_pair;
 
 static int pair_less(orc_pair x, orc_pair y) { return x.d < y.d || (x.d == y.d && x.id < y.id); }

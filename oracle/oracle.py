@@ -67,6 +67,8 @@ def lib():
         L.orc_merge_rev_row.argtypes = [_P, _P, ctypes.c_uint32, ctypes.c_uint32]
         L.orc_exact_l2.argtypes = [_P, _P, _I32]
         L.orc_exact_l2.restype = ctypes.c_float
+        L.orc_pair_l2.argtypes = [_P, _I32, _P, _P, _I64, _P]
+        L.orc_pair_l2.restype = None
         L.orc_num_threads.restype = ctypes.c_int
         L.orc_bucket_reorder.argtypes = [_P, _I64, _I32, _I32, _P, _P, _P]
         L.orc_bucket_reorder.restype = _I64
@@ -149,6 +151,17 @@ def default_sample_size(N: int) -> int:
 # --------------------------------------------------------------------------
 # stages
 # --------------------------------------------------------------------------
+def pair_l2(X, a, b) -> np.ndarray:
+    """Exact fp32 squared distances of the row pairs (X[a[i]], X[b[i]]): the ascending-dimension
+    fmaf chain of the reference's exact rerank (bucket.cu:4350-4363 s6_dot_rows)."""
+    X = _f32(X)
+    a = np.ascontiguousarray(a, dtype=np.int32).reshape(-1)
+    b = np.ascontiguousarray(b, dtype=np.int32).reshape(-1)
+    out = np.empty(a.shape[0], np.float32)
+    lib().orc_pair_l2(_p(X), X.shape[1], _p(a), _p(b), a.shape[0], _p(out))
+    return out
+
+
 def topk_assign(X, C, k: int):
     X = _f32(X); C = _f32(C)
     N, d = X.shape
@@ -214,6 +227,31 @@ def bucket_knn(X, offsets, members, M: int):
     lib().orc_bucket_knn(_p(X), X.shape[0], X.shape[1], _p(offsets), _p(members), offsets.shape[0] - 1, M,
                          _p(ids), _p(dist))
     return ids, dist
+
+
+def point_lists(X, top2, points, M: int):
+    """The oracle pipeline's merged kNN list of each of ``points`` (a sample), without building
+    every bucket: the point's exact top-M within each of its two buckets (fp32 chain, ties by id,
+    itself excluded: bucket_knn's rule), merged with the lower bucket's list as the running side
+    (merge_memberships' rule, bucket.cu:5025-5059).  Returns (ids, dists) [len(points) x M]."""
+    X = _f32(X)
+    top2 = np.asarray(top2, dtype=np.int64)
+    points = np.asarray(points, dtype=np.int64)
+    flat = top2.reshape(-1)
+    order = np.argsort(flat, kind="stable")
+    starts = np.searchsorted(flat[order], np.arange(flat.max() + 2))
+    P = len(points)
+    lists = [(np.full((P, M), -1, np.int32), np.full((P, M), np.inf, np.float32)) for _ in range(2)]
+    for i, p in enumerate(points):
+        bs = np.sort(top2[p])
+        for way, b in enumerate(bs):
+            mem = (order[starts[b]:starts[b + 1]] // top2.shape[1]).astype(np.int64)
+            mem = mem[mem != p]
+            dist = pair_l2(X, np.full(mem.shape[0], p), mem)
+            sel = np.lexsort((mem, dist))[:M]
+            lists[way][0][i, :sel.size] = mem[sel]
+            lists[way][1][i, :sel.size] = dist[sel]
+    return merge_lists(lists[0][0], lists[0][1], lists[1][0], lists[1][1])
 
 
 def merge_lists(run_n, run_d, new_n, new_d):

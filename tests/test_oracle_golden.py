@@ -221,3 +221,19 @@ def test_bucket_reorder_known_answer():
     # a duplicate in inverse_perm is refused
     _, bad = orc.permute_graph(np.zeros((3, 1), np.int32), np.array([0, 0, 1], np.uint32), True, False)
     assert bad == -1
+
+
+def test_point_lists_equal_the_full_pipeline():
+    """oracle.point_lists (a sample of points: per-bucket top-M + the resident merge rule) gives
+    exactly the rows of the full bucket_knn + merge_memberships pipeline, ties included."""
+    rng = np.random.default_rng(3)
+    X = np.rint(rng.normal(0, 4, (2500, 16))).astype(np.float32)   # integer rows: many exact ties
+    C = X[rng.choice(2500, 10, replace=False)] + 0.25
+    top2, _ = orc.topk_assign(X, C, 2)
+    offs, mem, mrow = orc.build_csr(top2, 10)
+    li, ld = orc.bucket_knn(X, offs, mem, 24)
+    ki, kd = orc.merge_memberships(li, ld, mrow)
+    pts = rng.choice(2500, 300, replace=False)
+    pi, pd = orc.point_lists(X, top2, pts, 24)
+    np.testing.assert_array_equal(pi, ki[pts])
+    np.testing.assert_array_equal(pd, kd[pts])
