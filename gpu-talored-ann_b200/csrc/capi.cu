@@ -405,7 +405,8 @@ void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* 
         ScreenProblem sp;
         sp.X = X; sp.dtype = dtype; sp.d = d;
         sp.ids = members + j0; sp.gid = (gid ? gid : members) + j0; sp.n_rows = n_mem;
-        sp.work = work.get(); sp.n_work = static_cast<int>(wl.size()); sp.max_cols = static_cast<int>(max_nb);
+        sp.work = work.get(); sp.work_host = wl; sp.n_work = static_cast<int>(wl.size());
+        sp.max_cols = static_cast<int>(max_nb);
         sp.m_out = M; sp.parts = 2; sp.out_ids = list_ids; sp.out_dists = list_dists; sp.err = err;
         sp.prof_name = "dist_topk_bucket"; sp.flops = flops;
         screen_knn(sp, st);

@@ -147,7 +147,8 @@ struct ScreenProblem {
     const int32_t* ids = nullptr;   // [n_rows] pool row -> dataset row
     const int32_t* gid = nullptr;   // [n_rows] pool row -> output id
     int64_t n_rows = 0;
-    const WorkItem* work = nullptr;
+    const WorkItem* work = nullptr;   // device copy of work_host
+    std::vector<WorkItem> work_host;  // one item per 128 A rows of a segment (self_col0: its first row's column)
     int n_work = 0;
     int max_cols = 0;               // longest segment (at most 2^17)
     int m_out = 0;

@@ -7,10 +7,13 @@
 // s6_scan_kernel: fp16 screen with a strict error bound; :4604 s6_rerank_kernel: exact
 // rerank):
 //
-//   screen_kernel   per A row, every B column whose approximate distance lies within a proven
-//                   margin of the row's M-th smallest (the candidates);
-//   rerank          the candidates' exact distances and the top-M (dist_topk.cu rerank_kernel,
-//                   reading the dataset's own rows).
+//   screen_kernel   per A row, the kL smallest approximate distances (kL = 128 or 256 > M),
+//                   keeping every B column within a proven margin of the row's M-th;
+//   rerank_kernel   exact distances of the first M keys, whose largest (E) bounds the row's
+//                   exact M-th; then of the keys whose approximate distance may lie within E
+//                   plus the one-sided error bound; the top-M.  Only when even the list's last
+//                   key may lie within that bound (columns beyond the list may qualify) is the
+//                   row's whole segment rescanned exactly (rescan_kernel).
 //
 // Operands: each row x is scaled by a power of two S (exact; S = 2^floor(log2(2^15 / max ||x||)),
 // so every coordinate stays below 2^15) and split into fp16 parts hi = rn(S x) and
@@ -68,8 +71,8 @@ struct ScreenArgs {
     int32_t stages;
     int32_t col_bits;          // 16 or 17
     float mc1, mc2;            // margin = mc1 |a| bmax + mc2 (|a| + bmax)^2 (unscaled)
-    int32_t* cand_cols;        // [a_total x L] segment columns
-    int32_t* cand_n;           // [a_total] candidates, -1: rescan the row exactly
+    int32_t* cand_cols;        // [a_total x L] the row's list: keys (code << col_bits | column), ascending
+    int32_t* cand_n;           // [a_total] keys in the row's list
     unsigned long long* stats; // optional: the library's eight profile counters
     int* err;
     uint32_t buf_off, pn_off, bar_off;
@@ -508,18 +511,9 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
             nb = 0;
         }
         if (ok) {
-            // candidates: the list's keys whose distance may lie within the bound (sorted: a prefix);
-            // overflow when keys beyond the list may as well
-            const uint32_t km = tmem_ld1(tl + static_cast<uint32_t>(p.m_sel - 1));
-            const float bnd = km == kSEmpty ? INFINITY : decode(km >> p.col_bits) + margin;
-            const uint32_t kl = tmem_ld1(tl + static_cast<uint32_t>(kL - 1));
-            auto may_pass = [&](uint32_t key) {
-                const uint32_t code = key >> p.col_bits;
-                return key != kSEmpty && (code == 0u || decode(code - 1u) < bnd);
-            };
-            const bool overflow = may_pass(kl);
-            int nc = 0;
-            bool open = true;
+            // the row's list (ascending keys, sentinels last) for the rerank, which decides from
+            // exact distances which keys it needs and whether columns beyond the list may qualify
+            int nv = 0;
 #pragma unroll 1
             for (int blk = 0; blk < kL; blk += 32) {
                 uint32_t c[32];
@@ -527,12 +521,11 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
                 tmem_ld_wait_regs32(c);
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    open = open && may_pass(c[j]);
-                    if (row_ok && !overflow && open) p.cand_cols[arow * kL + blk + j] = static_cast<int32_t>(c[j] & col_mask);
-                    nc += open ? 1 : 0;
+                    if (row_ok && c[j] != kSEmpty) p.cand_cols[arow * kL + blk + j] = static_cast<int32_t>(c[j]);
+                    nv += c[j] != kSEmpty ? 1 : 0;
                 }
             }
-            if (row_ok) p.cand_n[arow] = overflow ? -1 : nc;
+            if (row_ok) p.cand_n[arow] = nv;
             if (st_on) {
                 if (row_ok) {
                     atomicAdd(&p.stats[0], static_cast<unsigned long long>(n_pass));
@@ -560,20 +553,19 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
 }
 
 // ---- operand rows: scaled fp16 parts ---------------------------------------------------
-// One warp per pool row: row j of the pool is dataset row ids[j]; out row j holds its hi part
-// (d16 fp16, zero past d) and, with two parts, its lo part after d16 elements.
-template <typename T>
-__global__ void split_rows_kernel(const T* __restrict__ X, int d, const int32_t* __restrict__ ids, int64_t n,
+// One warp per pool row (f32, pitch dp): out row j holds its hi part (d16 fp16, zero past d) and,
+// with two parts, its lo part after d16 elements.
+__global__ void split_rows_kernel(const float* __restrict__ pool, int dp, int d, int64_t n,
                                   const float* __restrict__ maxnorm, __half* __restrict__ out, int d16, int parts)
 {
     const int lane = threadIdx.x & 31;
     const int64_t j = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
     if (j >= n) return;
     const float sc = screen_scale(*maxnorm);
-    const T* x = X + static_cast<int64_t>(ids[j]) * d;
+    const float* x = pool + j * dp;
     __half* o = out + j * static_cast<int64_t>(parts) * d16;
     for (int i = lane; i < d16; i += 32) {
-        const float v = i < d ? to_f32(x[i]) * sc : 0.0f;
+        const float v = i < d ? x[i] * sc : 0.0f;
         const __half h = __float2half_rn(v);
         o[i] = h;
         if (parts == 2) o[d16 + i] = __float2half_rn(v - __half2float(h));
@@ -581,54 +573,57 @@ __global__ void split_rows_kernel(const T* __restrict__ X, int d, const int32_t*
 }
 
 // ---- exact rerank ------------------------------------------------------------------------
-// One warp per A row of a work item: the row's candidates (or, after an overflow, every column
-// of its segment but itself) with the exact fp32 chain over the dataset's own rows, as
-// (distance, output id) keys; a bitonic sort; the first m_out written.  Two candidates per lane
-// at a time (independent chains), rows read four elements per load where aligned.
+// The exact distances run on a bucket-contiguous f32 copy of the pool rows (pitch dp, a
+// multiple of 32, zero past d: the extra terms add +0 to the chain and change nothing).  A warp
+// evaluates 32 candidates at a time, one per lane: each 32-dimension chunk of the 32 candidate
+// rows is loaded coalesced (a 128-byte row segment per load instruction, the next chunk already
+// in flight while this one is consumed), transposed through shared memory, and every lane
+// continues its own ascending fmaf chain over the chunk.
 constexpr int kRrWarps = 4;
 constexpr int kRrKeys = 512;
+constexpr int kRrRows = 8;        // A rows per rerank work item (few rows in flight per bucket)
+constexpr int kTileLd = 33;       // padded leading dimension of the transposed chunk
 
-template <typename T>
-__device__ __forceinline__ float chain_dist(const float* __restrict__ a, const T* __restrict__ b, int d)
+// exact fp32 chain (ascending dimensions) of the query row q_s (shared memory, dp floats) against
+// pool row `brow` of this lane (-1: none, the result is ignored); warp-collective
+__device__ __forceinline__ float tile_chain(const float* __restrict__ q_s, const float* __restrict__ pool, int dp,
+                                            int64_t brow, float* __restrict__ tile, int lane)
 {
     float acc = 0.0f;
-    for (int i = 0; i < d; ++i) {
-        const float t = a[i] - to_f32(b[i]);
-        acc = fmaf(t, t, acc);
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+        const int64_t br = __shfl_sync(0xffffffffu, brow, j);
+        v[j] = br >= 0 ? __ldg(pool + br * dp + lane) : 0.0f;
+    }
+    for (int k0 = 0; k0 < dp; k0 += 32) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) tile[lane * kTileLd + j] = v[j];
+        __syncwarp();
+        if (k0 + 32 < dp) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+                const int64_t br = __shfl_sync(0xffffffffu, brow, j);
+                v[j] = br >= 0 ? __ldg(pool + br * dp + k0 + 32 + lane) : 0.0f;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < 32; ++k) {
+            const float t = q_s[k0 + k] - tile[k * kTileLd + lane];
+            acc = fmaf(t, t, acc);
+        }
+        __syncwarp();
     }
     return acc;
-}
-
-// two independent chains (same order of operations as chain_dist for each)
-__device__ __forceinline__ void chain_dist2_f4(const float* __restrict__ a, const float* __restrict__ b0,
-                                               const float* __restrict__ b1, int d, float& o0, float& o1)
-{
-    float acc0 = 0.0f, acc1 = 0.0f;
-    const float4* a4 = reinterpret_cast<const float4*>(a);
-    const float4* p0 = reinterpret_cast<const float4*>(b0);
-    const float4* p1 = reinterpret_cast<const float4*>(b1);
-    for (int i = 0; i < d / 4; ++i) {
-        const float4 x = a4[i], u = __ldg(p0 + i), v = __ldg(p1 + i);
-        float t;
-        t = x.x - u.x; acc0 = fmaf(t, t, acc0);
-        t = x.x - v.x; acc1 = fmaf(t, t, acc1);
-        t = x.y - u.y; acc0 = fmaf(t, t, acc0);
-        t = x.y - v.y; acc1 = fmaf(t, t, acc1);
-        t = x.z - u.z; acc0 = fmaf(t, t, acc0);
-        t = x.z - v.z; acc1 = fmaf(t, t, acc1);
-        t = x.w - u.w; acc0 = fmaf(t, t, acc0);
-        t = x.w - v.w; acc1 = fmaf(t, t, acc1);
-    }
-    o0 = acc0;
-    o1 = acc1;
 }
 
 __device__ __forceinline__ void rr_sort(uint64_t* keys, int n, int lane)
 {
     for (int k = 2; k <= n; k <<= 1) {
         for (int j = k >> 1; j > 0; j >>= 1) {
+            const int lj = __ffs(j) - 1;
             for (int t = lane; t < (n >> 1); t += 32) {
-                const int i = 2 * j * (t / j) + (t % j);
+                const int i = ((t >> lj) << (lj + 1)) + (t & (j - 1));
                 const int l = i + j;
                 const bool up = (i & k) == 0;
                 const uint64_t x = keys[i], y = keys[l];
@@ -643,91 +638,172 @@ __device__ __forceinline__ void rr_sort(uint64_t* keys, int n, int lane)
 }
 
 struct RerankX {
-    const WorkItem* work;
-    const void* X;
-    int d;
-    int vec4;                  // float rows, d % 4 == 0, 16-byte aligned rows: four-element loads
-    const int32_t* ids;        // pool row -> dataset row
+    const WorkItem* work;      // groups of up to kRrRows A rows (self_col0: the first row's column)
+    const float* pool;         // f32 pool rows, pitch dp
+    int dp;
     const int32_t* gid;        // pool row -> output id
-    const int32_t* cand_cols;
+    const int32_t* cand_cols;  // the screen's row lists (keys), by pool row
     const int32_t* cand_n;
+    const float* norm;         // exact ||x||^2 of the pool rows
+    const float* maxnorm;      // device scalar: max ||x|| (the screen's scale and margin)
+    float mc1, mc2;            // the screen's margin coefficients (two-sided)
+    int col_bits;
     int L;
     int m_out;
     int32_t* out_ids;
     float* out_dists;
+    unsigned long long* stats;  // optional: [exact candidates, rows rescanned, rows]
+    int2* rescan;               // [rows] (A row, work item) of the rows whose segment is rescanned
+    unsigned* n_rescan;         // device counter of those rows
 };
 
-template <typename T>
-__global__ void __launch_bounds__(kRrWarps * 32) rerank_x_kernel(const RerankX p)
+__device__ __forceinline__ void write_list(const RerankX& p, int64_t arow, const uint64_t* keys, int n_sorted, int lane)
+{
+    for (int j = lane; j < p.m_out; j += 32) {
+        const uint64_t key = j < n_sorted ? keys[j] : ~0ull;
+        const bool v = key != ~0ull;
+        p.out_ids[arow * p.m_out + j] = v ? static_cast<int32_t>(static_cast<uint32_t>(key)) : -1;
+        p.out_dists[arow * p.m_out + j] = v ? key2f(static_cast<uint32_t>(key >> 32)) : INFINITY;
+    }
+}
+
+__global__ void __launch_bounds__(kRrWarps * 32) rerank_kernel(const RerankX p)
 {
     extern __shared__ uint8_t sm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t* keys = reinterpret_cast<uint64_t*>(sm) + warp * kRrKeys;
-    const int d4 = (p.d + 3) / 4 * 4;
-    float* arow_s = reinterpret_cast<float*>(sm + kRrWarps * kRrKeys * sizeof(uint64_t)) + warp * d4;
+    float* tile = reinterpret_cast<float*>(sm + kRrWarps * kRrKeys * sizeof(uint64_t)) + warp * 32 * kTileLd;
+    float* q_s = reinterpret_cast<float*>(sm + kRrWarps * kRrKeys * sizeof(uint64_t) + kRrWarps * 32 * kTileLd * 4) +
+                 warp * p.dp;
     const WorkItem w = p.work[blockIdx.x];
-    const T* X = static_cast<const T*>(p.X);
-    auto brow_ptr = [&](int c) { return X + static_cast<int64_t>(p.ids[static_cast<int64_t>(w.b_row0) + c]) * p.d; };
-    auto out_id = [&](int c) { return static_cast<uint32_t>(p.gid[static_cast<int64_t>(w.b_row0) + c]); };
+    const float bm = *p.maxnorm;
+    const float sc = screen_scale(bm);
+    const float inv_s2 = 1.0f / (sc * sc);   // a power of two: exact
+    const int shift = p.col_bits - 1;
+    const uint32_t col_mask = (1u << p.col_bits) - 1u;
+    // lower bound of a key's approximate distance (unscaled): decode(code - 1) < approx
+    auto approx_lo = [&](uint32_t key) {
+        const uint32_t code = key >> p.col_bits;
+        return code == 0u ? -INFINITY : __uint_as_float((code - 1u) << shift) * inv_s2;
+    };
     for (int r = warp; r < w.a_rows; r += kRrWarps) {
         const int64_t arow = static_cast<int64_t>(w.a_row0) + r;
-        const T* xa = X + static_cast<int64_t>(p.ids[arow]) * p.d;
-        for (int i = lane; i < d4; i += 32) arow_s[i] = i < p.d ? to_f32(xa[i]) : 0.0f;
+        for (int i = lane; i < p.dp; i += 32) q_s[i] = p.pool[arow * p.dp + i];
         __syncwarp();
-        const int n = p.cand_n[arow];
-        const int self = (w.self_col0 >= 0) ? w.self_col0 + r : -1;
-        int n_sorted = 0;
-        if (n >= 0) {
-            int np2 = 1;
-            while (np2 < n) np2 <<= 1;
-            const int32_t* cc = p.cand_cols + arow * p.L;
-            for (int j0 = 0; j0 < np2; j0 += 64) {
-                const int ja = j0 + lane, jb = j0 + 32 + lane;
-                const bool va = ja < n, vb = jb < n;
-                const int ca = va ? cc[ja] : 0, cb = vb ? cc[jb] : 0;
-                float da = 0.0f, db = 0.0f;
-                if constexpr (sizeof(T) == 4) {
-                    if (p.vec4 && va && vb) {
-                        chain_dist2_f4(arow_s, reinterpret_cast<const float*>(brow_ptr(ca)),
-                                       reinterpret_cast<const float*>(brow_ptr(cb)), p.d, da, db);
-                    } else {
-                        if (va) da = chain_dist(arow_s, brow_ptr(ca), p.d);
-                        if (vb) db = chain_dist(arow_s, brow_ptr(cb), p.d);
-                    }
-                } else {
-                    if (va) da = chain_dist(arow_s, brow_ptr(ca), p.d);
-                    if (vb) db = chain_dist(arow_s, brow_ptr(cb), p.d);
+        const int nv = p.cand_n[arow];
+        const uint32_t* kl = reinterpret_cast<const uint32_t*>(p.cand_cols) + arow * p.L;
+        // exact keys of list positions [j_lo, j_hi) into keys[j]; returns the largest distance
+        auto exact_range = [&](int j_lo, int j_hi) {
+            float mx = -INFINITY;
+            for (int j0 = j_lo; j0 < j_hi; j0 += 32) {
+                const int j = j0 + lane;
+                const int c = j < j_hi ? static_cast<int>(kl[j] & col_mask) : -1;
+                const int64_t brow = c >= 0 ? static_cast<int64_t>(w.b_row0) + c : -1;
+                const float dd = tile_chain(q_s, p.pool, p.dp, brow, tile, lane);
+                if (c >= 0) {
+                    keys[j] = (static_cast<uint64_t>(f2key(dd)) << 32) | static_cast<uint32_t>(p.gid[brow]);
+                    mx = fmaxf(mx, dd);
                 }
-                if (ja < np2) keys[ja] = va ? (static_cast<uint64_t>(f2key(da)) << 32) | out_id(ca) : ~0ull;
-                if (jb < np2) keys[jb] = vb ? (static_cast<uint64_t>(f2key(db)) << 32) | out_id(cb) : ~0ull;
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+            return mx;
+        };
+        // 1. the first M keys: their largest exact distance bounds the row's exact M-th
+        const int n1 = nv < p.m_out ? nv : p.m_out;
+        const float e_m = exact_range(0, n1);
+        int n_tot = n1;
+        bool rescan = false;
+        if (nv > n1) {
+            // 2. the keys whose approximate distance may lie within e_m plus the one-sided error
+            const float an = sqrtf(fmaxf(p.norm[arow], 0.0f));
+            const float bound = e_m + 0.5f * (p.mc1 * an * bm + p.mc2 * (an + bm) * (an + bm));
+            int n2 = nv - n1;
+            for (int j0 = n1; j0 < nv; j0 += 32) {
+                const int j = j0 + lane;
+                const unsigned fail = __ballot_sync(0xffffffffu, j < nv && !(approx_lo(kl[j]) <= bound));
+                if (fail) {
+                    n2 = j0 + __ffs(fail) - 1 - n1;
+                    break;
+                }
+            }
+            exact_range(n1, n1 + n2);
+            n_tot = n1 + n2;
+            // 3. every key of a full list passed: columns beyond the list may lie within the bound
+            rescan = nv == p.L && n_tot == p.L;
+        }
+        if (p.stats && lane == 0) {
+            atomicAdd(&p.stats[0], static_cast<unsigned long long>(n_tot));
+            atomicAdd(&p.stats[1], rescan ? 1ull : 0ull);
+            atomicAdd(&p.stats[2], 1ull);
+        }
+        if (rescan) {
+            // the whole segment, exactly, by rescan_kernel (a CTA per row, the columns split over its warps)
+            if (lane == 0) {
+                const unsigned slot = atomicAdd(p.n_rescan, 1u);
+                p.rescan[slot] = make_int2(static_cast<int>(arow), static_cast<int>(blockIdx.x));
             }
             __syncwarp();
-            rr_sort(keys, np2, lane);
-            n_sorted = np2;
-        } else {
-            // exact rescan of the whole segment: keys[0, 256) the best so far, [256, 512) the next chunk
-            for (int j = lane; j < kRrKeys; j += 32) keys[j] = ~0ull;
+            continue;
+        }
+        int np2 = 1;
+        while (np2 < n_tot) np2 <<= 1;
+        for (int j = n_tot + lane; j < np2; j += 32) keys[j] = ~0ull;
+        __syncwarp();
+        rr_sort(keys, np2, lane);
+        write_list(p, arow, keys, np2, lane);
+        __syncwarp();
+    }
+}
+
+// Exact top-m_out of whole segments for the rows the rerank could not settle from its list:
+// persistent CTAs walk the rescan list; per row, each of the 8 warps keeps the 256 best
+// (distance, id) keys of its share of the columns (a bitonic sort of 512 keys per 256 columns),
+// then warp 0 merges the warps' lists.
+constexpr int kRsWarps = 8;
+
+__global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p)
+{
+    extern __shared__ uint8_t sm[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    uint64_t* all = reinterpret_cast<uint64_t*>(sm);
+    uint64_t* keys = all + warp * kRrKeys;
+    float* tile = reinterpret_cast<float*>(sm + kRsWarps * kRrKeys * sizeof(uint64_t)) + warp * 32 * kTileLd;
+    float* q_s = reinterpret_cast<float*>(sm + kRsWarps * kRrKeys * sizeof(uint64_t) + kRsWarps * 32 * kTileLd * 4);
+    const unsigned n = *p.n_rescan;
+    for (unsigned i = blockIdx.x; i < n; i += gridDim.x) {
+        const int2 e = p.rescan[i];
+        const int64_t arow = e.x;
+        const WorkItem w = p.work[e.y];
+        const int self = w.self_col0 + static_cast<int>(arow - w.a_row0);
+        __syncthreads();
+        for (int j = threadIdx.x; j < p.dp; j += blockDim.x) q_s[j] = p.pool[arow * p.dp + j];
+        for (int j = lane; j < kRrKeys; j += 32) keys[j] = ~0ull;
+        __syncthreads();
+        // this warp's columns: chunks of 256 starting at 256 * warp, strided by the CTA
+        for (int c0 = 256 * warp; c0 < w.b_rows; c0 += 256 * kRsWarps) {
+            for (int j = 0; j < kRrKeys / 2; j += 32) {
+                const int c = c0 + j + lane;
+                const bool ok = c < w.b_rows && c != self;
+                const int64_t brow = ok ? static_cast<int64_t>(w.b_row0) + c : -1;
+                const float dd = tile_chain(q_s, p.pool, p.dp, brow, tile, lane);
+                keys[kRrKeys / 2 + j + lane] =
+                    ok ? (static_cast<uint64_t>(f2key(dd)) << 32) | static_cast<uint32_t>(p.gid[brow]) : ~0ull;
+            }
             __syncwarp();
-            for (int c0 = 0; c0 < w.b_rows; c0 += kRrKeys / 2) {
-                for (int j = lane; j < kRrKeys / 2; j += 32) {
-                    const int c = c0 + j;
-                    uint64_t key = ~0ull;
-                    if (c < w.b_rows && c != self)
-                        key = (static_cast<uint64_t>(f2key(chain_dist(arow_s, brow_ptr(c), p.d))) << 32) | out_id(c);
-                    keys[kRrKeys / 2 + j] = key;
-                }
+            rr_sort(keys, kRrKeys, lane);
+        }
+        __syncthreads();
+        if (warp == 0) {
+            // the warps' best m_out each (their lists are sorted) -> the row's best m_out
+            for (int q = 1; q < kRsWarps; ++q) {
+                const uint64_t* other = all + q * kRrKeys;
+                for (int j = lane; j < kRrKeys / 2; j += 32) keys[kRrKeys / 2 + j] = j < p.m_out ? other[j] : ~0ull;
                 __syncwarp();
                 rr_sort(keys, kRrKeys, lane);
             }
-            n_sorted = kRrKeys / 2;
+            write_list(p, arow, keys, kRrKeys / 2, lane);
         }
-        for (int j = lane; j < p.m_out; j += 32) {
-            const uint64_t key = j < n_sorted ? keys[j] : ~0ull;
-            const bool v = key != ~0ull;
-            p.out_ids[arow * p.m_out + j] = v ? static_cast<int32_t>(static_cast<uint32_t>(key)) : -1;
-            p.out_dists[arow * p.m_out + j] = v ? key2f(static_cast<uint32_t>(key >> 32)) : INFINITY;
-        }
-        __syncwarp();
     }
 }
 
@@ -802,25 +878,20 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     const int d16 = (pr.d + 63) / 64 * 64;
     ScreenPlan pl;
     GTA_REQUIRE(screen_plan(split, pl), kInvalid, "screen: shared memory plan failed");
-    // exact squared norms, the scale's source (max ||x||) and the scaled fp16 operand rows
-    DevBuf<float> norm(static_cast<size_t>(pr.n_rows), st), bmax(1, st);
+    // the pool's rows as f32 (bucket-contiguous, pitch dp, zero past d) with their exact squared
+    // norms, the scale's source (max ||x||) and the scaled fp16 operand rows
+    const int dp = (pr.d + 31) / 32 * 32;
+    DevBuf<float> fpool(static_cast<size_t>(pr.n_rows) * dp, st), norm(static_cast<size_t>(pr.n_rows), st);
+    DevBuf<float> bmax(1, st);
     DevBuf<__half> rows(static_cast<size_t>(pr.n_rows) * pr.parts * d16, st);
     {
         const double in_bytes = static_cast<double>(pr.n_rows) * pr.d * (pr.dtype == GTA_F32 ? 4.0 : 1.0);
-        ProfScope prof("screen_rows", 2.0 * in_bytes + static_cast<double>(pr.n_rows) * 2.0 * pr.parts * d16, st);
-        convert_rows(pr.X, pr.dtype, pr.d, pr.ids, pr.n_rows, nullptr, kElemF32, pr.d, norm.get(), st);
+        ProfScope prof("screen_rows", in_bytes + static_cast<double>(pr.n_rows) * (8.0 * dp + 2.0 * pr.parts * d16), st);
+        convert_rows(pr.X, pr.dtype, pr.d, pr.ids, pr.n_rows, fpool.get(), kElemF32, dp, norm.get(), st);
         max_sqrt(norm.get(), pr.n_rows, bmax.get(), st);
         const int wpb = 8;
-        const unsigned grid = static_cast<unsigned>((pr.n_rows + wpb - 1) / wpb);
-        if (pr.dtype == GTA_F32)
-            split_rows_kernel<float><<<grid, wpb * 32, 0, st>>>(static_cast<const float*>(pr.X), pr.d, pr.ids,
-                                                                pr.n_rows, bmax.get(), rows.get(), d16, pr.parts);
-        else if (pr.dtype == GTA_U8)
-            split_rows_kernel<uint8_t><<<grid, wpb * 32, 0, st>>>(static_cast<const uint8_t*>(pr.X), pr.d, pr.ids,
-                                                                  pr.n_rows, bmax.get(), rows.get(), d16, pr.parts);
-        else
-            split_rows_kernel<int8_t><<<grid, wpb * 32, 0, st>>>(static_cast<const int8_t*>(pr.X), pr.d, pr.ids,
-                                                                 pr.n_rows, bmax.get(), rows.get(), d16, pr.parts);
+        split_rows_kernel<<<static_cast<unsigned>((pr.n_rows + wpb - 1) / wpb), wpb * 32, 0, st>>>(
+            fpool.get(), dp, pr.d, pr.n_rows, bmax.get(), rows.get(), d16, pr.parts);
         count_launches(1);
         GTA_CUDA(cudaGetLastError());
     }
@@ -871,34 +942,61 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
             else launch_screen<256, false>(tm, a, pr.n_work, pl.total, st);
         }
     }
+    // the rerank's work: groups of kRrRows rows of the same items, in the same (bucket) order
+    std::vector<WorkItem> groups;
+    groups.reserve(static_cast<size_t>(pr.n_rows / kRrRows + pr.n_work));
+    for (const WorkItem& it : pr.work_host) {
+        for (int g = 0; g < it.a_rows; g += kRrRows)
+            groups.push_back(WorkItem{it.a_row0 + g, std::min(kRrRows, it.a_rows - g), it.b_row0, it.b_rows,
+                                      it.self_col0 + g, 0, 0, 0});
+    }
+    DevBuf<WorkItem> gwork(groups.size(), st);
+    // pageable source: the copy is staged before cudaMemcpyAsync returns
+    GTA_CUDA(cudaMemcpyAsync(gwork.get(), groups.data(), sizeof(WorkItem) * groups.size(), cudaMemcpyHostToDevice, st));
     RerankX r{};
-    r.work = pr.work;
-    r.X = pr.X;
-    r.d = pr.d;
-    r.vec4 = (pr.dtype == GTA_F32 && pr.d % 4 == 0 && (reinterpret_cast<uintptr_t>(pr.X) & 15) == 0) ? 1 : 0;
-    r.ids = pr.ids;
+    r.work = gwork.get();
+    r.pool = fpool.get();
+    r.dp = dp;
     r.gid = pr.gid;
     r.cand_cols = cand_cols.get();
     r.cand_n = cand_n.get();
+    r.norm = norm.get();
+    r.maxnorm = bmax.get();
+    r.mc1 = a.mc1;
+    r.mc2 = a.mc2;
+    r.col_bits = a.col_bits;
     r.L = L;
     r.m_out = pr.m_out;
     r.out_ids = pr.out_ids;
     r.out_dists = pr.out_dists;
-    const size_t smem = kRrWarps * kRrKeys * sizeof(uint64_t) + kRrWarps * static_cast<size_t>((pr.d + 3) / 4 * 4) * 4;
-    GTA_REQUIRE(smem <= kSSmemMax, kInvalid, "rerank: dimension too large");
-    ProfScope prof("rerank", 0.0, st);
-    if (pr.dtype == GTA_F32) {
-        GTA_CUDA(cudaFuncSetAttribute(rerank_x_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-        rerank_x_kernel<float><<<pr.n_work, kRrWarps * 32, smem, st>>>(r);
-    } else if (pr.dtype == GTA_U8) {
-        GTA_CUDA(cudaFuncSetAttribute(rerank_x_kernel<uint8_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-        rerank_x_kernel<uint8_t><<<pr.n_work, kRrWarps * 32, smem, st>>>(r);
-    } else {
-        GTA_CUDA(cudaFuncSetAttribute(rerank_x_kernel<int8_t>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-        rerank_x_kernel<int8_t><<<pr.n_work, kRrWarps * 32, smem, st>>>(r);
+    DevBuf<int2> rescan(static_cast<size_t>(pr.n_rows), st);
+    DevBuf<unsigned> n_rescan(1, st);
+    GTA_CUDA(cudaMemsetAsync(n_rescan.get(), 0, sizeof(unsigned), st));
+    r.rescan = rescan.get();
+    r.n_rescan = n_rescan.get();
+    {
+        const size_t smem = kRrWarps * (kRrKeys * sizeof(uint64_t) + 32 * kTileLd * 4 + static_cast<size_t>(dp) * 4);
+        GTA_REQUIRE(smem <= kSSmemMax, kInvalid, "rerank: dimension too large");
+        ProfScope prof("rerank", 0.0, st);
+        r.stats = prof.counters(8);
+        GTA_CUDA(cudaFuncSetAttribute(rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+        rerank_kernel<<<static_cast<unsigned>(groups.size()), kRrWarps * 32, smem, st>>>(r);
+        count_launches(1);
+        GTA_CUDA(cudaGetLastError());
     }
-    count_launches(1);
-    GTA_CUDA(cudaGetLastError());
+    {
+        // the deferred whole-segment rescans: persistent CTAs over the device-side list
+        const size_t smem = kRsWarps * (kRrKeys * sizeof(uint64_t) + 32 * kTileLd * 4) + static_cast<size_t>(dp) * 4;
+        GTA_REQUIRE(smem <= kSSmemMax, kInvalid, "rescan: dimension too large");
+        int dev = 0, n_sm = 0;
+        GTA_CUDA(cudaGetDevice(&dev));
+        GTA_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+        ProfScope prof("rescan", 0.0, st);
+        GTA_CUDA(cudaFuncSetAttribute(rescan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+        rescan_kernel<<<static_cast<unsigned>(std::max(1, n_sm) * 2), kRsWarps * 32, smem, st>>>(r);
+        count_launches(1);
+        GTA_CUDA(cudaGetLastError());
+    }
 }
 
 }  // namespace gta
