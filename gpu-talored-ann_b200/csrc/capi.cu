@@ -383,32 +383,22 @@ void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* 
     if (n_mem == 0) return;
     GTA_REQUIRE(n_mem < (1ll << 31), kInvalid, "bucket_knn: too many memberships on one device");
     const int elem = knn_elem(dtype, d, M);
-    int64_t max_nb = 0;
-    for (int b = b_lo; b < b_hi; ++b) max_nb = std::max<int64_t>(max_nb, off[b + 1] - off[b]);
-    if (elem == kElemF32 && ph.phase == 0 && max_nb <= (1 << 17)) {
-        // float rows: tensor-core screen on fp16 parts + exact rerank over the dataset's rows
-        std::vector<WorkItem> wl;
-        double flops = 0.0;
+    if (elem == kElemF32 && ph.phase == 0) {
+        // float rows: tensor-core screen on fp16 parts + exact rerank over the pool's f32 rows
         std::vector<int> order(static_cast<size_t>(b_hi - b_lo));
         std::iota(order.begin(), order.end(), b_lo);
         std::stable_sort(order.begin(), order.end(),
                          [&](int a, int b) { return off[a + 1] - off[a] > off[b + 1] - off[b]; });
-        for (int b : order) {
-            const int64_t lo = off[b] - j0, nb = off[b + 1] - off[b];
-            for (int64_t t = 0; t < nb; t += 128)
-                wl.push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, nb - t)),
-                                      static_cast<int32_t>(lo), static_cast<int32_t>(nb), static_cast<int32_t>(t), 0, 0, 0});
-            flops += 2.0 * static_cast<double>(nb) * static_cast<double>(nb) * d;
-        }
-        if (wl.empty()) return;
-        auto work = upload(wl, st);
         ScreenProblem sp;
         sp.X = X; sp.dtype = dtype; sp.d = d;
         sp.ids = members + j0; sp.gid = (gid ? gid : members) + j0; sp.n_rows = n_mem;
-        sp.work = work.get(); sp.work_host = wl; sp.n_work = static_cast<int>(wl.size());
-        sp.max_cols = static_cast<int>(max_nb);
+        for (int b : order) {
+            if (off[b + 1] == off[b]) continue;
+            sp.seg_lo.push_back(off[b] - j0);
+            sp.seg_n.push_back(off[b + 1] - off[b]);
+        }
         sp.m_out = M; sp.parts = 2; sp.out_ids = list_ids; sp.out_dists = list_dists; sp.err = err;
-        sp.prof_name = "dist_topk_bucket"; sp.flops = flops;
+        sp.prof_name = "dist_topk_bucket";
         screen_knn(sp, st);
         return;
     }

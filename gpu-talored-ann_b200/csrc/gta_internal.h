@@ -88,7 +88,9 @@ struct WorkItem {
     int32_t b_row0;     // first B row of the segment
     int32_t b_rows;     // segment length (columns)
     int32_t self_col0;  // segment column of the tile's row 0 itself (self excluded), or -1
-    int32_t pad0, pad1, pad2;
+    int32_t item_row0;  // float screen only: the item's first row of candidate lists and outputs
+    int32_t has_self;   // float screen only: A row r is column self_col0 + r (when in range)
+    int32_t pad2;
 };
 
 // operand rows of the distance kernel: bf16 (8-bit data held exactly, kind::f16), f32 (tf32
@@ -136,10 +138,12 @@ struct DistTopkProblem {
 void dist_topk(const DistTopkProblem& pr, cudaStream_t st);
 
 // Float-row per-bucket kNN (screen.cu): pool row j is dataset row ids[j] (X: n x d rows of
-// dtype, dense); each work item's A rows get their exact top-m_out (fp32 chain) over the item's
-// segment of pool rows (self excluded), written with output ids gid[].  A tensor-core screen
-// (fp16 parts of the scaled rows, `parts` = 2: hi + lo) keeps every column within a proven
-// margin of the row's M-th; an exact rerank over the dataset's rows picks the list.
+// dtype, dense); the pool is grouped into segments (buckets, in processing order) and every row
+// of a segment gets its exact top-m_out (fp32 chain) over the segment's rows (itself excluded),
+// written with output ids gid[] into row j of out_ids / out_dists.  A tensor-core screen (fp16
+// parts of the scaled rows, `parts` = 2: hi + lo) keeps every column within a proven margin of
+// the row's M-th; an exact rerank over the pool's f32 rows picks the list.  Segments of more
+// than 65 536 rows run as column chunks whose exact lists are merged.
 struct ScreenProblem {
     const void* X = nullptr;
     int dtype = 0;                  // GTA_F32 / GTA_U8 / GTA_I8 (include/gta.h)
@@ -147,17 +151,13 @@ struct ScreenProblem {
     const int32_t* ids = nullptr;   // [n_rows] pool row -> dataset row
     const int32_t* gid = nullptr;   // [n_rows] pool row -> output id
     int64_t n_rows = 0;
-    const WorkItem* work = nullptr;   // device copy of work_host
-    std::vector<WorkItem> work_host;  // one item per 128 A rows of a segment (self_col0: its first row's column)
-    int n_work = 0;
-    int max_cols = 0;               // longest segment (at most 2^17)
+    std::vector<int64_t> seg_lo, seg_n;  // segments: first pool row and length
     int m_out = 0;
     int parts = 2;
     int32_t* out_ids = nullptr;     // [n_rows x m_out]
     float* out_dists = nullptr;
     int* err = nullptr;
     const char* prof_name = "dist_topk_bucket";
-    double flops = 0.0;
 };
 void screen_knn(const ScreenProblem& pr, cudaStream_t st);
 int screen_list_len(int m);

@@ -32,9 +32,12 @@
 //               f32x2 arithmetic, the admission test by sign bits, admitted columns staged in
 //               shared memory and merged (bitonic) into the row's sorted list of kL 32-bit keys
 //               kept in TMEM columns 256.. (key = distance code << col_bits | column).
-// The distance code is the distance's float bits rounded UP to its top 32 - col_bits bits:
-// decode(code) >= the distance > decode(code - 1), and the admission threshold and the final
-// bound are taken from decoded codes, so every test errs toward admitting.
+// The 16-bit distance code covers the 31 binades below 4 (S max ||x||)^2 (no scaled distance is
+// larger) with 11 mantissa bits: the distance's float bits above that base, rounded UP to a
+// multiple of 2^12; everything below the base codes as 0 and the top code (0xFFFE) decodes as
+// +inf (0xFFFF is the sentinel's).
+// decode(code) >= the distance > decode(code - 1), and the admission threshold and the
+// rerank's bound are taken from decoded codes, so every test errs toward admitting.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
@@ -71,12 +74,34 @@ struct ScreenArgs {
     int32_t stages;
     int32_t col_bits;          // 16 or 17
     float mc1, mc2;            // margin = mc1 |a| bmax + mc2 (|a| + bmax)^2 (unscaled)
-    int32_t* cand_cols;        // [a_total x L] the row's list: keys (code << col_bits | column), ascending
-    int32_t* cand_n;           // [a_total] keys in the row's list
+    int32_t* cand_cols;        // [item rows x L] the row's list: keys (code << col_bits | column), ascending
+    int32_t* cand_n;           // [item rows] keys in the row's list
     unsigned long long* stats; // optional: the library's eight profile counters
     int* err;
     uint32_t buf_off, pn_off, bar_off;
 };
+
+// the largest real code (decodes as +inf); code 0xFFFF only appears in the sentinel key
+constexpr uint32_t kCodeTop = 0xFFFEu;
+
+// The float bits every distance code counts from: 31 binades below 4 (S bmax)^2.
+__device__ __forceinline__ uint32_t code_base(float sc, float bm)
+{
+    const float top = 4.0f * (sc * bm) * (sc * bm);
+    const uint32_t tb = __float_as_uint(top) + (1u << 23);  // one binade of headroom for rounding
+    return tb > (31u << 23) ? tb - (31u << 23) : 0u;
+}
+__device__ __forceinline__ uint32_t dist_code(float dist, uint32_t base)
+{
+    const uint32_t bits = __float_as_uint(fmaxf(dist, 0.0f));
+    if (bits <= base) return 0u;
+    const uint32_t c = (bits - base + 4095u) >> 12;
+    return c < kCodeTop ? c : kCodeTop;
+}
+__device__ __forceinline__ float code_value(uint32_t code, uint32_t base)
+{
+    return code >= kCodeTop ? INFINITY : __uint_as_float(base + (code << 12));
+}
 
 // The power-of-two scale of the operands (the same in the conversion and the epilogue).
 __device__ __forceinline__ float screen_scale(float maxnorm)
@@ -209,9 +234,28 @@ __device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsig
     return r;
 }
 
-template <int kL, bool kSplit>
+// Wait for this thread's outstanding tcgen05.ld into two 16-register arrays (in/out operands keep
+// every use of them below the wait).
+__device__ __forceinline__ void tmem_ld_wait_2x16(uint32_t (&a)[16], uint32_t (&b)[16])
+{
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(a[0]), "+r"(a[1]), "+r"(a[2]), "+r"(a[3]), "+r"(a[4]), "+r"(a[5]), "+r"(a[6]), "+r"(a[7]),
+                   "+r"(a[8]), "+r"(a[9]), "+r"(a[10]), "+r"(a[11]), "+r"(a[12]), "+r"(a[13]), "+r"(a[14]), "+r"(a[15]),
+                   "+r"(b[0]), "+r"(b[1]), "+r"(b[2]), "+r"(b[3]), "+r"(b[4]), "+r"(b[5]), "+r"(b[6]), "+r"(b[7]),
+                   "+r"(b[8]), "+r"(b[9]), "+r"(b[10]), "+r"(b[11]), "+r"(b[12]), "+r"(b[13]), "+r"(b[14]), "+r"(b[15])
+                 :
+                 : "memory");
+}
+
+// kCorr (two operand parts, long rows): the small products hi.lo + lo.hi accumulate in their own
+// TMEM accumulator (columns 128..255) and only hi.hi in the main one (columns 0..127), so the
+// main accumulator's rounding grows with d products instead of 3 d; the epilogue adds the two.
+// Both halves of one tile's accumulator pair fill the 256 columns, so the tile is not double
+// buffered (the MMA of the next tile waits until the epilogue holds the last slice in registers).
+template <int kL, bool kSplit, bool kCorr>
 __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_constant__ CUtensorMap tm, const ScreenArgs p)
 {
+    static_assert(!kCorr || kSplit, "the correction accumulator holds the lo products");
     constexpr int kParts = kSplit ? 2 : 1;
     constexpr uint32_t kStageBytes = 2u * kParts * kSChunk;  // A parts then B parts
     constexpr uint32_t kTmemCols = 512u;
@@ -224,7 +268,8 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const WorkItem w = p.work[blockIdx.x];
     const int n_ct = (w.b_rows + kSTile - 1) / kSTile;
-    const int t0 = (w.self_col0 >= 0) ? min(n_ct - 1, w.self_col0 / kSTile) : 0;
+    // the column tile of the rows themselves first (clamped into the item's columns)
+    const int t0 = w.has_self ? max(0, min(n_ct - 1, w.self_col0 / kSTile)) : 0;
     const int S = p.stages;
     uint32_t* buf = reinterpret_cast<uint32_t*>(smem_raw + p.buf_off);
     float* pn_s = reinterpret_cast<float*>(smem_raw + p.pn_off);
@@ -297,8 +342,8 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
             long long wait_acc = 0, wait_full = 0;
             int it = 0;
             for (int k = 0; k < n_ct && ok; ++k) {
-                const int b = k & 1;
-                const uint32_t use = static_cast<uint32_t>(k >> 1);
+                const int b = kCorr ? 0 : (k & 1);
+                const uint32_t use = static_cast<uint32_t>(kCorr ? k : (k >> 1));
                 const long long m0 = p.stats ? clock64() : 0;
                 if (!mbar_wait_backoff(S_ACC_EMPTY(b), (use & 1u) ^ 1u, abort_flag, p.err, kDevTimeoutAcc)) break;
                 if (p.stats) wait_acc += clock64() - m0;
@@ -321,8 +366,10 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
                         umma<false>(d_tmem, ah + 2ull * kk, bh + 2ull * kk, idesc, (kc | kk) != 0 ? 1u : 0u);
                         if constexpr (kSplit) {
                             const uint64_t al = smem_desc_sw128(sa + kSChunk), bl = smem_desc_sw128(sa + 3u * kSChunk);
-                            umma<false>(d_tmem, ah + 2ull * kk, bl + 2ull * kk, idesc, 1u);
-                            umma<false>(d_tmem, al + 2ull * kk, bh + 2ull * kk, idesc, 1u);
+                            const uint32_t c_tmem = kCorr ? tmem_base + static_cast<uint32_t>(kSTile) : d_tmem;
+                            umma<false>(c_tmem, ah + 2ull * kk, bl + 2ull * kk, idesc,
+                                        (!kCorr || (kc | kk) != 0) ? 1u : 0u);
+                            umma<false>(c_tmem, al + 2ull * kk, bh + 2ull * kk, idesc, 1u);
                         }
                     }
                     umma_commit(S_EMPTY(s));
@@ -351,7 +398,7 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
         const float an_s = s2 * anorm;
         const float an = sqrtf(fmaxf(anorm, 0.0f));
         const float margin = s2 * (p.mc1 * an * bm + p.mc2 * (an + bm) * (an + bm));
-        const int shift = p.col_bits - 1;
+        const uint32_t cbase = code_base(sc, bm);
         const uint32_t col_mask = (1u << p.col_bits) - 1u;
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
         const uint32_t tl = lane_base + kSListCol;
@@ -366,7 +413,7 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
         }
         // admission threshold on the approximate (scaled) distance; rows past the tile admit nothing
         float thr = row_ok ? FLT_MAX : -FLT_MAX;
-        auto decode = [&](uint32_t code) { return __uint_as_float(code << shift); };
+        auto decode = [&](uint32_t code) { return code_value(code, cbase); };
         auto refresh_thr = [&]() {
             const uint32_t kl = tmem_ld1(tl + static_cast<uint32_t>(kL - 1));
             const uint32_t km = tmem_ld1(tl + static_cast<uint32_t>(p.m_sel - 1));
@@ -390,7 +437,9 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
                 pf[j] = col < w.b_rows ? s2 * p.norm[static_cast<int64_t>(w.b_row0) + col] : INFINITY;
             }
         };
-        const int self_col = w.self_col0 >= 0 ? w.self_col0 + r : -1;
+        // the row's own column, when it lies in this item's columns
+        const int self_col = (w.has_self && w.self_col0 + r >= 0 && w.self_col0 + r < w.b_rows) ? w.self_col0 + r : -1;
+        const int64_t irow = static_cast<int64_t>(w.item_row0) + r;
         const int self_ct = self_col >= 0 ? self_col / kSTile : -1;
         const int self_c = (self_col % kSTile) >> 4;
         const int self_el = self_col & 15;
@@ -398,8 +447,8 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
         prefetch_cols(0);
         for (int k = 0; k < n_ct && ok; ++k) {
             const int ct = tile_order(k, t0, n_ct);
-            const int b = k & 1;
-            const uint32_t use = static_cast<uint32_t>(k >> 1);
+            const int b = kCorr ? 0 : (k & 1);
+            const uint32_t use = static_cast<uint32_t>(kCorr ? k : (k >> 1));
             __syncwarp();
             reinterpret_cast<float4*>(pnw)[lane] = make_float4(pf[0], pf[1], pf[2], pf[3]);
             __syncwarp();
@@ -412,11 +461,27 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
             if (st_on) cyc_wait += clock64() - w0;
             tc_fence_after();
             const uint32_t tbase = lane_base + static_cast<uint32_t>(b * kSTile);
-            uint32_t va[16], vb[16];
+            const uint32_t cbase = lane_base + static_cast<uint32_t>(kSTile);  // kCorr: the correction accumulator
+            uint32_t va[16], vb[16], ca[16], cb[16];
+            // load slice c (and, kCorr, its corrections); wait for it (and add the corrections)
+            auto ld_slice = [&](int c, uint32_t (&m)[16], uint32_t (&cr)[16]) {
+                tmem_ld_32x32b_x16(tbase + static_cast<uint32_t>(c * 16), m);
+                if constexpr (kCorr) tmem_ld_32x32b_x16(cbase + static_cast<uint32_t>(c * 16), cr);
+            };
+            auto wait_slice = [&](uint32_t (&m)[16], uint32_t (&cr)[16]) {
+                if constexpr (kCorr) {
+                    tmem_ld_wait_2x16(m, cr);
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) m[e] = __float_as_uint(__uint_as_float(m[e]) + __uint_as_float(cr[e]));
+                } else {
+                    tmem_ld_wait_regs(m);
+                }
+            };
             // one slice of 16 columns: approximate distances by packed f32x2 arithmetic, the
             // admission test dist <= thr as the sign of thr - dist (an IEEE difference is +0 exactly
             // on equality and never takes the wrong sign), then this lane's admitted columns
-            auto scan_slice = [&](int c, const uint32_t (&v)[16], uint32_t (&nxt)[16], bool nxt_in_flight) {
+            auto scan_slice = [&](int c, const uint32_t (&v)[16], uint32_t (&nxt)[16], uint32_t (&nxtc)[16],
+                                  bool nxt_in_flight) {
                 const int self_e = (ct == self_ct && c == self_c) ? self_el : -1;
                 const uint32_t c0 = static_cast<uint32_t>(ct * kSTile + c * 16);
                 const ulonglong2* pn2 = reinterpret_cast<const ulonglong2*>(pnw + c * 16);
@@ -445,7 +510,10 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
                 if (__any_sync(0xffffffffu, m != 0u)) {
                     const int npass = __popc(m);
                     if (__any_sync(0xffffffffu, nb + npass > kSBuf)) {
-                        if (nxt_in_flight) tmem_ld_wait_regs(nxt);  // no TMEM load in flight across the call
+                        if (nxt_in_flight) {  // no TMEM load in flight across the call
+                            if constexpr (kCorr) tmem_ld_wait_2x16(nxt, nxtc);
+                            else tmem_ld_wait_regs(nxt);
+                        }
                         const long long f0 = st_on ? clock64() : 0;
                         n_pass += nb;
                         ++n_flush;
@@ -462,8 +530,7 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
                         if (m & (1u << (15 - e))) {
-                            const uint32_t bits = __float_as_uint(fmaxf(dist[e], 0.0f));
-                            const uint32_t code = (bits + ((1u << shift) - 1u)) >> shift;
+                            const uint32_t code = dist_code(dist[e], cbase);
                             my_buf[i * 128] = (code << p.col_bits) | ((c0 + static_cast<uint32_t>(e)) & col_mask);
                             ++i;
                         }
@@ -479,28 +546,28 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
                 if (lane == 0) mbar_arrive(S_ACC_EMPTY(b));
             };
             __syncwarp();
-            tmem_ld_32x32b_x16(tbase, va);
+            ld_slice(0, va, ca);
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 const bool more = c + 1 < 8;
                 if ((c & 1) == 0) {
-                    tmem_ld_wait_regs(va);
+                    wait_slice(va, ca);
                     if (more) {
                         __syncwarp();
-                        tmem_ld_32x32b_x16(tbase + static_cast<uint32_t>((c + 1) * 16), vb);
+                        ld_slice(c + 1, vb, cb);
                     } else {
                         release_acc();
                     }
-                    scan_slice(c, va, vb, more);
+                    scan_slice(c, va, vb, cb, more);
                 } else {
-                    tmem_ld_wait_regs(vb);
+                    wait_slice(vb, cb);
                     if (more) {
                         __syncwarp();
-                        tmem_ld_32x32b_x16(tbase + static_cast<uint32_t>((c + 1) * 16), va);
+                        ld_slice(c + 1, va, ca);
                     } else {
                         release_acc();
                     }
-                    scan_slice(c, vb, va, more);
+                    scan_slice(c, vb, va, ca, more);
                 }
             }
         }
@@ -521,11 +588,11 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
                 tmem_ld_wait_regs32(c);
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    if (row_ok && c[j] != kSEmpty) p.cand_cols[arow * kL + blk + j] = static_cast<int32_t>(c[j]);
+                    if (row_ok && c[j] != kSEmpty) p.cand_cols[irow * kL + blk + j] = static_cast<int32_t>(c[j]);
                     nv += c[j] != kSEmpty ? 1 : 0;
                 }
             }
-            if (row_ok) p.cand_n[arow] = nv;
+            if (row_ok) p.cand_n[irow] = nv;
             if (st_on) {
                 if (row_ok) {
                     atomicAdd(&p.stats[0], static_cast<unsigned long long>(n_pass));
@@ -650,20 +717,25 @@ struct RerankX {
     int col_bits;
     int L;
     int m_out;
-    int32_t* out_ids;
+    int32_t* out_ids;           // [n_rows x m_out]: item rows below n_rows (the pool row itself)
     float* out_dists;
+    int32_t* ext_ids;           // [item rows - n_rows x m_out]: the column chunks of long segments
+    float* ext_dists;
+    int64_t n_rows;
     unsigned long long* stats;  // optional: [exact candidates, rows rescanned, rows]
-    int2* rescan;               // [rows] (A row, work item) of the rows whose segment is rescanned
+    int2* rescan;               // [item rows] (item row, work item) of the rows whose columns are rescanned
     unsigned* n_rescan;         // device counter of those rows
 };
 
-__device__ __forceinline__ void write_list(const RerankX& p, int64_t arow, const uint64_t* keys, int n_sorted, int lane)
+__device__ __forceinline__ void write_list(const RerankX& p, int64_t irow, const uint64_t* keys, int n_sorted, int lane)
 {
+    int32_t* oi = irow < p.n_rows ? p.out_ids + irow * p.m_out : p.ext_ids + (irow - p.n_rows) * p.m_out;
+    float* od = irow < p.n_rows ? p.out_dists + irow * p.m_out : p.ext_dists + (irow - p.n_rows) * p.m_out;
     for (int j = lane; j < p.m_out; j += 32) {
         const uint64_t key = j < n_sorted ? keys[j] : ~0ull;
         const bool v = key != ~0ull;
-        p.out_ids[arow * p.m_out + j] = v ? static_cast<int32_t>(static_cast<uint32_t>(key)) : -1;
-        p.out_dists[arow * p.m_out + j] = v ? key2f(static_cast<uint32_t>(key >> 32)) : INFINITY;
+        oi[j] = v ? static_cast<int32_t>(static_cast<uint32_t>(key)) : -1;
+        od[j] = v ? key2f(static_cast<uint32_t>(key >> 32)) : INFINITY;
     }
 }
 
@@ -679,19 +751,20 @@ __global__ void __launch_bounds__(kRrWarps * 32) rerank_kernel(const RerankX p)
     const float bm = *p.maxnorm;
     const float sc = screen_scale(bm);
     const float inv_s2 = 1.0f / (sc * sc);   // a power of two: exact
-    const int shift = p.col_bits - 1;
+    const uint32_t cbase = code_base(sc, bm);
     const uint32_t col_mask = (1u << p.col_bits) - 1u;
     // lower bound of a key's approximate distance (unscaled): decode(code - 1) < approx
     auto approx_lo = [&](uint32_t key) {
         const uint32_t code = key >> p.col_bits;
-        return code == 0u ? -INFINITY : __uint_as_float((code - 1u) << shift) * inv_s2;
+        return code == 0u ? -INFINITY : code_value(code - 1u, cbase) * inv_s2;
     };
     for (int r = warp; r < w.a_rows; r += kRrWarps) {
         const int64_t arow = static_cast<int64_t>(w.a_row0) + r;
+        const int64_t irow = static_cast<int64_t>(w.item_row0) + r;
         for (int i = lane; i < p.dp; i += 32) q_s[i] = p.pool[arow * p.dp + i];
         __syncwarp();
-        const int nv = p.cand_n[arow];
-        const uint32_t* kl = reinterpret_cast<const uint32_t*>(p.cand_cols) + arow * p.L;
+        const int nv = p.cand_n[irow];
+        const uint32_t* kl = reinterpret_cast<const uint32_t*>(p.cand_cols) + irow * p.L;
         // exact keys of list positions [j_lo, j_hi) into keys[j]; returns the largest distance
         auto exact_range = [&](int j_lo, int j_hi) {
             float mx = -INFINITY;
@@ -741,7 +814,7 @@ __global__ void __launch_bounds__(kRrWarps * 32) rerank_kernel(const RerankX p)
             // the whole segment, exactly, by rescan_kernel (a CTA per row, the columns split over its warps)
             if (lane == 0) {
                 const unsigned slot = atomicAdd(p.n_rescan, 1u);
-                p.rescan[slot] = make_int2(static_cast<int>(arow), static_cast<int>(blockIdx.x));
+                p.rescan[slot] = make_int2(static_cast<int>(irow), static_cast<int>(blockIdx.x));
             }
             __syncwarp();
             continue;
@@ -751,7 +824,7 @@ __global__ void __launch_bounds__(kRrWarps * 32) rerank_kernel(const RerankX p)
         for (int j = n_tot + lane; j < np2; j += 32) keys[j] = ~0ull;
         __syncwarp();
         rr_sort(keys, np2, lane);
-        write_list(p, arow, keys, np2, lane);
+        write_list(p, irow, keys, np2, lane);
         __syncwarp();
     }
 }
@@ -773,9 +846,11 @@ __global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p)
     const unsigned n = *p.n_rescan;
     for (unsigned i = blockIdx.x; i < n; i += gridDim.x) {
         const int2 e = p.rescan[i];
-        const int64_t arow = e.x;
+        const int64_t irow = e.x;
         const WorkItem w = p.work[e.y];
-        const int self = w.self_col0 + static_cast<int>(arow - w.a_row0);
+        const int r = static_cast<int>(irow - w.item_row0);
+        const int64_t arow = static_cast<int64_t>(w.a_row0) + r;
+        const int self = w.has_self ? w.self_col0 + r : -1;  // outside [0, b_rows): no column is skipped
         __syncthreads();
         for (int j = threadIdx.x; j < p.dp; j += blockDim.x) q_s[j] = p.pool[arow * p.dp + j];
         for (int j = lane; j < kRrKeys; j += 32) keys[j] = ~0ull;
@@ -802,8 +877,55 @@ __global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p)
                 __syncwarp();
                 rr_sort(keys, kRrKeys, lane);
             }
-            write_list(p, arow, keys, kRrKeys / 2, lane);
+            write_list(p, irow, keys, kRrKeys / 2, lane);
         }
+    }
+}
+
+// Rows of segments that ran as column chunks: the chunks' exact lists (each ascending by
+// (distance, id)) merged into the row's top-m_out.  One warp per row; chunk k of pool row
+// lo + i sits at extension row base + k * nb + i.
+struct ChunkSeg {
+    int64_t lo, nb, base_ext, row_prefix;  // base_ext: extension row of (chunk 0, row 0)
+    int32_t nch, pad;
+};
+
+__global__ void __launch_bounds__(kRrWarps * 32)
+    merge_chunks_kernel(const ChunkSeg* __restrict__ segs, int n_segs, int64_t n_rows_total, const int32_t* __restrict__ ext_ids,
+                        const float* __restrict__ ext_dists, int m_out, int32_t* __restrict__ out_ids,
+                        float* __restrict__ out_dists)
+{
+    __shared__ uint64_t s_keys[kRrWarps][kRrKeys];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int64_t j = static_cast<int64_t>(blockIdx.x) * kRrWarps + warp;
+    if (j >= n_rows_total) return;
+    int lo = 0, hi = n_segs - 1;  // the segment holding row j: last with row_prefix <= j
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (segs[mid].row_prefix <= j) lo = mid;
+        else hi = mid - 1;
+    }
+    const ChunkSeg sg = segs[lo];
+    const int64_t i = j - sg.row_prefix;
+    uint64_t* keys = s_keys[warp];
+    auto key_of = [&](int64_t er, int t) {
+        const int32_t id = ext_ids[er * m_out + t];
+        return id < 0 ? ~0ull : (static_cast<uint64_t>(f2key(ext_dists[er * m_out + t])) << 32) | static_cast<uint32_t>(id);
+    };
+    for (int t = lane; t < kRrKeys / 2; t += 32) keys[t] = t < m_out ? key_of(sg.base_ext + i, t) : ~0ull;
+    for (int k = 1; k < sg.nch; ++k) {
+        const int64_t er = sg.base_ext + static_cast<int64_t>(k) * sg.nb + i;
+        for (int t = lane; t < kRrKeys / 2; t += 32) keys[kRrKeys / 2 + t] = t < m_out ? key_of(er, t) : ~0ull;
+        __syncwarp();
+        rr_sort(keys, kRrKeys, lane);
+    }
+    __syncwarp();
+    const int64_t prow = sg.lo + i;
+    for (int t = lane; t < m_out; t += 32) {
+        const uint64_t key = keys[t];
+        const bool v = key != ~0ull;
+        out_ids[prow * m_out + t] = v ? static_cast<int32_t>(static_cast<uint32_t>(key)) : -1;
+        out_dists[prow * m_out + t] = v ? key2f(static_cast<uint32_t>(key >> 32)) : INFINITY;
     }
 }
 
@@ -851,10 +973,10 @@ EncodeFnS screen_encode()
     return fn;
 }
 
-template <int kL, bool kSplit>
+template <int kL, bool kSplit, bool kCorr = false>
 void launch_screen(const CUtensorMap& tm, const ScreenArgs& a, int n_work, uint32_t smem, cudaStream_t st)
 {
-    auto fn = screen_kernel<kL, kSplit>;
+    auto fn = screen_kernel<kL, kSplit, kCorr>;
     GTA_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
     fn<<<n_work, kSThreads, smem, st>>>(tm, a);
     count_launches(1);
@@ -867,11 +989,47 @@ int screen_list_len(int m) { return m <= 64 ? 128 : 256; }
 
 void screen_knn(const ScreenProblem& pr, cudaStream_t st)
 {
-    if (pr.n_work == 0) return;
-    GTA_REQUIRE(pr.X && pr.ids && pr.gid && pr.work && pr.out_ids && pr.out_dists, kInvalid, "screen: null operand");
+    if (pr.seg_lo.empty()) return;
+    GTA_REQUIRE(pr.X && pr.ids && pr.gid && pr.out_ids && pr.out_dists && pr.seg_lo.size() == pr.seg_n.size(), kInvalid,
+                "screen: null operand");
     GTA_REQUIRE(pr.dtype == GTA_F32 || pr.dtype == GTA_U8 || pr.dtype == GTA_I8, kInvalid, "screen: bad dtype");
-    GTA_REQUIRE(pr.d >= 1 && pr.m_out >= 1 && pr.m_out <= 128 && pr.max_cols >= 1 && pr.max_cols <= (1 << 17),
-                kInvalid, "screen: unsupported shape");
+    GTA_REQUIRE(pr.d >= 1 && pr.m_out >= 1 && pr.m_out <= 128, kInvalid, "screen: unsupported shape");
+    // work: one item per 128 rows of a segment; a segment longer than kChunk runs as column chunks
+    // of kChunk, each (row, chunk) with its own list row past the pool rows (item rows), merged later
+    constexpr int64_t kChunk = 1 << 16;
+    std::vector<WorkItem> items;
+    std::vector<ChunkSeg> chunked;
+    int64_t ext_rows = 0, chunked_rows = 0;
+    double flops = 0.0;
+    for (size_t sgi = 0; sgi < pr.seg_lo.size(); ++sgi) {
+        const int64_t lo = pr.seg_lo[sgi], nb = pr.seg_n[sgi];
+        GTA_REQUIRE(lo >= 0 && nb >= 1 && lo + nb <= pr.n_rows, kInvalid, "screen: bad segment");
+        flops += 2.0 * static_cast<double>(nb) * static_cast<double>(nb) * pr.d;
+        const int nch = static_cast<int>((nb + kChunk - 1) / kChunk);
+        if (nch == 1) {
+            for (int64_t t = 0; t < nb; t += 128)
+                items.push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, nb - t)),
+                                         static_cast<int32_t>(lo), static_cast<int32_t>(nb), static_cast<int32_t>(t),
+                                         static_cast<int32_t>(lo + t), 1, 0});
+            continue;
+        }
+        const int64_t base = pr.n_rows + ext_rows;
+        chunked.push_back(ChunkSeg{lo, nb, ext_rows, chunked_rows, nch, 0});
+        for (int k = 0; k < nch; ++k) {
+            const int64_t c0 = k * kChunk, cn = std::min<int64_t>(kChunk, nb - c0);
+            for (int64_t t = 0; t < nb; t += 128)
+                items.push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, nb - t)),
+                                         static_cast<int32_t>(lo + c0), static_cast<int32_t>(cn),
+                                         static_cast<int32_t>(t - c0), static_cast<int32_t>(base + k * nb + t), 1, 0});
+        }
+        ext_rows += static_cast<int64_t>(nch) * nb;
+        chunked_rows += nb;
+    }
+    const int64_t item_rows = pr.n_rows + ext_rows;
+    GTA_REQUIRE(item_rows < (1ll << 31), kInvalid, "screen: too many list rows");
+    DevBuf<WorkItem> work(items.size(), st);
+    // pageable source: the copy is staged before cudaMemcpyAsync returns
+    GTA_CUDA(cudaMemcpyAsync(work.get(), items.data(), sizeof(WorkItem) * items.size(), cudaMemcpyHostToDevice, st));
     GTA_REQUIRE(pr.parts == 1 || pr.parts == 2, kInvalid, "screen: one or two operand parts");
     const bool split = pr.parts == 2;
     const int L = screen_list_len(pr.m_out);
@@ -906,25 +1064,32 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
                                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         GTA_REQUIRE(r == CUDA_SUCCESS, kCuda, "cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
     }
-    DevBuf<int32_t> cand_cols(static_cast<size_t>(pr.n_rows) * L, st), cand_n(static_cast<size_t>(pr.n_rows), st);
+    DevBuf<int32_t> cand_cols(static_cast<size_t>(item_rows) * L, st), cand_n(static_cast<size_t>(item_rows), st);
     ScreenArgs a{};
-    a.work = pr.work;
+    a.work = work.get();
     a.norm = norm.get();
     a.maxnorm = bmax.get();
     a.k_chunks = d16 / 64;
     a.part_stride = d16;
     a.m_sel = pr.m_out;
     a.stages = pl.stages;
-    a.col_bits = pr.max_cols <= (1 << 16) ? 16 : 17;
-    // error bound of the screened distance (the margin, applied to the M-th key): operand parts
-    // (split: 3 * 2^-22 of |a||b|, one part: 2^-10), fp32 accumulation of the products (2^-22
-    // per product, 3 d products split, d single), fp32 norms and the two fused operations, with
-    // a 1.25 safety factor; the bound is on |a.b| <= |a| |b| <= |a| bmax
+    a.col_bits = 16;  // columns of an item: at most kChunk
+    // error bound of the screened distance (the margin, applied to the M-th key), relative to
+    // |a||b| <= |a| bmax:
+    //  * operand parts: split 3 * 2^-22 (the dropped lo.lo and the rounding of lo), one part 2^-10;
+    //  * fp32 accumulation, 2^-22 per product added to an accumulator: split into one accumulator
+    //    3 d products; with the correction accumulator (corr) d products plus the final addition
+    //    (the corrections themselves are below 2^-10 of the sum); one part d;
+    // and, relative to (|a| + bmax)^2, the fp32 squared norms (each lane of the norm kernel chains
+    // 4 ceil(dp / 128) products, then five butterfly additions) and the two fused operations of
+    // the score; a 1.25 safety factor on both
+    const bool corr = split && pr.d >= 256;
     const double dd = pr.d;
     const double part_err = split ? 3.0 * std::ldexp(1.0, -22) : std::ldexp(1.0, -10);
-    const double n_prod = split ? 3.0 * dd : dd;
+    const double n_prod = split ? (corr ? dd + 3.0 : 3.0 * dd) : dd;
+    const double k_norm = 4.0 * ((dp + 127) / 128) + 8.0;
     a.mc1 = static_cast<float>(1.25 * 4.0 * (part_err + n_prod * std::ldexp(1.0, -22)));
-    a.mc2 = static_cast<float>(1.25 * 3.0 * (dd + 4.0) * std::ldexp(1.0, -24));
+    a.mc2 = static_cast<float>(1.25 * 3.0 * (k_norm + 4.0) * std::ldexp(1.0, -24));
     a.cand_cols = cand_cols.get();
     a.cand_n = cand_n.get();
     a.err = pr.err;
@@ -932,23 +1097,26 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     a.pn_off = pl.pn_off;
     a.bar_off = pl.bar_off;
     {
-        ProfScope prof(pr.prof_name, pr.flops, st);
+        ProfScope prof(pr.prof_name, flops, st);
         a.stats = prof.counters(8);
+        const int n_work = static_cast<int>(items.size());
         if (L == 128) {
-            if (split) launch_screen<128, true>(tm, a, pr.n_work, pl.total, st);
-            else launch_screen<128, false>(tm, a, pr.n_work, pl.total, st);
+            if (corr) launch_screen<128, true, true>(tm, a, n_work, pl.total, st);
+            else if (split) launch_screen<128, true>(tm, a, n_work, pl.total, st);
+            else launch_screen<128, false>(tm, a, n_work, pl.total, st);
         } else {
-            if (split) launch_screen<256, true>(tm, a, pr.n_work, pl.total, st);
-            else launch_screen<256, false>(tm, a, pr.n_work, pl.total, st);
+            if (corr) launch_screen<256, true, true>(tm, a, n_work, pl.total, st);
+            else if (split) launch_screen<256, true>(tm, a, n_work, pl.total, st);
+            else launch_screen<256, false>(tm, a, n_work, pl.total, st);
         }
     }
     // the rerank's work: groups of kRrRows rows of the same items, in the same (bucket) order
     std::vector<WorkItem> groups;
-    groups.reserve(static_cast<size_t>(pr.n_rows / kRrRows + pr.n_work));
-    for (const WorkItem& it : pr.work_host) {
+    groups.reserve(static_cast<size_t>(item_rows / kRrRows + items.size()));
+    for (const WorkItem& it : items) {
         for (int g = 0; g < it.a_rows; g += kRrRows)
             groups.push_back(WorkItem{it.a_row0 + g, std::min(kRrRows, it.a_rows - g), it.b_row0, it.b_rows,
-                                      it.self_col0 + g, 0, 0, 0});
+                                      it.self_col0 + g, it.item_row0 + g, it.has_self, 0});
     }
     DevBuf<WorkItem> gwork(groups.size(), st);
     // pageable source: the copy is staged before cudaMemcpyAsync returns
@@ -969,7 +1137,12 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     r.m_out = pr.m_out;
     r.out_ids = pr.out_ids;
     r.out_dists = pr.out_dists;
-    DevBuf<int2> rescan(static_cast<size_t>(pr.n_rows), st);
+    DevBuf<int32_t> ext_ids(static_cast<size_t>(ext_rows) * pr.m_out, st);
+    DevBuf<float> ext_dists(static_cast<size_t>(ext_rows) * pr.m_out, st);
+    r.ext_ids = ext_ids.get();
+    r.ext_dists = ext_dists.get();
+    r.n_rows = pr.n_rows;
+    DevBuf<int2> rescan(static_cast<size_t>(item_rows), st);
     DevBuf<unsigned> n_rescan(1, st);
     GTA_CUDA(cudaMemsetAsync(n_rescan.get(), 0, sizeof(unsigned), st));
     r.rescan = rescan.get();
@@ -994,6 +1167,16 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         ProfScope prof("rescan", 0.0, st);
         GTA_CUDA(cudaFuncSetAttribute(rescan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
         rescan_kernel<<<static_cast<unsigned>(std::max(1, n_sm) * 2), kRsWarps * 32, smem, st>>>(r);
+        count_launches(1);
+        GTA_CUDA(cudaGetLastError());
+    }
+    if (!chunked.empty()) {
+        DevBuf<ChunkSeg> segs(chunked.size(), st);
+        GTA_CUDA(cudaMemcpyAsync(segs.get(), chunked.data(), sizeof(ChunkSeg) * chunked.size(), cudaMemcpyHostToDevice, st));
+        ProfScope prof("merge_chunks", 8.0 * pr.m_out * static_cast<double>(ext_rows + chunked_rows), st);
+        merge_chunks_kernel<<<static_cast<unsigned>((chunked_rows + kRrWarps - 1) / kRrWarps), kRrWarps * 32, 0, st>>>(
+            segs.get(), static_cast<int>(chunked.size()), chunked_rows, ext_ids.get(), ext_dists.get(), pr.m_out, pr.out_ids,
+            pr.out_dists);
         count_launches(1);
         GTA_CUDA(cudaGetLastError());
     }

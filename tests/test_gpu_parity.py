@@ -258,6 +258,28 @@ def test_bucket_knn_f32_vs_oracle(N, d, B, M):
     assert_lists_match(host(gi), host(gd), ri, rd, exact=False, X=X, qrows=mem)
 
 
+def test_bucket_knn_f32_long_segment_column_chunks():
+    """A float segment longer than 65 536 rows runs as column chunks whose exact lists are merged:
+    sampled rows (chunk edges included) against the oracle's exact top-M over the whole segment."""
+    rng = np.random.default_rng(70)
+    N, M = 70000, 16
+    X = mixture(rng, N, 8, 40, 0.2)
+    mem = np.arange(N, dtype=np.int32)
+    off = np.array([0, N], np.int64)
+    gi, gd = gta.bucket_knn(dev(X), dev(mem), dev(off), M)
+    gi, gd = host(gi), host(gd)
+    rows = np.concatenate([rng.choice(N, 200, replace=False), [0, 1, 65535, 65536, 65537, N - 1]])
+    ri = np.empty((len(rows), M), np.int32)
+    rd = np.empty((len(rows), M), np.float32)
+    allc = np.arange(N)
+    for k, r in enumerate(rows):
+        dd = orc.pair_l2(X, np.full(N, r), allc)
+        dd[r] = np.inf
+        sel = np.lexsort((allc, dd))[:M]
+        ri[k], rd[k] = sel, dd[sel]
+    assert_lists_match(gi[rows], gd[rows], ri, rd, exact=False, X=X, qrows=rows)
+
+
 def test_bucket_knn_f32_overflow_rescan():
     # 400 identical points in one bucket: the screen list overflows and the rows are rescanned exactly
     rng = np.random.default_rng(8)
