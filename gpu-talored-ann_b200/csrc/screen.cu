@@ -398,7 +398,7 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
         const float an_s = s2 * anorm;
         const float an = sqrtf(fmaxf(anorm, 0.0f));
         const float margin = s2 * (p.mc1 * an * bm + p.mc2 * (an + bm) * (an + bm));
-        const uint32_t cbase = code_base(sc, bm);
+        const uint32_t code_b = code_base(sc, bm);
         const uint32_t col_mask = (1u << p.col_bits) - 1u;
         const uint32_t lane_base = tmem_base + (static_cast<uint32_t>(q * 32) << 16);
         const uint32_t tl = lane_base + kSListCol;
@@ -413,7 +413,7 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
         }
         // admission threshold on the approximate (scaled) distance; rows past the tile admit nothing
         float thr = row_ok ? FLT_MAX : -FLT_MAX;
-        auto decode = [&](uint32_t code) { return code_value(code, cbase); };
+        auto decode = [&](uint32_t code) { return code_value(code, code_b); };
         auto refresh_thr = [&]() {
             const uint32_t kl = tmem_ld1(tl + static_cast<uint32_t>(kL - 1));
             const uint32_t km = tmem_ld1(tl + static_cast<uint32_t>(p.m_sel - 1));
@@ -461,12 +461,12 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
             if (st_on) cyc_wait += clock64() - w0;
             tc_fence_after();
             const uint32_t tbase = lane_base + static_cast<uint32_t>(b * kSTile);
-            const uint32_t cbase = lane_base + static_cast<uint32_t>(kSTile);  // kCorr: the correction accumulator
+            const uint32_t corr_base = lane_base + static_cast<uint32_t>(kSTile);  // kCorr: the correction accumulator
             uint32_t va[16], vb[16], ca[16], cb[16];
             // load slice c (and, kCorr, its corrections); wait for it (and add the corrections)
             auto ld_slice = [&](int c, uint32_t (&m)[16], uint32_t (&cr)[16]) {
                 tmem_ld_32x32b_x16(tbase + static_cast<uint32_t>(c * 16), m);
-                if constexpr (kCorr) tmem_ld_32x32b_x16(cbase + static_cast<uint32_t>(c * 16), cr);
+                if constexpr (kCorr) tmem_ld_32x32b_x16(corr_base + static_cast<uint32_t>(c * 16), cr);
             };
             auto wait_slice = [&](uint32_t (&m)[16], uint32_t (&cr)[16]) {
                 if constexpr (kCorr) {
@@ -530,7 +530,7 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
 #pragma unroll
                     for (int e = 0; e < 16; ++e) {
                         if (m & (1u << (15 - e))) {
-                            const uint32_t code = dist_code(dist[e], cbase);
+                            const uint32_t code = dist_code(dist[e], code_b);
                             my_buf[i * 128] = (code << p.col_bits) | ((c0 + static_cast<uint32_t>(e)) & col_mask);
                             ++i;
                         }
@@ -751,12 +751,12 @@ __global__ void __launch_bounds__(kRrWarps * 32) rerank_kernel(const RerankX p)
     const float bm = *p.maxnorm;
     const float sc = screen_scale(bm);
     const float inv_s2 = 1.0f / (sc * sc);   // a power of two: exact
-    const uint32_t cbase = code_base(sc, bm);
+    const uint32_t code_b = code_base(sc, bm);
     const uint32_t col_mask = (1u << p.col_bits) - 1u;
     // lower bound of a key's approximate distance (unscaled): decode(code - 1) < approx
     auto approx_lo = [&](uint32_t key) {
         const uint32_t code = key >> p.col_bits;
-        return code == 0u ? -INFINITY : code_value(code - 1u, cbase) * inv_s2;
+        return code == 0u ? -INFINITY : code_value(code - 1u, code_b) * inv_s2;
     };
     for (int r = warp; r < w.a_rows; r += kRrWarps) {
         const int64_t arow = static_cast<int64_t>(w.a_row0) + r;
