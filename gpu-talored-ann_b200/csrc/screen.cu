@@ -74,6 +74,8 @@ struct ScreenArgs {
     int32_t stages;
     int32_t col_bits;          // 16 or 17
     float mc1, mc2;            // margin = mc1 |a| bmax + mc2 (|a| + bmax)^2 (unscaled)
+    const float* seed;         // [seeded rows] a known bound on the row's exact M-th (unscaled); item
+                               // rows with pad2 >= 0 read seed[pad2 + r]
     int32_t* cand_cols;        // [item rows x L] the row's list: keys (code << col_bits | column), ascending
     int32_t* cand_n;           // [item rows] keys in the row's list
     unsigned long long* stats; // optional: the library's eight profile counters
@@ -413,13 +415,21 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
         }
         // admission threshold on the approximate (scaled) distance; rows past the tile admit nothing
         float thr = row_ok ? FLT_MAX : -FLT_MAX;
+        // a seeded row needs only the columns whose exact distance may lie within the seed: their
+        // approximate distance is at most the seed plus the one-sided error (half the margin)
+        float seed_thr = FLT_MAX;
+        if (row_ok && w.pad2 >= 0) {
+            const float sd = p.seed[static_cast<int64_t>(w.pad2) + r];
+            if (sd < FLT_MAX) seed_thr = fmaf(s2, sd, 0.5f * margin);
+            thr = seed_thr;
+        }
         auto decode = [&](uint32_t code) { return code_value(code, code_b); };
         auto refresh_thr = [&]() {
             const uint32_t kl = tmem_ld1(tl + static_cast<uint32_t>(kL - 1));
             const uint32_t km = tmem_ld1(tl + static_cast<uint32_t>(p.m_sel - 1));
             float t = kl == kSEmpty ? FLT_MAX : decode(kl >> p.col_bits);
             if (km != kSEmpty) t = fminf(t, decode(km >> p.col_bits) + margin);
-            if (row_ok) thr = t;
+            if (row_ok) thr = fminf(t, seed_thr);
         };
         int nb = 0, n_pass = 0, n_flush = 0;
         bool ok = true;
@@ -723,6 +733,7 @@ struct RerankX {
     float* ext_dists;
     int64_t n_rows;
     unsigned long long* stats;  // optional: [exact candidates, rows rescanned, rows]
+    const float* seed;          // as ScreenArgs::seed (work items with pad2 >= 0)
     int2* rescan;               // [item rows] (item row, work item) of the rows whose columns are rescanned
     unsigned* n_rescan;         // device counter of those rows
 };
@@ -788,9 +799,11 @@ __global__ void __launch_bounds__(kRrWarps * 32) rerank_kernel(const RerankX p)
         int n_tot = n1;
         bool rescan = false;
         if (nv > n1) {
-            // 2. the keys whose approximate distance may lie within e_m plus the one-sided error
+            // 2. the keys whose approximate distance may lie within e_m (or the row's seed, when
+            //    smaller: both bound its exact M-th) plus the one-sided error
             const float an = sqrtf(fmaxf(p.norm[arow], 0.0f));
-            const float bound = e_m + 0.5f * (p.mc1 * an * bm + p.mc2 * (an + bm) * (an + bm));
+            const float sd = w.pad2 >= 0 ? p.seed[static_cast<int64_t>(w.pad2) + r] : INFINITY;
+            const float bound = fminf(e_m, sd) + 0.5f * (p.mc1 * an * bm + p.mc2 * (an + bm) * (an + bm));
             int n2 = nv - n1;
             for (int j0 = n1; j0 < nv; j0 += 32) {
                 const int j = j0 + lane;
@@ -882,18 +895,22 @@ __global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p)
     }
 }
 
-// Rows of segments that ran as column chunks: the chunks' exact lists (each ascending by
-// (distance, id)) merged into the row's top-m_out.  One warp per row; chunk k of pool row
-// lo + i sits at extension row base + k * nb + i.
+// Rows of segments that run as column chunks, one chunk per wave: the row's running list (the
+// exact top-m_out of the chunks so far, in its chunk-0 extension row) and its seed (the running
+// list's m_out-th distance, a bound on the row's exact M-th that the next chunk's screen and
+// rerank use).  Chunk k of pool row lo + i sits at extension row base_ext + k * nb + i.
 struct ChunkSeg {
     int64_t lo, nb, base_ext, row_prefix;  // base_ext: extension row of (chunk 0, row 0)
     int32_t nch, pad;
 };
 
+// k = 0: seeds from the chunk-0 lists; k > 0: chunk k merged into the running list (by
+// (distance, id)), then the seed; k < 0: the running lists written to the rows' outputs.
+// One warp per row of the chunked segments.
 __global__ void __launch_bounds__(kRrWarps * 32)
-    merge_chunks_kernel(const ChunkSeg* __restrict__ segs, int n_segs, int64_t n_rows_total, const int32_t* __restrict__ ext_ids,
-                        const float* __restrict__ ext_dists, int m_out, int32_t* __restrict__ out_ids,
-                        float* __restrict__ out_dists)
+    merge_step_kernel(const ChunkSeg* __restrict__ segs, int n_segs, int64_t n_rows_total, int k,
+                      int32_t* __restrict__ ext_ids, float* __restrict__ ext_dists, int m_out, float* __restrict__ seeds,
+                      int32_t* __restrict__ out_ids, float* __restrict__ out_dists)
 {
     __shared__ uint64_t s_keys[kRrWarps][kRrKeys];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -907,25 +924,41 @@ __global__ void __launch_bounds__(kRrWarps * 32)
     }
     const ChunkSeg sg = segs[lo];
     const int64_t i = j - sg.row_prefix;
-    uint64_t* keys = s_keys[warp];
-    auto key_of = [&](int64_t er, int t) {
-        const int32_t id = ext_ids[er * m_out + t];
-        return id < 0 ? ~0ull : (static_cast<uint64_t>(f2key(ext_dists[er * m_out + t])) << 32) | static_cast<uint32_t>(id);
-    };
-    for (int t = lane; t < kRrKeys / 2; t += 32) keys[t] = t < m_out ? key_of(sg.base_ext + i, t) : ~0ull;
-    for (int k = 1; k < sg.nch; ++k) {
+    const int64_t run = sg.base_ext + i;
+    if (k < 0) {
+        const int64_t prow = sg.lo + i;
+        for (int t = lane; t < m_out; t += 32) {
+            out_ids[prow * m_out + t] = ext_ids[run * m_out + t];
+            out_dists[prow * m_out + t] = ext_dists[run * m_out + t];
+        }
+        return;
+    }
+    if (k >= sg.nch) return;
+    if (k > 0) {
+        uint64_t* keys = s_keys[warp];
+        auto key_of = [&](int64_t er, int t) {
+            const int32_t id = ext_ids[er * m_out + t];
+            return id < 0 ? ~0ull
+                          : (static_cast<uint64_t>(f2key(ext_dists[er * m_out + t])) << 32) | static_cast<uint32_t>(id);
+        };
         const int64_t er = sg.base_ext + static_cast<int64_t>(k) * sg.nb + i;
-        for (int t = lane; t < kRrKeys / 2; t += 32) keys[kRrKeys / 2 + t] = t < m_out ? key_of(er, t) : ~0ull;
+        for (int t = lane; t < kRrKeys / 2; t += 32) {
+            keys[t] = t < m_out ? key_of(run, t) : ~0ull;
+            keys[kRrKeys / 2 + t] = t < m_out ? key_of(er, t) : ~0ull;
+        }
         __syncwarp();
         rr_sort(keys, kRrKeys, lane);
+        for (int t = lane; t < m_out; t += 32) {
+            const uint64_t key = keys[t];
+            const bool v = key != ~0ull;
+            ext_ids[run * m_out + t] = v ? static_cast<int32_t>(static_cast<uint32_t>(key)) : -1;
+            ext_dists[run * m_out + t] = v ? key2f(static_cast<uint32_t>(key >> 32)) : INFINITY;
+        }
+        __syncwarp();
     }
-    __syncwarp();
-    const int64_t prow = sg.lo + i;
-    for (int t = lane; t < m_out; t += 32) {
-        const uint64_t key = keys[t];
-        const bool v = key != ~0ull;
-        out_ids[prow * m_out + t] = v ? static_cast<int32_t>(static_cast<uint32_t>(key)) : -1;
-        out_dists[prow * m_out + t] = v ? key2f(static_cast<uint32_t>(key >> 32)) : INFINITY;
+    if (lane == 0) {
+        const bool full = ext_ids[run * m_out + m_out - 1] >= 0;
+        seeds[j] = full ? ext_dists[run * m_out + m_out - 1] : INFINITY;
     }
 }
 
@@ -994,43 +1027,50 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
                 "screen: null operand");
     GTA_REQUIRE(pr.dtype == GTA_F32 || pr.dtype == GTA_U8 || pr.dtype == GTA_I8, kInvalid, "screen: bad dtype");
     GTA_REQUIRE(pr.d >= 1 && pr.m_out >= 1 && pr.m_out <= 128, kInvalid, "screen: unsupported shape");
-    // work: one item per 128 rows of a segment; a segment longer than kChunk runs as column chunks
-    // of kChunk, each (row, chunk) with its own list row past the pool rows (item rows), merged later
+    GTA_REQUIRE(pr.parts == 1 || pr.parts == 2, kInvalid, "screen: one or two operand parts");
+    // Work: one item per 128 rows of a segment.  A segment longer than kChunk runs as column
+    // chunks of kChunk in waves: wave 0 holds every short segment and the chunk 0 of the long
+    // ones; wave k > 0 holds chunk k, its rows seeded with the m-th distance of their running list
+    // (the exact top-m of chunks 0 .. k-1).  Each (row, chunk) has its own list row past the pool
+    // rows (an extension row).
     constexpr int64_t kChunk = 1 << 16;
-    std::vector<WorkItem> items;
+    std::vector<std::vector<WorkItem>> waves(1);
+    std::vector<double> wave_flops(1, 0.0);
     std::vector<ChunkSeg> chunked;
     int64_t ext_rows = 0, chunked_rows = 0;
-    double flops = 0.0;
     for (size_t sgi = 0; sgi < pr.seg_lo.size(); ++sgi) {
         const int64_t lo = pr.seg_lo[sgi], nb = pr.seg_n[sgi];
         GTA_REQUIRE(lo >= 0 && nb >= 1 && lo + nb <= pr.n_rows, kInvalid, "screen: bad segment");
-        flops += 2.0 * static_cast<double>(nb) * static_cast<double>(nb) * pr.d;
         const int nch = static_cast<int>((nb + kChunk - 1) / kChunk);
         if (nch == 1) {
             for (int64_t t = 0; t < nb; t += 128)
-                items.push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, nb - t)),
-                                         static_cast<int32_t>(lo), static_cast<int32_t>(nb), static_cast<int32_t>(t),
-                                         static_cast<int32_t>(lo + t), 1, 0});
+                waves[0].push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, nb - t)),
+                                            static_cast<int32_t>(lo), static_cast<int32_t>(nb), static_cast<int32_t>(t),
+                                            static_cast<int32_t>(lo + t), 1, -1});
+            wave_flops[0] += 2.0 * static_cast<double>(nb) * static_cast<double>(nb) * pr.d;
             continue;
         }
         const int64_t base = pr.n_rows + ext_rows;
         chunked.push_back(ChunkSeg{lo, nb, ext_rows, chunked_rows, nch, 0});
+        if (static_cast<int>(waves.size()) < nch) {
+            waves.resize(static_cast<size_t>(nch));
+            wave_flops.resize(static_cast<size_t>(nch), 0.0);
+        }
         for (int k = 0; k < nch; ++k) {
             const int64_t c0 = k * kChunk, cn = std::min<int64_t>(kChunk, nb - c0);
             for (int64_t t = 0; t < nb; t += 128)
-                items.push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, nb - t)),
-                                         static_cast<int32_t>(lo + c0), static_cast<int32_t>(cn),
-                                         static_cast<int32_t>(t - c0), static_cast<int32_t>(base + k * nb + t), 1, 0});
+                waves[static_cast<size_t>(k)].push_back(
+                    WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, nb - t)),
+                             static_cast<int32_t>(lo + c0), static_cast<int32_t>(cn), static_cast<int32_t>(t - c0),
+                             static_cast<int32_t>(base + k * nb + t), 1,
+                             k == 0 ? -1 : static_cast<int32_t>(chunked_rows + t)});
+            wave_flops[static_cast<size_t>(k)] += 2.0 * static_cast<double>(nb) * static_cast<double>(cn) * pr.d;
         }
         ext_rows += static_cast<int64_t>(nch) * nb;
         chunked_rows += nb;
     }
     const int64_t item_rows = pr.n_rows + ext_rows;
     GTA_REQUIRE(item_rows < (1ll << 31), kInvalid, "screen: too many list rows");
-    DevBuf<WorkItem> work(items.size(), st);
-    // pageable source: the copy is staged before cudaMemcpyAsync returns
-    GTA_CUDA(cudaMemcpyAsync(work.get(), items.data(), sizeof(WorkItem) * items.size(), cudaMemcpyHostToDevice, st));
-    GTA_REQUIRE(pr.parts == 1 || pr.parts == 2, kInvalid, "screen: one or two operand parts");
     const bool split = pr.parts == 2;
     const int L = screen_list_len(pr.m_out);
     const int d16 = (pr.d + 63) / 64 * 64;
@@ -1065,8 +1105,15 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         GTA_REQUIRE(r == CUDA_SUCCESS, kCuda, "cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
     }
     DevBuf<int32_t> cand_cols(static_cast<size_t>(item_rows) * L, st), cand_n(static_cast<size_t>(item_rows), st);
+    DevBuf<int32_t> ext_ids(static_cast<size_t>(ext_rows) * pr.m_out, st);
+    DevBuf<float> ext_dists(static_cast<size_t>(ext_rows) * pr.m_out, st);
+    DevBuf<float> seeds(static_cast<size_t>(chunked_rows), st);
+    DevBuf<int2> rescan(static_cast<size_t>(item_rows), st);
+    DevBuf<unsigned> n_rescan(1, st);
+    DevBuf<ChunkSeg> segs(chunked.size(), st);
+    if (!chunked.empty())
+        GTA_CUDA(cudaMemcpyAsync(segs.get(), chunked.data(), sizeof(ChunkSeg) * chunked.size(), cudaMemcpyHostToDevice, st));
     ScreenArgs a{};
-    a.work = work.get();
     a.norm = norm.get();
     a.maxnorm = bmax.get();
     a.k_chunks = d16 / 64;
@@ -1090,39 +1137,14 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     const double k_norm = 4.0 * ((dp + 127) / 128) + 8.0;
     a.mc1 = static_cast<float>(1.25 * 4.0 * (part_err + n_prod * std::ldexp(1.0, -22)));
     a.mc2 = static_cast<float>(1.25 * 3.0 * (k_norm + 4.0) * std::ldexp(1.0, -24));
+    a.seed = seeds.get();
     a.cand_cols = cand_cols.get();
     a.cand_n = cand_n.get();
     a.err = pr.err;
     a.buf_off = pl.buf_off;
     a.pn_off = pl.pn_off;
     a.bar_off = pl.bar_off;
-    {
-        ProfScope prof(pr.prof_name, flops, st);
-        a.stats = prof.counters(8);
-        const int n_work = static_cast<int>(items.size());
-        if (L == 128) {
-            if (corr) launch_screen<128, true, true>(tm, a, n_work, pl.total, st);
-            else if (split) launch_screen<128, true>(tm, a, n_work, pl.total, st);
-            else launch_screen<128, false>(tm, a, n_work, pl.total, st);
-        } else {
-            if (corr) launch_screen<256, true, true>(tm, a, n_work, pl.total, st);
-            else if (split) launch_screen<256, true>(tm, a, n_work, pl.total, st);
-            else launch_screen<256, false>(tm, a, n_work, pl.total, st);
-        }
-    }
-    // the rerank's work: groups of kRrRows rows of the same items, in the same (bucket) order
-    std::vector<WorkItem> groups;
-    groups.reserve(static_cast<size_t>(item_rows / kRrRows + items.size()));
-    for (const WorkItem& it : items) {
-        for (int g = 0; g < it.a_rows; g += kRrRows)
-            groups.push_back(WorkItem{it.a_row0 + g, std::min(kRrRows, it.a_rows - g), it.b_row0, it.b_rows,
-                                      it.self_col0 + g, it.item_row0 + g, it.has_self, 0});
-    }
-    DevBuf<WorkItem> gwork(groups.size(), st);
-    // pageable source: the copy is staged before cudaMemcpyAsync returns
-    GTA_CUDA(cudaMemcpyAsync(gwork.get(), groups.data(), sizeof(WorkItem) * groups.size(), cudaMemcpyHostToDevice, st));
     RerankX r{};
-    r.work = gwork.get();
     r.pool = fpool.get();
     r.dp = dp;
     r.gid = pr.gid;
@@ -1137,46 +1159,83 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     r.m_out = pr.m_out;
     r.out_ids = pr.out_ids;
     r.out_dists = pr.out_dists;
-    DevBuf<int32_t> ext_ids(static_cast<size_t>(ext_rows) * pr.m_out, st);
-    DevBuf<float> ext_dists(static_cast<size_t>(ext_rows) * pr.m_out, st);
     r.ext_ids = ext_ids.get();
     r.ext_dists = ext_dists.get();
     r.n_rows = pr.n_rows;
-    DevBuf<int2> rescan(static_cast<size_t>(item_rows), st);
-    DevBuf<unsigned> n_rescan(1, st);
-    GTA_CUDA(cudaMemsetAsync(n_rescan.get(), 0, sizeof(unsigned), st));
+    r.seed = seeds.get();
     r.rescan = rescan.get();
     r.n_rescan = n_rescan.get();
-    {
-        const size_t smem = kRrWarps * (kRrKeys * sizeof(uint64_t) + 32 * kTileLd * 4 + static_cast<size_t>(dp) * 4);
-        GTA_REQUIRE(smem <= kSSmemMax, kInvalid, "rerank: dimension too large");
-        ProfScope prof("rerank", 0.0, st);
-        r.stats = prof.counters(8);
-        GTA_CUDA(cudaFuncSetAttribute(rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-        rerank_kernel<<<static_cast<unsigned>(groups.size()), kRrWarps * 32, smem, st>>>(r);
-        count_launches(1);
-        GTA_CUDA(cudaGetLastError());
-    }
-    {
-        // the deferred whole-segment rescans: persistent CTAs over the device-side list
-        const size_t smem = kRsWarps * (kRrKeys * sizeof(uint64_t) + 32 * kTileLd * 4) + static_cast<size_t>(dp) * 4;
-        GTA_REQUIRE(smem <= kSSmemMax, kInvalid, "rescan: dimension too large");
-        int dev = 0, n_sm = 0;
-        GTA_CUDA(cudaGetDevice(&dev));
-        GTA_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
-        ProfScope prof("rescan", 0.0, st);
-        GTA_CUDA(cudaFuncSetAttribute(rescan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-        rescan_kernel<<<static_cast<unsigned>(std::max(1, n_sm) * 2), kRsWarps * 32, smem, st>>>(r);
-        count_launches(1);
-        GTA_CUDA(cudaGetLastError());
+    const size_t smem_rr = kRrWarps * (kRrKeys * sizeof(uint64_t) + 32 * kTileLd * 4 + static_cast<size_t>(dp) * 4);
+    const size_t smem_rs = kRsWarps * (kRrKeys * sizeof(uint64_t) + 32 * kTileLd * 4) + static_cast<size_t>(dp) * 4;
+    GTA_REQUIRE(smem_rr <= kSSmemMax && smem_rs <= kSSmemMax, kInvalid, "rerank: dimension too large");
+    GTA_CUDA(cudaFuncSetAttribute(rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_rr)));
+    GTA_CUDA(cudaFuncSetAttribute(rescan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_rs)));
+    int dev = 0, n_sm = 0;
+    GTA_CUDA(cudaGetDevice(&dev));
+    GTA_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+    const unsigned merge_grid = static_cast<unsigned>((chunked_rows + kRrWarps - 1) / kRrWarps);
+    for (size_t k = 0; k < waves.size(); ++k) {
+        const std::vector<WorkItem>& items = waves[k];
+        if (items.empty()) continue;
+        DevBuf<WorkItem> work(items.size(), st);
+        // pageable sources: each copy is staged before cudaMemcpyAsync returns
+        GTA_CUDA(cudaMemcpyAsync(work.get(), items.data(), sizeof(WorkItem) * items.size(), cudaMemcpyHostToDevice, st));
+        a.work = work.get();
+        {
+            ProfScope prof(pr.prof_name, wave_flops[k], st);
+            a.stats = prof.counters(8);
+            const int n_work = static_cast<int>(items.size());
+            if (L == 128) {
+                if (corr) launch_screen<128, true, true>(tm, a, n_work, pl.total, st);
+                else if (split) launch_screen<128, true>(tm, a, n_work, pl.total, st);
+                else launch_screen<128, false>(tm, a, n_work, pl.total, st);
+            } else {
+                if (corr) launch_screen<256, true, true>(tm, a, n_work, pl.total, st);
+                else if (split) launch_screen<256, true>(tm, a, n_work, pl.total, st);
+                else launch_screen<256, false>(tm, a, n_work, pl.total, st);
+            }
+        }
+        // the rerank's work: groups of kRrRows rows of the same items, in the same (bucket) order
+        std::vector<WorkItem> groups;
+        groups.reserve(items.size() * (128 / kRrRows));
+        for (const WorkItem& it : items)
+            for (int g = 0; g < it.a_rows; g += kRrRows)
+                groups.push_back(WorkItem{it.a_row0 + g, std::min(kRrRows, it.a_rows - g), it.b_row0, it.b_rows,
+                                          it.self_col0 + g, it.item_row0 + g, it.has_self, it.pad2 >= 0 ? it.pad2 + g : -1});
+        DevBuf<WorkItem> gwork(groups.size(), st);
+        GTA_CUDA(cudaMemcpyAsync(gwork.get(), groups.data(), sizeof(WorkItem) * groups.size(), cudaMemcpyHostToDevice, st));
+        r.work = gwork.get();
+        GTA_CUDA(cudaMemsetAsync(n_rescan.get(), 0, sizeof(unsigned), st));
+        {
+            ProfScope prof("rerank", 0.0, st);
+            r.stats = prof.counters(8);
+            rerank_kernel<<<static_cast<unsigned>(groups.size()), kRrWarps * 32, smem_rr, st>>>(r);
+            count_launches(1);
+            GTA_CUDA(cudaGetLastError());
+        }
+        {
+            // the deferred whole-segment rescans: persistent CTAs over the device-side list
+            ProfScope prof("rescan", 0.0, st);
+            rescan_kernel<<<static_cast<unsigned>(std::max(1, n_sm) * 2), kRsWarps * 32, smem_rs, st>>>(r);
+            count_launches(1);
+            GTA_CUDA(cudaGetLastError());
+        }
+        if (!chunked.empty()) {
+            // chunk k into the running lists (k = 0: the seeds of chunk 0's lists)
+            ProfScope prof("merge_chunks", 24.0 * pr.m_out * static_cast<double>(chunked_rows), st);
+            merge_step_kernel<<<merge_grid, kRrWarps * 32, 0, st>>>(segs.get(), static_cast<int>(chunked.size()),
+                                                                    chunked_rows, static_cast<int>(k), ext_ids.get(),
+                                                                    ext_dists.get(), pr.m_out, seeds.get(), pr.out_ids,
+                                                                    pr.out_dists);
+            count_launches(1);
+            GTA_CUDA(cudaGetLastError());
+        }
     }
     if (!chunked.empty()) {
-        DevBuf<ChunkSeg> segs(chunked.size(), st);
-        GTA_CUDA(cudaMemcpyAsync(segs.get(), chunked.data(), sizeof(ChunkSeg) * chunked.size(), cudaMemcpyHostToDevice, st));
-        ProfScope prof("merge_chunks", 8.0 * pr.m_out * static_cast<double>(ext_rows + chunked_rows), st);
-        merge_chunks_kernel<<<static_cast<unsigned>((chunked_rows + kRrWarps - 1) / kRrWarps), kRrWarps * 32, 0, st>>>(
-            segs.get(), static_cast<int>(chunked.size()), chunked_rows, ext_ids.get(), ext_dists.get(), pr.m_out, pr.out_ids,
-            pr.out_dists);
+        ProfScope prof("merge_chunks", 16.0 * pr.m_out * static_cast<double>(chunked_rows), st);
+        merge_step_kernel<<<merge_grid, kRrWarps * 32, 0, st>>>(segs.get(), static_cast<int>(chunked.size()), chunked_rows,
+                                                                -1, ext_ids.get(), ext_dists.get(), pr.m_out, seeds.get(),
+                                                                pr.out_ids, pr.out_dists);
         count_launches(1);
         GTA_CUDA(cudaGetLastError());
     }
