@@ -81,6 +81,7 @@ struct ScreenArgs {
     unsigned long long* stats; // optional: the library's eight profile counters
     int* err;
     uint32_t buf_off, pn_off, bar_off;
+    uint32_t stg_off;          // kCorr: the drained tile (128 columns x 128 rows of fp32)
 };
 
 // the largest real code (decodes as +inf); code 0xFFFF only appears in the sentinel key
@@ -236,6 +237,19 @@ __device__ __forceinline__ unsigned long long f2_add(unsigned long long a, unsig
     return r;
 }
 
+// Shared-memory matrix descriptor of a K-major tile of 64-byte rows with the 64-byte swizzle
+// written by TMA (8-row atoms, 512 B apart).
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr)
+{
+    uint64_t d = 0;
+    d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);   // start address
+    d |= static_cast<uint64_t>(1u) << 16;                  // leading byte offset (unused for swizzled K-major)
+    d |= static_cast<uint64_t>(512u >> 4) << 32;           // stride byte offset: 8 rows x 64 B
+    d |= static_cast<uint64_t>(1u) << 46;                  // descriptor version (sm_100)
+    d |= static_cast<uint64_t>(4u) << 61;                  // layout: 64-byte swizzle
+    return d;
+}
+
 // Wait for this thread's outstanding tcgen05.ld into two 16-register arrays (in/out operands keep
 // every use of them below the wait).
 __device__ __forceinline__ void tmem_ld_wait_2x16(uint32_t (&a)[16], uint32_t (&b)[16])
@@ -259,7 +273,11 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
 {
     static_assert(!kCorr || kSplit, "the correction accumulator holds the lo products");
     constexpr int kParts = kSplit ? 2 : 1;
-    constexpr uint32_t kStageBytes = 2u * kParts * kSChunk;  // A parts then B parts
+    // operand chunks of 64 fp16 (128-byte swizzle) or, kCorr, 32 fp16 (64-byte swizzle: smaller
+    // stages leave room for the drained tile)
+    constexpr int kChunkElems = kCorr ? 32 : 64;
+    constexpr uint32_t kPartChunk = 128u * static_cast<uint32_t>(kChunkElems) * 2u;
+    constexpr uint32_t kStageBytes = 2u * kParts * kPartChunk;  // A parts then B parts
     constexpr uint32_t kTmemCols = 512u;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t base = smem_u32(smem_raw);
@@ -325,9 +343,9 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
                     mbar_arrive_expect_tx(S_FULL(s), kStageBytes);
 #pragma unroll
                     for (int q = 0; q < kParts; ++q) {
-                        const int x = q * p.part_stride + kc * 64;
-                        tma_load_2d(dst + static_cast<uint32_t>(q) * kSChunk, &tm, S_FULL(s), x, w.a_row0);
-                        tma_load_2d(dst + static_cast<uint32_t>(kParts + q) * kSChunk, &tm, S_FULL(s), x,
+                        const int x = q * p.part_stride + kc * kChunkElems;
+                        tma_load_2d(dst + static_cast<uint32_t>(q) * kPartChunk, &tm, S_FULL(s), x, w.a_row0);
+                        tma_load_2d(dst + static_cast<uint32_t>(kParts + q) * kPartChunk, &tm, S_FULL(s), x,
                                     w.b_row0 + ct * kSTile);
                     }
                     ++it;
@@ -362,12 +380,13 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
                     if (p.stats) wait_full += clock64() - m1;
                     tc_fence_after();
                     const uint32_t sa = base + static_cast<uint32_t>(s) * kStageBytes;
-                    const uint64_t ah = smem_desc_sw128(sa), bh = smem_desc_sw128(sa + kParts * kSChunk);
+                    auto desc = [](uint32_t addr) { return kCorr ? smem_desc_sw64(addr) : smem_desc_sw128(addr); };
+                    const uint64_t ah = desc(sa), bh = desc(sa + kParts * kPartChunk);
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {  // 4 x 16 fp16 of K per 128-byte chunk
+                    for (int kk = 0; kk < kChunkElems / 16; ++kk) {  // 16 fp16 of K per MMA
                         umma<false>(d_tmem, ah + 2ull * kk, bh + 2ull * kk, idesc, (kc | kk) != 0 ? 1u : 0u);
                         if constexpr (kSplit) {
-                            const uint64_t al = smem_desc_sw128(sa + kSChunk), bl = smem_desc_sw128(sa + 3u * kSChunk);
+                            const uint64_t al = desc(sa + kPartChunk), bl = desc(sa + 3u * kPartChunk);
                             const uint32_t c_tmem = kCorr ? tmem_base + static_cast<uint32_t>(kSTile) : d_tmem;
                             umma<false>(c_tmem, ah + 2ull * kk, bl + 2ull * kk, idesc,
                                         (!kCorr || (kc | kk) != 0) ? 1u : 0u);
@@ -557,27 +576,55 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
             };
             __syncwarp();
             ld_slice(0, va, ca);
+            if constexpr (kCorr) {
+                // the single accumulator pair goes back to the MMA as soon as the whole tile (main
+                // plus corrections) sits in shared memory; the scan then reads it from there
+                float* stg = reinterpret_cast<float*>(smem_raw + p.stg_off) + r;
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const bool more = c + 1 < 8;
-                if ((c & 1) == 0) {
-                    wait_slice(va, ca);
+                for (int c = 0; c < 8; ++c) {
+                    const bool more = c + 1 < 8;
+                    uint32_t (&cur)[16] = (c & 1) == 0 ? va : vb;
+                    uint32_t (&curc)[16] = (c & 1) == 0 ? ca : cb;
+                    uint32_t (&nxt)[16] = (c & 1) == 0 ? vb : va;
+                    uint32_t (&nxtc)[16] = (c & 1) == 0 ? cb : ca;
+                    wait_slice(cur, curc);
                     if (more) {
                         __syncwarp();
-                        ld_slice(c + 1, vb, cb);
-                    } else {
-                        release_acc();
+                        ld_slice(c + 1, nxt, nxtc);
                     }
-                    scan_slice(c, va, vb, cb, more);
-                } else {
-                    wait_slice(vb, cb);
-                    if (more) {
-                        __syncwarp();
-                        ld_slice(c + 1, va, ca);
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) stg[(c * 16 + e) * 128] = __uint_as_float(cur[e]);
+                }
+                release_acc();
+#pragma unroll 1
+                for (int c = 0; c < 8; ++c) {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) va[e] = __float_as_uint(stg[(c * 16 + e) * 128]);
+                    scan_slice(c, va, vb, cb, false);
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const bool more = c + 1 < 8;
+                    if ((c & 1) == 0) {
+                        wait_slice(va, ca);
+                        if (more) {
+                            __syncwarp();
+                            ld_slice(c + 1, vb, cb);
+                        } else {
+                            release_acc();
+                        }
+                        scan_slice(c, va, vb, cb, more);
                     } else {
-                        release_acc();
+                        wait_slice(vb, cb);
+                        if (more) {
+                            __syncwarp();
+                            ld_slice(c + 1, va, ca);
+                        } else {
+                            release_acc();
+                        }
+                        scan_slice(c, vb, va, ca, more);
                     }
-                    scan_slice(c, vb, va, ca, more);
                 }
             }
         }
@@ -964,12 +1011,13 @@ __global__ void __launch_bounds__(kRrWarps * 32)
 
 struct ScreenPlan {
     int stages = 0;
-    uint32_t buf_off = 0, pn_off = 0, bar_off = 0, total = 0;
+    uint32_t buf_off = 0, pn_off = 0, stg_off = 0, bar_off = 0, total = 0;
 };
 
-bool screen_plan(bool split, ScreenPlan& pl)
+bool screen_plan(bool split, bool corr, ScreenPlan& pl)
 {
-    const uint32_t stage_bytes = 2u * (split ? 2u : 1u) * kSChunk;
+    // operand chunk: 64 fp16 per row (corr: 32) of each part of A and B
+    const uint32_t stage_bytes = 2u * (split ? 2u : 1u) * (corr ? kSChunk / 2u : kSChunk);
     for (int S = 6; S >= 2; --S) {
         ScreenPlan t;
         t.stages = S;
@@ -978,6 +1026,8 @@ bool screen_plan(bool split, ScreenPlan& pl)
         off += static_cast<uint32_t>(kSBuf) * 128u * 4u;
         t.pn_off = off;
         off += 4u * kSTile * 4u;
+        t.stg_off = off;
+        if (corr) off += 128u * 128u * 4u;
         t.bar_off = off;
         off += 8u * (2u * S + 5u) + 16u;
         t.total = off;
@@ -1075,7 +1125,9 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     const int L = screen_list_len(pr.m_out);
     const int d16 = (pr.d + 63) / 64 * 64;
     ScreenPlan pl;
-    GTA_REQUIRE(screen_plan(split, pl), kInvalid, "screen: shared memory plan failed");
+    // long rows: the corrections in their own accumulator (see screen_kernel)
+    const bool corr = split && pr.d >= 256;
+    GTA_REQUIRE(screen_plan(split, corr, pl), kInvalid, "screen: shared memory plan failed");
     // the pool's rows as f32 (bucket-contiguous, pitch dp, zero past d) with their exact squared
     // norms, the scale's source (max ||x||) and the scaled fp16 operand rows
     const int dp = (pr.d + 31) / 32 * 32;
@@ -1097,10 +1149,11 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     {
         cuuint64_t dims[2] = {static_cast<cuuint64_t>(pr.parts) * d16, static_cast<cuuint64_t>(pr.n_rows)};
         cuuint64_t strides[1] = {static_cast<cuuint64_t>(pr.parts) * d16 * 2u};
-        cuuint32_t box[2] = {64u, 128u};
+        cuuint32_t box[2] = {corr ? 32u : 64u, 128u};
         cuuint32_t estr[2] = {1u, 1u};
         const CUresult r = screen_encode()(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, rows.get(), dims, strides, box, estr,
-                                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                           CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                           corr ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         GTA_REQUIRE(r == CUDA_SUCCESS, kCuda, "cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
     }
@@ -1116,7 +1169,7 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     ScreenArgs a{};
     a.norm = norm.get();
     a.maxnorm = bmax.get();
-    a.k_chunks = d16 / 64;
+    a.k_chunks = d16 / (corr ? 32 : 64);
     a.part_stride = d16;
     a.m_sel = pr.m_out;
     a.stages = pl.stages;
@@ -1130,7 +1183,6 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     // and, relative to (|a| + bmax)^2, the fp32 squared norms (each lane of the norm kernel chains
     // 4 ceil(dp / 128) products, then five butterfly additions) and the two fused operations of
     // the score; a 1.25 safety factor on both
-    const bool corr = split && pr.d >= 256;
     const double dd = pr.d;
     const double part_err = split ? 3.0 * std::ldexp(1.0, -22) : std::ldexp(1.0, -10);
     const double n_prod = split ? (corr ? dd + 3.0 : 3.0 * dd) : dd;
@@ -1144,6 +1196,7 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     a.buf_off = pl.buf_off;
     a.pn_off = pl.pn_off;
     a.bar_off = pl.bar_off;
+    a.stg_off = pl.stg_off;
     RerankX r{};
     r.pool = fpool.get();
     r.dp = dp;
