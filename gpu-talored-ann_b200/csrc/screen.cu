@@ -206,16 +206,14 @@ __device__ __noinline__ void flush_list(uint32_t tl, const uint32_t* buf, int nb
     tmem_st_wait();
 }
 
+// Column tiles of an item: the rows' own tile first (the nearest candidates: its threshold
+// tightens early), then every other tile in ascending order -- the CTAs of one bucket, which run
+// side by side, then read the same B tiles at about the same time and share them in L2.
 __device__ __forceinline__ int tile_order(int k, int t0, int n_ct)
 {
+    (void)n_ct;
     if (k == 0) return t0;
-    const int right = n_ct - 1 - t0, left = t0, m = min(right, left);
-    if (k <= 2 * m) {
-        const int j = (k + 1) >> 1;
-        return (k & 1) ? t0 + j : t0 - j;
-    }
-    const int rem = k - 2 * m;
-    return right > left ? t0 + m + rem : t0 - m - rem;
+    return k <= t0 ? k - 1 : k;
 }
 
 __device__ __forceinline__ bool drain_wait(uint32_t bar, uint32_t parity, int* err)
