@@ -358,7 +358,8 @@ def main():
               "knn_degree": cfg.knn_degree, "graph_degree": cfg.graph_degree, "kmeans_iters": cfg.kmeans_iters,
               "kmeans_sample": cfg.kmeans_sample or None,
               "l2": "inputs and intermediates larger than L2 (no flush needed)",
-              "parallelism": (f"{world} ranks, buckets sharded (NCCL all-reduce / all-to-all / all-gather)"
+              "parallelism": (f"{world} ranks, buckets sharded, a bucket above a rank's share of n_b^2 cut into "
+                              "row ranges on several ranks (NCCL all-reduce / all-to-all / all-gather)"
                               if world > 1 else "1 GPU"),
               "shards": "one seeded mixture; rank r holds its contiguous block of N/W rows (strong scaling)"}
 
@@ -536,11 +537,17 @@ def main():
         res = gd.build_sharded(Xd, prm, timing=True)
         sizes = torch.tensor(res.sizes, dtype=torch.float64)
         phases = {k: round(v, 3) for k, v in res.phase_ms.items()}
+        n_pieces = {}
+        for b, _, _, _ in res.pieces:
+            n_pieces[b] = n_pieces.get(b, 0) + 1
+        split = {b: c for b, c in n_pieces.items() if c > 1}
         t = torch.tensor([phases[k] for k in phases], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         phases = {k: round(float(v), 3) for k, v in zip(phases, t.tolist())}
     skew = {"max_bucket": int(sizes.max()), "sum_sq_over_balanced": float((sizes * sizes).sum() * sizes.numel()
                                                                          / sizes.sum() ** 2)}
+    if world > 1:
+        skew["split_buckets"] = {str(b): c for b, c in sorted(split.items())}  # bucket -> ranks sharing it
 
     # quality: recall@32 of the pre-prune kNN graph on 1000 sampled points of rank 0's rows
     # (exact GT over the whole job's dataset in fp64 on the GPU)

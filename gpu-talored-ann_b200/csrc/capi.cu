@@ -358,6 +358,8 @@ struct KnnPhase {
     int64_t seed_stride = 1;
     const int64_t* mem_row = nullptr;  // phase 3: seeds read from the phase-1 rows of the lists
     int64_t n_points = 0;              // phase 3: N
+    const int64_t* row_lo = nullptr;   // host [B] (with row_hi): only rows [row_lo[b], row_hi[b]) of
+    const int64_t* row_hi = nullptr;   // bucket b (relative to its first row) get lists; null: all
 };
 
 // members: the row of X gathered into each membership slot (grouped by bucket);
@@ -396,6 +398,10 @@ void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* 
             if (off[b + 1] == off[b]) continue;
             sp.seg_lo.push_back(off[b] - j0);
             sp.seg_n.push_back(off[b + 1] - off[b]);
+            if (ph.row_lo) {
+                sp.seg_r0.push_back(ph.row_lo[b]);
+                sp.seg_r1.push_back(ph.row_hi[b]);
+            }
         }
         sp.m_out = M; sp.parts = 2; sp.out_ids = list_ids; sp.out_dists = list_dists; sp.err = err;
         sp.prof_name = "dist_topk_bucket";
@@ -421,6 +427,10 @@ void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* 
         const int64_t s = phase == 0 ? 0 : std::min(nb, std::max<int64_t>(0, ph.split[b] - off[b]));
         r_lo = phase == 1 ? s : 0;
         r_hi = phase == 2 ? s : nb;
+        if (ph.row_lo) {
+            r_lo = std::max(r_lo, ph.row_lo[b]);
+            r_hi = std::max(r_lo, std::min(r_hi, ph.row_hi[b]));
+        }
     };
     DistTopkProblem pr;
     pr.A = pool.get(); pr.a_total = n_mem; pr.B = pool.get(); pr.b_total = n_mem; pr.elem = elem; pr.d = d;
@@ -1876,38 +1886,72 @@ int gta_bucket_knn_rows(const void* R, int32_t dtype, int64_t n, int32_t d, cons
     });
 }
 
+namespace {
+void bucket_knn_rows_seeded(const void* R, int32_t dtype, int64_t n, int32_t d, const int32_t* order, const int32_t* gid,
+                            const int64_t* offsets, const int32_t* partner, int32_t B, int32_t M, int32_t phase,
+                            const float* seed, const int64_t* row_lo, const int64_t* row_hi, int32_t* list_ids,
+                            float* list_dists, cudaStream_t st, const char* who)
+{
+    GTA_REQUIRE(offsets && B >= 1 && M >= 1 && M <= 128 && n >= 0 && (phase == 1 || phase == 2) &&
+                    (n == 0 || (R && order && gid && partner && list_ids && list_dists)) &&
+                    (phase == 1 || n == 0 || seed) && (row_lo == nullptr) == (row_hi == nullptr),
+                kInvalid, std::string(who) + ": bad argument");
+    if (n == 0) return;
+    std::vector<int64_t> off;
+    if (row_lo) {
+        off.resize(static_cast<size_t>(B) + 1);
+        GTA_CUDA(cudaMemcpyAsync(off.data(), offsets, sizeof(int64_t) * (B + 1), cudaMemcpyDeviceToHost, st));
+        GTA_CUDA(cudaStreamSynchronize(st));
+        for (int b = 0; b < B; ++b)
+            GTA_REQUIRE(0 <= row_lo[b] && row_lo[b] <= row_hi[b] && row_hi[b] <= off[b + 1] - off[b], kInvalid,
+                        std::string(who) + ": row range outside its bucket");
+    }
+    const int elem = knn_elem(dtype, d, M);
+    const bool seedable = dist_topk_seedable(elem, pad_dim(d, elem), M);
+    if (!seedable && phase == 2) return;  // phase 1 wrote every row
+    DevBuf<int> err(1, st);
+    GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+    DevBuf<int32_t> gid_sorted(static_cast<size_t>(n), st);
+    gather_i32(gid, order, n, gid_sorted.get(), st);
+    KnnPhase ph;
+    std::vector<int64_t> split_h;
+    if (seedable) {
+        DevBuf<int64_t> split_d(static_cast<size_t>(B), st);
+        split_from_partner(partner, offsets, B, split_d.get(), st);
+        split_h.resize(static_cast<size_t>(B));
+        GTA_CUDA(cudaMemcpyAsync(split_h.data(), split_d.get(), sizeof(int64_t) * B, cudaMemcpyDeviceToHost, st));
+        GTA_CUDA(cudaStreamSynchronize(st));
+        ph.phase = phase; ph.split = split_h.data(); ph.partner = partner; ph.seed = seed; ph.seed_stride = 1;
+    }
+    ph.row_lo = row_lo;
+    ph.row_hi = row_hi;
+    bucket_knn_impl(R, dtype, n, d, order, offsets, B, M, list_ids, list_dists, err.get(), st, gid_sorted.get(), 0, -1,
+                    off.empty() ? nullptr : off.data(), ph);
+    check_device_error(err.get(), st, who);
+}
+}  // namespace
+
 int gta_bucket_knn_rows_phased(const void* R, int32_t dtype, int64_t n, int32_t d, const int32_t* order,
                                const int32_t* gid, const int64_t* offsets, const int32_t* partner, int32_t B, int32_t M,
                                int32_t phase, const float* seed, int32_t* list_ids, float* list_dists, void* stream)
 {
     return guard([&] {
         GTA_WORKSPACE(stream);
-        GTA_REQUIRE(offsets && B >= 1 && M >= 1 && M <= 128 && n >= 0 && (phase == 1 || phase == 2) &&
-                        (n == 0 || (R && order && gid && partner && list_ids && list_dists)) &&
-                        (phase == 1 || n == 0 || seed),
-                    kInvalid, "gta_bucket_knn_rows_phased: bad argument");
-        if (n == 0) return;
-        cudaStream_t st = S(stream);
-        const int elem = knn_elem(dtype, d, M);
-        const bool seedable = dist_topk_seedable(elem, pad_dim(d, elem), M);
-        if (!seedable && phase == 2) return;  // phase 1 wrote every row
-        DevBuf<int> err(1, st);
-        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
-        DevBuf<int32_t> gid_sorted(static_cast<size_t>(n), st);
-        gather_i32(gid, order, n, gid_sorted.get(), st);
-        KnnPhase ph;
-        std::vector<int64_t> split_h;
-        if (seedable) {
-            DevBuf<int64_t> split_d(static_cast<size_t>(B), st);
-            split_from_partner(partner, offsets, B, split_d.get(), st);
-            split_h.resize(static_cast<size_t>(B));
-            GTA_CUDA(cudaMemcpyAsync(split_h.data(), split_d.get(), sizeof(int64_t) * B, cudaMemcpyDeviceToHost, st));
-            GTA_CUDA(cudaStreamSynchronize(st));
-            ph.phase = phase; ph.split = split_h.data(); ph.partner = partner; ph.seed = seed; ph.seed_stride = 1;
-        }
-        bucket_knn_impl(R, dtype, n, d, order, offsets, B, M, list_ids, list_dists, err.get(), st, gid_sorted.get(), 0,
-                        -1, nullptr, ph);
-        check_device_error(err.get(), st, "gta_bucket_knn_rows_phased");
+        bucket_knn_rows_seeded(R, dtype, n, d, order, gid, offsets, partner, B, M, phase, seed, nullptr, nullptr,
+                               list_ids, list_dists, S(stream), "gta_bucket_knn_rows_phased");
+    });
+}
+
+int gta_bucket_knn_rows_ranged(const void* R, int32_t dtype, int64_t n, int32_t d, const int32_t* order,
+                               const int32_t* gid, const int64_t* offsets, const int32_t* partner, int32_t B, int32_t M,
+                               int32_t phase, const float* seed, const int64_t* row_lo, const int64_t* row_hi,
+                               int32_t* list_ids, float* list_dists, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(row_lo && row_hi, kInvalid, "gta_bucket_knn_rows_ranged: null row range");
+        bucket_knn_rows_seeded(R, dtype, n, d, order, gid, offsets, partner, B, M, phase, seed, row_lo, row_hi,
+                               list_ids, list_dists, S(stream), "gta_bucket_knn_rows_ranged");
     });
 }
 

@@ -152,6 +152,7 @@ struct ScreenProblem {
     const int32_t* gid = nullptr;   // [n_rows] pool row -> output id
     int64_t n_rows = 0;
     std::vector<int64_t> seg_lo, seg_n;  // segments: first pool row and length
+    std::vector<int64_t> seg_r0, seg_r1; // rows [r0, r1) of each segment get lists (empty: all)
     int m_out = 0;
     int parts = 2;
     int32_t* out_ids = nullptr;     // [n_rows x m_out]

@@ -943,7 +943,9 @@ __global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p)
 // Rows of segments that run as column chunks, one chunk per wave: the row's running list (the
 // exact top-m_out of the chunks so far, in its chunk-0 extension row) and its seed (the running
 // list's m_out-th distance, a bound on the row's exact M-th that the next chunk's screen and
-// rerank use).  Chunk k of pool row lo + i sits at extension row base_ext + k * nb + i.
+// rerank use).  lo, nb: the first pool row with a list and the count of such rows (a row range of
+// the segment, whose columns are all its rows).  Chunk k of pool row lo + i sits at extension row
+// base_ext + k * nb + i.
 struct ChunkSeg {
     int64_t lo, nb, base_ext, row_prefix;  // base_ext: extension row of (chunk 0, row 0)
     int32_t nch, pad;
@@ -1086,36 +1088,45 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     std::vector<double> wave_flops(1, 0.0);
     std::vector<ChunkSeg> chunked;
     int64_t ext_rows = 0, chunked_rows = 0;
+    GTA_REQUIRE((pr.seg_r0.empty() && pr.seg_r1.empty()) ||
+                    (pr.seg_r0.size() == pr.seg_lo.size() && pr.seg_r1.size() == pr.seg_lo.size()),
+                kInvalid, "screen: row ranges need one entry per segment");
     for (size_t sgi = 0; sgi < pr.seg_lo.size(); ++sgi) {
         const int64_t lo = pr.seg_lo[sgi], nb = pr.seg_n[sgi];
         GTA_REQUIRE(lo >= 0 && nb >= 1 && lo + nb <= pr.n_rows, kInvalid, "screen: bad segment");
+        // the segment's rows that get lists: [r0, r1) of its nb (every row is a column)
+        const int64_t r0 = pr.seg_r0.empty() ? 0 : pr.seg_r0[sgi];
+        const int64_t r1 = pr.seg_r1.empty() ? nb : pr.seg_r1[sgi];
+        GTA_REQUIRE(0 <= r0 && r0 <= r1 && r1 <= nb, kInvalid, "screen: bad row range");
+        if (r0 == r1) continue;
+        const int64_t nr = r1 - r0;
         const int nch = static_cast<int>((nb + kChunk - 1) / kChunk);
         if (nch == 1) {
-            for (int64_t t = 0; t < nb; t += 128)
-                waves[0].push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, nb - t)),
+            for (int64_t t = r0; t < r1; t += 128)
+                waves[0].push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, r1 - t)),
                                             static_cast<int32_t>(lo), static_cast<int32_t>(nb), static_cast<int32_t>(t),
                                             static_cast<int32_t>(lo + t), 1, -1});
-            wave_flops[0] += 2.0 * static_cast<double>(nb) * static_cast<double>(nb) * pr.d;
+            wave_flops[0] += 2.0 * static_cast<double>(nr) * static_cast<double>(nb) * pr.d;
             continue;
         }
         const int64_t base = pr.n_rows + ext_rows;
-        chunked.push_back(ChunkSeg{lo, nb, ext_rows, chunked_rows, nch, 0});
+        chunked.push_back(ChunkSeg{lo + r0, nr, ext_rows, chunked_rows, nch, 0});
         if (static_cast<int>(waves.size()) < nch) {
             waves.resize(static_cast<size_t>(nch));
             wave_flops.resize(static_cast<size_t>(nch), 0.0);
         }
         for (int k = 0; k < nch; ++k) {
             const int64_t c0 = k * kChunk, cn = std::min<int64_t>(kChunk, nb - c0);
-            for (int64_t t = 0; t < nb; t += 128)
+            for (int64_t t = r0; t < r1; t += 128)
                 waves[static_cast<size_t>(k)].push_back(
-                    WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, nb - t)),
+                    WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, r1 - t)),
                              static_cast<int32_t>(lo + c0), static_cast<int32_t>(cn), static_cast<int32_t>(t - c0),
-                             static_cast<int32_t>(base + k * nb + t), 1,
-                             k == 0 ? -1 : static_cast<int32_t>(chunked_rows + t)});
-            wave_flops[static_cast<size_t>(k)] += 2.0 * static_cast<double>(nb) * static_cast<double>(cn) * pr.d;
+                             static_cast<int32_t>(base + k * nr + (t - r0)), 1,
+                             k == 0 ? -1 : static_cast<int32_t>(chunked_rows + (t - r0))});
+            wave_flops[static_cast<size_t>(k)] += 2.0 * static_cast<double>(nr) * static_cast<double>(cn) * pr.d;
         }
-        ext_rows += static_cast<int64_t>(nch) * nb;
-        chunked_rows += nb;
+        ext_rows += static_cast<int64_t>(nch) * nr;
+        chunked_rows += nr;
     }
     const int64_t item_rows = pr.n_rows + ext_rows;
     GTA_REQUIRE(item_rows < (1ll << 31), kInvalid, "screen: too many list rows");

@@ -17,15 +17,19 @@ come before rank r+1's).  The steps and their exchanges:
      an all-reduce of both, new means.
   2. Top-2 buckets of the local rows.
   3. Bucket placement: global bucket sizes (all-reduce), then longest-processing-
-     time placement on the cost n_b^2, the same on every rank.
-  4. Points to bucket owners (all-to-all of rows and (id, bucket, other) triples),
-     grouped by (bucket, other) in arrival order: the membership order of the
-     single-GPU build.
-  5. Per-bucket all-pairs top-M on the owner, in two passes: the rows whose bucket is
-     the lower of their point's two, then (after an all-reduce (min) of each point's
-     lower-list M-th distance by global id) the other rows, bounded by that distance
-     and skipping the points of the lower bucket; the merged lists are unchanged.
-  6. Lists back to the points' owners (all-to-all), merged per point.
+     time placement on the cost n_b^2, the same on every rank.  A bucket that costs
+     more than a rank's share of the whole is cut into row ranges (pieces) placed on
+     distinct ranks, each of which holds all the bucket's rows as columns.
+  4. Points to every rank holding a piece of their bucket (all-to-all of rows and
+     (id, bucket, other) triples), grouped by (bucket, other) in arrival order: the
+     membership order of the single-GPU build, the same on every holder.
+  5. Per-bucket all-pairs top-M on the holders, each for its row range, in two
+     passes: the rows whose bucket is the lower of their point's two, then (after an
+     all-reduce (min) of each point's lower-list M-th distance by global id) the
+     other rows, bounded by that distance and skipping the points of the lower
+     bucket; the merged lists are unchanged.
+  6. The lists of each rank's row ranges back to the points' owners (all-to-all),
+     merged per point.
   7. CAGRA: sanitize the local rows, all-gather the id table, prune the local rows,
      all-gather the pruned graph, merge reverse edges into the local rows.
 
@@ -61,6 +65,9 @@ class ShardParams:
     kmeans_iters: int = 10
     kmeans_sample: int = 0
     seed: int = 42
+    # a bucket whose cost n_b^2 exceeds split_share x (sum n_b^2 / ranks) runs as row ranges on
+    # several ranks (inf: whole buckets only)
+    split_share: float = 1.0
 
 
 @dataclass
@@ -72,7 +79,8 @@ class ShardResult:
     centroids: torch.Tensor  # B x d float32
     top2: torch.Tensor  # n_local x 2 int32
     graph: Optional[torch.Tensor] = None  # n_local x K (int32 view of uint32 ids)
-    owner: Optional[list] = None  # bucket -> rank
+    owner: Optional[list] = None  # bucket -> rank (of its first piece)
+    pieces: Optional[list] = None  # (bucket, rank, row_lo, row_hi) per piece, by (bucket, row_lo)
     sizes: Optional[list] = None  # memberships per bucket (whole job)
     comm_bytes: int = 0  # bytes this rank sent
     phase_ms: Optional[dict] = None  # device time per phase when timing was requested
@@ -163,6 +171,17 @@ class CudaStages:
                                                   _p(offsets), _p(partner), offsets.numel() - 1, M, phase, _p(seed),
                                                   _p(lid), _p(ldist), self._st()))
 
+    def bucket_knn_rows_ranged(self, R, order, gid, offsets, partner, M, phase, seed, row_lo, row_hi, lid, ldist):
+        """Rows of one phase and of each bucket's range [row_lo[b], row_hi[b]) (host int64 tensors)
+        into lid / ldist (see gta_bucket_knn_rows_ranged)."""
+        n = R.shape[0]
+        rlo = row_lo.to(torch.int64).contiguous()
+        rhi = row_hi.to(torch.int64).contiguous()
+        L.check(self.L.gta_bucket_knn_rows_ranged(_p(R), _ELEM[R.dtype], n, R.shape[1], _p(order), _p(gid),
+                                                  _p(offsets), _p(partner), offsets.numel() - 1, M, phase, _p(seed),
+                                                  ctypes.c_void_p(rlo.data_ptr()), ctypes.c_void_p(rhi.data_ptr()),
+                                                  _p(lid), _p(ldist), self._st()))
+
     def merge_memberships(self, lid, ldist, mem_row):
         n, M = mem_row.shape[0], lid.shape[1]
         ids = torch.empty((n, M), dtype=torch.int32, device=lid.device)
@@ -192,20 +211,46 @@ class CudaStages:
 
 # ---------------------------------------------------------------- host logic
 def place_buckets(sizes, world: int) -> list:
-    """Longest-processing-time placement of buckets on ranks by cost n_b^2.
+    """Longest-processing-time placement of whole buckets on ranks by cost n_b^2.
 
     Largest cost first (ties: lower bucket id), each to the least-loaded rank
     (ties: lower rank).  Deterministic, so every rank computes the same owners.
     """
-    sizes = [int(s) for s in sizes]
-    order = sorted(range(len(sizes)), key=lambda b: (-sizes[b] * sizes[b], b))
+    return [p[1] for p in place_pieces(sizes, world, float("inf"))]
+
+
+def place_pieces(sizes, world: int, split_share: float = 1.0, align: int = 128) -> list:
+    """Row ranges of buckets placed on ranks: [(bucket, rank, row_lo, row_hi)] by (bucket, row_lo).
+
+    A bucket of n rows costs n^2 (all pairs).  One whose cost exceeds split_share x the
+    mean cost per rank is cut into s = min(ranks, ceil(cost / that), n // align) pieces of
+    about n / s rows (cuts at multiples of ``align``), each costing its rows x n; every
+    other bucket is one piece [0, n).  Pieces are placed longest-processing-time: largest
+    cost first (ties: bucket, then row_lo), each on the least-loaded rank (ties: lower rank)
+    that holds no other piece of its bucket.  Deterministic, so every rank computes the
+    same placement.
+    """
+    sizes = [int(x) for x in sizes]
+    share = split_share * sum(x * x for x in sizes) / max(world, 1)
+    items = []
+    for b, n in enumerate(sizes):
+        s = 1
+        if world > 1 and n > 0 and n * n > share:
+            s = max(1, min(world, -(-(n * n) // max(int(share), 1)), n // align))
+        cuts = [(i * n // s) // align * align for i in range(s)] + [n]
+        for i in range(s):
+            items.append(((cuts[i + 1] - cuts[i]) * n, b, cuts[i], cuts[i + 1]))
+    items.sort(key=lambda it: (-it[0], it[1], it[2]))
     load = [0] * world
-    owner = [0] * len(sizes)
-    for b in order:
-        r = min(range(world), key=lambda q: (load[q], q))
-        owner[b] = r
-        load[r] += sizes[b] * sizes[b]
-    return owner
+    held = [set() for _ in range(world)]
+    out = []
+    for cost, b, lo, hi in items:
+        r = min((q for q in range(world) if b not in held[q]), key=lambda q: (load[q], q))
+        load[r] += cost
+        held[r].add(b)
+        out.append((b, r, lo, hi))
+    out.sort(key=lambda p: (p[0], p[2]))
+    return out
 
 
 def _exchange(send: torch.Tensor, send_counts: torch.Tensor, recv_counts: torch.Tensor, group=None) -> torch.Tensor:
@@ -315,15 +360,33 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
     sizes = torch.bincount(top2.reshape(-1).long(), minlength=B).to(torch.int64)
     dist.all_reduce(sizes, group=group)
     sizes_l = sizes.tolist()
-    owner = place_buckets(sizes_l, world)
-    owner_t = torch.tensor(owner, dtype=torch.int64, device=dev)
+    pieces = place_pieces(sizes_l, world, prm.split_share)
+    hold_n = [0] * B
+    row_lo, row_hi = [0] * B, [0] * B
+    owner = [-1] * B
+    for b, r, lo, hi in pieces:
+        hold_n[b] += 1
+        if owner[b] < 0:
+            owner[b] = r
+        if r == rank:
+            row_lo[b], row_hi[b] = lo, hi
+    hold_off = [0] * (B + 1)
+    for b in range(B):
+        hold_off[b + 1] = hold_off[b] + hold_n[b]
+    hold_n_t = torch.tensor(hold_n, dtype=torch.int64, device=dev)
+    hold_off_t = torch.tensor(hold_off[:B], dtype=torch.int64, device=dev)
+    hold_rank_t = torch.tensor([p[1] for p in pieces], dtype=torch.int64, device=dev)
     ph.mark("top2_placement")
 
-    # ---- 4. memberships to bucket owners: slot s of point p is membership 2p+s
+    # ---- 4. memberships to every holder of their bucket: slot s of point p is membership 2p+s,
+    # sent once per piece of its bucket, in membership order within each destination
     bucket = top2.reshape(-1)
     other = top2.flip(1).reshape(-1)
-    dest = owner_t[bucket.long()]
-    perm = torch.sort(dest, stable=True).indices
+    nh = hold_n_t[bucket.long()]
+    mi = torch.repeat_interleave(torch.arange(bucket.numel(), device=dev), nh)
+    copy = torch.arange(mi.numel(), device=dev) - (torch.cumsum(nh, 0) - nh)[mi]
+    dest = hold_rank_t[hold_off_t[bucket[mi].long()] + copy]
+    perm = mi[torch.sort(dest, stable=True).indices]
     send_counts = torch.bincount(dest, minlength=world).to(torch.int64)
     recv_counts = torch.empty_like(send_counts)
     dist.all_to_all_single(recv_counts, send_counts, group=group)
@@ -335,44 +398,52 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
     R = R.view(X_local.dtype).reshape(-1, d)
     meta_r = _exchange(meta, send_counts, recv_counts, group)
     sent += rows.numel() * elem + meta.numel() * 4
-    del rows, meta
+    del rows, meta, mi, copy, dest
     ph.mark("exchange_points")
 
-    # ---- 5. per-bucket top-M on the owner: first the rows whose bucket is the lower of their
-    # point's two, then the others, bounded by the point's lower-bucket list (its M-th distance,
-    # gathered by global id over the ranks) and skipping the points of that lower bucket
+    # ---- 5. per-bucket top-M for this rank's row range of each bucket it holds: first the rows
+    # whose bucket is the lower of their point's two, then the others, bounded by the point's
+    # lower-bucket list (its M-th distance, gathered by global id over the ranks) and skipping the
+    # points of that lower bucket
     gid_r = meta_r[:, 0].contiguous()
     order, offsets = st.group_memberships(meta_r[:, 1].contiguous(), meta_r[:, 2].contiguous(), B)
     n_r = R.shape[0]
     ol = order.long()
     bucket_s = meta_r[:, 1][ol]
     partner_s = meta_r[:, 2][ol].contiguous()
+    bl = bucket_s.long()
+    rel = torch.arange(n_r, device=dev) - offsets[bl]
+    mine = (rel >= torch.tensor(row_lo, dtype=torch.int64, device=dev)[bl]) & \
+        (rel < torch.tensor(row_hi, dtype=torch.int64, device=dev)[bl])
+    rlo_h = torch.tensor(row_lo, dtype=torch.int64)
+    rhi_h = torch.tensor(row_hi, dtype=torch.int64)
     lid = torch.full((n_r, M), -1, dtype=torch.int32, device=dev)
     ldist = torch.full((n_r, M), float("inf"), dtype=torch.float32, device=dev)
-    st.bucket_knn_rows_phased(R, order, gid_r, offsets, partner_s, M, 1, None, lid, ldist)
+    st.bucket_knn_rows_ranged(R, order, gid_r, offsets, partner_s, M, 1, None, rlo_h, rhi_h, lid, ldist)
     seed = torch.full((N,), float("inf"), dtype=torch.float32, device=dev)
-    lower = partner_s > bucket_s
+    lower = (partner_s > bucket_s) & mine
     seed[gid_r[ol][lower].long()] = ldist[lower, M - 1]
     dist.all_reduce(seed, op=dist.ReduceOp.MIN, group=group)
-    st.bucket_knn_rows_phased(R, order, gid_r, offsets, partner_s, M, 2, seed, lid, ldist)
+    st.bucket_knn_rows_ranged(R, order, gid_r, offsets, partner_s, M, 2, seed, rlo_h, rhi_h, lid, ldist)
     del R, seed
     ph.mark("bucket_knn")
 
-    # ---- 6. lists back to the points' owners, merged per point
-    og = gid_r[order.long()]
-    ob = meta_r[:, 1][order.long()]
+    # ---- 6. the range's lists back to the points' owners, merged per point
+    sel = mine.nonzero().squeeze(1)
+    og = gid_r[ol[sel]]
+    ob = bucket_s[sel]
     starts_t = torch.tensor(starts[1:world], dtype=torch.int64, device=dev)
     dest2 = torch.bucketize(og.long(), starts_t, right=True)
-    perm2 = torch.sort(dest2, stable=True).indices
+    perm2 = sel[torch.sort(dest2, stable=True).indices]
     send2 = torch.bincount(dest2, minlength=world).to(torch.int64)
     recv2 = torch.empty_like(send2)
     dist.all_to_all_single(recv2, send2, group=group)
-    meta2 = torch.stack([og[perm2], ob[perm2]], dim=1).to(torch.int32)
+    meta2 = torch.stack([gid_r[ol[perm2]], bucket_s[perm2]], dim=1).to(torch.int32)
     lid_b = _exchange(lid[perm2], send2, recv2, group)
     ldist_b = _exchange(ldist[perm2], send2, recv2, group)
     meta_b = _exchange(meta2, send2, recv2, group)
-    sent += lid.numel() * 8 + meta2.numel() * 4
-    del lid, ldist
+    sent += perm2.numel() * M * 8 + meta2.numel() * 4
+    del lid, ldist, og, ob
     ph.mark("exchange_lists")
     p = (meta_b[:, 0].long() - row0)
     lo_bucket = torch.minimum(top2[:, 0], top2[:, 1])
@@ -384,7 +455,7 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
     ph.mark("merge")
 
     res = ShardResult(row0=row0, n_total=N, knn_ids=knn_ids, knn_dists=knn_dists, centroids=C, top2=top2,
-                      owner=owner, sizes=sizes_l)
+                      owner=owner, pieces=pieces, sizes=sizes_l)
     # ---- 7. CAGRA
     if prm.graph_degree > 0:
         K = prm.graph_degree

@@ -368,6 +368,20 @@ int gta_bucket_knn_rows_phased(const void* R, int32_t dtype, int64_t n, int32_t 
                                const int32_t* gid, const int64_t* offsets, const int32_t* partner, int32_t B, int32_t M,
                                int32_t phase, const float* seed, int32_t* list_ids, float* list_dists, void* stream);
 
+/* gta_bucket_knn_rows_phased restricted to row ranges: only grouped rows
+ * [offsets[b] + row_lo[b], offsets[b] + row_hi[b]) of bucket b get lists (row_lo, row_hi: HOST
+ * arrays [B], 0 <= row_lo[b] <= row_hi[b] <= the bucket's size); every row of the bucket stays a
+ * column.  Other rows of list_ids / list_dists are left as they are.  The sharded build's split
+ * buckets: each rank that shares a bucket holds all its rows and fills a disjoint range, so the
+ * ranges' lists together equal the bucket's lists of gta_bucket_knn_rows_phased.  Returns
+ * GTA_EINVAL for a range outside its bucket.  Extends the interface gta_bucket_knn_rows
+ * replaces (the per-bucket kNN of one bucket's memberships, multi-GPU: one bucket on several
+ * devices). */
+int gta_bucket_knn_rows_ranged(const void* R, int32_t dtype, int64_t n, int32_t d, const int32_t* order,
+                               const int32_t* gid, const int64_t* offsets, const int32_t* partner, int32_t B, int32_t M,
+                               int32_t phase, const float* seed, const int64_t* row_lo, const int64_t* row_hi,
+                               int32_t* list_ids, float* list_dists, void* stream);
+
 /* gta_sanitize for rows [row0, row0 + n_rows) of an n-row graph (knn and out
  * hold only those rows). */
 int gta_sanitize_rows(const int32_t* knn, int64_t n_rows, int64_t row0, int64_t n, int32_t m, uint32_t* out,

@@ -118,6 +118,16 @@ class OracleStages:
             lid[int(j)] = torch.from_numpy(row_i)
             ldist[int(j)] = torch.from_numpy(row_d)
 
+    def bucket_knn_rows_ranged(self, R, order, gid, offsets, partner, M, phase, seed, row_lo, row_hi, lid, ldist):
+        """bucket_knn_rows_phased, then only the rows of each bucket's range kept."""
+        tl, td = lid.clone(), ldist.clone()
+        self.bucket_knn_rows_phased(R, order, gid, offsets, partner, M, phase, seed, tl, td)
+        off = _np(offsets)
+        for b in range(off.shape[0] - 1):
+            lo, hi = off[b] + int(row_lo[b]), off[b] + int(row_hi[b])
+            lid[lo:hi] = tl[lo:hi]
+            ldist[lo:hi] = td[lo:hi]
+
     def merge_memberships(self, lid, ldist, mem_row):
         ids, dd = orc.merge_memberships(_np(lid), _np(ldist), _np(mem_row))
         return _t(ids), _t(dd)
@@ -155,7 +165,8 @@ def gloo_worker(rank, world, port, X, counts, C0, prm_kw, out_dir):
         res = gd.build_sharded(Xl, prm, stages=OracleStages(), init_centroids=torch.from_numpy(C0))
         np.savez(os.path.join(out_dir, f"rank{rank}.npz"), row0=res.row0, ids=_np(res.knn_ids),
                  dists=_np(res.knn_dists), C=_np(res.centroids), top2=_np(res.top2),
-                 graph=_np(res.graph) if res.graph is not None else np.zeros(0), owner=np.array(res.owner))
+                 graph=_np(res.graph) if res.graph is not None else np.zeros(0), owner=np.array(res.owner),
+                 pieces=np.array(res.pieces, dtype=np.int64))
     finally:
         dist.destroy_process_group()
 

@@ -49,13 +49,40 @@ def test_place_buckets_is_deterministic_and_balanced():
     assert gd.place_buckets([5, 5], 1) == [0, 0]
 
 
-@pytest.mark.parametrize("world,counts", [(2, [1300, 1700]), (3, [1000, 1000, 1000])])
-def test_sharded_build_matches_single_pipeline(world, counts):
+def test_place_pieces_splits_a_dominant_bucket_over_distinct_ranks():
+    sizes = [5000, 300, 280, 260, 250, 240, 230, 220]
+    for world in (2, 4, 8):
+        pcs = gd.place_pieces(sizes, world)
+        assert pcs == gd.place_pieces(sizes, world)
+        big = [p for p in pcs if p[0] == 0]
+        assert len(big) == world  # 5000^2 is almost the whole job
+        assert len({p[1] for p in big}) == world  # distinct ranks
+        assert big[0][2] == 0 and big[-1][3] == 5000
+        assert all(a[3] == b[2] for a, b in zip(big, big[1:]))  # contiguous row ranges
+        assert all(p[2] % 128 == 0 for p in big)
+        for b in range(1, len(sizes)):  # the others stay whole
+            assert [(p[2], p[3]) for p in pcs if p[0] == b] == [(0, sizes[b])]
+        load = np.zeros(world)
+        for b, r, lo, hi in pcs:
+            load[r] += (hi - lo) * sizes[b]
+        assert load.max() <= 1.15 * load.mean()
+    # whole buckets only: one piece each, the placement of place_buckets
+    pcs = gd.place_pieces(sizes, 4, float("inf"))
+    assert [(p[2], p[3]) for p in pcs] == [(0, n) for n in sizes]
+    assert [p[1] for p in pcs] == gd.place_buckets(sizes, 4)
+    # a bucket is never cut below the alignment
+    assert [(p[2], p[3]) for p in gd.place_pieces([200, 10], 4) if p[0] == 0] == [(0, 200)]
+
+
+@pytest.mark.parametrize("world,counts,split", [(2, [1300, 1700], 1.0), (3, [1000, 1000, 1000], 1.0),
+                                                (2, [1300, 1700], 0.05), (3, [1000, 1000, 1000], 0.05)])
+def test_sharded_build_matches_single_pipeline(world, counts, split):
     N, d, B, M, K, iters = sum(counts), 16, 8, 16, 8, 3
     X = _data(N, d, 20, seed=7)
     rng = np.random.default_rng(1)
     C0 = X[rng.choice(N, B, replace=False)].astype(np.float32)
-    prm = dict(n_buckets=B, knn_degree=M, graph_degree=K, kmeans_iters=iters, kmeans_sample=0, seed=42)
+    prm = dict(n_buckets=B, knn_degree=M, graph_degree=K, kmeans_iters=iters, kmeans_sample=0, seed=42,
+               split_share=split)
 
     # the single-process oracle pipeline on the same sample
     n_s = max(orc.default_sample_size(N), B)
@@ -75,6 +102,9 @@ def test_sharded_build_matches_single_pipeline(world, counts):
         np.testing.assert_array_equal(p["C"], ref["centroids"])
         np.testing.assert_array_equal(p["owner"], parts[0]["owner"])
     assert len(set(parts[0]["owner"].tolist())) == world  # every rank owns buckets
+    pcs = parts[0]["pieces"]
+    if split < 1.0:  # buckets cut into row ranges on several ranks
+        assert len(pcs) > B
     np.testing.assert_array_equal(top2, ref["top2"])
     np.testing.assert_array_equal(ids, ref["knn_ids"])
     np.testing.assert_array_equal(dists, ref["knn_dists"])

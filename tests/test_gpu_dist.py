@@ -97,6 +97,81 @@ def test_centroid_partials_and_grouping():
     assert not g[2].any() and not g[4].any()
 
 
+def _memberships(X, top2, B):
+    """Every membership (point p, slot s) as received row 2p+s: rows, global ids, grouping."""
+    st = gd.CudaStages()
+    bucket = top2.reshape(-1).contiguous()
+    other = top2.flip(1).reshape(-1).contiguous()
+    p_of = torch.arange(bucket.numel(), device="cuda") // 2
+    R = X[p_of].contiguous()
+    gid = p_of.to(torch.int32)
+    order, offsets = st.group_memberships(bucket, other, B)
+    ol = order.long()
+    return st, R, gid, order, offsets, bucket[ol], other[ol].contiguous()
+
+
+def _two_phases(st, R, gid, order, offsets, bucket_s, partner_s, M, rng=None, seed2=None):
+    """Both passes; phase 2's seeds from phase 1's lists, or seed2 (a whole run's seeds: the
+    all-reduce of the sharded build)."""
+    n, N = R.shape[0], R.shape[0] // 2
+    lid = torch.full((n, M), -1, dtype=torch.int32, device="cuda")
+    ldist = torch.full((n, M), float("inf"), dtype=torch.float32, device="cuda")
+    run = (lambda ph, sd: st.bucket_knn_rows_phased(R, order, gid, offsets, partner_s, M, ph, sd, lid, ldist)) \
+        if rng is None else \
+        (lambda ph, sd: st.bucket_knn_rows_ranged(R, order, gid, offsets, partner_s, M, ph, sd, rng[0], rng[1], lid,
+                                                  ldist))
+    run(1, None)
+    seed = torch.full((N,), float("inf"), dtype=torch.float32, device="cuda")
+    lower = partner_s > bucket_s
+    seed[gid[order.long()][lower].long()] = ldist[lower, M - 1]
+    run(2, seed if seed2 is None else seed2)
+    return lid, ldist, seed
+
+
+@pytest.mark.parametrize("kind", ["u8", "f32", "f32_long"])
+def test_ranged_rows_match_whole_buckets(kind):
+    """gta_bucket_knn_rows_ranged fills exactly the rows of each bucket's range, with the lists of
+    the whole-bucket call (a split bucket's pieces on several ranks put together); rows outside
+    the ranges keep their contents.  f32_long: buckets of 70000 rows (column chunks)."""
+    rng = np.random.default_rng(4)
+    if kind == "u8":
+        X = torch.from_numpy(_data(30000, d=128, seed=5)).cuda()
+        B, M = 6, 32
+    elif kind == "f32":
+        X = torch.from_numpy(_data(30000, d=96, seed=5).astype(np.float32) * 0.37).cuda()
+        B, M = 6, 32
+    else:
+        X = torch.from_numpy(rng.normal(size=(70000, 32)).astype(np.float32)).cuda()
+        B, M = 2, 32
+    _, _, _, top2 = gta.build_bucket(X, B, M, 2, 0, 42, with_extras=True)
+    st, R, gid, order, offsets, bucket_s, partner_s = _memberships(X, top2, B)
+    full_i, full_d, seed = _two_phases(st, R, gid, order, offsets, bucket_s, partner_s, M)
+    off = offsets.cpu().numpy()
+    sizes = np.diff(off)
+    # three pieces per bucket, cut at a multiple of 128 and at an arbitrary row
+    cuts = [np.array([0, (n // 3) // 128 * 128, max((n // 3) // 128 * 128, 2 * n // 3 + 5), n]) for n in sizes]
+    got_i = torch.full_like(full_i, -1)
+    got_d = torch.full_like(full_d, float("inf"))
+    for k in range(3):
+        lo = torch.tensor([min(c[k], c[3]) for c in cuts], dtype=torch.int64)
+        hi = torch.tensor([min(c[k + 1], c[3]) for c in cuts], dtype=torch.int64)
+        pi, pd, _ = _two_phases(st, R, gid, order, offsets, bucket_s, partner_s, M, (lo, hi), seed)
+        inside = np.zeros(R.shape[0], bool)
+        for b in range(B):
+            inside[off[b] + lo[b]: off[b] + hi[b]] = True
+        ins = torch.from_numpy(inside).cuda()
+        assert (pi[~ins] == -1).all() and torch.isinf(pd[~ins]).all()  # untouched outside the range
+        got_i[ins] = pi[ins]
+        got_d[ins] = pd[ins]
+    assert torch.equal(got_i, full_i)
+    assert torch.equal(got_d, full_d)
+    # a range outside its bucket is refused before device work
+    bad = torch.tensor([0] * B, dtype=torch.int64)
+    badh = torch.tensor([int(n) + 1 for n in sizes], dtype=torch.int64)
+    with pytest.raises(L.GtaError):
+        st.bucket_knn_rows_ranged(R, order, gid, offsets, partner_s, M, 1, None, bad, badh, got_i, got_d)
+
+
 def _run_ranks(world, X, prm):
     with tempfile.TemporaryDirectory() as out:
         mp.start_processes(dist_helpers.nccl_worker, args=(world, _free_port(), X, prm, out), nprocs=world,
@@ -104,10 +179,11 @@ def _run_ranks(world, X, prm):
         return [dict(np.load(f"{out}/rank{r}.npz")) for r in range(world)]
 
 
-def _check_against_single(world):
+def _check_against_single(world, split_share=1.0):
     N, B, M, K = 60000, 16, 32, 16
     X = _data(N, d=128, seed=11)
-    prm = dict(n_buckets=B, knn_degree=M, graph_degree=K, kmeans_iters=4, kmeans_sample=0, seed=42)
+    prm = dict(n_buckets=B, knn_degree=M, graph_degree=K, kmeans_iters=4, kmeans_sample=0, seed=42,
+               split_share=split_share)
     parts = _run_ranks(world, X, prm)
     Xd = torch.from_numpy(X).cuda()
     ids, dists, C, top2 = gta.build_bucket(Xd, B, M, 4, 0, 42, with_extras=True)
@@ -125,5 +201,7 @@ def test_sharded_one_rank_matches_single_gpu_build():
 
 
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
-def test_sharded_two_ranks_match_single_gpu_build():
-    _check_against_single(2)
+@pytest.mark.parametrize("split_share", [1.0, 0.05])
+def test_sharded_two_ranks_match_single_gpu_build(split_share):
+    """split_share 0.05: most buckets cut into row ranges on both ranks."""
+    _check_against_single(2, split_share)
