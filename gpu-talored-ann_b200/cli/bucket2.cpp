@@ -27,6 +27,7 @@
 #include <cmath>
 #include <cstdio>
 #include <filesystem>
+#include <cstdlib>
 #include <string>
 #include <vector>
 
@@ -142,6 +143,9 @@ int run(int argc, char** argv)
         q.knn_k = knn_k;
         q.rounds = iters;
         q.centroid_ratio = ratio;
+        // the reference tool's environment switch for the balanced choice
+        const char* rule = std::getenv("BUCKET2_ASSIGN_RULE");
+        q.assign_rule = (rule && std::string(rule) == "diskjoin") ? 1 : 0;
         q.seed = seed;
         q.assign_out = bucket_of.data();
         q.centroid_ids_out = cid.data();

@@ -8,14 +8,16 @@
 //                                   subsample of the candidates down to n_centroids (:3150-3172)
 //   balanced 1-way assignment       batch_assign_with_cagra_anns (:1552, the choice at :2276-2301):
 //                                   nearest or second-nearest centroid, the second when its bucket
-//                                   holds fewer than 0.8 x the first's points; centroid points stay
-//                                   in their own bucket, every bucket starts at size 1 (:1655-1660)
+//                                   holds fewer than 0.8 x the first's points (or, with the diskjoin
+//                                   rule of :2290-2292, fewer points and d2 < 1.2 d1); centroid
+//                                   points stay in their own bucket, every bucket starts at size 1
+//                                   (:1655-1660)
 //   own + nprobe pools              GpuResidentKnn::run_round (:5310-5365): the pool of bucket c is
 //                                   c's members followed by those of its nprobe nearest buckets
 // Randomness comes from splitmix64 streams keyed by the seed (the reference's raft / mt19937
-// streams cannot be reproduced), and the balanced choice reads the bucket sizes as they stood
-// at the start of each 1024-point batch (the reference updates them with relaxed atomics from
-// parallel threads, an order that is not reproducible); both rules are restated by the oracle.
+// streams cannot be reproduced).  The balanced choice runs in the reference loop's sequential
+// order (each point sees every earlier point's choice): the reference's result on one OpenMP
+// thread; with more threads its relaxed-atomic interleaving is not reproducible.
 #include <cub/cub.cuh>
 
 #include <algorithm>
@@ -62,32 +64,72 @@ __global__ void min_update_kernel(float* __restrict__ min_d, const float* __rest
     if (i < n) min_d[i] = fminf(min_d[i], d_new[i]);
 }
 
-// One CTA walks the non-centroid points in index order, kBalanceBatch at a time: every point of
-// a batch chooses against the sizes at the batch's start, then the batch's choices are added.
-constexpr int kBalanceBatch = 1024;
-
-__global__ void __launch_bounds__(kBalanceBatch)
-    balanced_assign_kernel(const int32_t* __restrict__ top2, const int32_t* __restrict__ nc_ids, int64_t n_nc,
-                           int32_t n_c, int32_t* __restrict__ sizes, int32_t* __restrict__ assign, int* err)
+// The balanced choice in the reference's sequential order: every non-centroid point, in index
+// order, decides against the sizes left by all earlier points.  One warp takes 32 points at a
+// time; lane i waits for the earlier lanes of its group that share one of its two buckets, and
+// the lanes whose earlier sharers have decided choose together (their buckets are disjoint, so
+// none of them sees another's update).  Sizes live in shared memory when they fit.
+// rule 0: c2 when size(c2) < 0.8 size(c1) (double); rule 1 (diskjoin): c2 when
+// size(c2) < size(c1) and d2 < 1.2f d1 (d: the two centroids' squared distances).
+template <bool kShared>
+__global__ void __launch_bounds__(32)
+    balanced_assign_kernel(const int32_t* __restrict__ top2, const float* __restrict__ top2_d,
+                           const int32_t* __restrict__ nc_ids, int64_t n_nc, int32_t n_c, int rule,
+                           int32_t* __restrict__ g_sizes, int32_t* __restrict__ assign, int* err)
 {
-    for (int64_t b0 = 0; b0 < n_nc; b0 += kBalanceBatch) {
-        const int64_t j = b0 + threadIdx.x;
-        int32_t chosen = -1;
+    extern __shared__ int32_t s_sizes[];
+    volatile int32_t* sizes = kShared ? s_sizes : g_sizes;
+    const int lane = threadIdx.x;
+    if (kShared) {
+        for (int32_t c = lane; c < n_c; c += 32) s_sizes[c] = g_sizes[c];
+        __syncwarp();
+    }
+    // the group's points, loaded one group ahead
+    auto load = [&](int64_t b0, int32_t& i, int32_t& c1, int32_t& c2, float& d1, float& d2) {
+        const int64_t j = b0 + lane;
+        i = -1; c1 = c2 = -1; d1 = d2 = 0.f;
         if (j < n_nc) {
-            const int32_t i = nc_ids[j];
-            const int32_t c1 = top2[2 * static_cast<int64_t>(i)], c2 = top2[2 * static_cast<int64_t>(i) + 1];
-            if (c1 < 0 || c1 >= n_c || c2 < 0 || c2 >= n_c) {
-                atomicCAS(err, 0, kDevBadIndex);
-            } else {
-                // L2 reads: the sizes change by atomics between batches
-                const double s1 = static_cast<double>(__ldcg(&sizes[c1])), s2 = static_cast<double>(__ldcg(&sizes[c2]));
-                chosen = (s2 < 0.8 * s1) ? c2 : c1;
-                assign[i] = chosen;
+            i = nc_ids[j];
+            c1 = top2[2 * static_cast<int64_t>(i)];
+            c2 = top2[2 * static_cast<int64_t>(i) + 1];
+            if (rule == 1) {
+                d1 = top2_d[2 * static_cast<int64_t>(i)];
+                d2 = top2_d[2 * static_cast<int64_t>(i) + 1];
             }
         }
-        __syncthreads();  // every choice of the batch read the sizes before any update
-        if (chosen >= 0) atomicAdd(&sizes[chosen], 1);
-        __syncthreads();
+    };
+    int32_t ni, nc1, nc2;
+    float nd1, nd2;
+    load(0, ni, nc1, nc2, nd1, nd2);
+    for (int64_t b0 = 0; b0 < n_nc; b0 += 32) {
+        const int32_t i = ni, c1 = nc1, c2 = nc2;
+        const float d1 = nd1, d2 = nd2;
+        if (b0 + 32 < n_nc) load(b0 + 32, ni, nc1, nc2, nd1, nd2);
+        const bool valid = i >= 0 && c1 >= 0 && c1 < n_c && c2 >= 0 && c2 < n_c;
+        if (i >= 0 && !valid) atomicCAS(err, 0, kDevBadIndex);
+        // the earlier lanes of the group that share a bucket with this one
+        unsigned dep = 0;
+        for (int t = 0; t < 31; ++t) {
+            const int32_t a = __shfl_sync(0xffffffffu, valid ? c1 : -1, t);
+            const int32_t b = __shfl_sync(0xffffffffu, valid ? c2 : -1, t);
+            if (t < lane && a >= 0 && (a == c1 || a == c2 || b == c1 || b == c2)) dep |= 1u << t;
+        }
+        unsigned pending = __ballot_sync(0xffffffffu, valid);
+        while (pending) {
+            const bool ready = ((pending >> lane) & 1u) && (dep & pending) == 0;
+            int32_t chosen = -1;
+            if (ready) {
+                const int32_t s1 = sizes[c1], s2 = sizes[c2];
+                const bool take2 = rule == 1 ? (s2 < s1 && d2 < 1.2f * d1)
+                                             : (static_cast<double>(s2) < 0.8 * static_cast<double>(s1));
+                chosen = take2 ? c2 : c1;
+                assign[i] = chosen;
+            }
+            __syncwarp();
+            if (ready) sizes[chosen] = sizes[chosen] + 1;  // the ready lanes' buckets are disjoint
+            __syncwarp();
+            pending &= ~__ballot_sync(0xffffffffu, ready);
+        }
     }
 }
 
@@ -175,10 +217,11 @@ void min_update(float* min_d, const float* d_new, int64_t n, cudaStream_t st)
     GTA_CUDA(cudaGetLastError());
 }
 
-void balanced_assign(const int32_t* top2, const int32_t* cid, int32_t n_c, int64_t n, int32_t* assign, int* err,
-                     cudaStream_t st)
+void balanced_assign(const int32_t* top2, const float* top2_d, int rule, const int32_t* cid, int32_t n_c, int64_t n,
+                     int32_t* assign, int* err, cudaStream_t st)
 {
     ProfScope prof("balanced_assign", 12.0 * static_cast<double>(n), st);
+    GTA_REQUIRE(rule == 0 || (rule == 1 && top2_d), kInvalid, "balanced_assign: unknown rule");
     DevBuf<int32_t> sizes(static_cast<size_t>(n_c), st);
     DevBuf<uint8_t> is_c(static_cast<size_t>(n), st), not_c(static_cast<size_t>(n), st);
     GTA_CUDA(cudaMemsetAsync(is_c.get(), 0, static_cast<size_t>(n), st));
@@ -187,7 +230,16 @@ void balanced_assign(const int32_t* top2, const int32_t* cid, int32_t n_c, int64
     count_launches(2);
     DevBuf<int32_t> nc_ids(static_cast<size_t>(n), st);
     const int64_t n_nc = select_flagged(not_c.get(), n, nc_ids.get(), st);
-    balanced_assign_kernel<<<1, kBalanceBatch, 0, st>>>(top2, nc_ids.get(), n_nc, n_c, sizes.get(), assign, err);
+    const size_t smem = sizeof(int32_t) * static_cast<size_t>(n_c);
+    if (smem <= 200u * 1024u) {
+        GTA_CUDA(cudaFuncSetAttribute(balanced_assign_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      static_cast<int>(smem)));
+        balanced_assign_kernel<true><<<1, 32, smem, st>>>(top2, top2_d, nc_ids.get(), n_nc, n_c, rule, sizes.get(),
+                                                          assign, err);
+    } else {
+        balanced_assign_kernel<false><<<1, 32, 0, st>>>(top2, top2_d, nc_ids.get(), n_nc, n_c, rule, sizes.get(),
+                                                        assign, err);
+    }
     count_launches(1);
     GTA_CUDA(cudaGetLastError());
 }

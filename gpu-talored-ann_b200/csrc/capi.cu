@@ -883,7 +883,7 @@ void build_bucket2_round(const void* X, int dtype, int64_t N, int d, const gta_b
         DevBuf<int32_t> top2(static_cast<size_t>(N) * 2, st);
         DevBuf<float> t2d(static_cast<size_t>(N) * 2, st);
         sp.assign(nullptr, N, cid.get(), B, 2, top2.get(), t2d.get(), err.get(), st);
-        balanced_assign(top2.get(), cid.get(), B, N, assign.get(), err.get(), st);
+        balanced_assign(top2.get(), t2d.get(), p.assign_rule, cid.get(), B, N, assign.get(), err.get(), st);
     }
     DevBuf<int32_t> members(static_cast<size_t>(N), st);
     DevBuf<int64_t> offsets(static_cast<size_t>(B) + 1, st);
@@ -997,8 +997,8 @@ void build_bucket2_impl(const gta_dataset& ds, const gta_bucket2_params& p, Buck
     GTA_REQUIRE(ds.dtype == GTA_F32 || ds.dtype == GTA_U8 || ds.dtype == GTA_I8, kInvalid, "build_bucket2: bad dtype");
     GTA_REQUIRE(M >= 1 && M <= 128, kInvalid, "build_bucket2: knn_degree must be in [1, 128]");
     GTA_REQUIRE(p.nprobe >= 0 && p.nprobe <= 127 && p.knn_k >= 0 && p.knn_k <= 127 && p.rounds >= 0 &&
-                    p.centroid_ratio >= 0.0f && p.centroid_ratio <= 1.0f,
-                kInvalid, "build_bucket2: need 0 <= nprobe, knn_k <= 127, 0 <= centroid_ratio <= 1");
+                    p.centroid_ratio >= 0.0f && p.centroid_ratio <= 1.0f && (p.assign_rule == 0 || p.assign_rule == 1),
+                kInvalid, "build_bucket2: need 0 <= nprobe, knn_k <= 127, 0 <= centroid_ratio <= 1, assign_rule 0 or 1");
     const void* X = ds.data;
     DevBuf<uint8_t> xhold;
     if (!ds.on_device) {

@@ -245,8 +245,8 @@ void kpar_sample(const float* min_d, int64_t n, uint64_t seed, int round, double
                  uint8_t* sel, cudaStream_t st);
 int64_t select_flagged(const uint8_t* flags, int64_t n, int32_t* out, cudaStream_t st);  // ids in order; syncs
 void min_update(float* min_d, const float* d_new, int64_t n, cudaStream_t st);
-void balanced_assign(const int32_t* top2, const int32_t* cid, int32_t n_c, int64_t n, int32_t* assign, int* err,
-                     cudaStream_t st);
+void balanced_assign(const int32_t* top2, const float* top2_d, int rule, const int32_t* cid, int32_t n_c, int64_t n,
+                     int32_t* assign, int* err, cudaStream_t st);
 void pool_fill(const int32_t* members, const int64_t* offsets, const int32_t* seg_b, const int64_t* seg_dst, int32_t S,
                int32_t c_lo, int32_t n_buckets, int32_t* pool_ids, cudaStream_t st);
 void one_way_rows(const int32_t* members, int64_t n, int64_t* mem_row, cudaStream_t st);

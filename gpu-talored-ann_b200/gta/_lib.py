@@ -48,7 +48,7 @@ class gta_bucket_params(ctypes.Structure):
 class gta_bucket2_params(ctypes.Structure):
     _fields_ = [
         ("knn_degree", _I32), ("nprobe", _I32), ("knn_k", _I32), ("rounds", _I32),
-        ("centroid_ratio", ctypes.c_float), ("reserved0", _I32), ("seed", _U64),
+        ("centroid_ratio", ctypes.c_float), ("assign_rule", _I32), ("seed", _U64),
         ("out_on_device", _I32), ("reserved1", _I32),
         ("assign_out", _P), ("centroid_ids_out", _P), ("n_buckets_out", ctypes.POINTER(_I32)),
     ]

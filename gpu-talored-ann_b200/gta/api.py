@@ -113,12 +113,17 @@ def build_bucket(X, n_buckets: int, knn_degree: int = 64, kmeans_iters: int = 10
 
 
 def build_bucket2(X, knn_degree: int = 64, nprobe: int = 0, centroid_ratio: float = 0.01, seed: int = 42,
-                  rounds: int = 1, knn_k: int = 0, with_extras: bool = False):
+                  rounds: int = 1, knn_k: int = 0, with_extras: bool = False, assign_rule: str = "default"):
     """kNN graph with the reference's own bucketing (its bucket2 tool): KMeans|| data-point
     centroids (max(2, N * centroid_ratio) requested), balanced 1-way buckets, every bucket's
     points searched in the pool of their bucket and its ``nprobe`` nearest buckets (0: knn_k,
-    0: 32), ``rounds`` builds merged.  Returns (ids[N, M], dists[N, M]); with ``with_extras``
-    also the bucket of every point (N,) and the centroids' point ids."""
+    0: 32), ``rounds`` builds merged.  ``assign_rule``: "default" (the second centroid when its
+    bucket is below 0.8 x the first's) or "diskjoin" (the tool's BUCKET2_ASSIGN_RULE=diskjoin).
+    Returns (ids[N, M], dists[N, M]); with ``with_extras`` also the bucket of every point (N,)
+    and the centroids' point ids."""
+    rules = {"default": 0, "diskjoin": 1}
+    if assign_rule not in rules:
+        raise L.GtaError(L.GTA_EINVAL, f"build_bucket2: assign_rule must be one of {sorted(rules)}")
     dev = _is_dev(X)
     N = X.shape[0]
     ids = _empty((N, knn_degree), "int32", dev)
@@ -128,7 +133,8 @@ def build_bucket2(X, knn_degree: int = 64, nprobe: int = 0, centroid_ratio: floa
     cid = _empty((n_req,), "int32", dev) if with_extras else None
     nb = ctypes.c_int32(0)
     p = L.gta_bucket2_params(knn_degree=knn_degree, nprobe=nprobe, knn_k=knn_k, rounds=rounds,
-                             centroid_ratio=centroid_ratio, reserved0=0, seed=seed, out_on_device=1 if dev else 0,
+                             centroid_ratio=centroid_ratio, assign_rule=rules[assign_rule], seed=seed,
+                             out_on_device=1 if dev else 0,
                              reserved1=0, assign_out=_ptr(assign), centroid_ids_out=_ptr(cid),
                              n_buckets_out=ctypes.pointer(nb))
     ds = _dataset(X)

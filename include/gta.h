@@ -97,7 +97,9 @@ typedef struct {
     int32_t knn_k;            /* bucket2 --knn-k: the pool width when nprobe is 0 (0 = 32) */
     int32_t rounds;           /* bucket2 -t: builds with seeds seed, seed+1, ... merged (0 or 1: one) */
     float centroid_ratio;     /* buckets = max(2, N * ratio) requested (bucket2 --centroid-ratio; 0 = 0.01) */
-    int32_t reserved0;
+    int32_t assign_rule;      /* the balanced choice: 0 the reference's default (second centroid when its
+                                 bucket is below 0.8 x the first's), 1 its BUCKET2_ASSIGN_RULE=diskjoin
+                                 (second when its bucket is smaller and d2 < 1.2 d1) */
     uint64_t seed;
     int32_t out_on_device;    /* outputs are device pointers */
     int32_t reserved1;
@@ -122,8 +124,9 @@ int gta_build_bucket(const gta_dataset* ds, const gta_bucket_params* p, int32_t*
  * (three rounds taking each point with probability 0.5 B d(x)^2 / psi, then a
  * uniform subsample of the candidates to B), exact centroid kNN graph, top-2
  * centroids of every point with the balanced choice (the second when its bucket
- * is below 0.8 x the first's size, sizes as they stood at the start of each
- * 1024-point batch), then for every bucket the exact top-M of its points over
+ * is below 0.8 x the first's size, each point against the sizes left by the
+ * points before it in index order; assign_rule selects the diskjoin rule),
+ * then for every bucket the exact top-M of its points over
  * the pool of its own and its nprobe nearest buckets' points (self excluded).
  * Writes knn_ids / knn_dists [N x M] like gta_build_bucket.
  * Replaces bucket2 Steps 2-6 on the GPU-resident path

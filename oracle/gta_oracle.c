@@ -786,36 +786,66 @@ ORC_API int64_t orc_kmeans_parallel(const float* X, int64_t N, int d, int64_t n_
 }
 
 /* Balanced 1-way assignment (bucket.cu:1655-1660, :2276-2301): centroid points stay in their
- * own bucket, every bucket starts at size 1; the other points in index order, 1024 at a time,
- * choose the second-nearest centroid when its size is below 0.8 x the nearest's size (sizes as
- * at the start of the batch), then the batch's choices are counted.  Returns the number of
- * top-2 entries out of range (0 on success). */
-ORC_API int64_t orc_balanced_assign(const int32_t* top2, int64_t N, int32_t B, const int32_t* cid, int32_t* assign)
+ * own bucket, every bucket starts at size 1; the other points, in index order, each choose
+ * against the sizes left by every earlier point (the reference's loop run by one thread: its
+ * OpenMP threads update the sizes with relaxed atomics, whose interleaving is not reproducible).
+ * rule 0 (the reference's default): the second-nearest centroid c2 when size(c2) < 0.8 size(c1)
+ * in double; rule 1 (BUCKET2_ASSIGN_RULE=diskjoin, :2290-2292): c2 when size(c2) < size(c1) and
+ * d2 < 1.2f * d1 in float, d = top2_d (the squared distances of the two centroids).  Returns
+ * the number of top-2 entries out of range (0 on success). */
+ORC_API int64_t orc_balanced_assign(const int32_t* top2, const float* top2_d, int64_t N, int32_t B,
+                                    const int32_t* cid, int32_t rule, int32_t* assign)
 {
     int64_t* size = (int64_t*)malloc(sizeof(int64_t) * (size_t)B);
     unsigned char* is_c = (unsigned char*)calloc((size_t)N, 1);
-    int32_t* chosen = (int32_t*)malloc(sizeof(int32_t) * 1024);
     int64_t bad = 0;
     for (int32_t c = 0; c < B; ++c) { size[c] = 1; assign[cid[c]] = c; is_c[cid[c]] = 1; }
-    int64_t i = 0;
-    while (i < N) {
-        int nb = 0;
-        int64_t ids[1024];
-        while (nb < 1024 && i < N) {
-            if (!is_c[i]) ids[nb++] = i;
-            ++i;
+    for (int64_t i = 0; i < N; ++i) {
+        if (is_c[i]) continue;
+        const int32_t c1 = top2[2 * i], c2 = top2[2 * i + 1];
+        if (c1 < 0 || c1 >= B || c2 < 0 || c2 >= B) { ++bad; continue; }
+        int take2;
+        if (rule == 1) {
+            const float d1 = top2_d[2 * i], d2 = top2_d[2 * i + 1];
+            take2 = size[c2] < size[c1] && d2 < 1.2f * d1;
+        } else {
+            take2 = (double)size[c2] < 0.8 * (double)size[c1];
         }
-        for (int t = 0; t < nb; ++t) {
-            const int32_t c1 = top2[2 * ids[t]], c2 = top2[2 * ids[t] + 1];
-            if (c1 < 0 || c1 >= B || c2 < 0 || c2 >= B) { chosen[t] = -1; ++bad; continue; }
-            chosen[t] = ((double)size[c2] < 0.8 * (double)size[c1]) ? c2 : c1;
-            assign[ids[t]] = chosen[t];
-        }
-        for (int t = 0; t < nb; ++t)
-            if (chosen[t] >= 0) size[chosen[t]]++;
+        const int32_t ch = take2 ? c2 : c1;
+        assign[i] = ch;
+        size[ch]++;
     }
-    free(size); free(is_c); free(chosen);
+    free(size); free(is_c);
     return bad;
+}
+
+/* The pools of the resident round (bucket.cu:5317-5346): members[N] grouped by bucket in
+ * ascending point id with off[B+1]; for bucket c its S = P + 1 segments, segment 0 bucket c
+ * itself and segment j the neighbour adj[c][j-1] (-1 when outside [0, B)): seg_b[c*S + j], and
+ * seg_ofs[c*S + j] the offset of the segment in c's pool (a -1 segment is empty); pool[c] = the
+ * pool's length. */
+ORC_API void orc_pool_tables(const int32_t* assign, int64_t N, int32_t B, const int32_t* adj, int32_t P,
+                             int64_t* off, int32_t* members, int32_t* seg_b, int64_t* seg_ofs, int64_t* pool)
+{
+    for (int32_t c = 0; c <= B; ++c) off[c] = 0;
+    for (int64_t i = 0; i < N; ++i) off[assign[i] + 1]++;
+    for (int32_t c = 0; c < B; ++c) off[c + 1] += off[c];
+    int64_t* cur = (int64_t*)malloc(sizeof(int64_t) * (size_t)(B > 0 ? B : 1));
+    for (int32_t c = 0; c < B; ++c) cur[c] = off[c];
+    for (int64_t i = 0; i < N; ++i) members[cur[assign[i]]++] = (int32_t)i;
+    free(cur);
+    const int64_t S = (int64_t)P + 1;
+    for (int32_t c = 0; c < B; ++c) {
+        int64_t o = 0;
+        for (int64_t j = 0; j < S; ++j) {
+            int32_t b = j == 0 ? c : adj[(int64_t)c * P + j - 1];
+            if (b < 0 || b >= B) b = -1;
+            seg_b[c * S + j] = b;
+            seg_ofs[c * S + j] = o;
+            if (b >= 0) o += off[b + 1] - off[b];
+        }
+        pool[c] = o;
+    }
 }
 
 /* Per-bucket pool kNN (bucket.cu:5310-5365, the resident round): the pool of bucket c is its
@@ -824,27 +854,22 @@ ORC_API int64_t orc_balanced_assign(const int32_t* top2, int64_t N, int32_t B, c
 ORC_API void orc_pool_knn(const float* X, int64_t N, int d, const int32_t* assign, int32_t B, const int32_t* adj,
                           int32_t P, int32_t M, int32_t* out_ids, float* out_d)
 {
-    int64_t* off = (int64_t*)calloc((size_t)B + 1, sizeof(int64_t));
-    int32_t* mem = (int32_t*)malloc(sizeof(int32_t) * (size_t)N);
-    for (int64_t i = 0; i < N; ++i) off[assign[i] + 1]++;
-    for (int32_t c = 0; c < B; ++c) off[c + 1] += off[c];
-    int64_t* cur = (int64_t*)malloc(sizeof(int64_t) * (size_t)B);
-    for (int32_t c = 0; c < B; ++c) cur[c] = off[c];
-    for (int64_t i = 0; i < N; ++i) mem[cur[assign[i]]++] = (int32_t)i;
+    const int64_t S = (int64_t)P + 1;
+    int64_t* off = (int64_t*)malloc(sizeof(int64_t) * ((size_t)B + 1));
+    int32_t* mem = (int32_t*)malloc(sizeof(int32_t) * (size_t)(N > 0 ? N : 1));
+    int32_t* seg_b = (int32_t*)malloc(sizeof(int32_t) * (size_t)(B * S));
+    int64_t* seg_ofs = (int64_t*)malloc(sizeof(int64_t) * (size_t)(B * S));
+    int64_t* psz = (int64_t*)malloc(sizeof(int64_t) * (size_t)B);
+    orc_pool_tables(assign, N, B, adj, P, off, mem, seg_b, seg_ofs, psz);
 #pragma omp parallel for schedule(dynamic)
     for (int32_t c = 0; c < B; ++c) {
-        int64_t ps = 0;
-        for (int j = 0; j <= P; ++j) {
-            const int32_t b = j == 0 ? c : adj[(int64_t)c * P + j - 1];
-            if (b >= 0 && b < B) ps += off[b + 1] - off[b];
-        }
+        const int64_t ps = psz[c];
         int32_t* pool = (int32_t*)malloc(sizeof(int32_t) * (size_t)(ps > 0 ? ps : 1));
         orc_pair* cand = (orc_pair*)malloc(sizeof(orc_pair) * (size_t)(ps > 0 ? ps : 1));
-        int64_t w = 0;
-        for (int j = 0; j <= P; ++j) {
-            const int32_t b = j == 0 ? c : adj[(int64_t)c * P + j - 1];
-            if (b < 0 || b >= B) continue;
-            for (int64_t k = off[b]; k < off[b + 1]; ++k) pool[w++] = mem[k];
+        for (int64_t j = 0; j < S; ++j) {
+            const int32_t b = seg_b[c * S + j];
+            if (b < 0) continue;
+            for (int64_t k = off[b]; k < off[b + 1]; ++k) pool[seg_ofs[c * S + j] + k - off[b]] = mem[k];
         }
         for (int64_t q = off[c]; q < off[c + 1]; ++q) {
             const int32_t pt = mem[q];
@@ -859,5 +884,5 @@ ORC_API void orc_pool_knn(const float* X, int64_t N, int d, const int32_t* assig
         }
         free(pool); free(cand);
     }
-    free(off); free(mem); free(cur);
+    free(off); free(mem); free(seg_b); free(seg_ofs); free(psz);
 }

@@ -78,8 +78,10 @@ def lib():
         L.orc_bucket_order.restype = None
         L.orc_kmeans_parallel.argtypes = [_P, _I64, _I32, _I64, ctypes.c_uint64, _P]
         L.orc_kmeans_parallel.restype = _I64
-        L.orc_balanced_assign.argtypes = [_P, _I64, _I32, _P, _P]
+        L.orc_balanced_assign.argtypes = [_P, _P, _I64, _I32, _P, _I32, _P]
         L.orc_balanced_assign.restype = _I64
+        L.orc_pool_tables.argtypes = [_P, _I64, _I32, _P, _I32, _P, _P, _P, _P, _P]
+        L.orc_pool_tables.restype = None
         L.orc_pool_knn.argtypes = [_P, _I64, _I32, _P, _I32, _P, _I32, _I32, _P, _P]
         L.orc_pool_knn.restype = None
         _lib = L
@@ -104,6 +106,25 @@ def ref_lib():
         R.ref_translate_npy.argtypes = [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p]
         _ref = R
     return _ref
+
+
+_REF_ASSIGN_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "_ref", "libgta_ref_assign.so")
+_ref_assign = None
+
+
+def ref_assign_lib():
+    """The reference's own balanced-choice loop and pool tables (oracle/_ref), or None."""
+    global _ref_assign
+    if _ref_assign is None:
+        if not os.path.exists(_REF_ASSIGN_PATH):
+            return None
+        R = ctypes.CDLL(_REF_ASSIGN_PATH)
+        R.ref_balanced_assign.argtypes = [_P, _P, _I64, _I32, _P, _I32, _I64, _P]
+        R.ref_balanced_assign.restype = None
+        R.ref_pool_tables.argtypes = [_P, _I64, _I64, _P, ctypes.c_uint32, _P, _P, _P, _P, _P]
+        R.ref_pool_tables.restype = None
+        _ref_assign = R
+    return _ref_assign
 
 
 def _p(a: np.ndarray):
@@ -389,14 +410,34 @@ def kmeans_parallel(X, n_req: int, seed: int) -> np.ndarray:
     return out[:n].copy()
 
 
-def balanced_assign(top2, B: int, cid) -> np.ndarray:
-    """The balanced 1-way choice (bucket.cu:1655-1660, :2276-2301), 1024-point batches."""
+def balanced_assign(top2, B: int, cid, top2_d=None, rule: int = 0) -> np.ndarray:
+    """The balanced 1-way choice (bucket.cu:1655-1660, :2276-2301), each point against the sizes
+    left by the earlier ones; rule 1 = BUCKET2_ASSIGN_RULE=diskjoin (needs top2_d)."""
     top2 = np.ascontiguousarray(top2, np.int32)
     cid = np.ascontiguousarray(cid, np.int32)
+    td = None if top2_d is None else np.ascontiguousarray(top2_d, np.float32)
+    assert rule == 0 or td is not None
     out = np.full(top2.shape[0], -1, np.int32)
-    bad = lib().orc_balanced_assign(_p(top2), top2.shape[0], B, _p(cid), _p(out))
+    bad = lib().orc_balanced_assign(_p(top2), None if td is None else _p(td), top2.shape[0], B, _p(cid), rule,
+                                    _p(out))
     assert bad == 0
     return out
+
+
+def pool_tables(assign, B: int, adj):
+    """The resident round's pool tables (bucket.cu:5317-5346 restated): (offsets[B+1], members[N],
+    seg_bucket[B, P+1], seg_ofs[B, P+1], pool_size[B])."""
+    assign = np.ascontiguousarray(assign, np.int32)
+    adj = np.ascontiguousarray(adj, np.int32).reshape(B, -1)
+    P = adj.shape[1]
+    N = assign.shape[0]
+    off = np.empty(B + 1, np.int64)
+    mem = np.empty(max(N, 1), np.int32)
+    seg_b = np.empty((B, P + 1), np.int32)
+    seg_o = np.empty((B, P + 1), np.int64)
+    pool = np.empty(B, np.int64)
+    lib().orc_pool_tables(_p(assign), N, B, _p(adj), P, _p(off), _p(mem), _p(seg_b), _p(seg_o), _p(pool))
+    return off, mem[:N], seg_b, seg_o, pool
 
 
 def pool_knn(X, assign, B: int, adj, M: int):
@@ -412,7 +453,7 @@ def pool_knn(X, assign, B: int, adj, M: int):
 
 
 def build_bucket2(X, M: int, nprobe: int = 0, centroid_ratio: float = 0.01, seed: int = 42, rounds: int = 1,
-                  knn_k: int = 0):
+                  knn_k: int = 0, assign_rule: int = 0):
     """The reference-bucketing build restated: (ids, dists, assign, centroid ids) of the last round,
     rounds merged with the resident merge rule."""
     Xf = _f32(X)
@@ -432,8 +473,8 @@ def build_bucket2(X, M: int, nprobe: int = 0, centroid_ratio: float = 0.01, seed
                 row = list(ki[b])
                 row.remove(b) if b in row else row.pop()
                 adj[b] = row[:P]
-        top2, _ = topk_assign(Xf, C, 2)
-        assign = balanced_assign(top2, B, cid)
+        top2, t2d = topk_assign(Xf, C, 2)
+        assign = balanced_assign(top2, B, cid, t2d, assign_rule)
         ids, dist = pool_knn(Xf, assign, B, adj, M)
         run = (ids, dist) if run is None else merge_lists(run[0], run[1], ids, dist)
     return run[0], run[1], assign, cid

@@ -9,6 +9,9 @@ the repository, so the tests themselves never read the reference tree.
   * The reference's header-only C++ prune / reverse-edge code
     (prune_windowed_core.hpp, edge_chunk_accumulator.hpp) runs through
     oracle/_ref/libgta_ref.so, compiled in place by oracle/Makefile.
+  * The reference's balanced-choice loop and pool tables (bucket.cu lines
+    streamed by oracle/Makefile into oracle/ref_assign_bridge.cpp) run through
+    oracle/_ref/libgta_ref_assign.so.
 
     GTA_REFERENCE=<reference root> python tests/golden/make_golden.py
 """
@@ -213,6 +216,61 @@ def make_reorder_fixture():
     np.savez_compressed(os.path.join(HERE, "reorder.npz"), **out)
 
 
+def make_assign_fixture():
+    """The reference's own balanced-choice loop (bucket.cu:2277-2302, one thread) and pool tables
+    (bucket.cu:5317-5347), compiled from their lines into oracle/_ref, on seeded inputs: top-2
+    centroids of mixture points (both rules) and random top-2 pairs over few buckets."""
+    R = orc.ref_assign_lib()
+    if R is None:
+        raise SystemExit("oracle/_ref/libgta_ref_assign.so missing: run `make -C oracle` with the reference tree present")
+    p = orc._p
+    rng = np.random.default_rng(31)
+    out = {}
+    cases = []
+    X = _mixture(rng, 6000, 8, 30, 0.15, -1.0, 1.0)
+    cid = rng.choice(6000, 60, replace=False).astype(np.int32)
+    t2, t2d = orc.topk_assign(X, X[cid], 2)
+    cases.append(("mix", t2.astype(np.int32), t2d.astype(np.float32), cid))
+    N, B = 4000, 5
+    c1 = rng.integers(0, B, N)
+    c2 = (c1 + rng.integers(1, B, N)) % B
+    d1 = rng.uniform(0.5, 2.0, N).astype(np.float32)
+    d2 = (d1 * rng.uniform(1.0, 1.4, N)).astype(np.float32)
+    cases.append(("few", np.stack([c1, c2], 1).astype(np.int32), np.stack([d1, d2], 1),
+                  rng.choice(N, B, replace=False).astype(np.int32)))
+    for name, t2, t2d, cid in cases:
+        t2, t2d = np.ascontiguousarray(t2), np.ascontiguousarray(t2d, np.float32)
+        B = cid.size
+        for rule in (0, 1):
+            res = []
+            for batch in (1024, 333, t2.shape[0]):  # one thread: the batch size does not matter
+                a = np.full(t2.shape[0], -1, np.int32)
+                R.ref_balanced_assign(p(t2), p(t2d), t2.shape[0], B, p(cid), rule, batch, p(a))
+                res.append(a)
+            assert all((r == res[0]).all() for r in res)
+            out[f"assign_{name}_rule{rule}"] = res[0]
+        out[f"top2_{name}"] = t2
+        out[f"top2d_{name}"] = t2d
+        out[f"cid_{name}"] = cid
+    # pool tables of the mixture's default-rule buckets over each bucket's 8 nearest buckets
+    # (some entries past the last bucket: the reference drops them)
+    assign = out["assign_mix_rule0"]
+    cid = out["cid_mix"]
+    B, P = cid.size, 8
+    ki, _ = orc.topk_assign(X[cid], X[cid], P + 1)
+    adj = ki[:, 1:].astype(np.uint32)
+    adj[rng.random(adj.shape) < 0.05] = B + 2
+    off = np.empty(B + 1, np.int64)
+    mem = np.empty(assign.size, np.int32)
+    sb = np.empty((B, P + 1), np.int32)
+    so = np.empty((B, P + 1), np.int32)
+    ps = np.empty(B, np.int64)
+    R.ref_pool_tables(p(assign), assign.size, B, p(adj), P, p(off), p(mem), p(sb), p(so), p(ps))
+    out.update(pool_assign=assign, pool_adj=adj, pool_off=off, pool_members=mem, pool_seg_bucket=sb,
+               pool_seg_ofs=so, pool_size=ps)
+    np.savez_compressed(os.path.join(HERE, "bucket2_assign.npz"), **out)
+
+
 def _random_graph(rng, N, M):
     """M distinct non-self candidates per row (the reference test's generator shape)."""
     g = np.empty((N, M), np.uint32)
@@ -265,9 +323,9 @@ def make_cpp_fixtures():
 
 
 if __name__ == "__main__":
-    # `python make_golden.py [python] [cpp] [search] [eval] [reorder] [occlusion]`: the named fixture groups
-    # (default all)
-    want = set(sys.argv[1:]) or {"python", "cpp", "search", "eval", "reorder", "occlusion"}
+    # `python make_golden.py [python] [cpp] [search] [eval] [reorder] [occlusion] [assign]`: the named
+    # fixture groups (default all)
+    want = set(sys.argv[1:]) or {"python", "cpp", "search", "eval", "reorder", "occlusion", "assign"}
     orc.build()
     if "python" in want:
         make_python_fixtures()
@@ -281,6 +339,8 @@ if __name__ == "__main__":
         make_reorder_fixture()
     if "occlusion" in want:
         make_occlusion_fixture()
+    if "assign" in want:
+        make_assign_fixture()
     for f in sorted(os.listdir(HERE)):
         if f.endswith(".npz"):
             print(f, os.path.getsize(os.path.join(HERE, f)), "bytes")

@@ -14,18 +14,20 @@ from oracle import oracle as orc  # noqa: E402
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("cfg_name,n,M,nprobe,ratio,rounds", [
-    ("c2", 20000, 32, 8, 0.01, 1),      # ~200 buckets: the FP32-pipe assignment path
-    ("c2", 60000, 64, 16, 0.01, 1),     # ~600 buckets: the tensor-core assignment path
-    ("c2", 12000, 16, 4, 0.02, 2),      # two rounds merged
-    ("c1", 10000, 32, 6, 0.01, 1),      # float data
+@pytest.mark.parametrize("cfg_name,n,M,nprobe,ratio,rounds,rule", [
+    ("c2", 20000, 32, 8, 0.01, 1, "default"),    # ~200 buckets: the FP32-pipe assignment path
+    ("c2", 60000, 64, 16, 0.01, 1, "default"),   # ~600 buckets: the tensor-core assignment path
+    ("c2", 12000, 16, 4, 0.02, 2, "default"),    # two rounds merged
+    ("c1", 10000, 32, 6, 0.01, 1, "default"),    # float data
+    ("c2", 20000, 32, 8, 0.01, 1, "diskjoin"),   # BUCKET2_ASSIGN_RULE=diskjoin
+    ("c1", 10000, 32, 6, 0.01, 1, "diskjoin"),
 ])
-def test_build_bucket2_vs_oracle(cfg_name, n, M, nprobe, ratio, rounds):
+def test_build_bucket2_vs_oracle(cfg_name, n, M, nprobe, ratio, rounds, rule):
     cfg = gta.scaled(gta.CONFIGS[cfg_name], n)
     X = gta.generate(cfg, seed=3)
     ids, dists, assign, cid = gta.build_bucket2(torch.from_numpy(X).cuda(), M, nprobe, ratio, 7, rounds,
-                                                with_extras=True)
-    ri, rd, ra, rc = orc.build_bucket2(X, M, nprobe, ratio, 7, rounds)
+                                                with_extras=True, assign_rule=rule)
+    ri, rd, ra, rc = orc.build_bucket2(X, M, nprobe, ratio, 7, rounds, assign_rule={"default": 0, "diskjoin": 1}[rule])
     np.testing.assert_array_equal(cid.cpu().numpy(), rc)
     np.testing.assert_array_equal(assign.cpu().numpy(), ra)
     np.testing.assert_array_equal(dists.cpu().numpy(), rd)
@@ -46,7 +48,8 @@ def test_build_bucket2_host_arrays_and_graph():
 
 def test_build_bucket2_rejects_bad_parameters():
     X = torch.zeros((100, 8), dtype=torch.uint8, device="cuda")
-    for kw in ({"knn_degree": 0}, {"knn_degree": 8, "nprobe": 200}, {"knn_degree": 8, "centroid_ratio": 2.0}):
+    for kw in ({"knn_degree": 0}, {"knn_degree": 8, "nprobe": 200}, {"knn_degree": 8, "centroid_ratio": 2.0},
+               {"knn_degree": 8, "assign_rule": "other"}):
         with pytest.raises(gta.GtaError) as e:
             gta.build_bucket2(X, **kw)
         assert e.value.code == L.GTA_EINVAL
