@@ -1955,6 +1955,92 @@ int gta_bucket_knn_rows_ranged(const void* R, int32_t dtype, int64_t n, int32_t 
     });
 }
 
+int gta_shard_pack_memberships(const void* X, int32_t dtype, int64_t n_local, int32_t d, int64_t row0,
+                               const int32_t* top2, int32_t B, const uint64_t* holders, int32_t world,
+                               int64_t* send_counts, void* send_rows, int32_t* send_meta, int64_t capacity,
+                               void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(send_counts && holders && B >= 1 && world >= 1 && world <= 64 && n_local >= 0 && d >= 1 &&
+                        row0 >= 0 && (n_local == 0 || (X && top2)) && (send_rows == nullptr) == (send_meta == nullptr),
+                    kInvalid, "gta_shard_pack_memberships: bad argument");
+        GTA_REQUIRE(dtype == GTA_F32 || dtype == GTA_U8 || dtype == GTA_I8, kInvalid,
+                    "gta_shard_pack_memberships: bad dtype");
+        cudaStream_t st = S(stream);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        ShardPackMem a{X, n_local, static_cast<int64_t>(d) * elem_size(dtype), row0, top2, B, world, holders,
+                       send_rows, send_meta, capacity, err.get()};
+        std::vector<int64_t> counts;
+        shard_pack_memberships(a, counts, st);
+        check_device_error(err.get(), st, "gta_shard_pack_memberships");
+        std::copy(counts.begin(), counts.end(), send_counts);
+    });
+}
+
+int gta_shard_pack_lists(const int32_t* list_ids, const float* list_dists, int64_t n, int32_t M, const int32_t* order,
+                         const int32_t* gid, const int64_t* offsets, int32_t B, const int64_t* row_lo,
+                         const int64_t* row_hi, const int64_t* starts, int32_t world, int64_t* send_counts,
+                         int32_t* send_ids, float* send_dists, int32_t* send_meta, int64_t capacity, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(send_counts && offsets && row_lo && row_hi && starts && B >= 1 && M >= 1 && world >= 1 &&
+                        world <= 64 && n >= 0 && (n == 0 || (list_ids && list_dists && order && gid)) &&
+                        (send_ids == nullptr) == (send_dists == nullptr) &&
+                        (send_ids == nullptr) == (send_meta == nullptr),
+                    kInvalid, "gta_shard_pack_lists: bad argument");
+        for (int r = 0; r < world; ++r)
+            GTA_REQUIRE(starts[r] <= starts[r + 1], kInvalid, "gta_shard_pack_lists: row ranges out of order");
+        cudaStream_t st = S(stream);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        ShardPackLists a{list_ids, list_dists, n, M, order, gid, offsets, B, world, row_lo, row_hi, starts,
+                         send_ids, send_dists, send_meta, capacity, err.get()};
+        std::vector<int64_t> counts;
+        shard_pack_lists(a, counts, st);
+        check_device_error(err.get(), st, "gta_shard_pack_lists");
+        std::copy(counts.begin(), counts.end(), send_counts);
+    });
+}
+
+int gta_shard_member_rows(const int32_t* meta, int64_t n, int64_t row0, int64_t n_local, const int32_t* top2,
+                          int64_t* mem_row, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(n >= 0 && n_local >= 0 && row0 >= 0 && (n == 0 || meta) && (n_local == 0 || (top2 && mem_row)),
+                    kInvalid, "gta_shard_member_rows: bad argument");
+        cudaStream_t st = S(stream);
+        if (n_local == 0) {
+            GTA_REQUIRE(n == 0, kData, "gta_shard_member_rows: lists for a rank without rows");
+            return;
+        }
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        shard_member_rows(meta, n, row0, n_local, top2, mem_row, err.get(), st);
+        check_device_error(err.get(), st, "gta_shard_member_rows");
+    });
+}
+
+int gta_shard_lower_seeds(const float* list_dists, int32_t M, int64_t n, const int32_t* order, const int32_t* gid,
+                          const int64_t* offsets, const int32_t* partner, int32_t B, const int64_t* row_lo,
+                          const int64_t* row_hi, int64_t N, float* seed, void* stream)
+{
+    return guard([&] {
+        GTA_WORKSPACE(stream);
+        GTA_REQUIRE(offsets && row_lo && row_hi && B >= 1 && M >= 1 && n >= 0 && N >= 0 && (N == 0 || seed) &&
+                        (n == 0 || (list_dists && order && gid && partner)),
+                    kInvalid, "gta_shard_lower_seeds: bad argument");
+        cudaStream_t st = S(stream);
+        DevBuf<int> err(1, st);
+        GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        shard_lower_seeds(list_dists, M, n, order, gid, offsets, partner, B, row_lo, row_hi, N, seed, err.get(), st);
+        check_device_error(err.get(), st, "gta_shard_lower_seeds");
+    });
+}
+
 int gta_sanitize_rows(const int32_t* knn, int64_t n_rows, int64_t row0, int64_t n, int32_t m, uint32_t* out,
                       void* stream)
 {

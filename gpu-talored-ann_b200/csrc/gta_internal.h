@@ -245,6 +245,48 @@ void kpar_sample(const float* min_d, int64_t n, uint64_t seed, int round, double
                  uint8_t* sel, cudaStream_t st);
 int64_t select_flagged(const uint8_t* flags, int64_t n, int32_t* out, cudaStream_t st);  // ids in order; syncs
 void min_update(float* min_d, const float* d_new, int64_t n, cudaStream_t st);
+// ---- sharded build (shard.cu): the exchanges' packing
+// perm: for each rank in turn, the items whose mask carries the rank's bit, in item order;
+// counts[r] (host) the number of items for rank r.
+void stable_partition(const uint64_t* masks, int64_t n, int world, DevBuf<int64_t>& perm, std::vector<int64_t>& counts,
+                      cudaStream_t st);
+struct ShardPackMem {
+    const void* X;            // n_local rows of row_bytes bytes (this rank's dataset rows)
+    int64_t n_local, row_bytes, row0;
+    const int32_t* top2;      // [n_local x 2]: the two buckets of every local point
+    int32_t B, world;
+    const uint64_t* holders;  // [B]: bit r set when rank r holds a piece of the bucket
+    void* send_rows;          // null: counts only
+    int32_t* send_meta;       // [total x 3]: (global id, bucket, other bucket)
+    int64_t capacity;         // rows the send buffers hold
+    int* err;
+};
+void shard_pack_memberships(const ShardPackMem& a, std::vector<int64_t>& counts, cudaStream_t st);
+struct ShardPackLists {
+    const int32_t* lid;       // [n_r x M] lists of the grouped received rows
+    const float* ldist;
+    int64_t n_r;
+    int32_t M;
+    const int32_t* order;     // grouped row j = received row order[j]
+    const int32_t* gid;       // [n_r] global id of every received row
+    const int64_t* offsets;   // [B + 1] grouped rows of each bucket
+    int32_t B, world;
+    const int64_t* row_lo;    // host [B]: this rank's row range of each bucket
+    const int64_t* row_hi;
+    const int64_t* starts;    // host [world + 1]: rank r owns global rows [starts[r], starts[r+1])
+    int32_t* send_ids;        // null: counts only
+    float* send_dists;
+    int32_t* send_meta;       // [total x 2]: (global id, bucket)
+    int64_t capacity;
+    int* err;
+};
+void shard_pack_lists(const ShardPackLists& a, std::vector<int64_t>& counts, cudaStream_t st);
+void shard_member_rows(const int32_t* meta, int64_t n_b, int64_t row0, int64_t n_local, const int32_t* top2,
+                       int64_t* mem_row, int* err, cudaStream_t st);
+void shard_lower_seeds(const float* ldist, int32_t M, int64_t n_r, const int32_t* order, const int32_t* gid,
+                       const int64_t* offsets, const int32_t* partner, int32_t B, const int64_t* row_lo_h,
+                       const int64_t* row_hi_h, int64_t N, float* seed, int* err, cudaStream_t st);
+
 void balanced_assign(const int32_t* top2, const float* top2_d, int rule, const int32_t* cid, int32_t n_c, int64_t n,
                      int32_t* assign, int* err, cudaStream_t st);
 void pool_fill(const int32_t* members, const int64_t* offsets, const int32_t* seg_b, const int64_t* seg_dst, int32_t S,

@@ -696,45 +696,47 @@ __global__ void split_rows_kernel(const float* __restrict__ pool, int dp, int d,
 
 // ---- exact rerank ------------------------------------------------------------------------
 // The exact distances run on a bucket-contiguous f32 copy of the pool rows (pitch dp, a
-// multiple of 32, zero past d: the extra terms add +0 to the chain and change nothing).  A warp
-// evaluates 32 candidates at a time, one per lane: each 32-dimension chunk of the 32 candidate
-// rows is loaded coalesced (a 128-byte row segment per load instruction, the next chunk already
-// in flight while this one is consumed), transposed through shared memory, and every lane
-// continues its own ascending fmaf chain over the chunk.
+// multiple of 32, zero past d: the extra terms add +0 to the chain and change nothing; rows
+// 128-byte aligned).  A warp evaluates 32 candidates at a time, one per lane: each lane streams
+// its candidate's row with 16-byte loads (eight in flight, the next 32 floats loading while these
+// are consumed) and continues its ascending fmaf chain against the query row, read from shared
+// memory as broadcasts.
 constexpr int kRrWarps = 4;
 constexpr int kRrKeys = 512;
 constexpr int kRrRows = 8;        // A rows per rerank work item (few rows in flight per bucket)
-constexpr int kTileLd = 33;       // padded leading dimension of the transposed chunk
+constexpr int kChainVec = 8;      // 16-byte loads in flight per lane
 
-// exact fp32 chain (ascending dimensions) of the query row q_s (shared memory, dp floats) against
-// pool row `brow` of this lane (-1: none, the result is ignored); warp-collective
-__device__ __forceinline__ float tile_chain(const float* __restrict__ q_s, const float* __restrict__ pool, int dp,
-                                            int64_t brow, float* __restrict__ tile, int lane)
+// exact fp32 chain (ascending dimensions) of the query row q_s (shared memory, dp floats, 16-byte
+// aligned) against pool row `brow` of this lane (-1: none, the result is ignored)
+__device__ __forceinline__ float lane_chain(const float* __restrict__ q_s, const float* __restrict__ pool, int dp,
+                                            int64_t brow)
 {
+    const float4* r4 = reinterpret_cast<const float4*>(pool + (brow >= 0 ? brow : 0) * static_cast<int64_t>(dp));
+    const float4* q4 = reinterpret_cast<const float4*>(q_s);
+    const int n4 = dp >> 2;  // a multiple of kChainVec
     float acc = 0.0f;
-    float v[32];
+    float4 cur[kChainVec], nxt[kChainVec];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-        const int64_t br = __shfl_sync(0xffffffffu, brow, j);
-        v[j] = br >= 0 ? __ldg(pool + br * dp + lane) : 0.0f;
-    }
-    for (int k0 = 0; k0 < dp; k0 += 32) {
+    for (int b = 0; b < kChainVec; ++b) cur[b] = __ldg(r4 + b);
+    for (int i = 0; i < n4; i += kChainVec) {
+        if (i + kChainVec < n4) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) tile[lane * kTileLd + j] = v[j];
-        __syncwarp();
-        if (k0 + 32 < dp) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int64_t br = __shfl_sync(0xffffffffu, brow, j);
-                v[j] = br >= 0 ? __ldg(pool + br * dp + k0 + 32 + lane) : 0.0f;
-            }
+            for (int b = 0; b < kChainVec; ++b) nxt[b] = __ldg(r4 + i + kChainVec + b);
         }
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
-            const float t = q_s[k0 + k] - tile[k * kTileLd + lane];
+        for (int b = 0; b < kChainVec; ++b) {
+            const float4 q = q4[i + b];
+            float t = q.x - cur[b].x;
+            acc = fmaf(t, t, acc);
+            t = q.y - cur[b].y;
+            acc = fmaf(t, t, acc);
+            t = q.z - cur[b].z;
+            acc = fmaf(t, t, acc);
+            t = q.w - cur[b].w;
             acc = fmaf(t, t, acc);
         }
-        __syncwarp();
+#pragma unroll
+        for (int b = 0; b < kChainVec; ++b) cur[b] = nxt[b];
     }
     return acc;
 }
@@ -783,11 +785,24 @@ struct RerankX {
     unsigned* n_rescan;         // device counter of those rows
 };
 
-__device__ __forceinline__ void write_list(const RerankX& p, int64_t irow, const uint64_t* keys, int n_sorted, int lane)
+// The row's top-m_out (keys ascending, n_sorted of them in keys[]).  compact (a chunk k > 0
+// list, read only by merge_step_kernel): the valid entries and, when there are fewer than m_out,
+// one id -1 after them; the rest of the row keeps stale entries.
+__device__ __forceinline__ void write_list(const RerankX& p, int64_t irow, const uint64_t* keys, int n_sorted, int lane,
+                                           bool compact = false)
 {
     int32_t* oi = irow < p.n_rows ? p.out_ids + irow * p.m_out : p.ext_ids + (irow - p.n_rows) * p.m_out;
     float* od = irow < p.n_rows ? p.out_dists + irow * p.m_out : p.ext_dists + (irow - p.n_rows) * p.m_out;
-    for (int j = lane; j < p.m_out; j += 32) {
+    int n_w = p.m_out;
+    if (compact) {
+        int nv = 0;  // valid keys (sorted first)
+        for (int j0 = 0; j0 < n_sorted && j0 < p.m_out; j0 += 32) {
+            const int j = j0 + lane;
+            nv += __popc(__ballot_sync(0xffffffffu, j < n_sorted && j < p.m_out && keys[j] != ~0ull));
+        }
+        n_w = nv < p.m_out ? nv + 1 : p.m_out;
+    }
+    for (int j = lane; j < n_w; j += 32) {
         const uint64_t key = j < n_sorted ? keys[j] : ~0ull;
         const bool v = key != ~0ull;
         oi[j] = v ? static_cast<int32_t>(static_cast<uint32_t>(key)) : -1;
@@ -795,14 +810,12 @@ __device__ __forceinline__ void write_list(const RerankX& p, int64_t irow, const
     }
 }
 
-__global__ void __launch_bounds__(kRrWarps * 32) rerank_kernel(const RerankX p)
+__global__ void __launch_bounds__(kRrWarps * 32, 4) rerank_kernel(const RerankX p)
 {
     extern __shared__ uint8_t sm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t* keys = reinterpret_cast<uint64_t*>(sm) + warp * kRrKeys;
-    float* tile = reinterpret_cast<float*>(sm + kRrWarps * kRrKeys * sizeof(uint64_t)) + warp * 32 * kTileLd;
-    float* q_s = reinterpret_cast<float*>(sm + kRrWarps * kRrKeys * sizeof(uint64_t) + kRrWarps * 32 * kTileLd * 4) +
-                 warp * p.dp;
+    float* q_s = reinterpret_cast<float*>(sm + kRrWarps * kRrKeys * sizeof(uint64_t)) + warp * p.dp;
     const WorkItem w = p.work[blockIdx.x];
     const float bm = *p.maxnorm;
     const float sc = screen_scale(bm);
@@ -814,12 +827,20 @@ __global__ void __launch_bounds__(kRrWarps * 32) rerank_kernel(const RerankX p)
         const uint32_t code = key >> p.col_bits;
         return code == 0u ? -INFINITY : code_value(code - 1u, code_b) * inv_s2;
     };
+    // a seeded chunk (pad2 >= 0) writes its list compactly: merge_step_kernel reads it
+    const bool compact = w.pad2 >= 0 && static_cast<int64_t>(w.item_row0) >= p.n_rows;
     for (int r = warp; r < w.a_rows; r += kRrWarps) {
         const int64_t arow = static_cast<int64_t>(w.a_row0) + r;
         const int64_t irow = static_cast<int64_t>(w.item_row0) + r;
+        const int nv = p.cand_n[irow];
+        if (nv == 0) {  // nothing admitted: an empty list
+            if (p.stats && lane == 0) atomicAdd(&p.stats[2], 1ull);
+            write_list(p, irow, keys, 0, lane, compact);
+            __syncwarp();
+            continue;
+        }
         for (int i = lane; i < p.dp; i += 32) q_s[i] = p.pool[arow * p.dp + i];
         __syncwarp();
-        const int nv = p.cand_n[irow];
         const uint32_t* kl = reinterpret_cast<const uint32_t*>(p.cand_cols) + irow * p.L;
         // exact keys of list positions [j_lo, j_hi) into keys[j]; returns the largest distance
         auto exact_range = [&](int j_lo, int j_hi) {
@@ -828,7 +849,7 @@ __global__ void __launch_bounds__(kRrWarps * 32) rerank_kernel(const RerankX p)
                 const int j = j0 + lane;
                 const int c = j < j_hi ? static_cast<int>(kl[j] & col_mask) : -1;
                 const int64_t brow = c >= 0 ? static_cast<int64_t>(w.b_row0) + c : -1;
-                const float dd = tile_chain(q_s, p.pool, p.dp, brow, tile, lane);
+                const float dd = lane_chain(q_s, p.pool, p.dp, brow);
                 if (c >= 0) {
                     keys[j] = (static_cast<uint64_t>(f2key(dd)) << 32) | static_cast<uint32_t>(p.gid[brow]);
                     mx = fmaxf(mx, dd);
@@ -882,7 +903,7 @@ __global__ void __launch_bounds__(kRrWarps * 32) rerank_kernel(const RerankX p)
         for (int j = n_tot + lane; j < np2; j += 32) keys[j] = ~0ull;
         __syncwarp();
         rr_sort(keys, np2, lane);
-        write_list(p, irow, keys, np2, lane);
+        write_list(p, irow, keys, np2, lane, compact);
         __syncwarp();
     }
 }
@@ -899,8 +920,7 @@ __global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t* all = reinterpret_cast<uint64_t*>(sm);
     uint64_t* keys = all + warp * kRrKeys;
-    float* tile = reinterpret_cast<float*>(sm + kRsWarps * kRrKeys * sizeof(uint64_t)) + warp * 32 * kTileLd;
-    float* q_s = reinterpret_cast<float*>(sm + kRsWarps * kRrKeys * sizeof(uint64_t) + kRsWarps * 32 * kTileLd * 4);
+    float* q_s = reinterpret_cast<float*>(sm + kRsWarps * kRrKeys * sizeof(uint64_t));
     const unsigned n = *p.n_rescan;
     for (unsigned i = blockIdx.x; i < n; i += gridDim.x) {
         const int2 e = p.rescan[i];
@@ -919,7 +939,7 @@ __global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p)
                 const int c = c0 + j + lane;
                 const bool ok = c < w.b_rows && c != self;
                 const int64_t brow = ok ? static_cast<int64_t>(w.b_row0) + c : -1;
-                const float dd = tile_chain(q_s, p.pool, p.dp, brow, tile, lane);
+                const float dd = lane_chain(q_s, p.pool, p.dp, brow);
                 keys[kRrKeys / 2 + j + lane] =
                     ok ? (static_cast<uint64_t>(f2key(dd)) << 32) | static_cast<uint32_t>(p.gid[brow]) : ~0ull;
             }
@@ -944,15 +964,17 @@ __global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p)
 // exact top-m_out of the chunks so far, in its chunk-0 extension row) and its seed (the running
 // list's m_out-th distance, a bound on the row's exact M-th that the next chunk's screen and
 // rerank use).  lo, nb: the first pool row with a list and the count of such rows (a row range of
-// the segment, whose columns are all its rows).  Chunk k of pool row lo + i sits at extension row
-// base_ext + k * nb + i.
+// the segment, whose columns are all its rows).  Two extension slots per row: chunk 0's list (then
+// the running list) at base_ext + i, the current chunk k > 0 at base_ext + nb + i (reused by every
+// wave: a wave's lists are merged before the next wave's rerank writes).
 struct ChunkSeg {
     int64_t lo, nb, base_ext, row_prefix;  // base_ext: extension row of (chunk 0, row 0)
     int32_t nch, pad;
 };
 
 // k = 0: seeds from the chunk-0 lists; k > 0: chunk k merged into the running list (by
-// (distance, id)), then the seed; k < 0: the running lists written to the rows' outputs.
+// (distance, id)), then the seed (nothing to do for an empty chunk list); k < 0: the running
+// lists written to the rows' outputs.
 // One warp per row of the chunked segments.
 __global__ void __launch_bounds__(kRrWarps * 32)
     merge_step_kernel(const ChunkSeg* __restrict__ segs, int n_segs, int64_t n_rows_total, int k,
@@ -982,19 +1004,46 @@ __global__ void __launch_bounds__(kRrWarps * 32)
     }
     if (k >= sg.nch) return;
     if (k > 0) {
+        const int64_t er = sg.base_ext + sg.nb + i;
+        // a chunk list with no entry (every column beyond the seed) leaves the running list and
+        // its seed as they are
+        if (ext_ids[er * m_out] < 0) return;
         uint64_t* keys = s_keys[warp];
-        auto key_of = [&](int64_t er, int t) {
-            const int32_t id = ext_ids[er * m_out + t];
+        // the chunk list is compact: its entries end at the first id -1 (or at m_out)
+        int n_new = m_out;
+        for (int t0 = 0; t0 < m_out; t0 += 32) {
+            const unsigned neg = __ballot_sync(0xffffffffu, t0 + lane < m_out && ext_ids[er * m_out + t0 + lane] < 0);
+            if (neg) {
+                n_new = t0 + __ffs(neg) - 1;
+                break;
+            }
+        }
+        auto key_of = [&](int64_t row, int t) {
+            const int32_t id = (row == er && t >= n_new) ? -1 : ext_ids[row * m_out + t];
             return id < 0 ? ~0ull
-                          : (static_cast<uint64_t>(f2key(ext_dists[er * m_out + t])) << 32) | static_cast<uint32_t>(id);
+                          : (static_cast<uint64_t>(f2key(ext_dists[row * m_out + t])) << 32) | static_cast<uint32_t>(id);
         };
-        const int64_t er = sg.base_ext + static_cast<int64_t>(k) * sg.nb + i;
-        for (int t = lane; t < kRrKeys / 2; t += 32) {
+        // both lists ascending by (distance, id), disjoint (chunks split the columns): the running
+        // list then the chunk's reversed form one bitonic sequence of 2P keys; half-cleaners sort it
+        int P = 32;
+        while (P < m_out) P <<= 1;
+        for (int t = lane; t < P; t += 32) {
             keys[t] = t < m_out ? key_of(run, t) : ~0ull;
-            keys[kRrKeys / 2 + t] = t < m_out ? key_of(er, t) : ~0ull;
+            keys[2 * P - 1 - t] = t < m_out ? key_of(er, t) : ~0ull;
         }
         __syncwarp();
-        rr_sort(keys, kRrKeys, lane);
+        for (int j = P; j > 0; j >>= 1) {
+            const int lj = __ffs(j) - 1;
+            for (int t = lane; t < P; t += 32) {
+                const int a = ((t >> lj) << (lj + 1)) + (t & (j - 1));
+                const uint64_t x = keys[a], y = keys[a + j];
+                if (x > y) {
+                    keys[a] = y;
+                    keys[a + j] = x;
+                }
+            }
+            __syncwarp();
+        }
         for (int t = lane; t < m_out; t += 32) {
             const uint64_t key = keys[t];
             const bool v = key != ~0ull;
@@ -1081,9 +1130,21 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     // Work: one item per 128 rows of a segment.  A segment longer than kChunk runs as column
     // chunks of kChunk in waves: wave 0 holds every short segment and the chunk 0 of the long
     // ones; wave k > 0 holds chunk k, its rows seeded with the m-th distance of their running list
-    // (the exact top-m of chunks 0 .. k-1).  Each (row, chunk) has its own list row past the pool
-    // rows (an extension row).
-    constexpr int64_t kChunk = 1 << 16;
+    // (the exact top-m of chunks 0 .. k-1).  A chunked row has two list rows past the pool rows
+    // (extension rows): its running list and the current chunk's.
+    // kChunk: the CTAs of a wave re-read their own A tiles and the chunk's B tiles from L2 once per
+    // column tile, so a chunk is sized for both to stay in L2 (the A tiles of one CTA per SM plus
+    // the chunk's columns within 90% of it; a power of two, 4096 .. 65536 columns).
+    const int64_t row_bytes = static_cast<int64_t>(pr.parts) * ((pr.d + 63) / 64 * 64) * 2;
+    int64_t kChunk = 1 << 16;
+    {
+        int dev = 0, l2 = 0, n_sm = 0;
+        GTA_CUDA(cudaGetDevice(&dev));
+        GTA_CUDA(cudaDeviceGetAttribute(&l2, cudaDevAttrL2CacheSize, dev));
+        GTA_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
+        const int64_t room = static_cast<int64_t>(0.9 * l2) - static_cast<int64_t>(n_sm) * kSTile * row_bytes;
+        while (kChunk > 4096 && kChunk * row_bytes > room) kChunk >>= 1;
+    }
     std::vector<std::vector<WorkItem>> waves(1);
     std::vector<double> wave_flops(1, 0.0);
     std::vector<ChunkSeg> chunked;
@@ -1121,11 +1182,11 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
                 waves[static_cast<size_t>(k)].push_back(
                     WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, r1 - t)),
                              static_cast<int32_t>(lo + c0), static_cast<int32_t>(cn), static_cast<int32_t>(t - c0),
-                             static_cast<int32_t>(base + k * nr + (t - r0)), 1,
+                             static_cast<int32_t>(base + (k == 0 ? 0 : nr) + (t - r0)), 1,
                              k == 0 ? -1 : static_cast<int32_t>(chunked_rows + (t - r0))});
             wave_flops[static_cast<size_t>(k)] += 2.0 * static_cast<double>(nr) * static_cast<double>(cn) * pr.d;
         }
-        ext_rows += static_cast<int64_t>(nch) * nr;
+        ext_rows += 2 * nr;
         chunked_rows += nr;
     }
     const int64_t item_rows = pr.n_rows + ext_rows;
@@ -1227,8 +1288,8 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     r.seed = seeds.get();
     r.rescan = rescan.get();
     r.n_rescan = n_rescan.get();
-    const size_t smem_rr = kRrWarps * (kRrKeys * sizeof(uint64_t) + 32 * kTileLd * 4 + static_cast<size_t>(dp) * 4);
-    const size_t smem_rs = kRsWarps * (kRrKeys * sizeof(uint64_t) + 32 * kTileLd * 4) + static_cast<size_t>(dp) * 4;
+    const size_t smem_rr = kRrWarps * (kRrKeys * sizeof(uint64_t) + static_cast<size_t>(dp) * 4);
+    const size_t smem_rs = kRsWarps * kRrKeys * sizeof(uint64_t) + static_cast<size_t>(dp) * 4;
     GTA_REQUIRE(smem_rr <= kSSmemMax && smem_rs <= kSSmemMax, kInvalid, "rerank: dimension too large");
     GTA_CUDA(cudaFuncSetAttribute(rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_rr)));
     GTA_CUDA(cudaFuncSetAttribute(rescan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_rs)));

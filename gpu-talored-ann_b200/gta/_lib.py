@@ -92,6 +92,10 @@ _SIGS = {
     "gta_bucket_knn_rows": [_P, _I32, _I64, _I32, _P, _P, _P, _I32, _I32, _P, _P, _P],
     "gta_bucket_knn_rows_phased": [_P, _I32, _I64, _I32, _P, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _P],
     "gta_bucket_knn_rows_ranged": [_P, _I32, _I64, _I32, _P, _P, _P, _P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _P],
+    "gta_shard_pack_memberships": [_P, _I32, _I64, _I32, _I64, _P, _I32, _P, _I32, _P, _P, _P, _I64, _P],
+    "gta_shard_pack_lists": [_P, _P, _I64, _I32, _P, _P, _P, _I32, _P, _P, _P, _I32, _P, _P, _P, _P, _I64, _P],
+    "gta_shard_member_rows": [_P, _I64, _I64, _I64, _P, _P, _P],
+    "gta_shard_lower_seeds": [_P, _I32, _I64, _P, _P, _P, _P, _I32, _P, _P, _I64, _P, _P],
     "gta_sanitize_rows": [_P, _I64, _I64, _I64, _I32, _P, _P],
     "gta_prune_rows": [_P, _I64, _I32, _I32, _I64, _I64, _P, _I32, _P, _P],
     "gta_reverse_merge_rows": [_P, _I64, _I32, _I64, _I64, _P, _P],

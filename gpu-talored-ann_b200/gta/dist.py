@@ -38,8 +38,9 @@ reproduced exactly: the centroid sums are sums of integers in fp64, and every
 other stage sees the same inputs in the same order.  For f32 data the centroid
 sums are added in a different order, so centroids may differ in the last bit.
 
-``Stages`` is the per-rank compute interface; ``CudaStages`` binds libgta.  The
-driver itself only sorts, counts and moves data between ranks.
+``Stages`` is the per-rank compute interface; ``CudaStages`` binds libgta (the packing of
+every exchange included: gta_shard_pack_memberships / gta_shard_pack_lists).  The driver
+itself only places buckets (host arithmetic on B sizes) and runs the collectives.
 """
 from __future__ import annotations
 
@@ -181,6 +182,55 @@ class CudaStages:
                                                   _p(offsets), _p(partner), offsets.numel() - 1, M, phase, _p(seed),
                                                   ctypes.c_void_p(rlo.data_ptr()), ctypes.c_void_p(rhi.data_ptr()),
                                                   _p(lid), _p(ldist), self._st()))
+
+    def pack_memberships(self, X_local, row0, top2, holders, world):
+        """Every local membership to the holders of its bucket, packed by destination rank:
+        (rows [k x d] of X's dtype, meta [k x 3] int32, per-rank counts)."""
+        n, d = X_local.shape
+        cnt = (ctypes.c_int64 * world)()
+        h = holders.to(device=X_local.device, dtype=torch.int64).contiguous()
+        args = (_p(X_local), _ELEM[X_local.dtype], n, d, row0, _p(top2), h.numel(), _p(h), world, cnt)
+        L.check(self.L.gta_shard_pack_memberships(*args, None, None, 0, self._st()))
+        k = sum(cnt)
+        rows = torch.empty((k, d), dtype=X_local.dtype, device=X_local.device)
+        meta = torch.empty((k, 3), dtype=torch.int32, device=X_local.device)
+        L.check(self.L.gta_shard_pack_memberships(*args, _p(rows), _p(meta), k, self._st()))
+        return rows, meta, list(cnt)
+
+    def pack_lists(self, lid, ldist, order, gid, offsets, row_lo, row_hi, starts, world):
+        """The lists of this rank's row ranges to their points' owners, packed by destination:
+        (ids [k x M], dists [k x M], meta [k x 2] = (global id, bucket), per-rank counts)."""
+        n, M = lid.shape
+        cnt = (ctypes.c_int64 * world)()
+        lo = row_lo.to(torch.int64).contiguous()
+        hi = row_hi.to(torch.int64).contiguous()
+        stt = torch.tensor(starts, dtype=torch.int64)
+        args = (_p(lid), _p(ldist), n, M, _p(order), _p(gid), _p(offsets), offsets.numel() - 1,
+                ctypes.c_void_p(lo.data_ptr()), ctypes.c_void_p(hi.data_ptr()), ctypes.c_void_p(stt.data_ptr()),
+                world, cnt)
+        L.check(self.L.gta_shard_pack_lists(*args, None, None, None, 0, self._st()))
+        k = sum(cnt)
+        ids = torch.empty((k, M), dtype=torch.int32, device=lid.device)
+        dd = torch.empty((k, M), dtype=torch.float32, device=lid.device)
+        meta = torch.empty((k, 2), dtype=torch.int32, device=lid.device)
+        L.check(self.L.gta_shard_pack_lists(*args, _p(ids), _p(dd), _p(meta), k, self._st()))
+        return ids, dd, meta, list(cnt)
+
+    def member_rows(self, meta, row0, n_local, top2):
+        mem_row = torch.empty((n_local, 2), dtype=torch.int64, device=top2.device)
+        L.check(self.L.gta_shard_member_rows(_p(meta), meta.shape[0], row0, n_local, _p(top2), _p(mem_row),
+                                             self._st()))
+        return mem_row
+
+    def lower_seeds(self, ldist, order, gid, offsets, partner, row_lo, row_hi, N):
+        seed = torch.empty((N,), dtype=torch.float32, device=ldist.device)
+        lo = row_lo.to(torch.int64).contiguous()
+        hi = row_hi.to(torch.int64).contiguous()
+        L.check(self.L.gta_shard_lower_seeds(_p(ldist), ldist.shape[1], ldist.shape[0], _p(order), _p(gid),
+                                             _p(offsets), _p(partner), offsets.numel() - 1,
+                                             ctypes.c_void_p(lo.data_ptr()), ctypes.c_void_p(hi.data_ptr()), N,
+                                             _p(seed), self._st()))
+        return seed
 
     def merge_memberships(self, lid, ldist, mem_row):
         n, M = mem_row.shape[0], lid.shape[1]
@@ -361,44 +411,33 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
     dist.all_reduce(sizes, group=group)
     sizes_l = sizes.tolist()
     pieces = place_pieces(sizes_l, world, prm.split_share)
-    hold_n = [0] * B
+    holders = [0] * B
     row_lo, row_hi = [0] * B, [0] * B
     owner = [-1] * B
     for b, r, lo, hi in pieces:
-        hold_n[b] += 1
+        holders[b] |= 1 << r
         if owner[b] < 0:
             owner[b] = r
         if r == rank:
             row_lo[b], row_hi[b] = lo, hi
-    hold_off = [0] * (B + 1)
-    for b in range(B):
-        hold_off[b + 1] = hold_off[b] + hold_n[b]
-    hold_n_t = torch.tensor(hold_n, dtype=torch.int64, device=dev)
-    hold_off_t = torch.tensor(hold_off[:B], dtype=torch.int64, device=dev)
-    hold_rank_t = torch.tensor([p[1] for p in pieces], dtype=torch.int64, device=dev)
+    # the holder masks as int64 bit patterns (bit 63 is rank 63)
+    holders_t = torch.tensor([h - (1 << 64) if h >= 1 << 63 else h for h in holders], dtype=torch.int64)
+    rlo_h = torch.tensor(row_lo, dtype=torch.int64)
+    rhi_h = torch.tensor(row_hi, dtype=torch.int64)
     ph.mark("top2_placement")
 
-    # ---- 4. memberships to every holder of their bucket: slot s of point p is membership 2p+s,
-    # sent once per piece of its bucket, in membership order within each destination
-    bucket = top2.reshape(-1)
-    other = top2.flip(1).reshape(-1)
-    nh = hold_n_t[bucket.long()]
-    mi = torch.repeat_interleave(torch.arange(bucket.numel(), device=dev), nh)
-    copy = torch.arange(mi.numel(), device=dev) - (torch.cumsum(nh, 0) - nh)[mi]
-    dest = hold_rank_t[hold_off_t[bucket[mi].long()] + copy]
-    perm = mi[torch.sort(dest, stable=True).indices]
-    send_counts = torch.bincount(dest, minlength=world).to(torch.int64)
+    # ---- 4. memberships to every holder of their bucket (slot s of point p is membership 2p+s),
+    # packed by destination in membership order
+    rows, meta, send_l = st.pack_memberships(X_local, row0, top2, holders_t, world)
+    send_counts = torch.tensor(send_l, dtype=torch.int64, device=dev)
     recv_counts = torch.empty_like(send_counts)
     dist.all_to_all_single(recv_counts, send_counts, group=group)
-    p_of = (perm // 2)
-    meta = torch.stack([gid_local[p_of], bucket[perm], other[perm]], dim=1).to(torch.int32)
-    rows = X_local[p_of]
     elem = rows.element_size()
     R = _exchange(rows.reshape(rows.shape[0], -1).view(torch.uint8), send_counts, recv_counts, group)
     R = R.view(X_local.dtype).reshape(-1, d)
     meta_r = _exchange(meta, send_counts, recv_counts, group)
     sent += rows.numel() * elem + meta.numel() * 4
-    del rows, meta, mi, copy, dest
+    del rows, meta
     ph.mark("exchange_points")
 
     # ---- 5. per-bucket top-M for this rank's row range of each bucket it holds: first the rows
@@ -408,48 +447,28 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
     gid_r = meta_r[:, 0].contiguous()
     order, offsets = st.group_memberships(meta_r[:, 1].contiguous(), meta_r[:, 2].contiguous(), B)
     n_r = R.shape[0]
-    ol = order.long()
-    bucket_s = meta_r[:, 1][ol]
-    partner_s = meta_r[:, 2][ol].contiguous()
-    bl = bucket_s.long()
-    rel = torch.arange(n_r, device=dev) - offsets[bl]
-    mine = (rel >= torch.tensor(row_lo, dtype=torch.int64, device=dev)[bl]) & \
-        (rel < torch.tensor(row_hi, dtype=torch.int64, device=dev)[bl])
-    rlo_h = torch.tensor(row_lo, dtype=torch.int64)
-    rhi_h = torch.tensor(row_hi, dtype=torch.int64)
+    partner_s = meta_r[:, 2][order.long()].contiguous()
     lid = torch.full((n_r, M), -1, dtype=torch.int32, device=dev)
     ldist = torch.full((n_r, M), float("inf"), dtype=torch.float32, device=dev)
     st.bucket_knn_rows_ranged(R, order, gid_r, offsets, partner_s, M, 1, None, rlo_h, rhi_h, lid, ldist)
-    seed = torch.full((N,), float("inf"), dtype=torch.float32, device=dev)
-    lower = (partner_s > bucket_s) & mine
-    seed[gid_r[ol][lower].long()] = ldist[lower, M - 1]
+    seed = st.lower_seeds(ldist, order, gid_r, offsets, partner_s, rlo_h, rhi_h, N)
     dist.all_reduce(seed, op=dist.ReduceOp.MIN, group=group)
     st.bucket_knn_rows_ranged(R, order, gid_r, offsets, partner_s, M, 2, seed, rlo_h, rhi_h, lid, ldist)
     del R, seed
     ph.mark("bucket_knn")
 
-    # ---- 6. the range's lists back to the points' owners, merged per point
-    sel = mine.nonzero().squeeze(1)
-    og = gid_r[ol[sel]]
-    ob = bucket_s[sel]
-    starts_t = torch.tensor(starts[1:world], dtype=torch.int64, device=dev)
-    dest2 = torch.bucketize(og.long(), starts_t, right=True)
-    perm2 = sel[torch.sort(dest2, stable=True).indices]
-    send2 = torch.bincount(dest2, minlength=world).to(torch.int64)
+    # ---- 6. the ranges' lists back to the points' owners, merged per point
+    ids_s, dists_s, meta2, send2_l = st.pack_lists(lid, ldist, order, gid_r, offsets, rlo_h, rhi_h, starts, world)
+    send2 = torch.tensor(send2_l, dtype=torch.int64, device=dev)
     recv2 = torch.empty_like(send2)
     dist.all_to_all_single(recv2, send2, group=group)
-    meta2 = torch.stack([gid_r[ol[perm2]], bucket_s[perm2]], dim=1).to(torch.int32)
-    lid_b = _exchange(lid[perm2], send2, recv2, group)
-    ldist_b = _exchange(ldist[perm2], send2, recv2, group)
+    lid_b = _exchange(ids_s, send2, recv2, group)
+    ldist_b = _exchange(dists_s, send2, recv2, group)
     meta_b = _exchange(meta2, send2, recv2, group)
-    sent += perm2.numel() * M * 8 + meta2.numel() * 4
-    del lid, ldist, og, ob
+    sent += ids_s.numel() * 8 + meta2.numel() * 4
+    del lid, ldist, ids_s, dists_s, meta2
     ph.mark("exchange_lists")
-    p = (meta_b[:, 0].long() - row0)
-    lo_bucket = torch.minimum(top2[:, 0], top2[:, 1])
-    slot = (meta_b[:, 1] != lo_bucket[p]).long()
-    mem_row = torch.full((n_local, 2), -1, dtype=torch.int64, device=dev)
-    mem_row[p, slot] = torch.arange(meta_b.shape[0], dtype=torch.int64, device=dev)
+    mem_row = st.member_rows(meta_b, row0, n_local, top2)
     knn_ids, knn_dists = st.merge_memberships(lid_b.contiguous(), ldist_b.contiguous(), mem_row)
     del lid_b, ldist_b
     ph.mark("merge")

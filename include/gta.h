@@ -385,6 +385,50 @@ int gta_bucket_knn_rows_ranged(const void* R, int32_t dtype, int64_t n, int32_t 
                                int32_t phase, const float* seed, const int64_t* row_lo, const int64_t* row_hi,
                                int32_t* list_ids, float* list_dists, void* stream);
 
+/* The sharded build's packing for its all-to-all exchanges (device pointers, one stream).
+ * Items go to ranks by a stable multi-destination partition: rank by rank, in item order.
+ *
+ * gta_shard_pack_memberships: membership m = 2p + s (local point p, slot s of top2[p]) goes to
+ * every rank r whose bit is set in holders[top2[m]] (device uint64 [B]: the ranks holding a piece
+ * of the bucket; world <= 64).  send_counts (HOST [world]) receives the items per rank; with
+ * send_rows and send_meta null only the counts are computed (size the buffers, then call again).
+ * Otherwise item k of the packed order gets row p of X (n_local rows of d elements of dtype) in
+ * send_rows[k] and (row0 + p, top2[m], top2[m ^ 1]) in send_meta[3k..3k+2]; capacity = rows the
+ * buffers hold.  A bucket outside [0, B), or one without a holder, returns GTA_EDATA.
+ * Replaces the reference's point exchange to bucket owners (bucket.cu multi-GPU plan: points to
+ * the GPUs that own their buckets). */
+int gta_shard_pack_memberships(const void* X, int32_t dtype, int64_t n_local, int32_t d, int64_t row0,
+                               const int32_t* top2, int32_t B, const uint64_t* holders, int32_t world,
+                               int64_t* send_counts, void* send_rows, int32_t* send_meta, int64_t capacity,
+                               void* stream);
+
+/* gta_shard_pack_lists: the lists a rank computed go back to their points' owners.  Grouped row j
+ * (list_ids / list_dists [n x M], order / gid / offsets as for gta_bucket_knn_rows_ranged) is sent
+ * when it lies in [row_lo[b], row_hi[b]) of its bucket b (HOST arrays [B]), to the rank r with
+ * starts[r] <= gid[order[j]] < starts[r + 1] (HOST [world + 1]).  Packed as send_ids / send_dists
+ * [k x M] and send_meta [k x 2] = (global id, bucket); counts and the null-buffer call as above.
+ * Replaces the reference's list exchange back to the points' GPUs before the merge. */
+int gta_shard_pack_lists(const int32_t* list_ids, const float* list_dists, int64_t n, int32_t M, const int32_t* order,
+                         const int32_t* gid, const int64_t* offsets, int32_t B, const int64_t* row_lo,
+                         const int64_t* row_hi, const int64_t* starts, int32_t world, int64_t* send_counts,
+                         int32_t* send_ids, float* send_dists, int32_t* send_meta, int64_t capacity, void* stream);
+
+/* gta_shard_member_rows: for received lists i (meta [n x 2] = (global id, bucket)) of this rank's
+ * rows [row0, row0 + n_local) with buckets top2 [n_local x 2]: mem_row[2p + slot] = i, slot 0 for
+ * the lower of the point's two buckets, -1 where no list arrived (the input of
+ * gta_merge_memberships).  An id outside the rows, or a bucket not among the point's two, returns
+ * GTA_EDATA. */
+int gta_shard_member_rows(const int32_t* meta, int64_t n, int64_t row0, int64_t n_local, const int32_t* top2,
+                          int64_t* mem_row, void* stream);
+
+/* gta_shard_lower_seeds: seed[N] = +inf, then for every grouped row j in this rank's ranges
+ * (row_lo / row_hi HOST [B]) whose bucket is below its partner: seed[gid[order[j]]] =
+ * list_dists[j][M-1] (the point's lower-bucket M-th distance; the ranks' seeds are then
+ * all-reduced with min before phase 2 of gta_bucket_knn_rows_ranged). */
+int gta_shard_lower_seeds(const float* list_dists, int32_t M, int64_t n, const int32_t* order, const int32_t* gid,
+                          const int64_t* offsets, const int32_t* partner, int32_t B, const int64_t* row_lo,
+                          const int64_t* row_hi, int64_t N, float* seed, void* stream);
+
 /* gta_sanitize for rows [row0, row0 + n_rows) of an n-row graph (knn and out
  * hold only those rows). */
 int gta_sanitize_rows(const int32_t* knn, int64_t n_rows, int64_t row0, int64_t n, int32_t m, uint32_t* out,

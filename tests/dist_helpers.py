@@ -128,6 +128,52 @@ class OracleStages:
             lid[lo:hi] = tl[lo:hi]
             ldist[lo:hi] = td[lo:hi]
 
+    def pack_memberships(self, X_local, row0, top2, holders, world):
+        """Membership m = 2p + s to every holder of its bucket, rank by rank, in membership order."""
+        t2 = _np(top2).reshape(-1)
+        h = _np(holders).astype(np.int64).view(np.uint64)
+        X = _np(X_local)
+        items = [[m for m in range(t2.size) if (int(h[t2[m]]) >> r) & 1] for r in range(world)]
+        flat = np.array([m for it in items for m in it], np.int64)
+        rows = X[flat // 2] if flat.size else np.zeros((0, X.shape[1]), X.dtype)
+        meta = np.stack([row0 + flat // 2, t2[flat], t2[flat ^ 1]], 1).astype(np.int32) if flat.size else \
+            np.zeros((0, 3), np.int32)
+        return torch.from_numpy(np.ascontiguousarray(rows)), _t(meta), [len(it) for it in items]
+
+    def pack_lists(self, lid, ldist, order, gid, offsets, row_lo, row_hi, starts, world):
+        """Grouped rows inside this rank's ranges to their points' owners, rank by rank, in row order."""
+        o, g, off = _np(order).astype(np.int64), _np(gid), _np(offsets)
+        lo, hi = _np(row_lo), _np(row_hi)
+        n = o.shape[0]
+        bucket = np.repeat(np.arange(off.shape[0] - 1), np.diff(off))
+        rel = np.arange(n) - off[bucket]
+        mine = (rel >= lo[bucket]) & (rel < hi[bucket])
+        owner = np.searchsorted(np.asarray(starts[1:world]), g[o], side="right")
+        items = [np.nonzero(mine & (owner == r))[0] for r in range(world)]
+        flat = np.concatenate(items) if items else np.zeros(0, np.int64)
+        li, ld = _np(lid), _np(ldist)
+        meta = np.stack([g[o[flat]], bucket[flat]], 1).astype(np.int32)
+        return _t(li[flat]), _t(ld[flat]), _t(meta), [len(it) for it in items]
+
+    def member_rows(self, meta, row0, n_local, top2):
+        m, t2 = _np(meta), _np(top2)
+        mem_row = np.full((n_local, 2), -1, np.int64)
+        for i in range(m.shape[0]):
+            p = int(m[i, 0]) - row0
+            mem_row[p, 0 if m[i, 1] == t2[p].min() else 1] = i
+        return _t(mem_row)
+
+    def lower_seeds(self, ldist, order, gid, offsets, partner, row_lo, row_hi, N):
+        o, g, off, part = _np(order).astype(np.int64), _np(gid), _np(offsets), _np(partner)
+        lo, hi, ld = _np(row_lo), _np(row_hi), _np(ldist)
+        n = o.shape[0]
+        bucket = np.repeat(np.arange(off.shape[0] - 1), np.diff(off))
+        rel = np.arange(n) - off[bucket]
+        sel = (rel >= lo[bucket]) & (rel < hi[bucket]) & (part > bucket)
+        seed = np.full(N, np.inf, np.float32)
+        seed[g[o[sel]]] = ld[sel, -1]
+        return _t(seed)
+
     def merge_memberships(self, lid, ldist, mem_row):
         ids, dd = orc.merge_memberships(_np(lid), _np(ldist), _np(mem_row))
         return _t(ids), _t(dd)

@@ -172,6 +172,68 @@ def test_ranged_rows_match_whole_buckets(kind):
         st.bucket_knn_rows_ranged(R, order, gid, offsets, partner_s, M, 1, None, bad, badh, got_i, got_d)
 
 
+@pytest.mark.parametrize("dtype", ["u8", "f32"])
+def test_shard_packing_matches_host_restatement(dtype):
+    """gta_shard_pack_memberships / _pack_lists / _member_rows / _lower_seeds against the host
+    restatement the gloo tests use (dist_helpers.OracleStages), on random placements with split
+    buckets (several holders), uneven rank row ranges and rows outside every range."""
+    rng = np.random.default_rng(9)
+    n_local, d, B, world, row0, M = 5000, 24, 40, 5, 12345, 16
+    X = rng.integers(0, 256, (n_local, d)).astype(np.uint8)
+    if dtype == "f32":
+        X = rng.normal(size=(n_local, d)).astype(np.float32)
+    c1 = rng.integers(0, B, n_local)
+    top2 = np.stack([c1, (c1 + rng.integers(1, B, n_local)) % B], 1).astype(np.int32)
+    holders = np.zeros(B, np.int64)
+    for b in range(B):
+        for r in rng.choice(world, int(rng.integers(1, 4)), replace=False):
+            holders[b] |= 1 << int(r)
+    cs, hs = gd.CudaStages(), dist_helpers.OracleStages()
+    Xd, t2d = torch.from_numpy(X).cuda(), torch.from_numpy(top2).cuda()
+    got = cs.pack_memberships(Xd, row0, t2d, torch.from_numpy(holders), world)
+    want = hs.pack_memberships(torch.from_numpy(X), row0, torch.from_numpy(top2), torch.from_numpy(holders), world)
+    assert got[2] == want[2]
+    assert torch.equal(got[0].cpu(), want[0]) and torch.equal(got[1].cpu(), want[1])
+    # lists: received rows grouped by (bucket, other), ranges inside each bucket, owners by row ranges
+    n_r = 7000
+    bucket = rng.integers(0, B, n_r).astype(np.int32)
+    other = rng.integers(0, B, n_r).astype(np.int32)
+    gid = rng.permutation(100000)[:n_r].astype(np.int32)  # one received row per point
+    order, offsets = cs.group_memberships(torch.from_numpy(bucket).cuda(), torch.from_numpy(other).cuda(), B)
+    sizes = np.diff(offsets.cpu().numpy())
+    lo = np.array([int(rng.integers(0, s + 1)) for s in sizes], np.int64)
+    hi = np.array([int(rng.integers(l, s + 1)) for l, s in zip(lo, sizes)], np.int64)
+    starts = [0, 20000, 20001, 55000, 90000, 100000]
+    lid = torch.from_numpy(rng.integers(0, 100000, (n_r, M)).astype(np.int32)).cuda()
+    ldist = torch.from_numpy(rng.random((n_r, M)).astype(np.float32)).cuda()
+    gid_t = torch.from_numpy(gid).cuda()
+    lo_t, hi_t = torch.from_numpy(lo), torch.from_numpy(hi)
+    got = cs.pack_lists(lid, ldist, order, gid_t, offsets, lo_t, hi_t, starts, world)
+    want = hs.pack_lists(lid.cpu(), ldist.cpu(), order.cpu(), gid_t.cpu(), offsets.cpu(), lo_t, hi_t, starts, world)
+    assert got[3] == want[3]
+    for a, b in zip(got[:3], want[:3]):
+        assert torch.equal(a.cpu(), b)
+    partner = torch.from_numpy(other).cuda()[order.long()].contiguous()
+    sd = cs.lower_seeds(ldist, order, gid_t, offsets, partner, lo_t, hi_t, 100000)
+    hsd = hs.lower_seeds(ldist.cpu(), order.cpu(), gid_t.cpu(), offsets.cpu(), partner.cpu(), lo_t, hi_t, 100000)
+    assert torch.equal(sd.cpu(), hsd)
+    # member rows: each local point receives its two lists in a shuffled order
+    meta = np.stack([np.repeat(np.arange(n_local) + row0, 2), top2.reshape(-1)], 1).astype(np.int32)
+    meta = meta[rng.permutation(meta.shape[0])]
+    mr = cs.member_rows(torch.from_numpy(meta).cuda(), row0, n_local, t2d)
+    assert torch.equal(mr.cpu(), hs.member_rows(torch.from_numpy(meta), row0, n_local, torch.from_numpy(top2)))
+    # a bucket with no holder, a list of a point outside the rows: data errors
+    bad_h = holders.copy()
+    bad_h[int(top2[0, 0])] = 0
+    with pytest.raises(L.GtaError) as e:
+        cs.pack_memberships(Xd, row0, t2d, torch.from_numpy(bad_h), world)
+    assert e.value.code == L.GTA_EDATA
+    meta[0, 0] = row0 + n_local
+    with pytest.raises(L.GtaError) as e:
+        cs.member_rows(torch.from_numpy(meta).cuda(), row0, n_local, t2d)
+    assert e.value.code == L.GTA_EDATA
+
+
 def _run_ranks(world, X, prm):
     with tempfile.TemporaryDirectory() as out:
         mp.start_processes(dist_helpers.nccl_worker, args=(world, _free_port(), X, prm, out), nprocs=world,

@@ -258,17 +258,21 @@ def test_bucket_knn_f32_vs_oracle(N, d, B, M):
     assert_lists_match(host(gi), host(gd), ri, rd, exact=False, X=X, qrows=mem)
 
 
-def test_bucket_knn_f32_long_segment_column_chunks():
-    """A float segment longer than 65 536 rows runs as column chunks whose exact lists are merged:
-    sampled rows (chunk edges included) against the oracle's exact top-M over the whole segment."""
+@pytest.mark.parametrize("N,d,M,edges", [
+    (70000, 8, 16, [65535, 65536, 65537]),                    # 65 536-column chunks: two waves
+    (30000, 960, 128, [8191, 8192, 8193, 16384, 24575, 24576]),  # long rows: 8 192-column chunks, four waves
+])
+def test_bucket_knn_f32_long_segment_column_chunks(N, d, M, edges):
+    """A long float segment runs as column chunks (sized for the L2: 65 536 columns for short rows,
+    8 192 at d = 960) whose exact lists are merged wave by wave: sampled rows (chunk edges included)
+    against the oracle's exact top-M over the whole segment."""
     rng = np.random.default_rng(70)
-    N, M = 70000, 16
-    X = mixture(rng, N, 8, 40, 0.2)
+    X = mixture(rng, N, d, 40, 0.2)
     mem = np.arange(N, dtype=np.int32)
     off = np.array([0, N], np.int64)
     gi, gd = gta.bucket_knn(dev(X), dev(mem), dev(off), M)
     gi, gd = host(gi), host(gd)
-    rows = np.concatenate([rng.choice(N, 200, replace=False), [0, 1, 65535, 65536, 65537, N - 1]])
+    rows = np.concatenate([rng.choice(N, 200, replace=False), [0, 1, N - 1] + edges])
     ri = np.empty((len(rows), M), np.int32)
     rd = np.empty((len(rows), M), np.float32)
     allc = np.arange(N)
