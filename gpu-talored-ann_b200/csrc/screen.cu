@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
     const WorkItem w = p.work[blockIdx.x];
     const int n_ct = (w.b_rows + kSTile - 1) / kSTile;
     // the column tile of the rows themselves first (clamped into the item's columns)
-    const int t0 = w.has_self ? max(0, min(n_ct - 1, w.self_col0 / kSTile)) : 0;
+    const int t0 = (w.has_self & 1) ? max(0, min(n_ct - 1, w.self_col0 / kSTile)) : 0;
     const int S = p.stages;
     uint32_t* buf = reinterpret_cast<uint32_t*>(smem_raw + p.buf_off);
     float* pn_s = reinterpret_cast<float*>(smem_raw + p.pn_off);
@@ -465,7 +465,8 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
             }
         };
         // the row's own column, when it lies in this item's columns
-        const int self_col = (w.has_self && w.self_col0 + r >= 0 && w.self_col0 + r < w.b_rows) ? w.self_col0 + r : -1;
+        const int self_col =
+            ((w.has_self & 1) && w.self_col0 + r >= 0 && w.self_col0 + r < w.b_rows) ? w.self_col0 + r : -1;
         const int64_t irow = static_cast<int64_t>(w.item_row0) + r;
         const int self_ct = self_col >= 0 ? self_col / kSTile : -1;
         const int self_c = (self_col % kSTile) >> 4;
@@ -674,6 +675,12 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
     }
 }
 
+__global__ void fill_inf_kernel(float* __restrict__ p, int64_t n)
+{
+    const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) p[i] = INFINITY;
+}
+
 // ---- operand rows: scaled fp16 parts ---------------------------------------------------
 // One warp per pool row (f32, pitch dp): out row j holds its hi part (d16 fp16, zero past d) and,
 // with two parts, its lo part after d16 elements.
@@ -781,6 +788,7 @@ struct RerankX {
     int64_t n_rows;
     unsigned long long* stats;  // optional: [exact candidates, rows rescanned, rows]
     const float* seed;          // as ScreenArgs::seed (work items with pad2 >= 0)
+    float* seed_out;            // the same array: pilot items write their rows' bounds into it
     int2* rescan;               // [item rows] (item row, work item) of the rows whose columns are rescanned
     unsigned* n_rescan;         // device counter of those rows
 };
@@ -827,15 +835,19 @@ __global__ void __launch_bounds__(kRrWarps * 32, 4) rerank_kernel(const RerankX 
         const uint32_t code = key >> p.col_bits;
         return code == 0u ? -INFINITY : code_value(code - 1u, code_b) * inv_s2;
     };
-    // a seeded chunk (pad2 >= 0) writes its list compactly: merge_step_kernel reads it
-    const bool compact = w.pad2 >= 0 && static_cast<int64_t>(w.item_row0) >= p.n_rows;
+    // has_self bit 1: a chunk k > 0 list, written compactly (merge_step_kernel reads it); bit 2: a
+    // pilot item, which only bounds its rows' M-th distance (seed_out[pad2 + r])
+    const bool compact = (w.has_self & 2) != 0;
+    const bool pilot = (w.has_self & 4) != 0;
     for (int r = warp; r < w.a_rows; r += kRrWarps) {
         const int64_t arow = static_cast<int64_t>(w.a_row0) + r;
         const int64_t irow = static_cast<int64_t>(w.item_row0) + r;
         const int nv = p.cand_n[irow];
         if (nv == 0) {  // nothing admitted: an empty list
-            if (p.stats && lane == 0) atomicAdd(&p.stats[2], 1ull);
-            write_list(p, irow, keys, 0, lane, compact);
+            if (!pilot) {
+                if (p.stats && lane == 0) atomicAdd(&p.stats[2], 1ull);
+                write_list(p, irow, keys, 0, lane, compact);
+            }
             __syncwarp();
             continue;
         }
@@ -862,6 +874,13 @@ __global__ void __launch_bounds__(kRrWarps * 32, 4) rerank_kernel(const RerankX 
         // 1. the first M keys: their largest exact distance bounds the row's exact M-th
         const int n1 = nv < p.m_out ? nv : p.m_out;
         const float e_m = exact_range(0, n1);
+        if (pilot) {
+            // m_out distinct columns of the row's bucket at exact distances <= e_m: the row's exact
+            // M-th distance over the whole bucket is at most e_m
+            if (lane == 0 && n1 == p.m_out) p.seed_out[static_cast<int64_t>(w.pad2) + r] = e_m;
+            __syncwarp();
+            continue;
+        }
         int n_tot = n1;
         bool rescan = false;
         if (nv > n1) {
@@ -928,7 +947,7 @@ __global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p)
         const WorkItem w = p.work[e.y];
         const int r = static_cast<int>(irow - w.item_row0);
         const int64_t arow = static_cast<int64_t>(w.a_row0) + r;
-        const int self = w.has_self ? w.self_col0 + r : -1;  // outside [0, b_rows): no column is skipped
+        const int self = (w.has_self & 1) ? w.self_col0 + r : -1;  // outside [0, b_rows): no column is skipped
         __syncthreads();
         for (int j = threadIdx.x; j < p.dp; j += blockDim.x) q_s[j] = p.pool[arow * p.dp + j];
         for (int j = lane; j < kRrKeys; j += 32) keys[j] = ~0ull;
@@ -972,7 +991,7 @@ struct ChunkSeg {
     int32_t nch, pad;
 };
 
-// k = 0: seeds from the chunk-0 lists; k > 0: chunk k merged into the running list (by
+// k = 0: seeds tightened by the chunk-0 lists; k > 0: chunk k merged into the running list (by
 // (distance, id)), then the seed (nothing to do for an empty chunk list); k < 0: the running
 // lists written to the rows' outputs.
 // One warp per row of the chunked segments.
@@ -1052,9 +1071,9 @@ __global__ void __launch_bounds__(kRrWarps * 32)
         }
         __syncwarp();
     }
-    if (lane == 0) {
+    if (lane == 0) {  // the running list's m_out-th distance tightens the row's seed (the pilot's bound)
         const bool full = ext_ids[run * m_out + m_out - 1] >= 0;
-        seeds[j] = full ? ext_dists[run * m_out + m_out - 1] : INFINITY;
+        if (full) seeds[j] = fminf(seeds[j], ext_dists[run * m_out + m_out - 1]);
     }
 }
 
@@ -1148,6 +1167,9 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     std::vector<std::vector<WorkItem>> waves(1);
     std::vector<double> wave_flops(1, 0.0);
     std::vector<ChunkSeg> chunked;
+    std::vector<WorkItem> pilot;  // seeds of the chunked rows (one item per row tile)
+    double pilot_flops = 0.0;
+    constexpr int64_t kPilot = 4096;
     int64_t ext_rows = 0, chunked_rows = 0;
     GTA_REQUIRE((pr.seg_r0.empty() && pr.seg_r1.empty()) ||
                     (pr.seg_r0.size() == pr.seg_lo.size() && pr.seg_r1.size() == pr.seg_lo.size()),
@@ -1176,14 +1198,26 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
             waves.resize(static_cast<size_t>(nch));
             wave_flops.resize(static_cast<size_t>(nch), 0.0);
         }
+        // the pilot: each row tile against a window of kPilot columns around its own tile (rows
+        // of a bucket are grouped by their other bucket, so the window holds points of the same
+        // region); the exact M-th distance over its first M candidates seeds every chunk
+        const int64_t W = std::min<int64_t>(kPilot, nb);
+        for (int64_t t = r0; t < r1; t += 128) {
+            const int64_t ws = std::max<int64_t>(0, std::min<int64_t>(t + 64 - W / 2, nb - W));
+            pilot.push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, r1 - t)),
+                                     static_cast<int32_t>(lo + ws), static_cast<int32_t>(W),
+                                     static_cast<int32_t>(t - ws), static_cast<int32_t>(base + nr + (t - r0)), 1,
+                                     static_cast<int32_t>(chunked_rows + (t - r0))});
+        }
+        pilot_flops += 2.0 * static_cast<double>(nr) * static_cast<double>(W) * pr.d;
         for (int k = 0; k < nch; ++k) {
             const int64_t c0 = k * kChunk, cn = std::min<int64_t>(kChunk, nb - c0);
             for (int64_t t = r0; t < r1; t += 128)
                 waves[static_cast<size_t>(k)].push_back(
                     WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, r1 - t)),
                              static_cast<int32_t>(lo + c0), static_cast<int32_t>(cn), static_cast<int32_t>(t - c0),
-                             static_cast<int32_t>(base + (k == 0 ? 0 : nr) + (t - r0)), 1,
-                             k == 0 ? -1 : static_cast<int32_t>(chunked_rows + (t - r0))});
+                             static_cast<int32_t>(base + (k == 0 ? 0 : nr) + (t - r0)), k == 0 ? 1 : 3,
+                             static_cast<int32_t>(chunked_rows + (t - r0))});
             wave_flops[static_cast<size_t>(k)] += 2.0 * static_cast<double>(nr) * static_cast<double>(cn) * pr.d;
         }
         ext_rows += 2 * nr;
@@ -1297,15 +1331,30 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     GTA_CUDA(cudaGetDevice(&dev));
     GTA_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
     const unsigned merge_grid = static_cast<unsigned>((chunked_rows + kRrWarps - 1) / kRrWarps);
-    for (size_t k = 0; k < waves.size(); ++k) {
-        const std::vector<WorkItem>& items = waves[k];
+    r.seed_out = seeds.get();
+    if (chunked_rows > 0) {
+        fill_inf_kernel<<<static_cast<unsigned>((chunked_rows + 255) / 256), 256, 0, st>>>(seeds.get(), chunked_rows);
+        count_launches(1);
+        GTA_CUDA(cudaGetLastError());
+    }
+    // wave -1: the pilot (unseeded screen of the windows, then the bound of each row)
+    for (size_t k = 0; k < waves.size() + (pilot.empty() ? 0 : 1); ++k) {
+        const bool is_pilot = !pilot.empty() && k == 0;
+        const size_t wk = pilot.empty() ? k : k - 1;
+        const std::vector<WorkItem>& items = is_pilot ? pilot : waves[wk];
         if (items.empty()) continue;
         DevBuf<WorkItem> work(items.size(), st);
         // pageable sources: each copy is staged before cudaMemcpyAsync returns
         GTA_CUDA(cudaMemcpyAsync(work.get(), items.data(), sizeof(WorkItem) * items.size(), cudaMemcpyHostToDevice, st));
         a.work = work.get();
+        if (is_pilot) {  // the screen's items are unseeded; the rerank groups carry the seed slots
+            std::vector<WorkItem> unseeded(items);
+            for (WorkItem& it : unseeded) it.pad2 = -1;
+            GTA_CUDA(cudaMemcpyAsync(work.get(), unseeded.data(), sizeof(WorkItem) * unseeded.size(),
+                                     cudaMemcpyHostToDevice, st));
+        }
         {
-            ProfScope prof(pr.prof_name, wave_flops[k], st);
+            ProfScope prof(is_pilot ? "screen_pilot" : pr.prof_name, is_pilot ? pilot_flops : wave_flops[wk], st);
             a.stats = prof.counters(8);
             const int n_work = static_cast<int>(items.size());
             if (L == 128) {
@@ -1324,18 +1373,20 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         for (const WorkItem& it : items)
             for (int g = 0; g < it.a_rows; g += kRrRows)
                 groups.push_back(WorkItem{it.a_row0 + g, std::min(kRrRows, it.a_rows - g), it.b_row0, it.b_rows,
-                                          it.self_col0 + g, it.item_row0 + g, it.has_self, it.pad2 >= 0 ? it.pad2 + g : -1});
+                                          it.self_col0 + g, it.item_row0 + g, it.has_self | (is_pilot ? 4 : 0),
+                                          it.pad2 >= 0 ? it.pad2 + g : -1});
         DevBuf<WorkItem> gwork(groups.size(), st);
         GTA_CUDA(cudaMemcpyAsync(gwork.get(), groups.data(), sizeof(WorkItem) * groups.size(), cudaMemcpyHostToDevice, st));
         r.work = gwork.get();
         GTA_CUDA(cudaMemsetAsync(n_rescan.get(), 0, sizeof(unsigned), st));
         {
-            ProfScope prof("rerank", 0.0, st);
+            ProfScope prof(is_pilot ? "rerank_pilot" : "rerank", 0.0, st);
             r.stats = prof.counters(8);
             rerank_kernel<<<static_cast<unsigned>(groups.size()), kRrWarps * 32, smem_rr, st>>>(r);
             count_launches(1);
             GTA_CUDA(cudaGetLastError());
         }
+        if (is_pilot) continue;  // the pilot writes no lists: nothing to rescan or merge
         {
             // the deferred whole-segment rescans: persistent CTAs over the device-side list
             ProfScope prof("rescan", 0.0, st);
@@ -1347,7 +1398,7 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
             // chunk k into the running lists (k = 0: the seeds of chunk 0's lists)
             ProfScope prof("merge_chunks", 24.0 * pr.m_out * static_cast<double>(chunked_rows), st);
             merge_step_kernel<<<merge_grid, kRrWarps * 32, 0, st>>>(segs.get(), static_cast<int>(chunked.size()),
-                                                                    chunked_rows, static_cast<int>(k), ext_ids.get(),
+                                                                    chunked_rows, static_cast<int>(wk), ext_ids.get(),
                                                                     ext_dists.get(), pr.m_out, seeds.get(), pr.out_ids,
                                                                     pr.out_dists);
             count_launches(1);
