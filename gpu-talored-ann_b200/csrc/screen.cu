@@ -266,16 +266,28 @@ __device__ __forceinline__ void tmem_ld_wait_2x16(uint32_t (&a)[16], uint32_t (&
 // main accumulator's rounding grows with d products instead of 3 d; the epilogue adds the two.
 // Both halves of one tile's accumulator pair fill the 256 columns, so the tile is not double
 // buffered (the MMA of the next tile waits until the epilogue holds the last slice in registers).
-template <int kL, bool kSplit, bool kCorr>
-__global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_constant__ CUtensorMap tm, const ScreenArgs p)
+//
+// kPair (a cluster of two CTAs on two SMs, kCorr only): the pair screens 256 A rows (each CTA its
+// own item of 128) against the same column tiles.  Each CTA loads its A rows and half of every B
+// tile (64 columns); the first CTA's thread issues two-SM MMAs (M = 256) that read both CTAs'
+// shared memory and write both CTAs' TMEM, so B crosses L2 and shared memory once per pair.  The
+// TMA of both CTAs completes on the first CTA's stage barriers (which expect the pair's bytes); the
+// MMA commits arrive on the barriers of both CTAs; the second CTA's epilogue releases the
+// accumulator on the first CTA's barrier.
+template <int kL, bool kSplit, bool kCorr, bool kPair = false>
+__global__ void __launch_bounds__(kSThreads, 1)
+    screen_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tmb, const ScreenArgs p)
 {
     static_assert(!kCorr || kSplit, "the correction accumulator holds the lo products");
+    static_assert(!kPair || kCorr, "CTA pairs run the corrected split screen");
     constexpr int kParts = kSplit ? 2 : 1;
     // operand chunks of 64 fp16 (128-byte swizzle) or, kCorr, 32 fp16 (64-byte swizzle: smaller
     // stages leave room for the drained tile)
     constexpr int kChunkElems = kCorr ? 32 : 64;
+    constexpr int kBRows = kPair ? kSTile / 2 : kSTile;  // B rows this CTA loads per column tile
     constexpr uint32_t kPartChunk = 128u * static_cast<uint32_t>(kChunkElems) * 2u;
-    constexpr uint32_t kStageBytes = 2u * kParts * kPartChunk;  // A parts then B parts
+    constexpr uint32_t kPartChunkB = static_cast<uint32_t>(kBRows) * static_cast<uint32_t>(kChunkElems) * 2u;
+    constexpr uint32_t kStageBytes = kParts * (kPartChunk + kPartChunkB);  // A parts then B parts
     constexpr uint32_t kTmemCols = 512u;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t base = smem_u32(smem_raw);
@@ -284,10 +296,14 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
         return;
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = kPair ? cluster_ctarank() : 0u;
+    const bool leader = rank == 0u;
     const WorkItem w = p.work[blockIdx.x];
+    // the pair's column order follows its first item (both CTAs sweep the same tiles)
+    const WorkItem w0 = kPair ? p.work[blockIdx.x & ~1u] : w;
     const int n_ct = (w.b_rows + kSTile - 1) / kSTile;
     // the column tile of the rows themselves first (clamped into the item's columns)
-    const int t0 = (w.has_self & 1) ? max(0, min(n_ct - 1, w.self_col0 / kSTile)) : 0;
+    const int t0 = (w0.has_self & 1) ? max(0, min(n_ct - 1, w0.self_col0 / kSTile)) : 0;
     const int S = p.stages;
     uint32_t* buf = reinterpret_cast<uint32_t*>(smem_raw + p.buf_off);
     float* pn_s = reinterpret_cast<float*>(smem_raw + p.pn_off);
@@ -307,18 +323,24 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(S_ACC_FULL(b), 1);
-            mbar_init(S_ACC_EMPTY(b), 4);
+            mbar_init(S_ACC_EMPTY(b), kPair ? 8 : 4);  // the epilogue warps of the pair
         }
         mbar_init(mma_done, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
     if (warp == 1) {
-        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
-        tmem_relinquish();
+        if constexpr (kPair) {
+            tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+            tmem_relinquish_pair();
+        } else {
+            tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+            tmem_relinquish();
+        }
     }
     tc_fence_before();
     __syncthreads();
+    if constexpr (kPair) cluster_sync();  // both CTAs' barriers exist before either signals the other
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -338,24 +360,53 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
                         break;
                     }
                     const uint32_t dst = base + static_cast<uint32_t>(s) * kStageBytes;
-                    mbar_arrive_expect_tx(S_FULL(s), kStageBytes);
+                    if constexpr (kPair) {
+                        // the pair's bytes complete on the first CTA's barrier
+                        const uint32_t fb = mapa_shared(S_FULL(s), 0u);
+                        if (leader) mbar_arrive_expect_tx(S_FULL(s), 2u * kStageBytes);
 #pragma unroll
-                    for (int q = 0; q < kParts; ++q) {
-                        const int x = q * p.part_stride + kc * kChunkElems;
-                        tma_load_2d(dst + static_cast<uint32_t>(q) * kPartChunk, &tm, S_FULL(s), x, w.a_row0);
-                        tma_load_2d(dst + static_cast<uint32_t>(kParts + q) * kPartChunk, &tm, S_FULL(s), x,
-                                    w.b_row0 + ct * kSTile);
+                        for (int q = 0; q < kParts; ++q) {
+                            const int x = q * p.part_stride + kc * kChunkElems;
+                            tma_load_2d_pair(dst + static_cast<uint32_t>(q) * kPartChunk, &tm, fb, x, w.a_row0);
+                            tma_load_2d_pair(dst + kParts * kPartChunk + static_cast<uint32_t>(q) * kPartChunkB, &tmb,
+                                             fb, x, w.b_row0 + ct * kSTile + static_cast<int>(rank) * kBRows);
+                        }
+                    } else {
+                        mbar_arrive_expect_tx(S_FULL(s), kStageBytes);
+#pragma unroll
+                        for (int q = 0; q < kParts; ++q) {
+                            const int x = q * p.part_stride + kc * kChunkElems;
+                            tma_load_2d(dst + static_cast<uint32_t>(q) * kPartChunk, &tm, S_FULL(s), x, w.a_row0);
+                            tma_load_2d(dst + kParts * kPartChunk + static_cast<uint32_t>(q) * kPartChunkB, &tm,
+                                        S_FULL(s), x, w.b_row0 + ct * kSTile);
+                        }
                     }
                     ++it;
                 }
             }
-            // every issued copy lands before the CTA can exit
-            for (int j = max(0, it - S); j < it; ++j) drain_wait(S_FULL(j % S), static_cast<uint32_t>(j / S) & 1u, p.err);
+            // every issued copy lands before the CTA can exit (a pair's copies all complete on the
+            // first CTA's barriers; the second CTA leaves only after the closing cluster barrier)
+            if (leader)
+                for (int j = max(0, it - S); j < it; ++j)
+                    drain_wait(S_FULL(j % S), static_cast<uint32_t>(j / S) & 1u, p.err);
         }
     } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
-        if (lane == 0) {
-            const uint32_t idesc = make_idesc(0u, kSTile, kSTile);  // fp16 x fp16 -> fp32
+        // ------------------------------------------------------------ MMA issuer (a pair: its first CTA)
+        if (lane == 0 && leader) {
+            const uint32_t idesc = make_idesc(0u, kPair ? 2 * kSTile : kSTile, kSTile);  // fp16 x fp16 -> fp32
+            // the pair's commits: this CTA's barrier and the same barrier of the second CTA
+            auto commit = [&](uint32_t bar) {
+                if constexpr (kPair) {
+                    umma_commit_pair(mapa_shared(bar, 0u));
+                    umma_commit_pair(mapa_shared(bar, 1u));
+                } else {
+                    umma_commit(bar);
+                }
+            };
+            auto mma = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
+                if constexpr (kPair) umma_pair(d, a, b, idesc, acc);
+                else umma<false>(d, a, b, idesc, acc);
+            };
             bool ok = true;
             long long wait_acc = 0, wait_full = 0;
             int it = 0;
@@ -382,22 +433,22 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
                     const uint64_t ah = desc(sa), bh = desc(sa + kParts * kPartChunk);
 #pragma unroll
                     for (int kk = 0; kk < kChunkElems / 16; ++kk) {  // 16 fp16 of K per MMA
-                        umma<false>(d_tmem, ah + 2ull * kk, bh + 2ull * kk, idesc, (kc | kk) != 0 ? 1u : 0u);
+                        mma(d_tmem, ah + 2ull * kk, bh + 2ull * kk, (kc | kk) != 0 ? 1u : 0u);
                         if constexpr (kSplit) {
-                            const uint64_t al = desc(sa + kPartChunk), bl = desc(sa + 3u * kPartChunk);
+                            const uint64_t al = desc(sa + kPartChunk), bl = desc(sa + kParts * kPartChunk + kPartChunkB);
                             const uint32_t c_tmem = kCorr ? tmem_base + static_cast<uint32_t>(kSTile) : d_tmem;
-                            umma<false>(c_tmem, ah + 2ull * kk, bl + 2ull * kk, idesc,
-                                        (!kCorr || (kc | kk) != 0) ? 1u : 0u);
-                            umma<false>(c_tmem, al + 2ull * kk, bh + 2ull * kk, idesc, 1u);
+                            mma(c_tmem, ah + 2ull * kk, bl + 2ull * kk, (!kCorr || (kc | kk) != 0) ? 1u : 0u);
+                            mma(c_tmem, al + 2ull * kk, bh + 2ull * kk, 1u);
                         }
                     }
-                    umma_commit(S_EMPTY(s));
+                    commit(S_EMPTY(s));
                     ++it;
                 }
                 if (!ok) break;
-                umma_commit(S_ACC_FULL(b));
+                commit(S_ACC_FULL(b));
             }
-            umma_commit(mma_done);
+            if constexpr (kPair) umma_commit_pair(mapa_shared(mma_done, 0u));
+            else umma_commit(mma_done);
             drain_wait(mma_done, 0, p.err);
             if (p.stats) {
                 atomicAdd(&p.stats[6], static_cast<unsigned long long>(wait_acc));
@@ -571,7 +622,10 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
             auto release_acc = [&]() {
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(S_ACC_EMPTY(b));
+                if (lane == 0) {
+                    if (leader) mbar_arrive(S_ACC_EMPTY(b));
+                    else mbar_arrive_cluster(mapa_shared(S_ACC_EMPTY(b), 0u));  // the pair's MMA waits there
+                }
             };
             __syncwarp();
             ld_slice(0, va, ca);
@@ -669,9 +723,11 @@ __global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_const
 #undef S_ACC_EMPTY
     tc_fence_before();
     __syncthreads();
+    if constexpr (kPair) cluster_sync();  // the pair's MMAs and copies are done with both CTAs
     if (warp == 1) {
         tc_fence_after();
-        tmem_dealloc(tmem_base, kTmemCols);
+        if constexpr (kPair) tmem_dealloc_pair(tmem_base, kTmemCols);
+        else tmem_dealloc(tmem_base, kTmemCols);
     }
 }
 
@@ -704,46 +760,74 @@ __global__ void split_rows_kernel(const float* __restrict__ pool, int dp, int d,
 // ---- exact rerank ------------------------------------------------------------------------
 // The exact distances run on a bucket-contiguous f32 copy of the pool rows (pitch dp, a
 // multiple of 32, zero past d: the extra terms add +0 to the chain and change nothing; rows
-// 128-byte aligned).  A warp evaluates 32 candidates at a time, one per lane: each lane streams
-// its candidate's row with 16-byte loads (eight in flight, the next 32 floats loading while these
-// are consumed) and continues its ascending fmaf chain against the query row, read from shared
-// memory as broadcasts.
+// 128-byte aligned).  A warp evaluates 32 candidates at a time, one per lane: 32-dimension
+// chunks of the 32 candidate rows are staged in shared memory by cp.async (each 128-byte row
+// segment one transaction; two chunks in flight), and every lane reads its own row from there
+// (16-byte loads, rows 36 floats apart: conflict-free) and continues its ascending fmaf chain
+// against the query row (shared memory, broadcast reads).
 constexpr int kRrWarps = 4;
 constexpr int kRrKeys = 512;
-constexpr int kRrRows = 8;        // A rows per rerank work item (few rows in flight per bucket)
-constexpr int kChainVec = 8;      // 16-byte loads in flight per lane
+constexpr int kRrRows = 8;          // A rows per rerank work item (few rows in flight per bucket)
+constexpr int kChainStride = 36;    // floats between staged rows
+constexpr int kChainStage = 32 * kChainStride;          // floats of one staged chunk
+constexpr int kChainBufBytes = 2 * kChainStage * 4;     // per warp: two chunks
 
-// exact fp32 chain (ascending dimensions) of the query row q_s (shared memory, dp floats, 16-byte
-// aligned) against pool row `brow` of this lane (-1: none, the result is ignored)
-__device__ __forceinline__ float lane_chain(const float* __restrict__ q_s, const float* __restrict__ pool, int dp,
-                                            int64_t brow)
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint32_t src_bytes)
 {
-    const float4* r4 = reinterpret_cast<const float4*>(pool + (brow >= 0 ? brow : 0) * static_cast<int64_t>(dp));
-    const float4* q4 = reinterpret_cast<const float4*>(q_s);
-    const int n4 = dp >> 2;  // a multiple of kChainVec
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// exact fp32 chain (ascending dimensions) of the query row q_s (shared memory, dp floats) against
+// pool row `brow` of this lane (-1: none, the result is ignored); warp-collective, buf: this
+// warp's kChainBufBytes of shared memory
+__device__ __forceinline__ float warp_chain(const float* __restrict__ q_s, const float* __restrict__ pool, int dp,
+                                            int64_t brow, float* __restrict__ buf, int lane)
+{
+    // per chunk this lane copies 16 bytes of rows 4 i + lane / 8 (i = 0..7), piece lane % 8
+    const float* src[8];
+    uint32_t nbytes[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int64_t br = __shfl_sync(0xffffffffu, brow, 4 * i + (lane >> 3));
+        src[i] = pool + (br >= 0 ? br : 0) * static_cast<int64_t>(dp) + (lane & 7) * 4;
+        nbytes[i] = br >= 0 ? 16u : 0u;  // no candidate: zeros
+    }
+    const uint32_t dst0 = smem_u32(buf) + static_cast<uint32_t>(((lane >> 3) * kChainStride + (lane & 7) * 4) * 4);
+    auto issue = [&](int c) {
+        const uint32_t d = dst0 + static_cast<uint32_t>((c & 1) * kChainStage * 4);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            cp_async16(d + static_cast<uint32_t>(i * 4 * kChainStride * 4), src[i] + c * 32, nbytes[i]);
+        cp_async_commit();
+    };
+    const int nc = dp >> 5;
+    issue(0);
+    if (nc > 1) issue(1);
     float acc = 0.0f;
-    float4 cur[kChainVec], nxt[kChainVec];
+    for (int c = 0; c < nc; ++c) {
+        if (c + 1 < nc) cp_async_wait<1>();
+        else cp_async_wait<0>();
+        __syncwarp();
+        const float4* mine = reinterpret_cast<const float4*>(buf + (c & 1) * kChainStage + lane * kChainStride);
+        const float4* q4 = reinterpret_cast<const float4*>(q_s + c * 32);
 #pragma unroll
-    for (int b = 0; b < kChainVec; ++b) cur[b] = __ldg(r4 + b);
-    for (int i = 0; i < n4; i += kChainVec) {
-        if (i + kChainVec < n4) {
-#pragma unroll
-            for (int b = 0; b < kChainVec; ++b) nxt[b] = __ldg(r4 + i + kChainVec + b);
+        for (int b = 0; b < 8; ++b) {
+            const float4 x = mine[b];
+            const float4 q = q4[b];
+            float t = q.x - x.x;
+            acc = fmaf(t, t, acc);
+            t = q.y - x.y;
+            acc = fmaf(t, t, acc);
+            t = q.z - x.z;
+            acc = fmaf(t, t, acc);
+            t = q.w - x.w;
+            acc = fmaf(t, t, acc);
         }
-#pragma unroll
-        for (int b = 0; b < kChainVec; ++b) {
-            const float4 q = q4[i + b];
-            float t = q.x - cur[b].x;
-            acc = fmaf(t, t, acc);
-            t = q.y - cur[b].y;
-            acc = fmaf(t, t, acc);
-            t = q.z - cur[b].z;
-            acc = fmaf(t, t, acc);
-            t = q.w - cur[b].w;
-            acc = fmaf(t, t, acc);
-        }
-#pragma unroll
-        for (int b = 0; b < kChainVec; ++b) cur[b] = nxt[b];
+        __syncwarp();
+        if (c + 2 < nc) issue(c + 2);
     }
     return acc;
 }
@@ -818,12 +902,13 @@ __device__ __forceinline__ void write_list(const RerankX& p, int64_t irow, const
     }
 }
 
-__global__ void __launch_bounds__(kRrWarps * 32, 4) rerank_kernel(const RerankX p)
+__global__ void __launch_bounds__(kRrWarps * 32) rerank_kernel(const RerankX p)
 {
     extern __shared__ uint8_t sm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t* keys = reinterpret_cast<uint64_t*>(sm) + warp * kRrKeys;
-    float* q_s = reinterpret_cast<float*>(sm + kRrWarps * kRrKeys * sizeof(uint64_t)) + warp * p.dp;
+    float* cbuf = reinterpret_cast<float*>(sm + kRrWarps * kRrKeys * sizeof(uint64_t) + warp * kChainBufBytes);
+    float* q_s = reinterpret_cast<float*>(sm + kRrWarps * (kRrKeys * sizeof(uint64_t) + kChainBufBytes)) + warp * p.dp;
     const WorkItem w = p.work[blockIdx.x];
     const float bm = *p.maxnorm;
     const float sc = screen_scale(bm);
@@ -861,7 +946,7 @@ __global__ void __launch_bounds__(kRrWarps * 32, 4) rerank_kernel(const RerankX 
                 const int j = j0 + lane;
                 const int c = j < j_hi ? static_cast<int>(kl[j] & col_mask) : -1;
                 const int64_t brow = c >= 0 ? static_cast<int64_t>(w.b_row0) + c : -1;
-                const float dd = lane_chain(q_s, p.pool, p.dp, brow);
+                const float dd = warp_chain(q_s, p.pool, p.dp, brow, cbuf, lane);
                 if (c >= 0) {
                     keys[j] = (static_cast<uint64_t>(f2key(dd)) << 32) | static_cast<uint32_t>(p.gid[brow]);
                     mx = fmaxf(mx, dd);
@@ -939,7 +1024,8 @@ __global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p)
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t* all = reinterpret_cast<uint64_t*>(sm);
     uint64_t* keys = all + warp * kRrKeys;
-    float* q_s = reinterpret_cast<float*>(sm + kRsWarps * kRrKeys * sizeof(uint64_t));
+    float* cbuf = reinterpret_cast<float*>(sm + kRsWarps * kRrKeys * sizeof(uint64_t) + warp * kChainBufBytes);
+    float* q_s = reinterpret_cast<float*>(sm + kRsWarps * (kRrKeys * sizeof(uint64_t) + kChainBufBytes));
     const unsigned n = *p.n_rescan;
     for (unsigned i = blockIdx.x; i < n; i += gridDim.x) {
         const int2 e = p.rescan[i];
@@ -958,7 +1044,7 @@ __global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p)
                 const int c = c0 + j + lane;
                 const bool ok = c < w.b_rows && c != self;
                 const int64_t brow = ok ? static_cast<int64_t>(w.b_row0) + c : -1;
-                const float dd = lane_chain(q_s, p.pool, p.dp, brow);
+                const float dd = warp_chain(q_s, p.pool, p.dp, brow, cbuf, lane);
                 keys[kRrKeys / 2 + j + lane] =
                     ok ? (static_cast<uint64_t>(f2key(dd)) << 32) | static_cast<uint32_t>(p.gid[brow]) : ~0ull;
             }
@@ -1082,10 +1168,11 @@ struct ScreenPlan {
     uint32_t buf_off = 0, pn_off = 0, stg_off = 0, bar_off = 0, total = 0;
 };
 
-bool screen_plan(bool split, bool corr, ScreenPlan& pl)
+bool screen_plan(bool split, bool corr, bool pair, ScreenPlan& pl)
 {
-    // operand chunk: 64 fp16 per row (corr: 32) of each part of A and B
-    const uint32_t stage_bytes = 2u * (split ? 2u : 1u) * (corr ? kSChunk / 2u : kSChunk);
+    // operand chunk: 64 fp16 per row (corr: 32) of each part of A and B (a pair: half of B)
+    const uint32_t chunk = corr ? kSChunk / 2u : kSChunk;
+    const uint32_t stage_bytes = (split ? 2u : 1u) * (chunk + (pair ? chunk / 2u : chunk));
     for (int S = 6; S >= 2; --S) {
         ScreenPlan t;
         t.stages = S;
@@ -1127,11 +1214,60 @@ EncodeFnS screen_encode()
 template <int kL, bool kSplit, bool kCorr = false>
 void launch_screen(const CUtensorMap& tm, const ScreenArgs& a, int n_work, uint32_t smem, cudaStream_t st)
 {
-    auto fn = screen_kernel<kL, kSplit, kCorr>;
+    auto fn = screen_kernel<kL, kSplit, kCorr, false>;
     GTA_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    fn<<<n_work, kSThreads, smem, st>>>(tm, a);
+    fn<<<n_work, kSThreads, smem, st>>>(tm, tm, a);
     count_launches(1);
     GTA_CUDA(cudaGetLastError());
+}
+
+// CTA pairs: clusters of two, n_work (even) items, items 2 i and 2 i + 1 with the same columns
+template <int kL>
+void launch_screen_pair(const CUtensorMap& tm, const CUtensorMap& tmb, const ScreenArgs& a, int n_work, uint32_t smem,
+                        cudaStream_t st)
+{
+    auto fn = screen_kernel<kL, true, true, true>;
+    GTA_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(n_work));
+    cfg.blockDim = dim3(kSThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    GTA_CUDA(cudaLaunchKernelEx(&cfg, fn, tm, tmb, a));
+    count_launches(1);
+    GTA_CUDA(cudaGetLastError());
+}
+
+// The items of a wave as CTA pairs: consecutive items over the same columns share a pair; an item
+// left alone is paired with a copy that has no rows (it loads the second half of the columns).
+std::vector<WorkItem> pair_items(const std::vector<WorkItem>& items)
+{
+    std::vector<WorkItem> out;
+    out.reserve(items.size() + items.size() / 2 + 1);
+    for (size_t i = 0; i < items.size();) {
+        const WorkItem& a = items[i];
+        if (i + 1 < items.size() && items[i + 1].b_row0 == a.b_row0 && items[i + 1].b_rows == a.b_rows) {
+            out.push_back(a);
+            out.push_back(items[i + 1]);
+            i += 2;
+        } else {
+            WorkItem e = a;
+            e.a_rows = 0;
+            e.has_self = 0;
+            e.pad2 = -1;
+            out.push_back(a);
+            out.push_back(e);
+            i += 1;
+        }
+    }
+    return out;
 }
 
 }  // namespace
@@ -1231,7 +1367,9 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     ScreenPlan pl;
     // long rows: the corrections in their own accumulator (see screen_kernel)
     const bool corr = split && pr.d >= 256;
-    GTA_REQUIRE(screen_plan(split, corr, pl), kInvalid, "screen: shared memory plan failed");
+    // two-SM CTA pairs for the corrected screen: B crosses L2 and shared memory once per 256 rows
+    const bool pair = false;
+    GTA_REQUIRE(screen_plan(split, corr, pair, pl), kInvalid, "screen: shared memory plan failed");
     // the pool's rows as f32 (bucket-contiguous, pitch dp, zero past d) with their exact squared
     // norms, the scale's source (max ||x||) and the scaled fp16 operand rows
     const int dp = (pr.d + 31) / 32 * 32;
@@ -1249,14 +1387,14 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         count_launches(1);
         GTA_CUDA(cudaGetLastError());
     }
-    CUtensorMap tm;
-    {
+    CUtensorMap tm, tmb;  // A tiles (128 rows); a pair's half B tiles (64 rows)
+    for (int m = 0; m < 2; ++m) {
         cuuint64_t dims[2] = {static_cast<cuuint64_t>(pr.parts) * d16, static_cast<cuuint64_t>(pr.n_rows)};
         cuuint64_t strides[1] = {static_cast<cuuint64_t>(pr.parts) * d16 * 2u};
-        cuuint32_t box[2] = {corr ? 32u : 64u, 128u};
+        cuuint32_t box[2] = {corr ? 32u : 64u, m == 0 ? 128u : 64u};
         cuuint32_t estr[2] = {1u, 1u};
-        const CUresult r = screen_encode()(&tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, rows.get(), dims, strides, box, estr,
-                                           CU_TENSOR_MAP_INTERLEAVE_NONE,
+        const CUresult r = screen_encode()(m == 0 ? &tm : &tmb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, rows.get(), dims,
+                                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                                            corr ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         GTA_REQUIRE(r == CUDA_SUCCESS, kCuda, "cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
@@ -1322,8 +1460,8 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     r.seed = seeds.get();
     r.rescan = rescan.get();
     r.n_rescan = n_rescan.get();
-    const size_t smem_rr = kRrWarps * (kRrKeys * sizeof(uint64_t) + static_cast<size_t>(dp) * 4);
-    const size_t smem_rs = kRsWarps * kRrKeys * sizeof(uint64_t) + static_cast<size_t>(dp) * 4;
+    const size_t smem_rr = kRrWarps * (kRrKeys * sizeof(uint64_t) + kChainBufBytes + static_cast<size_t>(dp) * 4);
+    const size_t smem_rs = kRsWarps * (kRrKeys * sizeof(uint64_t) + kChainBufBytes) + static_cast<size_t>(dp) * 4;
     GTA_REQUIRE(smem_rr <= kSSmemMax && smem_rs <= kSSmemMax, kInvalid, "rerank: dimension too large");
     GTA_CUDA(cudaFuncSetAttribute(rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_rr)));
     GTA_CUDA(cudaFuncSetAttribute(rescan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_rs)));
@@ -1343,26 +1481,28 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         const size_t wk = pilot.empty() ? k : k - 1;
         const std::vector<WorkItem>& items = is_pilot ? pilot : waves[wk];
         if (items.empty()) continue;
-        DevBuf<WorkItem> work(items.size(), st);
+        // the screen's items (the pilot's unseeded: its rerank groups carry the seed slots), as CTA
+        // pairs when the screen runs in pairs
+        std::vector<WorkItem> launch(items);
+        if (is_pilot)
+            for (WorkItem& it : launch) it.pad2 = -1;
+        if (pair) launch = pair_items(launch);
+        DevBuf<WorkItem> work(launch.size(), st);
         // pageable sources: each copy is staged before cudaMemcpyAsync returns
-        GTA_CUDA(cudaMemcpyAsync(work.get(), items.data(), sizeof(WorkItem) * items.size(), cudaMemcpyHostToDevice, st));
+        GTA_CUDA(cudaMemcpyAsync(work.get(), launch.data(), sizeof(WorkItem) * launch.size(), cudaMemcpyHostToDevice, st));
         a.work = work.get();
-        if (is_pilot) {  // the screen's items are unseeded; the rerank groups carry the seed slots
-            std::vector<WorkItem> unseeded(items);
-            for (WorkItem& it : unseeded) it.pad2 = -1;
-            GTA_CUDA(cudaMemcpyAsync(work.get(), unseeded.data(), sizeof(WorkItem) * unseeded.size(),
-                                     cudaMemcpyHostToDevice, st));
-        }
         {
             ProfScope prof(is_pilot ? "screen_pilot" : pr.prof_name, is_pilot ? pilot_flops : wave_flops[wk], st);
             a.stats = prof.counters(8);
-            const int n_work = static_cast<int>(items.size());
+            const int n_work = static_cast<int>(launch.size());
             if (L == 128) {
-                if (corr) launch_screen<128, true, true>(tm, a, n_work, pl.total, st);
+                if (pair) launch_screen_pair<128>(tm, tmb, a, n_work, pl.total, st);
+                else if (corr) launch_screen<128, true, true>(tm, a, n_work, pl.total, st);
                 else if (split) launch_screen<128, true>(tm, a, n_work, pl.total, st);
                 else launch_screen<128, false>(tm, a, n_work, pl.total, st);
             } else {
-                if (corr) launch_screen<256, true, true>(tm, a, n_work, pl.total, st);
+                if (pair) launch_screen_pair<256>(tm, tmb, a, n_work, pl.total, st);
+                else if (corr) launch_screen<256, true, true>(tm, a, n_work, pl.total, st);
                 else if (split) launch_screen<256, true>(tm, a, n_work, pl.total, st);
                 else launch_screen<256, false>(tm, a, n_work, pl.total, st);
             }
