@@ -1339,7 +1339,9 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         // region); the exact M-th distance over its first M candidates seeds every chunk
         const int64_t W = std::min<int64_t>(kPilot, nb);
         for (int64_t t = r0; t < r1; t += 128) {
-            const int64_t ws = std::max<int64_t>(0, std::min<int64_t>(t + 64 - W / 2, nb - W));
+            // centred on the tile pair (t and its neighbour share a window, so a CTA pair shares it)
+            const int64_t tp = r0 + (t - r0) / 256 * 256;
+            const int64_t ws = std::max<int64_t>(0, std::min<int64_t>(tp + 128 - W / 2, nb - W));
             pilot.push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, r1 - t)),
                                      static_cast<int32_t>(lo + ws), static_cast<int32_t>(W),
                                      static_cast<int32_t>(t - ws), static_cast<int32_t>(base + nr + (t - r0)), 1,
@@ -1367,7 +1369,9 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     ScreenPlan pl;
     // long rows: the corrections in their own accumulator (see screen_kernel)
     const bool corr = split && pr.d >= 256;
-    // two-SM CTA pairs for the corrected screen: B crosses L2 and shared memory once per 256 rows
+    // two-SM CTA pairs (B across L2 and shared memory once per 256 rows) are built and pass the
+    // parity tests, but measured slower at C3 (screen 2.60 s against 2.45 s per build: a pair waits
+    // for the slower of its two epilogue drains before the next tile), so the screen runs single CTAs
     const bool pair = false;
     GTA_REQUIRE(screen_plan(split, corr, pair, pl), kInvalid, "screen: shared memory plan failed");
     // the pool's rows as f32 (bucket-contiguous, pitch dp, zero past d) with their exact squared
