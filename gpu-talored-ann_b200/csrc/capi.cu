@@ -15,6 +15,8 @@
 #include <numeric>
 #include <string>
 #include <vector>
+#include <memory>
+#include <unistd.h>
 
 #include "../../include/gta.h"
 #include "gta_internal.h"
@@ -473,6 +475,39 @@ void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* 
     }
 }
 
+// A host dataset the build reads in place (gta_dataset.on_device == 2): the pages are registered
+// (pinned, mapped, read-only) for the call and the kernels read rows through the mapped address
+// over the host link; nothing holds the whole dataset in device memory.
+struct HostRows {
+    const void* dev = nullptr;
+    void* reg = nullptr;  // the registered page range (ours to unregister), or null
+    HostRows(const void* data, size_t bytes)
+    {
+        const long page = sysconf(_SC_PAGESIZE) > 0 ? sysconf(_SC_PAGESIZE) : 4096;
+        const uintptr_t b = reinterpret_cast<uintptr_t>(data) & ~static_cast<uintptr_t>(page - 1);
+        const uintptr_t e = (reinterpret_cast<uintptr_t>(data) + bytes + page - 1) & ~static_cast<uintptr_t>(page - 1);
+        const cudaError_t r = cudaHostRegister(reinterpret_cast<void*>(b), e - b,
+                                               cudaHostRegisterMapped | cudaHostRegisterReadOnly |
+                                                   cudaHostRegisterPortable);
+        if (r == cudaSuccess) {
+            reg = reinterpret_cast<void*>(b);
+        } else {
+            (void)cudaGetLastError();  // already registered (by the caller): its mapping serves
+            GTA_REQUIRE(r == cudaErrorHostMemoryAlreadyRegistered, kCuda,
+                        std::string("cudaHostRegister of the host dataset failed: ") + cudaGetErrorString(r));
+        }
+        void* dp = nullptr;
+        GTA_CUDA(cudaHostGetDevicePointer(&dp, const_cast<void*>(data), 0));
+        dev = dp;
+    }
+    ~HostRows()
+    {
+        if (reg) (void)cudaHostUnregister(reg);
+    }
+    HostRows(const HostRows&) = delete;
+    HostRows& operator=(const HostRows&) = delete;
+};
+
 struct BucketOut {
     int32_t* ids;      // device [N x M]
     float* dists;      // device [N x M]
@@ -501,11 +536,15 @@ void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const
     GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
     ProfScope prof_all("build_bucket_total", 0.0, st);
 
-    // dataset on the device in its own element type
+    // dataset on the device in its own element type, or (on_device 2) read in place from host memory
     DevBuf<uint8_t> xhold;
     const void* X = ds.data;
     const size_t xbytes = static_cast<size_t>(N) * d * elem_size(ds.dtype);
-    if (!ds.on_device) {
+    std::unique_ptr<HostRows> xhost;
+    if (ds.on_device == 2) {
+        xhost = std::make_unique<HostRows>(ds.data, xbytes);
+        X = xhost->dev;
+    } else if (!ds.on_device) {
         xhold = DevBuf<uint8_t>(xbytes, st);
         GTA_CUDA(cudaMemcpyAsync(xhold.get(), ds.data, xbytes, cudaMemcpyHostToDevice, st));
         X = xhold.get();
@@ -685,7 +724,7 @@ void build_bucket_impl(const gta_dataset& ds, const gta_bucket_params& p, const 
     GTA_REQUIRE(ds.data && N >= 2 && M >= 1 && M <= 128, kInvalid, "build_bucket: bad dataset or knn_degree");
     gta_dataset dd = ds;
     DevBuf<uint8_t> xhold;
-    if (!ds.on_device) {  // one upload for all rounds
+    if (ds.on_device == 0) {  // one upload for all rounds (on_device 2: every round reads the host rows)
         const size_t xbytes = static_cast<size_t>(N) * ds.d * elem_size(ds.dtype);
         xhold = DevBuf<uint8_t>(xbytes, st);
         GTA_CUDA(cudaMemcpyAsync(xhold.get(), ds.data, xbytes, cudaMemcpyHostToDevice, st));
@@ -999,6 +1038,8 @@ void build_bucket2_impl(const gta_dataset& ds, const gta_bucket2_params& p, Buck
     GTA_REQUIRE(p.nprobe >= 0 && p.nprobe <= 127 && p.knn_k >= 0 && p.knn_k <= 127 && p.rounds >= 0 &&
                     p.centroid_ratio >= 0.0f && p.centroid_ratio <= 1.0f && (p.assign_rule == 0 || p.assign_rule == 1),
                 kInvalid, "build_bucket2: need 0 <= nprobe, knn_k <= 127, 0 <= centroid_ratio <= 1, assign_rule 0 or 1");
+    GTA_REQUIRE(ds.on_device == 0 || ds.on_device == 1, kInvalid,
+                "build_bucket2: the dataset is a host (0) or device (1) pointer");
     const void* X = ds.data;
     DevBuf<uint8_t> xhold;
     if (!ds.on_device) {
@@ -1358,7 +1399,8 @@ int gta_optimize_knn(const gta_dataset* ds, const int32_t* knn, int64_t n, int32
         GTA_WORKSPACE(stream);
         GTA_REQUIRE(knn && graph && n >= 2 && m >= 2 && m <= 128 && k >= 1 && k <= m && n < (1ll << 31), kInvalid,
                     "gta_optimize_knn: need knn, graph, 2 <= n < 2^31, 1 <= K <= M <= 128");
-        GTA_REQUIRE(!ds || (ds->data && ds->n == n && ds->d >= 1 && (ds->on_device != 0) == (on_device != 0) &&
+        GTA_REQUIRE(!ds || (ds->data && ds->n == n && ds->d >= 1 && (ds->on_device == 0 || ds->on_device == 1) &&
+                            (ds->on_device != 0) == (on_device != 0) &&
                             (ds->dtype == GTA_F32 || ds->dtype == GTA_U8 || ds->dtype == GTA_I8)),
                     kInvalid, "gta_optimize_knn: dataset must match the graph's N and placement");
         cudaStream_t st = S(stream);
@@ -1750,6 +1792,8 @@ int gta_search(const gta_dataset* base, const void* queries, int64_t nq, const u
                     kInvalid, "gta_search: bad argument");
         GTA_REQUIRE(base->dtype == GTA_F32 || base->dtype == GTA_U8 || base->dtype == GTA_I8, kInvalid,
                     "gta_search: bad dtype");
+        GTA_REQUIRE(base->on_device == 0 || base->on_device == 1, kInvalid,
+                    "gta_search: the base is a host (0) or device (1) pointer");
         if (nq == 0) return;
         cudaStream_t st = S(stream);
         const int64_t n = base->n;

@@ -69,9 +69,12 @@ def _empty(shape, dtype, like_dev: bool):
     return np.empty(shape, dtype=dtype)
 
 
-def _dataset(X, metric: str = "l2") -> L.gta_dataset:
+def _dataset(X, metric: str = "l2", host_resident: bool = False) -> L.gta_dataset:
+    if host_resident and (_is_dev(X) or not X.flags["C_CONTIGUOUS"]):
+        raise L.GtaError(L.GTA_EINVAL, "host_resident needs a C-contiguous host array")
     return L.gta_dataset(data=_ptr(X), n=X.shape[0], d=X.shape[1], dtype=_dtype_code(X),
-                         metric=L.GTA_IP if metric == "ip" else L.GTA_L2, on_device=1 if _is_dev(X) else 0)
+                         metric=L.GTA_IP if metric == "ip" else L.GTA_L2,
+                         on_device=2 if host_resident else (1 if _is_dev(X) else 0))
 
 
 def _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, init_centroids, dev, cent_out, top2_out,
@@ -87,7 +90,7 @@ def _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, ini
 # ---------------------------------------------------------------- pipeline
 def build_bucket(X, n_buckets: int, knn_degree: int = 64, kmeans_iters: int = 10, kmeans_sample: int = 0,
                  seed: int = 42, init_centroids=None, metric: str = "l2", with_extras: bool = False,
-                 rounds: int = 1, device_budget: int = 0):
+                 rounds: int = 1, device_budget: int = 0, host_resident: bool = False):
     """Bucketed kNN graph of X (N x d, float32 / uint8 / int8; torch CUDA tensor or numpy).
 
     Returns (ids[N, M] int32, dists[N, M] float32) on X's side (device or host);
@@ -95,6 +98,8 @@ def build_bucket(X, n_buckets: int, knn_degree: int = 64, kmeans_iters: int = 10
     ``rounds`` > 1 repeats the build with seeds seed+1, ... and merges each round's
     lists into the running ones (bucket2 ``-t``).  ``device_budget`` (bytes, 0 = 80% of free
     device memory) bounds the bucket kNN stage; buckets beyond it run in batches, same result.
+    ``host_resident`` (numpy X): the build reads X in place from host memory (registered for the
+    call) and never copies it whole to the device -- datasets larger than the device's memory.
     """
     dev = _is_dev(X)
     N, d = X.shape
@@ -102,7 +107,7 @@ def build_bucket(X, n_buckets: int, knn_degree: int = 64, kmeans_iters: int = 10
     dists = _empty((N, knn_degree), "float32", dev)
     cent = _empty((n_buckets, d), "float32", dev) if with_extras else None
     top2 = _empty((N, 2), "int32", dev) if with_extras else None
-    ds = _dataset(X, metric)
+    ds = _dataset(X, metric, host_resident)
     p = _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, init_centroids, dev, cent, top2,
                        rounds, device_budget)
     L.check(L.lib().gta_build_bucket(ctypes.byref(ds), ctypes.byref(p), _ptr(ids), _ptr(dists),
@@ -147,12 +152,13 @@ def build_bucket2(X, knn_degree: int = 64, nprobe: int = 0, centroid_ratio: floa
 
 def build_cagra(X, n_buckets: int, knn_degree: int = 64, graph_degree: int = 32, kmeans_iters: int = 10,
                 kmeans_sample: int = 0, seed: int = 42, init_centroids=None, metric: str = "l2", rounds: int = 1,
-                device_budget: int = 0):
-    """Whole build: bucketed kNN (degree M), sanitize, CAGRA optimize -> graph[N, K] uint32."""
+                device_budget: int = 0, host_resident: bool = False):
+    """Whole build: bucketed kNN (degree M), sanitize, CAGRA optimize -> graph[N, K] uint32.
+    ``host_resident``: as for build_bucket."""
     dev = _is_dev(X)
     N = X.shape[0]
     graph = _empty((N, graph_degree), "uint32" if not dev else "int32", dev)
-    ds = _dataset(X, metric)
+    ds = _dataset(X, metric, host_resident)
     bp = _bucket_params(n_buckets, knn_degree, kmeans_iters, kmeans_sample, seed, init_centroids, dev, None, None,
                         rounds, device_budget)
     p = L.gta_cagra_params(bucket=bp, graph_degree=graph_degree, reserved0=0)

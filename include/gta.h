@@ -57,7 +57,12 @@ typedef struct {
     int32_t d;
     int32_t dtype;     /* GTA_F32 / GTA_U8 / GTA_I8 */
     int32_t metric;    /* GTA_L2 / GTA_IP */
-    int32_t on_device; /* 1: data is a device pointer */
+    int32_t on_device; /* 0: host pointer (copied to the device once); 1: device pointer;
+                          2: host memory read in place by gta_build_bucket / gta_build_cagra (the
+                          pages are registered pinned, mapped and read-only for the call, the
+                          kernels read rows through the host link and the whole dataset is never
+                          copied to the device: datasets larger than the device's memory, with
+                          device_budget bounding the bucket stage; other entry points take 0 or 1) */
 } gta_dataset;
 
 /* Parameters of the bucketed kNN build (bucket2 / build_bucket.py). */

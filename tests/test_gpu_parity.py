@@ -478,3 +478,28 @@ def test_assign_topk_integer_rows_split_screen(B, k):
     ri, rd = orc.topk_assign(X, C, k)
     np.testing.assert_array_equal(host(ids), ri)
     np.testing.assert_array_equal(host(dd), rd)
+
+
+@pytest.mark.parametrize("kind", ["u8", "f32"])
+def test_host_resident_dataset_matches_device_copy(kind):
+    """gta_dataset.on_device == 2: the build reads the rows in place from host memory (registered
+    and mapped for the call, never copied whole to the device); with a small device budget the
+    bucket stage runs in batches.  The graph and lists equal those of the ordinary build."""
+    rng = np.random.default_rng(21)
+    if kind == "u8":
+        cfg = gta.scaled(gta.CONFIGS["c2"], 30000)
+        X = gta.generate(cfg, seed=5)
+        B, M, K = 24, 32, 16
+    else:
+        X = mixture(rng, 20000, 300, 30, 0.3)
+        B, M, K = 12, 32, 16
+    ids0, d0 = gta.build_bucket(X, B, M, 3)
+    ids1, d1 = gta.build_bucket(X, B, M, 3, host_resident=True, device_budget=8 << 20)
+    np.testing.assert_array_equal(ids1, ids0)
+    np.testing.assert_array_equal(d1, d0)
+    g0 = gta.build_cagra(X, B, M, K, 3)
+    g1 = gta.build_cagra(X, B, M, K, 3, host_resident=True, device_budget=8 << 20)
+    np.testing.assert_array_equal(g1, g0)
+    # a device tensor cannot be host-resident; the other entry points take host (0) or device (1)
+    with pytest.raises(gta.GtaError):
+        gta.build_bucket(torch.from_numpy(X).cuda(), B, M, 3, host_resident=True)
