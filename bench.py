@@ -67,21 +67,21 @@ def _peaks():
 def _compute_dtype(cfg) -> str:
     """Operand type of the bucket distance kernel: u8 rows with lists of at most 64 run on
     kind::i8 MMAs (int32 accumulation), other exact 8-bit rows on bf16, float rows on the
-    fp16 hi/lo screen (three kind::f16 products per element) with an exact fp32 rerank."""
+    fp16 screen with an exact fp32 rerank: one fp16 part per element for d >= 256 ("f16"; a wave
+    falls back to the hi/lo split when it rescans too many rows), the hi/lo split (three kind::f16
+    products per element, "f16x3") below."""
     if cfg.dtype == "uint8" and cfg.knn_degree <= 64 and cfg.d <= 129:
         return "u8"
     if cfg.dtype in ("uint8", "int8") and cfg.d <= 129:
         return "bf16"
-    return "f16x3"
+    return "f16" if cfg.d >= 256 else "f16x3"
 
 
 # DRAM bytes (read + write) per launch of the dominant stage's kernel, averaged over the launches
 # of one build, from the committed one-pass ncu launch list of the same command and workload
 # (`dram__bytes_read.sum + dram__bytes_write.sum`, profiles/launches_*.md):
 # {(stage, config, N): (bytes per launch, source)}.
-TRAFFIC_PER_LAUNCH = {
-    ("dist_topk_bucket", "c3", 1000000): (6.02e9, "profiles/launches_c3_bench.md"),
-}
+TRAFFIC_PER_LAUNCH = {}
 
 
 # ---------------------------------------------------------------- clocks
@@ -467,9 +467,11 @@ def main():
     roof = {}
     for k, v in stages.items():
         r = roof.setdefault("dist_topk_bucket" if k.startswith("dist_topk_bucket") else k,
-                            {"ms": 0.0, "units": 0.0, "launches": 0, "rows": 0.0})
+                            {"ms": 0.0, "units": 0.0, "launches": 0, "rows": 0.0, "issued": 0.0})
         r["ms"] += v["ms"]
         r["units"] += v["units"]
+        # the float screen's split waves issue three fp16 products per element, the others one
+        r["issued"] += v["units"] * (3.0 if k.endswith("_split") else 1.0)
         r["launches"] += v["launches"]
         r["rows"] += v["counters"][2] if k.startswith("dist_topk") else 0.0
     kernels = [k for k in roof if not k.endswith("_total") and roof[k]["units"] > 0]
@@ -491,14 +493,16 @@ def main():
                 roofline["note"] = ("kind::i8 MMAs: algorithmic operations per second against the measured bf16 "
                                     "sustained rate; frac_i8_nominal divides by twice that (the nominal dense i8 "
                                     "rate is twice bf16)")
-            elif cd == "f16x3":
-                roofline["kernel_detail"] = "screen_kernel: kind::f16 on fp16 hi/lo parts, 3 MMAs per K step"
-                roofline["mma_issued_per_algorithmic"] = 3.0
-                roofline["frac_issued"] = 3.0 * achieved / tflops
+            elif cd in ("f16", "f16x3"):
+                issued = s["issued"] / s["units"] if s["units"] > 0 else 1.0
+                roofline["kernel_detail"] = ("screen_kernel: kind::f16 on scaled fp16 rows, one product per element "
+                                             "(hi.hi), three (hi/lo split) in the waves that fall back to the split")
+                roofline["mma_issued_per_algorithmic"] = issued
+                roofline["frac_issued"] = issued * achieved / tflops
                 roofline["note"] = ("algorithmic flops (sum 2 n_b^2 d, once) per second of the screen launches; "
-                                    "the split operands issue three fp16 products per element (frac_issued: the "
-                                    "tensor pipe's issued rate against the measured bf16 sustained rate, fp16 "
-                                    "runs at the bf16 rate)")
+                                    "frac_issued: the tensor pipe's issued rate (split waves count three products "
+                                    "per element) against the measured bf16 sustained rate, fp16 runs at the "
+                                    "bf16 rate")
         else:
             achieved = per_launch_units / per_launch_s / 1e9
             roofline = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",

@@ -266,28 +266,16 @@ __device__ __forceinline__ void tmem_ld_wait_2x16(uint32_t (&a)[16], uint32_t (&
 // main accumulator's rounding grows with d products instead of 3 d; the epilogue adds the two.
 // Both halves of one tile's accumulator pair fill the 256 columns, so the tile is not double
 // buffered (the MMA of the next tile waits until the epilogue holds the last slice in registers).
-//
-// kPair (a cluster of two CTAs on two SMs, kCorr only): the pair screens 256 A rows (each CTA its
-// own item of 128) against the same column tiles.  Each CTA loads its A rows and half of every B
-// tile (64 columns); the first CTA's thread issues two-SM MMAs (M = 256) that read both CTAs'
-// shared memory and write both CTAs' TMEM, so B crosses L2 and shared memory once per pair.  The
-// TMA of both CTAs completes on the first CTA's stage barriers (which expect the pair's bytes); the
-// MMA commits arrive on the barriers of both CTAs; the second CTA's epilogue releases the
-// accumulator on the first CTA's barrier.
-template <int kL, bool kSplit, bool kCorr, bool kPair = false>
-__global__ void __launch_bounds__(kSThreads, 1)
-    screen_kernel(const __grid_constant__ CUtensorMap tm, const __grid_constant__ CUtensorMap tmb, const ScreenArgs p)
+template <int kL, bool kSplit, bool kCorr>
+__global__ void __launch_bounds__(kSThreads, 1) screen_kernel(const __grid_constant__ CUtensorMap tm, const ScreenArgs p)
 {
     static_assert(!kCorr || kSplit, "the correction accumulator holds the lo products");
-    static_assert(!kPair || kCorr, "CTA pairs run the corrected split screen");
     constexpr int kParts = kSplit ? 2 : 1;
     // operand chunks of 64 fp16 (128-byte swizzle) or, kCorr, 32 fp16 (64-byte swizzle: smaller
     // stages leave room for the drained tile)
     constexpr int kChunkElems = kCorr ? 32 : 64;
-    constexpr int kBRows = kPair ? kSTile / 2 : kSTile;  // B rows this CTA loads per column tile
     constexpr uint32_t kPartChunk = 128u * static_cast<uint32_t>(kChunkElems) * 2u;
-    constexpr uint32_t kPartChunkB = static_cast<uint32_t>(kBRows) * static_cast<uint32_t>(kChunkElems) * 2u;
-    constexpr uint32_t kStageBytes = kParts * (kPartChunk + kPartChunkB);  // A parts then B parts
+    constexpr uint32_t kStageBytes = 2u * kParts * kPartChunk;  // A parts then B parts
     constexpr uint32_t kTmemCols = 512u;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     const uint32_t base = smem_u32(smem_raw);
@@ -296,14 +284,10 @@ __global__ void __launch_bounds__(kSThreads, 1)
         return;
     }
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const uint32_t rank = kPair ? cluster_ctarank() : 0u;
-    const bool leader = rank == 0u;
     const WorkItem w = p.work[blockIdx.x];
-    // the pair's column order follows its first item (both CTAs sweep the same tiles)
-    const WorkItem w0 = kPair ? p.work[blockIdx.x & ~1u] : w;
     const int n_ct = (w.b_rows + kSTile - 1) / kSTile;
     // the column tile of the rows themselves first (clamped into the item's columns)
-    const int t0 = (w0.has_self & 1) ? max(0, min(n_ct - 1, w0.self_col0 / kSTile)) : 0;
+    const int t0 = (w.has_self & 1) ? max(0, min(n_ct - 1, w.self_col0 / kSTile)) : 0;
     const int S = p.stages;
     uint32_t* buf = reinterpret_cast<uint32_t*>(smem_raw + p.buf_off);
     float* pn_s = reinterpret_cast<float*>(smem_raw + p.pn_off);
@@ -323,24 +307,18 @@ __global__ void __launch_bounds__(kSThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(S_ACC_FULL(b), 1);
-            mbar_init(S_ACC_EMPTY(b), kPair ? 8 : 4);  // the epilogue warps of the pair
+            mbar_init(S_ACC_EMPTY(b), 4);
         }
         mbar_init(mma_done, 1);
         *abort_flag = 0;
         fence_barrier_init();
     }
     if (warp == 1) {
-        if constexpr (kPair) {
-            tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
-            tmem_relinquish_pair();
-        } else {
-            tmem_alloc(smem_u32(tmem_slot), kTmemCols);
-            tmem_relinquish();
-        }
+        tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+        tmem_relinquish();
     }
     tc_fence_before();
     __syncthreads();
-    if constexpr (kPair) cluster_sync();  // both CTAs' barriers exist before either signals the other
     tc_fence_after();
     const uint32_t tmem_base = *tmem_slot;
 
@@ -360,53 +338,25 @@ __global__ void __launch_bounds__(kSThreads, 1)
                         break;
                     }
                     const uint32_t dst = base + static_cast<uint32_t>(s) * kStageBytes;
-                    if constexpr (kPair) {
-                        // the pair's bytes complete on the first CTA's barrier
-                        const uint32_t fb = mapa_shared(S_FULL(s), 0u);
-                        if (leader) mbar_arrive_expect_tx(S_FULL(s), 2u * kStageBytes);
+                    mbar_arrive_expect_tx(S_FULL(s), kStageBytes);
 #pragma unroll
-                        for (int q = 0; q < kParts; ++q) {
-                            const int x = q * p.part_stride + kc * kChunkElems;
-                            tma_load_2d_pair(dst + static_cast<uint32_t>(q) * kPartChunk, &tm, fb, x, w.a_row0);
-                            tma_load_2d_pair(dst + kParts * kPartChunk + static_cast<uint32_t>(q) * kPartChunkB, &tmb,
-                                             fb, x, w.b_row0 + ct * kSTile + static_cast<int>(rank) * kBRows);
-                        }
-                    } else {
-                        mbar_arrive_expect_tx(S_FULL(s), kStageBytes);
-#pragma unroll
-                        for (int q = 0; q < kParts; ++q) {
-                            const int x = q * p.part_stride + kc * kChunkElems;
-                            tma_load_2d(dst + static_cast<uint32_t>(q) * kPartChunk, &tm, S_FULL(s), x, w.a_row0);
-                            tma_load_2d(dst + kParts * kPartChunk + static_cast<uint32_t>(q) * kPartChunkB, &tm,
-                                        S_FULL(s), x, w.b_row0 + ct * kSTile);
-                        }
+                    for (int q = 0; q < kParts; ++q) {
+                        const int x = q * p.part_stride + kc * kChunkElems;
+                        tma_load_2d(dst + static_cast<uint32_t>(q) * kPartChunk, &tm, S_FULL(s), x, w.a_row0);
+                        tma_load_2d(dst + static_cast<uint32_t>(kParts + q) * kPartChunk, &tm, S_FULL(s), x,
+                                    w.b_row0 + ct * kSTile);
                     }
                     ++it;
                 }
             }
-            // every issued copy lands before the CTA can exit (a pair's copies all complete on the
-            // first CTA's barriers; the second CTA leaves only after the closing cluster barrier)
-            if (leader)
-                for (int j = max(0, it - S); j < it; ++j)
-                    drain_wait(S_FULL(j % S), static_cast<uint32_t>(j / S) & 1u, p.err);
+            // every issued copy lands before the CTA can exit
+            for (int j = max(0, it - S); j < it; ++j) drain_wait(S_FULL(j % S), static_cast<uint32_t>(j / S) & 1u, p.err);
         }
     } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer (a pair: its first CTA)
-        if (lane == 0 && leader) {
-            const uint32_t idesc = make_idesc(0u, kPair ? 2 * kSTile : kSTile, kSTile);  // fp16 x fp16 -> fp32
-            // the pair's commits: this CTA's barrier and the same barrier of the second CTA
-            auto commit = [&](uint32_t bar) {
-                if constexpr (kPair) {
-                    umma_commit_pair(mapa_shared(bar, 0u));
-                    umma_commit_pair(mapa_shared(bar, 1u));
-                } else {
-                    umma_commit(bar);
-                }
-            };
-            auto mma = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t acc) {
-                if constexpr (kPair) umma_pair(d, a, b, idesc, acc);
-                else umma<false>(d, a, b, idesc, acc);
-            };
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t idesc = make_idesc(0u, kSTile, kSTile);  // fp16 x fp16 -> fp32
+            auto mma = [&](uint32_t d, uint64_t a, uint64_t b, uint32_t acc) { umma<false>(d, a, b, idesc, acc); };
             bool ok = true;
             long long wait_acc = 0, wait_full = 0;
             int it = 0;
@@ -435,20 +385,19 @@ __global__ void __launch_bounds__(kSThreads, 1)
                     for (int kk = 0; kk < kChunkElems / 16; ++kk) {  // 16 fp16 of K per MMA
                         mma(d_tmem, ah + 2ull * kk, bh + 2ull * kk, (kc | kk) != 0 ? 1u : 0u);
                         if constexpr (kSplit) {
-                            const uint64_t al = desc(sa + kPartChunk), bl = desc(sa + kParts * kPartChunk + kPartChunkB);
+                            const uint64_t al = desc(sa + kPartChunk), bl = desc(sa + 3u * kPartChunk);
                             const uint32_t c_tmem = kCorr ? tmem_base + static_cast<uint32_t>(kSTile) : d_tmem;
                             mma(c_tmem, ah + 2ull * kk, bl + 2ull * kk, (!kCorr || (kc | kk) != 0) ? 1u : 0u);
                             mma(c_tmem, al + 2ull * kk, bh + 2ull * kk, 1u);
                         }
                     }
-                    commit(S_EMPTY(s));
+                    umma_commit(S_EMPTY(s));
                     ++it;
                 }
                 if (!ok) break;
-                commit(S_ACC_FULL(b));
+                umma_commit(S_ACC_FULL(b));
             }
-            if constexpr (kPair) umma_commit_pair(mapa_shared(mma_done, 0u));
-            else umma_commit(mma_done);
+            umma_commit(mma_done);
             drain_wait(mma_done, 0, p.err);
             if (p.stats) {
                 atomicAdd(&p.stats[6], static_cast<unsigned long long>(wait_acc));
@@ -622,10 +571,7 @@ __global__ void __launch_bounds__(kSThreads, 1)
             auto release_acc = [&]() {
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) {
-                    if (leader) mbar_arrive(S_ACC_EMPTY(b));
-                    else mbar_arrive_cluster(mapa_shared(S_ACC_EMPTY(b), 0u));  // the pair's MMA waits there
-                }
+                if (lane == 0) mbar_arrive(S_ACC_EMPTY(b));
             };
             __syncwarp();
             ld_slice(0, va, ca);
@@ -723,11 +669,9 @@ __global__ void __launch_bounds__(kSThreads, 1)
 #undef S_ACC_EMPTY
     tc_fence_before();
     __syncthreads();
-    if constexpr (kPair) cluster_sync();  // the pair's MMAs and copies are done with both CTAs
     if (warp == 1) {
         tc_fence_after();
-        if constexpr (kPair) tmem_dealloc_pair(tmem_base, kTmemCols);
-        else tmem_dealloc(tmem_base, kTmemCols);
+        tmem_dealloc(tmem_base, kTmemCols);
     }
 }
 
@@ -1168,11 +1112,10 @@ struct ScreenPlan {
     uint32_t buf_off = 0, pn_off = 0, stg_off = 0, bar_off = 0, total = 0;
 };
 
-bool screen_plan(bool split, bool corr, bool pair, ScreenPlan& pl)
+bool screen_plan(bool split, bool corr, ScreenPlan& pl)
 {
-    // operand chunk: 64 fp16 per row (corr: 32) of each part of A and B (a pair: half of B)
-    const uint32_t chunk = corr ? kSChunk / 2u : kSChunk;
-    const uint32_t stage_bytes = (split ? 2u : 1u) * (chunk + (pair ? chunk / 2u : chunk));
+    // operand chunk: 64 fp16 per row (corr: 32) of each part of A and B
+    const uint32_t stage_bytes = 2u * (split ? 2u : 1u) * (corr ? kSChunk / 2u : kSChunk);
     for (int S = 6; S >= 2; --S) {
         ScreenPlan t;
         t.stages = S;
@@ -1214,60 +1157,11 @@ EncodeFnS screen_encode()
 template <int kL, bool kSplit, bool kCorr = false>
 void launch_screen(const CUtensorMap& tm, const ScreenArgs& a, int n_work, uint32_t smem, cudaStream_t st)
 {
-    auto fn = screen_kernel<kL, kSplit, kCorr, false>;
+    auto fn = screen_kernel<kL, kSplit, kCorr>;
     GTA_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    fn<<<n_work, kSThreads, smem, st>>>(tm, tm, a);
+    fn<<<n_work, kSThreads, smem, st>>>(tm, a);
     count_launches(1);
     GTA_CUDA(cudaGetLastError());
-}
-
-// CTA pairs: clusters of two, n_work (even) items, items 2 i and 2 i + 1 with the same columns
-template <int kL>
-void launch_screen_pair(const CUtensorMap& tm, const CUtensorMap& tmb, const ScreenArgs& a, int n_work, uint32_t smem,
-                        cudaStream_t st)
-{
-    auto fn = screen_kernel<kL, true, true, true>;
-    GTA_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(static_cast<unsigned>(n_work));
-    cfg.blockDim = dim3(kSThreads);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = 2;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    GTA_CUDA(cudaLaunchKernelEx(&cfg, fn, tm, tmb, a));
-    count_launches(1);
-    GTA_CUDA(cudaGetLastError());
-}
-
-// The items of a wave as CTA pairs: consecutive items over the same columns share a pair; an item
-// left alone is paired with a copy that has no rows (it loads the second half of the columns).
-std::vector<WorkItem> pair_items(const std::vector<WorkItem>& items)
-{
-    std::vector<WorkItem> out;
-    out.reserve(items.size() + items.size() / 2 + 1);
-    for (size_t i = 0; i < items.size();) {
-        const WorkItem& a = items[i];
-        if (i + 1 < items.size() && items[i + 1].b_row0 == a.b_row0 && items[i + 1].b_rows == a.b_rows) {
-            out.push_back(a);
-            out.push_back(items[i + 1]);
-            i += 2;
-        } else {
-            WorkItem e = a;
-            e.a_rows = 0;
-            e.has_self = 0;
-            e.pad2 = -1;
-            out.push_back(a);
-            out.push_back(e);
-            i += 1;
-        }
-    }
-    return out;
 }
 
 }  // namespace
@@ -1290,7 +1184,8 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     // kChunk: the CTAs of a wave re-read their own A tiles and the chunk's B tiles from L2 once per
     // column tile, so a chunk is sized for both to stay in L2 (the A tiles of one CTA per SM plus
     // the chunk's columns within 90% of it; a power of two, 4096 .. 65536 columns).
-    const int64_t row_bytes = static_cast<int64_t>(pr.parts) * ((pr.d + 63) / 64 * 64) * 2;
+    // (the operand bytes a row tile reads: one fp16 part when the screen starts with one part)
+    const int64_t row_bytes = static_cast<int64_t>(pr.parts == 1 || pr.d >= 256 ? 1 : pr.parts) * ((pr.d + 63) / 64 * 64) * 2;
     int64_t kChunk = 1 << 16;
     {
         int dev = 0, l2 = 0, n_sm = 0;
@@ -1339,9 +1234,7 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         // region); the exact M-th distance over its first M candidates seeds every chunk
         const int64_t W = std::min<int64_t>(kPilot, nb);
         for (int64_t t = r0; t < r1; t += 128) {
-            // centred on the tile pair (t and its neighbour share a window, so a CTA pair shares it)
-            const int64_t tp = r0 + (t - r0) / 256 * 256;
-            const int64_t ws = std::max<int64_t>(0, std::min<int64_t>(tp + 128 - W / 2, nb - W));
+            const int64_t ws = std::max<int64_t>(0, std::min<int64_t>(t + 64 - W / 2, nb - W));
             pilot.push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, r1 - t)),
                                      static_cast<int32_t>(lo + ws), static_cast<int32_t>(W),
                                      static_cast<int32_t>(t - ws), static_cast<int32_t>(base + nr + (t - r0)), 1,
@@ -1363,17 +1256,8 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     }
     const int64_t item_rows = pr.n_rows + ext_rows;
     GTA_REQUIRE(item_rows < (1ll << 31), kInvalid, "screen: too many list rows");
-    const bool split = pr.parts == 2;
     const int L = screen_list_len(pr.m_out);
     const int d16 = (pr.d + 63) / 64 * 64;
-    ScreenPlan pl;
-    // long rows: the corrections in their own accumulator (see screen_kernel)
-    const bool corr = split && pr.d >= 256;
-    // two-SM CTA pairs (B across L2 and shared memory once per 256 rows) are built and pass the
-    // parity tests, but measured slower at C3 (screen 2.60 s against 2.45 s per build: a pair waits
-    // for the slower of its two epilogue drains before the next tile), so the screen runs single CTAs
-    const bool pair = false;
-    GTA_REQUIRE(screen_plan(split, corr, pair, pl), kInvalid, "screen: shared memory plan failed");
     // the pool's rows as f32 (bucket-contiguous, pitch dp, zero past d) with their exact squared
     // norms, the scale's source (max ||x||) and the scaled fp16 operand rows
     const int dp = (pr.d + 31) / 32 * 32;
@@ -1391,18 +1275,58 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         count_launches(1);
         GTA_CUDA(cudaGetLastError());
     }
-    CUtensorMap tm, tmb;  // A tiles (128 rows); a pair's half B tiles (64 rows)
-    for (int m = 0; m < 2; ++m) {
+    // Screen modes (each with its kernel, shared-memory plan, tensor map and error bound):
+    //  * split: hi.hi + hi.lo + lo.hi (the lo products in their own accumulator for d >= 256);
+    //  * one part: hi.hi only, on the hi half of the same rows -- a margin about 2^12 times wider
+    //    (2^-10 of |a| bmax per element) but a third of the tensor work and half the operand
+    //    bytes.  Long rows (d >= 256) start with it: their neighbour distances are large against
+    //    the margin (C3, 1M x 960: 1.78 s per build against 3.16 s split).  A wave that sends more
+    //    than 5% of its rows to a rescan (too many columns within the wider margin) hands the
+    //    remaining waves to the split screen; the seeds carry over (they are exact bounds).
+    // error bound of the screened distance (the margin, applied to the M-th key), relative to
+    // |a||b| <= |a| bmax:
+    //  * operand parts: split 3 * 2^-22 (the dropped lo.lo and the rounding of lo), one part 2^-10;
+    //  * fp32 accumulation, 2^-22 per product added to an accumulator: split into one accumulator
+    //    3 d products; with the correction accumulator (corr) d products plus the final addition
+    //    (the corrections themselves are below 2^-10 of the sum); one part d;
+    // and, relative to (|a| + bmax)^2, the fp32 squared norms (each lane of the norm kernel chains
+    // 4 ceil(dp / 128) products, then five butterfly additions) and the two fused operations of
+    // the score; a 1.25 safety factor on both
+    struct Mode {
+        bool split = false, corr = false;
+        ScreenPlan pl;
+        CUtensorMap tm;
+        int k_chunks = 0;
+        float mc1 = 0.f, mc2 = 0.f;
+    };
+    auto make_mode = [&](bool split) {
+        Mode m;
+        m.split = split;
+        m.corr = split && pr.d >= 256;
+        GTA_REQUIRE(screen_plan(m.split, m.corr, m.pl), kInvalid, "screen: shared memory plan failed");
         cuuint64_t dims[2] = {static_cast<cuuint64_t>(pr.parts) * d16, static_cast<cuuint64_t>(pr.n_rows)};
         cuuint64_t strides[1] = {static_cast<cuuint64_t>(pr.parts) * d16 * 2u};
-        cuuint32_t box[2] = {corr ? 32u : 64u, m == 0 ? 128u : 64u};
+        cuuint32_t box[2] = {m.corr ? 32u : 64u, 128u};
         cuuint32_t estr[2] = {1u, 1u};
-        const CUresult r = screen_encode()(m == 0 ? &tm : &tmb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, rows.get(), dims,
-                                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                           corr ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+        const CUresult r = screen_encode()(&m.tm, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, rows.get(), dims, strides, box,
+                                           estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                           m.corr ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
                                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
         GTA_REQUIRE(r == CUDA_SUCCESS, kCuda, "cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
-    }
+        m.k_chunks = d16 / (m.corr ? 32 : 64);
+        const double dd = pr.d;
+        const double part_err = split ? 3.0 * std::ldexp(1.0, -22) : std::ldexp(1.0, -10);
+        const double n_prod = split ? (m.corr ? dd + 3.0 : 3.0 * dd) : dd;
+        const double k_norm = 4.0 * ((dp + 127) / 128) + 8.0;
+        m.mc1 = static_cast<float>(1.25 * 4.0 * (part_err + n_prod * std::ldexp(1.0, -22)));
+        m.mc2 = static_cast<float>(1.25 * 3.0 * (k_norm + 4.0) * std::ldexp(1.0, -24));
+        return m;
+    };
+    Mode modes[2];
+    int n_modes = 0, cur = 0;
+    if (pr.parts == 1 || pr.d >= 256) modes[n_modes++] = make_mode(false);
+    const int split_mode = pr.parts == 2 ? n_modes : -1;
+    if (pr.parts == 2) modes[n_modes++] = make_mode(true);
     DevBuf<int32_t> cand_cols(static_cast<size_t>(item_rows) * L, st), cand_n(static_cast<size_t>(item_rows), st);
     DevBuf<int32_t> ext_ids(static_cast<size_t>(ext_rows) * pr.m_out, st);
     DevBuf<float> ext_dists(static_cast<size_t>(ext_rows) * pr.m_out, st);
@@ -1415,34 +1339,13 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     ScreenArgs a{};
     a.norm = norm.get();
     a.maxnorm = bmax.get();
-    a.k_chunks = d16 / (corr ? 32 : 64);
     a.part_stride = d16;
     a.m_sel = pr.m_out;
-    a.stages = pl.stages;
     a.col_bits = 16;  // columns of an item: at most kChunk
-    // error bound of the screened distance (the margin, applied to the M-th key), relative to
-    // |a||b| <= |a| bmax:
-    //  * operand parts: split 3 * 2^-22 (the dropped lo.lo and the rounding of lo), one part 2^-10;
-    //  * fp32 accumulation, 2^-22 per product added to an accumulator: split into one accumulator
-    //    3 d products; with the correction accumulator (corr) d products plus the final addition
-    //    (the corrections themselves are below 2^-10 of the sum); one part d;
-    // and, relative to (|a| + bmax)^2, the fp32 squared norms (each lane of the norm kernel chains
-    // 4 ceil(dp / 128) products, then five butterfly additions) and the two fused operations of
-    // the score; a 1.25 safety factor on both
-    const double dd = pr.d;
-    const double part_err = split ? 3.0 * std::ldexp(1.0, -22) : std::ldexp(1.0, -10);
-    const double n_prod = split ? (corr ? dd + 3.0 : 3.0 * dd) : dd;
-    const double k_norm = 4.0 * ((dp + 127) / 128) + 8.0;
-    a.mc1 = static_cast<float>(1.25 * 4.0 * (part_err + n_prod * std::ldexp(1.0, -22)));
-    a.mc2 = static_cast<float>(1.25 * 3.0 * (k_norm + 4.0) * std::ldexp(1.0, -24));
     a.seed = seeds.get();
     a.cand_cols = cand_cols.get();
     a.cand_n = cand_n.get();
     a.err = pr.err;
-    a.buf_off = pl.buf_off;
-    a.pn_off = pl.pn_off;
-    a.bar_off = pl.bar_off;
-    a.stg_off = pl.stg_off;
     RerankX r{};
     r.pool = fpool.get();
     r.dp = dp;
@@ -1451,8 +1354,6 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     r.cand_n = cand_n.get();
     r.norm = norm.get();
     r.maxnorm = bmax.get();
-    r.mc1 = a.mc1;
-    r.mc2 = a.mc2;
     r.col_bits = a.col_bits;
     r.L = L;
     r.m_out = pr.m_out;
@@ -1485,30 +1386,38 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         const size_t wk = pilot.empty() ? k : k - 1;
         const std::vector<WorkItem>& items = is_pilot ? pilot : waves[wk];
         if (items.empty()) continue;
-        // the screen's items (the pilot's unseeded: its rerank groups carry the seed slots), as CTA
-        // pairs when the screen runs in pairs
+        // the screen's items (the pilot's unseeded: its rerank groups carry the seed slots)
         std::vector<WorkItem> launch(items);
         if (is_pilot)
             for (WorkItem& it : launch) it.pad2 = -1;
-        if (pair) launch = pair_items(launch);
         DevBuf<WorkItem> work(launch.size(), st);
         // pageable sources: each copy is staged before cudaMemcpyAsync returns
         GTA_CUDA(cudaMemcpyAsync(work.get(), launch.data(), sizeof(WorkItem) * launch.size(), cudaMemcpyHostToDevice, st));
         a.work = work.get();
+        const Mode& md = modes[cur];
+        a.k_chunks = md.k_chunks;
+        a.stages = md.pl.stages;
+        a.buf_off = md.pl.buf_off;
+        a.pn_off = md.pl.pn_off;
+        a.bar_off = md.pl.bar_off;
+        a.stg_off = md.pl.stg_off;
+        a.mc1 = r.mc1 = md.mc1;
+        a.mc2 = r.mc2 = md.mc2;
         {
-            ProfScope prof(is_pilot ? "screen_pilot" : pr.prof_name, is_pilot ? pilot_flops : wave_flops[wk], st);
+            // split waves are named apart (three issued products per element against one)
+            const std::string pname = std::string(is_pilot ? "screen_pilot" : pr.prof_name) + (md.split ? "_split" : "");
+            ProfScope prof(pname.c_str(), is_pilot ? pilot_flops : wave_flops[wk], st);
             a.stats = prof.counters(8);
             const int n_work = static_cast<int>(launch.size());
+            const uint32_t smem = md.pl.total;
             if (L == 128) {
-                if (pair) launch_screen_pair<128>(tm, tmb, a, n_work, pl.total, st);
-                else if (corr) launch_screen<128, true, true>(tm, a, n_work, pl.total, st);
-                else if (split) launch_screen<128, true>(tm, a, n_work, pl.total, st);
-                else launch_screen<128, false>(tm, a, n_work, pl.total, st);
+                if (md.corr) launch_screen<128, true, true>(md.tm, a, n_work, smem, st);
+                else if (md.split) launch_screen<128, true>(md.tm, a, n_work, smem, st);
+                else launch_screen<128, false>(md.tm, a, n_work, smem, st);
             } else {
-                if (pair) launch_screen_pair<256>(tm, tmb, a, n_work, pl.total, st);
-                else if (corr) launch_screen<256, true, true>(tm, a, n_work, pl.total, st);
-                else if (split) launch_screen<256, true>(tm, a, n_work, pl.total, st);
-                else launch_screen<256, false>(tm, a, n_work, pl.total, st);
+                if (md.corr) launch_screen<256, true, true>(md.tm, a, n_work, smem, st);
+                else if (md.split) launch_screen<256, true>(md.tm, a, n_work, smem, st);
+                else launch_screen<256, false>(md.tm, a, n_work, smem, st);
             }
         }
         // the rerank's work: groups of kRrRows rows of the same items, in the same (bucket) order
@@ -1537,6 +1446,15 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
             rescan_kernel<<<static_cast<unsigned>(std::max(1, n_sm) * 2), kRsWarps * 32, smem_rs, st>>>(r);
             count_launches(1);
             GTA_CUDA(cudaGetLastError());
+        }
+        if (split_mode >= 0 && cur != split_mode && wk + 1 < waves.size()) {
+            // too many rescans under the one-part margin: the remaining waves screen split
+            unsigned n_rs = 0;
+            GTA_CUDA(cudaMemcpyAsync(&n_rs, n_rescan.get(), sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+            GTA_CUDA(cudaStreamSynchronize(st));
+            int64_t wave_rows = 0;
+            for (const WorkItem& it : items) wave_rows += it.a_rows;
+            if (static_cast<double>(n_rs) > 0.05 * static_cast<double>(wave_rows)) cur = split_mode;
         }
         if (!chunked.empty()) {
             // chunk k into the running lists (k = 0: the seeds of chunk 0's lists)

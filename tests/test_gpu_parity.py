@@ -258,16 +258,23 @@ def test_bucket_knn_f32_vs_oracle(N, d, B, M):
     assert_lists_match(host(gi), host(gd), ri, rd, exact=False, X=X, qrows=mem)
 
 
-@pytest.mark.parametrize("N,d,M,edges", [
-    (70000, 8, 16, [65535, 65536, 65537]),                    # 65 536-column chunks: two waves
-    (30000, 960, 128, [8191, 8192, 8193, 16384, 24575, 24576]),  # long rows: 8 192-column chunks, four waves
+@pytest.mark.parametrize("N,d,M,edges,dup", [
+    (70000, 8, 16, [65535, 65536, 65537], False),               # 65 536-column chunks: two waves
+    (70000, 960, 128, [32767, 32768, 32769, 65535, 65536], False),  # long rows, one-part screen: three waves
+    (70000, 512, 64, [65535, 65536, 65537], True),              # near-duplicates: rescans, split screen after wave 0
 ])
-def test_bucket_knn_f32_long_segment_column_chunks(N, d, M, edges):
-    """A long float segment runs as column chunks (sized for the L2: 65 536 columns for short rows,
-    8 192 at d = 960) whose exact lists are merged wave by wave: sampled rows (chunk edges included)
-    against the oracle's exact top-M over the whole segment."""
+def test_bucket_knn_f32_long_segment_column_chunks(N, d, M, edges, dup):
+    """A long float segment runs as column chunks (sized for the L2 with the operand bytes a row
+    tile reads) whose exact lists are merged wave by wave: sampled rows (chunk edges included)
+    against the oracle's exact top-M over the whole segment.  dup: groups of near-identical rows,
+    so the one-part screen's margin holds more columns than a list and rows are rescanned (the
+    later waves run the split screen)."""
     rng = np.random.default_rng(70)
     X = mixture(rng, N, d, 40, 0.2)
+    if dup:
+        base = X[rng.integers(0, N, 200)]
+        idx = rng.choice(N, N // 2, replace=False)
+        X[idx] = base[rng.integers(0, 200, idx.size)] + rng.normal(0, 1e-4, (idx.size, d)).astype(np.float32)
     mem = np.arange(N, dtype=np.int32)
     off = np.array([0, N], np.int64)
     gi, gd = gta.bucket_knn(dev(X), dev(mem), dev(off), M)
