@@ -81,7 +81,9 @@ def _compute_dtype(cfg) -> str:
 # of one build, from the committed one-pass ncu launch list of the same command and workload
 # (`dram__bytes_read.sum + dram__bytes_write.sum`, profiles/launches_*.md):
 # {(stage, config, N): (bytes per launch, source)}.
-TRAFFIC_PER_LAUNCH = {}
+TRAFFIC_PER_LAUNCH = {
+    ("dist_topk_bucket", "c3", 1000000): (2.104e10, "profiles/launches_c3_bench.md"),
+}
 
 
 # ---------------------------------------------------------------- clocks

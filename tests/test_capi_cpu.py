@@ -103,6 +103,33 @@ def test_phased_bucket_knn_rejects_bad_arguments_before_device_work():
     assert f(*args(0, dummy)) == L.GTA_EINVAL
 
 
+def test_ranged_bucket_knn_and_shard_entry_points_reject_bad_arguments():
+    """The sharded build's entry points check their arguments before any device work."""
+    lib = L.lib()
+    d = ctypes.c_void_p(16)  # never dereferenced: the checks come first
+    z = ctypes.c_void_p(0)
+    # ranged kNN: both row-range arrays or neither (the ranged entry needs both)
+    assert lib.gta_bucket_knn_rows_ranged(d, L.GTA_F32, 100, 16, d, d, d, d, 4, 8, 1, z, z, z, d, d, z) == L.GTA_EINVAL
+    assert lib.gta_bucket_knn_rows_ranged(d, L.GTA_F32, 100, 16, d, d, d, d, 4, 8, 1, z, d, z, d, d, z) == L.GTA_EINVAL
+    cnt = (ctypes.c_int64 * 65)()
+    # membership packing: 1 to 64 ranks, a known dtype, both send buffers or neither
+    pm = lib.gta_shard_pack_memberships
+    assert pm(d, L.GTA_U8, 10, 8, 0, d, 4, d, 65, cnt, z, z, 0, z) == L.GTA_EINVAL
+    assert pm(d, 7, 10, 8, 0, d, 4, d, 2, cnt, z, z, 0, z) == L.GTA_EINVAL
+    assert pm(d, L.GTA_U8, 10, 8, 0, d, 4, d, 2, cnt, d, z, 0, z) == L.GTA_EINVAL
+    assert pm(d, L.GTA_U8, 10, 8, 0, d, 4, z, 2, cnt, z, z, 0, z) == L.GTA_EINVAL
+    # list packing: owner ranges in order, buffers all or none
+    pl = lib.gta_shard_pack_lists
+    lo = (ctypes.c_int64 * 4)()
+    hi = (ctypes.c_int64 * 4)()
+    bad_starts = (ctypes.c_int64 * 3)(0, 50, 40)
+    good_starts = (ctypes.c_int64 * 3)(0, 40, 50)
+    assert pl(d, d, 10, 8, d, d, d, 4, lo, hi, bad_starts, 2, cnt, z, z, z, 0, z) == L.GTA_EINVAL
+    assert pl(d, d, 10, 8, d, d, d, 4, lo, hi, good_starts, 2, cnt, d, z, z, 0, z) == L.GTA_EINVAL
+    assert lib.gta_shard_member_rows(z, 5, 0, 10, d, d, z) == L.GTA_EINVAL
+    assert lib.gta_shard_lower_seeds(d, 8, 10, d, d, d, d, 4, lo, hi, 100, z, z) == L.GTA_EINVAL
+
+
 def test_synthetic_generators_are_seeded():
     cfg = gta.scaled(gta.CONFIGS["c2"], 2000)
     a, b = gta.generate(cfg, seed=5), gta.generate(cfg, seed=5)
@@ -155,3 +182,11 @@ def test_npy_reader_and_u32_files(tmp_path):
     gta.write_u32(str(tmp_path / "inv.bin"), v)
     np.testing.assert_array_equal(gta.read_u32(str(tmp_path / "inv.bin")), v)
     assert (tmp_path / "inv.bin").stat().st_size == 40  # raw, no header
+
+
+def test_host_resident_needs_a_contiguous_host_array():
+    """host_resident datasets are read in place: a strided view is refused before any device work."""
+    X = np.zeros((100, 16), np.uint8)
+    with pytest.raises(gta.GtaError) as e:
+        gta.build_bucket(X[:, ::2], 4, 8, host_resident=True)
+    assert e.value.code == L.GTA_EINVAL
