@@ -1394,7 +1394,9 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         // pageable sources: each copy is staged before cudaMemcpyAsync returns
         GTA_CUDA(cudaMemcpyAsync(work.get(), launch.data(), sizeof(WorkItem) * launch.size(), cudaMemcpyHostToDevice, st));
         a.work = work.get();
-        const Mode& md = modes[cur];
+        // the pilot's rows are unseeded: under the one-part margin they admit many more keys (slow
+        // list merges), so it runs the split screen when there is one (its windows are short)
+        const Mode& md = modes[is_pilot && split_mode >= 0 ? split_mode : cur];
         a.k_chunks = md.k_chunks;
         a.stages = md.pl.stages;
         a.buf_off = md.pl.buf_off;
