@@ -140,10 +140,12 @@ void dist_topk(const DistTopkProblem& pr, cudaStream_t st);
 // Float-row per-bucket kNN (screen.cu): pool row j is dataset row ids[j] (X: n x d rows of
 // dtype, dense); the pool is grouped into segments (buckets, in processing order) and every row
 // of a segment gets its exact top-m_out (fp32 chain) over the segment's rows (itself excluded),
-// written with output ids gid[] into row j of out_ids / out_dists.  A tensor-core screen (fp16
-// parts of the scaled rows, `parts` = 2: hi + lo) keeps every column within a proven margin of
-// the row's M-th; an exact rerank over the pool's f32 rows picks the list.  Segments of more
-// than 65 536 rows run as column chunks whose exact lists are merged.
+// written with output ids gid[] into row j of out_ids / out_dists.  A tensor-core screen on fp16
+// parts of the scaled rows keeps every column within a proven margin of the row's M-th; an exact
+// rerank over the pool's f32 rows picks the list.  `parts` = 2 stores hi and lo parts (the split
+// screen; rows with d >= 256 start on the hi part alone and return to the split in a wave that
+// rescans too many rows), 1 the hi part only.  Segments longer than an L2-sized column chunk run
+// as chunk waves whose exact lists are merged.
 struct ScreenProblem {
     const void* X = nullptr;
     int dtype = 0;                  // GTA_F32 / GTA_U8 / GTA_I8 (include/gta.h)

@@ -17,14 +17,19 @@
 //
 // Operands: each row x is scaled by a power of two S (exact; S = 2^floor(log2(2^15 / max ||x||)),
 // so every coordinate stays below 2^15) and split into fp16 parts hi = rn(S x) and
-// lo = rn(S x - hi).  kind::f16 MMAs form hi.hi + hi.lo + lo.hi (the dropped lo.lo and the
-// rounding of lo are below 3 * 2^-22 of |x||y|); with one part only hi.hi.  Products of fp16
+// lo = rn(S x - hi).  The split screen's kind::f16 MMAs form hi.hi + hi.lo + lo.hi (the dropped
+// lo.lo and the rounding of lo are below 3 * 2^-22 of |x||y|); the one-part screen forms hi.hi
+// alone (rounding 2^-10 per element, a wider margin, a third of the MMAs).  Products of fp16
 // values are exact in fp32, so the error left is the parts' rounding and the fp32
-// accumulation, both bounded in the margin.
+// accumulation, both bounded in the margin.  screen_knn picks the mode per wave (long rows
+// start one-part, a wave with many rescans hands the rest to the split screen).
+//
+// Long segments run as column chunks sized for the L2, in waves; a pilot wave seeds their rows
+// with an exact bound on the M-th distance, and each wave's lists tighten it (see screen_knn).
 //
 // CTA = 128 A rows against one bucket segment, one CTA per SM:
-//   warp 0      TMA producer: per K chunk of 64 fp16, the A and B parts (128 x 128 B each)
-//               into a 4-6 stage ring;
+//   warp 0      TMA producer: per K chunk of 64 fp16 (32 with the correction accumulator), the
+//               A and B parts into a 4-6 stage ring;
 //   warp 1      TMEM allocator (all 512 columns) + single-thread tcgen05.mma issuer into two
 //               128-column accumulators (column tile j+1 overlaps the epilogue of tile j);
 //   warps 2..5  epilogue: thread t owns TMEM lane t = A row t.  Scores of 16 columns at a time
