@@ -75,7 +75,9 @@ def test_place_pieces_splits_a_dominant_bucket_over_distinct_ranks():
 
 
 @pytest.mark.parametrize("world,counts,split", [(2, [1300, 1700], 1.0), (3, [1000, 1000, 1000], 1.0),
-                                                (2, [1300, 1700], 0.05), (3, [1000, 1000, 1000], 0.05)])
+                                                (2, [1300, 1700], 0.05), (3, [1000, 1000, 1000], 0.05),
+                                                (4, [700, 800, 750, 750], 0.05),
+                                                (8, [375] * 8, 0.05)])
 def test_sharded_build_matches_single_pipeline(world, counts, split):
     N, d, B, M, K, iters = sum(counts), 16, 8, 16, 8, 3
     X = _data(N, d, 20, seed=7)
@@ -101,8 +103,8 @@ def test_sharded_build_matches_single_pipeline(world, counts, split):
     for p in parts:
         np.testing.assert_array_equal(p["C"], ref["centroids"])
         np.testing.assert_array_equal(p["owner"], parts[0]["owner"])
-    assert len(set(parts[0]["owner"].tolist())) == world  # every rank owns buckets
     pcs = parts[0]["pieces"]
+    assert set(pcs[:, 1].tolist()) == set(range(world))  # every rank holds a piece of some bucket
     if split < 1.0:  # buckets cut into row ranges on several ranks
         assert len(pcs) > B
     np.testing.assert_array_equal(top2, ref["top2"])
