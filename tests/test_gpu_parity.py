@@ -277,7 +277,14 @@ def test_bucket_knn_f32_long_segment_column_chunks(N, d, M, edges, dup):
         X[idx] = base[rng.integers(0, 200, idx.size)] + rng.normal(0, 1e-4, (idx.size, d)).astype(np.float32)
     mem = np.arange(N, dtype=np.int32)
     off = np.array([0, N], np.int64)
+    from gta import _lib as GL
+    GL.profile_enable(True)
     gi, gd = gta.bucket_knn(dev(X), dev(mem), dev(off), M)
+    torch.cuda.synchronize()
+    stages = {rec[0] for rec in GL.profile_records()}
+    GL.profile_enable(False)
+    if dup:  # half the rows rescanned in wave 0: wave 1 ran the split screen
+        assert "dist_topk_bucket_split" in stages
     gi, gd = host(gi), host(gd)
     rows = np.concatenate([rng.choice(N, 200, replace=False), [0, 1, N - 1] + edges])
     ri = np.empty((len(rows), M), np.int32)
