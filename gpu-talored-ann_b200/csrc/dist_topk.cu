@@ -30,7 +30,7 @@
 //          directly.
 //   screen (f32 operands, kind::tf32): s is approximate with a proven error
 //          bound; the kernel keeps every column whose approximate s is within
-//          the bound of the running M-th, and rerank_kernel recomputes those
+//          the bound of the running M-th, and topk_rerank_kernel recomputes those
 //          candidates with the exact fp32 distance and selects the top-M.
 //
 // Reference behaviour this replaces (paths relative to the reference root):
@@ -1057,7 +1057,7 @@ __device__ __forceinline__ void warp_bitonic_sort(uint64_t* keys, int n, int lan
 }
 
 template <typename T>
-__global__ void __launch_bounds__(128) rerank_kernel(const RerankArgs p)
+__global__ void __launch_bounds__(128) topk_rerank_kernel(const RerankArgs p)
 {
     extern __shared__ uint8_t sm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -1334,10 +1334,10 @@ void dist_topk(const DistTopkProblem& pr, cudaStream_t st)
         r.out_ids = pr.out_ids; r.out_dists = pr.out_dists;
         const size_t smem = 4 * kSortMax * sizeof(uint64_t) + 4 * static_cast<size_t>(pr.d_pad) * sizeof(float);
         GTA_REQUIRE(smem <= kSmemMax, kInvalid, "rerank: dimension too large");
-        GTA_CUDA(cudaFuncSetAttribute(rerank_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        GTA_CUDA(cudaFuncSetAttribute(topk_rerank_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                       static_cast<int>(smem)));
         ProfScope prof("rerank", 0.0, st);
-        rerank_kernel<float><<<pr.n_work, 128, smem, st>>>(r);
+        topk_rerank_kernel<float><<<pr.n_work, 128, smem, st>>>(r);
         count_launches(1);
         GTA_CUDA(cudaGetLastError());
     }
