@@ -481,7 +481,8 @@ void bucket_knn_impl(const void* X, int dtype, int64_t n, int d, const int32_t* 
 struct HostRows {
     const void* dev = nullptr;
     void* reg = nullptr;  // the registered page range (ours to unregister), or null
-    HostRows(const void* data, size_t bytes)
+    cudaStream_t st;      // the stream whose kernels read the rows
+    HostRows(const void* data, size_t bytes, cudaStream_t stream) : st(stream)
     {
         const long page = sysconf(_SC_PAGESIZE) > 0 ? sysconf(_SC_PAGESIZE) : 4096;
         const uintptr_t b = reinterpret_cast<uintptr_t>(data) & ~static_cast<uintptr_t>(page - 1);
@@ -502,7 +503,12 @@ struct HostRows {
     }
     ~HostRows()
     {
-        if (reg) (void)cudaHostUnregister(reg);
+        // an error thrown between launches leaves kernels that read the mapping in flight: they
+        // finish before the pages are unregistered (the normal path has synchronized already)
+        if (reg) {
+            (void)cudaStreamSynchronize(st);
+            (void)cudaHostUnregister(reg);
+        }
     }
     HostRows(const HostRows&) = delete;
     HostRows& operator=(const HostRows&) = delete;
@@ -542,7 +548,7 @@ void build_bucket_round(const gta_dataset& ds, const gta_bucket_params& p, const
     const size_t xbytes = static_cast<size_t>(N) * d * elem_size(ds.dtype);
     std::unique_ptr<HostRows> xhost;
     if (ds.on_device == 2) {
-        xhost = std::make_unique<HostRows>(ds.data, xbytes);
+        xhost = std::make_unique<HostRows>(ds.data, xbytes, st);
         X = xhost->dev;
     } else if (!ds.on_device) {
         xhold = DevBuf<uint8_t>(xbytes, st);
