@@ -403,13 +403,18 @@ def build_sharded(X_local: torch.Tensor, prm: ShardParams, stages=None, init_cen
     Xf = st.gather_rows(X_local, row0, gid_local)
     top2 = st.assign_topk(Xf, C, 2, int_rows).contiguous()
     del Xf
-    if n_local and not bool(((top2 >= 0) & (top2 < B)).all()):
-        raise L.GtaError(L.GTA_EDATA, "build_sharded: a row has no valid bucket (non-finite input?)")
 
-    # ---- 3. placement
-    sizes = torch.bincount(top2.reshape(-1).long(), minlength=B).to(torch.int64)
+    # ---- 3. placement.  The count of memberships without a valid bucket (a non-finite row) rides
+    # on the sizes' all-reduce, so every rank raises together rather than one rank leaving the
+    # others waiting in the next collective.
+    flat = top2.reshape(-1).long()
+    ok = (flat >= 0) & (flat < B)
+    sizes = torch.cat([torch.bincount(flat[ok], minlength=B).to(torch.int64),
+                       (~ok).sum().reshape(1).to(torch.int64)])
     dist.all_reduce(sizes, group=group)
     sizes_l = sizes.tolist()
+    if sizes_l.pop() > 0:
+        raise L.GtaError(L.GTA_EDATA, "build_sharded: a row has no valid bucket (non-finite input?)")
     pieces = place_pieces(sizes_l, world, prm.split_share)
     holders = [0] * B
     row_lo, row_hi = [0] * B, [0] * B

@@ -217,6 +217,38 @@ def gloo_worker(rank, world, port, X, counts, C0, prm_kw, out_dir):
         dist.destroy_process_group()
 
 
+class _BadBucketStages(OracleStages):
+    """OracleStages whose top-2 pass leaves one membership of its first row without a bucket (what
+    a non-finite row gives): a data fault made on the host, on one rank only."""
+
+    def assign_topk(self, Xf, C, k, integer_rows=False):
+        out = super().assign_topk(Xf, C, k, integer_rows)
+        if k == 2 and out.shape[0]:
+            out[0, 1] = -1
+        return out
+
+
+def gloo_fault_worker(rank, world, port, X, counts, C0, prm_kw, bad_rank, out_dir):
+    """One CPU rank of a build where rank ``bad_rank`` meets a row without a bucket: records the
+    status each rank's build_sharded raised (every rank must raise, none may wait in a collective)."""
+    import gta.dist as gd
+    from gta import _lib as L
+
+    _init(rank, world, port, "gloo")
+    try:
+        row0 = int(sum(counts[:rank]))
+        Xl = torch.from_numpy(np.ascontiguousarray(X[row0:row0 + counts[rank]]))
+        stages = _BadBucketStages() if rank == bad_rank else OracleStages()
+        status = 0
+        try:
+            gd.build_sharded(Xl, gd.ShardParams(**prm_kw), stages=stages, init_centroids=torch.from_numpy(C0))
+        except L.GtaError as e:
+            status = e.code
+        np.save(os.path.join(out_dir, f"rank{rank}.npy"), np.array([status]))
+    finally:
+        dist.destroy_process_group()
+
+
 def nccl_worker(rank, world, port, X, prm_kw, out_dir):
     """One GPU rank: build_sharded with the libgta stages; saves its results."""
     import gta.dist as gd

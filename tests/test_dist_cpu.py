@@ -1,4 +1,4 @@
-"""The sharded (multi-GPU) build's host logic on CPU ranks (gloo, world 2 and 3).
+"""The sharded (multi-GPU) build's host logic on CPU ranks (gloo, worlds 2 to 8).
 
 Every per-rank computation is done by the CPU oracle (tests/dist_helpers.py), so
 these tests check what the driver in gta/dist.py adds: row ranges, bucket
@@ -8,6 +8,7 @@ tables.  The concatenated per-rank results must equal the single-process oracle
 pipeline bit for bit (u8 data, so the fp64 centroid sums are exact)."""
 import socket
 import tempfile
+import time
 
 import numpy as np
 import pytest
@@ -111,3 +112,20 @@ def test_sharded_build_matches_single_pipeline(world, counts, split):
     np.testing.assert_array_equal(ids, ref["knn_ids"])
     np.testing.assert_array_equal(dists, ref["knn_dists"])
     np.testing.assert_array_equal(graph, g_ref)
+
+
+def test_bad_bucket_on_one_rank_raises_on_every_rank():
+    """A row without a valid bucket on one rank (a fault made on the host) ends the build with
+    status 5 (data check failed) on every rank, promptly: the flag rides on the bucket sizes'
+    all-reduce, so no rank is left waiting in a later collective for the process-group timeout."""
+    world, counts, B = 3, [400, 500, 600], 6
+    X = _data(sum(counts), 16, 12, seed=9)
+    C0 = X[np.random.default_rng(2).choice(sum(counts), B, replace=False)].astype(np.float32)
+    prm = dict(n_buckets=B, knn_degree=8, graph_degree=0, kmeans_iters=1, kmeans_sample=0, seed=42)
+    t0 = time.monotonic()
+    with tempfile.TemporaryDirectory() as out:
+        mp.start_processes(dist_helpers.gloo_fault_worker, args=(world, _free_port(), X, counts, C0, prm, 1, out),
+                           nprocs=world, join=True, start_method="spawn")
+        status = [int(np.load(f"{out}/rank{r}.npy")[0]) for r in range(world)]
+    assert status == [5] * world
+    assert time.monotonic() - t0 < 90  # well under the 120 s process-group timeout
