@@ -75,6 +75,35 @@ def test_place_pieces_splits_a_dominant_bucket_over_distinct_ranks():
     assert [(p[2], p[3]) for p in gd.place_pieces([200, 10], 4) if p[0] == 0] == [(0, 200)]
 
 
+def test_place_pieces_properties():
+    """For any sizes, ranks and split share: every bucket's pieces tile [0, n) in order, sit on
+    distinct ranks, are cut at multiples of 128 and are non-empty (a bucket of n > 0 rows); the
+    placement is the same on every call."""
+    hyp = pytest.importorskip("hypothesis")
+    st = hyp.strategies
+
+    @hyp.settings(max_examples=300, deadline=None)
+    @hyp.given(sizes=st.lists(st.integers(0, 3000), min_size=1, max_size=40), world=st.integers(1, 8),
+               share=st.sampled_from([0.01, 0.1, 0.5, 1.0, float("inf")]))
+    def check(sizes, world, share):
+        pcs = gd.place_pieces(sizes, world, share)
+        assert pcs == gd.place_pieces(sizes, world, share)
+        assert pcs == sorted(pcs, key=lambda p: (p[0], p[2]))
+        for b, n in enumerate(sizes):
+            mine = [p for p in pcs if p[0] == b]
+            assert mine and mine[0][2] == 0 and mine[-1][3] == n
+            assert all(a[3] == c[2] for a, c in zip(mine, mine[1:]))
+            assert len({p[1] for p in mine}) == len(mine) <= world
+            assert all(0 <= p[1] < world for p in mine)
+            assert all(p[2] % 128 == 0 for p in mine)
+            if n > 0:
+                assert all(p[3] > p[2] for p in mine)
+            if world == 1 or share == float("inf") or n < 256:
+                assert len(mine) == 1
+
+    check()
+
+
 @pytest.mark.parametrize("world,counts,split", [(2, [1300, 1700], 1.0), (3, [1000, 1000, 1000], 1.0),
                                                 (2, [1300, 1700], 0.05), (3, [1000, 1000, 1000], 0.05),
                                                 (4, [700, 800, 750, 750], 0.05),
