@@ -50,6 +50,7 @@
 #include <algorithm>
 #include <cfloat>
 #include <cmath>
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -1201,10 +1202,8 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         while (kChunk > 4096 && kChunk * row_bytes > room) kChunk >>= 1;
     }
     std::vector<std::vector<WorkItem>> waves(1);
-    std::vector<double> wave_flops(1, 0.0);
     std::vector<ChunkSeg> chunked;
     std::vector<WorkItem> pilot;  // seeds of the chunked rows (one item per row tile)
-    double pilot_flops = 0.0;
     constexpr int64_t kPilot = 4096;
     int64_t ext_rows = 0, chunked_rows = 0;
     GTA_REQUIRE((pr.seg_r0.empty() && pr.seg_r1.empty()) ||
@@ -1225,15 +1224,11 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
                 waves[0].push_back(WorkItem{static_cast<int32_t>(lo + t), static_cast<int32_t>(std::min<int64_t>(128, r1 - t)),
                                             static_cast<int32_t>(lo), static_cast<int32_t>(nb), static_cast<int32_t>(t),
                                             static_cast<int32_t>(lo + t), 1, -1});
-            wave_flops[0] += 2.0 * static_cast<double>(nr) * static_cast<double>(nb) * pr.d;
             continue;
         }
         const int64_t base = pr.n_rows + ext_rows;
         chunked.push_back(ChunkSeg{lo + r0, nr, ext_rows, chunked_rows, nch, 0});
-        if (static_cast<int>(waves.size()) < nch) {
-            waves.resize(static_cast<size_t>(nch));
-            wave_flops.resize(static_cast<size_t>(nch), 0.0);
-        }
+        if (static_cast<int>(waves.size()) < nch) waves.resize(static_cast<size_t>(nch));
         // the pilot: each row tile against a window of kPilot columns around its own tile (rows
         // of a bucket are grouped by their other bucket, so the window holds points of the same
         // region); the exact M-th distance over its first M candidates seeds every chunk
@@ -1245,7 +1240,6 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
                                      static_cast<int32_t>(t - ws), static_cast<int32_t>(base + nr + (t - r0)), 1,
                                      static_cast<int32_t>(chunked_rows + (t - r0))});
         }
-        pilot_flops += 2.0 * static_cast<double>(nr) * static_cast<double>(W) * pr.d;
         for (int k = 0; k < nch; ++k) {
             const int64_t c0 = k * kChunk, cn = std::min<int64_t>(kChunk, nb - c0);
             for (int64_t t = r0; t < r1; t += 128)
@@ -1254,10 +1248,32 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
                              static_cast<int32_t>(lo + c0), static_cast<int32_t>(cn), static_cast<int32_t>(t - c0),
                              static_cast<int32_t>(base + (k == 0 ? 0 : nr) + (t - r0)), k == 0 ? 1 : 3,
                              static_cast<int32_t>(chunked_rows + (t - r0))});
-            wave_flops[static_cast<size_t>(k)] += 2.0 * static_cast<double>(nr) * static_cast<double>(cn) * pr.d;
         }
         ext_rows += 2 * nr;
         chunked_rows += nr;
+    }
+    // per wave: the chunk whose lists its merge step takes (-1: none), and whether it runs the
+    // split screen whatever the current mode
+    std::vector<int> wave_chunk(waves.size());
+    for (size_t k = 0; k < waves.size(); ++k) wave_chunk[k] = static_cast<int>(k);
+    std::vector<char> wave_split(waves.size(), 0);
+    // GTA_SCREEN_UNSEEDED_SPLIT=1 (off by default): the rows of segments shorter than a chunk have
+    // no seed, so under the one-part margin their full lists admit many columns and often a
+    // rescan; with the option they run as a wave of their own on the split screen (as the pilot
+    // does), before chunk 0 of the long segments
+    static const bool unseeded_split = [] {
+        const char* e = std::getenv("GTA_SCREEN_UNSEEDED_SPLIT");
+        return e != nullptr && e[0] == '1';
+    }();
+    if (unseeded_split && pr.parts == 2 && pr.d >= 256) {
+        std::vector<WorkItem> unseeded, seeded;
+        for (const WorkItem& it : waves[0]) (it.pad2 < 0 ? unseeded : seeded).push_back(it);
+        if (!unseeded.empty()) {
+            waves[0] = std::move(seeded);
+            waves.insert(waves.begin(), std::move(unseeded));
+            wave_chunk.insert(wave_chunk.begin(), -1);
+            wave_split.insert(wave_split.begin(), 1);
+        }
     }
     const int64_t item_rows = pr.n_rows + ext_rows;
     GTA_REQUIRE(item_rows < (1ll << 31), kInvalid, "screen: too many list rows");
@@ -1391,6 +1407,9 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         const size_t wk = pilot.empty() ? k : k - 1;
         const std::vector<WorkItem>& items = is_pilot ? pilot : waves[wk];
         if (items.empty()) continue;
+        const bool force_split = is_pilot ? true : wave_split[wk] != 0;
+        double flops = 0.0;  // algorithmic: 2 d per (row, column) pair
+        for (const WorkItem& it : items) flops += 2.0 * it.a_rows * static_cast<double>(it.b_rows) * pr.d;
         // the screen's items (the pilot's unseeded: its rerank groups carry the seed slots)
         std::vector<WorkItem> launch(items);
         if (is_pilot)
@@ -1401,7 +1420,7 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         a.work = work.get();
         // the pilot's rows are unseeded: under the one-part margin they admit many more keys (slow
         // list merges), so it runs the split screen when there is one (its windows are short)
-        const Mode& md = modes[is_pilot && split_mode >= 0 ? split_mode : cur];
+        const Mode& md = modes[force_split && split_mode >= 0 ? split_mode : cur];
         a.k_chunks = md.k_chunks;
         a.stages = md.pl.stages;
         a.buf_off = md.pl.buf_off;
@@ -1413,7 +1432,7 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         {
             // split waves are named apart (three issued products per element against one)
             const std::string pname = std::string(is_pilot ? "screen_pilot" : pr.prof_name) + (md.split ? "_split" : "");
-            ProfScope prof(pname.c_str(), is_pilot ? pilot_flops : wave_flops[wk], st);
+            ProfScope prof(pname.c_str(), flops, st);
             a.stats = prof.counters(8);
             const int n_work = static_cast<int>(launch.size());
             const uint32_t smem = md.pl.total;
@@ -1454,7 +1473,7 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
             count_launches(1);
             GTA_CUDA(cudaGetLastError());
         }
-        if (split_mode >= 0 && cur != split_mode && wk + 1 < waves.size()) {
+        if (split_mode >= 0 && cur != split_mode && !wave_split[wk] && wk + 1 < waves.size()) {
             // too many rescans under the one-part margin: the remaining waves screen split
             unsigned n_rs = 0;
             GTA_CUDA(cudaMemcpyAsync(&n_rs, n_rescan.get(), sizeof(unsigned), cudaMemcpyDeviceToHost, st));
@@ -1463,11 +1482,11 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
             for (const WorkItem& it : items) wave_rows += it.a_rows;
             if (static_cast<double>(n_rs) > 0.05 * static_cast<double>(wave_rows)) cur = split_mode;
         }
-        if (!chunked.empty()) {
+        if (!chunked.empty() && wave_chunk[wk] >= 0) {
             // chunk k into the running lists (k = 0: the seeds of chunk 0's lists)
             ProfScope prof("merge_chunks", 24.0 * pr.m_out * static_cast<double>(chunked_rows), st);
             merge_step_kernel<<<merge_grid, kRrWarps * 32, 0, st>>>(segs.get(), static_cast<int>(chunked.size()),
-                                                                    chunked_rows, static_cast<int>(wk), ext_ids.get(),
+                                                                    chunked_rows, wave_chunk[wk], ext_ids.get(),
                                                                     ext_dists.get(), pr.m_out, seeds.get(), pr.out_ids,
                                                                     pr.out_dists);
             count_launches(1);
