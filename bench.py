@@ -297,27 +297,35 @@ SEARCH_QUERIES = 2000
 SEARCH_SAMPLES = 16384
 
 
-def exact_knn(Xall, Xq, k: int, exclude=None) -> np.ndarray:
-    """Exact k nearest rows of ``Xall`` (device) for each row of ``Xq``, fp64 on the GPU;
-    ``exclude[i]`` (a row index of Xall) is left out of query i's answer."""
+def exact_knn(Xall, Xq, k: int, exclude=None, q_chunk: int = 2048, col_chunk: int = 1 << 18) -> np.ndarray:
+    """Exact k nearest rows of ``Xall`` for each row of ``Xq`` (fp64, on the tensors' device);
+    ``exclude[i]`` (a row index of Xall) is left out of query i's answer.  Queries run in blocks
+    of ``q_chunk`` against column blocks of ``col_chunk`` rows (bounded scratch)."""
     import torch
 
-    Xq = Xq.double()
-    best = []
-    for c0 in range(0, Xall.shape[0], 1 << 18):
-        Xc = Xall[c0:c0 + (1 << 18)].double()
-        dd = (Xq * Xq).sum(1, keepdim=True) + (Xc * Xc).sum(1)[None, :] - 2.0 * Xq @ Xc.T
-        if exclude is not None:
-            idx = torch.arange(c0, c0 + Xc.shape[0], device="cuda")
-            dd[exclude[:, None] == idx[None, :]] = float("inf")
-        v, i = torch.topk(dd, k, dim=1, largest=False)
-        best.append((v, i + c0))
-    v = torch.cat([b[0] for b in best], 1)
-    i = torch.cat([b[1] for b in best], 1)
-    return torch.gather(i, 1, torch.topk(v, k, dim=1, largest=False).indices).cpu().numpy()
+    out = []
+    for q0 in range(0, Xq.shape[0], q_chunk):
+        xq = Xq[q0:q0 + q_chunk].double()
+        ex = None if exclude is None else exclude[q0:q0 + q_chunk]
+        vals, idxs = [], []
+        for c0 in range(0, Xall.shape[0], col_chunk):
+            Xc = Xall[c0:c0 + col_chunk].double()
+            dd = (xq * xq).sum(1, keepdim=True) + (Xc * Xc).sum(1)[None, :] - 2.0 * xq @ Xc.T
+            if ex is not None:
+                idx = torch.arange(c0, c0 + Xc.shape[0], device=Xc.device)
+                dd[ex[:, None] == idx[None, :]] = float("inf")
+            v, i = torch.topk(dd, min(k, Xc.shape[0]), dim=1, largest=False)
+            vals.append(v)
+            idxs.append(i + c0)
+        v = torch.cat(vals, 1)
+        i = torch.cat(idxs, 1)
+        out.append(torch.gather(i, 1, torch.topk(v, k, dim=1, largest=False).indices).cpu().numpy())
+    return np.concatenate(out) if out else np.empty((0, k), np.int64)
 
 
 DEFAULT_CONFIG = "c3"
+# recall@32 of the kNN lists is measured on this many sampled points (exact ground truth for those)
+RECALL_POINTS = 10000
 # stage names whose work unit is flops (the rest count bytes; "search" counts queries)
 FLOP_STAGES = ("dist_topk", "assign_exact", "screen_pilot")
 
@@ -565,7 +573,7 @@ def main():
     if world > 1:
         skew["split_buckets"] = {str(b): c for b, c in sorted(split.items())}  # bucket -> ranks sharing it
 
-    # quality: recall@32 of the pre-prune kNN graph on 1000 sampled points of rank 0's rows
+    # quality: recall@32 of the pre-prune kNN graph on RECALL_POINTS sampled points of rank 0's rows
     # (exact GT over the whole job's dataset in fp64 on the GPU)
     recall = None
     if world == 1:
@@ -582,10 +590,11 @@ def main():
     search_q = None
     if rank == 0:
         # points of rank 0's row block (global ids 0 .. its rows - 1)
-        q = torch.from_numpy(np.random.default_rng(0).choice(X.shape[0], 1000, replace=False)).cuda()
+        n_q = min(RECALL_POINTS, X.shape[0])
+        q = torch.from_numpy(np.random.default_rng(0).choice(X.shape[0], n_q, replace=False)).cuda()
         gt = exact_knn(Xall, Xall[q], 32, exclude=q)
         approx = ids[q].cpu().numpy()[:, :32]
-        recall = float(np.mean([len(np.intersect1d(approx[r], gt[r])) / 32.0 for r in range(1000)]))
+        recall = float(np.mean([len(np.intersect1d(approx[r], gt[r])) / 32.0 for r in range(n_q)]))
     parity = None
     if rank == 0 and world == 1 and not args.no_parity:
         # the build's own lists at full size against the oracle pipeline on 500 of the sampled points
@@ -631,7 +640,7 @@ def main():
         approx = rids[q].cpu().numpy()[:, :32]
         ref_bucketing = {"centroid_ratio": 0.01, "nprobe": 32, "ms": rms, "value": cfg.n / (rms / 1e3) / 1e6,
                          "unit": UNIT, "recall_at_32": float(np.mean([len(np.intersect1d(approx[r], gt[r])) / 32.0
-                                                                      for r in range(1000)])),
+                                                                      for r in range(n_q)])),
                          "stage": "kNN lists only (no CAGRA optimize)"}
     del Xall, g_all
 
@@ -690,7 +699,8 @@ def main():
                 "vs_baseline": None, "dtype": _compute_dtype(cfg),
                 "data": "synthetic (seeded Gaussian mixture)", "config": config, "roofline": roofline,
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches,
-                "clocks": clocks, "recall_at_32": recall, "parity": parity, "search": search_q, "reference_bucketing": ref_bucketing, "bucket_skew": skew, "phases_ms_max_over_ranks": phases,
+                "clocks": clocks, "recall_at_32": recall,
+                "recall_points": n_q if rank == 0 else None, "parity": parity, "search": search_q, "reference_bucketing": ref_bucketing, "bucket_skew": skew, "phases_ms_max_over_ranks": phases,
                 "stages": stage_summary,
                 "instrumented_ms_per_step": step_ms_sum}
         print(json.dumps(line))
