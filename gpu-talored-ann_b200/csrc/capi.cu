@@ -1691,6 +1691,29 @@ int gta_build_memberships(const int32_t* top2, int64_t n, int32_t B, int32_t* me
     });
 }
 
+namespace {
+// The membership CSR a stage entry point was given, checked before any kernel reads a row
+// through it: the offsets (device, B + 1) copied to the host, non-decreasing from >= 0 and
+// covering at most max_entries slots, and the row ids of those slots inside [0, n_rows).
+std::vector<int64_t> checked_csr(const int32_t* ids, const int64_t* offsets_dev, int32_t B, int64_t max_entries,
+                                 int64_t n_rows, int* err, cudaStream_t st, const char* who)
+{
+    GTA_REQUIRE(n_rows >= 0 && n_rows < (1ll << 31), kInvalid, std::string(who) + ": row count out of range");
+    std::vector<int64_t> off(static_cast<size_t>(B) + 1);
+    GTA_CUDA(cudaMemcpyAsync(off.data(), offsets_dev, sizeof(int64_t) * off.size(), cudaMemcpyDeviceToHost, st));
+    GTA_CUDA(cudaStreamSynchronize(st));
+    GTA_REQUIRE(off[0] >= 0, kData, std::string(who) + ": negative offset");
+    for (int32_t b = 0; b < B; ++b)
+        GTA_REQUIRE(off[b] <= off[b + 1], kData, std::string(who) + ": offsets must be non-decreasing");
+    GTA_REQUIRE(off[B] <= max_entries, kData, std::string(who) + ": offsets cover more slots than the rows allow");
+    if (off[B] > off[0]) {
+        check_ids(ids + off[0], off[B] - off[0], static_cast<int32_t>(n_rows), err, st);
+        check_device_error(err, st, who);
+    }
+    return off;
+}
+}  // namespace
+
 int gta_bucket_knn(const void* X, int32_t dtype, int64_t n, int32_t d, const int32_t* members, const int64_t* offsets,
                    int32_t B, int32_t M, int32_t* list_ids, float* list_dists, void* stream)
 {
@@ -1701,7 +1724,10 @@ int gta_bucket_knn(const void* X, int32_t dtype, int64_t n, int32_t d, const int
         cudaStream_t st = S(stream);
         DevBuf<int> err(1, st);
         GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
-        bucket_knn_impl(X, dtype, n, d, members, offsets, B, M, list_ids, list_dists, err.get(), st);
+        // at most two memberships per point (the 2-way CSR of gta_build_memberships)
+        const std::vector<int64_t> off = checked_csr(members, offsets, B, 2 * n, n, err.get(), st, "gta_bucket_knn");
+        bucket_knn_impl(X, dtype, n, d, members, offsets, B, M, list_ids, list_dists, err.get(), st, nullptr, 0, -1,
+                        off.data());
         check_device_error(err.get(), st, "gta_bucket_knn");
     });
 }
@@ -1929,9 +1955,12 @@ int gta_bucket_knn_rows(const void* R, int32_t dtype, int64_t n, int32_t d, cons
         cudaStream_t st = S(stream);
         DevBuf<int> err(1, st);
         GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+        // order: each received row once, grouped by bucket
+        const std::vector<int64_t> off = checked_csr(order, offsets, B, n, n, err.get(), st, "gta_bucket_knn_rows");
         DevBuf<int32_t> gid_sorted(static_cast<size_t>(n), st);
         gather_i32(gid, order, n, gid_sorted.get(), st);
-        bucket_knn_impl(R, dtype, n, d, order, offsets, B, M, list_ids, list_dists, err.get(), st, gid_sorted.get());
+        bucket_knn_impl(R, dtype, n, d, order, offsets, B, M, list_ids, list_dists, err.get(), st, gid_sorted.get(), 0,
+                        -1, off.data());
         check_device_error(err.get(), st, "gta_bucket_knn_rows");
     });
 }
@@ -1947,11 +1976,11 @@ void bucket_knn_rows_seeded(const void* R, int32_t dtype, int64_t n, int32_t d, 
                     (phase == 1 || n == 0 || seed) && (row_lo == nullptr) == (row_hi == nullptr),
                 kInvalid, std::string(who) + ": bad argument");
     if (n == 0) return;
-    std::vector<int64_t> off;
+    DevBuf<int> err(1, st);
+    GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
+    // order: each received row once, grouped by bucket
+    const std::vector<int64_t> off = checked_csr(order, offsets, B, n, n, err.get(), st, who);
     if (row_lo) {
-        off.resize(static_cast<size_t>(B) + 1);
-        GTA_CUDA(cudaMemcpyAsync(off.data(), offsets, sizeof(int64_t) * (B + 1), cudaMemcpyDeviceToHost, st));
-        GTA_CUDA(cudaStreamSynchronize(st));
         for (int b = 0; b < B; ++b)
             GTA_REQUIRE(0 <= row_lo[b] && row_lo[b] <= row_hi[b] && row_hi[b] <= off[b + 1] - off[b], kInvalid,
                         std::string(who) + ": row range outside its bucket");
@@ -1959,8 +1988,6 @@ void bucket_knn_rows_seeded(const void* R, int32_t dtype, int64_t n, int32_t d, 
     const int elem = knn_elem(dtype, d, M);
     const bool seedable = dist_topk_seedable(elem, pad_dim(d, elem), M);
     if (!seedable && phase == 2) return;  // phase 1 wrote every row
-    DevBuf<int> err(1, st);
-    GTA_CUDA(cudaMemsetAsync(err.get(), 0, sizeof(int), st));
     DevBuf<int32_t> gid_sorted(static_cast<size_t>(n), st);
     gather_i32(gid, order, n, gid_sorted.get(), st);
     KnnPhase ph;
@@ -1976,7 +2003,7 @@ void bucket_knn_rows_seeded(const void* R, int32_t dtype, int64_t n, int32_t d, 
     ph.row_lo = row_lo;
     ph.row_hi = row_hi;
     bucket_knn_impl(R, dtype, n, d, order, offsets, B, M, list_ids, list_dists, err.get(), st, gid_sorted.get(), 0, -1,
-                    off.empty() ? nullptr : off.data(), ph);
+                    off.data(), ph);
     check_device_error(err.get(), st, who);
 }
 }  // namespace

@@ -423,6 +423,25 @@ def test_reverse_merge_refuses_out_of_range_neighbours():
     assert e.value.code == 5
 
 
+def test_bucket_knn_refuses_a_bad_membership_csr():
+    """A membership id outside [0, n) or offsets that decrease are a data error (status 5), found
+    before any kernel reads a row through them."""
+    rng = np.random.default_rng(11)
+    X = rng.normal(size=(300, 16)).astype(np.float32)
+    mem = np.arange(300, dtype=np.int32)
+    off = np.array([0, 100, 300], np.int64)
+    gi, _ = gta.bucket_knn(dev(X), dev(mem), dev(off), 8)   # the valid CSR runs
+    assert (host(gi) >= 0).all()
+    bad = mem.copy()
+    bad[150] = 300                                          # one past the last row
+    with pytest.raises(gta.GtaError) as e:
+        gta.bucket_knn(dev(X), dev(bad), dev(off), 8)
+    assert e.value.code == 5
+    with pytest.raises(gta.GtaError) as e:
+        gta.bucket_knn(dev(X), dev(mem), dev(np.array([0, 200, 100], np.int64)), 8)
+    assert e.value.code == 5
+
+
 @pytest.mark.parametrize("N,K,hubs", [(4000, 32, 3), (3000, 64, 2), (2000, 100, 2), (5000, 1, 1), (900, 5, 4)])
 def test_reverse_merge_random_graphs_with_repeats_vs_oracle(N, K, hubs):
     """Random pruned-graph-shaped inputs with repeated ids inside rows (sanitized padding) and hub
