@@ -377,8 +377,8 @@ def main():
                               "row ranges on several ranks (NCCL all-reduce / all-to-all / all-gather)"
                               if world > 1 else "1 GPU"),
               "shards": "one seeded mixture; rank r holds its contiguous block of N/W rows (strong scaling)"}
-    if os.environ.get("GTA_SCREEN_UNSEEDED_SPLIT", "") == "1":
-        config["screen_unseeded_split"] = True  # the library option is on for this run
+    if os.environ.get("GTA_SCREEN_UNSEEDED_SPLIT", "").startswith("0"):
+        config["screen_unseeded_split"] = False  # the library option is off for this run
 
     if args.impl == "reference":
         if rank != 0:

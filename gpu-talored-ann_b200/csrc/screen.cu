@@ -1257,13 +1257,14 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     std::vector<int> wave_chunk(waves.size());
     for (size_t k = 0; k < waves.size(); ++k) wave_chunk[k] = static_cast<int>(k);
     std::vector<char> wave_split(waves.size(), 0);
-    // GTA_SCREEN_UNSEEDED_SPLIT=1 (off by default): the rows of segments shorter than a chunk have
-    // no seed, so under the one-part margin their full lists admit many columns and often a
-    // rescan; with the option they run as a wave of their own on the split screen (as the pilot
-    // does), before chunk 0 of the long segments
+    // The rows of segments shorter than a chunk have no seed: under the one-part margin their full
+    // lists admit many columns and often a rescan (C3: 81 ms of rerank and 96 ms of rescans for
+    // 6 597 row tiles), against about 10 exact keys per row and no rescan under the split margin.
+    // So they run as a wave of their own on the split screen (as the pilot does), before chunk 0
+    // of the long segments; GTA_SCREEN_UNSEEDED_SPLIT=0 keeps them in wave 0 on the current mode.
     static const bool unseeded_split = [] {
         const char* e = std::getenv("GTA_SCREEN_UNSEEDED_SPLIT");
-        return e != nullptr && e[0] == '1';
+        return e == nullptr || e[0] != '0';
     }();
     if (unseeded_split && pr.parts == 2 && pr.d >= 256) {
         std::vector<WorkItem> unseeded, seeded;
@@ -1418,8 +1419,8 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         // pageable sources: each copy is staged before cudaMemcpyAsync returns
         GTA_CUDA(cudaMemcpyAsync(work.get(), launch.data(), sizeof(WorkItem) * launch.size(), cudaMemcpyHostToDevice, st));
         a.work = work.get();
-        // the pilot's rows are unseeded: under the one-part margin they admit many more keys (slow
-        // list merges), so it runs the split screen when there is one (its windows are short)
+        // unseeded rows (the pilot's, the short segments') admit many more keys under the one-part
+        // margin (slow list merges, more exact keys, rescans): they run the split screen
         const Mode& md = modes[force_split && split_mode >= 0 ? split_mode : cur];
         a.k_chunks = md.k_chunks;
         a.stages = md.pl.stages;
