@@ -508,7 +508,8 @@ def main():
             elif cd in ("f16", "f16x3"):
                 issued = s["issued"] / s["units"] if s["units"] > 0 else 1.0
                 roofline["kernel_detail"] = ("screen_kernel: kind::f16 on scaled fp16 rows, one product per element "
-                                             "(hi.hi), three (hi/lo split) in the waves that fall back to the split")
+                                             "(hi.hi) in the seeded chunk waves, three (hi/lo split) for unseeded rows "
+                                             "and in the waves that fall back to the split")
                 roofline["mma_issued_per_algorithmic"] = issued
                 roofline["frac_issued"] = issued * achieved / tflops
                 roofline["note"] = ("algorithmic flops (sum 2 n_b^2 d, once) per second of the screen launches; "
