@@ -80,10 +80,15 @@ def _compute_dtype(cfg) -> str:
 # DRAM bytes (read + write) per launch of the dominant stage's kernel, averaged over the launches
 # of one build, from the committed one-pass ncu launch list of the same command and workload
 # (`dram__bytes_read.sum + dram__bytes_write.sum`, profiles/launches_*.md):
-# {(stage, config, N): (bytes per launch, source)}.
+# {(stage, config, N, unseeded rows on the split screen): (bytes per launch, source)}.
 TRAFFIC_PER_LAUNCH = {
-    ("dist_topk_bucket", "c3", 1000000): (2.104e10, "profiles/launches_c3_bench.md"),
+    ("dist_topk_bucket", "c3", 1000000, False): (2.104e10, "profiles/launches_c3_bench.md"),
 }
+
+
+def _unseeded_split() -> bool:
+    """The library's screen option for rows without a seed (on unless GTA_SCREEN_UNSEEDED_SPLIT=0)."""
+    return not os.environ.get("GTA_SCREEN_UNSEEDED_SPLIT", "").startswith("0")
 
 
 # ---------------------------------------------------------------- clocks
@@ -377,7 +382,7 @@ def main():
                               "row ranges on several ranks (NCCL all-reduce / all-to-all / all-gather)"
                               if world > 1 else "1 GPU"),
               "shards": "one seeded mixture; rank r holds its contiguous block of N/W rows (strong scaling)"}
-    if os.environ.get("GTA_SCREEN_UNSEEDED_SPLIT", "").startswith("0"):
+    if not _unseeded_split():
         config["screen_unseeded_split"] = False  # the library option is off for this run
 
     if args.impl == "reference":
@@ -520,11 +525,15 @@ def main():
             achieved = per_launch_units / per_launch_s / 1e9
             roofline = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
                         "frac": achieved / hbm, "peak_source": f"{peak_src} HBM copy"}
-        # DRAM bytes of one launch, from the committed capture of this workload (None elsewhere)
-        tpl = TRAFFIC_PER_LAUNCH.get((dom, args.config, cfg.n))
+        # DRAM bytes of one launch, from the committed capture of this workload and screen
+        # configuration (None elsewhere)
+        tpl = TRAFFIC_PER_LAUNCH.get((dom, args.config, cfg.n, _unseeded_split()))
         roofline["traffic"] = tpl[0] if tpl else None
         if tpl:
             roofline["traffic_source"] = tpl[1]
+        elif any(k[:3] == (dom, args.config, cfg.n) for k in TRAFFIC_PER_LAUNCH):
+            roofline["traffic_note"] = ("the committed capture of this workload ran the unseeded rows on the one-part "
+                                        "screen (GTA_SCREEN_UNSEEDED_SPLIT=0); none yet of this configuration")
     step_ms_sum = sum(s["ms"] for k, s in stages.items() if not k.endswith("_total")) / args.steps
     stage_summary = {k: {"ms_per_step": v["ms"] / args.steps, "launches_per_step": v["launches"] / args.steps,
                          "share": v["ms"] / args.steps / ms} for k, v in sorted(stages.items(), key=lambda kv: -kv[1]["ms"])}
