@@ -480,21 +480,64 @@ __global__ void seg_offsets_kernel(const int32_t* __restrict__ keys_sorted, int6
     offsets[b] = lo;
 }
 
-__global__ void centroid_sum_kernel(const float* __restrict__ Xs, int d, int d_pad, const int32_t* __restrict__ order,
-                                    const int64_t* __restrict__ offsets, const float* __restrict__ C_in,
-                                    float* __restrict__ C_out)
+// One thread per (centroid, dimension): the members' values added in ascending member order in
+// fp64, then divided by the count (the oracle's rule, bit for bit).  The chain of a large centroid
+// is long (C3: tens of thousands of members), so a thread keeps loads in flight ahead of its
+// additions: the values of the next kSumBatch members (their ids already in registers) and the
+// ids of the batch after that are issued before the current batch is added.
+constexpr int kSumBatch = 32;
+
+__global__ void __launch_bounds__(128)
+    centroid_sum_kernel(const float* __restrict__ Xs, int d, int d_pad, const int32_t* __restrict__ order,
+                        const int64_t* __restrict__ offsets, const float* __restrict__ C_in, float* __restrict__ C_out)
 {
     const int b = blockIdx.x;
+    const int k = static_cast<int>(blockIdx.y) * blockDim.x + threadIdx.x;
+    if (k >= d_pad) return;
     const int64_t lo = offsets[b], hi = offsets[b + 1];
     const int64_t cnt = hi - lo;
-    for (int k = threadIdx.x; k < d_pad; k += blockDim.x) {
-        const int64_t o = static_cast<int64_t>(b) * d_pad + k;
-        if (k >= d) { C_out[o] = 0.0f; continue; }
-        if (cnt == 0) { C_out[o] = C_in[o]; continue; }
-        double s = 0.0;
-        for (int64_t j = lo; j < hi; ++j) s += static_cast<double>(Xs[static_cast<int64_t>(order[j]) * d_pad + k]);
-        C_out[o] = static_cast<float>(s / static_cast<double>(cnt));
+    const int64_t o = static_cast<int64_t>(b) * d_pad + k;
+    if (k >= d) {
+        C_out[o] = 0.0f;
+        return;
     }
+    if (cnt == 0) {
+        C_out[o] = C_in[o];
+        return;
+    }
+    double s = 0.0;
+    int64_t j = lo;
+    const int64_t end_full = lo + cnt / kSumBatch * kSumBatch;  // members in whole batches
+    if (end_full > lo) {
+        int32_t ids[kSumBatch];  // the ids of the batch whose values are loaded next
+        float cur[kSumBatch];    // the values of the batch added next
+#pragma unroll
+        for (int u = 0; u < kSumBatch; ++u) ids[u] = order[lo + u];
+#pragma unroll
+        for (int u = 0; u < kSumBatch; ++u) cur[u] = Xs[static_cast<int64_t>(ids[u]) * d_pad + k];
+        if (lo + kSumBatch < end_full) {
+#pragma unroll
+            for (int u = 0; u < kSumBatch; ++u) ids[u] = order[lo + kSumBatch + u];
+        }
+        for (; j + kSumBatch < end_full; j += kSumBatch) {
+            float nxt[kSumBatch];  // the batch starting at j + kSumBatch
+#pragma unroll
+            for (int u = 0; u < kSumBatch; ++u) nxt[u] = Xs[static_cast<int64_t>(ids[u]) * d_pad + k];
+            if (j + 2 * kSumBatch < end_full) {
+#pragma unroll
+                for (int u = 0; u < kSumBatch; ++u) ids[u] = order[j + 2 * kSumBatch + u];
+            }
+#pragma unroll
+            for (int u = 0; u < kSumBatch; ++u) s += static_cast<double>(cur[u]);
+#pragma unroll
+            for (int u = 0; u < kSumBatch; ++u) cur[u] = nxt[u];
+        }
+#pragma unroll
+        for (int u = 0; u < kSumBatch; ++u) s += static_cast<double>(cur[u]);  // the batch at end_full - kSumBatch
+        j = end_full;
+    }
+    for (; j < hi; ++j) s += static_cast<double>(Xs[static_cast<int64_t>(order[j]) * d_pad + k]);
+    C_out[o] = static_cast<float>(s / static_cast<double>(cnt));
 }
 
 // Integer-valued rows (8-bit data): every partial sum is an integer below 2^53, so fp64 adds
@@ -1406,7 +1449,8 @@ void centroid_update(const float* Xs, int64_t n_s, int d, int d_pad, const int32
             sums.get(), offsets.get(), C_in, B, d, d_pad, C_out);
         count_launches(2);
     } else {
-        centroid_sum_kernel<<<B, 128, 0, st>>>(Xs, d, d_pad, idx_out.get(), offsets.get(), C_in, C_out);
+        const dim3 grid(static_cast<unsigned>(B), static_cast<unsigned>((d_pad + 127) / 128));
+        centroid_sum_kernel<<<grid, 128, 0, st>>>(Xs, d, d_pad, idx_out.get(), offsets.get(), C_in, C_out);
         count_launches(1);
     }
     if (C_norm) convert_rows(C_out, 0, d_pad, nullptr, B, C_out, kElemF32, d_pad, C_norm, st);
