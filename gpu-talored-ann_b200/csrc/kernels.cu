@@ -374,8 +374,15 @@ __device__ __forceinline__ double block_incl_scan(double v, double* s_warp)
     return v + off;
 }
 
-// With `resident`, each CTA keeps its 256 pool rows in shared memory, transposed
-// (dimension-major, so thread t reads column t without bank conflicts).
+// With `resident` 1, each CTA keeps its 256 pool rows in shared memory, transposed
+// (dimension-major, so thread t reads column t without bank conflicts).  With `resident` 2
+// (rows too long for that), the rows pass through shared memory kKppDims dimensions at a time,
+// transposed the same way (row stride kKppStride: conflict-free both ways), every warp loading
+// 32 rows' slices with coalesced loads; each thread's chain still runs over the dimensions in
+// ascending order, so the distances are those of exact_l2_f bit for bit.
+constexpr int kKppDims = 64;
+constexpr int kKppStride = kKppCoopThreads + 1;
+
 __global__ void __launch_bounds__(kKppCoopThreads)
     kpp_coop_kernel(const float* __restrict__ pool, int64_t pool_n, int d, int d_pad, float* __restrict__ C, int B,
                     uint64_t seed, double* __restrict__ gpre, double* __restrict__ gtot, unsigned* arrive,
@@ -392,7 +399,7 @@ __global__ void __launch_bounds__(kKppCoopThreads)
     const int64_t i = static_cast<int64_t>(blockIdx.x) * kKppCoopThreads + tid;
     const bool valid = i < pool_n;
     float md = INFINITY;
-    if (resident)
+    if (resident == 1)
         for (int k = 0; k < d; ++k) rows_t[k * kKppCoopThreads + tid] = valid ? pool[i * d_pad + k] : 0.0f;
     if (tid == 0) {
         const int64_t f = static_cast<int64_t>(uniform01(seed, 0) * static_cast<double>(pool_n));
@@ -409,16 +416,44 @@ __global__ void __launch_bounds__(kKppCoopThreads)
         if (t + 1 >= B) break;
         if (valid) {
             float dd;
-            if (resident) {  // the same fp32 chain as exact_l2_f, operands from shared memory
+            if (resident == 1) {  // the same fp32 chain as exact_l2_f, operands from shared memory
                 dd = 0.0f;
                 for (int k = 0; k < d; ++k) {
                     const float t = rows_t[k * kKppCoopThreads + tid] - cen[k];
                     dd = fmaf(t, t, dd);
                 }
-            } else {
+                md = fminf(md, dd);
+            } else if (resident == 0) {
                 dd = exact_l2_f(pool + i * d_pad, cen, d);
+                md = fminf(md, dd);
             }
-            md = fminf(md, dd);
+        }
+        if (resident == 2) {
+            // every thread of the CTA stages (the barriers below), the valid ones add
+            const int warp = tid >> 5, lane = tid & 31;
+            float dd = 0.0f;
+            for (int k0 = 0; k0 < d; k0 += kKppDims) {
+                const int nk = d - k0 < kKppDims ? d - k0 : kKppDims;
+#pragma unroll 8
+                for (int p = 0; p < 32; ++p) {
+                    const int col = warp * 32 + p;  // this CTA's point
+                    const int64_t ip = static_cast<int64_t>(blockIdx.x) * kKppCoopThreads + col;
+                    const float* src = pool + (ip < pool_n ? ip : 0) * d_pad + k0;
+                    const float v0 = (ip < pool_n && lane < nk) ? src[lane] : 0.0f;
+                    const float v1 = (ip < pool_n && lane + 32 < nk) ? src[lane + 32] : 0.0f;
+                    rows_t[lane * kKppStride + col] = v0;
+                    rows_t[(lane + 32) * kKppStride + col] = v1;
+                }
+                __syncthreads();
+                if (valid) {
+                    for (int c = 0; c < nk; ++c) {
+                        const float t = rows_t[c * kKppStride + tid] - cen[k0 + c];
+                        dd = fmaf(t, t, dd);
+                    }
+                }
+                __syncthreads();
+            }
+            if (valid) md = fminf(md, dd);
         }
         const double incl = block_incl_scan(valid ? static_cast<double>(md) : 0.0, s_warp);
         const int par = t & 1;
@@ -1360,21 +1395,24 @@ void kmeanspp_init(const float* pool, const float* /*pool_norm*/, int64_t pool_n
         GTA_CUDA(cudaGetDevice(&dev));
         GTA_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
         GTA_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
-        // pool rows resident in shared memory when they fit (d <= 200: about 200 KB per CTA)
-        int resident = d <= 200 ? 1 : 0;
-        size_t smem1 = sizeof(float) * static_cast<size_t>(d_pad) * (resident ? 1 + kKppCoopThreads : 1);
+        // pool rows resident in shared memory when they fit (d <= 200: about 200 KB per CTA), else
+        // staged through it kKppDims dimensions at a time
+        const size_t staged = sizeof(float) * (static_cast<size_t>(d_pad) + static_cast<size_t>(kKppDims) * kKppStride);
+        int resident = d <= 200 ? 1 : (staged <= 227 * 1024 ? 2 : 0);
+        size_t smem1 = resident == 1 ? sizeof(float) * static_cast<size_t>(d_pad) * (1 + kKppCoopThreads)
+                                     : (resident == 2 ? staged : sizeof(float) * static_cast<size_t>(d_pad));
         if (smem1 > 227 * 1024) {
             // one centroid row alone does not fit either: the per-centroid launches below
             resident = 0;
             smem1 = sizeof(float) * static_cast<size_t>(d_pad);
         }
-        // the attribute covers the layout chosen here (the non-resident one needs less)
+        // the attribute covers the layout chosen here and the staged one it may fall back to
         GTA_CUDA(cudaFuncSetAttribute(kpp_coop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      static_cast<int>(std::min<size_t>(smem1, 227 * 1024))));
+                                      static_cast<int>(std::min<size_t>(std::max(smem1, staged), 227 * 1024))));
         GTA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kpp_coop_kernel, kKppCoopThreads, smem1));
-        if (resident && G > per_sm * n_sm) {
-            resident = 0;
-            smem1 = sizeof(float) * static_cast<size_t>(d_pad);
+        if (resident == 1 && G > per_sm * n_sm) {
+            resident = staged <= 227 * 1024 ? 2 : 0;
+            smem1 = resident == 2 ? staged : sizeof(float) * static_cast<size_t>(d_pad);
             GTA_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kpp_coop_kernel, kKppCoopThreads, smem1));
         }
         if (coop && smem1 <= 227 * 1024 && G <= per_sm * n_sm && G <= kKppCoopThreads) {
