@@ -44,9 +44,11 @@ def _ptr(x) -> ctypes.c_void_p:
     if x is None:
         return ctypes.c_void_p(0)
     if _is_dev(x):
-        assert x.is_contiguous(), "device arrays must be contiguous"
+        if not x.is_contiguous():
+            raise L.GtaError(L.GTA_EINVAL, "device arrays must be contiguous")
         return ctypes.c_void_p(x.data_ptr())
-    assert isinstance(x, np.ndarray) and x.flags["C_CONTIGUOUS"], "host arrays must be C-contiguous numpy arrays"
+    if not (isinstance(x, np.ndarray) and x.flags["C_CONTIGUOUS"]):
+        raise L.GtaError(L.GTA_EINVAL, "host arrays must be C-contiguous numpy arrays")
     return x.ctypes.data_as(ctypes.c_void_p)
 
 

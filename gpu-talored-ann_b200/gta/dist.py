@@ -91,7 +91,8 @@ class ShardResult:
 def _p(t: Optional[torch.Tensor]) -> ctypes.c_void_p:
     if t is None:
         return ctypes.c_void_p(0)
-    assert t.is_contiguous()
+    if not t.is_contiguous():
+        raise L.GtaError(L.GTA_EINVAL, "libgta stages take contiguous tensors")
     return ctypes.c_void_p(t.data_ptr())
 
 

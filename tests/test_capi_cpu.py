@@ -190,3 +190,12 @@ def test_host_resident_needs_a_contiguous_host_array():
     with pytest.raises(gta.GtaError) as e:
         gta.build_bucket(X[:, ::2], 4, 8, host_resident=True)
     assert e.value.code == L.GTA_EINVAL
+
+
+def test_strided_host_arrays_are_refused_with_a_status():
+    """Every entry point takes C-contiguous buffers: a strided host view raises GtaError (status 1),
+    not an assertion that optimised Python would skip."""
+    X = np.zeros((64, 16), np.float32)
+    with pytest.raises(gta.GtaError) as e:
+        gta.build_bucket(X[:, ::2], 4, 8)
+    assert e.value.code == L.GTA_EINVAL
