@@ -52,6 +52,21 @@ def _ptr(x) -> ctypes.c_void_p:
     return x.ctypes.data_as(ctypes.c_void_p)
 
 
+def _dev(*xs) -> None:
+    """Stage entry points read and write device memory only: every array argument (None skipped)
+    must be a CUDA tensor, checked before anything is allocated or launched."""
+    for x in xs:
+        if x is not None and not _is_dev(x):
+            raise L.GtaError(L.GTA_EINVAL, "stage entry points take torch CUDA tensors")
+
+
+def _same_side(dev: bool, *xs) -> None:
+    """Arguments of one call all on the device or all on the host (None skipped)."""
+    for x in xs:
+        if x is not None and _is_dev(x) != dev:
+            raise L.GtaError(L.GTA_EINVAL, "arguments must be all torch CUDA tensors or all numpy arrays")
+
+
 def _stream():
     torch = _torch()
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
@@ -213,6 +228,7 @@ def search(base, graph, queries, topk: int = 10, ef: int = 200, num_entry: int =
     entry points, seed 42).  ``base`` / ``queries`` / ``graph`` all on the device (torch)
     or all on the host (numpy).  Returns (ids[nq, topk], dists[nq, topk])."""
     dev = _is_dev(base)
+    _same_side(dev, queries, graph)
     n, d = base.shape
     nq = queries.shape[0]
     ef = max(ef, topk)
@@ -237,12 +253,14 @@ def search(base, graph, queries, topk: int = 10, ef: int = 200, num_entry: int =
 
 # ---------------------------------------------------------------- stages (device tensors)
 def kmeans_init(X, pool_n: int, n_buckets: int, seed: int = 42):
+    _dev(X)
     C = _empty((n_buckets, X.shape[1]), "float32", True)
     L.check(L.lib().gta_kmeans_init(_ptr(X), pool_n, X.shape[1], n_buckets, seed, _ptr(C), _stream()))
     return C
 
 
 def kmeans_fit(X, C0, iters: int):
+    _dev(X, C0)
     C = C0.clone().contiguous()
     assign = _empty((X.shape[0],), "int32", True)
     L.check(L.lib().gta_kmeans_fit(_ptr(X), X.shape[0], X.shape[1], _ptr(C), C.shape[0], iters, _ptr(assign),
@@ -251,6 +269,7 @@ def kmeans_fit(X, C0, iters: int):
 
 
 def assign_topk(X, C, k: int):
+    _dev(X, C)
     ids = _empty((X.shape[0], k), "int32", True)
     dists = _empty((X.shape[0], k), "float32", True)
     L.check(L.lib().gta_assign_topk(_ptr(X), X.shape[0], X.shape[1], _ptr(C), C.shape[0], k, _ptr(ids), _ptr(dists),
@@ -259,6 +278,7 @@ def assign_topk(X, C, k: int):
 
 
 def build_memberships(top2, n_buckets: int):
+    _dev(top2)
     torch = _torch()
     N = top2.shape[0]
     members = torch.empty(2 * N, dtype=torch.int32, device="cuda")
@@ -270,6 +290,7 @@ def build_memberships(top2, n_buckets: int):
 
 
 def bucket_knn(X, members, offsets, knn_degree: int):
+    _dev(X, members, offsets)
     n_mem = members.shape[0]
     ids = _empty((n_mem, knn_degree), "int32", True)
     dists = _empty((n_mem, knn_degree), "float32", True)
@@ -279,6 +300,7 @@ def bucket_knn(X, members, offsets, knn_degree: int):
 
 
 def merge_memberships(list_ids, list_dists, mem_row):
+    _dev(list_ids, list_dists, mem_row)
     N, M = mem_row.shape[0], list_ids.shape[1]
     ids = _empty((N, M), "int32", True)
     dists = _empty((N, M), "float32", True)
@@ -288,6 +310,7 @@ def merge_memberships(list_ids, list_dists, mem_row):
 
 
 def merge_lists(run_ids, run_dists, new_ids, new_dists):
+    _dev(run_ids, run_dists, new_ids, new_dists)
     N, M = run_ids.shape
     ids = _empty((N, M), "int32", True)
     dists = _empty((N, M), "float32", True)
@@ -297,24 +320,28 @@ def merge_lists(run_ids, run_dists, new_ids, new_dists):
 
 
 def sanitize(knn):
+    _dev(knn)
     out = _empty(tuple(knn.shape), "int32", True)
     L.check(L.lib().gta_sanitize(_ptr(knn), knn.shape[0], knn.shape[1], _ptr(out), _stream()))
     return out
 
 
 def sort_rows(X, knn):
+    _dev(X, knn)
     out = _empty(tuple(knn.shape), "int32", True)
     L.check(L.lib().gta_sort_rows(_ptr(X), X.shape[0], X.shape[1], _ptr(knn), knn.shape[1], _ptr(out), _stream()))
     return out
 
 
 def prune(knn, graph_degree: int):
+    _dev(knn)
     out = _empty((knn.shape[0], graph_degree), "int32", True)
     L.check(L.lib().gta_prune(_ptr(knn), knn.shape[0], knn.shape[1], graph_degree, _ptr(out), _stream()))
     return out
 
 
 def reverse_merge(pruned):
+    _dev(pruned)
     out = _empty(tuple(pruned.shape), "int32", True)
     L.check(L.lib().gta_reverse_merge(_ptr(pruned), pruned.shape[0], pruned.shape[1], _ptr(out), _stream()))
     return out
@@ -343,6 +370,7 @@ def bucket_reorder(assign, n_buckets: int, order=None):
     old id inside a bucket.  ``assign`` is (N,) or an (N, 2) top-2 table (column 0 is used).
     Returns (inverse_perm[N] uint32 (int32 view on the device), offsets[B+1] int64)."""
     dev, st = _side(assign)
+    _same_side(dev, order)
     n = assign.shape[0]
     stride = 1 if assign.ndim == 1 else assign.shape[1]
     inv = _empty((n,), "int32" if dev else "uint32", dev)
@@ -355,6 +383,7 @@ def bucket_reorder(assign, n_buckets: int, order=None):
 def permute_rows(X, inverse_perm):
     """Row i of the result = row inverse_perm[i] of X (the reordered dataset)."""
     dev, st = _side(X)
+    _same_side(dev, inverse_perm)
     if dev:
         torch = _torch()
         out = torch.empty_like(X)
@@ -369,6 +398,7 @@ def permute_graph(g, inverse_perm, to_original: bool = True, keep_padding: bool 
     """translate_ids (to_original) or the renumbering into the reordered id space of an
     N x M id table; -1 padding kept when ``keep_padding``."""
     dev, st = _side(g)
+    _same_side(dev, inverse_perm)
     if not dev:
         g = np.ascontiguousarray(g)
         g = g.view(np.int32) if g.dtype.itemsize == 4 else g.astype(np.int32)

@@ -199,3 +199,21 @@ def test_strided_host_arrays_are_refused_with_a_status():
     with pytest.raises(gta.GtaError) as e:
         gta.build_bucket(X[:, ::2], 4, 8)
     assert e.value.code == L.GTA_EINVAL
+
+
+def test_stage_wrappers_refuse_host_arrays_before_device_work():
+    """The stage entry points read device memory: numpy arguments are refused (status 1) before
+    anything is allocated or launched, and mixed host / device arguments likewise."""
+    X = np.zeros((64, 16), np.float32)
+    mem = np.arange(64, dtype=np.int32)
+    off = np.array([0, 64], np.int64)
+    g = np.zeros((64, 8), np.int32)
+    for call in (lambda: gta.bucket_knn(X, mem, off, 8), lambda: gta.prune(g, 4), lambda: gta.reverse_merge(g),
+                 lambda: gta.sanitize(g), lambda: gta.assign_topk(X, X[:4], 2), lambda: gta.kmeans_fit(X, X[:4], 1)):
+        with pytest.raises(gta.GtaError) as e:
+            call()
+        assert e.value.code == L.GTA_EINVAL
+    fake_dev = type("FakeCudaTensor", (), {"is_cuda": True})()  # a device-side argument beside host X
+    with pytest.raises(gta.GtaError) as e:
+        gta.permute_rows(X, fake_dev)
+    assert e.value.code == L.GTA_EINVAL
