@@ -886,9 +886,29 @@ __global__ void __launch_bounds__(kRrWarps * 32) rerank_kernel(const RerankX p)
             __syncwarp();
             continue;
         }
+        const uint32_t* kl = reinterpret_cast<const uint32_t*>(p.cand_cols) + irow * p.L;
+        const int n1 = nv < p.m_out ? nv : p.m_out;
+        if (pilot) {
+            // The row's exact M-th distance over the whole bucket is at most the largest exact
+            // distance of any m_out distinct columns of it.  A listed column's exact distance is at
+            // most its approximate one plus the screen's one-sided error (the bound of step 2
+            // below), and its code's value is at least the approximate distance, so the window's
+            // first m_out keys give the bound without exact chains (rounded up throughout).
+            if (n1 == p.m_out) {
+                float mx = -INFINITY;
+                for (int j = lane; j < n1; j += 32)
+                    mx = fmaxf(mx, __fmul_ru(code_value(kl[j] >> p.col_bits, code_b), inv_s2));
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                const float an = sqrtf(fmaxf(p.norm[arow], 0.0f));
+                const float err = 0.5f * (p.mc1 * an * bm + p.mc2 * (an + bm) * (an + bm));
+                if (lane == 0) p.seed_out[static_cast<int64_t>(w.pad2) + r] = __fadd_ru(mx, err);
+            }
+            __syncwarp();
+            continue;
+        }
         for (int i = lane; i < p.dp; i += 32) q_s[i] = p.pool[arow * p.dp + i];
         __syncwarp();
-        const uint32_t* kl = reinterpret_cast<const uint32_t*>(p.cand_cols) + irow * p.L;
         // exact keys of list positions [j_lo, j_hi) into keys[j]; returns the largest distance
         auto exact_range = [&](int j_lo, int j_hi) {
             float mx = -INFINITY;
@@ -907,15 +927,7 @@ __global__ void __launch_bounds__(kRrWarps * 32) rerank_kernel(const RerankX p)
             return mx;
         };
         // 1. the first M keys: their largest exact distance bounds the row's exact M-th
-        const int n1 = nv < p.m_out ? nv : p.m_out;
         const float e_m = exact_range(0, n1);
-        if (pilot) {
-            // m_out distinct columns of the row's bucket at exact distances <= e_m: the row's exact
-            // M-th distance over the whole bucket is at most e_m
-            if (lane == 0 && n1 == p.m_out) p.seed_out[static_cast<int64_t>(w.pad2) + r] = e_m;
-            __syncwarp();
-            continue;
-        }
         int n_tot = n1;
         bool rescan = false;
         if (nv > n1) {
