@@ -975,11 +975,13 @@ __global__ void __launch_bounds__(kRrWarps * 32) rerank_kernel(const RerankX p)
 }
 
 // Exact top-m_out of whole segments for the rows the rerank could not settle from its list:
-// persistent CTAs walk the rescan list; per row, each of the 8 warps keeps the 256 best
+// persistent CTAs walk the rescan list; per row, each of the kRsWarps warps keeps the 256 best
 // (distance, id) keys of its share of the columns (a bitonic sort of 512 keys per 256 columns),
-// then warp 0 merges the warps' lists.
-constexpr int kRsWarps = 8;
-
+// then warp 0 merges the warps' lists.  A wave usually rescans fewer rows than there are CTAs,
+// so its time is one row's scan (C3: 3.7 ms per wave for a 32 768-column chunk with 8 warps):
+// 16 warps per CTA (one CTA per SM) halve it where their shared memory fits, 8 (two per SM)
+// serve longer rows.  The list does not depend on the split of the columns over the warps.
+template <int kRsWarps>
 __global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p)
 {
     extern __shared__ uint8_t sm[];
@@ -1400,10 +1402,13 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
     r.rescan = rescan.get();
     r.n_rescan = n_rescan.get();
     const size_t smem_rr = kRrWarps * (kRrKeys * sizeof(uint64_t) + kChainBufBytes + static_cast<size_t>(dp) * 4);
-    const size_t smem_rs = kRsWarps * (kRrKeys * sizeof(uint64_t) + kChainBufBytes) + static_cast<size_t>(dp) * 4;
+    const size_t smem_rs16 = 16 * (kRrKeys * sizeof(uint64_t) + kChainBufBytes) + static_cast<size_t>(dp) * 4;
+    const bool rs16 = smem_rs16 <= kSSmemMax;
+    const size_t smem_rs = rs16 ? smem_rs16 : 8 * (kRrKeys * sizeof(uint64_t) + kChainBufBytes) + static_cast<size_t>(dp) * 4;
     GTA_REQUIRE(smem_rr <= kSSmemMax && smem_rs <= kSSmemMax, kInvalid, "rerank: dimension too large");
     GTA_CUDA(cudaFuncSetAttribute(rerank_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_rr)));
-    GTA_CUDA(cudaFuncSetAttribute(rescan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem_rs)));
+    GTA_CUDA(cudaFuncSetAttribute(rs16 ? rescan_kernel<16> : rescan_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(smem_rs)));
     int dev = 0, n_sm = 0;
     GTA_CUDA(cudaGetDevice(&dev));
     GTA_CUDA(cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev));
@@ -1482,7 +1487,10 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
         {
             // the deferred whole-segment rescans: persistent CTAs over the device-side list
             ProfScope prof("rescan", 0.0, st);
-            rescan_kernel<<<static_cast<unsigned>(std::max(1, n_sm) * 2), kRsWarps * 32, smem_rs, st>>>(r);
+            if (rs16)
+                rescan_kernel<16><<<static_cast<unsigned>(std::max(1, n_sm)), 16 * 32, smem_rs, st>>>(r);
+            else
+                rescan_kernel<8><<<static_cast<unsigned>(std::max(1, n_sm) * 2), 8 * 32, smem_rs, st>>>(r);
             count_launches(1);
             GTA_CUDA(cudaGetLastError());
         }
