@@ -980,9 +980,11 @@ __global__ void __launch_bounds__(kRrWarps * 32) rerank_kernel(const RerankX p)
 // then warp 0 merges the warps' lists.  A wave usually rescans fewer rows than there are CTAs,
 // so its time is one row's scan (C3: 3.7 ms per wave for a 32 768-column chunk with 8 warps):
 // 16 warps per CTA (one CTA per SM) halve it where their shared memory fits, 8 (two per SM)
-// serve longer rows.  The list does not depend on the split of the columns over the warps.
+// serve longer rows.  With fewer rows than CTAs a row's columns are also cut into `slices`
+// ranges (multiples of 256 columns), one per CTA, each writing its best m_out keys to `partial`
+// for rescan_merge_kernel.  The list depends on neither split.
 template <int kRsWarps>
-__global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p)
+__global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p, int slices, uint64_t* partial)
 {
     extern __shared__ uint8_t sm[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -990,23 +992,30 @@ __global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p)
     uint64_t* keys = all + warp * kRrKeys;
     float* cbuf = reinterpret_cast<float*>(sm + kRsWarps * kRrKeys * sizeof(uint64_t) + warp * kChainBufBytes);
     float* q_s = reinterpret_cast<float*>(sm + kRsWarps * (kRrKeys * sizeof(uint64_t) + kChainBufBytes));
-    const unsigned n = *p.n_rescan;
-    for (unsigned i = blockIdx.x; i < n; i += gridDim.x) {
+    const uint64_t n = *p.n_rescan;
+    const uint64_t units = n * static_cast<uint64_t>(slices);
+    for (uint64_t u = blockIdx.x; u < units; u += gridDim.x) {
+        const uint64_t i = u / static_cast<uint64_t>(slices);
+        const int sl = static_cast<int>(u - i * static_cast<uint64_t>(slices));
         const int2 e = p.rescan[i];
         const int64_t irow = e.x;
         const WorkItem w = p.work[e.y];
         const int r = static_cast<int>(irow - w.item_row0);
         const int64_t arow = static_cast<int64_t>(w.a_row0) + r;
         const int self = (w.has_self & 1) ? w.self_col0 + r : -1;  // outside [0, b_rows): no column is skipped
+        // this unit's columns [c_lo, c_hi) of the row's b_rows
+        const int span = ((w.b_rows + slices - 1) / slices + 255) / 256 * 256;
+        const int c_lo = sl * span;
+        const int c_hi = c_lo + span < w.b_rows ? c_lo + span : w.b_rows;
         __syncthreads();
         for (int j = threadIdx.x; j < p.dp; j += blockDim.x) q_s[j] = p.pool[arow * p.dp + j];
         for (int j = lane; j < kRrKeys; j += 32) keys[j] = ~0ull;
         __syncthreads();
-        // this warp's columns: chunks of 256 starting at 256 * warp, strided by the CTA
-        for (int c0 = 256 * warp; c0 < w.b_rows; c0 += 256 * kRsWarps) {
+        // this warp's columns: chunks of 256 starting at c_lo + 256 * warp, strided by the CTA
+        for (int c0 = c_lo + 256 * warp; c0 < c_hi; c0 += 256 * kRsWarps) {
             for (int j = 0; j < kRrKeys / 2; j += 32) {
                 const int c = c0 + j + lane;
-                const bool ok = c < w.b_rows && c != self;
+                const bool ok = c < c_hi && c != self;
                 const int64_t brow = ok ? static_cast<int64_t>(w.b_row0) + c : -1;
                 const float dd = warp_chain(q_s, p.pool, p.dp, brow, cbuf, lane);
                 keys[kRrKeys / 2 + j + lane] =
@@ -1024,9 +1033,39 @@ __global__ void __launch_bounds__(kRsWarps * 32) rescan_kernel(const RerankX p)
                 __syncwarp();
                 rr_sort(keys, kRrKeys, lane);
             }
-            write_list(p, irow, keys, kRrKeys / 2, lane);
+            if (slices == 1) {
+                write_list(p, irow, keys, kRrKeys / 2, lane);
+            } else {
+                uint64_t* dst = partial + (i * static_cast<uint64_t>(slices) + static_cast<uint64_t>(sl)) * p.m_out;
+                for (int j = lane; j < p.m_out; j += 32) dst[j] = keys[j];
+            }
         }
     }
+}
+
+// The rows rescanned in slices: one warp per row merges its slices' best m_out keys (each
+// slice's list sorted; the row's list kept in the first half of the buffer as in the CTA merge
+// above) and writes the row's list.
+__global__ void __launch_bounds__(kRrWarps * 32)
+    rescan_merge_kernel(const RerankX p, int slices, const uint64_t* __restrict__ partial)
+{
+    __shared__ uint64_t s_keys[kRrWarps][kRrKeys];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint64_t n = *p.n_rescan;
+    const uint64_t i = static_cast<uint64_t>(blockIdx.x) * kRrWarps + warp;
+    if (i >= n) return;
+    uint64_t* keys = s_keys[warp];
+    const uint64_t* src = partial + i * static_cast<uint64_t>(slices) * p.m_out;
+    for (int j = lane; j < kRrKeys; j += 32) keys[j] = j < p.m_out ? src[j] : ~0ull;
+    for (int sl = 1; sl < slices; ++sl) {
+        __syncwarp();
+        for (int j = lane; j < kRrKeys / 2; j += 32)
+            keys[kRrKeys / 2 + j] = j < p.m_out ? src[static_cast<int64_t>(sl) * p.m_out + j] : ~0ull;
+        __syncwarp();
+        rr_sort(keys, kRrKeys, lane);
+    }
+    __syncwarp();
+    write_list(p, p.rescan[i].x, keys, kRrKeys / 2, lane);
 }
 
 // Rows of segments that run as column chunks, one chunk per wave: the row's running list (the
@@ -1484,21 +1523,31 @@ void screen_knn(const ScreenProblem& pr, cudaStream_t st)
             GTA_CUDA(cudaGetLastError());
         }
         if (is_pilot) continue;  // the pilot writes no lists: nothing to rescan or merge
-        {
-            // the deferred whole-segment rescans: persistent CTAs over the device-side list
+        // the rows the rerank left to a whole-segment rescan (the launch shape depends on their count)
+        unsigned n_rs = 0;
+        GTA_CUDA(cudaMemcpyAsync(&n_rs, n_rescan.get(), sizeof(unsigned), cudaMemcpyDeviceToHost, st));
+        GTA_CUDA(cudaStreamSynchronize(st));
+        if (n_rs > 0) {
+            // persistent CTAs over the device-side list; fewer rows than CTAs: each row's columns
+            // in slices over several CTAs, then a merge of the slices' lists
             ProfScope prof("rescan", 0.0, st);
+            const int ctas = std::max(1, n_sm) * (rs16 ? 1 : 2);
+            const int slices = n_rs >= static_cast<unsigned>(ctas) ? 1 : std::min(16, ctas / static_cast<int>(n_rs));
+            DevBuf<uint64_t> partial(slices > 1 ? static_cast<size_t>(n_rs) * slices * pr.m_out : 0, st);
             if (rs16)
-                rescan_kernel<16><<<static_cast<unsigned>(std::max(1, n_sm)), 16 * 32, smem_rs, st>>>(r);
+                rescan_kernel<16><<<static_cast<unsigned>(ctas), 16 * 32, smem_rs, st>>>(r, slices, partial.get());
             else
-                rescan_kernel<8><<<static_cast<unsigned>(std::max(1, n_sm) * 2), 8 * 32, smem_rs, st>>>(r);
+                rescan_kernel<8><<<static_cast<unsigned>(ctas), 8 * 32, smem_rs, st>>>(r, slices, partial.get());
             count_launches(1);
             GTA_CUDA(cudaGetLastError());
+            if (slices > 1) {
+                rescan_merge_kernel<<<(n_rs + kRrWarps - 1) / kRrWarps, kRrWarps * 32, 0, st>>>(r, slices, partial.get());
+                count_launches(1);
+                GTA_CUDA(cudaGetLastError());
+            }
         }
         if (split_mode >= 0 && cur != split_mode && !wave_split[wk] && wk + 1 < waves.size()) {
             // too many rescans under the one-part margin: the remaining waves screen split
-            unsigned n_rs = 0;
-            GTA_CUDA(cudaMemcpyAsync(&n_rs, n_rescan.get(), sizeof(unsigned), cudaMemcpyDeviceToHost, st));
-            GTA_CUDA(cudaStreamSynchronize(st));
             int64_t wave_rows = 0;
             for (const WorkItem& it : items) wave_rows += it.a_rows;
             if (static_cast<double>(n_rs) > 0.05 * static_cast<double>(wave_rows)) cur = split_mode;

@@ -311,6 +311,38 @@ def test_bucket_knn_f32_overflow_rescan():
     np.testing.assert_array_equal(host(gd), rd)
 
 
+@pytest.mark.parametrize("lo,hi", [(0, 40), (150, 151), (260, 300)])
+def test_rescan_of_few_rows_in_column_slices(lo, hi):
+    """A row range of a bucket whose rows all need the whole-segment rescan (300 identical points:
+    more columns within the bound than a list holds): so few rows that each is spread over several
+    CTAs in column slices whose lists are merged by key.  Exact top-M against the oracle; rows
+    outside the range untouched."""
+    import gta.dist as gd
+
+    rng = np.random.default_rng(12)
+    n, d, M = 2500, 32, 16
+    X = mixture(rng, n, d, 6, 0.3)
+    X[:300] = X[0]
+    order = torch.arange(n, dtype=torch.int32, device="cuda")
+    offsets = dev(np.array([0, n], np.int64))
+    partner = torch.ones(n, dtype=torch.int32, device="cuda")
+    lid = torch.full((n, M), -1, dtype=torch.int32, device="cuda")
+    ldist = torch.full((n, M), float("inf"), dtype=torch.float32, device="cuda")
+    gd.CudaStages().bucket_knn_rows_ranged(dev(X), order, order.clone(), offsets, partner, M, 1, None,
+                                           torch.tensor([lo]), torch.tensor([hi]), lid, ldist)
+    gi, gdist = host(lid), host(ldist)
+    allc = np.arange(n)
+    for r in range(lo, hi):
+        dd = orc.pair_l2(X, np.full(n, r), allc)
+        dd[r] = np.inf
+        sel = np.lexsort((allc, dd))[:M]
+        np.testing.assert_array_equal(gi[r], sel)
+        np.testing.assert_array_equal(gdist[r], dd[sel])
+    outside = np.ones(n, bool)
+    outside[lo:hi] = False
+    assert (gi[outside] == -1).all()
+
+
 def test_bucket_knn_tiny_and_ragged_buckets():
     rng = np.random.default_rng(10)
     X = rng.integers(0, 256, (700, 64)).astype(np.uint8)
